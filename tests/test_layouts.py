@@ -1,0 +1,273 @@
+"""Megatron / SGLang layouts against an independent dense oracle, and host-side resharding.
+
+Checks that (1) the synthetic fill through the strided views produces exactly the fused
+parameters one builds by hand from the full HF tensors, and (2) packing the overlap of
+every (Megatron rank, SGLang rank) pair and unpacking it reproduces the SGLang parameters
+bit for bit, for each model family and several TP/PP/EP combinations.
+"""
+import pytest
+import torch
+
+from weightbridge_b200 import WeightData
+from weightbridge_b200.core.binding import bind, pack_into, unpack_from
+from weightbridge_b200.models.arch import get_arch
+from weightbridge_b200.models.synthetic import synth_full
+from weightbridge_b200.ops.quant_ref import block_quant_fp8_ref
+from weightbridge_b200.parallel.megatron import MegatronLayout
+from weightbridge_b200.parallel.sglang import SGLangLayout
+
+
+def hf_full(arch, dtype=torch.float32):
+    return {n: synth_full(n, s, dtype) for n, s in arch.hf_tensors()}
+
+
+def megatron_oracle(arch, lay: MegatronLayout, hf):
+    """Build this rank's Megatron params by hand from the full HF tensors."""
+    tp, r = lay.tp, lay.tp_rank
+    H, hd, qpg, G = arch.hidden, arch.head_dim, arch.q_per_group, arch.num_kv_heads
+    out = {}
+    Vp = lay.padded_vocab
+    def vocab(t):
+        pad = torch.zeros(Vp, H, dtype=t.dtype)
+        pad[: arch.vocab] = t
+        return pad.chunk(tp)[r]
+    if lay.first_stage:
+        out["embedding.word_embeddings.weight"] = vocab(hf["model.embed_tokens.weight"])
+    G_loc = G // tp
+    for i in range(lay.num_local_layers):
+        g = i + lay.layer_offset
+        p, m = f"decoder.layers.{i}.", f"model.layers.{g}."
+        q = hf[m + "self_attn.q_proj.weight"].view(G, qpg * hd, H)
+        k = hf[m + "self_attn.k_proj.weight"].view(G, hd, H)
+        v = hf[m + "self_attn.v_proj.weight"].view(G, hd, H)
+        out[p + "self_attention.linear_qkv.weight"] = torch.cat([q, k, v], 1)[r * G_loc:(r + 1) * G_loc].reshape(-1, H)
+        if arch.qkv_bias:
+            qb = hf[m + "self_attn.q_proj.bias"].view(G, qpg * hd)
+            kb = hf[m + "self_attn.k_proj.bias"].view(G, hd)
+            vb = hf[m + "self_attn.v_proj.bias"].view(G, hd)
+            out[p + "self_attention.linear_qkv.bias"] = torch.cat([qb, kb, vb], 1)[r * G_loc:(r + 1) * G_loc].reshape(-1)
+        out[p + "self_attention.linear_qkv.layer_norm_weight"] = hf[m + "input_layernorm.weight"]
+        if arch.qk_norm:
+            out[p + "self_attention.q_layernorm.weight"] = hf[m + "self_attn.q_norm.weight"]
+            out[p + "self_attention.k_layernorm.weight"] = hf[m + "self_attn.k_norm.weight"]
+        out[p + "self_attention.linear_proj.weight"] = hf[m + "self_attn.o_proj.weight"].chunk(tp, 1)[r]
+        if arch.is_moe:
+            out[p + "pre_mlp_layernorm.weight"] = hf[m + "post_attention_layernorm.weight"]
+            out[p + "mlp.router.weight"] = hf[m + "mlp.gate.weight"]
+            E_loc = arch.num_experts // lay.ep
+            for e in range(E_loc):
+                eg = lay.ep_rank * E_loc + e
+                x = f"{m}mlp.experts.{eg}."
+                gate = hf[x + "gate_proj.weight"].chunk(lay.etp, 0)[lay.etp_rank]
+                up = hf[x + "up_proj.weight"].chunk(lay.etp, 0)[lay.etp_rank]
+                out[lay._expert_name(i, e, 1)] = torch.cat([gate, up])
+                out[lay._expert_name(i, e, 2)] = hf[x + "down_proj.weight"].chunk(lay.etp, 1)[lay.etp_rank]
+        else:
+            out[p + "mlp.linear_fc1.layer_norm_weight"] = hf[m + "post_attention_layernorm.weight"]
+            out[p + "mlp.linear_fc1.weight"] = torch.cat([hf[m + "mlp.gate_proj.weight"].chunk(tp)[r],
+                                                          hf[m + "mlp.up_proj.weight"].chunk(tp)[r]])
+            out[p + "mlp.linear_fc2.weight"] = hf[m + "mlp.down_proj.weight"].chunk(tp, 1)[r]
+    if lay.last_stage:
+        out["decoder.final_layernorm.weight"] = hf["model.norm.weight"]
+        if not arch.tie_embeddings:
+            out["output_layer.weight"] = vocab(hf["lm_head.weight"])
+    return out
+
+
+MEGATRON_CASES = [
+    ("tiny-llama", dict(tp=2)),
+    ("tiny-llama", dict(tp=1, pp=2)),
+    ("tiny-qwen2", dict(tp=2)),
+    ("tiny-qwen3", dict(tp=2, pp=2)),
+    ("tiny-qwen3-moe", dict(tp=1, ep=2)),
+    ("tiny-qwen3-moe", dict(tp=2, ep=2, etp=2, expert_naming="sequential")),
+]
+
+
+@pytest.mark.parametrize("model,cfg", MEGATRON_CASES)
+def test_megatron_fill_matches_oracle(model, cfg):
+    arch = get_arch(model)
+    hf = hf_full(arch)
+    ranks = [dict(tp_rank=t, pp_rank=p, ep_rank=e)
+             for t in range(cfg.get("tp", 1)) for p in range(cfg.get("pp", 1)) for e in range(cfg.get("ep", 1))]
+    for rk in ranks:
+        kw = dict(cfg, **rk)
+        if cfg.get("etp", 1) > 1:
+            kw["etp_rank"] = rk["tp_rank"]
+        lay = MegatronLayout(arch, **kw)
+        params = lay.allocate(dtype=torch.float32)
+        oracle = megatron_oracle(arch, lay, hf)
+        assert set(params) == set(oracle)
+        for n in params:
+            assert torch.equal(params[n], oracle[n]), n
+
+
+def test_megatron_unknown_name_raises():
+    lay = MegatronLayout(get_arch("tiny-llama"))
+    with pytest.raises(ValueError):
+        lay.split_param("decoder.layers.0.mystery.weight", torch.zeros(4))
+
+
+def test_megatron_module_prefix_and_pp_offset():
+    arch = get_arch("tiny-llama")
+    lay = MegatronLayout(arch, pp=2, pp_rank=1)
+    params = lay.allocate(dtype=torch.float32, fill=False)
+    prefixed = {"module.module." + k: v for k, v in params.items()}
+    meta, _ = lay.to_wb(prefixed)
+    assert "model.layers.1.self_attn.q_proj.weight" in meta
+    assert "model.layers.0.self_attn.q_proj.weight" not in meta
+    assert "lm_head.weight" in meta and "model.embed_tokens.weight" not in meta
+
+
+def sglang_oracle(arch, lay: SGLangLayout, hf):
+    H, hd = arch.hidden, arch.head_dim
+    r, tp = lay.tp_rank, lay.tp
+    out = {}
+    Vp = lay.padded_vocab
+    def vocab(t):
+        pad = torch.zeros(Vp, H, dtype=t.dtype)
+        pad[: arch.vocab] = t
+        return pad.chunk(tp)[r]
+    out["model.embed_tokens.weight"] = vocab(hf["model.embed_tokens.weight"])
+    ar, atp = lay.attn_tp_rank, lay.attn_tp
+    kv0 = lay.kv_head0
+    for i in range(arch.num_layers):
+        m = f"model.layers.{i}."
+        q = hf[m + "self_attn.q_proj.weight"].chunk(atp)[ar]
+        k = hf[m + "self_attn.k_proj.weight"][kv0 * hd:(kv0 + lay.kv_local) * hd]
+        v = hf[m + "self_attn.v_proj.weight"][kv0 * hd:(kv0 + lay.kv_local) * hd]
+        out[m + "self_attn.qkv_proj.weight"] = torch.cat([q, k, v])
+        if arch.qkv_bias:
+            out[m + "self_attn.qkv_proj.bias"] = torch.cat([
+                hf[m + "self_attn.q_proj.bias"].chunk(atp)[ar],
+                hf[m + "self_attn.k_proj.bias"][kv0 * hd:(kv0 + lay.kv_local) * hd],
+                hf[m + "self_attn.v_proj.bias"][kv0 * hd:(kv0 + lay.kv_local) * hd]])
+        out[m + "self_attn.o_proj.weight"] = hf[m + "self_attn.o_proj.weight"].chunk(atp, 1)[ar]
+        for n in ("input_layernorm.weight", "post_attention_layernorm.weight"):
+            out[m + n] = hf[m + n]
+        if arch.qk_norm:
+            out[m + "self_attn.q_norm.weight"] = hf[m + "self_attn.q_norm.weight"]
+            out[m + "self_attn.k_norm.weight"] = hf[m + "self_attn.k_norm.weight"]
+        if arch.is_moe:
+            out[m + "mlp.gate.weight"] = hf[m + "mlp.gate.weight"]
+            E_loc = arch.num_experts // lay.moe_ep
+            w13, w2 = [], []
+            for e in range(E_loc):
+                eg = lay.moe_ep_rank * E_loc + e
+                x = f"{m}mlp.experts.{eg}."
+                t = lay.moe_tp_rank
+                w13.append(torch.cat([hf[x + "gate_proj.weight"].chunk(lay.moe_tp)[t],
+                                      hf[x + "up_proj.weight"].chunk(lay.moe_tp)[t]]))
+                w2.append(hf[x + "down_proj.weight"].chunk(lay.moe_tp, 1)[t])
+            out[m + "mlp.experts.w13_weight"] = torch.stack(w13)
+            out[m + "mlp.experts.w2_weight"] = torch.stack(w2)
+        else:
+            out[m + "mlp.gate_up_proj.weight"] = torch.cat([hf[m + "mlp.gate_proj.weight"].chunk(tp)[r],
+                                                            hf[m + "mlp.up_proj.weight"].chunk(tp)[r]])
+            out[m + "mlp.down_proj.weight"] = hf[m + "mlp.down_proj.weight"].chunk(tp, 1)[r]
+    out["model.norm.weight"] = hf["model.norm.weight"]
+    if not arch.tie_embeddings:
+        out["lm_head.weight"] = vocab(hf["lm_head.weight"])
+    return out
+
+
+SGLANG_CASES = [
+    ("tiny-llama", dict(tp=2)),
+    ("tiny-llama", dict(tp=4)),                 # 2 KV heads on 4 ranks: replication
+    ("tiny-qwen2", dict(tp=2)),
+    ("tiny-qwen3", dict(tp=2, attn_tp=1)),      # DP-attention style: attention unsharded
+    ("tiny-qwen3-moe", dict(tp=2)),
+    ("tiny-qwen3-moe", dict(tp=2, moe_ep=2)),
+]
+
+
+@pytest.mark.parametrize("model,cfg", SGLANG_CASES)
+def test_sglang_fill_matches_oracle(model, cfg):
+    arch = get_arch(model)
+    hf = hf_full(arch)
+    for r in range(cfg["tp"]):
+        kw = dict(cfg, tp_rank=r)
+        if "attn_tp" in kw:
+            kw["attn_tp_rank"] = r % kw["attn_tp"]
+        lay = SGLangLayout(arch, **kw)
+        params = lay.allocate(dtype=torch.float32, fill=True)
+        oracle = sglang_oracle(arch, lay, hf)
+        assert set(params) == set(oracle)
+        for n in params:
+            assert torch.equal(params[n], oracle[n]), n
+
+
+def _host_sync(meg_layouts, sgl_layouts, dtype):
+    senders = []
+    for lay in meg_layouts:
+        params = lay.allocate(dtype=dtype)
+        meta, views = lay.to_wb(params)
+        senders.append((meta, bind(meta, views)))
+    results = []
+    for lay in sgl_layouts:
+        params = lay.allocate(dtype=dtype)
+        meta, views = lay.to_wb(params)
+        rb = bind(meta, views)
+        done = set()
+        for smeta, sb in senders:
+            ov = WeightData.compute_overlap(smeta, meta)
+            if not ov:
+                continue
+            buf = torch.empty(ov.total_nbytes(), dtype=torch.uint8)
+            pack_into(sb, ov, buf)
+            unpack_from(rb, ov, buf)
+            done |= set(ov.names())
+        expected = lay.allocate(dtype=dtype, fill=True)
+        results.append((params, expected, done, meta))
+    return results
+
+
+SYNC_CASES = [
+    ("tiny-llama", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)], [dict(tp=1)]),
+    ("tiny-llama", [dict(tp=1, pp=2, pp_rank=0), dict(tp=1, pp=2, pp_rank=1)], [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)]),
+    ("tiny-llama", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)], [dict(tp=4, tp_rank=i) for i in range(4)]),
+    ("tiny-qwen2", [dict(tp=2, tp_rank=i) for i in range(2)], [dict(tp=1)]),
+    ("tiny-qwen3", [dict(tp=1)], [dict(tp=2, tp_rank=i, attn_tp=1, attn_tp_rank=0) for i in range(2)]),
+    ("tiny-qwen3-moe", [dict(ep=2, ep_rank=i) for i in range(2)], [dict(tp=2, tp_rank=i) for i in range(2)]),
+    ("tiny-qwen3-moe", [dict(ep=2, ep_rank=i) for i in range(2)], [dict(tp=2, tp_rank=i, moe_ep=2) for i in range(2)]),
+]
+
+
+@pytest.mark.parametrize("model,meg,sgl", SYNC_CASES)
+def test_host_reshard_is_bitwise(model, meg, sgl):
+    arch = get_arch(model)
+    res = _host_sync([MegatronLayout(arch, **m) for m in meg], [SGLangLayout(arch, **s) for s in sgl],
+                     torch.float32)
+    for params, expected, done, meta in res:
+        assert done == set(meta.names())
+        for n in params:
+            assert torch.equal(params[n], expected[n]), n
+
+
+def test_sglang_fp8_expert_layout():
+    arch = get_arch("tiny-qwen3-moe")
+    lay = SGLangLayout(arch, tp=2, tp_rank=1, moe_ep=2, quant="fp8_experts")
+    params = lay.allocate(dtype=torch.bfloat16, fill=True)
+    assert params["model.layers.0.mlp.experts.w13_weight"].dtype == torch.float8_e4m3fn
+    s = params["model.layers.0.mlp.experts.w13_weight_scale_inv"]
+    assert s.dtype == torch.float32 and tuple(s.shape) == (4, 4, 2)
+    meta, views = lay.to_wb(params)
+    name = "model.layers.0.mlp.experts.5.up_proj.weight"
+    q = meta.quant(name)
+    assert q["scale"] == name + "_scale_inv" and q["block"] == [128, 128]
+    full = synth_full(name, (256, 256), torch.bfloat16)
+    qv, sv = block_quant_fp8_ref(full)
+    assert torch.equal(views[name].view(torch.uint8), qv.view(torch.uint8))
+    assert torch.equal(views[name + "_scale_inv"], sv)
+
+
+def test_host_reshard_fp8_experts():
+    """bf16 Megatron EP2 -> SGLang TP2 (EP2) with fp8 experts: sender-side block quant."""
+    arch = get_arch("tiny-qwen3-moe")
+    meg = [MegatronLayout(arch, ep=2, ep_rank=i) for i in range(2)]
+    sgl = [SGLangLayout(arch, tp=2, tp_rank=i, moe_ep=2, quant="fp8_experts") for i in range(2)]
+    for params, expected, done, meta in _host_sync(meg, sgl, torch.bfloat16):
+        assert done == set(meta.names())
+        for n in params:
+            assert torch.equal(params[n].view(torch.uint8) if params[n].dtype == torch.float8_e4m3fn else params[n],
+                               expected[n].view(torch.uint8) if expected[n].dtype == torch.float8_e4m3fn else expected[n]), n

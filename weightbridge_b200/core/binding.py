@@ -120,14 +120,26 @@ def _region_views(binding: Binding, name: str, box: Shard, wire: torch.Tensor):
 
 def pack_into(binding: Binding, overlap: WeightData, out: torch.Tensor) -> None:
     """Gather ``overlap``'s regions of the bound tensors into ``out`` (flat uint8)."""
-    from ..ops.quant_ref import convert_region
+    from ..ops.quant_ref import block_quant_fp8_ref, convert_region
+    starts = {name: start for start, _e, name, _s, _d in overlap.iter_with_intv()}
     for start, _end, name, shards, dtype in overlap.iter_with_intv():
+        q = overlap.quant(name)
+        if q and q.get("role") == "scale":
+            continue                     # written together with its quantised weight
         off = start
-        for box in shards:
+        soff = starts.get(q["scale"]) if q else None
+        for bi, box in enumerate(shards):
             n = shard_numel(box)
             seg = out[off:off + n * dtype.itemsize].view(dtype)
             local, packed = _region_views(binding, name, box, seg)
-            if local.dtype == packed.dtype:
+            if q:
+                qv, sv = block_quant_fp8_ref(local.reshape(shard_extents(box)), tuple(q["block"]))
+                packed.copy_(qv.view(packed.shape))
+                sbox = overlap.shards(q["scale"])[bi]
+                ns = shard_numel(sbox)
+                out[soff:soff + ns * 4].view(torch.float32).copy_(sv.reshape(-1))
+                soff += ns * 4
+            elif local.dtype == packed.dtype:
                 packed.copy_(local)
             else:
                 packed.copy_(convert_region(local, packed.dtype))

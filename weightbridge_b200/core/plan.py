@@ -1,0 +1,337 @@
+"""Transfer planner: overlaps between bound shards -> strided ops -> flat device work tables.
+
+A sender binds its local views (absolute addresses); a receiver publishes a *physical
+binding*: for each entry shard, the allocation it lives in (an index into the receiver's
+exported allocation table), the byte offset inside it and the element strides.  With
+both, every overlap becomes one op:
+
+* ``copy``  - same dtype, N-d strided copy (coalesced to as few dims as possible);
+* ``cast``  - float -> float elementwise conversion (fp32 <-> bf16 <-> fp16);
+* ``quant`` - a block-aligned 2-D region quantised to fp8 e4m3 with fp32 block scales
+  written to the receiver's scale tensor.
+
+Ops are lowered to the work tables the sm_100a kernel and the C++ CPU executor walk:
+``ITEM`` rows (one 2-D copy/cast of at most ``item_bytes``) and ``QDESC`` rows (one
+quantised matrix) with one ``QWORK`` row per 128x128 block.  The reference instead packs
+each overlap into a wire buffer with one torch copy per box and sends it over NCCL
+(``wbridge/utils/data.py:240-320``, ``wbridge/backend/direct_sender.py:184-198``).
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import math
+from dataclasses import dataclass, field
+from typing import Any, Callable, Iterable, Sequence
+
+import numpy as np
+import torch
+
+from ..utils.dtypes import FLOAT_CAST_DTYPES, as_dtype, dtype_code, dtype_to_str
+from .binding import Binding
+from .shard import Shard, WeightData, box_copy, coalesce, contiguous_strides, shard_extents, shard_numel
+
+# -- device table layouts (csrc/wb_common.h declares the same structs) ----------------------
+ITEM_DTYPE = np.dtype([
+    ("src", "<u8"), ("dst", "<u8"), ("src_pitch", "<i8"), ("dst_pitch", "<i8"),
+    ("row_bytes", "<u4"), ("rows", "<u4"), ("op", "<u4"), ("dst_row_bytes", "<u4"),
+])
+QDESC_DTYPE = np.dtype([
+    ("src", "<u8"), ("dst", "<u8"), ("scale", "<u8"), ("src_pitch", "<i8"), ("dst_pitch", "<i8"),
+    ("scale_pitch", "<i8"), ("rows", "<u4"), ("cols", "<u4"), ("src_code", "<u4"),
+    ("bn", "<u2"), ("bk", "<u2"),
+])
+QWORK_DTYPE = np.dtype([("desc", "<u4"), ("block", "<u4")])
+assert ITEM_DTYPE.itemsize == 48 and QDESC_DTYPE.itemsize == 64 and QWORK_DTYPE.itemsize == 8
+
+OP_COPY, OP_CAST, OP_COPY_MC = 0, 1, 2
+DEFAULT_ITEM_BYTES = 1 << 19
+
+
+def op_word(kind: int, src: torch.dtype | None = None, dst: torch.dtype | None = None) -> int:
+    w = kind
+    if src is not None:
+        w |= dtype_code(src) << 8
+    if dst is not None:
+        w |= dtype_code(dst) << 16
+    return w
+
+
+# -- physical bindings --------------------------------------------------------------------
+
+@dataclass
+class PhysShard:
+    """Where one entry shard lives: allocation index (-1: ``offset`` is an absolute
+    address in the current process), byte offset, element strides per box dim."""
+    shard: Shard
+    alloc: int
+    offset: int
+    strides: list[int]
+
+    def to_json(self) -> list:
+        return [[list(t) for t in self.shard], self.alloc, self.offset, list(self.strides)]
+
+    @staticmethod
+    def from_json(j) -> "PhysShard":
+        return PhysShard([tuple(t) for t in j[0]], int(j[1]), int(j[2]), [int(s) for s in j[3]])
+
+
+@dataclass
+class PhysBinding:
+    """Serializable description of a rank's bound tensors (address-level)."""
+    meta: WeightData
+    entries: dict[str, list[PhysShard]] = field(default_factory=dict)
+
+    def to_json(self) -> dict:
+        return {"meta": self.meta.to_jsonable(),
+                "entries": {k: [p.to_json() for p in v] for k, v in self.entries.items()}}
+
+    @staticmethod
+    def from_json(j: dict) -> "PhysBinding":
+        return PhysBinding(WeightData(j["meta"]),
+                           {k: [PhysShard.from_json(p) for p in v] for k, v in j["entries"].items()})
+
+
+def phys_binding(binding: Binding, locate: Callable[[int], tuple[int, int]] | None = None) -> PhysBinding:
+    """Physical binding of a local ``Binding``.  ``locate(addr) -> (alloc, offset)`` maps a
+    data pointer into an exported allocation table; without it addresses are absolute."""
+    pb = PhysBinding(binding.meta)
+    for name, views in binding.entries.items():
+        lst = []
+        for bs in views:
+            addr = bs.tensor.data_ptr()
+            alloc, off = locate(addr) if locate is not None else (-1, addr)
+            lst.append(PhysShard(bs.shard, alloc, off, list(bs.strides)))
+        pb.entries[name] = lst
+    return pb
+
+
+def wire_binding(overlap: WeightData, base: int = 0, alloc: int = -1) -> PhysBinding:
+    """Physical binding of a packed wire buffer laid out in ``overlap.iter_with_intv()`` order."""
+    pb = PhysBinding(overlap)
+    for start, _e, name, shards, dtype in overlap.iter_with_intv():
+        off = base + start
+        lst = []
+        for s in shards:
+            lst.append(PhysShard(s, alloc, off, contiguous_strides(shard_extents(s))))
+            off += shard_numel(s) * dtype.itemsize
+        pb.entries[name] = lst
+    return pb
+
+
+# -- ops --------------------------------------------------------------------------------
+
+@dataclass
+class Op:
+    kind: str                     # copy | cast | quant
+    name: str
+    src: tuple[int, int]          # (alloc, byte offset) on the source side
+    dst: tuple[int, int]          # (alloc, byte offset) on the destination side
+    extents: list[int]
+    src_strides: list[int]        # elements
+    dst_strides: list[int]
+    src_dtype: torch.dtype
+    dst_dtype: torch.dtype
+    scale: tuple[int, int] | None = None      # quant: scale tensor start (alloc, byte offset)
+    scale_strides: list[int] | None = None    # quant: element strides of the scale grid
+    block: tuple[int, int] | None = None
+
+    @property
+    def src_bytes(self) -> int:
+        return math.prod(self.extents) * self.src_dtype.itemsize
+
+    @property
+    def dst_bytes(self) -> int:
+        n = math.prod(self.extents) * self.dst_dtype.itemsize
+        if self.kind == "quant":
+            bn, bk = self.block
+            n += math.ceil(self.extents[0] / bn) * math.ceil(self.extents[1] / bk) * 4
+        return n
+
+
+def _shift(p: PhysShard, nbytes: int) -> tuple[int, int]:
+    return (p.alloc, p.offset + nbytes)
+
+
+def plan_pair(src: PhysBinding, dst: PhysBinding, names: Iterable[str] | None = None,
+              overlap_meta: WeightData | None = None) -> list[Op]:
+    """All ops moving the overlap of ``src`` into ``dst`` (optionally restricted to ``names``).
+
+    ``overlap_meta`` (when ``dst`` is a wire buffer) supplies quant specs and the scale
+    entries of the overlap; otherwise they come from ``dst.meta``.
+    """
+    qsrc = overlap_meta if overlap_meta is not None else dst.meta
+    ops: list[Op] = []
+    wanted = set(names) if names is not None else None
+    for name, s_shards, s_dtype in src.meta:
+        if name not in dst.meta or (wanted is not None and name not in wanted):
+            continue
+        d_dtype = dst.meta.dtype(name)
+        q = qsrc.quant(name) if name in qsrc else None
+        if q and q.get("role") == "scale":
+            continue
+        quant = bool(q and q.get("format") == "fp8_block" and d_dtype != s_dtype)
+        if not quant and d_dtype != s_dtype and not (s_dtype in FLOAT_CAST_DTYPES and d_dtype in FLOAT_CAST_DTYPES):
+            raise TypeError(f"{name}: no conversion from {s_dtype} to {d_dtype}")
+        for sp in src.entries[name]:
+            for di, dp in enumerate(dst.entries[name]):
+                try:
+                    bc = box_copy(sp.shard, dp.shard, sp.strides, dp.strides)
+                except ValueError:
+                    raise ValueError(f"shard compatibility check failed for {name}: "
+                                     f"{sp.shard} vs {dp.shard}") from None
+                if bc is None:
+                    continue
+                src_at = _shift(sp, bc.src_offset * s_dtype.itemsize)
+                dst_at = _shift(dp, bc.dst_offset * d_dtype.itemsize)
+                if quant:
+                    ops.append(_quant_op(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst, di, qsrc))
+                    continue
+                e, ss, ds = coalesce(bc.extents, bc.src_strides, bc.dst_strides)
+                ops.append(Op("copy" if s_dtype == d_dtype else "cast", name, src_at, dst_at, e, ss, ds,
+                              s_dtype, d_dtype))
+    return ops
+
+
+def _quant_op(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst: PhysBinding, di: int, qmeta: WeightData) -> Op:
+    if len(bc.extents) != 2:
+        raise ValueError(f"{name}: a block-quantised overlap must be a 2-D region, got {bc.region}")
+    if bc.src_strides[1] != 1 or bc.dst_strides[1] != 1:
+        raise ValueError(f"{name}: quantised rows must be contiguous on both sides")
+    block = tuple(int(b) for b in q["block"])
+    sname = q["scale"]
+    (r0, _r1, _), (c0, _c1, _) = bc.region
+    for (l, r, w), b in zip(bc.region, block):
+        if l % b or (r % b and r != w):
+            raise ValueError(f"{name}: overlap {bc.region} not aligned to {list(block)} blocks")
+    # locate the scale tensor cell of the region's first block on the destination side
+    sregion = [(r0 // block[0], r0 // block[0] + 1, 0), (c0 // block[1], c0 // block[1] + 1, 0)]
+    scale_at, sstr = None, None
+    for sp in dst.entries[sname]:
+        (a0, a1, _), (b0, b1, _) = sp.shard
+        if a0 <= sregion[0][0] < a1 and b0 <= sregion[1][0] < b1:
+            off = (sregion[0][0] - a0) * sp.strides[0] + (sregion[1][0] - b0) * sp.strides[1]
+            scale_at, sstr = (sp.alloc, sp.offset + off * 4), list(sp.strides)
+            break
+    if scale_at is None:
+        raise ValueError(f"{name}: destination has no scale cell for region {bc.region}")
+    return Op("quant", name, src_at, dst_at, list(bc.extents), list(bc.src_strides), list(bc.dst_strides),
+              s_dtype, d_dtype, scale_at, sstr, block)
+
+
+def plan_digest(ops: Sequence[Op] | WeightData) -> str:
+    """Hash of a plan's logical content; both sides compare it at connect."""
+    if isinstance(ops, WeightData):
+        payload = str(ops)
+    else:
+        payload = json.dumps([[o.kind, o.name, o.extents, dtype_to_str(o.src_dtype), dtype_to_str(o.dst_dtype)]
+                              for o in ops])
+    return hashlib.sha256(payload.encode()).hexdigest()[:16]
+
+
+# -- lowering to device tables ------------------------------------------------------------
+
+@dataclass
+class Tables:
+    items: np.ndarray                 # ITEM_DTYPE
+    qdescs: np.ndarray                # QDESC_DTYPE
+    qwork: np.ndarray                 # QWORK_DTYPE
+    bytes_read: int = 0
+    bytes_written: int = 0
+
+    @staticmethod
+    def empty() -> "Tables":
+        return Tables(np.zeros(0, ITEM_DTYPE), np.zeros(0, QDESC_DTYPE), np.zeros(0, QWORK_DTYPE))
+
+    @staticmethod
+    def concat(ts: Sequence["Tables"]) -> "Tables":
+        ts = list(ts)
+        if not ts:
+            return Tables.empty()
+        qd, qw, off = [], [], 0
+        for t in ts:
+            qd.append(t.qdescs)
+            w = t.qwork.copy()
+            w["desc"] += off
+            qw.append(w)
+            off += len(t.qdescs)
+        return Tables(np.concatenate([t.items for t in ts]), np.concatenate(qd), np.concatenate(qw),
+                      sum(t.bytes_read for t in ts), sum(t.bytes_written for t in ts))
+
+    def __len__(self) -> int:
+        return len(self.items) + len(self.qwork)
+
+
+def _split_rows(src, dst, sp, dp, row_bytes, rows, op, drb, item_bytes, out: list):
+    """Append items for ``rows`` rows of ``row_bytes`` (source bytes), at most ``item_bytes`` each."""
+    if rows == 0 or row_bytes == 0:
+        return
+    dst_elem_ratio = drb / row_bytes if row_bytes else 1.0
+    if row_bytes > item_bytes:
+        # long rows: pieces along the row, aligned to 16 bytes on the source side
+        piece = max(16, (item_bytes // 16) * 16)
+        for r in range(rows):
+            off = 0
+            while off < row_bytes:
+                n = min(piece, row_bytes - off)
+                doff = int(off * dst_elem_ratio)
+                dn = int(n * dst_elem_ratio)
+                out.append((src + r * sp + off, dst + r * dp + doff, sp, dp, n, 1, op, dn))
+                off += n
+        return
+    per = max(1, item_bytes // row_bytes)
+    for r0 in range(0, rows, per):
+        n = min(per, rows - r0)
+        out.append((src + r0 * sp, dst + r0 * dp, sp, dp, row_bytes, n, op, drb))
+
+
+def lower_ops(ops: Sequence[Op], src_base: Callable[[int], int], dst_base: Callable[[int], int],
+              item_bytes: int = DEFAULT_ITEM_BYTES, multicast: bool = False) -> Tables:
+    """Resolve allocation indices to addresses and cut ops into device work rows."""
+    items: list[tuple] = []
+    qdescs: list[tuple] = []
+    qwork: list[np.ndarray] = []
+    rd = wr = 0
+    for o in ops:
+        s_addr = src_base(o.src[0]) + o.src[1]
+        d_addr = dst_base(o.dst[0]) + o.dst[1]
+        se, de = o.src_dtype.itemsize, o.dst_dtype.itemsize
+        rd += o.src_bytes
+        wr += o.dst_bytes
+        if o.kind == "quant":
+            rows, cols = o.extents
+            bn, bk = o.block
+            sc = dst_base(o.scale[0]) + o.scale[1]
+            qdescs.append((s_addr, d_addr, sc, o.src_strides[0] * se, o.dst_strides[0] * de,
+                           o.scale_strides[0] * 4, rows, cols, dtype_code(o.src_dtype), bn, bk))
+            nb = math.ceil(rows / bn) * math.ceil(cols / bk)
+            w = np.zeros(nb, QWORK_DTYPE)
+            w["desc"] = len(qdescs) - 1
+            w["block"] = np.arange(nb, dtype=np.uint32)
+            qwork.append(w)
+            continue
+        kind = OP_COPY if o.kind == "copy" else OP_CAST
+        if multicast:
+            kind = OP_COPY_MC
+        word = op_word(kind, o.src_dtype, o.dst_dtype)
+        ext, ss, ds = list(o.extents), list(o.src_strides), list(o.dst_strides)
+        if ss[-1] == 1 and ds[-1] == 1:
+            run = ext.pop()
+            ss.pop(); ds.pop()
+        else:
+            run = 1
+        rb, drb = run * se, run * de
+        if not ext:
+            _split_rows(s_addr, d_addr, rb, drb, rb, 1, word, drb, item_bytes, items)
+            continue
+        rows = ext[-1]
+        sp, dp = ss[-1] * se, ds[-1] * de
+        outer = ext[:-1]
+        for idx in np.ndindex(*outer) if outer else [()]:
+            so = sum(i * s for i, s in zip(idx, ss[:-1])) * se
+            do = sum(i * s for i, s in zip(idx, ds[:-1])) * de
+            _split_rows(s_addr + so, d_addr + do, sp, dp, rb, rows, word, drb, item_bytes, items)
+    it = np.array(items, dtype=ITEM_DTYPE) if items else np.zeros(0, ITEM_DTYPE)
+    qd = np.array(qdescs, dtype=QDESC_DTYPE) if qdescs else np.zeros(0, QDESC_DTYPE)
+    qw = np.concatenate(qwork) if qwork else np.zeros(0, QWORK_DTYPE)
+    return Tables(it, qd, qw, rd, wr)

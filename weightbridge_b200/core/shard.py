@@ -245,6 +245,19 @@ def box_copy(src_shard: Shard, dst_shard: Shard,
     return BoxCopy(src_off, dst_off, ext, ss, ds, region)
 
 
+def scale_box(region: Shard, block: Sequence[int], name: str = "") -> Shard:
+    """Block-scale coordinates of a block-aligned 2-D region of a quantised tensor."""
+    if len(region) != 2:
+        raise ValueError(f"{name}: a block-quantised overlap must be 2-D, got {region}")
+    out = []
+    for (l, r, w), b in zip(region, block):
+        if l % b or (r % b and r != w):
+            raise ValueError(f"{name}: overlap {region} is not aligned to the {list(block)} blocks; "
+                             f"each block must come from one sender")
+        out.append((l // b, (r + b - 1) // b, (w + b - 1) // b))
+    return out
+
+
 def coalesce(extents: Sequence[int], src_strides: Sequence[int], dst_strides: Sequence[int]
              ) -> tuple[list[int], list[int], list[int]]:
     """Drop extent-1 dims and merge neighbours that are contiguous on both sides."""
@@ -410,8 +423,14 @@ class WeightData:
                 entry: dict[str, Any] = {"shard": boxes, "dtype": s_dtype}
                 if r_dtype != s_dtype:
                     entry = {"shard": boxes, "dtype": r_dtype, "src_dtype": s_dtype}
-                    if receiver.quant(name):
-                        entry["quant"] = receiver.quant(name)
+                    q = receiver.quant(name)
+                    if q and q.get("format") == "fp8_block":
+                        entry["quant"] = q
+                        result[name] = entry
+                        result[q["scale"]] = {
+                            "shard": [scale_box(b, q["block"], name) for b in boxes],
+                            "dtype": torch.float32, "quant": {"role": "scale", "of": name}}
+                        continue
                 result[name] = entry
         return WeightData(result)
 

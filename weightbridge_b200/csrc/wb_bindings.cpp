@@ -1,0 +1,113 @@
+// Python bindings of the native runtime (module weightbridge_b200._C).
+// Device tables and buffers are passed as integer addresses (tensor.data_ptr()), streams as
+// cudaStream_t handles (torch.cuda.Stream.cuda_stream).
+#include <torch/extension.h>
+
+#include <cuda_runtime.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "wb_common.h"
+#include "wb_cpu.h"
+#include "wb_ipc.h"
+#include "wb_transfer.h"
+
+namespace py = pybind11;
+
+namespace {
+
+template <typename T>
+T* P(uint64_t a) {
+  return reinterpret_cast<T*>(a);
+}
+
+void check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+void transfer(uint64_t items, uint32_t n_items, uint64_t bulk, uint32_t n_bulk, uint64_t qdescs, uint64_t qwork,
+              uint32_t n_qwork, uint32_t piece_bytes, uint32_t spin_limit, uint64_t counter, uint64_t flags,
+              uint32_t n_flags, uint64_t epoch, uint64_t status, int mode, int grid, uint64_t stream) {
+  if (mode == 0 && n_bulk) throw std::invalid_argument("bulk items need a TMA mode (1-3)");
+  if (piece_bytes % 16) throw std::invalid_argument("piece_bytes must be a multiple of 16");
+  wb::TransferArgs a{};
+  a.items = P<const wb::Item>(items);
+  a.n_items = n_items;
+  a.bulk_items = P<const wb::Item>(bulk);
+  a.n_bulk = n_bulk;
+  a.qdescs = P<const wb::QuantDesc>(qdescs);
+  a.qwork = P<const wb::QuantWork>(qwork);
+  a.n_qwork = n_qwork;
+  a.piece_bytes = piece_bytes;
+  a.mbar_spin_limit = spin_limit;
+  a.sig.counter = P<uint32_t>(counter);
+  a.sig.flag_addrs = P<const uint64_t>(flags);
+  a.sig.n_flags = n_flags;
+  a.sig.epoch = P<const uint64_t>(epoch);
+  a.sig.status = P<uint32_t>(status);
+  if (a.sig.counter && !a.sig.epoch) throw std::invalid_argument("a completion signal needs an epoch word");
+  check(wb::launch_transfer(a, mode, grid, reinterpret_cast<cudaStream_t>(stream)), "transfer launch");
+}
+
+void wait_flags(uint64_t flags, uint32_t n, uint64_t epoch, uint64_t timeout_ns, uint64_t status, uint64_t where,
+                uint64_t stream) {
+  check(wb::launch_wait_flags(P<const uint64_t>(flags), n, P<const uint64_t>(epoch), timeout_ns, P<uint32_t>(status),
+                              P<uint32_t>(where), reinterpret_cast<cudaStream_t>(stream)),
+        "wait_flags launch");
+}
+
+void cpu_execute(uint64_t items, size_t n_items, uint64_t qdescs, uint64_t qwork, size_t n_qwork) {
+  py::gil_scoped_release nogil;
+  wb::cpu_execute(P<const wb::Item>(items), n_items, P<const wb::QuantDesc>(qdescs), P<const wb::QuantWork>(qwork),
+                  n_qwork);
+}
+
+int num_sms(int device) {
+  int v = 0;
+  check(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device), "cudaDeviceGetAttribute");
+  return v;
+}
+
+py::tuple vmm_tuple(const wb::VmmAlloc& a) { return py::make_tuple(a.ptr, a.size, a.handle); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "weightbridge_b200 native runtime: sm_100a transfer kernel, CPU executor, IPC/VMM/multicast";
+  m.def("transfer", &transfer, "launch the persistent transfer kernel");
+  m.def("wait_flags", &wait_flags, "launch a bounded wait on flag words");
+  m.def("bulk_stages", &wb::bulk_stages);
+  m.def("cpu_execute", &cpu_execute, "run work tables on the host");
+  m.def("num_sms", &num_sms);
+  m.def("addr_range", [](uint64_t p) {
+    auto r = wb::addr_range(p);
+    return py::make_tuple(r.base, r.size);
+  });
+  m.def("ipc_handle", [](uint64_t base) { return py::bytes(wb::ipc_handle(base)); });
+  m.def("ipc_open", [](py::bytes h) { return wb::ipc_open(std::string(h)); });
+  m.def("ipc_close", &wb::ipc_close);
+  m.def("device_uuid", [](int d) { return py::bytes(wb::device_uuid(d)); });
+  m.def("can_access_peer", &wb::can_access_peer);
+  m.def("enable_peer_access", &wb::enable_peer_access);
+  m.def("vmm_granularity", &wb::vmm_granularity);
+  m.def("vmm_alloc", [](size_t size, int dev) { return vmm_tuple(wb::vmm_alloc(size, dev)); });
+  m.def("vmm_export_fd", &wb::vmm_export_fd);
+  m.def("vmm_import_fd", [](int fd, size_t size, int dev) { return vmm_tuple(wb::vmm_import_fd(fd, size, dev)); });
+  m.def("vmm_free", [](uint64_t ptr, uint64_t size, uint64_t handle) { wb::vmm_free(wb::VmmAlloc{ptr, size, handle}); });
+  m.def("multicast_supported", &wb::multicast_supported);
+  m.def("mc_create", &wb::mc_create);
+  m.def("mc_import_fd", &wb::mc_import_fd);
+  m.def("mc_add_device", &wb::mc_add_device);
+  m.def("mc_bind_mem", &wb::mc_bind_mem);
+  m.def("mc_unbind", &wb::mc_unbind);
+  m.def("mc_map", [](uint64_t mc, size_t size, int dev) { return vmm_tuple(wb::mc_map(mc, size, dev)); });
+  m.attr("ITEM_SIZE") = (int)sizeof(wb::Item);
+  m.attr("QDESC_SIZE") = (int)sizeof(wb::QuantDesc);
+  m.attr("QWORK_SIZE") = (int)sizeof(wb::QuantWork);
+  m.attr("ST_MBAR_TIMEOUT") = (int)wb::ST_MBAR_TIMEOUT;
+  m.attr("ST_FLAG_TIMEOUT") = (int)wb::ST_FLAG_TIMEOUT;
+  m.attr("ST_FLAG_STALE") = (int)wb::ST_FLAG_STALE;
+  m.attr("ST_BAD_ITEM") = (int)wb::ST_BAD_ITEM;
+  m.attr("ST_BAD_QUANT") = (int)wb::ST_BAD_QUANT;
+}

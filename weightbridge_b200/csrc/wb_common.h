@@ -1,0 +1,74 @@
+// Work-table layouts shared by the sm_100a transfer kernel, the CPU executor and the
+// Python planner (weightbridge_b200/core/plan.py declares the same byte layouts).
+#pragma once
+#include <cstdint>
+
+#if defined(__CUDACC__)
+#define WB_HD __host__ __device__
+#else
+#define WB_HD
+#endif
+
+namespace wb {
+
+// dtype wire codes (weightbridge_b200/utils/dtypes.py: DTYPE_CODES)
+enum DType : uint32_t {
+  DT_U8 = 0, DT_I8 = 1, DT_F16 = 2, DT_BF16 = 3, DT_F32 = 4, DT_E4M3 = 5,
+  DT_I32 = 6, DT_I64 = 7, DT_F64 = 8, DT_BOOL = 9, DT_I16 = 10, DT_E5M2 = 11,
+};
+
+// op word: bits 0-7 kind, 8-15 source dtype, 16-23 destination dtype
+enum OpKind : uint32_t { OP_COPY = 0, OP_CAST = 1, OP_COPY_MC = 2 };
+
+inline WB_HD uint32_t op_kind(uint32_t w) { return w & 0xffu; }
+inline WB_HD uint32_t op_src(uint32_t w) { return (w >> 8) & 0xffu; }
+inline WB_HD uint32_t op_dst(uint32_t w) { return (w >> 16) & 0xffu; }
+
+// One unit of copy work: `rows` rows of `row_bytes` source bytes.
+struct alignas(16) Item {
+  uint64_t src;
+  uint64_t dst;
+  int64_t src_pitch;       // bytes between source rows
+  int64_t dst_pitch;       // bytes between destination rows
+  uint32_t row_bytes;      // source bytes per row
+  uint32_t rows;
+  uint32_t op;             // op word
+  uint32_t dst_row_bytes;  // destination bytes per row (differs from row_bytes for casts)
+};
+static_assert(sizeof(Item) == 48, "Item layout");
+
+// One block-quantised matrix: rows x cols source elements -> e4m3 + fp32 block scales.
+struct alignas(16) QuantDesc {
+  uint64_t src;
+  uint64_t dst;
+  uint64_t scale;
+  int64_t src_pitch;       // bytes
+  int64_t dst_pitch;       // bytes
+  int64_t scale_pitch;     // bytes between scale rows; scale columns are contiguous fp32
+  uint32_t rows;
+  uint32_t cols;
+  uint32_t src_code;       // DT_BF16 / DT_F16 / DT_F32
+  uint16_t bn;             // block rows
+  uint16_t bk;             // block cols
+};
+static_assert(sizeof(QuantDesc) == 64, "QuantDesc layout");
+
+struct QuantWork {
+  uint32_t desc;
+  uint32_t block;          // row-major block index inside the matrix
+};
+static_assert(sizeof(QuantWork) == 8, "QuantWork layout");
+
+// Status bits a kernel reports through its status word.
+enum Status : uint32_t {
+  ST_OK = 0,
+  ST_MBAR_TIMEOUT = 1u << 0,   // a TMA load never completed within the wait limit
+  ST_FLAG_TIMEOUT = 1u << 1,   // a peer's flag never reached the expected epoch
+  ST_FLAG_STALE = 1u << 2,     // a flag holds an epoch other than the expected one
+  ST_BAD_ITEM = 1u << 3,       // an item violated the kernel's alignment contract
+  ST_BAD_QUANT = 1u << 4,      // a quant descriptor the kernel cannot handle
+};
+
+constexpr float kE4M3Max = 448.0f;
+
+}  // namespace wb

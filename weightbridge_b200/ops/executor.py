@@ -1,0 +1,144 @@
+"""Launchers for the work tables: the sm_100a transfer kernel and the C++ CPU executor.
+
+``TransferProgram`` keeps one sender's tables resident on its GPU (uploaded once at
+connect), plus the completion state of the launch: a scratch counter, the table of flag
+addresses the last CTA publishes to, the epoch word (copied host->device from pinned
+memory on every sync) and a status word.  A sync is then a single kernel launch.
+"""
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ..core.plan import ITEM_DTYPE, OP_COPY, QDESC_DTYPE, QWORK_DTYPE, Tables
+from ._ext import ext
+
+# TMA pipeline modes of the kernel (stages x piece bytes of shared memory per CTA)
+MODE_VECTOR, MODE_BULK8, MODE_BULK12, MODE_BULK4 = 0, 1, 2, 3
+DEFAULT_SPIN_LIMIT = 1 << 26
+
+
+def _np_to_tensor(a: np.ndarray, device) -> torch.Tensor:
+    if len(a) == 0:
+        return torch.zeros(16, dtype=torch.uint8, device=device)
+    t = torch.from_numpy(np.ascontiguousarray(a).view(np.uint8).copy())
+    return t.to(device)
+
+
+def bulk_eligible(items: np.ndarray) -> np.ndarray:
+    """Items the TMA pipeline may move: plain copies, 16-byte aligned everywhere."""
+    bits = (items["src"] | items["dst"] | items["src_pitch"].astype(np.uint64)
+            | items["dst_pitch"].astype(np.uint64) | items["row_bytes"].astype(np.uint64))
+    return ((items["op"] & 0xFF) == OP_COPY) & ((bits & np.uint64(15)) == 0)
+
+
+def cpu_execute(tables: Tables) -> None:
+    """Run work tables on the host (addresses are host pointers)."""
+    it = np.ascontiguousarray(tables.items)
+    qd = np.ascontiguousarray(tables.qdescs)
+    qw = np.ascontiguousarray(tables.qwork)
+    ext().cpu_execute(it.ctypes.data if len(it) else 0, len(it), qd.ctypes.data if len(qd) else 0,
+                      qw.ctypes.data if len(qw) else 0, len(qw))
+
+
+@dataclass
+class LaunchConfig:
+    mode: int = MODE_BULK8
+    piece_bytes: int = 16384
+    grid: int | None = None
+    spin_limit: int = DEFAULT_SPIN_LIMIT
+
+    @staticmethod
+    def from_env() -> "LaunchConfig":
+        c = LaunchConfig()
+        c.mode = int(os.environ.get("WBRIDGE_KERNEL_MODE", c.mode))
+        c.piece_bytes = int(os.environ.get("WBRIDGE_PIECE_BYTES", c.piece_bytes))
+        g = os.environ.get("WBRIDGE_GRID")
+        c.grid = int(g) if g else None
+        return c
+
+
+class TransferProgram:
+    """Device-resident tables of one sender plus its completion signal."""
+
+    def __init__(self, tables: Tables, device: torch.device | int | str,
+                 flag_addrs: list[int] | None = None, config: LaunchConfig | None = None):
+        self.device = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
+        self.config = config or LaunchConfig.from_env()
+        self.tables = tables
+        items = tables.items
+        if self.config.mode != MODE_VECTOR and len(items):
+            mask = bulk_eligible(items)
+            self.bulk_np, self.items_np = items[mask], items[~mask]
+        else:
+            self.bulk_np, self.items_np = items[:0], items
+        dev = self.device
+        self.items = _np_to_tensor(self.items_np, dev)
+        self.bulk = _np_to_tensor(self.bulk_np, dev)
+        self.qdescs = _np_to_tensor(tables.qdescs, dev)
+        self.qwork = _np_to_tensor(tables.qwork, dev)
+        flag_addrs = list(flag_addrs or [])
+        self.n_flags = len(flag_addrs)
+        self.flags = torch.tensor(flag_addrs or [0], dtype=torch.int64, device=dev)
+        self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.epoch_dev = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.epoch_host = torch.zeros(1, dtype=torch.int64, pin_memory=True)
+        self.n_sms = ext().num_sms(dev.index if dev.index is not None else torch.cuda.current_device())
+        self.launches = 0
+
+    @property
+    def bytes_read(self) -> int:
+        return self.tables.bytes_read
+
+    @property
+    def bytes_written(self) -> int:
+        return self.tables.bytes_written
+
+    def grid(self) -> int:
+        c = self.config
+        if c.grid:
+            return c.grid
+        work = len(self.items_np) + len(self.tables.qwork) + len(self.bulk_np)
+        if c.mode == MODE_VECTOR:
+            per_sm = 4
+        else:
+            smem = ext().bulk_stages(c.mode) * c.piece_bytes
+            per_sm = max(1, min(4, (200 * 1024) // max(smem, 1)))
+        return max(1, min(work, self.n_sms * per_sm))
+
+    def launch(self, epoch: int, stream: torch.cuda.Stream | None = None) -> None:
+        """Copy the epoch host->device and launch the kernel on ``stream``."""
+        stream = stream or torch.cuda.current_stream(self.device)
+        c = self.config
+        with torch.cuda.stream(stream):
+            self.epoch_host[0] = epoch
+            self.epoch_dev.copy_(self.epoch_host, non_blocking=True)
+            ext().transfer(
+                self.items.data_ptr(), len(self.items_np), self.bulk.data_ptr(), len(self.bulk_np),
+                self.qdescs.data_ptr(), self.qwork.data_ptr(), len(self.tables.qwork),
+                c.piece_bytes, c.spin_limit, self.counter.data_ptr(),
+                self.flags.data_ptr() if self.n_flags else 0, self.n_flags,
+                self.epoch_dev.data_ptr(), self.status.data_ptr(), c.mode if len(self.bulk_np) else MODE_VECTOR,
+                self.grid(), stream.cuda_stream)
+        self.launches += 1
+
+    def read_status(self) -> int:
+        return int(self.status.item())
+
+    def clear_status(self) -> None:
+        self.status.zero_()
+
+
+def wait_flags(flags: torch.Tensor, epoch: torch.Tensor, timeout_s: float, status: torch.Tensor,
+               where: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> None:
+    """Launch a bounded device-side wait until every flag word reaches ``epoch[0]``; on
+    timeout the kernel sets ST_FLAG_TIMEOUT in ``status`` (and the first index in ``where``)
+    and returns.  Only for flags written by another GPU: two kernels on one GPU that wait
+    on each other have no co-scheduling guarantee."""
+    stream = stream or torch.cuda.current_stream(flags.device)
+    ext().wait_flags(flags.data_ptr(), flags.numel(), epoch.data_ptr(), int(timeout_s * 1e9), status.data_ptr(),
+                     where.data_ptr() if where is not None else 0, stream.cuda_stream)

@@ -1,0 +1,322 @@
+"""SGLang rollout layout -> logical HF boxes bound to views of SGLang's fused parameters.
+
+SGLang stores ``qkv_proj`` as ``[q_local; k_local; v_local]`` (QKVParallelLinear), fuses
+``gate_up_proj`` as ``[gate_local; up_local]``, pads the vocab of ``embed_tokens`` /
+``lm_head`` and, for MoE, keeps all local experts in ``experts.w13_weight`` ``[E_loc,
+2*I_loc, H]`` and ``experts.w2_weight`` ``[E_loc, H, I_loc]``.  With block fp8 the
+weights are ``float8_e4m3fn`` and each has an fp32 ``*_scale_inv`` of 128 x 128 block
+scales.  Attention may use its own TP size (DP-attention); when TP exceeds the KV-head
+count each rank holds one replicated KV head.
+
+Parity: the routing and the column/row partition rules follow
+``wbridge/utils/sglang_utils/qwen2.py:1-173`` and ``sglang_utils/__init__.py:15-52``.
+Differences: the q/k/v split uses SGLang's ``[q; k; v]`` order rather than a grouped
+interleave, the bias split uses element sizes, the receiver gets views into its own fused
+buffers (the reference only returns metadata), KV-head replication and MoE/fp8 are added.
+"""
+from __future__ import annotations
+
+import re
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+
+from ..core.shard import WeightData
+from ..models.arch import ModelArch
+from ..models.synthetic import synth_fill
+from ..ops.quant_ref import block_quant_fp8_ref
+
+SKIP_PATTERNS = ("inv_freq", "cos_cached", "sin_cached", "projector", "vision_tower")
+
+
+@dataclass
+class SGLangLayout:
+    arch: ModelArch
+    tp: int = 1
+    tp_rank: int = 0
+    attn_tp: int | None = None
+    attn_tp_rank: int | None = None
+    moe_ep: int = 1                      # experts split over moe_ep of the tp ranks
+    quant: str | None = None             # None | "fp8_experts" | "fp8_linear"
+    block: tuple[int, int] = (128, 128)
+    vocab_pad_multiple: int = 64
+
+    def __post_init__(self):
+        if self.attn_tp is None:
+            self.attn_tp = self.tp
+        if self.attn_tp_rank is None:
+            self.attn_tp_rank = self.tp_rank % self.attn_tp
+        a = self.arch
+        if a.num_heads % self.attn_tp:
+            raise ValueError("num_heads not divisible by attention TP")
+        if a.num_kv_heads >= self.attn_tp and a.num_kv_heads % self.attn_tp:
+            raise ValueError("num_kv_heads not divisible by attention TP")
+        if a.num_kv_heads < self.attn_tp and self.attn_tp % a.num_kv_heads:
+            raise ValueError("attention TP not a multiple of num_kv_heads")
+        if a.is_moe:
+            if self.tp % self.moe_ep or a.num_experts % self.moe_ep:
+                raise ValueError("moe_ep must divide TP and the expert count")
+            if a.moe_ffn % self.moe_tp:
+                raise ValueError("expert FFN not divisible by the MoE TP size")
+        if self.quant not in (None, "fp8_experts", "fp8_linear"):
+            raise ValueError(f"unknown quant mode {self.quant!r}")
+
+    # -- sizes ------------------------------------------------------------------------
+    @property
+    def moe_tp(self) -> int:
+        return self.tp // self.moe_ep
+
+    @property
+    def moe_tp_rank(self) -> int:
+        return self.tp_rank % self.moe_tp
+
+    @property
+    def moe_ep_rank(self) -> int:
+        return self.tp_rank // self.moe_tp
+
+    @property
+    def padded_vocab(self) -> int:
+        m = self.vocab_pad_multiple
+        v = (self.arch.vocab + m - 1) // m * m
+        if v % self.tp:
+            v = (v + self.tp - 1) // self.tp * self.tp
+        return v
+
+    @property
+    def kv_local(self) -> int:
+        return max(1, self.arch.num_kv_heads // self.attn_tp)
+
+    @property
+    def kv_head0(self) -> int:
+        a = self.arch
+        if a.num_kv_heads >= self.attn_tp:
+            return self.attn_tp_rank * self.kv_local
+        return self.attn_tp_rank * a.num_kv_heads // self.attn_tp
+
+    def _fp8(self, kind: str) -> bool:
+        return (self.quant == "fp8_linear" and kind in ("linear", "expert")) or \
+               (self.quant == "fp8_experts" and kind == "expert")
+
+    def _scales(self, rows: int, cols: int) -> tuple[int, int]:
+        bn, bk = self.block
+        return (rows + bn - 1) // bn, (cols + bk - 1) // bk
+
+    def param_specs(self) -> dict[str, tuple[tuple[int, ...], str]]:
+        """SGLang parameter name -> (local shape, kind); kind in linear|expert|scale|other."""
+        a = self.arch
+        H, hd = a.hidden, a.head_dim
+        q_loc = a.num_heads // self.attn_tp * hd
+        kv_loc = self.kv_local * hd
+        out: dict[str, tuple[tuple[int, ...], str]] = {}
+        V = self.padded_vocab // self.tp
+        out["model.embed_tokens.weight"] = ((V, H), "other")
+        for i in range(a.num_layers):
+            p = f"model.layers.{i}."
+            out[p + "input_layernorm.weight"] = ((H,), "other")
+            out[p + "self_attn.qkv_proj.weight"] = ((q_loc + 2 * kv_loc, H), "linear")
+            if a.qkv_bias:
+                out[p + "self_attn.qkv_proj.bias"] = ((q_loc + 2 * kv_loc,), "other")
+            if a.qk_norm:
+                out[p + "self_attn.q_norm.weight"] = ((hd,), "other")
+                out[p + "self_attn.k_norm.weight"] = ((hd,), "other")
+            out[p + "self_attn.o_proj.weight"] = ((H, q_loc), "linear")
+            out[p + "post_attention_layernorm.weight"] = ((H,), "other")
+            if a.is_moe:
+                E_loc = a.num_experts // self.moe_ep
+                I_loc = a.moe_ffn // self.moe_tp
+                out[p + "mlp.gate.weight"] = ((a.num_experts, H), "other")
+                out[p + "mlp.experts.w13_weight"] = ((E_loc, 2 * I_loc, H), "expert")
+                out[p + "mlp.experts.w2_weight"] = ((E_loc, H, I_loc), "expert")
+            else:
+                F_loc = a.ffn // self.tp
+                out[p + "mlp.gate_up_proj.weight"] = ((2 * F_loc, H), "linear")
+                out[p + "mlp.down_proj.weight"] = ((H, F_loc), "linear")
+        out["model.norm.weight"] = ((H,), "other")
+        if not a.tie_embeddings:
+            out["lm_head.weight"] = ((V, H), "other")
+        for name, (shape, kind) in list(out.items()):
+            if self._fp8(kind):
+                lead, (r, c) = shape[:-2], shape[-2:]
+                out[name + "_scale_inv"] = (tuple(lead) + self._scales(r, c), "scale")
+        return out
+
+    def param_dtype(self, name: str, kind: str, dtype: torch.dtype) -> torch.dtype:
+        if kind == "scale":
+            return torch.float32
+        if self._fp8(kind):
+            return torch.float8_e4m3fn
+        return dtype
+
+    def allocate(self, device="cpu", dtype=torch.bfloat16, fill: bool = False, seed: int = 0
+                 ) -> dict[str, torch.Tensor]:
+        """Allocate this rank's parameters (zeros); ``fill`` writes the expected synthetic
+        weights (quantised where the layout is fp8), i.e. what a sync should produce."""
+        params = {n: torch.zeros(s, dtype=self.param_dtype(n, k, dtype), device=device)
+                  for n, (s, k) in self.param_specs().items()}
+        if fill:
+            self.fill_expected(params, seed)
+        return params
+
+    def fill_expected(self, params: dict[str, torch.Tensor], seed: int = 0) -> None:
+        meta, views = self.to_wb(params)
+        for name, shards, dtype in meta:
+            q = meta.quant(name)
+            if q and q.get("role") == "scale":
+                continue
+            box = shards[0]
+            if q:
+                src = torch.empty([r - l for l, r, _ in box], dtype=torch.bfloat16, device=views[name].device)
+                synth_fill(src, name, box, seed=seed)
+                qv, sv = block_quant_fp8_ref(src, tuple(q["block"]))
+                views[name].copy_(qv)
+                views[q["scale"]].copy_(sv)
+            else:
+                synth_fill(views[name], name, box, seed=seed)
+
+    # -- conversion ------------------------------------------------------------------------
+    def split_param(self, name: str, param: torch.Tensor, scale: torch.Tensor | None = None
+                    ) -> list[tuple[str, torch.Tensor, list, dict | None]]:
+        """One SGLang param -> [(hf_name, view, box, quant)] (quant: None or the fp8 spec)."""
+        a = self.arch
+        H, hd = a.hidden, a.head_dim
+        full = lambda shape: [(0, d, d) for d in shape]
+        bn, bk = self.block
+
+        def q_spec(hf: str) -> dict:
+            return {"format": "fp8_block", "block": [bn, bk], "scale": hf + "_scale_inv"}
+
+        def with_scale(hf, view, box, sview, sbox):
+            if scale is None:
+                return [(hf, view, box, None)]
+            return [(hf, view, box, q_spec(hf)),
+                    (hf + "_scale_inv", sview, sbox, {"role": "scale", "of": hf})]
+
+        def block_box(box):
+            out = []
+            for (l, r, w), b in zip(box, (bn, bk)):
+                if l % b or (r % b and r != w):
+                    raise ValueError(f"fp8 block {self.block} not aligned with box {box}")
+                out.append((l // b, (r + b - 1) // b, (w + b - 1) // b))
+            return out
+
+        if name in ("model.embed_tokens.weight", "lm_head.weight"):
+            rows = self.padded_vocab // self.tp
+            l, r = self.tp_rank * rows, min((self.tp_rank + 1) * rows, a.vocab)
+            if l >= a.vocab:
+                return []
+            return [(name, param[: r - l], [(l, r, a.vocab), (0, H, H)], None)]
+        if name == "model.norm.weight":
+            return [(name, param, full(param.shape), None)]
+        m = re.match(r"model\.layers\.(\d+)\.(.+)", name)
+        if not m:
+            raise ValueError(f"unknown SGLang parameter {name!r}")
+        p = f"model.layers.{m.group(1)}."
+        rest = m.group(2)
+        q_loc = a.num_heads // self.attn_tp * hd
+        kv_loc = self.kv_local * hd
+        ar = self.attn_tp_rank
+        qbox = (ar * q_loc, (ar + 1) * q_loc, a.num_heads * hd)
+        kvbox = (self.kv_head0 * hd, self.kv_head0 * hd + kv_loc, a.num_kv_heads * hd)
+
+        if rest == "self_attn.qkv_proj.weight":
+            parts = [("q_proj", 0, q_loc, qbox), ("k_proj", q_loc, kv_loc, kvbox),
+                     ("v_proj", q_loc + kv_loc, kv_loc, kvbox)]
+            out = []
+            for nm, r0, n, box in parts:
+                b2 = [box, (0, H, H)]
+                sv = sb = None
+                if scale is not None:
+                    sb = block_box(b2)
+                    sv = scale[r0 // bn:(r0 + n + bn - 1) // bn]
+                out += with_scale(f"{p}self_attn.{nm}.weight", param[r0:r0 + n], b2, sv, sb)
+            return out
+        if rest == "self_attn.qkv_proj.bias":
+            return [(f"{p}self_attn.q_proj.bias", param[:q_loc], [qbox], None),
+                    (f"{p}self_attn.k_proj.bias", param[q_loc:q_loc + kv_loc], [kvbox], None),
+                    (f"{p}self_attn.v_proj.bias", param[q_loc + kv_loc:], [kvbox], None)]
+        if rest == "self_attn.o_proj.weight":
+            box = [(0, H, H), qbox]
+            return with_scale(name, param, box, scale, block_box(box) if scale is not None else None)
+        if rest == "mlp.gate_up_proj.weight":
+            f = a.ffn // self.tp
+            fbox = (self.tp_rank * f, (self.tp_rank + 1) * f, a.ffn)
+            box = [fbox, (0, H, H)]
+            out = []
+            for j, nm in enumerate(("gate_proj", "up_proj")):
+                sv = sb = None
+                if scale is not None:
+                    sb = block_box(box)
+                    if f % bn:
+                        raise ValueError("gate/up split not aligned with the fp8 block")
+                    sv = scale[j * f // bn:(j + 1) * f // bn]
+                out += with_scale(f"{p}mlp.{nm}.weight", param[j * f:(j + 1) * f], box, sv, sb)
+            return out
+        if rest == "mlp.down_proj.weight":
+            f = a.ffn // self.tp
+            box = [(0, H, H), (self.tp_rank * f, (self.tp_rank + 1) * f, a.ffn)]
+            return with_scale(name, param, box, scale, block_box(box) if scale is not None else None)
+        if rest in ("mlp.experts.w13_weight", "mlp.experts.w2_weight"):
+            E_loc = a.num_experts // self.moe_ep
+            I = a.moe_ffn
+            i_loc = I // self.moe_tp
+            ibox = (self.moe_tp_rank * i_loc, (self.moe_tp_rank + 1) * i_loc, I)
+            out = []
+            for e in range(E_loc):
+                eg = self.moe_ep_rank * E_loc + e
+                q = f"{p}mlp.experts.{eg}."
+                if rest.endswith("w13_weight"):
+                    if scale is not None and i_loc % bn:
+                        raise ValueError("w13 gate/up split not aligned with the fp8 block")
+                    for j, nm in enumerate(("gate_proj", "up_proj")):
+                        box = [ibox, (0, H, H)]
+                        sv = scale[e, j * i_loc // bn:(j + 1) * i_loc // bn] if scale is not None else None
+                        out += with_scale(q + nm + ".weight", param[e, j * i_loc:(j + 1) * i_loc], box, sv,
+                                          block_box(box) if scale is not None else None)
+                else:
+                    box = [(0, H, H), ibox]
+                    out += with_scale(q + "down_proj.weight", param[e], box,
+                                      scale[e] if scale is not None else None,
+                                      block_box(box) if scale is not None else None)
+            return out
+        # replicated tensors: norms, router, q/k norm
+        return [(name, param, full(param.shape), None)]
+
+    def to_wb(self, params: dict[str, torch.Tensor]) -> tuple[WeightData, dict[str, torch.Tensor]]:
+        """(metadata, HF name -> view) for this rank's SGLang parameters.  fp8 entries carry
+        ``quant`` and their scale views appear as ``<name>_scale_inv`` entries."""
+        meta: dict[str, dict[str, Any]] = {}
+        views: dict[str, torch.Tensor] = {}
+        for name, param in params.items():
+            if not isinstance(param, torch.Tensor) or name.endswith("_scale_inv"):
+                continue
+            if any(s in name for s in SKIP_PATTERNS):
+                continue
+            t = param.data if isinstance(param, torch.nn.Parameter) else param
+            scale = params.get(name + "_scale_inv")
+            for hf, view, box, q in self.split_param(name, t, scale):
+                entry = {"shard": box, "dtype": view.dtype}
+                if q:
+                    entry["quant"] = q
+                meta[hf] = entry
+                views[hf] = view
+        return WeightData(meta), views
+
+
+def convert_to_wb(model_config: Any, state_dict: dict[str, torch.Tensor], tp_rank: int, tp_size: int,
+                  attn_tp_rank: int | None = None, attn_tp_size: int | None = None,
+                  moe_ep: int = 1, quant: str | None = None) -> WeightData:
+    """SGLang state_dict -> WeightData (the reference's signature,
+    ``wbridge/utils/sglang_utils/__init__.py:15-52``); ``convert_to_wb_and_views`` also
+    returns the views the receiver binds."""
+    return convert_to_wb_and_views(model_config, state_dict, tp_rank, tp_size, attn_tp_rank,
+                                   attn_tp_size, moe_ep, quant)[0]
+
+
+def convert_to_wb_and_views(model_config: Any, state_dict, tp_rank, tp_size, attn_tp_rank=None,
+                            attn_tp_size=None, moe_ep: int = 1, quant: str | None = None):
+    hf = getattr(model_config, "hf_text_config", None) or getattr(model_config, "hf_config", model_config)
+    arch = ModelArch.from_hf_config(hf)
+    layout = SGLangLayout(arch, tp=tp_size, tp_rank=tp_rank, attn_tp=attn_tp_size,
+                          attn_tp_rank=attn_tp_rank, moe_ep=moe_ep, quant=quant)
+    return layout.to_wb(state_dict)
