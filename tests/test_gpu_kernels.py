@@ -1,0 +1,198 @@
+"""sm_100a transfer kernel on one GPU: every mode against the C++ CPU executor / torch oracle.
+
+Numerics: copies and casts must be bit-exact against the CPU executor; fp8 block
+quantisation bit-exact against the plain-PyTorch fp32 reference (``quant_ref``).  Bounded
+waits are exercised with a flag that nothing sets: the kernel must return with
+ST_FLAG_TIMEOUT, and the context must stay usable.
+"""
+import random
+import time
+
+import numpy as np
+import pytest
+import torch
+
+from weightbridge_b200.core.binding import bind
+from weightbridge_b200.core.plan import Op, lower_ops, phys_binding, plan_pair
+from weightbridge_b200.core.shard import box_copy, coalesce
+from weightbridge_b200.models.arch import get_arch
+from weightbridge_b200.ops._ext import ext
+from weightbridge_b200.ops.executor import (MODE_BULK4, MODE_BULK8, MODE_BULK12, MODE_VECTOR, LaunchConfig,
+                                            TransferProgram, cpu_execute, wait_flags)
+from weightbridge_b200.ops.quant_ref import block_quant_fp8_ref
+from weightbridge_b200.parallel.megatron import MegatronLayout
+from weightbridge_b200.parallel.sglang import SGLangLayout
+
+pytestmark = pytest.mark.gpu
+ABS = lambda _a: 0
+MODES = [MODE_VECTOR, MODE_BULK8, MODE_BULK12, MODE_BULK4]
+
+
+def _u8(t):
+    return t.view(torch.uint8) if t.dtype == torch.float8_e4m3fn else t
+
+
+def _sync(meg, sgl, dtype, mode, item_bytes=1 << 19, piece=16384):
+    dev = torch.device("cuda", 0)
+    senders = []
+    for lay in meg:
+        params = lay.allocate(device=dev, dtype=dtype)
+        meta, views = lay.to_wb(params)
+        senders.append((params, phys_binding(bind(meta, views))))
+    out = []
+    for lay in sgl:
+        params = lay.allocate(device=dev, dtype=dtype)
+        meta, views = lay.to_wb(params)
+        rphys = phys_binding(bind(meta, views))
+        flag = torch.zeros(1, dtype=torch.int64, device=dev)
+        for _p, sphys in senders:
+            t = lower_ops(plan_pair(sphys, rphys), ABS, ABS, item_bytes=item_bytes)
+            prog = TransferProgram(t, dev, [flag.data_ptr()], LaunchConfig(mode=mode, piece_bytes=piece))
+            prog.launch(epoch=3)
+            torch.cuda.synchronize()
+            assert prog.read_status() == 0
+            assert int(flag.item()) == 3
+            flag.zero_()
+        out.append((lay, params))
+    return out
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("model,meg,sgl", [
+    ("tiny-llama", [dict(tp=2, tp_rank=i) for i in range(2)], [dict(tp=4, tp_rank=i) for i in range(4)]),
+    ("tiny-qwen2", [dict(pp=2, pp_rank=i) for i in range(2)], [dict(tp=2, tp_rank=i) for i in range(2)]),
+    ("tiny-qwen3-moe", [dict(ep=2, ep_rank=i) for i in range(2)], [dict(tp=2, tp_rank=i) for i in range(2)]),
+])
+def test_gpu_layout_sync_bitwise(mode, model, meg, sgl):
+    arch = get_arch(model)
+    res = _sync([MegatronLayout(arch, **m) for m in meg], [SGLangLayout(arch, **s) for s in sgl],
+                torch.bfloat16, mode, item_bytes=8192)
+    for lay, params in res:
+        expected = lay.allocate(device="cuda", dtype=torch.bfloat16, fill=True)
+        for n in params:
+            assert torch.equal(params[n], expected[n]), n
+
+
+@pytest.mark.parametrize("mode", [MODE_VECTOR, MODE_BULK8])
+def test_gpu_fp8_expert_quant_matches_oracle(mode):
+    arch = get_arch("tiny-qwen3-moe")
+    meg = [MegatronLayout(arch, ep=2, ep_rank=i) for i in range(2)]
+    sgl = [SGLangLayout(arch, tp=2, tp_rank=i, moe_ep=2, quant="fp8_experts") for i in range(2)]
+    for lay, params in _sync(meg, sgl, torch.bfloat16, mode):
+        expected = lay.allocate(device="cuda", dtype=torch.bfloat16, fill=True)
+        for n in params:
+            assert torch.equal(_u8(params[n]), _u8(expected[n])), n
+
+
+def test_gpu_quant_partial_blocks_and_fp32_source():
+    """Edge blocks (rows/cols not multiples of 128) and an fp32 source take the generic path."""
+    dev = torch.device("cuda", 0)
+    for src_dtype, (n, k) in [(torch.float32, (200, 300)), (torch.bfloat16, (130, 256)), (torch.float16, (64, 100))]:
+        x = (torch.randn(n, k, device=dev) * 3).to(src_dtype)
+        q = torch.zeros(n, k, dtype=torch.float8_e4m3fn, device=dev)
+        sn, sk = (n + 127) // 128, (k + 127) // 128
+        s = torch.zeros(sn, sk, dtype=torch.float32, device=dev)
+        op = Op("quant", "x", (-1, x.data_ptr()), (-1, q.data_ptr()), [n, k], [k, 1], [k, 1], src_dtype,
+                torch.float8_e4m3fn, (-1, s.data_ptr()), [sk, 1], (128, 128))
+        prog = TransferProgram(lower_ops([op], ABS, ABS), dev, [], LaunchConfig(mode=MODE_VECTOR))
+        prog.launch(1)
+        torch.cuda.synchronize()
+        assert prog.read_status() == 0
+        qr, sr = block_quant_fp8_ref(x.cpu())
+        assert torch.equal(s.cpu(), sr)
+        assert torch.equal(q.cpu().view(torch.uint8), qr.view(torch.uint8))
+
+
+def _random_ops(rng, dev, count=12):
+    """Random strided copies of odd sizes/offsets (exercise 1/2/4/8/16-byte paths)."""
+    ops, pairs = [], []
+    for _ in range(count):
+        dtype = rng.choice([torch.uint8, torch.float16, torch.float32, torch.bfloat16])
+        shape = [rng.randint(1, 40), rng.randint(1, 70)]
+        a = torch.randint(0, 100, shape, device=dev).to(dtype)
+        b = torch.zeros(shape, dtype=dtype, device=dev)
+        r0, c0 = rng.randrange(shape[0]), rng.randrange(shape[1])
+        r1, c1 = rng.randint(r0 + 1, shape[0]), rng.randint(c0 + 1, shape[1])
+        box = [(r0, r1, shape[0]), (c0, c1, shape[1])]
+        full = [(0, shape[0], shape[0]), (0, shape[1], shape[1])]
+        bc = box_copy(full, box, list(a.stride()), [shape[1], 1])
+        e, ss, ds = coalesce(bc.extents, bc.src_strides, bc.dst_strides)
+        es = a.element_size()
+        ops.append(Op("copy", "x", (-1, a.data_ptr() + bc.src_offset * es),
+                      (-1, b.data_ptr() + (r0 * shape[1] + c0) * es), e, ss, ds, dtype, dtype))
+        pairs.append((a, b, box))
+    return ops, pairs
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_gpu_random_strided_copies(mode):
+    rng = random.Random(mode)
+    dev = torch.device("cuda", 0)
+    ops, pairs = _random_ops(rng, dev)
+    prog = TransferProgram(lower_ops(ops, ABS, ABS, item_bytes=512), dev, [], LaunchConfig(mode=mode, piece_bytes=256))
+    prog.launch(1)
+    torch.cuda.synchronize()
+    assert prog.read_status() == 0
+    for a, b, box in pairs:
+        sl = tuple(slice(l, r) for l, r, _ in box)
+        assert torch.equal(b[sl], a[sl])
+        mask = torch.ones_like(b, dtype=torch.bool)
+        mask[sl] = False
+        assert not b[mask].any()
+
+
+def test_gpu_matches_cpu_executor_on_cast():
+    dev = torch.device("cuda", 0)
+    x = torch.randn(333, 77, device=dev)
+    for dst_dtype in (torch.bfloat16, torch.float16):
+        y = torch.zeros(333, 77, dtype=dst_dtype, device=dev)
+        op = Op("cast", "x", (-1, x.data_ptr()), (-1, y.data_ptr()), [333 * 77], [1], [1], torch.float32, dst_dtype)
+        prog = TransferProgram(lower_ops([op], ABS, ABS, item_bytes=4096), dev, [], LaunchConfig(mode=MODE_VECTOR))
+        prog.launch(1)
+        torch.cuda.synchronize()
+        xc = x.cpu()
+        yc = torch.zeros(333, 77, dtype=dst_dtype)
+        opc = Op("cast", "x", (-1, xc.data_ptr()), (-1, yc.data_ptr()), [333 * 77], [1], [1], torch.float32, dst_dtype)
+        cpu_execute(lower_ops([opc], ABS, ABS))
+        assert torch.equal(y.cpu(), yc)
+        assert torch.equal(yc, xc.to(dst_dtype))
+
+
+def test_wait_flags_times_out_with_status():
+    dev = torch.device("cuda", 0)
+    flags = torch.zeros(3, dtype=torch.int64, device=dev)
+    epoch = torch.tensor([5], dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    where = torch.full((1,), 0x7FFFFFFF, dtype=torch.int32, device=dev)
+    t0 = time.time()
+    wait_flags(flags, epoch, 0.05, status, where)
+    torch.cuda.synchronize()
+    assert time.time() - t0 < 5.0
+    assert int(status.item()) & ext().ST_FLAG_TIMEOUT
+    assert int(where.item()) == 0
+    # the context is still usable, and a satisfied wait reports nothing
+    flags.fill_(5)
+    status.zero_()
+    wait_flags(flags, epoch, 0.05, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    flags[1] = 9
+    wait_flags(flags, epoch, 0.05, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & ext().ST_FLAG_STALE
+
+
+def test_repeated_launches_reset_counter():
+    dev = torch.device("cuda", 0)
+    a = torch.randn(1 << 20, device=dev)
+    b = torch.zeros_like(a)
+    flag = torch.zeros(1, dtype=torch.int64, device=dev)
+    op = Op("copy", "x", (-1, a.data_ptr()), (-1, b.data_ptr()), [a.numel()], [1], [1], a.dtype, a.dtype)
+    prog = TransferProgram(lower_ops([op], ABS, ABS, item_bytes=1 << 16), dev, [flag.data_ptr()],
+                           LaunchConfig(mode=MODE_BULK8))
+    for e in range(1, 6):
+        prog.launch(e)
+        torch.cuda.synchronize()
+        assert int(flag.item()) == e
+        assert int(prog.counter.item()) == 0
+    assert torch.equal(a, b)
