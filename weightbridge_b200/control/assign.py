@@ -1,0 +1,96 @@
+"""Source assignment: which sender sends which entries to which receiver.
+
+Senders whose shards of an entry are identical are replicas (trainer DP, or the dense part
+of an EP-only layout); shards of different replica groups must not overlap.  For every
+receiver entry and every replica group that overlaps it, one member of the group is chosen:
+the least loaded one by bytes assigned so far (ties: lowest rank), so replicated weights
+spread over every sender's NVLink egress.
+
+Parity: the reference deduplicates identical shards by keeping the lowest rank and raises
+on partial overlap (``wbridge/backend/direct_sender.py:31-71``); the overlap rule is the
+same, the choice among replicas is load-balanced instead of lowest-rank.
+"""
+from __future__ import annotations
+
+import json
+from collections import defaultdict
+
+from ..core.shard import WeightData, box_copy, shard_numel
+
+
+def _key(shards) -> str:
+    return json.dumps(shards)
+
+
+def replica_groups(sender_metas: list[WeightData]) -> dict[str, list[list[int]]]:
+    """name -> list of replica groups (sender ranks with identical shards)."""
+    out: dict[str, list[list[int]]] = {}
+    by_name: dict[str, dict[str, list[int]]] = defaultdict(dict)
+    for s, meta in enumerate(sender_metas):
+        for name, shards, _ in meta:
+            by_name[name].setdefault(_key(shards), []).append(s)
+    for name, groups in by_name.items():
+        glist = list(groups.values())
+        keys = list(groups.keys())
+        # different groups must not overlap
+        for i in range(len(glist)):
+            for j in range(i + 1, len(glist)):
+                a = sender_metas[glist[i][0]].shards(name)
+                b = sender_metas[glist[j][0]].shards(name)
+                for sa in a:
+                    for sb in b:
+                        try:
+                            bc = box_copy(sa, sb)
+                        except ValueError:
+                            raise ValueError(f"senders {glist[i]} and {glist[j]} hold incompatible shards of {name!r}")
+                        if bc is not None:
+                            raise ValueError(
+                                f"Partial shard overlap for {name!r} between sender ranks {glist[i][0]} and "
+                                f"{glist[j][0]}: senders must have identical or non-overlapping shards")
+        out[name] = glist
+    return out
+
+
+def _overlap_bytes(s_shards, r_shards, itemsize: int) -> int:
+    n = 0
+    for a in s_shards:
+        for b in r_shards:
+            bc = box_copy(a, b)
+            if bc is not None:
+                n += bc.numel
+    return n * itemsize
+
+
+def assign_sources(sender_metas: list[WeightData], receiver_metas: dict[int, WeightData],
+                   load_balance: bool = True) -> dict[int, dict[int, list[str]]]:
+    """``plan[sender][receiver] = [entry names]`` (both as indices into the inputs)."""
+    groups = replica_groups(sender_metas)
+    load = [0] * len(sender_metas)
+    plan: dict[int, dict[int, list[str]]] = defaultdict(lambda: defaultdict(list))
+    for r in sorted(receiver_metas):
+        rmeta = receiver_metas[r]
+        for name, r_shards, r_dtype in rmeta:
+            q = rmeta.quant(name)
+            if q and q.get("role") == "scale":
+                continue
+            for group in groups.get(name, []):
+                s_shards = sender_metas[group[0]].shards(name)
+                nbytes = _overlap_bytes(s_shards, r_shards, r_dtype.itemsize)
+                if nbytes == 0:
+                    continue
+                if load_balance:
+                    s = min(group, key=lambda x: (load[x], x))
+                else:
+                    s = min(group)
+                load[s] += nbytes
+                plan[s][r].append(name)
+    return {s: dict(v) for s, v in plan.items()}
+
+
+def expected_senders(plan: dict[int, dict[int, list[str]]], receiver: int) -> list[int]:
+    return sorted(s for s, rs in plan.items() if receiver in rs and rs[receiver])
+
+
+def restrict(meta: WeightData, names) -> WeightData:
+    keep = set(names)
+    return WeightData({n: e for n, e in meta.to_jsonable().items() if n in keep})

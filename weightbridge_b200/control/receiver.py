@@ -1,0 +1,371 @@
+"""Rollout-side receiver worker (one per rollout GPU / scheduler process).
+
+A daemon thread serves two ZMQ sockets: a DEALER to the controller (metadata, connect,
+receive, stats) and a REP for the scheduler's ``request_update``.  State machine:
+DISCONNECTED -> CONNECTED (after joining a session) -> AWAITING_SCHEDULER_UPDATE (armed by
+``/wbridge/receive``) -> CONNECTED (after the update).
+
+On connect (``gpu_direct``) the worker exports the allocations holding its parameters as
+CUDA IPC handles, publishes them with the physical binding of every entry and a flag word
+per sender, and checks the senders' plan digests against its own overlap computation.
+On update it publishes ``ready/<rank>/<epoch>``; the senders' kernels store straight into
+the parameters and write the epoch to the flags; the worker waits (bounded) for every
+expected sender's ``done`` key, then reads the flag words back (one small device->host
+copy) and accepts the update only if every flag holds this epoch.
+
+Parity: ``wbridge/frontend/receiver.py:48-230``.  Differences: ``stop()`` stops the thread,
+the thread is a daemon, every wait has a deadline, the handshake only involves senders
+that overlap this worker (the reference waits on every sender), the state_dict is bound at
+connect (the senders write into it directly), and ``request_update`` can wait for arming.
+"""
+from __future__ import annotations
+
+import json
+import logging
+import os
+import socket
+import tempfile
+import threading
+import time
+from collections import deque
+from datetime import timedelta
+from typing import Any
+
+import torch
+import zmq
+
+from ..core.binding import bind
+from ..core.plan import lower_ops, phys_binding, plan_digest, plan_pair, wire_binding
+from ..core.shard import WeightData
+from ..utils.config import TransferConfig, normalize_mode
+from .assign import expected_senders, restrict
+from .protocol import (CONNECT_REQUEST, METADATA_REQUEST, RECEIVE_REQUEST, STATS_REQUEST, STOP_REQUEST,
+                       UPDATE_REQUEST, ReceiverState, b64)
+from .session import Session, SessionTimeout
+
+logger = logging.getLogger(__name__)
+
+
+class ReceiveError(RuntimeError):
+    pass
+
+
+class WeightReceiver:
+    def __init__(self, controller_ipc_name: str, rank: int, metadata: WeightData,
+                 state_dict: dict[str, Any] | None = None, device: torch.device | int | str | None = None,
+                 config: TransferConfig | None = None):
+        self.controller_ipc_name = controller_ipc_name
+        self.rank = rank
+        self.metadata = metadata if isinstance(metadata, WeightData) else WeightData(metadata)
+        self.state_dict = state_dict
+        self.config = config or TransferConfig.from_env()
+        self.device = self._infer_device(device, state_dict)
+        self._state = ReceiverState.DISCONNECTED
+        self._error: str | None = None
+        self._stop = threading.Event()
+        self._started = threading.Event()
+        self.stats: deque = deque(maxlen=64)
+        self.epoch = 0
+        self.session: Session | None = None
+        self._pending_update: dict | None = None
+        fd, path = tempfile.mkstemp(prefix=f"wbridge_sched_{rank}_")
+        os.close(fd)
+        os.unlink(path)
+        self._sched_path = path
+        self.scheduler_ipc_name = f"ipc://{path}"
+        self._ctx = zmq.Context()
+        self.receiver_thread = threading.Thread(target=self._loop, name=f"wbridge-receiver-{rank}", daemon=True)
+        self.receiver_thread.start()
+        if not self._started.wait(30):
+            raise ReceiveError("receiver thread did not start")
+        self._req_lock = threading.Lock()
+        self._req = self._new_req()
+
+    @staticmethod
+    def _infer_device(device, state_dict) -> torch.device:
+        if device is not None:
+            return torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        if state_dict:
+            for v in state_dict.values():
+                t = v[0] if isinstance(v, (list, tuple)) else v
+                if isinstance(t, torch.Tensor):
+                    return t.device
+        if torch.cuda.is_available():
+            return torch.device("cuda", torch.cuda.current_device())
+        return torch.device("cpu")
+
+    def _new_req(self):
+        s = self._ctx.socket(zmq.REQ)
+        s.setsockopt(zmq.LINGER, 0)
+        s.setsockopt(zmq.REQ_RELAXED, 1)
+        s.setsockopt(zmq.REQ_CORRELATE, 1)
+        s.connect(self.scheduler_ipc_name)
+        return s
+
+    @property
+    def state(self) -> ReceiverState:
+        return self._state
+
+    def set_state_dict(self, state_dict: dict[str, Any]) -> None:
+        """Tensors (or views) the senders write into; bound at the next connect."""
+        self.state_dict = state_dict
+        self.device = self._infer_device(None, state_dict)
+
+    # -- scheduler side ----------------------------------------------------------------
+    def request_update(self, state_dict: dict[str, Any] | None = None, timeout: float | None = None) -> bool:
+        """Receive the pending weights into the bound state_dict.
+
+        Returns False when no sync is pending (the controller has not armed this worker);
+        with ``timeout`` the call first waits up to that many seconds for the arm.
+        """
+        if state_dict is not None and state_dict is not self.state_dict:
+            if self.session is not None:
+                if not self._same_tensors(state_dict):
+                    raise ReceiveError("request_update got tensors other than the ones bound at connect; "
+                                       "reconnect the sender to rebind")
+            else:
+                self.set_state_dict(state_dict)
+        msg = {"type": UPDATE_REQUEST, "wait_s": float(timeout or 0.0)}
+        wait = (timeout or 0.0) + self.config.sync_timeout_s + 5.0
+        with self._req_lock:
+            self._req.send_string(json.dumps(msg))
+            if not self._req.poll(int(wait * 1000)):
+                self._req.close(0)
+                self._req = self._new_req()
+                raise ReceiveError(f"no reply from the receiver thread within {wait:.0f}s")
+            reply = json.loads(self._req.recv_string())
+        if reply.get("error"):
+            raise ReceiveError(reply["error"])
+        return bool(reply["success"])
+
+    def _same_tensors(self, state_dict) -> bool:
+        for name in self.metadata.names():
+            a, b = self.state_dict.get(name), state_dict.get(name)
+            if isinstance(a, torch.Tensor) and isinstance(b, torch.Tensor) and a.data_ptr() != b.data_ptr():
+                return False
+        return True
+
+    def stop(self) -> None:
+        """Stop the worker thread and release the session."""
+        self._stop.set()
+        if self.receiver_thread.is_alive():
+            self.receiver_thread.join(timeout=10)
+        try:
+            self._req.close(0)
+        except Exception:
+            pass
+        self._ctx.term()
+        for p in (self._sched_path,):
+            try:
+                os.unlink(p)
+            except OSError:
+                pass
+
+    # -- worker thread -----------------------------------------------------------------
+    def _loop(self) -> None:
+        ctl = self._ctx.socket(zmq.DEALER)
+        ctl.setsockopt(zmq.IDENTITY, f"worker-{self.rank}".encode())
+        ctl.setsockopt(zmq.LINGER, 0)
+        ctl.connect(self.controller_ipc_name)
+        rep = self._ctx.socket(zmq.REP)
+        rep.setsockopt(zmq.LINGER, 0)
+        rep.bind(self.scheduler_ipc_name)
+        poller = zmq.Poller()
+        poller.register(ctl, zmq.POLLIN)
+        poller.register(rep, zmq.POLLIN)
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)
+        self._started.set()
+        try:
+            while not self._stop.is_set():
+                socks = dict(poller.poll(50))
+                if ctl in socks:
+                    data = json.loads(ctl.recv_string())
+                    self._on_controller(ctl, data)
+                if rep in socks:
+                    msg = json.loads(rep.recv_string())
+                    self._on_scheduler(rep, msg)
+                if self._pending_update is not None:
+                    self._try_pending(rep)
+        finally:
+            ctl.close(0)
+            rep.close(0)
+            self._teardown()
+
+    def _reply(self, sock, data: dict, obj: dict) -> None:
+        obj = dict(obj, id=data.get("id"))
+        sock.send_string(json.dumps(obj))
+
+    def _on_controller(self, sock, data: dict) -> None:
+        t = data.get("type")
+        if t == METADATA_REQUEST:
+            self._reply(sock, data, {"rank": self.rank, "metadata": self.metadata.to_jsonable(),
+                                     "state": self._state.value, "device": str(self.device),
+                                     "host": socket.gethostname(), "pid": os.getpid()})
+        elif t == CONNECT_REQUEST:
+            if self._state == ReceiverState.AWAITING_SCHEDULER_UPDATE:
+                self._reply(sock, data, {"status": "error", "detail": "cannot connect while awaiting scheduler update"})
+                return
+            self._reply(sock, data, {"status": "ack"})
+            self._state = ReceiverState.CONNECTING
+            try:
+                self._join(data)
+                self._state = ReceiverState.CONNECTED
+                self._error = None
+            except Exception as e:  # reported through metadata/stats; sender times out
+                logger.exception("receiver %d failed to join", self.rank)
+                self._error = f"{type(e).__name__}: {e}"
+                self._state = ReceiverState.FAILED
+        elif t == RECEIVE_REQUEST:
+            if self._state != ReceiverState.CONNECTED:
+                self._reply(sock, data, {"status": "error", "detail": f"requires CONNECTED state, is {self._state.value}"})
+                return
+            self._state = ReceiverState.AWAITING_SCHEDULER_UPDATE
+            self._reply(sock, data, {"status": "ack"})
+        elif t == STATS_REQUEST:
+            self._reply(sock, data, {"rank": self.rank, "state": self._state.value, "epoch": self.epoch,
+                                     "error": self._error, "syncs": list(self.stats)})
+        elif t == STOP_REQUEST:
+            self._reply(sock, data, {"status": "ack"})
+            self._stop.set()
+        else:
+            self._reply(sock, data, {"status": "error", "detail": f"unknown message type {t!r}"})
+
+    def _on_scheduler(self, sock, msg: dict) -> None:
+        if msg.get("type") != UPDATE_REQUEST:
+            sock.send_string(json.dumps({"success": False, "message": "unknown message"}))
+            return
+        if self._state == ReceiverState.AWAITING_SCHEDULER_UPDATE:
+            self._do_update(sock)
+            return
+        wait_s = float(msg.get("wait_s") or 0.0)
+        if wait_s > 0 and self._state in (ReceiverState.CONNECTED, ReceiverState.CONNECTING,
+                                          ReceiverState.DISCONNECTED):
+            self._pending_update = {"deadline": time.monotonic() + wait_s}
+            return
+        sock.send_string(json.dumps({"success": False, "message": "no pending weights",
+                                     "state": self._state.value}))
+
+    def _try_pending(self, sock) -> None:
+        if self._state == ReceiverState.AWAITING_SCHEDULER_UPDATE:
+            self._pending_update = None
+            self._do_update(sock)
+        elif time.monotonic() > self._pending_update["deadline"]:
+            self._pending_update = None
+            sock.send_string(json.dumps({"success": False, "message": "no pending weights"}))
+
+    def _do_update(self, sock) -> None:
+        try:
+            rec = self._receive()
+            self.stats.append(rec)
+            self._state = ReceiverState.CONNECTED
+            sock.send_string(json.dumps({"success": True, "epoch": self.epoch, "stats": rec}))
+        except Exception as e:
+            logger.exception("receiver %d update failed", self.rank)
+            self._error = f"{type(e).__name__}: {e}"
+            self._state = ReceiverState.FAILED
+            sock.send_string(json.dumps({"success": False, "message": self._error, "error": self._error}))
+
+    # -- session -----------------------------------------------------------------------
+    def _join(self, data: dict) -> None:
+        self._teardown()
+        mode = normalize_mode({"nccl": "gpu_direct", "gloo": "cpu_direct"}.get(data["backend"], data["backend"]))
+        self.mode = mode
+        gr = int(data["rank"])
+        self.global_rank = gr
+        W = int(data["sender_world_size"])
+        self.world_size = int(data["world_size"])
+        sess = Session(data["master_address"], int(data["master_port"]), is_master=False,
+                       timeout_s=self.config.connect_timeout_s)
+        self.session = sess
+        if self.state_dict is None:
+            raise ReceiveError("the receiver needs its state_dict before connect (WeightReceiver(..., state_dict=...))")
+        binding = bind(self.metadata, self.state_dict)
+        info: dict[str, Any] = {"rank": gr, "worker": self.rank, "pid": os.getpid(), "host": socket.gethostname(),
+                                "mode": mode}
+        if mode in ("gpu_direct", "nvls"):
+            from ..parallel.ipc import ExportTable
+            from ..ops._ext import ext
+            if self.device.type != "cuda":
+                raise ReceiveError("gpu_direct needs the receiver's tensors on a CUDA device")
+            torch.cuda.set_device(self.device)
+            self.flags = torch.zeros(max(W, 1), dtype=torch.int64, device=self.device)
+            export = ExportTable(self.device)
+            phys = phys_binding(binding, export.locate)
+            falloc, foff = export.locate(self.flags.data_ptr())
+            info.update({"device": self.device.index, "uuid": b64(ext().device_uuid(self.device.index)),
+                         "allocs": export.to_json(), "binding": phys.to_json(), "flags": [falloc, foff, W]})
+            self._export = export
+        else:
+            self._rphys = phys_binding(binding)
+        sess.set_json(f"recv/{gr}", info)
+        # plan agreement: recompute every expected sender's overlap and compare digests
+        assignment = sess.get_json("assign")
+        smetas = sess.get_json("senders/meta")
+        plan = {int(s): {int(r): v for r, v in rs.items()} for s, rs in assignment.items()}
+        self.expected = expected_senders(plan, gr)
+        self.expected_bytes = 0
+        self.overlaps: dict[int, WeightData] = {}
+        for s in self.expected:
+            ov = WeightData.compute_overlap(restrict(WeightData(smetas[s]), plan[s][gr]), self.metadata)
+            digest = sess.get(f"digest/{s}/{gr}").decode()
+            if digest != plan_digest(ov):
+                raise ReceiveError(f"plan digest mismatch with sender {s}: the two sides disagree on the layout")
+            self.overlaps[s] = ov
+            self.expected_bytes += ov.total_nbytes()
+        if mode == "cpu_direct":
+            from .sender import gloo_group
+            self._gloo = gloo_group(sess, gr, self.world_size, self.config.sync_timeout_s, data["master_address"])
+            self._wires = {}
+            for s, ov in self.overlaps.items():
+                wire = torch.empty(ov.total_nbytes(), dtype=torch.uint8)
+                tables = lower_ops(plan_pair(wire_binding(ov, base=wire.data_ptr()), self._rphys),
+                                   lambda a: 0, lambda a: 0, item_bytes=self.config.item_bytes)
+                self._wires[s] = (wire, tables)
+        self.epoch = 0
+        sess.set(f"joined/{gr}", "1")
+        logger.info("receiver worker %d joined session as rank %d (mode=%s, senders=%s, %.3f GB expected)",
+                    self.rank, gr, mode, self.expected, self.expected_bytes / 1e9)
+
+    def _receive(self) -> dict:
+        sess = self.session
+        if sess is None:
+            raise ReceiveError("not connected")
+        epoch = self.epoch + 1
+        gr = self.global_rank
+        t0 = time.perf_counter()
+        if self.mode == "cpu_direct":
+            from ..ops.executor import cpu_execute
+            sess.set(f"ready/{gr}/{epoch}", "1")
+            works = [(s, self._gloo.recv([wire], s, epoch)) for s, (wire, _t) in self._wires.items()]
+            for s, w in works:
+                w.wait()
+            for s, (wire, tables) in self._wires.items():
+                cpu_execute(tables)
+        else:
+            sess.set(f"ready/{gr}/{epoch}", "1")
+            keys = [f"done/{s}/{gr}/{epoch}" for s in self.expected]
+            try:
+                sess.wait(keys, self.config.sync_timeout_s, what=f"senders {self.expected} to finish epoch {epoch}")
+            except SessionTimeout as e:
+                raise ReceiveError(str(e)) from None
+            bad = {s: int(sess.get(f"done/{s}/{gr}/{epoch}")) for s in self.expected}
+            bad = {s: v for s, v in bad.items() if v}
+            if bad:
+                raise ReceiveError(f"senders reported kernel status {bad} for epoch {epoch}")
+            if self.config.verify_flags and self.expected:
+                flags = self.flags.cpu()
+                stale = [s for s in self.expected if int(flags[s]) != epoch]
+                if stale:
+                    raise ReceiveError(f"flags of senders {stale} do not hold epoch {epoch}: {flags.tolist()}")
+            for s in self.expected:
+                sess.delete(f"done/{s}/{gr}/{epoch}")
+            sess.delete(f"ready/{gr}/{epoch - 1}")
+        self.epoch = epoch
+        return {"epoch": epoch, "host_ms": (time.perf_counter() - t0) * 1e3, "bytes": self.expected_bytes,
+                "senders": self.expected}
+
+    def _teardown(self) -> None:
+        self.session = None
+        self._gloo = None
+

@@ -1,0 +1,339 @@
+"""Trainer-side sender: ``WeightSender(transfer_mode, receiver_urls).connect(meta); .send(sd)``.
+
+connect (once, or to reshard):
+  1. all-gather every sender's metadata over the trainer group;
+  2. sender rank 0 queries ``/wbridge/metadata`` of every rollout URL, hosts the session
+     store (OS-chosen port), computes the load-balanced source assignment and the plan
+     digest of every (sender, receiver) pair, and POSTs ``/wbridge/connect``;
+  3. every sender joins the store, reads the receivers' exported memory tables and opens
+     the CUDA IPC handles of the receivers it writes to.
+send (each sync):
+  1. rank 0 POSTs ``/wbridge/receive`` (arms the workers; the schedulers call
+     ``request_update`` when they can take new weights);
+  2. the first send binds the state_dict, compiles the plan against the receivers'
+     addresses and uploads the work tables; later sends reuse them;
+  3. wait for every target's ``ready`` key, launch ONE transfer kernel (peer stores +
+     fused layout transform / fp8 quantisation + epoch flags), wait for it, publish
+     ``done`` with the kernel's status.
+
+Parity: ``wbridge/frontend/sender.py:7-26`` and ``wbridge/backend/direct_sender.py:16-211``
+(``transfer_mode`` ``gpu_direct`` / ``cpu_direct``, rank-0 HTTP control, dedup).  The
+payload path is new: no pack buffer, no NCCL ``isend``; ``cpu_direct`` works (the
+reference's ``CPUDirectSender.send`` is a stub).
+"""
+from __future__ import annotations
+
+import logging
+import os
+import socket
+import time
+import uuid
+from dataclasses import dataclass, field
+from datetime import timedelta
+from typing import Any
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from ..core.binding import bind
+from ..core.plan import Tables, lower_ops, phys_binding, plan_digest, plan_pair, wire_binding, PhysBinding
+from ..core.shard import WeightData
+from ..utils.config import TransferConfig, normalize_mode
+from .assign import assign_sources, restrict
+from .session import Session, SessionTimeout, local_address
+
+logger = logging.getLogger(__name__)
+
+
+class TransferError(RuntimeError):
+    pass
+
+
+@dataclass
+class SyncStats:
+    epoch: int
+    device_ms: float = 0.0          # transfer kernel, CUDA events on the transfer stream
+    host_ms: float = 0.0            # whole send() call
+    wait_ready_ms: float = 0.0
+    bytes_read: int = 0
+    bytes_written: int = 0
+    receivers: list[int] = field(default_factory=list)
+    status: int = 0
+
+    def to_dict(self) -> dict:
+        return dict(self.__dict__)
+
+
+def _http():
+    import requests
+    return requests
+
+
+class WeightSender:
+    def __init__(self, transfer_mode: str, receiver_urls: list[str], group: Any = None,
+                 config: TransferConfig | None = None):
+        self.transfer_mode = transfer_mode
+        self.config = config or TransferConfig.from_env(mode=transfer_mode)
+        self.config.mode = normalize_mode(transfer_mode)
+        self.receiver_urls = list(receiver_urls)
+        self.group = group
+        if dist.is_available() and dist.is_initialized():
+            self.rank = dist.get_rank(group)
+            self.world_size = dist.get_world_size(group)
+        else:
+            self.rank, self.world_size = 0, 1
+        self.connected = False
+        self.metadata: WeightData | None = None
+        self.session: Session | None = None
+        self.epoch = 0
+        self.targets: dict[int, list[str]] = {}
+        self.overlaps: dict[int, WeightData] = {}
+        self.history: list[SyncStats] = []
+        self._program = None
+        self._program_key = None
+        self._imports: dict[int, Any] = {}
+        self._rinfo: dict[int, dict] = {}
+
+    # -- collectives on the trainer group (no-ops for a single sender) -------------------
+    def _all_gather(self, obj):
+        if self.world_size == 1:
+            return [obj]
+        out = [None] * self.world_size
+        dist.all_gather_object(out, obj, group=self.group)
+        return out
+
+    def _broadcast(self, obj):
+        if self.world_size == 1:
+            return obj
+        lst = [obj]
+        src = dist.get_global_rank(self.group, 0) if self.group is not None else 0
+        dist.broadcast_object_list(lst, src=src, group=self.group)
+        return lst[0]
+
+    # -- connect ---------------------------------------------------------------------------
+    def connect(self, sender_metadata: WeightData) -> None:
+        if self.connected:
+            self.disconnect()
+        self.metadata = sender_metadata
+        cfg = self.config
+        metas = self._all_gather(sender_metadata.to_jsonable())
+        info = None
+        if self.rank == 0:
+            info = self._connect_rank0(metas)
+        info = self._broadcast(info)
+        if info.get("error"):
+            raise TransferError(info["error"])
+        addr, port, world = info["address"], info["port"], info["world_size"]
+        if self.rank != 0:
+            self.session = Session(addr, port, is_master=False, timeout_s=cfg.connect_timeout_s)
+        self.world_total = world
+        sess = self.session
+        assignment = sess.get_json("assign")
+        mine = assignment.get(str(self.rank), {})
+        self.targets = {int(r): names for r, names in mine.items() if names}
+        rmetas = {int(k): WeightData(v) for k, v in info["receivers"].items()}
+        self.overlaps = {r: WeightData.compute_overlap(restrict(sender_metadata, names), rmetas[r])
+                         for r, names in self.targets.items()}
+        # receivers publish their memory tables once they joined the store
+        for r in self.targets:
+            self._rinfo[r] = sess.get_json(f"recv/{r}", cfg.connect_timeout_s)
+        if cfg.mode == "cpu_direct":
+            self._gloo = gloo_group(sess, self.rank, world, cfg.sync_timeout_s, addr)
+        else:
+            self._open_receivers()
+        sess.wait([f"joined/{r}" for r in self.targets], cfg.connect_timeout_s, "receivers to join")
+        self.epoch = 0
+        self._program = None
+        self._program_key = None
+        self.connected = True
+        logger.info("sender %d connected: %d receiver targets, mode=%s", self.rank, len(self.targets), cfg.mode)
+
+    def _connect_rank0(self, metas: list[dict]) -> dict:
+        cfg = self.config
+        http = _http()
+        receivers: dict[int, dict] = {}
+        counts = []
+        base = self.world_size
+        for url in self.receiver_urls:
+            resp = http.get(f"{url}/wbridge/metadata", timeout=cfg.http_timeout_s)
+            resp.raise_for_status()
+            workers = sorted(resp.json(), key=lambda w: w["rank"])
+            for i, w in enumerate(workers):
+                receivers[base + i] = w["metadata"]
+            counts.append(len(workers))
+            base += len(workers)
+        world = self.world_size + sum(counts)
+        addr = cfg.master_address if cfg.master_address not in ("", "auto") else local_address()
+        self.session = Session(addr, cfg.master_port, is_master=True, timeout_s=cfg.connect_timeout_s)
+        sess = self.session
+        smeta_objs = [WeightData(m) for m in metas]
+        rmeta_objs = {r: WeightData(m) for r, m in receivers.items()}
+        plan = assign_sources(smeta_objs, rmeta_objs, cfg.load_balance)
+        sess.set_json("senders/meta", metas)
+        sess.set_json("assign", {str(s): {str(r): n for r, n in rs.items()} for s, rs in plan.items()})
+        for s, rs in plan.items():
+            for r, names in rs.items():
+                ov = WeightData.compute_overlap(restrict(smeta_objs[s], names), rmeta_objs[r])
+                sess.set(f"digest/{s}/{r}", plan_digest(ov))
+        session_id = uuid.uuid4().hex
+        backend = "gloo" if cfg.mode == "cpu_direct" else cfg.mode
+        base = self.world_size
+        for url, count in zip(self.receiver_urls, counts):
+            resp = http.post(f"{url}/wbridge/connect", timeout=cfg.http_timeout_s, json={
+                "master_address": addr, "master_port": sess.port, "base_rank": base, "world_size": world,
+                "group_name": "wbridge", "sender_world_size": self.world_size, "backend": backend,
+                "session": session_id})
+            resp.raise_for_status()
+            if resp.json().get("status") != "success":
+                return {"error": f"receiver {url} refused connect: {resp.json()}"}
+            base += count
+        return {"address": addr, "port": sess.port, "world_size": world,
+                "receivers": {str(r): m for r, m in receivers.items()}, "session": session_id}
+
+    def _open_receivers(self) -> None:
+        from ..parallel.ipc import ImportTable
+        host, pid = socket.gethostname(), os.getpid()
+        for r, info in self._rinfo.items():
+            if info.get("mode") not in ("gpu_direct", "nvls"):
+                raise TransferError(f"receiver {r} joined in mode {info.get('mode')}")
+            if info["host"] != host:
+                raise TransferError(f"receiver {r} is on host {info['host']}: gpu_direct needs one node")
+            self._imports[r] = ImportTable(info["allocs"], same_process=(info["pid"] == pid))
+
+    def disconnect(self) -> None:
+        for imp in self._imports.values():
+            imp.close()
+        self._imports.clear()
+        self._program = None
+        self.session = None
+        self.connected = False
+
+    # -- send ----------------------------------------------------------------------------------
+    def _compile(self, state_dict) -> None:
+        cfg = self.config
+        binding = bind(self.metadata, state_dict)
+        device = binding.device
+        sphys = phys_binding(binding)
+        parts, flags = [], []
+        for r, names in sorted(self.targets.items()):
+            info = self._rinfo[r]
+            rphys = PhysBinding.from_json(info["binding"])
+            imp = self._imports[r]
+            ops = plan_pair(sphys, rphys, names=names)
+            parts.append(lower_ops(ops, lambda a: 0, imp.base, item_bytes=cfg.item_bytes))
+            falloc, foff, _w = info["flags"]
+            flags.append(imp.base(falloc) + foff + 8 * self.rank)
+        tables = _interleave(parts)
+        from ..ops.executor import LaunchConfig, TransferProgram
+        lc = LaunchConfig(mode=cfg.kernel_mode, piece_bytes=cfg.piece_bytes, grid=cfg.grid or None)
+        torch.cuda.set_device(device)
+        self._program = TransferProgram(tables, device, flags, lc)
+        self._stream = torch.cuda.Stream(device)
+        self._ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+
+    def _compile_cpu(self, state_dict) -> None:
+        binding = bind(self.metadata, state_dict)
+        if binding.device.type != "cpu":
+            raise TransferError("cpu_direct sends CPU tensors")
+        sphys = phys_binding(binding)
+        self._wires = {}
+        for r, names in sorted(self.targets.items()):
+            ov = self.overlaps[r]
+            wire = torch.empty(ov.total_nbytes(), dtype=torch.uint8)
+            tables = lower_ops(plan_pair(sphys, wire_binding(ov, base=wire.data_ptr()), names=names, overlap_meta=ov),
+                               lambda a: 0, lambda a: 0, item_bytes=self.config.item_bytes)
+            self._wires[r] = (wire, tables)
+
+    def _key(self, state_dict) -> tuple:
+        out = []
+        for name in self.metadata.names():
+            v = state_dict.get(name)
+            if isinstance(v, (list, tuple)):
+                out.append(tuple(t.data_ptr() for t in v))
+            elif isinstance(v, torch.Tensor):
+                out.append(v.data_ptr())
+        return tuple(out)
+
+    def send(self, state_dict: dict[str, Any]) -> SyncStats:
+        if not self.connected or self.metadata is None:
+            raise RuntimeError("WeightSender.send requires connect() first")
+        cfg = self.config
+        t0 = time.perf_counter()
+        if self.rank == 0:
+            http = _http()
+            for url in self.receiver_urls:
+                resp = http.post(f"{url}/wbridge/receive", timeout=cfg.http_timeout_s)
+                resp.raise_for_status()
+                if resp.json().get("status") != "success":
+                    raise TransferError(f"receiver {url} refused the sync: {resp.json()}")
+        key = self._key(state_dict)
+        if self._program_key != key:
+            (self._compile_cpu if cfg.mode == "cpu_direct" else self._compile)(state_dict)
+            self._program_key = key
+        epoch = self.epoch + 1
+        sess = self.session
+        st = SyncStats(epoch=epoch, receivers=sorted(self.targets))
+        t1 = time.perf_counter()
+        try:
+            sess.wait([f"ready/{r}/{epoch}" for r in self.targets], cfg.sync_timeout_s,
+                      f"receivers {sorted(self.targets)} to be ready for epoch {epoch}")
+        except SessionTimeout as e:
+            raise TransferError(str(e)) from None
+        st.wait_ready_ms = (time.perf_counter() - t1) * 1e3
+        if cfg.mode == "cpu_direct":
+            from ..ops.executor import cpu_execute
+            works = []
+            for r, (wire, tables) in self._wires.items():
+                cpu_execute(tables)
+                works.append(self._gloo.send([wire], r, epoch))
+                st.bytes_written += wire.numel()
+            for w in works:
+                w.wait()
+        else:
+            prog = self._program
+            cur = torch.cuda.current_stream(prog.device)
+            self._stream.wait_stream(cur)
+            e0, e1 = self._ev
+            e0.record(self._stream)
+            prog.launch(epoch, self._stream)
+            e1.record(self._stream)
+            e1.synchronize()
+            st.device_ms = e0.elapsed_time(e1)
+            st.status = prog.read_status()
+            st.bytes_read, st.bytes_written = prog.bytes_read, prog.bytes_written
+            for r in self.targets:
+                sess.set(f"done/{self.rank}/{r}/{epoch}", str(st.status))
+            if st.status:
+                prog.clear_status()
+                raise TransferError(f"transfer kernel reported status {st.status:#x} at epoch {epoch}")
+        self.epoch = epoch
+        st.host_ms = (time.perf_counter() - t0) * 1e3
+        self.history.append(st)
+        if len(self.history) > 256:
+            del self.history[:128]
+        return st
+
+
+def gloo_group(sess: Session, rank: int, world: int, timeout_s: float, address: str):
+    """A gloo process group over the session store, separate from the trainer's groups."""
+    opts = dist.ProcessGroupGloo._Options()
+    opts._timeout = timedelta(seconds=timeout_s)
+    ifname = os.environ.get("GLOO_SOCKET_IFNAME")
+    dev = (dist.ProcessGroupGloo.create_device(interface=ifname) if ifname
+           else dist.ProcessGroupGloo.create_device(hostname=address))
+    opts._devices = [dev]
+    return dist.ProcessGroupGloo(dist.PrefixStore("gloo", sess.store), rank, world, opts)
+
+
+def _interleave(parts: list[Tables]) -> Tables:
+    """Concatenate per-receiver tables, interleaving items round-robin across receivers so
+    CTAs running at the same time store to different peers."""
+    if len(parts) <= 1:
+        return Tables.concat(parts)
+    merged = Tables.concat(parts)
+    lens = [len(p.items) for p in parts]
+    keys = np.concatenate([np.arange(n) * len(parts) + i for i, n in enumerate(lens)]) if lens else np.zeros(0)
+    order = np.argsort(keys, kind="stable")
+    merged.items = merged.items[order]
+    return merged

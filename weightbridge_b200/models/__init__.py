@@ -1,0 +1,2 @@
+"""Model architecture descriptors and deterministic synthetic weights."""
+from .arch import PRESETS, ModelArch, get_arch

@@ -45,7 +45,9 @@ def block_quant_fp8_ref(x: torch.Tensor, block: tuple[int, int] = (128, 128)
     pad = torch.zeros(sn * bn, sk * bk, dtype=torch.float32, device=x.device)
     pad[:n, :k] = x32.abs()
     amax = pad.view(sn, bn, sk, bk).amax(dim=(1, 3))
-    scale = torch.where(amax > 0, amax / FP8_E4M3_MAX, torch.ones_like(amax))
+    # tensor / tensor: torch on CUDA turns a division by a Python scalar into a multiply by
+    # the reciprocal, which rounds differently from the IEEE division the kernel performs
+    scale = torch.where(amax > 0, amax / torch.full_like(amax, FP8_E4M3_MAX), torch.ones_like(amax))
     full = scale.repeat_interleave(bn, 0).repeat_interleave(bk, 1)[:n, :k]
     q = (x32 / full).clamp(-FP8_E4M3_MAX, FP8_E4M3_MAX).to(torch.float8_e4m3fn)
     return q, scale

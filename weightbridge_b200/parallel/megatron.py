@@ -131,10 +131,14 @@ class MegatronLayout:
         """Allocate this rank's parameters; ``fill`` writes the synthetic HF weights."""
         params = {n: torch.zeros(s, dtype=dtype, device=device) for n, s in self.param_shapes().items()}
         if fill:
-            meta, views = self.to_wb(params)
-            for name, shards, _ in meta:
-                synth_fill(views[name], name, shards[0], seed=seed)
+            self.fill(params, seed)
         return params
+
+    def fill(self, params: dict[str, torch.Tensor], seed: int = 0) -> None:
+        """Write the synthetic HF weights of ``seed`` into existing parameters, in place."""
+        meta, views = self.to_wb(params)
+        for name, shards, _ in meta:
+            synth_fill(views[name], name, shards[0], seed=seed)
 
     # -- conversion ------------------------------------------------------------------------
     def split_param(self, name: str, param: torch.Tensor) -> list[tuple[str, torch.Tensor, list]]:

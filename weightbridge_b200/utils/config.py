@@ -1,0 +1,63 @@
+"""Transfer configuration (dataclass + ``WBRIDGE_*`` environment overrides).
+
+The reference has no configuration beyond constructor arguments (``transfer_mode`` in
+``wbridge/frontend/sender.py:15-20``, ``ConnectRequest`` in ``wbridge/frontend/receiver.py:38-45``)
+and derives ports from ``CUDA_VISIBLE_DEVICES`` (``wbridge/utils/distributed.py:24-25``).
+Here every wait has a deadline and the rendezvous port is chosen by the OS unless given.
+"""
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass, field, fields
+
+MODE_ALIASES = {
+    "gpu_direct": "gpu_direct", "p2p": "gpu_direct", "ipc": "gpu_direct", "ipc_local": "gpu_direct",
+    "cpu_direct": "cpu_direct", "cpu": "cpu_direct", "gloo": "cpu_direct",
+    "nvls": "nvls", "multicast": "nvls",
+}
+
+
+def normalize_mode(mode: str) -> str:
+    try:
+        return MODE_ALIASES[mode]
+    except KeyError:
+        raise ValueError(f"Invalid transfer mode: {mode!r} (expected one of {sorted(MODE_ALIASES)})") from None
+
+
+@dataclass
+class TransferConfig:
+    mode: str = "gpu_direct"
+    master_address: str = "127.0.0.1"     # address of the session store (sender rank 0)
+    master_port: int = 0                  # 0: let the OS pick a free port
+    connect_timeout_s: float = 120.0      # rendezvous, metadata exchange, plan agreement
+    sync_timeout_s: float = 300.0         # one send()/request_update() round
+    http_timeout_s: float = 60.0
+    zmq_timeout_s: float = 60.0
+    kernel_mode: int = 1                  # 0 vector, 1/2/3 TMA bulk pipeline depths
+    piece_bytes: int = 16384
+    item_bytes: int = 1 << 19
+    grid: int = 0                         # 0: sized from the SM count
+    verify_flags: bool = True             # receiver checks every sender's epoch flag
+    load_balance: bool = True             # spread replicated shards over senders
+    debug_bounds: bool = False            # validate every work row against registered ranges
+
+    def __post_init__(self):
+        self.mode = normalize_mode(self.mode)
+
+    @staticmethod
+    def from_env(**overrides) -> "TransferConfig":
+        kw = {}
+        for f in fields(TransferConfig):
+            v = os.environ.get("WBRIDGE_" + f.name.upper())
+            if v is None:
+                continue
+            if f.type in ("int", int):
+                kw[f.name] = int(v)
+            elif f.type in ("float", float):
+                kw[f.name] = float(v)
+            elif f.type in ("bool", bool):
+                kw[f.name] = v.lower() in ("1", "true", "yes", "on")
+            else:
+                kw[f.name] = v
+        kw.update({k: v for k, v in overrides.items() if v is not None})
+        return TransferConfig(**kw)
