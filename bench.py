@@ -1,129 +1,378 @@
-"""Full weight-sync benchmark: Megatron trainer layout -> SGLang rollout layout, synthetic
-random-init weights of the named architecture, device-timed (CUDA events, max over ranks).
+"""Full weight-sync benchmark through the public API: Megatron trainer layout -> SGLang
+rollout layout, synthetic random-init weights of the named architecture (N(0, 0.02),
+bf16), one process per GPU role, receivers' memory mapped into the senders with CUDA IPC.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--model llama3-8b] [--impl wbridge|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config llama8b] [--impl wbridge|reference]
+  (N > 1: torchrun --nproc-per-node N ... bench.py --gpus N ...)
 
-Layout per N (strong scaling: the model, hence the bytes moved per sync, is fixed):
-  N=1  colocated: trainer TP1 and rollout TP1 on the same GPU (HBM -> HBM)
-  N=2  TP1 -> TP1, trainer GPU 0, rollout GPU 1 (NVLink)
-  N=4  TP2 -> TP2, trainer GPUs 0-1, rollout GPUs 2-3
-  N=8  TP4 -> TP4, trainer GPUs 0-3, rollout GPUs 4-7
+Configurations (strong scaling: the model, hence the bytes moved per sync, is fixed):
+  llama8b            Llama-3-8B.  N=1: trainer TP1 and rollout TP1 colocated on GPU 0 (two
+                     processes); N=2: TP1 -> TP1; N=4: TP2 -> TP2; N=8: TP4 -> TP4 (disaggregated)
+  llama8b-fanout     Llama-3-8B, trainer TP2 x PP2 -> 4 rollout replicas at TP1 (N=8);
+                     N=2: TP1 -> 1 replica, N=4: PP2 -> 2 replicas
+  qwen3-moe-fp8      Qwen3-30B-A3B, trainer EP4 -> rollout TP4 (EP4 experts), experts quantised
+                     to fp8 e4m3 with 128x128 fp32 block scales in the transfer kernel (N=8)
+  llama70b-colocated Llama-3-70B, trainer TP8 on GPUs 0-7 -> two rollout replicas at TP4 in
+                     separate processes on GPUs 0-3 and 4-7 (N=8, 16 processes)
+
+Two timed phases, both after W warm-up syncs through the public API:
+  value: K back-to-back transfer launches per sender (WeightSender.launch) bracketed by CUDA
+         events on the transfer stream, barrier + synchronize on both sides, max over ranks;
+  e2e:   K full syncs through the public API (HTTP arm, ready/done handshake, epoch H2D from
+         pinned memory, kernel, status / flag words D2H), wall clock, max over ranks.
+Inputs are larger than L2 (GBs per sync), so no L2 flush is needed between iterations.
 """
 from __future__ import annotations
 
 import argparse
 import json
 import os
+import socket
 import sys
+import threading
 import time
-
-import torch
-import torch.distributed as dist
+from dataclasses import dataclass, field
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-if ROOT not in sys.path:
-    sys.path.insert(0, ROOT)
 
 METRIC = "full weight-sync latency (s, device-timed, max over ranks) + effective GB/s/GPU"
-BASELINE_PUBLISHED = None   # the reference publishes no number
+BASELINE_PUBLISHED = None   # the reference publishes no number (BASELINE.md)
 
 
-def parse():
+def parse(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--model", default="llama3-8b")
+    p.add_argument("--config", default="llama8b",
+                   choices=["llama8b", "llama8b-fanout", "qwen3-moe-fp8", "llama70b-colocated"])
     p.add_argument("--impl", default="wbridge", choices=["wbridge", "reference"])
-    p.add_argument("--mode", type=int, default=None, help="kernel mode (0 vector, 1/2/3 TMA bulk)")
+    p.add_argument("--mode", type=int, default=None, help="kernel mode: 0 vector, 1/2/3 TMA bulk")
     p.add_argument("--piece", type=int, default=None)
-    p.add_argument("--item-bytes", type=int, default=1 << 19)
+    p.add_argument("--item-bytes", type=int, default=None)
     p.add_argument("--no-verify", action="store_true")
-    return p.parse_args()
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args(argv)
 
 
-def reference_unavailable(args):
-    why = ("the reference's stock send path cannot run: WeightTensorBridge binds uint8 wire slices and "
-           "then asserts they match the bf16 metadata dtype (wbridge/utils/data.py:227-229, 300-305), and "
-           "GPUDirectSender NCCL-sends a CPU pack buffer (data.py:300, direct_sender.py:192-195)")
-    if int(os.environ.get("RANK", "0")) == 0:
-        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+# ----------------------------------------------------------------------------------------
+# reference arm: the unmodified reference, through its own public API, on CPU tensors
+# ----------------------------------------------------------------------------------------
+def reference_arm(args):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "wbridge")):
+        print(json.dumps({"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}))
+        return
+    sys.path.insert(0, ref)
+    try:
+        import torch
+        from wbridge import WeightData  # the reference package
+        # the exact call GPUDirectSender.send makes (wbridge/backend/direct_sender.py:192):
+        #   chunks = self.metadata(state_dict)[self.overlaps]
+        meta = WeightData({"w": {"shard": [(0, 4, 4), (0, 8, 8)], "dtype": "bfloat16"}})
+        peer = WeightData({"w": {"shard": [(0, 2, 4), (0, 8, 8)], "dtype": "bfloat16"}})
+        overlaps = {1: WeightData.compute_overlap(meta, peer)}
+        meta({"w": torch.zeros(4, 8, dtype=torch.bfloat16)})[overlaps]
+        why = None
+    except Exception as e:  # noqa: BLE001 - the reason is what we report
+        why = (f"the reference's stock GPUDirectSender.send path raises {type(e).__name__}: {e} "
+               "(wbridge/utils/data.py:227-229: uint8 wire slices checked against the bf16 metadata dtype); "
+               "its pack buffer is also a CPU tensor handed to NCCL isend (data.py:300, direct_sender.py:192-195)")
+    if why is None:
+        why = "the reference's pack path unexpectedly succeeded on CPU; its GPU path still NCCL-sends CPU buffers"
+    print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
 
 
-def colocated_one_gpu(args):
-    from weightbridge_b200.core.binding import bind
-    from weightbridge_b200.core.plan import lower_ops, phys_binding, plan_pair
+# ----------------------------------------------------------------------------------------
+# scenario: one role per process
+# ----------------------------------------------------------------------------------------
+@dataclass
+class Role:
+    kind: str                      # trainer | rollout
+    device: int
+    layout: dict = field(default_factory=dict)
+    engine: int = -1
+    worker: int = -1
+    host: bool = False
+
+
+def scenario(config: str, n: int) -> tuple[str, list[Role], str]:
+    if config == "llama8b":
+        if n == 1:
+            return "llama3-8b", [Role("trainer", 0, dict(tp=1)),
+                                 Role("rollout", 0, dict(tp=1), 0, 0, True)], "tp1->tp1 colocated (1 GPU, 2 processes)"
+        t = n // 2
+        roles = [Role("trainer", i, dict(tp=t, tp_rank=i)) for i in range(t)]
+        roles += [Role("rollout", t + i, dict(tp=t, tp_rank=i), 0, i, i == 0) for i in range(t)]
+        return "llama3-8b", roles, f"tp{t}->tp{t} disaggregated"
+    if config == "llama8b-fanout":
+        if n not in (2, 4, 8):
+            raise SystemExit("llama8b-fanout runs on 2, 4 or 8 GPUs")
+        tp, pp = {2: (1, 1), 4: (1, 2), 8: (2, 2)}[n]
+        roles = [Role("trainer", i, dict(tp=tp, pp=pp, tp_rank=i % tp, pp_rank=i // tp)) for i in range(tp * pp)]
+        reps = n - tp * pp
+        roles += [Role("rollout", tp * pp + j, dict(tp=1), j, 0, True) for j in range(reps)]
+        return "llama3-8b", roles, f"tp{tp}xpp{pp} -> {reps} replicas x tp1 (fan-out)"
+    if config == "qwen3-moe-fp8":
+        if n not in (2, 4, 8):
+            raise SystemExit("qwen3-moe-fp8 runs on 2, 4 or 8 GPUs")
+        t = n // 2
+        roles = [Role("trainer", i, dict(ep=t, ep_rank=i)) for i in range(t)]
+        roles += [Role("rollout", t + i, dict(tp=t, tp_rank=i, moe_ep=t, quant="fp8_experts"), 0, i, i == 0)
+                  for i in range(t)]
+        return "qwen3-30b-a3b", roles, f"ep{t}->tp{t} (ep{t} experts, fp8 e4m3 128x128 blocks)"
+    if config == "llama70b-colocated":
+        if n != 8:
+            raise SystemExit("llama70b-colocated runs on 8 GPUs")
+        roles = [Role("trainer", i, dict(tp=8, tp_rank=i)) for i in range(8)]
+        roles += [Role("rollout", i, dict(tp=4, tp_rank=i % 4), i // 4, i % 4, i % 4 == 0) for i in range(8)]
+        return "llama3-70b", roles, "tp8 -> 2 replicas x tp4, colocated (16 processes)"
+    raise SystemExit(f"unknown config {config}")
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def child_main(idx: int, port: int, nprocs: int, argv: list[str]):
+    args = parse(argv)
+    run_role(args, idx, nprocs, f"tcp://127.0.0.1:{port}")
+
+
+def launch_main(args):
+    import multiprocessing as mp
+
+    import torch.distributed as dist
+    launched = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if launched != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={launched}")
+    _model, roles, _desc = scenario(args.config, args.gpus)
+    nprocs = len(roles)
+    children = []
+    argv = sys.argv[1:]
+    if launched == 1:
+        port = _free_port()
+        init = f"tcp://127.0.0.1:{port}"
+    else:
+        dist.init_process_group("gloo")
+        if nprocs == launched:
+            init = None
+        else:
+            obj = [_free_port() if rank == 0 else None]
+            dist.broadcast_object_list(obj, src=0)
+            port = obj[0]
+            dist.destroy_process_group()
+            init = f"tcp://{os.environ.get('MASTER_ADDR', '127.0.0.1')}:{port}"
+    ctx = mp.get_context("spawn")
+    for idx in range(launched + rank, nprocs, launched) if nprocs > launched else []:
+        p = ctx.Process(target=child_main, args=(idx, port, nprocs, argv))
+        p.start()
+        children.append(p)
+    try:
+        run_role(args, rank, nprocs, init)
+    finally:
+        for p in children:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+
+
+def run_role(args, idx: int, nprocs: int, init: str | None):
+    sys.path.insert(0, ROOT)
+    import torch
+    import torch.distributed as dist
+
+    from weightbridge_b200 import TransferConfig, WeightReceiver, WeightReceiverController, WeightSender
     from weightbridge_b200.models.arch import get_arch
-    from weightbridge_b200.ops.executor import LaunchConfig, TransferProgram
     from weightbridge_b200.parallel.megatron import MegatronLayout
     from weightbridge_b200.parallel.sglang import SGLangLayout
-    from weightbridge_b200.utils.timing import ClockSampler, EventTimer
+    from weightbridge_b200.utils.timing import ClockSampler
 
-    dev = torch.device("cuda", 0)
+    if init is not None:
+        dist.init_process_group("gloo", init_method=init, rank=idx, world_size=nprocs)
+    model, roles, desc = scenario(args.config, args.gpus)
+    role = roles[idx]
+    arch = get_arch(model)
+    dev = torch.device("cuda", role.device)
     torch.cuda.set_device(dev)
-    arch = get_arch(args.model)
-    meg = MegatronLayout(arch, tp=1)
-    sgl = SGLangLayout(arch, tp=1)
-    t0 = time.time()
-    sparams = meg.allocate(device=dev, dtype=torch.bfloat16)
-    smeta, sviews = meg.to_wb(sparams)
-    rparams = sgl.allocate(device=dev, dtype=torch.bfloat16)
-    rmeta, rviews = sgl.to_wb(rparams)
-    ops = plan_pair(phys_binding(bind(smeta, sviews)), phys_binding(bind(rmeta, rviews)))
-    tables = lower_ops(ops, lambda a: 0, lambda a: 0, item_bytes=args.item_bytes)
-    cfg = LaunchConfig.from_env()
+    trainer_ranks = [i for i, r in enumerate(roles) if r.kind == "trainer"]
+    tgroup = dist.new_group(trainer_ranks, backend="gloo")
+    cfg = TransferConfig.from_env(mode="gpu_direct", connect_timeout_s=300, sync_timeout_s=300)
     if args.mode is not None:
-        cfg.mode = args.mode
+        cfg.kernel_mode = args.mode
     if args.piece is not None:
         cfg.piece_bytes = args.piece
-    flag = torch.zeros(1, dtype=torch.int64, device=dev)
-    prog = TransferProgram(tables, dev, [flag.data_ptr()], cfg)
-    setup_s = time.time() - t0
-    stream = torch.cuda.Stream(dev)
-    for w in range(args.warmup):
-        prog.launch(epoch=w + 1, stream=stream)
+    if args.item_bytes is not None:
+        cfg.item_bytes = args.item_bytes
+
+    t_setup = time.time()
+    server = ctl = recv = sender = None
+    if role.kind == "trainer":
+        lay = MegatronLayout(arch, **role.layout)
+        params = lay.allocate(device=dev, dtype=torch.bfloat16)
+        meta, views = lay.to_wb(params)
+    else:
+        lay = SGLangLayout(arch, **role.layout)
+        params = lay.allocate(device=dev, dtype=torch.bfloat16)
+        meta, views = lay.to_wb(params)
     torch.cuda.synchronize()
-    with ClockSampler(gpu_index=None) as clk:
+
+    # rollout engines: HTTP server + controller in the host process of each engine
+    engine_info = None
+    if role.kind == "rollout" and role.host:
+        import uvicorn
+        from fastapi import FastAPI
+        nworkers = sum(1 for r in roles if r.kind == "rollout" and r.engine == role.engine)
+        app = FastAPI()
+        ctl = WeightReceiverController(app, worker_num=nworkers, timeout_s=300)
+        port = _free_port()
+        server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="warning"))
+        threading.Thread(target=server.run, daemon=True).start()
+        while not server.started:
+            time.sleep(0.02)
+        engine_info = (role.engine, f"http://127.0.0.1:{port}", ctl.ipc_name)
+    infos = [None] * nprocs
+    dist.all_gather_object(infos, engine_info)
+    engines = {e[0]: e for e in infos if e is not None}
+    urls = [engines[k][1] for k in sorted(engines)]
+    if role.kind == "rollout":
+        recv = WeightReceiver(engines[role.engine][2], role.worker, meta, state_dict=views, device=dev, config=cfg)
+    dist.barrier()
+    if role.kind == "trainer":
+        sender = WeightSender("gpu_direct", urls, group=tgroup, config=cfg)
+        sender.connect(meta)
+    dist.barrier()
+    setup_s = time.time() - t_setup
+
+    def public_sync():
+        if sender is not None:
+            sender.send(views)
+        else:
+            ok = recv.request_update(timeout=cfg.sync_timeout_s)
+            if not ok:
+                raise RuntimeError("request_update returned False")
+
+    for _ in range(args.warmup):
+        public_sync()
+    torch.cuda.synchronize()
+
+    # phase A: device-timed transfer launches
+    stream = torch.cuda.Stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler() if idx == 0 else None
+    dist.barrier()
+    torch.cuda.synchronize()
+    if clk:
+        clk.__enter__()
+    dist.barrier()
+    e0.record(stream)
+    if sender is not None:
+        for _ in range(args.steps):
+            sender.launch(views, stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    if clk:
+        clk.__exit__(None, None, None)
+    my_ms = e0.elapsed_time(e1) / args.steps if sender is not None else 0.0
+
+    # phase B: public API end to end
+    e2e_ms = 0.0
+    if not args.no_e2e:
+        dist.barrier()
         torch.cuda.synchronize()
-        with EventTimer(stream) as tm:
-            for k in range(args.steps):
-                prog.launch(epoch=args.warmup + k + 1, stream=stream)
-        ms = tm.ms() / args.steps
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            public_sync()
         torch.cuda.synchronize()
-    status = prog.read_status()
-    ok = None
-    if not args.no_verify:
-        expected = sgl.allocate(device=dev, dtype=torch.bfloat16, fill=True)
-        ok = all(torch.equal(rparams[n], expected[n]) for n in rparams)
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+        dist.barrier()
+
+    ok = 1
+    if role.kind == "rollout" and not args.no_verify:
+        del_views = None
+        expected = lay.allocate(device=dev, dtype=torch.bfloat16, fill=True)
+        for n in params:
+            a, b = params[n], expected[n]
+            if a.dtype == torch.float8_e4m3fn:
+                a, b = a.view(torch.uint8), b.view(torch.uint8)
+            if not torch.equal(a, b):
+                ok = 0
+                print(f"[rank {idx}] mismatch in {n}", flush=True)
+                break
         del expected
-    payload = tables.bytes_written
-    lat = ms / 1e3
-    gbs = payload / lat / 1e9
-    return {
-        "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init N(0,0.02) weights, hashed per element)",
-        "config": {"model": args.model, "layout": "Megatron TP1 -> SGLang TP1, colocated on one GPU",
-                   "global_batch": None, "seq_len": None, "parallelism": "tp1->tp1",
-                   "payload_bytes": payload, "l2": "inputs larger than L2 (16 GB per sync)",
-                   "kernel_mode": cfg.mode, "piece_bytes": cfg.piece_bytes, "items": len(tables.items),
-                   "grid": prog.grid(), "path": "in-process data plane"},
-        "latency_s": round(lat, 6), "gbs_per_gpu": round(gbs, 2),
-        "hbm_traffic_gbs": round(2 * payload / lat / 1e9, 1),
-        "clocks": clk.summary(), "gpu_launches": args.steps, "status": status, "verified": ok,
-        "setup_s": round(setup_s, 1),
-    }
+    payload = sender.program.bytes_written if (sender is not None and sender.program is not None) else 0
+    read = sender.program.bytes_read if (sender is not None and sender.program is not None) else 0
+    active = 1 if payload else 0
+    h2d = 8 * active
+    d2h = 4 * active + (int(recv.flags.nbytes) if recv is not None and cfg.verify_flags else 0)
+    items = len(sender.program.tables.items) if (sender is not None and sender.program is not None) else 0
+    grid = sender.program.grid() if (sender is not None and sender.program is not None) else 0
+    stats = torch.tensor([my_ms, e2e_ms, payload, read, ok, h2d, d2h, active, items, grid, setup_s],
+                         dtype=torch.float64)
+    gathered = [torch.zeros_like(stats) for _ in range(nprocs)]
+    dist.all_gather(gathered, stats)
+    G = torch.stack(gathered)
+
+    if idx == 0:
+        ms = float(G[:, 0].max())
+        e2e = float(G[:, 1].max())
+        payload_total = float(G[:, 2].sum())
+        ngpu = args.gpus
+        lat = ms / 1e3
+        value = payload_total / lat / 1e9
+        res = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ngpu, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: random-init N(0,0.02) weights of the architecture (hashed per element)",
+            "config": {"model": model, "config": args.config, "layout": desc, "global_batch": None, "seq_len": None,
+                       "parallelism": desc, "payload_bytes_per_sync": int(payload_total),
+                       "bytes_read_per_sync": int(G[:, 3].sum()),
+                       "l2": "inputs larger than L2 (GBs per sync); no flush needed",
+                       "kernel_mode": cfg.kernel_mode, "piece_bytes": cfg.piece_bytes,
+                       "item_bytes": cfg.item_bytes, "work_items_max": int(G[:, 8].max()),
+                       "grid": int(G[:, 9].max()), "processes": nprocs},
+            "latency_s": round(lat, 6),
+            "gbs_per_gpu": round(value / ngpu, 2),
+            "gbs_per_sender": round(value / max(1.0, float(G[:, 7].sum())), 2),
+            "e2e": None if args.no_e2e else {
+                "value": round(payload_total / (e2e / 1e3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(e2e, 4), "latency_s": round(e2e / 1e3, 6),
+                "h2d_bytes_per_step": int(G[:, 5].sum()), "d2h_bytes_per_step": int(G[:, 6].sum()),
+                "path": "WeightSender.send + WeightReceiver.request_update (HTTP arm, store handshake, IPC peer stores)"},
+            "gpu_launches": int(args.steps * G[:, 7].sum()),
+            "clocks": clk.summary() if clk else None,
+            "verified": bool(G[:, 4].min() == 1) if not args.no_verify else None,
+            "setup_s": round(float(G[:, 10].max()), 1),
+            "impl": "wbridge",
+        }
+        print(json.dumps(res), flush=True)
+
+    dist.barrier()
+    if recv is not None:
+        recv.stop()
+    if sender is not None:
+        sender.disconnect()
+    dist.barrier()
+    if server is not None:
+        server.should_exit = True
+    if ctl is not None:
+        ctl.close()
+    dist.destroy_process_group()
 
 
 def main():
     args = parse()
     if args.impl == "reference":
-        reference_unavailable(args)
+        reference_arm(args)
         return
-    if args.gpus != 1:
-        raise SystemExit("multi-GPU bench arrives with the IPC control plane")
-    res = colocated_one_gpu(args)
-    print(json.dumps(res), flush=True)
+    launch_main(args)
 
 
 if __name__ == "__main__":

@@ -1,0 +1,118 @@
+"""Multi-process end-to-end harness: one rollout process (FastAPI + controller + receiver
+worker) and N trainer processes (torch.distributed gloo group), all through the public API.
+Used by the CPU (gloo transport) and GPU (CUDA IPC, colocated on one GPU) tests."""
+import multiprocessing as mp
+import queue
+import socket
+import time
+
+import torch
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype):
+    import threading
+    import uvicorn
+    from fastapi import FastAPI
+    from weightbridge_b200 import TransferConfig, WeightReceiver, WeightReceiverController
+    from weightbridge_b200.models.arch import get_arch
+    from weightbridge_b200.parallel.sglang import SGLangLayout
+    try:
+        if device != "cpu":
+            torch.cuda.set_device(torch.device(device))
+        app = FastAPI()
+        ctl = WeightReceiverController(app, worker_num=1, timeout_s=60)
+        lay = SGLangLayout(get_arch(model), **rlayout)
+        params = lay.allocate(device=device, dtype=dtype)
+        meta, views = lay.to_wb(params)
+        cfg = TransferConfig(mode=mode, connect_timeout_s=60, sync_timeout_s=60)
+        recv = WeightReceiver(ctl.ipc_name, 0, meta, state_dict=views, config=cfg)
+        server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="warning"))
+        threading.Thread(target=server.run, daemon=True).start()
+        t0 = time.time()
+        while not server.started and time.time() - t0 < 30:
+            time.sleep(0.05)
+        results = []
+        for i in range(n_syncs):
+            ok = recv.request_update(timeout=60)
+            exp = lay.allocate(device=device, dtype=dtype, fill=True, seed=i)
+            same = all(torch.equal(params[n].view(torch.uint8) if params[n].dtype == torch.float8_e4m3fn else params[n],
+                                   exp[n].view(torch.uint8) if exp[n].dtype == torch.float8_e4m3fn else exp[n])
+                       for n in params)
+            results.append(bool(ok) and same)
+        stats = ctl.get_stats()
+        q.put(("rollout", results, stats[0]["epoch"]))
+        recv.stop()
+        server.should_exit = True
+        ctl.close()
+    except Exception:
+        import traceback
+        q.put(("error", traceback.format_exc(), None))
+
+
+def trainer_proc(rank, world, tport, url, q, n_syncs, model, mode, device, layouts, dtype):
+    import torch.distributed as dist
+    from weightbridge_b200 import TransferConfig, WeightSender
+    from weightbridge_b200.models.arch import get_arch
+    from weightbridge_b200.parallel.megatron import MegatronLayout
+    try:
+        if device != "cpu":
+            torch.cuda.set_device(torch.device(device))
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{tport}", rank=rank, world_size=world)
+        lay = MegatronLayout(get_arch(model), **layouts[rank])
+        params = lay.allocate(device=device, dtype=dtype, seed=0)
+        meta, views = lay.to_wb(params)
+        cfg = TransferConfig(mode=mode, connect_timeout_s=60, sync_timeout_s=60)
+        sender = WeightSender(mode, [url], config=cfg)
+        sender.connect(meta)
+        for i in range(n_syncs):
+            if i:
+                lay.fill(params, seed=i)
+            sender.send(views)
+        q.put(("trainer", rank, sender.epoch))
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+        q.put(("error", traceback.format_exc(), rank))
+
+
+def run(model, mode, trainer_layouts, rollout_layout, device="cpu", dtype=torch.float32, n_syncs=3, timeout=240):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    hport, tport = _port(), _port()
+    url = f"http://127.0.0.1:{hport}"
+    world = len(trainer_layouts)
+    procs = [ctx.Process(target=rollout_proc, args=(hport, q, n_syncs, model, mode, device, rollout_layout, dtype))]
+    procs += [ctx.Process(target=trainer_proc, args=(r, world, tport, url, q, n_syncs, model, mode, device,
+                                                      trainer_layouts, dtype)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = []
+    deadline = time.time() + timeout
+    try:
+        while len(got) < world + 1 and time.time() < deadline:
+            try:
+                item = q.get(timeout=1)
+            except queue.Empty:
+                if any(p.exitcode not in (None, 0) for p in procs):
+                    break
+                continue
+            if item[0] == "error":
+                raise AssertionError(item[1])
+            got.append(item)
+    finally:
+        for p in procs:
+            p.join(timeout=15)
+            if p.is_alive():
+                p.kill()
+    roll = [g for g in got if g[0] == "rollout"]
+    assert roll, f"no rollout result: {got}"
+    assert roll[0][1] == [True] * n_syncs, roll
+    assert roll[0][2] == n_syncs
+    assert sorted(g[1] for g in got if g[0] == "trainer") == list(range(world))
+    return got

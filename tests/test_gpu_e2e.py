@@ -1,0 +1,19 @@
+"""Public API on one GPU: trainer and rollout in separate processes, colocated on cuda:0,
+receiver memory mapped into the senders with CUDA IPC, the sm_100a kernel moving the data.
+No kernel waits on another process's kernel (completion goes through the session store)."""
+import pytest
+import torch
+
+from tests.e2e_harness import run
+
+pytestmark = pytest.mark.gpu
+
+
+def test_colocated_ipc_tiny_llama_tp2_to_tp1():
+    run("tiny-llama", "gpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)], dict(tp=1),
+        device="cuda:0", dtype=torch.bfloat16)
+
+
+def test_colocated_ipc_qwen3_moe_fp8_experts():
+    run("tiny-qwen3-moe", "gpu_direct", [dict(ep=2, ep_rank=0), dict(ep=2, ep_rank=1)],
+        dict(tp=1, quant="fp8_experts"), device="cuda:0", dtype=torch.bfloat16, n_syncs=2)

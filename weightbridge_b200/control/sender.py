@@ -212,6 +212,9 @@ class WeightSender:
     # -- send ----------------------------------------------------------------------------------
     def _compile(self, state_dict) -> None:
         cfg = self.config
+        if not self.targets:
+            self._program = None
+            return
         binding = bind(self.metadata, state_dict)
         device = binding.device
         sphys = phys_binding(binding)
@@ -255,6 +258,27 @@ class WeightSender:
                 out.append(v.data_ptr())
         return tuple(out)
 
+    def launch(self, state_dict: dict[str, Any], stream: torch.cuda.Stream | None = None) -> None:
+        """Enqueue this sender's transfer kernel on ``stream`` with no HTTP arm, no handshake
+        and no host synchronisation.  For callers that already know the rollout side is
+        idle (and for device-timed benchmarks): the receivers' epoch flags are not touched,
+        so a later ``send`` still pairs with ``request_update``."""
+        if not self.connected:
+            raise RuntimeError("WeightSender.launch requires connect() first")
+        if self.config.mode == "cpu_direct":
+            raise RuntimeError("launch() is a device path; cpu_direct uses send()")
+        key = self._key(state_dict)
+        if self._program_key != key:
+            self._compile(state_dict)
+            self._program_key = key
+        if self._program is not None and len(self._program.tables):
+            self._program.launch(0, stream or torch.cuda.current_stream(self._program.device), signal=False)
+
+    @property
+    def program(self):
+        """The compiled transfer program (tables, grid, byte counts), once compiled."""
+        return self._program
+
     def send(self, state_dict: dict[str, Any]) -> SyncStats:
         if not self.connected or self.metadata is None:
             raise RuntimeError("WeightSender.send requires connect() first")
@@ -290,7 +314,7 @@ class WeightSender:
                 st.bytes_written += wire.numel()
             for w in works:
                 w.wait()
-        else:
+        elif self.targets:
             prog = self._program
             cur = torch.cuda.current_stream(prog.device)
             self._stream.wait_stream(cur)

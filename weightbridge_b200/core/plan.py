@@ -168,8 +168,6 @@ def plan_pair(src: PhysBinding, dst: PhysBinding, names: Iterable[str] | None = 
             continue
         d_dtype = dst.meta.dtype(name)
         q = qsrc.quant(name) if name in qsrc else None
-        if q and q.get("role") == "scale":
-            continue
         quant = bool(q and q.get("format") == "fp8_block" and d_dtype != s_dtype)
         if not quant and d_dtype != s_dtype and not (s_dtype in FLOAT_CAST_DTYPES and d_dtype in FLOAT_CAST_DTYPES):
             raise TypeError(f"{name}: no conversion from {s_dtype} to {d_dtype}")

@@ -110,18 +110,20 @@ class TransferProgram:
             per_sm = max(1, min(4, (200 * 1024) // max(smem, 1)))
         return max(1, min(work, self.n_sms * per_sm))
 
-    def launch(self, epoch: int, stream: torch.cuda.Stream | None = None) -> None:
-        """Copy the epoch host->device and launch the kernel on ``stream``."""
+    def launch(self, epoch: int, stream: torch.cuda.Stream | None = None, signal: bool = True) -> None:
+        """Copy the epoch host->device and launch the kernel on ``stream``.  With
+        ``signal=False`` the launch publishes no flags (ordering is the caller's job)."""
         stream = stream or torch.cuda.current_stream(self.device)
         c = self.config
         with torch.cuda.stream(stream):
-            self.epoch_host[0] = epoch
-            self.epoch_dev.copy_(self.epoch_host, non_blocking=True)
+            if signal:
+                self.epoch_host[0] = epoch
+                self.epoch_dev.copy_(self.epoch_host, non_blocking=True)
             ext().transfer(
                 self.items.data_ptr(), len(self.items_np), self.bulk.data_ptr(), len(self.bulk_np),
                 self.qdescs.data_ptr(), self.qwork.data_ptr(), len(self.tables.qwork),
-                c.piece_bytes, c.spin_limit, self.counter.data_ptr(),
-                self.flags.data_ptr() if self.n_flags else 0, self.n_flags,
+                c.piece_bytes, c.spin_limit, self.counter.data_ptr() if signal else 0,
+                self.flags.data_ptr() if self.n_flags else 0, self.n_flags if signal else 0,
                 self.epoch_dev.data_ptr(), self.status.data_ptr(), c.mode if len(self.bulk_np) else MODE_VECTOR,
                 self.grid(), stream.cuda_stream)
         self.launches += 1

@@ -1,0 +1,98 @@
+"""Microbenchmark of the transfer kernel on one GPU (also the small case for ncu captures).
+
+  python -m weightbridge_b200.ops.microbench --case copy  --gbytes 1 --mode 1
+  python -m weightbridge_b200.ops.microbench --case quant --gbytes 1
+  python -m weightbridge_b200.ops.microbench --case strided --gbytes 1
+
+copy:    one contiguous bf16 buffer -> another (HBM read + write), 16-byte aligned;
+strided: column block of a row-major matrix -> contiguous (TP column split), 2-D items;
+quant:   bf16 [E, 768, 2048] expert stack -> fp8 e4m3 + 128x128 fp32 block scales.
+Reports device time per launch (CUDA events, after warm-up) and achieved bandwidth against
+the measured copy peak in MEASURED_PEAKS.json when present.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+from ..core.plan import Op, lower_ops
+from .executor import LaunchConfig, TransferProgram
+
+
+def _peak_gbs() -> float | None:
+    here = os.path.dirname(os.path.abspath(__file__))
+    p = os.path.join(here, "..", "..", "MEASURED_PEAKS.json")
+    try:
+        return float(json.load(open(p))["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+def build(case: str, gbytes: float, dev, item_bytes: int):
+    n = int(gbytes * (1 << 30)) // 2
+    if case == "copy":
+        a = torch.randn(n, device=dev, dtype=torch.bfloat16)
+        b = torch.empty_like(a)
+        ops = [Op("copy", "x", (-1, a.data_ptr()), (-1, b.data_ptr()), [n], [1], [1], a.dtype, a.dtype)]
+        keep, traffic = (a, b), 2 * a.nbytes
+    elif case == "strided":
+        cols = 14336
+        rows = max(1, n // cols)
+        a = torch.randn(rows, cols, device=dev, dtype=torch.bfloat16)
+        half = cols // 2
+        b = torch.empty(rows, half, device=dev, dtype=torch.bfloat16)
+        ops = [Op("copy", "x", (-1, a.data_ptr() + half * 2), (-1, b.data_ptr()), [rows, half], [cols, 1], [half, 1],
+                  a.dtype, a.dtype)]
+        keep, traffic = (a, b), 2 * b.nbytes
+    elif case == "quant":
+        r, c = 768, 2048
+        e = max(1, n // (r * c))
+        a = torch.randn(e, r, c, device=dev, dtype=torch.bfloat16)
+        q = torch.empty(e, r, c, device=dev, dtype=torch.float8_e4m3fn)
+        s = torch.empty(e, r // 128, c // 128, device=dev, dtype=torch.float32)
+        ops = [Op("quant", "x", (-1, a[i].data_ptr()), (-1, q[i].data_ptr()), [r, c], [c, 1], [c, 1], a.dtype,
+                  q.dtype, (-1, s[i].data_ptr()), [c // 128, 1], (128, 128)) for i in range(e)]
+        keep, traffic = (a, q, s), a.nbytes + q.nbytes + s.nbytes
+    else:
+        raise SystemExit(f"unknown case {case}")
+    return lower_ops(ops, lambda x: 0, lambda x: 0, item_bytes=item_bytes), keep, traffic
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("--case", default="copy", choices=["copy", "strided", "quant"])
+    p.add_argument("--gbytes", type=float, default=1.0)
+    p.add_argument("--mode", type=int, default=1)
+    p.add_argument("--piece", type=int, default=16384)
+    p.add_argument("--grid", type=int, default=0)
+    p.add_argument("--item-bytes", type=int, default=1 << 19)
+    p.add_argument("--iters", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    a = p.parse_args(argv)
+    dev = torch.device("cuda", 0)
+    tables, keep, traffic = build(a.case, a.gbytes, dev, a.item_bytes)
+    prog = TransferProgram(tables, dev, [], LaunchConfig(mode=a.mode, piece_bytes=a.piece, grid=a.grid or None))
+    for _ in range(a.warmup):
+        prog.launch(0, signal=False)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        prog.launch(0, signal=False)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.iters
+    gbs = traffic / (ms / 1e3) / 1e9
+    peak = _peak_gbs()
+    print(json.dumps({"case": a.case, "gbytes": a.gbytes, "mode": a.mode, "piece": a.piece, "grid": prog.grid(),
+                      "items": len(tables.items), "qwork": len(tables.qwork), "ms": round(ms, 4),
+                      "traffic_bytes": traffic, "gbs": round(gbs, 1),
+                      "frac_of_measured_copy": round(gbs / peak, 3) if peak else None,
+                      "status": prog.read_status()}))
+
+
+if __name__ == "__main__":
+    main()
