@@ -81,14 +81,16 @@ def trainer_proc(rank, world, tport, url, q, n_syncs, model, mode, device, layou
         q.put(("error", traceback.format_exc(), rank))
 
 
-def run(model, mode, trainer_layouts, rollout_layout, device="cpu", dtype=torch.float32, n_syncs=3, timeout=240):
+def run(model, mode, trainer_layouts, rollout_layout, device="cpu", dtype=torch.float32, n_syncs=3, timeout=240,
+        trainer_devices=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     hport, tport = _port(), _port()
     url = f"http://127.0.0.1:{hport}"
     world = len(trainer_layouts)
     procs = [ctx.Process(target=rollout_proc, args=(hport, q, n_syncs, model, mode, device, rollout_layout, dtype))]
-    procs += [ctx.Process(target=trainer_proc, args=(r, world, tport, url, q, n_syncs, model, mode, device,
+    tdev = trainer_devices or [device] * world
+    procs += [ctx.Process(target=trainer_proc, args=(r, world, tport, url, q, n_syncs, model, mode, tdev[r],
                                                       trainer_layouts, dtype)) for r in range(world)]
     for p in procs:
         p.start()
