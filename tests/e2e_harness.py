@@ -37,6 +37,7 @@ def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype):
         t0 = time.time()
         while not server.started and time.time() - t0 < 30:
             time.sleep(0.05)
+        q.put(("serving", None, None))
         results = []
         for i in range(n_syncs):
             ok = recv.request_update(timeout=60)
@@ -92,10 +93,15 @@ def run(model, mode, trainer_layouts, rollout_layout, device="cpu", dtype=torch.
     tdev = trainer_devices or [device] * world
     procs += [ctx.Process(target=trainer_proc, args=(r, world, tport, url, q, n_syncs, model, mode, tdev[r],
                                                       trainer_layouts, dtype)) for r in range(world)]
-    for p in procs:
+    procs[0].start()
+    deadline = time.time() + timeout
+    first = q.get(timeout=120)
+    if first[0] == "error":
+        procs[0].join(timeout=10)
+        raise AssertionError(first[1])
+    for p in procs[1:]:
         p.start()
     got = []
-    deadline = time.time() + timeout
     try:
         while len(got) < world + 1 and time.time() < deadline:
             try:

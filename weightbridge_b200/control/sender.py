@@ -70,6 +70,22 @@ def _http():
     return requests
 
 
+def _get_with_retry(http, url: str, timeout_s: float):
+    """GET with bounded retries while the rollout server is still starting up."""
+    deadline = time.monotonic() + timeout_s
+    delay = 0.05
+    while True:
+        try:
+            resp = http.get(url, timeout=timeout_s)
+            resp.raise_for_status()
+            return resp
+        except http.ConnectionError:
+            if time.monotonic() + delay > deadline:
+                raise
+            time.sleep(delay)
+            delay = min(delay * 2, 1.0)
+
+
 class WeightSender:
     def __init__(self, transfer_mode: str, receiver_urls: list[str], group: Any = None,
                  config: TransferConfig | None = None):
@@ -156,8 +172,7 @@ class WeightSender:
         counts = []
         base = self.world_size
         for url in self.receiver_urls:
-            resp = http.get(f"{url}/wbridge/metadata", timeout=cfg.http_timeout_s)
-            resp.raise_for_status()
+            resp = _get_with_retry(http, f"{url}/wbridge/metadata", cfg.http_timeout_s)
             workers = sorted(resp.json(), key=lambda w: w["rank"])
             for i, w in enumerate(workers):
                 receivers[base + i] = w["metadata"]
