@@ -3,7 +3,7 @@
 // buffer into local shards - and is the oracle the GPU tests compare against.
 //
 // Casts round to nearest even (c10::BFloat16 / c10::Half); block fp8 computes
-// scale = amax / 448 and q = e4m3(clamp(x / scale, +-448)) with IEEE float division, the
+// scale = amax / 448, inv = 1 / scale and q = e4m3(clamp(x * inv, +-448)) in IEEE float, the
 // same arithmetic as the device kernel.
 #include "wb_cpu.h"
 
@@ -76,9 +76,10 @@ void run_quant(const QuantDesc& q, uint32_t block) {
   for (uint32_t r = 0; r < nr; ++r)
     for (uint32_t c = 0; c < nc; ++c) amax = std::max(amax, std::fabs(load_f(src + r * q.src_pitch + (uint64_t)c * es, q.src_code)));
   const float scale = amax > 0.f ? amax / kE4M3Max : 1.f;
+  const float inv = 1.f / scale;
   for (uint32_t r = 0; r < nr; ++r)
     for (uint32_t c = 0; c < nc; ++c) {
-      float x = load_f(src + r * q.src_pitch + (uint64_t)c * es, q.src_code) / scale;
+      float x = load_f(src + r * q.src_pitch + (uint64_t)c * es, q.src_code) * inv;
       x = std::min(std::max(x, -kE4M3Max), kE4M3Max);
       dst[r * q.dst_pitch + c] = c10::Float8_e4m3fn(x).x;
     }

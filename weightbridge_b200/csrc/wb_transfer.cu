@@ -192,7 +192,7 @@ __device__ void generic_item(const Item& it, uint32_t* status) {
 }
 
 // ------------------------------------------------------------------------------------
-// quant blocks: 128 x 128 -> e4m3 + fp32 scale (scale = amax / 448, q = satfinite(x / scale))
+// quant blocks: 128 x 128 -> e4m3 + fp32 scale (scale = amax / 448, q = satfinite(x * RN(1 / scale)))
 // ------------------------------------------------------------------------------------
 __device__ __forceinline__ float block_max(float v, float* red) {
   #pragma unroll
@@ -212,14 +212,6 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return red[32];
 }
 
-__device__ __forceinline__ uint32_t pack4_e4m3(float a, float b, float c, float d, float scale) {
-  const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(__fdiv_rn(a, scale), __fdiv_rn(b, scale)),
-                                                           __NV_SATFINITE, __NV_E4M3);
-  const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(__fdiv_rn(c, scale), __fdiv_rn(d, scale)),
-                                                           __NV_SATFINITE, __NV_E4M3);
-  return (uint32_t)lo | ((uint32_t)hi << 16);
-}
-
 __device__ __forceinline__ float2 unpack2(uint32_t w, bool bf16) {
   if (bf16) {
     __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&w);
@@ -229,6 +221,40 @@ __device__ __forceinline__ float2 unpack2(uint32_t w, bool bf16) {
   return __half22float2(h);
 }
 
+__device__ __forceinline__ uint32_t pack4_e4m3(float a, float b, float c, float d, float inv) {
+  const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(__fmul_rn(a, inv), __fmul_rn(b, inv)),
+                                                           __NV_SATFINITE, __NV_E4M3);
+  const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(__fmul_rn(c, inv), __fmul_rn(d, inv)),
+                                                           __NV_SATFINITE, __NV_E4M3);
+  return (uint32_t)lo | ((uint32_t)hi << 16);
+}
+
+// amax of 8 packed 16-bit floats (bf16 or fp16) without unpacking: max of |x| is exact in
+// the source format.
+__device__ __forceinline__ float amax8(const uint4 v, bool bf16) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  if (bf16) {
+    __nv_bfloat162 m = __float2bfloat162_rn(0.f);
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) m = __hmax2(m, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&w[j])));
+    const float2 f = __bfloat1622float2(m);
+    return fmaxf(f.x, f.y);
+  }
+  __half2 m = __float2half2_rn(0.f);
+  #pragma unroll
+  for (int j = 0; j < 4; ++j) m = __hmax2(m, __habs2(*reinterpret_cast<const __half2*>(&w[j])));
+  const float2 f = __half22float2(m);
+  return fmaxf(f.x, f.y);
+}
+
+// 8 source values (one uint4) -> 8 e4m3 bytes (one uint2)
+__device__ __forceinline__ uint2 quant8(const uint4 v, bool bf16, float inv) {
+  const float2 a = unpack2(v.x, bf16), b = unpack2(v.y, bf16), c = unpack2(v.z, bf16), e = unpack2(v.w, bf16);
+  return make_uint2(pack4_e4m3(a.x, a.y, b.x, b.y, inv), pack4_e4m3(c.x, c.y, e.x, e.y, inv));
+}
+
+// One block of a block-quantised matrix: scale = amax / 448 (IEEE division), inv = RN(1 / scale),
+// q = satfinite_e4m3(x * inv) with round-to-nearest-even; the block's scale goes to the scale grid.
 __device__ void quant_block(const QuantDesc& d, uint32_t block, float* red, uint32_t* status) {
   const uint32_t bn = d.bn, bk = d.bk;
   const uint32_t nbc = (d.cols + bk - 1) / bk;
@@ -245,39 +271,36 @@ __device__ void quant_block(const QuantDesc& d, uint32_t block, float* red, uint
   float scale;
   const bool fast = es == 2 && bk == 128 && bn <= 128 && nc == 128 && blockDim.x == 256 &&
                     ((reinterpret_cast<uint64_t>(src) | (uint64_t)d.src_pitch) & 15) == 0 &&
-                    ((reinterpret_cast<uint64_t>(dst) | (uint64_t)d.dst_pitch) & 7) == 0;
+                    ((reinterpret_cast<uint64_t>(dst) | (uint64_t)d.dst_pitch) & 15) == 0;
   if (fast) {
-    // 16 threads span a 128-element row (8 elements each); 16 row groups x 8 passes
-    const uint32_t col = threadIdx.x & 15, rg = threadIdx.x >> 4;
+    // 8 threads span a 128-column row (16 columns = 32 source bytes each); 32 rows per pass,
+    // 4 passes.  Every thread ends with one 16-byte store per row it owns.
+    const uint32_t col = threadIdx.x & 7, rg = threadIdx.x >> 3;
     const bool bf16 = d.src_code == DT_BF16;
-    uint4 v[8];
-    float amax = 0.f;
+    uint4 v[4][2];
     #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const uint32_t r = rg + 16u * k;
-      v[k] = r < nr ? ld_nc16(src + r * d.src_pitch + col * 16u) : make_uint4(0, 0, 0, 0);
-    }
-    #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-      #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = unpack2(w[j], bf16);
-        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t r = rg + 32u * k;
+      if (r < nr) {
+        const uint8_t* p = src + r * d.src_pitch + col * 32u;
+        v[k][0] = ld_nc16(p);
+        v[k][1] = ld_nc16(p + 16);
+      } else {
+        v[k][0] = v[k][1] = make_uint4(0, 0, 0, 0);
       }
     }
+    float amax = 0.f;
+    #pragma unroll
+    for (int k = 0; k < 4; ++k) amax = fmaxf(amax, fmaxf(amax8(v[k][0], bf16), amax8(v[k][1], bf16)));
     amax = block_max(amax, red);
     scale = amax > 0.f ? __fdiv_rn(amax, kE4M3Max) : 1.f;
+    const float inv = __frcp_rn(scale);
     #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const uint32_t r = rg + 16u * k;
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t r = rg + 32u * k;
       if (r >= nr) continue;
-      const float2 a = unpack2(v[k].x, bf16), b = unpack2(v[k].y, bf16);
-      const float2 c = unpack2(v[k].z, bf16), e = unpack2(v[k].w, bf16);
-      uint2 q;
-      q.x = pack4_e4m3(a.x, a.y, b.x, b.y, scale);
-      q.y = pack4_e4m3(c.x, c.y, e.x, e.y, scale);
-      *reinterpret_cast<uint2*>(dst + r * d.dst_pitch + col * 8u) = q;
+      const uint2 lo = quant8(v[k][0], bf16, inv), hi = quant8(v[k][1], bf16, inv);
+      st16(dst + r * d.dst_pitch + col * 16u, make_uint4(lo.x, lo.y, hi.x, hi.y));
     }
   } else {
     float amax = 0.f;
@@ -288,11 +311,11 @@ __device__ void quant_block(const QuantDesc& d, uint32_t block, float* red, uint
     }
     amax = block_max(amax, red);
     scale = amax > 0.f ? __fdiv_rn(amax, kE4M3Max) : 1.f;
+    const float inv = __frcp_rn(scale);
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
       const uint32_t r = i / nc, c = i - r * nc;
       const float x = ld_as_f32(src + r * d.src_pitch + (uint64_t)c * es, d.src_code);
-      const __nv_fp8_storage_t q = __nv_cvt_float_to_fp8(__fdiv_rn(x, scale), __NV_SATFINITE, __NV_E4M3);
-      dst[r * d.dst_pitch + c] = q;
+      dst[r * d.dst_pitch + c] = __nv_cvt_float_to_fp8(__fmul_rn(x, inv), __NV_SATFINITE, __NV_E4M3);
     }
   }
   if (threadIdx.x == 0)

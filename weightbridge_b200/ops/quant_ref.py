@@ -2,10 +2,10 @@
 
 Block-scaled fp8: a 2-D tensor is cut into ``bn x bk`` blocks (128 x 128 by default; edge
 blocks may be partial).  For each block, ``scale = amax / 448`` in fp32 (``scale = 1`` for an
-all-zero block) and ``q = satfinite_e4m3(x / scale)`` with round-to-nearest-even.  The
-receiver dequantises as ``q * scale``; the scale tensor is what SGLang names
-``weight_scale_inv``.  The CUDA kernel computes the same two IEEE divisions, so the CPU
-oracle and the device agree bit for bit.
+all-zero block), ``inv = 1 / scale`` (IEEE, round to nearest) and
+``q = satfinite_e4m3(x * inv)`` with round-to-nearest-even.  The receiver dequantises as
+``q * scale``; the scale tensor is what SGLang names ``weight_scale_inv``.  The CUDA kernel
+and the C++ CPU executor perform the same IEEE operations, so all three agree bit for bit.
 """
 from __future__ import annotations
 
@@ -48,8 +48,9 @@ def block_quant_fp8_ref(x: torch.Tensor, block: tuple[int, int] = (128, 128)
     # tensor / tensor: torch on CUDA turns a division by a Python scalar into a multiply by
     # the reciprocal, which rounds differently from the IEEE division the kernel performs
     scale = torch.where(amax > 0, amax / torch.full_like(amax, FP8_E4M3_MAX), torch.ones_like(amax))
-    full = scale.repeat_interleave(bn, 0).repeat_interleave(bk, 1)[:n, :k]
-    q = (x32 / full).clamp(-FP8_E4M3_MAX, FP8_E4M3_MAX).to(torch.float8_e4m3fn)
+    inv = torch.ones_like(scale) / scale
+    full = inv.repeat_interleave(bn, 0).repeat_interleave(bk, 1)[:n, :k]
+    q = (x32 * full).clamp(-FP8_E4M3_MAX, FP8_E4M3_MAX).to(torch.float8_e4m3fn)
     return q, scale
 
 
