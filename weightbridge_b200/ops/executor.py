@@ -16,8 +16,10 @@ import torch
 from ..core.plan import ITEM_DTYPE, OP_COPY, QDESC_DTYPE, QWORK_DTYPE, Tables
 from ._ext import ext
 
-# TMA pipeline modes of the kernel (stages x piece bytes of shared memory per CTA)
-MODE_VECTOR, MODE_BULK8, MODE_BULK12, MODE_BULK4 = 0, 1, 2, 3
+# TMA pipeline modes of the kernel (stages x piece bytes of shared memory per CTA).
+# MODE_AUTO: the TMA pipeline for copy-only programs; the vector path (more CTAs per SM)
+# when the program quantises, since quant blocks use every thread of a CTA.
+MODE_AUTO, MODE_VECTOR, MODE_BULK8, MODE_BULK12, MODE_BULK4 = -1, 0, 1, 2, 3
 DEFAULT_SPIN_LIMIT = 1 << 26
 
 
@@ -46,7 +48,7 @@ def cpu_execute(tables: Tables) -> None:
 
 @dataclass
 class LaunchConfig:
-    mode: int = MODE_BULK8
+    mode: int = MODE_AUTO
     piece_bytes: int = 16384
     grid: int | None = None
     spin_limit: int = DEFAULT_SPIN_LIMIT
@@ -68,6 +70,9 @@ class TransferProgram:
                  flag_addrs: list[int] | None = None, config: LaunchConfig | None = None):
         self.device = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
         self.config = config or LaunchConfig.from_env()
+        if self.config.mode == MODE_AUTO:
+            from dataclasses import replace
+            self.config = replace(self.config, mode=MODE_VECTOR if len(tables.qwork) else MODE_BULK8)
         self.tables = tables
         items = tables.items
         if self.config.mode != MODE_VECTOR and len(items):

@@ -65,7 +65,7 @@ def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--case", default="copy", choices=["copy", "strided", "quant"])
     p.add_argument("--gbytes", type=float, default=1.0)
-    p.add_argument("--mode", type=int, default=1)
+    p.add_argument("--mode", type=int, default=-1)
     p.add_argument("--piece", type=int, default=16384)
     p.add_argument("--grid", type=int, default=0)
     p.add_argument("--item-bytes", type=int, default=1 << 19)
@@ -87,7 +87,7 @@ def main(argv=None):
     ms = e0.elapsed_time(e1) / a.iters
     gbs = traffic / (ms / 1e3) / 1e9
     peak = _peak_gbs()
-    print(json.dumps({"case": a.case, "gbytes": a.gbytes, "mode": a.mode, "piece": a.piece, "grid": prog.grid(),
+    print(json.dumps({"case": a.case, "gbytes": a.gbytes, "mode": prog.config.mode, "piece": a.piece, "grid": prog.grid(),
                       "items": len(tables.items), "qwork": len(tables.qwork), "ms": round(ms, 4),
                       "traffic_bytes": traffic, "gbs": round(gbs, 1),
                       "frac_of_measured_copy": round(gbs / peak, 3) if peak else None,

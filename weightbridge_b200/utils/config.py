@@ -33,7 +33,7 @@ class TransferConfig:
     sync_timeout_s: float = 300.0         # one send()/request_update() round
     http_timeout_s: float = 60.0
     zmq_timeout_s: float = 60.0
-    kernel_mode: int = 1                  # 0 vector, 1/2/3 TMA bulk pipeline depths
+    kernel_mode: int = -1                 # -1 auto, 0 vector, 1/2/3 TMA bulk pipeline depths
     piece_bytes: int = 16384
     item_bytes: int = 1 << 19
     grid: int = 0                         # 0: sized from the SM count
