@@ -1,0 +1,187 @@
+"""Failure detection on the host (no GPU fault, trap or hang is ever provoked).
+
+A sender and its receivers run in one process (threads) over the real control plane:
+uvicorn + FastAPI controller, ZMQ worker thread, TCPStore session, gloo payload path.
+Each test injects one failure and checks that it surfaces as a clear error well before
+the configured deadline, instead of a hang.
+"""
+import socket
+import threading
+import time
+
+import pytest
+import torch
+
+from weightbridge_b200 import TransferConfig, WeightData, WeightReceiver, WeightReceiverController, WeightSender
+from weightbridge_b200.control.controller import ControllerError
+from weightbridge_b200.control.sender import TransferError
+from weightbridge_b200.models.arch import get_arch
+from weightbridge_b200.parallel.megatron import MegatronLayout
+from weightbridge_b200.parallel.sglang import SGLangLayout
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+class Rollout:
+    """FastAPI server + controller + one receiver worker, in this process."""
+
+    def __init__(self, cfg, state_dict=None, meta=None, workers=1, make_receiver=True):
+        import uvicorn
+        from fastapi import FastAPI
+        arch = get_arch("tiny-llama")
+        self.lay = SGLangLayout(arch, tp=1)
+        self.params = self.lay.allocate(dtype=torch.float32)
+        m, views = self.lay.to_wb(self.params)
+        self.meta = meta or m
+        app = FastAPI()
+        self.ctl = WeightReceiverController(app, worker_num=workers, timeout_s=2.0)
+        self.recv = None
+        if make_receiver:
+            self.recv = WeightReceiver(self.ctl.ipc_name, 0, self.meta,
+                                       state_dict=views if state_dict is None else state_dict, config=cfg)
+        port = _port()
+        self.server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="error"))
+        threading.Thread(target=self.server.run, daemon=True).start()
+        t0 = time.time()
+        while not self.server.started and time.time() - t0 < 20:
+            time.sleep(0.02)
+        self.url = f"http://127.0.0.1:{port}"
+
+    def close(self):
+        if self.recv is not None:
+            self.recv.stop()
+        self.server.should_exit = True
+        self.ctl.close()
+
+
+def _sender(cfg):
+    lay = MegatronLayout(get_arch("tiny-llama"), tp=1)
+    params = lay.allocate(dtype=torch.float32)
+    meta, views = lay.to_wb(params)
+    return lay, params, meta, views
+
+
+def _cfg(**kw):
+    base = dict(mode="cpu_direct", connect_timeout_s=30, sync_timeout_s=30, http_timeout_s=10)
+    base.update(kw)
+    return TransferConfig(**base)
+
+
+def test_sync_then_receiver_never_updates_times_out():
+    cfg = _cfg(sync_timeout_s=2.0)
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender("cpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        # one good sync first
+        th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+        th.start()
+        s.send(views)
+        th.join(20)
+        exp = ro.lay.allocate(dtype=torch.float32, fill=True)
+        assert all(torch.equal(ro.params[n], exp[n]) for n in exp)
+        # now nobody calls request_update: send must fail by the deadline, not hang
+        t0 = time.time()
+        with pytest.raises(TransferError, match="ready"):
+            s.send(views)
+        assert time.time() - t0 < 10
+    finally:
+        ro.close()
+
+
+def test_receiver_join_failure_reaches_sender_fast():
+    cfg = _cfg(connect_timeout_s=60)
+    # the receiver's state_dict lacks one entry: binding fails inside the worker's join
+    arch = get_arch("tiny-llama")
+    lay = SGLangLayout(arch, tp=1)
+    params = lay.allocate(dtype=torch.float32)
+    meta, views = lay.to_wb(params)
+    views.pop("model.norm.weight")
+    ro = Rollout(cfg, state_dict=views, meta=meta)
+    try:
+        _, _, smeta, _ = _sender(cfg)
+        s = WeightSender("cpu_direct", [ro.url], config=cfg)
+        t0 = time.time()
+        with pytest.raises(Exception, match="model.norm.weight"):
+            s.connect(smeta)
+        assert time.time() - t0 < 15, "sender should learn of the failure long before the 60 s deadline"
+        assert ro.recv.state.value == "failed"
+    finally:
+        ro.close()
+
+
+def test_plan_digest_mismatch_is_detected(monkeypatch):
+    import weightbridge_b200.control.receiver as rmod
+    monkeypatch.setattr(rmod, "plan_digest", lambda ov: "corrupted")
+    cfg = _cfg(connect_timeout_s=60)
+    ro = Rollout(cfg)
+    try:
+        _, _, smeta, _ = _sender(cfg)
+        s = WeightSender("cpu_direct", [ro.url], config=cfg)
+        t0 = time.time()
+        with pytest.raises(Exception, match="digest mismatch"):
+            s.connect(smeta)
+        assert time.time() - t0 < 15
+    finally:
+        ro.close()
+
+
+def test_controller_gather_times_out_on_missing_worker():
+    cfg = _cfg()
+    ro = Rollout(cfg, workers=2)      # two workers expected, one exists
+    try:
+        t0 = time.time()
+        with pytest.raises(ControllerError):
+            ro.ctl._query_receivers_metadata()
+        assert time.time() - t0 < 5
+    finally:
+        ro.close()
+
+
+def test_controller_query_metadata_two_workers():
+    """The reference's controller test, on the API it expected (worker_num kwarg and a
+    synchronous _query_receivers_metadata), with two workers and empty metadata."""
+    ctl = WeightReceiverController(None, worker_num=0)
+    ctl.set_worker_num(2)
+    empty = WeightData(meta_dict={})
+    r0 = WeightReceiver(ctl.ipc_name, 0, empty)
+    r1 = WeightReceiver(ctl.ipc_name, 1, empty)
+    try:
+        res = ctl._query_receivers_metadata()
+        assert [r["rank"] for r in res] == [0, 1]
+        assert all(r["metadata"] == {} for r in res)
+    finally:
+        r0.stop()
+        r1.stop()
+        ctl.close()
+
+
+def test_update_without_arm_returns_false_and_stop_is_clean():
+    cfg = _cfg()
+    ro = Rollout(cfg)
+    try:
+        assert ro.recv.request_update() is False
+        t0 = time.time()
+        assert ro.recv.request_update(timeout=0.5) is False
+        assert 0.4 < time.time() - t0 < 5
+    finally:
+        ro.close()
+    assert not ro.recv.receiver_thread.is_alive()
+
+
+def test_receive_request_rejected_before_connect():
+    cfg = _cfg()
+    ro = Rollout(cfg)
+    try:
+        import requests
+        r = requests.post(f"{ro.url}/wbridge/receive", timeout=5)
+        assert r.json()["status"] == "error"
+        stats = requests.get(f"{ro.url}/wbridge/stats", timeout=5).json()
+        assert stats[0]["state"] == "disconnected"
+    finally:
+        ro.close()

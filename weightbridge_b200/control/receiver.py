@@ -41,7 +41,7 @@ from ..utils.config import TransferConfig, normalize_mode
 from .assign import expected_senders, restrict
 from .protocol import (CONNECT_REQUEST, METADATA_REQUEST, RECEIVE_REQUEST, STATS_REQUEST, STOP_REQUEST,
                        UPDATE_REQUEST, ReceiverState, b64)
-from .session import Session, SessionTimeout
+from .session import PeerError, Session, SessionTimeout
 
 logger = logging.getLogger(__name__)
 
@@ -212,10 +212,15 @@ class WeightReceiver:
                 self._join(data)
                 self._state = ReceiverState.CONNECTED
                 self._error = None
-            except Exception as e:  # reported through metadata/stats; sender times out
+            except Exception as e:  # published to the session so the senders fail fast
                 logger.exception("receiver %d failed to join", self.rank)
                 self._error = f"{type(e).__name__}: {e}"
                 self._state = ReceiverState.FAILED
+                if self.session is not None:
+                    try:
+                        self.session.set(f"error/{data['rank']}", f"receiver {data['rank']}: {self._error}")
+                    except Exception:
+                        pass
         elif t == RECEIVE_REQUEST:
             if self._state != ReceiverState.CONNECTED:
                 self._reply(sock, data, {"status": "error", "detail": f"requires CONNECTED state, is {self._state.value}"})
@@ -264,6 +269,11 @@ class WeightReceiver:
             logger.exception("receiver %d update failed", self.rank)
             self._error = f"{type(e).__name__}: {e}"
             self._state = ReceiverState.FAILED
+            if self.session is not None:
+                try:
+                    self.session.set(f"error/{self.global_rank}", f"receiver {self.global_rank}: {self._error}")
+                except Exception:
+                    pass
             sock.send_string(json.dumps({"success": False, "message": self._error, "error": self._error}))
 
     # -- session -----------------------------------------------------------------------
@@ -313,9 +323,10 @@ class WeightReceiver:
                 raise ReceiveError(f"plan digest mismatch with sender {s}: the two sides disagree on the layout")
             self.overlaps[s] = ov
             self.expected_bytes += ov.total_nbytes()
+        sess.set(f"verified/{gr}", "1")
         if mode == "cpu_direct":
             from .sender import gloo_group
-            self._gloo = gloo_group(sess, gr, self.world_size, self.config.sync_timeout_s, data["master_address"])
+            self._gloo = gloo_group(sess, gr, self.world_size, self.config.connect_timeout_s, data["master_address"])
             self._wires = {}
             for s, ov in self.overlaps.items():
                 wire = torch.empty(ov.total_nbytes(), dtype=torch.uint8)
@@ -346,8 +357,9 @@ class WeightReceiver:
             sess.set(f"ready/{gr}/{epoch}", "1")
             keys = [f"done/{s}/{gr}/{epoch}" for s in self.expected]
             try:
-                sess.wait(keys, self.config.sync_timeout_s, what=f"senders {self.expected} to finish epoch {epoch}")
-            except SessionTimeout as e:
+                sess.wait_or_error(keys, [f"serror/{s}" for s in self.expected], self.config.sync_timeout_s,
+                                   what=f"senders {self.expected} to finish epoch {epoch}")
+            except (SessionTimeout, PeerError) as e:
                 raise ReceiveError(str(e)) from None
             bad = {s: int(sess.get(f"done/{s}/{gr}/{epoch}")) for s in self.expected}
             bad = {s: v for s, v in bad.items() if v}

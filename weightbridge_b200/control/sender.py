@@ -41,7 +41,7 @@ from ..core.plan import Tables, lower_ops, phys_binding, plan_digest, plan_pair,
 from ..core.shard import WeightData
 from ..utils.config import TransferConfig, normalize_mode
 from .assign import assign_sources, restrict
-from .session import Session, SessionTimeout, local_address
+from .session import PeerError, Session, SessionTimeout, local_address
 
 logger = logging.getLogger(__name__)
 
@@ -153,12 +153,17 @@ class WeightSender:
                          for r, names in self.targets.items()}
         # receivers publish their memory tables once they joined the store
         for r in self.targets:
-            self._rinfo[r] = sess.get_json(f"recv/{r}", cfg.connect_timeout_s)
+            self._rinfo[r] = sess.get_json(f"recv/{r}", cfg.connect_timeout_s, error_key=f"error/{r}")
         if cfg.mode == "cpu_direct":
-            self._gloo = gloo_group(sess, self.rank, world, cfg.sync_timeout_s, addr)
+            # the gloo group needs every rank: join it only once every receiver verified the plan
+            everyone = sorted(rmetas)
+            sess.wait_or_error([f"verified/{r}" for r in everyone], [f"error/{r}" for r in everyone],
+                               cfg.connect_timeout_s, "receivers to verify the plan")
+            self._gloo = gloo_group(sess, self.rank, world, cfg.connect_timeout_s, addr)
         else:
             self._open_receivers()
-        sess.wait([f"joined/{r}" for r in self.targets], cfg.connect_timeout_s, "receivers to join")
+        sess.wait_or_error([f"joined/{r}" for r in self.targets], [f"error/{r}" for r in self.targets],
+                           cfg.connect_timeout_s, "receivers to join")
         self.epoch = 0
         self._program = None
         self._program_key = None
@@ -315,9 +320,9 @@ class WeightSender:
         st = SyncStats(epoch=epoch, receivers=sorted(self.targets))
         t1 = time.perf_counter()
         try:
-            sess.wait([f"ready/{r}/{epoch}" for r in self.targets], cfg.sync_timeout_s,
-                      f"receivers {sorted(self.targets)} to be ready for epoch {epoch}")
-        except SessionTimeout as e:
+            sess.wait_or_error([f"ready/{r}/{epoch}" for r in self.targets], [f"error/{r}" for r in self.targets],
+                               cfg.sync_timeout_s, f"receivers {sorted(self.targets)} to be ready for epoch {epoch}")
+        except (SessionTimeout, PeerError) as e:
             raise TransferError(str(e)) from None
         st.wait_ready_ms = (time.perf_counter() - t1) * 1e3
         if cfg.mode == "cpu_direct":
@@ -344,6 +349,7 @@ class WeightSender:
             for r in self.targets:
                 sess.set(f"done/{self.rank}/{r}/{epoch}", str(st.status))
             if st.status:
+                sess.set(f"serror/{self.rank}", f"sender {self.rank}: kernel status {st.status:#x} at epoch {epoch}")
                 prog.clear_status()
                 raise TransferError(f"transfer kernel reported status {st.status:#x} at epoch {epoch}")
         self.epoch = epoch
