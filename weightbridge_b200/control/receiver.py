@@ -217,10 +217,9 @@ class WeightReceiver:
                 self._error = f"{type(e).__name__}: {e}"
                 self._state = ReceiverState.FAILED
                 if self.session is not None:
-                    try:
-                        self.session.set(f"error/{data['rank']}", f"receiver {data['rank']}: {self._error}")
-                    except Exception:
-                        pass
+                    gr = data["rank"]
+                    self.session.set_error([f"recv/{gr}", f"verified/{gr}", f"joined/{gr}"],
+                                           f"receiver {gr}: {self._error}")
         elif t == RECEIVE_REQUEST:
             if self._state != ReceiverState.CONNECTED:
                 self._reply(sock, data, {"status": "error", "detail": f"requires CONNECTED state, is {self._state.value}"})
@@ -270,10 +269,8 @@ class WeightReceiver:
             self._error = f"{type(e).__name__}: {e}"
             self._state = ReceiverState.FAILED
             if self.session is not None:
-                try:
-                    self.session.set(f"error/{self.global_rank}", f"receiver {self.global_rank}: {self._error}")
-                except Exception:
-                    pass
+                self.session.set_error([f"ready/{self.global_rank}/{self.epoch + 1}"],
+                                       f"receiver {self.global_rank}: {self._error}")
             sock.send_string(json.dumps({"success": False, "message": self._error, "error": self._error}))
 
     # -- session -----------------------------------------------------------------------
@@ -318,7 +315,7 @@ class WeightReceiver:
         self.overlaps: dict[int, WeightData] = {}
         for s in self.expected:
             ov = WeightData.compute_overlap(restrict(WeightData(smetas[s]), plan[s][gr]), self.metadata)
-            digest = sess.get(f"digest/{s}/{gr}").decode()
+            digest = sess.wait_checked([f"digest/{s}/{gr}"])[0].decode()
             if digest != plan_digest(ov):
                 raise ReceiveError(f"plan digest mismatch with sender {s}: the two sides disagree on the layout")
             self.overlaps[s] = ov
@@ -357,12 +354,11 @@ class WeightReceiver:
             sess.set(f"ready/{gr}/{epoch}", "1")
             keys = [f"done/{s}/{gr}/{epoch}" for s in self.expected]
             try:
-                sess.wait_or_error(keys, [f"serror/{s}" for s in self.expected], self.config.sync_timeout_s,
-                                   what=f"senders {self.expected} to finish epoch {epoch}")
+                vals = sess.wait_checked(keys, self.config.sync_timeout_s,
+                                         what=f"senders {self.expected} to finish epoch {epoch}")
             except (SessionTimeout, PeerError) as e:
                 raise ReceiveError(str(e)) from None
-            bad = {s: int(sess.get(f"done/{s}/{gr}/{epoch}")) for s in self.expected}
-            bad = {s: v for s, v in bad.items() if v}
+            bad = {s: int(v) for s, v in zip(self.expected, vals) if int(v)}
             if bad:
                 raise ReceiveError(f"senders reported kernel status {bad} for epoch {epoch}")
             if self.config.verify_flags and self.expected:

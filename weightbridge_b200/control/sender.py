@@ -153,17 +153,25 @@ class WeightSender:
                          for r, names in self.targets.items()}
         # receivers publish their memory tables once they joined the store
         for r in self.targets:
-            self._rinfo[r] = sess.get_json(f"recv/{r}", cfg.connect_timeout_s, error_key=f"error/{r}")
+            try:
+                self._rinfo[r] = sess.get_json(f"recv/{r}", cfg.connect_timeout_s)
+            except (SessionTimeout, PeerError) as e:
+                raise TransferError(str(e)) from None
         if cfg.mode == "cpu_direct":
             # the gloo group needs every rank: join it only once every receiver verified the plan
             everyone = sorted(rmetas)
-            sess.wait_or_error([f"verified/{r}" for r in everyone], [f"error/{r}" for r in everyone],
-                               cfg.connect_timeout_s, "receivers to verify the plan")
+            try:
+                sess.wait_checked([f"verified/{r}" for r in everyone], cfg.connect_timeout_s,
+                                  "receivers to verify the plan")
+            except (SessionTimeout, PeerError) as e:
+                raise TransferError(str(e)) from None
             self._gloo = gloo_group(sess, self.rank, world, cfg.connect_timeout_s, addr)
         else:
             self._open_receivers()
-        sess.wait_or_error([f"joined/{r}" for r in self.targets], [f"error/{r}" for r in self.targets],
-                           cfg.connect_timeout_s, "receivers to join")
+        try:
+            sess.wait_checked([f"joined/{r}" for r in self.targets], cfg.connect_timeout_s, "receivers to join")
+        except (SessionTimeout, PeerError) as e:
+            raise TransferError(str(e)) from None
         self.epoch = 0
         self._program = None
         self._program_key = None
@@ -299,6 +307,12 @@ class WeightSender:
         """The compiled transfer program (tables, grid, byte counts), once compiled."""
         return self._program
 
+    def _fail_epoch(self, epoch: int, message: str) -> None:
+        """Tell this epoch's receivers that no data is coming (they stop waiting at once)."""
+        if self.session is not None:
+            self.session.set_error([f"done/{self.rank}/{r}/{epoch}" for r in self.targets],
+                                   f"sender {self.rank}: {message}")
+
     def send(self, state_dict: dict[str, Any]) -> SyncStats:
         if not self.connected or self.metadata is None:
             raise RuntimeError("WeightSender.send requires connect() first")
@@ -311,18 +325,23 @@ class WeightSender:
                 resp.raise_for_status()
                 if resp.json().get("status") != "success":
                     raise TransferError(f"receiver {url} refused the sync: {resp.json()}")
-        key = self._key(state_dict)
-        if self._program_key != key:
-            (self._compile_cpu if cfg.mode == "cpu_direct" else self._compile)(state_dict)
-            self._program_key = key
         epoch = self.epoch + 1
+        try:
+            key = self._key(state_dict)
+            if self._program_key != key:
+                (self._compile_cpu if cfg.mode == "cpu_direct" else self._compile)(state_dict)
+                self._program_key = key
+        except Exception as e:
+            self._fail_epoch(epoch, f"{type(e).__name__}: {e}")
+            raise
         sess = self.session
         st = SyncStats(epoch=epoch, receivers=sorted(self.targets))
         t1 = time.perf_counter()
         try:
-            sess.wait_or_error([f"ready/{r}/{epoch}" for r in self.targets], [f"error/{r}" for r in self.targets],
-                               cfg.sync_timeout_s, f"receivers {sorted(self.targets)} to be ready for epoch {epoch}")
+            sess.wait_checked([f"ready/{r}/{epoch}" for r in self.targets], cfg.sync_timeout_s,
+                              f"receivers {sorted(self.targets)} to be ready for epoch {epoch}")
         except (SessionTimeout, PeerError) as e:
+            self._fail_epoch(epoch, str(e))
             raise TransferError(str(e)) from None
         st.wait_ready_ms = (time.perf_counter() - t1) * 1e3
         if cfg.mode == "cpu_direct":
@@ -348,8 +367,7 @@ class WeightSender:
             st.bytes_read, st.bytes_written = prog.bytes_read, prog.bytes_written
             for r in self.targets:
                 sess.set(f"done/{self.rank}/{r}/{epoch}", str(st.status))
-            if st.status:
-                sess.set(f"serror/{self.rank}", f"sender {self.rank}: kernel status {st.status:#x} at epoch {epoch}")
+
                 prog.clear_status()
                 raise TransferError(f"transfer kernel reported status {st.status:#x} at epoch {epoch}")
         self.epoch = epoch

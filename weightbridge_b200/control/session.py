@@ -26,6 +26,11 @@ class PeerError(RuntimeError):
     """A peer of the session published an error instead of the key we wait for."""
 
 
+# A failing peer stores this prefix + its message in the keys others wait on, so a single
+# blocking wait returns and the waiter raises instead of sitting out its deadline.
+ERROR_PREFIX = b"!error:"
+
+
 class Session:
     def __init__(self, host: str, port: int, is_master: bool, timeout_s: float, prefix: str = "wbridge"):
         self.timeout_s = timeout_s
@@ -63,50 +68,35 @@ class Session:
         self.wait([key], timeout_s, key)
         return self.store.get(key)
 
-    def get_json(self, key: str, timeout_s: float | None = None, error_key: str | None = None) -> Any:
-        head = (self.get_or_error(key, error_key, timeout_s) if error_key else self.get(key, timeout_s)).decode()
+    def get_json(self, key: str, timeout_s: float | None = None) -> Any:
+        head = self.get(key, timeout_s)
+        if head.startswith(ERROR_PREFIX):
+            raise PeerError(head[len(ERROR_PREFIX):].decode(errors="replace"))
+        head = head.decode()
         if not head.startswith("z:"):
             return json.loads(head)
         n = int(head[2:])
         blob = b"".join(self.store.get(f"{key}#{i}") for i in range(n))
         return json.loads(zlib.decompress(blob))
 
-    def get_or_error(self, key: str, error_key: str, timeout_s: float | None = None) -> bytes:
-        """Wait for ``key`` but fail fast when the peer publishes ``error_key`` instead."""
-        t = timeout_s if timeout_s is not None else self.timeout_s
-        deadline = time.monotonic() + t
-        while True:
-            left = deadline - time.monotonic()
-            try:
-                self.store.wait([key], timedelta(seconds=max(0.01, min(0.5, left))))
-                return self.store.get(key)
-            except Exception:
-                pass
-            if self.store.check([error_key]):
-                raise PeerError(self.store.get(error_key).decode())
-            if time.monotonic() >= deadline:
-                raise SessionTimeout(f"timed out after {t:.1f}s waiting for {key}")
+    def wait_checked(self, keys: Iterable[str], timeout_s: float | None = None, what: str = "") -> list[bytes]:
+        """Wait for ``keys`` (one blocking call) and raise ``PeerError`` if a peer stored an
+        error in any of them instead of a value."""
+        keys = list(keys)
+        self.wait(keys, timeout_s, what)
+        vals = [self.store.get(k) for k in keys] if keys else []
+        for k, v in zip(keys, vals):
+            if v.startswith(ERROR_PREFIX):
+                raise PeerError(v[len(ERROR_PREFIX):].decode(errors="replace"))
+        return vals
 
-    def wait_or_error(self, keys: Iterable[str], error_keys: Iterable[str], timeout_s: float | None = None,
-                      what: str = "") -> None:
-        """``wait`` that also fails fast when any peer publishes one of ``error_keys``."""
-        keys, error_keys = list(keys), list(error_keys)
-        if not keys:
-            return
-        t = timeout_s if timeout_s is not None else self.timeout_s
-        deadline = time.monotonic() + t
-        while True:
-            left = deadline - time.monotonic()
+    def set_error(self, keys: Iterable[str], message: str) -> None:
+        """Publish a failure in the keys a peer is (or will be) waiting for."""
+        for k in keys:
             try:
-                self.store.wait(keys, timedelta(seconds=max(0.01, min(0.5, left))))
-                return
+                self.store.set(k, ERROR_PREFIX + message.encode())
             except Exception:
                 pass
-            for ek in error_keys:
-                if self.store.check([ek]):
-                    raise PeerError(self.store.get(ek).decode())
-            if time.monotonic() >= deadline:
-                raise SessionTimeout(f"timed out after {t:.1f}s waiting for {what or keys[:4]}")
 
     def check(self, key: str) -> bool:
         return self.store.check([key])
