@@ -202,7 +202,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     torch.cuda.set_device(dev)
     trainer_ranks = [i for i, r in enumerate(roles) if r.kind == "trainer"]
     tgroup = dist.new_group(trainer_ranks, backend="gloo")
-    cfg = TransferConfig.from_env(mode="gpu_direct", connect_timeout_s=300, sync_timeout_s=300)
+    cfg = TransferConfig.from_env(mode="gpu_direct", connect_timeout_s=120, sync_timeout_s=60)
     if args.mode is not None:
         cfg.kernel_mode = args.mode
     if args.piece is not None:

@@ -71,12 +71,15 @@ def _cfg(**kw):
     return TransferConfig(**base)
 
 
-def test_sync_then_receiver_never_updates_times_out():
-    cfg = _cfg(sync_timeout_s=2.0)
+@pytest.mark.parametrize("mode", ["cpu_direct", "gpu_direct"])
+def test_sync_then_receiver_never_updates_times_out(mode):
+    """gpu_direct with host tensors in one process runs the device protocol (work tables,
+    flags, ready/done, status) through the C++ executor."""
+    cfg = _cfg(sync_timeout_s=2.0, mode=mode)
     ro = Rollout(cfg)
     try:
         lay, params, meta, views = _sender(cfg)
-        s = WeightSender("cpu_direct", [ro.url], config=cfg)
+        s = WeightSender(mode, [ro.url], config=cfg)
         s.connect(meta)
         # one good sync first
         th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
@@ -85,6 +88,18 @@ def test_sync_then_receiver_never_updates_times_out():
         th.join(20)
         exp = ro.lay.allocate(dtype=torch.float32, fill=True)
         assert all(torch.equal(ro.params[n], exp[n]) for n in exp)
+        assert ro.recv.epoch == 1
+        if mode == "gpu_direct":
+            assert int(ro.recv.flags[0]) == 1
+            # a second good sync with new weights
+            lay.fill(params, seed=5)
+            th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+            th.start()
+            st = s.send(views)
+            th.join(20)
+            assert st.epoch == 2 and st.status == 0 and int(ro.recv.flags[0]) == 2
+            exp = ro.lay.allocate(dtype=torch.float32, fill=True, seed=5)
+            assert all(torch.equal(ro.params[n], exp[n]) for n in exp)
         # now nobody calls request_update: send must fail by the deadline, not hang
         t0 = time.time()
         with pytest.raises(TransferError, match="ready"):

@@ -290,11 +290,15 @@ class WeightReceiver:
         binding = bind(self.metadata, self.state_dict)
         info: dict[str, Any] = {"rank": gr, "worker": self.rank, "pid": os.getpid(), "host": socket.gethostname(),
                                 "mode": mode}
-        if mode in ("gpu_direct", "nvls"):
+        if mode in ("gpu_direct", "nvls") and self.device.type == "cpu":
+            # host memory: only a sender in this same process can write it (tests, CPU runs)
+            self.flags = torch.zeros(max(W, 1), dtype=torch.int64)
+            phys = phys_binding(binding)
+            info.update({"device": -1, "allocs": [], "binding": phys.to_json(),
+                         "flags": [-1, self.flags.data_ptr(), W]})
+        elif mode in ("gpu_direct", "nvls"):
             from ..parallel.ipc import ExportTable
             from ..ops._ext import ext
-            if self.device.type != "cuda":
-                raise ReceiveError("gpu_direct needs the receiver's tensors on a CUDA device")
             torch.cuda.set_device(self.device)
             self.flags = torch.zeros(max(W, 1), dtype=torch.int64, device=self.device)
             export = ExportTable(self.device)

@@ -227,6 +227,8 @@ class WeightSender:
                 raise TransferError(f"receiver {r} joined in mode {info.get('mode')}")
             if info["host"] != host:
                 raise TransferError(f"receiver {r} is on host {info['host']}: gpu_direct needs one node")
+            if info.get("device", 0) < 0 and info["pid"] != pid:
+                raise TransferError(f"receiver {r} holds host memory in another process; use cpu_direct")
             self._imports[r] = ImportTable(info["allocs"], same_process=(info["pid"] == pid))
 
     def disconnect(self) -> None:
@@ -256,7 +258,12 @@ class WeightSender:
             falloc, foff, _w = info["flags"]
             flags.append(imp.base(falloc) + foff + 8 * self.rank)
         tables = _interleave(parts)
-        from ..ops.executor import LaunchConfig, TransferProgram
+        from ..ops.executor import HostProgram, LaunchConfig, TransferProgram
+        if device.type == "cpu":
+            if any(self._rinfo[r].get("device", 0) >= 0 for r in self.targets):
+                raise TransferError("a CPU sender cannot store into GPU receivers; use cpu_direct")
+            self._program = HostProgram(tables, flags)
+            return
         lc = LaunchConfig(mode=cfg.kernel_mode, piece_bytes=cfg.piece_bytes, grid=cfg.grid or None)
         torch.cuda.set_device(device)
         self._program = TransferProgram(tables, device, flags, lc)
@@ -300,7 +307,10 @@ class WeightSender:
             self._compile(state_dict)
             self._program_key = key
         if self._program is not None and len(self._program.tables):
-            self._program.launch(0, stream or torch.cuda.current_stream(self._program.device), signal=False)
+            if self._program.device.type == "cpu":
+                self._program.launch(0, signal=False)
+            else:
+                self._program.launch(0, stream or torch.cuda.current_stream(self._program.device), signal=False)
 
     @property
     def program(self):
@@ -353,6 +363,13 @@ class WeightSender:
                 st.bytes_written += wire.numel()
             for w in works:
                 w.wait()
+        elif self.targets and self._program.device.type == "cpu":
+            t2 = time.perf_counter()
+            self._program.launch(epoch)
+            st.device_ms = (time.perf_counter() - t2) * 1e3
+            st.bytes_read, st.bytes_written = self._program.bytes_read, self._program.bytes_written
+            for r in self.targets:
+                sess.set(f"done/{self.rank}/{r}/{epoch}", "0")
         elif self.targets:
             prog = self._program
             cur = torch.cuda.current_stream(prog.device)
@@ -367,7 +384,7 @@ class WeightSender:
             st.bytes_read, st.bytes_written = prog.bytes_read, prog.bytes_written
             for r in self.targets:
                 sess.set(f"done/{self.rank}/{r}/{epoch}", str(st.status))
-
+            if st.status:
                 prog.clear_status()
                 raise TransferError(f"transfer kernel reported status {st.status:#x} at epoch {epoch}")
         self.epoch = epoch

@@ -140,6 +140,38 @@ class TransferProgram:
         self.status.zero_()
 
 
+class HostProgram:
+    """The same work tables executed on the host by the C++ executor, with the epoch written
+    to the flag words afterwards.  Runs the device protocol (tables, flags, status) when the
+    sender and its receivers hold CPU tensors in one process, e.g. in CPU tests."""
+
+    def __init__(self, tables: Tables, flag_addrs: list[int] | None = None):
+        self.tables = tables
+        self.flag_addrs = list(flag_addrs or [])
+        self.device = torch.device("cpu")
+        self.launches = 0
+
+    bytes_read = property(lambda self: self.tables.bytes_read)
+    bytes_written = property(lambda self: self.tables.bytes_written)
+
+    def grid(self) -> int:
+        return 0
+
+    def launch(self, epoch: int, stream=None, signal: bool = True) -> None:
+        import ctypes
+        cpu_execute(self.tables)
+        if signal:
+            for a in self.flag_addrs:
+                ctypes.c_int64.from_address(a).value = epoch
+        self.launches += 1
+
+    def read_status(self) -> int:
+        return 0
+
+    def clear_status(self) -> None:
+        pass
+
+
 def wait_flags(flags: torch.Tensor, epoch: torch.Tensor, timeout_s: float, status: torch.Tensor,
                where: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> None:
     """Launch a bounded device-side wait until every flag word reaches ``epoch[0]``; on
