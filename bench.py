@@ -52,6 +52,10 @@ def parse(argv=None):
     p.add_argument("--item-bytes", type=int, default=None)
     p.add_argument("--no-verify", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-pool", action="store_true",
+                   help="allocate every rollout parameter separately (one IPC handle each)")
+    p.add_argument("--stall-dump-s", type=float, default=150.0,
+                   help="dump every thread's stack to stderr if a process is still running after this long")
     return p.parse_args(argv)
 
 
@@ -193,9 +197,18 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     from weightbridge_b200.parallel.sglang import SGLangLayout
     from weightbridge_b200.utils.timing import ClockSampler
 
+    import faulthandler
+    faulthandler.dump_traceback_later(args.stall_dump_s, exit=False)
+    t_start = time.time()
+
+    def phase(msg):
+        if idx == 0 or roles[idx].host:
+            print(f"[bench rank {idx}] {time.time() - t_start:7.1f}s {msg}", file=sys.stderr, flush=True)
+
     if init is not None:
         dist.init_process_group("gloo", init_method=init, rank=idx, world_size=nprocs)
     model, roles, desc = scenario(args.config, args.gpus)
+    phase("process group up")
     role = roles[idx]
     arch = get_arch(model)
     dev = torch.device("cuda", role.device)
@@ -218,9 +231,10 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
         meta, views = lay.to_wb(params)
     else:
         lay = SGLangLayout(arch, **role.layout)
-        params = lay.allocate(device=dev, dtype=torch.bfloat16)
+        params = lay.allocate(device=dev, dtype=torch.bfloat16, pool=not args.no_pool)
         meta, views = lay.to_wb(params)
     torch.cuda.synchronize()
+    phase("parameters allocated and filled")
 
     # rollout engines: HTTP server + controller in the host process of each engine
     engine_info = None
@@ -243,10 +257,12 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     if role.kind == "rollout":
         recv = WeightReceiver(engines[role.engine][2], role.worker, meta, state_dict=views, device=dev, config=cfg)
     dist.barrier()
+    phase("engines up")
     if role.kind == "trainer":
         sender = WeightSender("gpu_direct", urls, group=tgroup, config=cfg)
         sender.connect(meta)
     dist.barrier()
+    phase("connected")
     setup_s = time.time() - t_setup
 
     def public_sync():
@@ -260,6 +276,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     for _ in range(args.warmup):
         public_sync()
     torch.cuda.synchronize()
+    phase("warm-up syncs done")
 
     # phase A: device-timed transfer launches
     stream = torch.cuda.Stream(dev)
@@ -293,10 +310,11 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
         e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
         dist.barrier()
 
+    phase("timed phases done")
     ok = 1
     if role.kind == "rollout" and not args.no_verify:
         del_views = None
-        expected = lay.allocate(device=dev, dtype=torch.bfloat16, fill=True)
+        expected = lay.allocate(device=dev, dtype=torch.bfloat16, fill=True, pool=not args.no_pool)
         for n in params:
             a, b = params[n], expected[n]
             if a.dtype == torch.float8_e4m3fn:
@@ -337,7 +355,8 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                        "l2": "inputs larger than L2 (GBs per sync); no flush needed",
                        "kernel_mode": cfg.kernel_mode, "piece_bytes": cfg.piece_bytes,
                        "item_bytes": cfg.item_bytes, "work_items_max": int(G[:, 8].max()),
-                       "grid": int(G[:, 9].max()), "processes": nprocs},
+                       "grid": int(G[:, 9].max()), "processes": nprocs,
+                       "rollout_params": "separate allocations" if args.no_pool else "one pooled allocation per rank"},
             "latency_s": round(lat, 6),
             "gbs_per_gpu": round(value / ngpu, 2),
             "gbs_per_sender": round(value / max(1.0, float(G[:, 7].sum())), 2),
@@ -354,6 +373,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
         }
         print(json.dumps(res), flush=True)
 
+    faulthandler.cancel_dump_traceback_later()
     dist.barrier()
     if recv is not None:
         recv.stop()

@@ -134,3 +134,43 @@ def test_plan_digest_is_deterministic():
     assert plan_digest(plan_pair(s0, rphys)) == plan_digest(plan_pair(s0, rphys))
     ov = WeightData.compute_overlap(s0.meta, rmeta)
     assert plan_digest(ov) == plan_digest(WeightData(bytes(ov)))
+
+
+def test_validate_tables_catches_out_of_bounds_rows():
+    from weightbridge_b200.core.plan import Op, PlanBoundsError, storage_ranges, validate_tables
+    a = torch.arange(64, dtype=torch.float32)
+    b = torch.zeros(32, dtype=torch.float32)
+    good = Op("copy", "x", (-1, a.data_ptr()), (-1, b.data_ptr()), [32], [1], [1], a.dtype, a.dtype)
+    t = lower_ops([good], ABS, ABS)
+    validate_tables(t, storage_ranges([a]), storage_ranges([b]))
+    over = Op("copy", "x", (-1, a.data_ptr()), (-1, b.data_ptr() + 4), [32], [1], [1], a.dtype, a.dtype)
+    with pytest.raises(PlanBoundsError, match="write"):
+        validate_tables(lower_ops([over], ABS, ABS), storage_ranges([a]), storage_ranges([b]))
+    rd = Op("copy", "x", (-1, a.data_ptr() + 40 * 4), (-1, b.data_ptr()), [32], [1], [1], a.dtype, a.dtype)
+    with pytest.raises(PlanBoundsError, match="read"):
+        validate_tables(lower_ops([rd], ABS, ABS), storage_ranges([a]), storage_ranges([b]))
+    # 2-D rows: the last row's end is what matters
+    m = torch.zeros(8, 16)
+    o2 = Op("copy", "x", (-1, a.data_ptr()), (-1, m.data_ptr() + 4), [8, 8], [8, 1], [16, 1], a.dtype, a.dtype)
+    validate_tables(lower_ops([o2], ABS, ABS), storage_ranges([a]), storage_ranges([m]))
+    o3 = Op("copy", "x", (-1, a.data_ptr()), (-1, m.data_ptr() + 36 * 4), [8, 8], [8, 1], [16, 1], a.dtype, a.dtype)
+    with pytest.raises(PlanBoundsError):
+        validate_tables(lower_ops([o3], ABS, ABS), storage_ranges([a]), storage_ranges([m]))
+
+
+@pytest.mark.parametrize("model,meg,sgl", [c[:3] for c in CASES])
+def test_real_plans_validate(model, meg, sgl):
+    from weightbridge_b200.core.plan import storage_ranges, validate_tables
+    arch = get_arch(model)
+    dtype = torch.bfloat16
+    for m in meg:
+        lay = MegatronLayout(arch, **m)
+        params = lay.allocate(dtype=dtype)
+        smeta, sviews = lay.to_wb(params)
+        sphys = phys_binding(bind(smeta, sviews))
+        for s in sgl:
+            rl = SGLangLayout(arch, **s)
+            rparams = rl.allocate(dtype=dtype, pool=True)
+            rmeta, rviews = rl.to_wb(rparams)
+            t = lower_ops(plan_pair(sphys, phys_binding(bind(rmeta, rviews))), ABS, ABS)
+            validate_tables(t, storage_ranges(params.values()), storage_ranges(rparams.values()))

@@ -37,7 +37,8 @@ import torch
 import torch.distributed as dist
 
 from ..core.binding import bind
-from ..core.plan import Tables, lower_ops, phys_binding, plan_digest, plan_pair, wire_binding, PhysBinding
+from ..core.plan import (PhysBinding, PlanBoundsError, Tables, lower_ops, phys_binding, plan_digest, plan_pair,
+                         storage_ranges, validate_tables, wire_binding)
 from ..core.shard import WeightData
 from ..utils.config import TransferConfig, normalize_mode
 from .assign import assign_sources, restrict
@@ -248,7 +249,7 @@ class WeightSender:
         binding = bind(self.metadata, state_dict)
         device = binding.device
         sphys = phys_binding(binding)
-        parts, flags = [], []
+        parts, flags, dst_ranges = [], [], []
         for r, names in sorted(self.targets.items()):
             info = self._rinfo[r]
             rphys = PhysBinding.from_json(info["binding"])
@@ -257,7 +258,15 @@ class WeightSender:
             parts.append(lower_ops(ops, lambda a: 0, imp.base, item_bytes=cfg.item_bytes))
             falloc, foff, _w = info["flags"]
             flags.append(imp.base(falloc) + foff + 8 * self.rank)
+            if info["allocs"]:
+                dst_ranges += [(imp.base(i), imp.base(i) + int(a["size"])) for i, a in enumerate(info["allocs"])]
+            else:                          # host memory of this process: the bound regions themselves
+                dst_ranges += _phys_extents(rphys) + [(foff, foff + 8 * int(_w))]
         tables = _interleave(parts)
+        if cfg.validate_plan:
+            validate_tables(tables, storage_ranges(state_dict.values()), dst_ranges)
+            for f in flags:
+                _check_flag(f, dst_ranges)
         from ..ops.executor import HostProgram, LaunchConfig, TransferProgram
         if device.type == "cpu":
             if any(self._rinfo[r].get("device", 0) >= 0 for r in self.targets):
@@ -393,6 +402,22 @@ class WeightSender:
         if len(self.history) > 256:
             del self.history[:128]
         return st
+
+
+def _phys_extents(pb: PhysBinding) -> list[tuple[int, int]]:
+    """Byte extents of absolute-address bound shards (host receivers in this process)."""
+    out = []
+    for name, shards in pb.entries.items():
+        es = pb.meta.dtype(name).itemsize
+        for p in shards:
+            span = sum((r - l - 1) * st for (l, r, _w), st in zip(p.shard, p.strides)) + 1
+            out.append((p.offset, p.offset + span * es))
+    return out
+
+
+def _check_flag(addr: int, ranges) -> None:
+    if not any(lo <= addr and addr + 8 <= hi for lo, hi in ranges):
+        raise PlanBoundsError(f"flag word {addr:#x} outside the receiver's registered memory")
 
 
 def gloo_group(sess: Session, rank: int, world: int, timeout_s: float, address: str):

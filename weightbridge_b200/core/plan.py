@@ -333,3 +333,81 @@ def lower_ops(ops: Sequence[Op], src_base: Callable[[int], int], dst_base: Calla
     qd = np.array(qdescs, dtype=QDESC_DTYPE) if qdescs else np.zeros(0, QDESC_DTYPE)
     qw = np.concatenate(qwork) if qwork else np.zeros(0, QWORK_DTYPE)
     return Tables(it, qd, qw, rd, wr)
+
+
+# -- validation -----------------------------------------------------------------------------
+
+class PlanBoundsError(ValueError):
+    """A work row would read or write outside the memory registered for it."""
+
+
+def _merge(ranges: Sequence[tuple[int, int]]) -> tuple[np.ndarray, np.ndarray]:
+    rs = sorted((int(a), int(b)) for a, b in ranges if b > a)
+    lo, hi = [], []
+    for a, b in rs:
+        if lo and a <= hi[-1]:
+            hi[-1] = max(hi[-1], b)
+        else:
+            lo.append(a)
+            hi.append(b)
+    return np.array(lo, dtype=np.uint64), np.array(hi, dtype=np.uint64)
+
+
+def _check(starts: np.ndarray, ends: np.ndarray, ranges, what: str) -> None:
+    if len(starts) == 0:
+        return
+    lo, hi = _merge(ranges)
+    if len(lo) == 0:
+        raise PlanBoundsError(f"{what}: no registered memory")
+    idx = np.searchsorted(lo, starts, side="right").astype(np.int64) - 1
+    ok = idx >= 0
+    ok[ok] &= ends[ok] <= hi[idx[ok]]
+    if not ok.all():
+        bad = int(np.flatnonzero(~ok)[0])
+        raise PlanBoundsError(f"{what}: row {bad} spans [{int(starts[bad]):#x}, {int(ends[bad]):#x}) outside "
+                              f"every registered range")
+
+
+def validate_tables(tables: Tables, src_ranges: Sequence[tuple[int, int]],
+                    dst_ranges: Sequence[tuple[int, int]]) -> None:
+    """Check every work row against the memory it may touch: reads inside ``src_ranges``
+    (the sender's bound tensors), writes inside ``dst_ranges`` (the receivers' exported
+    allocations).  Runs on the host before a table is uploaded, so a planning error is an
+    exception rather than a stray store into another process's memory."""
+    it = tables.items
+    if len(it):
+        rows = it["rows"].astype(np.uint64)
+        last = np.maximum(rows, 1) - np.uint64(1)
+        s0 = it["src"]
+        s1 = s0 + last * it["src_pitch"].astype(np.uint64) + it["row_bytes"].astype(np.uint64)
+        d0 = it["dst"]
+        d1 = d0 + last * it["dst_pitch"].astype(np.uint64) + it["dst_row_bytes"].astype(np.uint64)
+        if (it["src_pitch"] < 0).any() or (it["dst_pitch"] < 0).any():
+            raise PlanBoundsError("negative row pitch in a work row")
+        _check(s0, s1, src_ranges, "read")
+        _check(d0, d1, dst_ranges, "write")
+    q = tables.qdescs
+    if len(q):
+        from ..utils.dtypes import CODE_DTYPES
+        es = np.array([CODE_DTYPES[int(c)].itemsize for c in q["src_code"]], dtype=np.uint64)
+        rows = q["rows"].astype(np.uint64)
+        cols = q["cols"].astype(np.uint64)
+        last = np.maximum(rows, 1) - np.uint64(1)
+        _check(q["src"], q["src"] + last * q["src_pitch"].astype(np.uint64) + cols * es, src_ranges, "quant read")
+        _check(q["dst"], q["dst"] + last * q["dst_pitch"].astype(np.uint64) + cols, dst_ranges, "quant write")
+        bn, bk = q["bn"].astype(np.uint64), q["bk"].astype(np.uint64)
+        nbr = (rows + bn - np.uint64(1)) // bn
+        nbc = (cols + bk - np.uint64(1)) // bk
+        _check(q["scale"], q["scale"] + (nbr - np.uint64(1)) * q["scale_pitch"].astype(np.uint64) + nbc * np.uint64(4),
+               dst_ranges, "scale write")
+
+
+def storage_ranges(tensors) -> list[tuple[int, int]]:
+    """Byte ranges of the storages behind a collection of tensors (or lists of views)."""
+    out = []
+    for v in tensors:
+        for t in (v if isinstance(v, (list, tuple)) else [v]):
+            if isinstance(t, torch.Tensor):
+                st = t.untyped_storage()
+                out.append((st.data_ptr(), st.data_ptr() + st.nbytes()))
+    return out

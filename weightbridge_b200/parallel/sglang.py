@@ -148,12 +148,17 @@ class SGLangLayout:
             return torch.float8_e4m3fn
         return dtype
 
-    def allocate(self, device="cpu", dtype=torch.bfloat16, fill: bool = False, seed: int = 0
-                 ) -> dict[str, torch.Tensor]:
+    def allocate(self, device="cpu", dtype=torch.bfloat16, fill: bool = False, seed: int = 0,
+                 pool: bool = False) -> dict[str, torch.Tensor]:
         """Allocate this rank's parameters (zeros); ``fill`` writes the expected synthetic
-        weights (quantised where the layout is fp8), i.e. what a sync should produce."""
-        params = {n: torch.zeros(s, dtype=self.param_dtype(n, k, dtype), device=device)
-                  for n, (s, k) in self.param_specs().items()}
+        weights (quantised where the layout is fp8), i.e. what a sync should produce.
+        ``pool`` places every parameter in one allocation (one CUDA IPC handle to export
+        instead of one per parameter), each start aligned to 256 bytes."""
+        specs = [(n, s, self.param_dtype(n, k, dtype)) for n, (s, k) in self.param_specs().items()]
+        if pool:
+            params = pooled_zeros(specs, device)
+        else:
+            params = {n: torch.zeros(s, dtype=dt, device=device) for n, s, dt in specs}
         if fill:
             self.fill_expected(params, seed)
         return params
@@ -301,6 +306,26 @@ class SGLangLayout:
                 meta[hf] = entry
                 views[hf] = view
         return WeightData(meta), views
+
+
+def pooled_zeros(specs, device, align: int = 256) -> dict[str, torch.Tensor]:
+    """Zero tensors of the given (name, shape, dtype) carved out of one allocation."""
+    offs, total = [], 0
+    for _n, shape, dt in specs:
+        total = (total + align - 1) // align * align
+        offs.append(total)
+        numel = 1
+        for d in shape:
+            numel *= d
+        total += numel * dt.itemsize
+    buf = torch.zeros(max(total, 1), dtype=torch.uint8, device=device)
+    out = {}
+    for (n, shape, dt), off in zip(specs, offs):
+        numel = 1
+        for d in shape:
+            numel *= d
+        out[n] = buf[off:off + numel * dt.itemsize].view(dt).view(shape)
+    return out
 
 
 def convert_to_wb(model_config: Any, state_dict: dict[str, torch.Tensor], tp_rank: int, tp_size: int,

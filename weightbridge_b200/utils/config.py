@@ -39,7 +39,7 @@ class TransferConfig:
     grid: int = 0                         # 0: sized from the SM count
     verify_flags: bool = True             # receiver checks every sender's epoch flag
     load_balance: bool = True             # spread replicated shards over senders
-    debug_bounds: bool = False            # validate every work row against registered ranges
+    validate_plan: bool = True            # check every work row against registered memory before upload
 
     def __post_init__(self):
         self.mode = normalize_mode(self.mode)
