@@ -1,0 +1,13 @@
+"""The single-node example runs end to end on CPU (gloo path)."""
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_single_node_example_cpu():
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "examples", "single_node.py"), "--device", "cpu",
+                          "--steps", "2", "--workers", "2"], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-3000:]
+    assert "all syncs verified" in out.stdout

@@ -38,6 +38,7 @@ from ..core.binding import bind
 from ..core.plan import lower_ops, phys_binding, plan_digest, plan_pair, wire_binding
 from ..core.shard import WeightData
 from ..utils.config import TransferConfig, normalize_mode
+from ..utils.trace import nvtx_range
 from .assign import expected_senders, restrict
 from .protocol import (CONNECT_REQUEST, METADATA_REQUEST, RECEIVE_REQUEST, STATS_REQUEST, STOP_REQUEST,
                        UPDATE_REQUEST, ReceiverState, b64)
@@ -260,7 +261,8 @@ class WeightReceiver:
 
     def _do_update(self, sock) -> None:
         try:
-            rec = self._receive()
+            with nvtx_range("wbridge.receive"):
+                rec = self._receive()
             self.stats.append(rec)
             self._state = ReceiverState.CONNECTED
             sock.send_string(json.dumps({"success": True, "epoch": self.epoch, "stats": rec}))

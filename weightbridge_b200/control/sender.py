@@ -42,6 +42,7 @@ from ..core.plan import (PhysBinding, PlanBoundsError, Tables, lower_ops, phys_b
 from ..core.shard import WeightData
 from ..utils.config import TransferConfig, normalize_mode
 from .assign import assign_sources, restrict
+from ..utils.trace import nvtx_range
 from .session import PeerError, Session, SessionTimeout, local_address
 
 logger = logging.getLogger(__name__)
@@ -66,9 +67,18 @@ class SyncStats:
         return dict(self.__dict__)
 
 
+_HTTP = None
+
+
 def _http():
-    import requests
-    return requests
+    """A shared ``requests.Session``: keep-alive connections to the rollout servers, so the
+    per-sync ``/wbridge/receive`` arm does not pay a TCP handshake."""
+    global _HTTP
+    if _HTTP is None:
+        import requests
+        _HTTP = requests.Session()
+        _HTTP.ConnectionError = requests.ConnectionError
+    return _HTTP
 
 
 def _get_with_retry(http, url: str, timeout_s: float):
@@ -333,17 +343,25 @@ class WeightSender:
                                    f"sender {self.rank}: {message}")
 
     def send(self, state_dict: dict[str, Any]) -> SyncStats:
+        """One full sync: arm the rollout side, wait until every target receiver is ready,
+        launch the transfer kernel, wait for it and report completion.  NVTX ranges mark
+        the phases (``wbridge.send/arm``, ``/ready``, ``/transfer``)."""
+        with nvtx_range("wbridge.send"):
+            return self._send(state_dict)
+
+    def _send(self, state_dict: dict[str, Any]) -> SyncStats:
         if not self.connected or self.metadata is None:
             raise RuntimeError("WeightSender.send requires connect() first")
         cfg = self.config
         t0 = time.perf_counter()
         if self.rank == 0:
             http = _http()
-            for url in self.receiver_urls:
-                resp = http.post(f"{url}/wbridge/receive", timeout=cfg.http_timeout_s)
-                resp.raise_for_status()
-                if resp.json().get("status") != "success":
-                    raise TransferError(f"receiver {url} refused the sync: {resp.json()}")
+            with nvtx_range("wbridge.send/arm"):
+                for url in self.receiver_urls:
+                    resp = http.post(f"{url}/wbridge/receive", timeout=cfg.http_timeout_s)
+                    resp.raise_for_status()
+                    if resp.json().get("status") != "success":
+                        raise TransferError(f"receiver {url} refused the sync: {resp.json()}")
         epoch = self.epoch + 1
         try:
             key = self._key(state_dict)
@@ -357,8 +375,9 @@ class WeightSender:
         st = SyncStats(epoch=epoch, receivers=sorted(self.targets))
         t1 = time.perf_counter()
         try:
-            sess.wait_checked([f"ready/{r}/{epoch}" for r in self.targets], cfg.sync_timeout_s,
-                              f"receivers {sorted(self.targets)} to be ready for epoch {epoch}")
+            with nvtx_range("wbridge.send/ready"):
+                sess.wait_checked([f"ready/{r}/{epoch}" for r in self.targets], cfg.sync_timeout_s,
+                                  f"receivers {sorted(self.targets)} to be ready for epoch {epoch}")
         except (SessionTimeout, PeerError) as e:
             self._fail_epoch(epoch, str(e))
             raise TransferError(str(e)) from None
@@ -384,10 +403,11 @@ class WeightSender:
             cur = torch.cuda.current_stream(prog.device)
             self._stream.wait_stream(cur)
             e0, e1 = self._ev
-            e0.record(self._stream)
-            prog.launch(epoch, self._stream)
-            e1.record(self._stream)
-            e1.synchronize()
+            with nvtx_range("wbridge.send/transfer"):
+                e0.record(self._stream)
+                prog.launch(epoch, self._stream)
+                e1.record(self._stream)
+                e1.synchronize()
             st.device_ms = e0.elapsed_time(e1)
             st.status = prog.read_status()
             st.bytes_read, st.bytes_written = prog.bytes_read, prog.bytes_written
