@@ -46,7 +46,8 @@ def parse(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--config", default="llama8b",
                    choices=["llama8b", "llama8b-fanout", "qwen3-moe-fp8", "llama70b-colocated"])
-    p.add_argument("--impl", default="wbridge", choices=["wbridge", "reference"])
+    p.add_argument("--impl", default="wbridge", choices=["wbridge", "reference", "torch-p2p"],
+                   help="torch-p2p: the reference's algorithm (per-box torch copies + NCCL isend/irecv)")
     p.add_argument("--mode", type=int, default=None, help="kernel mode: 0 vector, 1/2/3 TMA bulk")
     p.add_argument("--piece", type=int, default=None)
     p.add_argument("--item-bytes", type=int, default=None)
@@ -387,10 +388,85 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     dist.destroy_process_group()
 
 
+def torch_p2p_main(args):
+    """The reference's data path on torch.distributed (per-box torch copies + NCCL P2P), same
+    scenarios and bytes as the library path; device-timed, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, ROOT)
+    from weightbridge_b200.baselines.torch_p2p import build_plan, sync
+    from weightbridge_b200.core.binding import bind
+    from weightbridge_b200.models.arch import get_arch
+    from weightbridge_b200.parallel.megatron import MegatronLayout
+    from weightbridge_b200.parallel.sglang import SGLangLayout
+    launched = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    model, roles, desc = scenario(args.config, args.gpus)
+    if len(roles) != launched or len({r.device for r in roles}) != len(roles):
+        if rank == 0:
+            print(json.dumps({"impl": "torch-p2p", "unavailable":
+                              "this layout puts two ranks on one GPU, which NCCL point-to-point does not support"}))
+        return
+    role = roles[rank]
+    dev = torch.device("cuda", role.device)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("cpu:gloo,cuda:nccl", device_id=dev)
+    arch = get_arch(model)
+    if role.kind == "trainer":
+        lay = MegatronLayout(arch, **role.layout)
+        params = lay.allocate(device=dev, dtype=torch.bfloat16)
+    else:
+        lay = SGLangLayout(arch, **role.layout)
+        params = lay.allocate(device=dev, dtype=torch.bfloat16)
+    meta, views = lay.to_wb(params)
+    binding = bind(meta, views)
+    plan = build_plan(rank, launched, meta, role.kind == "trainer", dev)
+    for _ in range(args.warmup):
+        sync(plan, binding)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        sync(plan, binding)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    ok = 1
+    if role.kind == "rollout" and not args.no_verify:
+        exp = lay.allocate(device=dev, dtype=torch.bfloat16, fill=True)
+        ok = int(all(torch.equal(params[n].view(torch.uint8) if params[n].dtype == torch.float8_e4m3fn else params[n],
+                                 exp[n].view(torch.uint8) if exp[n].dtype == torch.float8_e4m3fn else exp[n])
+                     for n in params))
+    t = torch.tensor([ms, plan.bytes_sent, ok], dtype=torch.float64)
+    gathered = [torch.zeros_like(t) for _ in range(launched)]
+    dist.all_gather(gathered, t)
+    G = torch.stack(gathered)
+    if rank == 0:
+        ms_max = float(G[:, 0].max())
+        payload = float(G[:, 1].sum())
+        value = payload / (ms_max / 1e3) / 1e9
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic: random-init N(0,0.02) weights",
+            "config": {"model": model, "config": args.config, "layout": desc, "parallelism": desc,
+                       "payload_bytes_per_sync": int(payload)},
+            "latency_s": round(ms_max / 1e3, 6), "gbs_per_gpu": round(value / args.gpus, 2),
+            "verified": bool(G[:, 2].min() == 1) if not args.no_verify else None,
+            "impl": "torch-p2p", "path": "per-box torch copies + NCCL isend/irecv (the reference's algorithm)"}),
+            flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
+        return
+    if args.impl == "torch-p2p":
+        torch_p2p_main(args)
         return
     launch_main(args)
 
