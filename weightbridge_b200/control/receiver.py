@@ -69,6 +69,7 @@ class WeightReceiver:
         self.epoch = 0
         self.session: Session | None = None
         self._pending_update: dict | None = None
+        self._garbage: list[str] = []
         fd, path = tempfile.mkstemp(prefix=f"wbridge_sched_{rank}_")
         os.close(fd)
         os.unlink(path)
@@ -266,6 +267,7 @@ class WeightReceiver:
             self.stats.append(rec)
             self._state = ReceiverState.CONNECTED
             sock.send_string(json.dumps({"success": True, "epoch": self.epoch, "stats": rec}))
+            self._collect_garbage()
         except Exception as e:
             logger.exception("receiver %d update failed", self.rank)
             self._error = f"{type(e).__name__}: {e}"
@@ -372,14 +374,21 @@ class WeightReceiver:
                 stale = [s for s in self.expected if int(flags[s]) != epoch]
                 if stale:
                     raise ReceiveError(f"flags of senders {stale} do not hold epoch {epoch}: {flags.tolist()}")
-            for s in self.expected:
-                sess.delete(f"done/{s}/{gr}/{epoch}")
-            sess.delete(f"ready/{gr}/{epoch - 1}")
+            # handshake keys of this epoch are deleted after the reply (off the critical path)
+            self._garbage += [f"done/{s}/{gr}/{epoch}" for s in self.expected]
+            if epoch > 1:
+                self._garbage.append(f"ready/{gr}/{epoch - 1}")
         self.epoch = epoch
         return {"epoch": epoch, "host_ms": (time.perf_counter() - t0) * 1e3, "bytes": self.expected_bytes,
                 "senders": self.expected}
 
+    def _collect_garbage(self) -> None:
+        sess = self.session
+        while self._garbage and sess is not None:
+            sess.delete(self._garbage.pop())
+
     def _teardown(self) -> None:
         self.session = None
         self._gloo = None
+        self._garbage = []
 

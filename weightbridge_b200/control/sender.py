@@ -396,8 +396,7 @@ class WeightSender:
             self._program.launch(epoch)
             st.device_ms = (time.perf_counter() - t2) * 1e3
             st.bytes_read, st.bytes_written = self._program.bytes_read, self._program.bytes_written
-            for r in self.targets:
-                sess.set(f"done/{self.rank}/{r}/{epoch}", "0")
+            sess.multi_set([f"done/{self.rank}/{r}/{epoch}" for r in self.targets], ["0"] * len(self.targets))
         elif self.targets:
             prog = self._program
             cur = torch.cuda.current_stream(prog.device)
@@ -411,8 +410,7 @@ class WeightSender:
             st.device_ms = e0.elapsed_time(e1)
             st.status = prog.read_status()
             st.bytes_read, st.bytes_written = prog.bytes_read, prog.bytes_written
-            for r in self.targets:
-                sess.set(f"done/{self.rank}/{r}/{epoch}", str(st.status))
+            sess.multi_set([f"done/{self.rank}/{r}/{epoch}" for r in self.targets], [str(st.status)] * len(self.targets))
             if st.status:
                 prog.clear_status()
                 raise TransferError(f"transfer kernel reported status {st.status:#x} at epoch {epoch}")

@@ -83,8 +83,10 @@ class Session:
         """Wait for ``keys`` (one blocking call) and raise ``PeerError`` if a peer stored an
         error in any of them instead of a value."""
         keys = list(keys)
+        if not keys:
+            return []
         self.wait(keys, timeout_s, what)
-        vals = [self.store.get(k) for k in keys] if keys else []
+        vals = self.store.multi_get(keys) if len(keys) > 1 else [self.store.get(keys[0])]
         for k, v in zip(keys, vals):
             if v.startswith(ERROR_PREFIX):
                 raise PeerError(v[len(ERROR_PREFIX):].decode(errors="replace"))
@@ -97,6 +99,10 @@ class Session:
                 self.store.set(k, ERROR_PREFIX + message.encode())
             except Exception:
                 pass
+
+    def multi_set(self, keys: list[str], values: list[bytes | str]) -> None:
+        if keys:
+            self.store.multi_set(keys, [v if isinstance(v, bytes) else v.encode() for v in values])
 
     def check(self, key: str) -> bool:
         return self.store.check([key])
