@@ -200,3 +200,36 @@ def test_receive_request_rejected_before_connect():
         assert stats[0]["state"] == "disconnected"
     finally:
         ro.close()
+
+
+@pytest.mark.parametrize("mode", ["cpu_direct", "gpu_direct"])
+def test_resume_after_receiver_restart(mode):
+    """A rollout worker restarts (new process state, new tensors): the sender reconnects and
+    the next sync lands in the new worker's memory."""
+    cfg = _cfg(mode=mode)
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender(mode, [ro.url], config=cfg)
+        s.connect(meta)
+        th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+        th.start()
+        s.send(views)
+        th.join(20)
+        # the worker dies and comes back with fresh (zeroed) parameters under the same rank
+        ro.recv.stop()
+        fresh = ro.lay.allocate(dtype=torch.float32)
+        m2, v2 = ro.lay.to_wb(fresh)
+        ro.recv = WeightReceiver(ro.ctl.ipc_name, 0, m2, state_dict=v2, config=cfg)
+        time.sleep(0.2)
+        s.reconnect()
+        lay.fill(params, seed=9)
+        th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+        th.start()
+        st = s.send(views)
+        th.join(20)
+        assert st.epoch == 1
+        exp = ro.lay.allocate(dtype=torch.float32, fill=True, seed=9)
+        assert all(torch.equal(fresh[n], exp[n]) for n in exp)
+    finally:
+        ro.close()

@@ -44,6 +44,7 @@ class WeightReceiverController:
         self._ctx = zmq.Context()
         self._sock = self._ctx.socket(zmq.ROUTER)
         self._sock.setsockopt(zmq.ROUTER_MANDATORY, 1)
+        self._sock.setsockopt(zmq.ROUTER_HANDOVER, 1)     # a restarted worker takes over its identity
         self._sock.setsockopt(zmq.LINGER, 0)
         self._sock.bind(self._ipc_name)
         self._lock = threading.Lock()

@@ -121,6 +121,7 @@ class WeightSender:
         self._program_key = None
         self._imports: dict[int, Any] = {}
         self._rinfo: dict[int, dict] = {}
+        self._ops_cache: dict[tuple, list] = {}     # plan ops per (receiver, bindings, names)
 
     # -- collectives on the trainer group (no-ops for a single sender) -------------------
     def _all_gather(self, obj):
@@ -242,6 +243,14 @@ class WeightSender:
                 raise TransferError(f"receiver {r} holds host memory in another process; use cpu_direct")
             self._imports[r] = ImportTable(info["allocs"], same_process=(info["pid"] == pid))
 
+    def reconnect(self) -> None:
+        """Connect again with the last metadata, e.g. after a rollout worker restarted: a new
+        session, fresh IPC mappings, epochs restarting at 1.  Plan ops are reused for every
+        receiver whose physical binding did not change."""
+        if self.metadata is None:
+            raise RuntimeError("reconnect() needs a previous connect()")
+        self.connect(self.metadata)
+
     def disconnect(self) -> None:
         for imp in self._imports.values():
             imp.close()
@@ -259,12 +268,17 @@ class WeightSender:
         binding = bind(self.metadata, state_dict)
         device = binding.device
         sphys = phys_binding(binding)
+        skey = _digest(sphys.to_json())
         parts, flags, dst_ranges = [], [], []
         for r, names in sorted(self.targets.items()):
             info = self._rinfo[r]
-            rphys = PhysBinding.from_json(info["binding"])
             imp = self._imports[r]
-            ops = plan_pair(sphys, rphys, names=names)
+            ckey = (r, _digest(info["binding"]), skey, tuple(names))
+            ops = self._ops_cache.get(ckey)
+            rphys = PhysBinding.from_json(info["binding"])
+            if ops is None:
+                ops = plan_pair(sphys, rphys, names=names)
+                self._ops_cache[ckey] = ops
             parts.append(lower_ops(ops, lambda a: 0, imp.base, item_bytes=cfg.item_bytes))
             falloc, foff, _w = info["flags"]
             flags.append(imp.base(falloc) + foff + 8 * self.rank)
@@ -420,6 +434,12 @@ class WeightSender:
         if len(self.history) > 256:
             del self.history[:128]
         return st
+
+
+def _digest(obj) -> str:
+    import hashlib
+    import json
+    return hashlib.sha256(json.dumps(obj, sort_keys=True, separators=(",", ":")).encode()).hexdigest()
 
 
 def _phys_extents(pb: PhysBinding) -> list[tuple[int, int]]:
