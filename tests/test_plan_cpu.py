@@ -174,3 +174,22 @@ def test_real_plans_validate(model, meg, sgl):
             rmeta, rviews = rl.to_wb(rparams)
             t = lower_ops(plan_pair(sphys, phys_binding(bind(rmeta, rviews))), ABS, ABS)
             validate_tables(t, storage_ranges(params.values()), storage_ranges(rparams.values()))
+
+
+def test_multicast_lowering_rules():
+    from weightbridge_b200.core.plan import OP_COPY_MC, Op, multicast_ok
+    a = torch.zeros(64, dtype=torch.bfloat16)
+    ok = Op("copy", "x", (-1, 0), (0, 256), [64], [1], [1], torch.bfloat16, torch.bfloat16)
+    assert multicast_ok(ok, lambda x: a.data_ptr() // 16 * 16, lambda x: 1 << 20)
+    t = lower_ops([ok], lambda x: 4096, lambda x: 1 << 20, multicast=True)
+    assert ((t.items["op"] & 0xFF) == OP_COPY_MC).all()
+    odd = Op("copy", "x", (-1, 2), (0, 256), [64], [1], [1], torch.bfloat16, torch.bfloat16)
+    assert not multicast_ok(odd, lambda x: 4096, lambda x: 1 << 20)
+    cast = Op("cast", "x", (-1, 0), (0, 0), [64], [1], [1], torch.float32, torch.bfloat16)
+    assert not multicast_ok(cast, lambda x: 4096, lambda x: 1 << 20)
+    with pytest.raises(ValueError):
+        lower_ops([cast], lambda x: 0, lambda x: 0, multicast=True)
+    q = Op("quant", "x", (-1, 0), (0, 0), [128, 128], [128, 1], [128, 1], torch.bfloat16, torch.float8_e4m3fn,
+           (0, 0), [1, 1], (128, 128))
+    with pytest.raises(ValueError):
+        lower_ops([q], lambda x: 0, lambda x: 0, multicast=True)

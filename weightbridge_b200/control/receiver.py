@@ -300,7 +300,9 @@ class WeightReceiver:
             phys = phys_binding(binding)
             info.update({"device": -1, "allocs": [], "binding": phys.to_json(),
                          "flags": [-1, self.flags.data_ptr(), W]})
-        elif mode in ("gpu_direct", "nvls"):
+        elif mode == "nvls":
+            self._join_nvls_export(binding, info, W)
+        elif mode == "gpu_direct":
             from ..parallel.ipc import ExportTable
             from ..ops._ext import ext
             torch.cuda.set_device(self.device)
@@ -329,6 +331,8 @@ class WeightReceiver:
             self.overlaps[s] = ov
             self.expected_bytes += ov.total_nbytes()
         sess.set(f"verified/{gr}", "1")
+        if mode == "nvls" and self.device.type == "cuda":
+            self._join_nvls_group(sess, gr)
         if mode == "cpu_direct":
             from .sender import gloo_group
             self._gloo = gloo_group(sess, gr, self.world_size, self.config.connect_timeout_s, data["master_address"])
@@ -382,12 +386,77 @@ class WeightReceiver:
         return {"epoch": epoch, "host_ms": (time.perf_counter() - t0) * 1e3, "bytes": self.expected_bytes,
                 "senders": self.expected}
 
+    # -- NVLink multicast (mode "nvls") -----------------------------------------------------
+    def _join_nvls_export(self, binding, info: dict, W: int) -> None:
+        """Publish this worker's VMM pool (file descriptor server) and its pool-relative binding."""
+        from ..ops._ext import ext
+        from ..parallel.fdpass import FdServer
+        from ..parallel.vmm import find_pool
+        torch.cuda.set_device(self.device)
+        pools = {id(find_pool(bs.tensor.data_ptr())) for views in binding.entries.values() for bs in views}
+        pool = find_pool(next(iter(binding.entries.values()))[0].tensor.data_ptr()) if binding.entries else None
+        if pool is None or len(pools) != 1:
+            raise ReceiveError("mode 'nvls' needs every bound parameter inside one VmmPool "
+                               "(weightbridge_b200.parallel.vmm.VmmPool)")
+        self._pool = pool
+        self.flags = pool.tail(8 * max(W, 1)).view(torch.int64)
+        self.flags.zero_()
+        phys = phys_binding(binding, lambda ptr: (0, ptr - pool.ptr))
+        self._fd_server = FdServer()
+        self._fd_server.publish("pool", pool.export_fd())
+        info.update({"device": self.device.index, "uuid": b64(ext().device_uuid(self.device.index)),
+                     "allocs": [{"vmm": True, "fd_addr": self._fd_server.address, "key": "pool",
+                                 "size": pool.size, "base": pool.ptr}],
+                     "binding": phys.to_json(), "flags": [0, self.flags.data_ptr() - pool.ptr, W],
+                     "pool": {"size": pool.size}})
+
+    def _join_nvls_group(self, sess, gr: int) -> None:
+        """Join this worker's replica group: add the device, bind the pool (see parallel/nvls.py)."""
+        from ..parallel.nvls import McMember
+        plan = sess.get_json("nvls/plan", self.config.connect_timeout_s)
+        self._mc = None
+        for g in plan["groups"]:
+            if gr not in g["replicas"]:
+                continue
+            m = McMember(g["id"], g["size"], self.device.index)
+            m.join(g["addr"])
+            m.add_device()
+            self._mc = (m, g)
+            everyone = g["replicas"] + g["senders"]
+            sess.set(f"nvls/{g['id']}/added/{gr}", "1")
+            sess.wait_checked([f"nvls/{g['id']}/added/{x}" for x in everyone], self.config.connect_timeout_s,
+                              "multicast members to add their devices")
+            m.bind(self._pool)
+            sess.set(f"nvls/{g['id']}/bound/{gr}", "1")
+
+    def _leave_nvls(self) -> None:
+        """Unbind only once every sender of the group unmapped the object (bounded wait)."""
+        mc = getattr(self, "_mc", None)
+        if not mc:
+            return
+        m, g = mc
+        try:
+            if self.session is not None:
+                self.session.wait([f"nvls/{g['id']}/unmapped/{x}" for x in g["senders"]],
+                                  self.config.connect_timeout_s, "senders to unmap the multicast object")
+        finally:
+            m.teardown_binding()
+            self._mc = None
+
     def _collect_garbage(self) -> None:
         sess = self.session
         while self._garbage and sess is not None:
             sess.delete(self._garbage.pop())
 
     def _teardown(self) -> None:
+        try:
+            self._leave_nvls()
+        except Exception:
+            logger.exception("receiver %d: multicast teardown", self.rank)
+        srv = getattr(self, "_fd_server", None)
+        if srv is not None:
+            srv.close()
+            self._fd_server = None
         self.session = None
         self._gloo = None
         self._garbage = []

@@ -37,7 +37,8 @@ import torch
 import torch.distributed as dist
 
 from ..core.binding import bind
-from ..core.plan import (PhysBinding, PlanBoundsError, Tables, lower_ops, phys_binding, plan_digest, plan_pair,
+from ..core.plan import (PhysBinding, PlanBoundsError, Tables, lower_ops, multicast_ok, phys_binding, plan_digest,
+                         plan_pair,
                          storage_ranges, validate_tables, wire_binding)
 from ..core.shard import WeightData
 from ..utils.config import TransferConfig, normalize_mode
@@ -146,6 +147,7 @@ class WeightSender:
         self.metadata = sender_metadata
         cfg = self.config
         metas = self._all_gather(sender_metadata.to_jsonable())
+        self._sender_devices = self._all_gather(torch.cuda.current_device() if torch.cuda.is_available() else -1)
         info = None
         if self.rank == 0:
             info = self._connect_rank0(metas)
@@ -169,6 +171,8 @@ class WeightSender:
                 self._rinfo[r] = sess.get_json(f"recv/{r}", cfg.connect_timeout_s)
             except (SessionTimeout, PeerError) as e:
                 raise TransferError(str(e)) from None
+        if cfg.mode == "nvls":
+            self._setup_multicast(sess, info, assignment)
         if cfg.mode == "cpu_direct":
             # the gloo group needs every rank: join it only once every receiver verified the plan
             everyone = sorted(rmetas)
@@ -243,6 +247,76 @@ class WeightSender:
                 raise TransferError(f"receiver {r} holds host memory in another process; use cpu_direct")
             self._imports[r] = ImportTable(info["allocs"], same_process=(info["pid"] == pid))
 
+    # -- NVLink multicast (mode "nvls") --------------------------------------------------------
+    def _setup_multicast(self, sess: Session, info: dict, assignment: dict) -> None:
+        """Rank 0 finds replica groups and creates one multicast object per group; every
+        sender of a group adds its device, backs the object with a scratch pool and maps it."""
+        from ..parallel.nvls import McMember, nvls_supported, replica_groups
+        cfg = self.config
+        self._mc: dict[int, tuple] = {}
+        self._mc_created: list = []
+        if self.rank == 0:
+            everyone = sorted(int(r) for r in info["receivers"])
+            try:
+                allinfo = {r: sess.get_json(f"recv/{r}", cfg.connect_timeout_s) for r in everyone}
+            except (SessionTimeout, PeerError) as e:
+                raise TransferError(str(e)) from None
+            plan = {int(s): {int(r): n for r, n in rs.items()} for s, rs in assignment.items()}
+            groups = []
+            dev0 = torch.cuda.current_device()
+            for gid, reps in enumerate(replica_groups(allinfo)):
+                senders = [s for s, rs in plan.items()
+                           if all(r in rs for r in reps) and all(rs[r] == rs[reps[0]] for r in reps)]
+                devs = {allinfo[r]["device"] for r in reps} | {self._sender_devices[s] for s in senders}
+                if not senders or not nvls_supported(dev0):
+                    continue
+                size = int(allinfo[reps[0]]["pool"]["size"])
+                m = McMember(gid, size, dev0)
+                m.create(num_devices=len(devs))
+                self._mc_created.append(m)
+                groups.append({"id": gid, "replicas": reps, "senders": senders, "size": size,
+                               "addr": m.server.address})
+            sess.set_json("nvls/plan", {"groups": groups})
+        plan = sess.get_json("nvls/plan", cfg.connect_timeout_s)
+        dev = torch.cuda.current_device()
+        for g in plan["groups"]:
+            if self.rank not in g["senders"]:
+                continue
+            creator = next((m for m in self._mc_created if m.group == g["id"]), None)
+            m = creator if creator is not None else McMember(g["id"], g["size"], dev)
+            if creator is None:
+                m.join(g["addr"])
+            m.add_device()
+            sess.set(f"nvls/{g['id']}/added/{self.rank}", "1")
+            members = g["replicas"] + g["senders"]
+            sess.wait_checked([f"nvls/{g['id']}/added/{x}" for x in members], cfg.connect_timeout_s,
+                              "multicast members to add their devices")
+            m.bind_scratch()
+            sess.set(f"nvls/{g['id']}/bound/{self.rank}", "1")
+            sess.wait_checked([f"nvls/{g['id']}/bound/{x}" for x in members], cfg.connect_timeout_s,
+                              "multicast members to bind memory")
+            m.map()
+            self._mc[g["id"]] = (m, g)
+        logger.info("sender %d: %d multicast group(s)", self.rank, len(self._mc))
+
+    def _teardown_multicast(self) -> None:
+        mc = getattr(self, "_mc", {}) or {}
+        sess = self.session
+        for m, g in mc.values():
+            m.teardown_mapping()
+            if sess is not None:
+                sess.set(f"nvls/{g['id']}/unmapped/{self.rank}", "1")
+        for m, g in mc.values():
+            try:
+                if sess is not None:
+                    sess.wait([f"nvls/{g['id']}/unmapped/{x}" for x in g["senders"]], self.config.connect_timeout_s)
+            finally:
+                m.teardown_binding()
+        for m in getattr(self, "_mc_created", []):
+            if all(m is not x for x, _g in mc.values()):
+                m.teardown_binding()
+        self._mc, self._mc_created = {}, []
+
     def reconnect(self) -> None:
         """Connect again with the last metadata, e.g. after a rollout worker restarted: a new
         session, fresh IPC mappings, epochs restarting at 1.  Plan ops are reused for every
@@ -252,6 +326,7 @@ class WeightSender:
         self.connect(self.metadata)
 
     def disconnect(self) -> None:
+        self._teardown_multicast()
         for imp in self._imports.values():
             imp.close()
         self._imports.clear()
@@ -270,7 +345,29 @@ class WeightSender:
         sphys = phys_binding(binding)
         skey = _digest(sphys.to_json())
         parts, flags, dst_ranges = [], [], []
+        covered: set[int] = set()
+        for m, g in (getattr(self, "_mc", {}) or {}).values():
+            reps = g["replicas"]
+            rep = reps[0]
+            names = self.targets[rep]
+            rphys = PhysBinding.from_json(self._rinfo[rep]["binding"])
+            ops = plan_pair(sphys, rphys, names=names)
+            mc_base = lambda a, va=m.va: va
+            mc_ops = [o for o in ops if multicast_ok(o, lambda a: 0, mc_base)]
+            uni_ops = [o for o in ops if not multicast_ok(o, lambda a: 0, mc_base)]
+            parts.append(lower_ops(mc_ops, lambda a: 0, mc_base, item_bytes=cfg.item_bytes, multicast=True))
+            dst_ranges.append((m.va, m.va + m.size))
+            for r in reps:
+                info, imp = self._rinfo[r], self._imports[r]
+                if uni_ops:          # casts, quantised blocks, unaligned copies: one store per replica
+                    parts.append(lower_ops(uni_ops, lambda a: 0, imp.base, item_bytes=cfg.item_bytes))
+                falloc, foff, _w = info["flags"]
+                flags.append(imp.base(falloc) + foff + 8 * self.rank)
+                dst_ranges += [(imp.base(i), imp.base(i) + int(a["size"])) for i, a in enumerate(info["allocs"])]
+            covered |= set(reps)
         for r, names in sorted(self.targets.items()):
+            if r in covered:
+                continue
             info = self._rinfo[r]
             imp = self._imports[r]
             ckey = (r, _digest(info["binding"]), skey, tuple(names))

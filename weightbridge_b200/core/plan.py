@@ -297,6 +297,8 @@ def lower_ops(ops: Sequence[Op], src_base: Callable[[int], int], dst_base: Calla
         rd += o.src_bytes
         wr += o.dst_bytes
         if o.kind == "quant":
+            if multicast:
+                raise ValueError(f"{o.name}: quantised blocks are stored per receiver, not multicast")
             rows, cols = o.extents
             bn, bk = o.block
             sc = dst_base(o.scale[0]) + o.scale[1]
@@ -310,6 +312,8 @@ def lower_ops(ops: Sequence[Op], src_base: Callable[[int], int], dst_base: Calla
             continue
         kind = OP_COPY if o.kind == "copy" else OP_CAST
         if multicast:
+            if o.kind != "copy":
+                raise ValueError(f"{o.name}: only same-dtype copies can be multicast, not {o.kind}")
             kind = OP_COPY_MC
         word = op_word(kind, o.src_dtype, o.dst_dtype)
         ext, ss, ds = list(o.extents), list(o.src_strides), list(o.dst_strides)
@@ -411,3 +415,16 @@ def storage_ranges(tensors) -> list[tuple[int, int]]:
                 st = t.untyped_storage()
                 out.append((st.data_ptr(), st.data_ptr() + st.nbytes()))
     return out
+
+
+def multicast_ok(op: Op, src_base: Callable[[int], int], dst_base: Callable[[int], int]) -> bool:
+    """Whether an op can go out as 16-byte multimem stores: a same-dtype copy whose rows
+    start, end and stride on 16-byte boundaries on both sides."""
+    if op.kind != "copy":
+        return False
+    es = op.src_dtype.itemsize
+    if op.src_strides[-1] != 1 or op.dst_strides[-1] != 1:
+        return False
+    vals = [src_base(op.src[0]) + op.src[1], dst_base(op.dst[0]) + op.dst[1], op.extents[-1] * es]
+    vals += [st * es for st in op.src_strides[:-1]] + [st * es for st in op.dst_strides[:-1]]
+    return all(v % 16 == 0 for v in vals)

@@ -102,6 +102,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mc_bind_mem", &wb::mc_bind_mem);
   m.def("mc_unbind", &wb::mc_unbind);
   m.def("mc_map", [](uint64_t mc, size_t size, int dev) { return vmm_tuple(wb::mc_map(mc, size, dev)); });
+  m.def("mem_release", &wb::mem_release);
+  m.def("va_unmap", &wb::va_unmap);
   m.attr("ITEM_SIZE") = (int)sizeof(wb::Item);
   m.attr("QDESC_SIZE") = (int)sizeof(wb::QuantDesc);
   m.attr("QWORK_SIZE") = (int)sizeof(wb::QuantWork);

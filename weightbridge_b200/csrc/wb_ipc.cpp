@@ -252,6 +252,21 @@ void mc_unbind(uint64_t mc, int device, size_t mc_offset, size_t size) {
   check_drv(fn((CUmemGenericAllocationHandle)mc, (CUdevice)device, mc_offset, size), "cuMulticastUnbind");
 }
 
+void mem_release(uint64_t handle) {
+  using Fn = CUresult (*)(CUmemGenericAllocationHandle);
+  static Fn fn = entry<Fn>("cuMemRelease");
+  check_drv(fn((CUmemGenericAllocationHandle)handle), "cuMemRelease");
+}
+
+void va_unmap(uint64_t ptr, size_t size) {
+  using Unmap = CUresult (*)(CUdeviceptr, size_t);
+  using Free = CUresult (*)(CUdeviceptr, size_t);
+  static Unmap unmap = entry<Unmap>("cuMemUnmap");
+  static Free afree = entry<Free>("cuMemAddressFree");
+  check_drv(unmap((CUdeviceptr)ptr, size), "cuMemUnmap");
+  check_drv(afree((CUdeviceptr)ptr, size), "cuMemAddressFree");
+}
+
 VmmAlloc mc_map(uint64_t mc, size_t size, int device) {
   using Reserve = CUresult (*)(CUdeviceptr*, size_t, size_t, CUdeviceptr, unsigned long long);
   using Map = CUresult (*)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long);

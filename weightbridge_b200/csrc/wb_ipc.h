@@ -38,5 +38,7 @@ void mc_add_device(uint64_t mc, int device);
 void mc_bind_mem(uint64_t mc, size_t mc_offset, uint64_t mem_handle, size_t mem_offset, size_t size);
 void mc_unbind(uint64_t mc, int device, size_t mc_offset, size_t size);
 VmmAlloc mc_map(uint64_t mc, size_t size, int device);
+void mem_release(uint64_t handle);
+void va_unmap(uint64_t ptr, size_t size);
 
 }  // namespace wb

@@ -54,9 +54,23 @@ class ImportTable:
         self.same_process = same_process
         self.bases: list[int] = []
         self._handles: list[bytes] = []
+        self._pools = []
         for a in allocs:
             if same_process:
                 self.bases.append(int(a["base"]))
+                continue
+            if a.get("vmm"):
+                # a VMM pool served as a file descriptor by the receiver process
+                import os
+                from .fdpass import fetch_fd
+                from .vmm import ImportedPool
+                fd = fetch_fd(a["fd_addr"], a["key"])
+                try:
+                    pool = ImportedPool(fd, int(a["size"]), torch.cuda.current_device())
+                finally:
+                    os.close(fd)
+                self._pools.append(pool)
+                self.bases.append(pool.ptr)
                 continue
             h = unb64(a["handle"])
             with _OPEN_LOCK:
@@ -74,6 +88,9 @@ class ImportTable:
         return self.bases[alloc]
 
     def close(self) -> None:
+        for pool in self._pools:
+            pool.close()
+        self._pools = []
         with _OPEN_LOCK:
             for h in self._handles:
                 ent = _OPEN.get(h)
