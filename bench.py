@@ -53,6 +53,8 @@ def parse(argv=None):
     p.add_argument("--item-bytes", type=int, default=None)
     p.add_argument("--no-verify", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--transfer", default="gpu_direct", choices=["gpu_direct", "nvls"],
+                   help="nvls: rollout pools in VMM memory, multicast stores to replica groups")
     p.add_argument("--no-pool", action="store_true",
                    help="allocate every rollout parameter separately (one IPC handle each)")
     p.add_argument("--stall-dump-s", type=float, default=150.0,
@@ -216,7 +218,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     torch.cuda.set_device(dev)
     trainer_ranks = [i for i, r in enumerate(roles) if r.kind == "trainer"]
     tgroup = dist.new_group(trainer_ranks, backend="gloo")
-    cfg = TransferConfig.from_env(mode="gpu_direct", connect_timeout_s=120, sync_timeout_s=60)
+    cfg = TransferConfig.from_env(mode=args.transfer, connect_timeout_s=120, sync_timeout_s=60)
     if args.mode is not None:
         cfg.kernel_mode = args.mode
     if args.piece is not None:
@@ -232,7 +234,12 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
         meta, views = lay.to_wb(params)
     else:
         lay = SGLangLayout(arch, **role.layout)
-        params = lay.allocate(device=dev, dtype=torch.bfloat16, pool=not args.no_pool)
+        if args.transfer == "nvls":
+            from weightbridge_b200.parallel.vmm import VmmPool
+            vpool = VmmPool(lay.pool_bytes(torch.bfloat16), dev)
+            params = lay.allocate(device=dev, dtype=torch.bfloat16, buffer=vpool.params_buffer())
+        else:
+            params = lay.allocate(device=dev, dtype=torch.bfloat16, pool=not args.no_pool)
         meta, views = lay.to_wb(params)
     torch.cuda.synchronize()
     phase("parameters allocated and filled")
@@ -260,7 +267,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     dist.barrier()
     phase("engines up")
     if role.kind == "trainer":
-        sender = WeightSender("gpu_direct", urls, group=tgroup, config=cfg)
+        sender = WeightSender(args.transfer, urls, group=tgroup, config=cfg)
         sender.connect(meta)
     dist.barrier()
     phase("connected")
@@ -357,7 +364,8 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                        "kernel_mode": cfg.kernel_mode, "piece_bytes": cfg.piece_bytes,
                        "item_bytes": cfg.item_bytes, "work_items_max": int(G[:, 8].max()),
                        "grid": int(G[:, 9].max()), "processes": nprocs,
-                       "rollout_params": "separate allocations" if args.no_pool else "one pooled allocation per rank"},
+                       "rollout_params": "separate allocations" if args.no_pool else "one pooled allocation per rank",
+                       "transfer": args.transfer},
             "latency_s": round(lat, 6),
             "gbs_per_gpu": round(value / ngpu, 2),
             "gbs_per_sender": round(value / max(1.0, float(G[:, 7].sum())), 2),

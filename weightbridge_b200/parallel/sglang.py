@@ -148,15 +148,26 @@ class SGLangLayout:
             return torch.float8_e4m3fn
         return dtype
 
+    def pool_bytes(self, dtype=torch.bfloat16, align: int = 256) -> int:
+        """Bytes ``allocate(pool=True)`` needs (for sizing an external buffer such as a VmmPool)."""
+        total = 0
+        for n, (shape, k) in self.param_specs().items():
+            total = (total + align - 1) // align * align
+            numel = 1
+            for d in shape:
+                numel *= d
+            total += numel * self.param_dtype(n, k, dtype).itemsize
+        return total
+
     def allocate(self, device="cpu", dtype=torch.bfloat16, fill: bool = False, seed: int = 0,
-                 pool: bool = False) -> dict[str, torch.Tensor]:
+                 pool: bool = False, buffer: torch.Tensor | None = None) -> dict[str, torch.Tensor]:
         """Allocate this rank's parameters (zeros); ``fill`` writes the expected synthetic
         weights (quantised where the layout is fp8), i.e. what a sync should produce.
         ``pool`` places every parameter in one allocation (one CUDA IPC handle to export
         instead of one per parameter), each start aligned to 256 bytes."""
         specs = [(n, s, self.param_dtype(n, k, dtype)) for n, (s, k) in self.param_specs().items()]
-        if pool:
-            params = pooled_zeros(specs, device)
+        if pool or buffer is not None:
+            params = pooled_zeros(specs, device, buffer=buffer)
         else:
             params = {n: torch.zeros(s, dtype=dt, device=device) for n, s, dt in specs}
         if fill:
@@ -308,8 +319,9 @@ class SGLangLayout:
         return WeightData(meta), views
 
 
-def pooled_zeros(specs, device, align: int = 256) -> dict[str, torch.Tensor]:
-    """Zero tensors of the given (name, shape, dtype) carved out of one allocation."""
+def pooled_zeros(specs, device, align: int = 256, buffer: torch.Tensor | None = None) -> dict[str, torch.Tensor]:
+    """Zero tensors of the given (name, shape, dtype) carved out of one allocation (a new
+    one, or ``buffer``: a uint8 tensor such as a VmmPool's parameter region)."""
     offs, total = [], 0
     for _n, shape, dt in specs:
         total = (total + align - 1) // align * align
@@ -318,7 +330,13 @@ def pooled_zeros(specs, device, align: int = 256) -> dict[str, torch.Tensor]:
         for d in shape:
             numel *= d
         total += numel * dt.itemsize
-    buf = torch.zeros(max(total, 1), dtype=torch.uint8, device=device)
+    if buffer is not None:
+        if buffer.numel() < total:
+            raise ValueError(f"buffer of {buffer.numel()} bytes cannot hold {total} bytes of parameters")
+        buf = buffer
+        buf[:total].zero_()
+    else:
+        buf = torch.zeros(max(total, 1), dtype=torch.uint8, device=device)
     out = {}
     for (n, shape, dt), off in zip(specs, offs):
         numel = 1
