@@ -29,3 +29,10 @@ def test_three_gpus_two_senders_one_receiver():
     _need(3)
     run("tiny-qwen2", "gpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)], dict(tp=1), device="cuda:2",
         dtype=torch.bfloat16, trainer_devices=["cuda:0", "cuda:1"])
+
+
+def test_two_gpus_nccl_wire_mode():
+    """Cross-node capable path: pack kernel -> NCCL send/recv -> unpack kernel."""
+    _need(2)
+    run("tiny-qwen2", "nccl", [dict(tp=1)], dict(tp=1), device="cuda:1", dtype=torch.bfloat16,
+        trainer_devices=["cuda:0"])

@@ -36,7 +36,7 @@ class ConnectRequest(BaseModel):
     world_size: int
     group_name: str
     sender_world_size: int
-    backend: str = "gpu_direct"          # transfer mode ("nccl"/"gloo" accepted as aliases)
+    backend: str = "gpu_direct"          # transfer mode: gpu_direct | nvls | nccl | cpu_direct ("gloo" = cpu_direct)
     session: Optional[str] = None
 
 

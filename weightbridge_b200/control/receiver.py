@@ -37,7 +37,7 @@ import zmq
 from ..core.binding import bind
 from ..core.plan import lower_ops, phys_binding, plan_digest, plan_pair, wire_binding
 from ..core.shard import WeightData
-from ..utils.config import TransferConfig, normalize_mode
+from ..utils.config import WIRE_MODES, TransferConfig, normalize_mode
 from ..utils.trace import nvtx_range
 from .assign import expected_senders, restrict
 from .protocol import (CONNECT_REQUEST, METADATA_REQUEST, RECEIVE_REQUEST, STATS_REQUEST, STOP_REQUEST,
@@ -280,7 +280,7 @@ class WeightReceiver:
     # -- session -----------------------------------------------------------------------
     def _join(self, data: dict) -> None:
         self._teardown()
-        mode = normalize_mode({"nccl": "gpu_direct", "gloo": "cpu_direct"}.get(data["backend"], data["backend"]))
+        mode = normalize_mode(data["backend"])
         self.mode = mode
         gr = int(data["rank"])
         self.global_rank = gr
@@ -333,15 +333,26 @@ class WeightReceiver:
         sess.set(f"verified/{gr}", "1")
         if mode == "nvls" and self.device.type == "cuda":
             self._join_nvls_group(sess, gr)
-        if mode == "cpu_direct":
-            from .sender import gloo_group
-            self._gloo = gloo_group(sess, gr, self.world_size, self.config.connect_timeout_s, data["master_address"])
-            self._wires = {}
+        if mode in WIRE_MODES:
+            from ..core.plan import Tables
+            from ..ops.executor import LaunchConfig, TransferProgram
+            from .sender import wire_group
+            if (mode == "nccl") != (self.device.type == "cuda"):
+                raise ReceiveError(f"mode {mode} does not take tensors on {self.device}")
+            self._pg = wire_group(mode, sess, gr, self.world_size, self.config.connect_timeout_s,
+                                  data["master_address"])
+            self._wires, parts = {}, []
             for s, ov in self.overlaps.items():
-                wire = torch.empty(ov.total_nbytes(), dtype=torch.uint8)
+                wire = torch.empty(ov.total_nbytes(), dtype=torch.uint8, device=self.device)
                 tables = lower_ops(plan_pair(wire_binding(ov, base=wire.data_ptr()), self._rphys),
                                    lambda a: 0, lambda a: 0, item_bytes=self.config.item_bytes)
                 self._wires[s] = (wire, tables)
+                parts.append(tables)
+            self._unpack = None
+            if self.device.type == "cuda" and parts:
+                self._unpack = TransferProgram(Tables.concat(parts), self.device, [],
+                                               LaunchConfig(mode=self.config.kernel_mode))
+                self._stream = torch.cuda.Stream(self.device)
         self.epoch = 0
         sess.set(f"joined/{gr}", "1")
         logger.info("receiver worker %d joined session as rank %d (mode=%s, senders=%s, %.3f GB expected)",
@@ -354,14 +365,22 @@ class WeightReceiver:
         epoch = self.epoch + 1
         gr = self.global_rank
         t0 = time.perf_counter()
-        if self.mode == "cpu_direct":
+        if self.mode in WIRE_MODES:
             from ..ops.executor import cpu_execute
             sess.set(f"ready/{gr}/{epoch}", "1")
-            works = [(s, self._gloo.recv([wire], s, epoch)) for s, (wire, _t) in self._wires.items()]
-            for s, w in works:
-                w.wait()
-            for s, (wire, tables) in self._wires.items():
-                cpu_execute(tables)
+            if self._unpack is not None:     # device wires: NCCL receives, then one unpack launch
+                with torch.cuda.stream(self._stream):
+                    works = [self._pg.recv([wire], s, epoch) for s, (wire, _t) in self._wires.items()]
+                    for w in works:
+                        w.wait()
+                    self._unpack.launch(epoch, self._stream, signal=False)
+                self._stream.synchronize()
+            else:
+                works = [self._pg.recv([wire], s, epoch) for s, (wire, _t) in self._wires.items()]
+                for w in works:
+                    w.wait()
+                for s, (wire, tables) in self._wires.items():
+                    cpu_execute(tables)
         else:
             sess.set(f"ready/{gr}/{epoch}", "1")
             keys = [f"done/{s}/{gr}/{epoch}" for s in self.expected]
@@ -458,6 +477,6 @@ class WeightReceiver:
             srv.close()
             self._fd_server = None
         self.session = None
-        self._gloo = None
+        self._pg = None
         self._garbage = []
 

@@ -41,7 +41,7 @@ from ..core.plan import (PhysBinding, PlanBoundsError, Tables, lower_ops, multic
                          plan_pair,
                          storage_ranges, validate_tables, wire_binding)
 from ..core.shard import WeightData
-from ..utils.config import TransferConfig, normalize_mode
+from ..utils.config import WIRE_MODES, TransferConfig, normalize_mode
 from .assign import assign_sources, restrict
 from ..utils.trace import nvtx_range
 from .session import PeerError, Session, SessionTimeout, local_address
@@ -173,15 +173,15 @@ class WeightSender:
                 raise TransferError(str(e)) from None
         if cfg.mode == "nvls":
             self._setup_multicast(sess, info, assignment)
-        if cfg.mode == "cpu_direct":
-            # the gloo group needs every rank: join it only once every receiver verified the plan
+        if cfg.mode in WIRE_MODES:
+            # the group needs every rank: join it only once every receiver verified the plan
             everyone = sorted(rmetas)
             try:
                 sess.wait_checked([f"verified/{r}" for r in everyone], cfg.connect_timeout_s,
                                   "receivers to verify the plan")
             except (SessionTimeout, PeerError) as e:
                 raise TransferError(str(e)) from None
-            self._gloo = gloo_group(sess, self.rank, world, cfg.connect_timeout_s, addr)
+            self._pg = wire_group(cfg.mode, sess, self.rank, world, cfg.connect_timeout_s, addr)
         else:
             self._open_receivers()
         try:
@@ -221,7 +221,7 @@ class WeightSender:
                 ov = WeightData.compute_overlap(restrict(smeta_objs[s], names), rmeta_objs[r])
                 sess.set(f"digest/{s}/{r}", plan_digest(ov))
         session_id = uuid.uuid4().hex
-        backend = "gloo" if cfg.mode == "cpu_direct" else cfg.mode
+        backend = cfg.mode
         base = self.world_size
         for url, count in zip(self.receiver_urls, counts):
             resp = http.post(f"{url}/wbridge/connect", timeout=cfg.http_timeout_s, json={
@@ -400,18 +400,36 @@ class WeightSender:
         self._stream = torch.cuda.Stream(device)
         self._ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
 
-    def _compile_cpu(self, state_dict) -> None:
+    def _compile_wire(self, state_dict) -> None:
+        """Wire modes: pack every target's overlap into one buffer per target (the C++
+        executor for host tensors, one transfer-kernel launch for device tensors)."""
+        from ..ops.executor import LaunchConfig, TransferProgram
+        cfg = self.config
         binding = bind(self.metadata, state_dict)
-        if binding.device.type != "cpu":
-            raise TransferError("cpu_direct sends CPU tensors")
+        dev = binding.device
+        if cfg.mode == "cpu_direct" and dev.type != "cpu":
+            raise TransferError("cpu_direct sends host tensors; use nccl or gpu_direct for device tensors")
+        if cfg.mode == "nccl" and dev.type != "cuda":
+            raise TransferError("nccl mode sends device tensors; use cpu_direct for host tensors")
         sphys = phys_binding(binding)
-        self._wires = {}
+        self._wires, parts = {}, []
         for r, names in sorted(self.targets.items()):
             ov = self.overlaps[r]
-            wire = torch.empty(ov.total_nbytes(), dtype=torch.uint8)
+            wire = torch.empty(ov.total_nbytes(), dtype=torch.uint8, device=dev)
             tables = lower_ops(plan_pair(sphys, wire_binding(ov, base=wire.data_ptr()), names=names, overlap_meta=ov),
-                               lambda a: 0, lambda a: 0, item_bytes=self.config.item_bytes)
+                               lambda a: 0, lambda a: 0, item_bytes=cfg.item_bytes)
+            if cfg.validate_plan:
+                validate_tables(tables, storage_ranges(state_dict.values()), storage_ranges([wire]))
             self._wires[r] = (wire, tables)
+            parts.append(tables)
+        self._program = None
+        if dev.type == "cuda" and parts:
+            torch.cuda.set_device(dev)
+            self._program = TransferProgram(Tables.concat(parts), dev, [],
+                                            LaunchConfig(mode=cfg.kernel_mode, piece_bytes=cfg.piece_bytes,
+                                                         grid=cfg.grid or None))
+            self._stream = torch.cuda.Stream(dev)
+            self._ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
 
     def _key(self, state_dict) -> tuple:
         out = []
@@ -430,8 +448,8 @@ class WeightSender:
         so a later ``send`` still pairs with ``request_update``."""
         if not self.connected:
             raise RuntimeError("WeightSender.launch requires connect() first")
-        if self.config.mode == "cpu_direct":
-            raise RuntimeError("launch() is a device path; cpu_direct uses send()")
+        if self.config.mode in WIRE_MODES:
+            raise RuntimeError("launch() stores into receiver memory; wire modes use send()")
         key = self._key(state_dict)
         if self._program_key != key:
             self._compile(state_dict)
@@ -477,7 +495,7 @@ class WeightSender:
         try:
             key = self._key(state_dict)
             if self._program_key != key:
-                (self._compile_cpu if cfg.mode == "cpu_direct" else self._compile)(state_dict)
+                (self._compile_wire if cfg.mode in WIRE_MODES else self._compile)(state_dict)
                 self._program_key = key
         except Exception as e:
             self._fail_epoch(epoch, f"{type(e).__name__}: {e}")
@@ -493,15 +511,30 @@ class WeightSender:
             self._fail_epoch(epoch, str(e))
             raise TransferError(str(e)) from None
         st.wait_ready_ms = (time.perf_counter() - t1) * 1e3
-        if cfg.mode == "cpu_direct":
+        if cfg.mode in WIRE_MODES:
             from ..ops.executor import cpu_execute
             works = []
-            for r, (wire, tables) in self._wires.items():
-                cpu_execute(tables)
-                works.append(self._gloo.send([wire], r, epoch))
-                st.bytes_written += wire.numel()
-            for w in works:
-                w.wait()
+            if self._program is not None:        # device tensors: one pack launch, then NCCL sends
+                e0, e1 = self._ev
+                with torch.cuda.stream(self._stream):
+                    self._stream.wait_stream(torch.cuda.current_stream(self._program.device))
+                    e0.record(self._stream)
+                    self._program.launch(epoch, self._stream, signal=False)
+                    for r, (wire, _t) in self._wires.items():
+                        works.append(self._pg.send([wire], r, epoch))
+                    for w in works:
+                        w.wait()
+                    e1.record(self._stream)
+                e1.synchronize()
+                st.device_ms = e0.elapsed_time(e1)
+                st.bytes_read = self._program.bytes_read
+            else:
+                for r, (wire, tables) in self._wires.items():
+                    cpu_execute(tables)
+                    works.append(self._pg.send([wire], r, epoch))
+                for w in works:
+                    w.wait()
+            st.bytes_written = sum(w.numel() for w, _t in self._wires.values())
         elif self.targets and self._program.device.type == "cpu":
             t2 = time.perf_counter()
             self._program.launch(epoch)
@@ -553,6 +586,16 @@ def _phys_extents(pb: PhysBinding) -> list[tuple[int, int]]:
 def _check_flag(addr: int, ranges) -> None:
     if not any(lo <= addr and addr + 8 <= hi for lo, hi in ranges):
         raise PlanBoundsError(f"flag word {addr:#x} outside the receiver's registered memory")
+
+
+def wire_group(mode: str, sess: Session, rank: int, world: int, timeout_s: float, address: str):
+    """The payload process group of a wire mode: gloo (host tensors) or NCCL (device tensors),
+    separate from the trainer's own groups and built on the session store."""
+    if mode == "nccl":
+        opts = dist.ProcessGroupNCCL.Options()
+        opts._timeout = timedelta(seconds=timeout_s)
+        return dist.ProcessGroupNCCL(dist.PrefixStore("nccl", sess.store), rank, world, opts)
+    return gloo_group(sess, rank, world, timeout_s, address)
 
 
 def gloo_group(sess: Session, rank: int, world: int, timeout_s: float, address: str):

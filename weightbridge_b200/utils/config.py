@@ -14,7 +14,11 @@ MODE_ALIASES = {
     "gpu_direct": "gpu_direct", "p2p": "gpu_direct", "ipc": "gpu_direct", "ipc_local": "gpu_direct",
     "cpu_direct": "cpu_direct", "cpu": "cpu_direct", "gloo": "cpu_direct",
     "nvls": "nvls", "multicast": "nvls",
+    "nccl": "nccl", "nccl_wire": "nccl",
 }
+
+# modes whose payload travels as packed wire buffers over a process group
+WIRE_MODES = ("cpu_direct", "nccl")
 
 
 def normalize_mode(mode: str) -> str:
