@@ -339,7 +339,8 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     d2h = 4 * active + (int(recv.flags.nbytes) if recv is not None and cfg.verify_flags else 0)
     items = len(sender.program.tables.items) if (sender is not None and sender.program is not None) else 0
     grid = sender.program.grid() if (sender is not None and sender.program is not None) else 0
-    stats = torch.tensor([my_ms, e2e_ms, payload, read, ok, h2d, d2h, active, items, grid, setup_s],
+    kmode = sender.program.config.mode if (sender is not None and sender.program is not None) else -1
+    stats = torch.tensor([my_ms, e2e_ms, payload, read, ok, h2d, d2h, active, items, grid, setup_s, kmode],
                          dtype=torch.float64)
     gathered = [torch.zeros_like(stats) for _ in range(nprocs)]
     dist.all_gather(gathered, stats)
@@ -361,7 +362,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                        "parallelism": desc, "payload_bytes_per_sync": int(payload_total),
                        "bytes_read_per_sync": int(G[:, 3].sum()),
                        "l2": "inputs larger than L2 (GBs per sync); no flush needed",
-                       "kernel_mode": cfg.kernel_mode, "piece_bytes": cfg.piece_bytes,
+                       "kernel_mode": int(G[:, 11].max()), "piece_bytes": cfg.piece_bytes,
                        "item_bytes": cfg.item_bytes, "work_items_max": int(G[:, 8].max()),
                        "grid": int(G[:, 9].max()), "processes": nprocs,
                        "rollout_params": "separate allocations" if args.no_pool else "one pooled allocation per rank",

@@ -29,7 +29,7 @@ from __future__ import annotations
 import json
 import math
 from dataclasses import dataclass
-from typing import Any, Iterable, Iterator, Sequence
+from typing import Any, Iterator, Sequence
 
 import torch
 
@@ -66,11 +66,6 @@ def shard_numel(shard: Shard) -> int:
 
 def shard_extents(shard: Shard) -> list[int]:
     return [r - l for l, r, _ in shard]
-
-
-def logical_numel(shard: Shard) -> int:
-    """Number of elements of the whole logical tensor the shard lives in."""
-    return math.prod(w for _, _, w in shard)
 
 
 def contiguous_strides(extents: Sequence[int]) -> list[int]:
@@ -494,10 +489,3 @@ class TensorBridge:
         for rank, ov in src_metas.items():
             unpack_from(self.binding, ov, chunks[rank])
 
-
-def union_names(metas: Iterable[WeightData]) -> list[str]:
-    seen: dict[str, None] = {}
-    for m in metas:
-        for n in m.meta_dict:
-            seen.setdefault(n, None)
-    return list(seen)
