@@ -233,3 +233,28 @@ def test_resume_after_receiver_restart(mode):
         assert all(torch.equal(fresh[n], exp[n]) for n in exp)
     finally:
         ro.close()
+
+
+@pytest.mark.parametrize("mode", ["cpu_direct", "gpu_direct"])
+def test_reference_style_receiver_gets_tensors_at_update(mode):
+    """The reference's flow: WeightReceiver(controller_ipc_name, rank, metadata) without
+    tensors; the scheduler hands its state_dict to request_update."""
+    cfg = _cfg(mode=mode)
+    ro = Rollout(cfg, make_receiver=False)
+    try:
+        ro.recv = WeightReceiver(ro.ctl.ipc_name, 0, ro.meta, config=cfg)
+        _, views = ro.lay.to_wb(ro.params)
+        lay, params, meta, sviews = _sender(cfg)
+        s = WeightSender(mode, [ro.url], config=cfg)
+        s.connect(meta)
+        for step in range(2):
+            if step:
+                lay.fill(params, seed=step)
+            th = threading.Thread(target=lambda: ro.recv.request_update(views, timeout=20))
+            th.start()
+            s.send(sviews)
+            th.join(20)
+            exp = ro.lay.allocate(dtype=torch.float32, fill=True, seed=step)
+            assert all(torch.equal(ro.params[n], exp[n]) for n in exp), step
+    finally:
+        ro.close()

@@ -121,7 +121,7 @@ class WeightReceiver:
         with ``timeout`` the call first waits up to that many seconds for the arm.
         """
         if state_dict is not None and state_dict is not self.state_dict:
-            if self.session is not None:
+            if getattr(self, "_bound", False):
                 if not self._same_tensors(state_dict):
                     raise ReceiveError("request_update got tensors other than the ones bound at connect; "
                                        "reconnect the sender to rebind")
@@ -289,11 +289,52 @@ class WeightReceiver:
         sess = Session(data["master_address"], int(data["master_port"]), is_master=False,
                        timeout_s=self.config.connect_timeout_s)
         self.session = sess
-        if self.state_dict is None:
-            raise ReceiveError("the receiver needs its state_dict before connect (WeightReceiver(..., state_dict=...))")
-        binding = bind(self.metadata, self.state_dict)
         info: dict[str, Any] = {"rank": gr, "worker": self.rank, "pid": os.getpid(), "host": socket.gethostname(),
                                 "mode": mode}
+        self._W = W
+        self._bound = False
+        if self.state_dict is not None:
+            info.update(self._bind())
+        elif mode == "nvls":
+            raise ReceiveError("mode 'nvls' needs the receiver's state_dict (inside a VmmPool) before connect")
+        else:
+            # late binding: the tensors arrive with the first request_update(state_dict)
+            info["late"] = True
+        sess.set_json(f"recv/{gr}", info)
+        # plan agreement: recompute every expected sender's overlap and compare digests
+        assignment = sess.get_json("assign")
+        smetas = sess.get_json("senders/meta")
+        plan = {int(s): {int(r): v for r, v in rs.items()} for s, rs in assignment.items()}
+        self.expected = expected_senders(plan, gr)
+        self.expected_bytes = 0
+        self.overlaps: dict[int, WeightData] = {}
+        for s in self.expected:
+            ov = WeightData.compute_overlap(restrict(WeightData(smetas[s]), plan[s][gr]), self.metadata)
+            digest = sess.wait_checked([f"digest/{s}/{gr}"])[0].decode()
+            if digest != plan_digest(ov):
+                raise ReceiveError(f"plan digest mismatch with sender {s}: the two sides disagree on the layout")
+            self.overlaps[s] = ov
+            self.expected_bytes += ov.total_nbytes()
+        sess.set(f"verified/{gr}", "1")
+        if mode == "nvls" and self.device.type == "cuda":
+            self._join_nvls_group(sess, gr)
+        if mode in WIRE_MODES:
+            from .sender import wire_group
+            self._pg = wire_group(mode, sess, gr, self.world_size, self.config.connect_timeout_s,
+                                  data["master_address"])
+            self._wires = None
+            if self._bound:
+                self._setup_wires()
+        self.epoch = 0
+        sess.set(f"joined/{gr}", "1")
+        logger.info("receiver worker %d joined session as rank %d (mode=%s, senders=%s, %.3f GB expected)",
+                    self.rank, gr, mode, self.expected, self.expected_bytes / 1e9)
+
+    def _bind(self) -> dict:
+        """Bind the state_dict to the metadata and describe the memory for the senders."""
+        mode, W = self.mode, self._W
+        binding = bind(self.metadata, self.state_dict)
+        info: dict[str, Any] = {}
         if mode in ("gpu_direct", "nvls") and self.device.type == "cpu":
             # host memory: only a sender in this same process can write it (tests, CPU runs)
             self.flags = torch.zeros(max(W, 1), dtype=torch.int64)
@@ -315,48 +356,39 @@ class WeightReceiver:
             self._export = export
         else:
             self._rphys = phys_binding(binding)
-        sess.set_json(f"recv/{gr}", info)
-        # plan agreement: recompute every expected sender's overlap and compare digests
-        assignment = sess.get_json("assign")
-        smetas = sess.get_json("senders/meta")
-        plan = {int(s): {int(r): v for r, v in rs.items()} for s, rs in assignment.items()}
-        self.expected = expected_senders(plan, gr)
-        self.expected_bytes = 0
-        self.overlaps: dict[int, WeightData] = {}
-        for s in self.expected:
-            ov = WeightData.compute_overlap(restrict(WeightData(smetas[s]), plan[s][gr]), self.metadata)
-            digest = sess.wait_checked([f"digest/{s}/{gr}"])[0].decode()
-            if digest != plan_digest(ov):
-                raise ReceiveError(f"plan digest mismatch with sender {s}: the two sides disagree on the layout")
-            self.overlaps[s] = ov
-            self.expected_bytes += ov.total_nbytes()
-        sess.set(f"verified/{gr}", "1")
-        if mode == "nvls" and self.device.type == "cuda":
-            self._join_nvls_group(sess, gr)
-        if mode in WIRE_MODES:
-            from ..core.plan import Tables
-            from ..ops.executor import LaunchConfig, TransferProgram
-            from .sender import wire_group
-            if (mode == "nccl") != (self.device.type == "cuda"):
-                raise ReceiveError(f"mode {mode} does not take tensors on {self.device}")
-            self._pg = wire_group(mode, sess, gr, self.world_size, self.config.connect_timeout_s,
-                                  data["master_address"])
-            self._wires, parts = {}, []
-            for s, ov in self.overlaps.items():
-                wire = torch.empty(ov.total_nbytes(), dtype=torch.uint8, device=self.device)
-                tables = lower_ops(plan_pair(wire_binding(ov, base=wire.data_ptr()), self._rphys),
-                                   lambda a: 0, lambda a: 0, item_bytes=self.config.item_bytes)
-                self._wires[s] = (wire, tables)
-                parts.append(tables)
-            self._unpack = None
-            if self.device.type == "cuda" and parts:
-                self._unpack = TransferProgram(Tables.concat(parts), self.device, [],
-                                               LaunchConfig(mode=self.config.kernel_mode))
-                self._stream = torch.cuda.Stream(self.device)
-        self.epoch = 0
-        sess.set(f"joined/{gr}", "1")
-        logger.info("receiver worker %d joined session as rank %d (mode=%s, senders=%s, %.3f GB expected)",
-                    self.rank, gr, mode, self.expected, self.expected_bytes / 1e9)
+        self._bound = True
+        return info
+
+    def _setup_wires(self) -> None:
+        """Wire modes: one receive buffer per expected sender and the unpack tables."""
+        from ..core.plan import Tables
+        from ..ops.executor import LaunchConfig, TransferProgram
+        if (self.mode == "nccl") != (self.device.type == "cuda"):
+            raise ReceiveError(f"mode {self.mode} does not take tensors on {self.device}")
+        self._wires, parts = {}, []
+        for s, ov in self.overlaps.items():
+            wire = torch.empty(ov.total_nbytes(), dtype=torch.uint8, device=self.device)
+            tables = lower_ops(plan_pair(wire_binding(ov, base=wire.data_ptr()), self._rphys),
+                               lambda a: 0, lambda a: 0, item_bytes=self.config.item_bytes)
+            self._wires[s] = (wire, tables)
+            parts.append(tables)
+        self._unpack = None
+        if self.device.type == "cuda" and parts:
+            self._unpack = TransferProgram(Tables.concat(parts), self.device, [],
+                                           LaunchConfig(mode=self.config.kernel_mode))
+            self._stream = torch.cuda.Stream(self.device)
+
+    def _late_bind(self) -> None:
+        """First update of a receiver that joined without tensors: bind, export, publish."""
+        if self.state_dict is None:
+            raise ReceiveError("request_update needs the state_dict to receive into")
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)
+        extra = self._bind()
+        if self.mode in WIRE_MODES:
+            self._setup_wires()
+        else:
+            self.session.set_json(f"recvbind/{self.global_rank}", extra)
 
     def _receive(self) -> dict:
         sess = self.session
@@ -365,6 +397,8 @@ class WeightReceiver:
         epoch = self.epoch + 1
         gr = self.global_rank
         t0 = time.perf_counter()
+        if not self._bound:
+            self._late_bind()
         if self.mode in WIRE_MODES:
             from ..ops.executor import cpu_execute
             sess.set(f"ready/{gr}/{epoch}", "1")

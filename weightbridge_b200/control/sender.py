@@ -241,6 +241,8 @@ class WeightSender:
         for r, info in self._rinfo.items():
             if info.get("mode") not in ("gpu_direct", "nvls"):
                 raise TransferError(f"receiver {r} joined in mode {info.get('mode')}")
+            if info.get("late"):
+                continue            # bound at its first update; opened in _resolve_late
             if info["host"] != host:
                 raise TransferError(f"receiver {r} is on host {info['host']}: gpu_direct needs one node")
             if info.get("device", 0) < 0 and info["pid"] != pid:
@@ -316,6 +318,22 @@ class WeightSender:
             if all(m is not x for x, _g in mc.values()):
                 m.teardown_binding()
         self._mc, self._mc_created = {}, []
+
+    def _resolve_late(self) -> bool:
+        """Receivers that joined without tensors publish their memory at their first update
+        (before they mark themselves ready); open it now.  True if anything changed."""
+        from ..parallel.ipc import ImportTable
+        changed = False
+        for r, info in self._rinfo.items():
+            if not info.get("late") or r in self._imports:
+                continue
+            try:
+                info.update(self.session.get_json(f"recvbind/{r}", self.config.sync_timeout_s))
+            except (SessionTimeout, PeerError) as e:
+                raise TransferError(str(e)) from None
+            self._imports[r] = ImportTable(info["allocs"], same_process=(info["pid"] == os.getpid()))
+            changed = True
+        return changed
 
     def reconnect(self) -> None:
         """Connect again with the last metadata, e.g. after a rollout worker restarted: a new
@@ -450,6 +468,8 @@ class WeightSender:
             raise RuntimeError("WeightSender.launch requires connect() first")
         if self.config.mode in WIRE_MODES:
             raise RuntimeError("launch() stores into receiver memory; wire modes use send()")
+        if any(info.get("late") and r not in self._imports for r, info in self._rinfo.items()):
+            raise RuntimeError("launch() needs every receiver's memory; run one send() first")
         key = self._key(state_dict)
         if self._program_key != key:
             self._compile(state_dict)
@@ -492,14 +512,6 @@ class WeightSender:
                     if resp.json().get("status") != "success":
                         raise TransferError(f"receiver {url} refused the sync: {resp.json()}")
         epoch = self.epoch + 1
-        try:
-            key = self._key(state_dict)
-            if self._program_key != key:
-                (self._compile_wire if cfg.mode in WIRE_MODES else self._compile)(state_dict)
-                self._program_key = key
-        except Exception as e:
-            self._fail_epoch(epoch, f"{type(e).__name__}: {e}")
-            raise
         sess = self.session
         st = SyncStats(epoch=epoch, receivers=sorted(self.targets))
         t1 = time.perf_counter()
@@ -511,6 +523,16 @@ class WeightSender:
             self._fail_epoch(epoch, str(e))
             raise TransferError(str(e)) from None
         st.wait_ready_ms = (time.perf_counter() - t1) * 1e3
+        try:
+            key = self._key(state_dict)
+            if cfg.mode not in WIRE_MODES and self._resolve_late():
+                self._program_key = None
+            if self._program_key != key:
+                (self._compile_wire if cfg.mode in WIRE_MODES else self._compile)(state_dict)
+                self._program_key = key
+        except Exception as e:
+            self._fail_epoch(epoch, f"{type(e).__name__}: {e}")
+            raise
         if cfg.mode in WIRE_MODES:
             from ..ops.executor import cpu_execute
             works = []
