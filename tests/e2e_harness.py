@@ -15,7 +15,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype):
+def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype, late=False):
     import threading
     import uvicorn
     from fastapi import FastAPI
@@ -31,7 +31,8 @@ def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype):
         params = lay.allocate(device=device, dtype=dtype)
         meta, views = lay.to_wb(params)
         cfg = TransferConfig(mode=mode, connect_timeout_s=60, sync_timeout_s=60)
-        recv = WeightReceiver(ctl.ipc_name, 0, meta, state_dict=views, config=cfg)
+        # late: the reference's flow, tensors handed over at request_update
+        recv = WeightReceiver(ctl.ipc_name, 0, meta, state_dict=None if late else views, config=cfg)
         server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="warning"))
         threading.Thread(target=server.run, daemon=True).start()
         t0 = time.time()
@@ -40,7 +41,7 @@ def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype):
         q.put(("serving", None, None))
         results = []
         for i in range(n_syncs):
-            ok = recv.request_update(timeout=60)
+            ok = recv.request_update(views if late else None, timeout=60)
             exp = lay.allocate(device=device, dtype=dtype, fill=True, seed=i)
             same = all(torch.equal(params[n].view(torch.uint8) if params[n].dtype == torch.float8_e4m3fn else params[n],
                                    exp[n].view(torch.uint8) if exp[n].dtype == torch.float8_e4m3fn else exp[n])
@@ -83,13 +84,14 @@ def trainer_proc(rank, world, tport, url, q, n_syncs, model, mode, device, layou
 
 
 def run(model, mode, trainer_layouts, rollout_layout, device="cpu", dtype=torch.float32, n_syncs=3, timeout=240,
-        trainer_devices=None):
+        trainer_devices=None, late=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     hport, tport = _port(), _port()
     url = f"http://127.0.0.1:{hport}"
     world = len(trainer_layouts)
-    procs = [ctx.Process(target=rollout_proc, args=(hport, q, n_syncs, model, mode, device, rollout_layout, dtype))]
+    procs = [ctx.Process(target=rollout_proc, args=(hport, q, n_syncs, model, mode, device, rollout_layout, dtype,
+                                                    late))]
     tdev = trainer_devices or [device] * world
     procs += [ctx.Process(target=trainer_proc, args=(r, world, tport, url, q, n_syncs, model, mode, tdev[r],
                                                       trainer_layouts, dtype)) for r in range(world)]

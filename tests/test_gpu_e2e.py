@@ -17,3 +17,9 @@ def test_colocated_ipc_tiny_llama_tp2_to_tp1():
 def test_colocated_ipc_qwen3_moe_fp8_experts():
     run("tiny-qwen3-moe", "gpu_direct", [dict(ep=2, ep_rank=0), dict(ep=2, ep_rank=1)],
         dict(tp=1, quant="fp8_experts"), device="cuda:0", dtype=torch.bfloat16, n_syncs=2)
+
+
+def test_colocated_ipc_reference_style_late_binding():
+    """Receiver created with metadata only; tensors handed over at request_update."""
+    run("tiny-qwen3", "gpu_direct", [dict(tp=1)], dict(tp=2, tp_rank=1), device="cuda:0",
+        dtype=torch.bfloat16, late=True)
