@@ -145,12 +145,16 @@ class WeightSender:
         if self.connected:
             self.disconnect()
         self.metadata = sender_metadata
+        self._rinfo = {}
         cfg = self.config
         metas = self._all_gather(sender_metadata.to_jsonable())
         self._sender_devices = self._all_gather(torch.cuda.current_device() if torch.cuda.is_available() else -1)
         info = None
         if self.rank == 0:
-            info = self._connect_rank0(metas)
+            try:
+                info = self._connect_rank0(metas)
+            except Exception as e:   # every rank fails together instead of waiting in the broadcast
+                info = {"error": f"rank 0 could not set up the session: {type(e).__name__}: {e}"}
         info = self._broadcast(info)
         if info.get("error"):
             raise TransferError(info["error"])

@@ -6,7 +6,11 @@
 
 copy:    one contiguous bf16 buffer -> another (HBM read + write), 16-byte aligned;
 strided: column block of a row-major matrix -> contiguous (TP column split), 2-D items;
-quant:   bf16 [E, 768, 2048] expert stack -> fp8 e4m3 + 128x128 fp32 block scales.
+quant:   bf16 [E, 768, 2048] expert stack -> fp8 e4m3 + 128x128 fp32 block scales;
+peer-push / peer-pull / peer-quant (two GPUs, one process, peer access enabled): the kernel
+         runs on GPU 0 and stores into GPU 1 (push), or runs on GPU 1 and loads from GPU 0
+         (pull; plain and bulk loads from a peer, no cluster multicast), or quantises on
+         GPU 0 into GPU 1; bandwidth counts the bytes that cross NVLink.
 Reports device time per launch (CUDA events, after warm-up) and achieved bandwidth against
 the measured copy peak in MEASURED_PEAKS.json when present.
 """
@@ -56,6 +60,28 @@ def build(case: str, gbytes: float, dev, item_bytes: int):
         ops = [Op("quant", "x", (-1, a[i].data_ptr()), (-1, q[i].data_ptr()), [r, c], [c, 1], [c, 1], a.dtype,
                   q.dtype, (-1, s[i].data_ptr()), [c // 128, 1], (128, 128)) for i in range(e)]
         keep, traffic = (a, q, s), a.nbytes + q.nbytes + s.nbytes
+    elif case in ("peer-push", "peer-pull", "peer-quant"):
+        from ._ext import ext
+        if torch.cuda.device_count() < 2:
+            raise SystemExit("peer cases need two GPUs")
+        d0, d1 = torch.device("cuda", 0), torch.device("cuda", 1)
+        for a_, b_ in ((0, 1), (1, 0)):
+            with torch.cuda.device(a_):
+                ext().enable_peer_access(b_)
+        if case == "peer-quant":
+            r, c = 768, 2048
+            e = max(1, n // (r * c))
+            a = torch.randn(e, r, c, device=d0, dtype=torch.bfloat16)
+            q = torch.empty(e, r, c, device=d1, dtype=torch.float8_e4m3fn)
+            s_ = torch.empty(e, r // 128, c // 128, device=d1, dtype=torch.float32)
+            ops = [Op("quant", "x", (-1, a[i].data_ptr()), (-1, q[i].data_ptr()), [r, c], [c, 1], [c, 1], a.dtype,
+                      q.dtype, (-1, s_[i].data_ptr()), [c // 128, 1], (128, 128)) for i in range(e)]
+            keep, traffic = (a, q, s_), q.nbytes + s_.nbytes
+        else:
+            a = torch.randn(n, device=d0, dtype=torch.bfloat16)
+            b = torch.empty(n, device=d1, dtype=torch.bfloat16)
+            ops = [Op("copy", "x", (-1, a.data_ptr()), (-1, b.data_ptr()), [n], [1], [1], a.dtype, a.dtype)]
+            keep, traffic = (a, b), a.nbytes
     else:
         raise SystemExit(f"unknown case {case}")
     return lower_ops(ops, lambda x: 0, lambda x: 0, item_bytes=item_bytes), keep, traffic
@@ -63,7 +89,8 @@ def build(case: str, gbytes: float, dev, item_bytes: int):
 
 def main(argv=None):
     p = argparse.ArgumentParser()
-    p.add_argument("--case", default="copy", choices=["copy", "strided", "quant"])
+    p.add_argument("--case", default="copy",
+                   choices=["copy", "strided", "quant", "peer-push", "peer-pull", "peer-quant"])
     p.add_argument("--gbytes", type=float, default=1.0)
     p.add_argument("--mode", type=int, default=-1)
     p.add_argument("--piece", type=int, default=16384)
@@ -72,7 +99,8 @@ def main(argv=None):
     p.add_argument("--iters", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     a = p.parse_args(argv)
-    dev = torch.device("cuda", 0)
+    dev = torch.device("cuda", 1 if a.case == "peer-pull" else 0)   # pull: the kernel runs on the reader
+    torch.cuda.set_device(dev)
     tables, keep, traffic = build(a.case, a.gbytes, dev, a.item_bytes)
     prog = TransferProgram(tables, dev, [], LaunchConfig(mode=a.mode, piece_bytes=a.piece, grid=a.grid or None))
     for _ in range(a.warmup):
@@ -86,11 +114,11 @@ def main(argv=None):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.iters
     gbs = traffic / (ms / 1e3) / 1e9
-    peak = _peak_gbs()
+    peak = 770.0 if a.case.startswith("peer") else _peak_gbs()   # measured peer copy vs HBM copy
     print(json.dumps({"case": a.case, "gbytes": a.gbytes, "mode": prog.config.mode, "piece": a.piece, "grid": prog.grid(),
                       "items": len(tables.items), "qwork": len(tables.qwork), "ms": round(ms, 4),
                       "traffic_bytes": traffic, "gbs": round(gbs, 1),
-                      "frac_of_measured_copy": round(gbs / peak, 3) if peak else None,
+                      "frac_of_measured": round(gbs / peak, 3) if peak else None,
                       "status": prog.read_status()}))
 
 
