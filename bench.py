@@ -53,6 +53,8 @@ def parse(argv=None):
     p.add_argument("--item-bytes", type=int, default=None)
     p.add_argument("--no-verify", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--direction", default="push", choices=["push", "pull"],
+                   help="gpu_direct: senders store (push) or receivers load the copies (pull)")
     p.add_argument("--transfer", default="gpu_direct", choices=["gpu_direct", "nvls"],
                    help="nvls: rollout pools in VMM memory, multicast stores to replica groups")
     p.add_argument("--no-pool", action="store_true",
@@ -218,7 +220,8 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     torch.cuda.set_device(dev)
     trainer_ranks = [i for i, r in enumerate(roles) if r.kind == "trainer"]
     tgroup = dist.new_group(trainer_ranks, backend="gloo")
-    cfg = TransferConfig.from_env(mode=args.transfer, connect_timeout_s=120, sync_timeout_s=60)
+    cfg = TransferConfig.from_env(mode=args.transfer, connect_timeout_s=120, sync_timeout_s=60,
+                                  direction=args.direction)
     if args.mode is not None:
         cfg.kernel_mode = args.mode
     if args.piece is not None:
@@ -296,15 +299,19 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
         clk.__enter__()
     dist.barrier()
     e0.record(stream)
+    pulls = recv is not None and recv.pull_program is not None and len(recv.pull_program.tables) > 0
     if sender is not None:
         for _ in range(args.steps):
-            sender.launch(views, stream)
+            sender.launch(views, stream)         # the pushed part (everything, unless pulling)
+    elif pulls:
+        for _ in range(args.steps):
+            recv.launch(stream)                  # pull direction: receivers load the copies
     e1.record(stream)
     torch.cuda.synchronize()
     dist.barrier()
     if clk:
         clk.__exit__(None, None, None)
-    my_ms = e0.elapsed_time(e1) / args.steps if sender is not None else 0.0
+    my_ms = e0.elapsed_time(e1) / args.steps if (sender is not None or pulls) else 0.0
 
     # phase B: public API end to end
     e2e_ms = 0.0
@@ -333,10 +340,15 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                 break
         del expected
     payload = sender.program.bytes_written if (sender is not None and sender.program is not None) else 0
+    if recv is not None and recv.pull_program is not None:
+        payload += recv.pull_program.bytes_written
     read = sender.program.bytes_read if (sender is not None and sender.program is not None) else 0
-    active = 1 if payload else 0
-    h2d = 8 * active
-    d2h = 4 * active + (int(recv.flags.nbytes) if recv is not None and cfg.verify_flags else 0)
+    active = 1 if (sender is not None and sender.program is not None and len(sender.program.tables)) else 0
+    active += 1 if (recv is not None and recv.pull_program is not None and len(recv.pull_program.tables)) else 0
+    pushed = 1 if (sender is not None and sender.program is not None and len(sender.program.tables)) else 0
+    pulled = 1 if (recv is not None and recv.pull_program is not None and len(recv.pull_program.tables)) else 0
+    h2d = 8 * pushed                                  # the epoch word, from pinned memory
+    d2h = 4 * (pushed + pulled) + (int(recv.flags.nbytes) if recv is not None and cfg.verify_flags else 0)
     items = len(sender.program.tables.items) if (sender is not None and sender.program is not None) else 0
     grid = sender.program.grid() if (sender is not None and sender.program is not None) else 0
     kmode = sender.program.config.mode if (sender is not None and sender.program is not None) else -1
@@ -366,7 +378,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                        "item_bytes": cfg.item_bytes, "work_items_max": int(G[:, 8].max()),
                        "grid": int(G[:, 9].max()), "processes": nprocs,
                        "rollout_params": "separate allocations" if args.no_pool else "one pooled allocation per rank",
-                       "transfer": args.transfer},
+                       "transfer": args.transfer, "direction": args.direction},
             "latency_s": round(lat, 6),
             "gbs_per_gpu": round(value / ngpu, 2),
             "gbs_per_sender": round(value / max(1.0, float(G[:, 7].sum())), 2),

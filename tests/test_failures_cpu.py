@@ -258,3 +258,65 @@ def test_reference_style_receiver_gets_tensors_at_update(mode):
             assert all(torch.equal(ro.params[n], exp[n]) for n in exp), step
     finally:
         ro.close()
+
+
+def test_pull_direction_in_process():
+    """direction='pull': the receiver loads the copies from the sender's memory (host path in
+    one process), two syncs with new weights, sender waits until the receiver pulled."""
+    cfg = _cfg(mode="gpu_direct", direction="pull")
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender("gpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        for step in range(2):
+            if step:
+                lay.fill(params, seed=step)
+            th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+            th.start()
+            st = s.send(views)
+            th.join(20)
+            assert st.status == 0 and s.program is None          # nothing pushed: no quantised blocks
+            exp = ro.lay.allocate(dtype=torch.float32, fill=True, seed=step)
+            assert all(torch.equal(ro.params[n], exp[n]) for n in exp), step
+        assert ro.recv.pull_program is not None and len(ro.recv.pull_program.tables) > 0
+    finally:
+        ro.close()
+
+
+def test_pull_direction_with_pushed_fp8_blocks():
+    """Hybrid sync: quantised expert blocks pushed by the sender, everything else pulled."""
+    import uvicorn
+    from fastapi import FastAPI
+    cfg = _cfg(mode="gpu_direct", direction="pull")
+    arch = get_arch("tiny-qwen3-moe")
+    rl = SGLangLayout(arch, tp=1, quant="fp8_experts")
+    rparams = rl.allocate(dtype=torch.bfloat16)
+    rmeta, rviews = rl.to_wb(rparams)
+    app = FastAPI()
+    ctl = WeightReceiverController(app, worker_num=1, timeout_s=5)
+    recv = WeightReceiver(ctl.ipc_name, 0, rmeta, state_dict=rviews, config=cfg)
+    port = _port()
+    server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="error"))
+    threading.Thread(target=server.run, daemon=True).start()
+    while not server.started:
+        time.sleep(0.02)
+    try:
+        ml = MegatronLayout(arch, ep=1)
+        sparams = ml.allocate(dtype=torch.bfloat16)
+        smeta, sviews = ml.to_wb(sparams)
+        s = WeightSender("gpu_direct", [f"http://127.0.0.1:{port}"], config=cfg)
+        s.connect(smeta)
+        th = threading.Thread(target=lambda: recv.request_update(timeout=20))
+        th.start()
+        s.send(sviews)
+        th.join(20)
+        assert s.program is not None and len(s.program.tables.qwork) > 0 and len(s.program.tables.items) == 0
+        assert len(recv.pull_program.tables.items) > 0 and len(recv.pull_program.tables.qwork) == 0
+        exp = rl.allocate(dtype=torch.bfloat16, fill=True)
+        u8 = lambda t: t.view(torch.uint8) if t.dtype == torch.float8_e4m3fn else t
+        assert all(torch.equal(u8(rparams[n]), u8(exp[n])) for n in exp)
+    finally:
+        recv.stop()
+        server.should_exit = True
+        ctl.close()

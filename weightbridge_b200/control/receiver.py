@@ -306,6 +306,9 @@ class WeightReceiver:
         smetas = sess.get_json("senders/meta")
         plan = {int(s): {int(r): v for r, v in rs.items()} for s, rs in assignment.items()}
         self.expected = expected_senders(plan, gr)
+        self._names = {s: plan[s][gr] for s in self.expected}
+        self.direction = sess.wait_checked(["direction"])[0].decode() if mode == "gpu_direct" else "push"
+        self._pull_versions, self._pull_prog, self._pull_imports = None, None, {}
         self.expected_bytes = 0
         self.overlaps: dict[int, WeightData] = {}
         for s in self.expected:
@@ -334,6 +337,7 @@ class WeightReceiver:
         """Bind the state_dict to the metadata and describe the memory for the senders."""
         mode, W = self.mode, self._W
         binding = bind(self.metadata, self.state_dict)
+        self._rphys_abs = phys_binding(binding)          # local addresses (pull programs write here)
         info: dict[str, Any] = {}
         if mode in ("gpu_direct", "nvls") and self.device.type == "cpu":
             # host memory: only a sender in this same process can write it (tests, CPU runs)
@@ -423,12 +427,16 @@ class WeightReceiver:
                                          what=f"senders {self.expected} to finish epoch {epoch}")
             except (SessionTimeout, PeerError) as e:
                 raise ReceiveError(str(e)) from None
-            bad = {s: int(v) for s, v in zip(self.expected, vals) if int(v)}
+            done = [v.decode().split(":") for v in vals]          # status:binding-version:pushed
+            bad = {s: int(d[0]) for s, d in zip(self.expected, done) if int(d[0])}
             if bad:
                 raise ReceiveError(f"senders reported kernel status {bad} for epoch {epoch}")
-            if self.config.verify_flags and self.expected:
+            pushed = [s for s, d in zip(self.expected, done) if len(d) < 3 or d[2] == "1"]
+            if self.direction == "pull":
+                self._pull(epoch, {s: int(d[1]) for s, d in zip(self.expected, done)})
+            if self.config.verify_flags and pushed:
                 flags = self.flags.cpu()
-                stale = [s for s in self.expected if int(flags[s]) != epoch]
+                stale = [s for s in pushed if int(flags[s]) != epoch]
                 if stale:
                     raise ReceiveError(f"flags of senders {stale} do not hold epoch {epoch}: {flags.tolist()}")
             # handshake keys of this epoch are deleted after the reply (off the critical path)
@@ -438,6 +446,83 @@ class WeightReceiver:
         self.epoch = epoch
         return {"epoch": epoch, "host_ms": (time.perf_counter() - t0) * 1e3, "bytes": self.expected_bytes,
                 "senders": self.expected}
+
+    # -- pull direction --------------------------------------------------------------------
+    def _pull(self, epoch: int, versions: dict[int, int]) -> None:
+        """Load this worker's copies from the senders' memory (they keep it unchanged until
+        every receiver has reported ``pulled``)."""
+        status = 0
+        try:
+            if versions != self._pull_versions:
+                self._compile_pull(versions)
+            prog = self._pull_prog
+            if prog is not None and len(prog.tables):
+                if prog.device.type == "cpu":
+                    prog.launch(epoch, signal=False)
+                else:
+                    with nvtx_range("wbridge.receive/pull"):
+                        prog.launch(epoch, self._pull_stream, signal=False)
+                        self._pull_stream.synchronize()
+                    status = prog.read_status()
+        except Exception as e:
+            self.session.set_error([f"pulled/{self.global_rank}/{epoch}"], f"receiver {self.global_rank}: {e}")
+            raise
+        self.session.set(f"pulled/{self.global_rank}/{epoch}", str(status))
+        if epoch > 1:   # the senders read epoch e's key before this worker can reach epoch e + 1
+            self._garbage.append(f"pulled/{self.global_rank}/{epoch - 1}")
+        if status:
+            raise ReceiveError(f"pull kernel reported status {status:#x} at epoch {epoch}")
+
+    def _compile_pull(self, versions: dict[int, int]) -> None:
+        from ..core.plan import PhysBinding, Tables, storage_ranges, validate_tables
+        from ..ops.executor import HostProgram, LaunchConfig, TransferProgram
+        from ..parallel.ipc import ImportTable
+        from .sender import _phys_extents
+        for imp in self._pull_imports.values():
+            imp.close()
+        self._pull_imports, parts, src_ranges = {}, [], []
+        for s in self.expected:
+            sb = self.session.get_json(f"sendbind/{s}", self.config.sync_timeout_s)
+            if sb["host"] != socket.gethostname():
+                raise ReceiveError(f"sender {s} is on host {sb['host']}: pulling needs one node")
+            same = sb["pid"] == os.getpid()
+            if not sb["allocs"] and not same:
+                raise ReceiveError(f"sender {s} holds host memory in another process")
+            imp = ImportTable(sb["allocs"], same_process=same)
+            self._pull_imports[s] = imp
+            sphys = PhysBinding.from_json(sb["binding"])
+            ops = [o for o in plan_pair(sphys, self._rphys_abs, names=self._names[s]) if o.kind != "quant"]
+            parts.append(lower_ops(ops, imp.base, lambda a: 0, item_bytes=self.config.item_bytes))
+            if sb["allocs"]:
+                src_ranges += [(imp.base(i), imp.base(i) + int(a["size"])) for i, a in enumerate(sb["allocs"])]
+            else:
+                src_ranges += _phys_extents(sphys)
+        tables = Tables.concat(parts)
+        if self.config.validate_plan:
+            validate_tables(tables, src_ranges, storage_ranges(self.state_dict.values()))
+        if self.device.type == "cpu":
+            self._pull_prog = HostProgram(tables)
+        else:
+            self._pull_prog = TransferProgram(tables, self.device, [], LaunchConfig(mode=self.config.kernel_mode))
+            self._pull_stream = torch.cuda.Stream(self.device)
+        self._pull_versions = dict(versions)
+
+    def launch(self, stream: torch.cuda.Stream | None = None) -> None:
+        """Pull direction: enqueue this worker's pull kernel on ``stream`` with no handshake
+        (for callers that know the senders' memory is stable, e.g. device-timed benchmarks).
+        Needs one completed ``request_update`` (which compiles the pull program)."""
+        prog = getattr(self, "_pull_prog", None)
+        if prog is None:
+            raise RuntimeError("no pull program: the receiver is not in the pull direction or has not synced yet")
+        if len(prog.tables):
+            if prog.device.type == "cpu":
+                prog.launch(0, signal=False)
+            else:
+                prog.launch(0, stream or torch.cuda.current_stream(prog.device), signal=False)
+
+    @property
+    def pull_program(self):
+        return getattr(self, "_pull_prog", None)
 
     # -- NVLink multicast (mode "nvls") -----------------------------------------------------
     def _join_nvls_export(self, binding, info: dict, W: int) -> None:
@@ -502,6 +587,12 @@ class WeightReceiver:
             sess.delete(self._garbage.pop())
 
     def _teardown(self) -> None:
+        for imp in (getattr(self, "_pull_imports", None) or {}).values():
+            try:
+                imp.close()
+            except Exception:
+                pass
+        self._pull_imports = {}
         try:
             self._leave_nvls()
         except Exception:

@@ -123,6 +123,7 @@ class WeightSender:
         self._imports: dict[int, Any] = {}
         self._rinfo: dict[int, dict] = {}
         self._ops_cache: dict[tuple, list] = {}     # plan ops per (receiver, bindings, names)
+        self._bind_version = 0                       # bumped whenever the bound tensors change
 
     # -- collectives on the trainer group (no-ops for a single sender) -------------------
     def _all_gather(self, obj):
@@ -219,6 +220,7 @@ class WeightSender:
         rmeta_objs = {r: WeightData(m) for r, m in receivers.items()}
         plan = assign_sources(smeta_objs, rmeta_objs, cfg.load_balance)
         sess.set_json("senders/meta", metas)
+        sess.set("direction", cfg.direction if cfg.mode == "gpu_direct" else "push")
         sess.set_json("assign", {str(s): {str(r): n for r, n in rs.items()} for s, rs in plan.items()})
         for s, rs in plan.items():
             for r, names in rs.items():
@@ -366,6 +368,10 @@ class WeightSender:
         device = binding.device
         sphys = phys_binding(binding)
         skey = _digest(sphys.to_json())
+        pull = cfg.mode == "gpu_direct" and cfg.direction == "pull"
+        self._bind_version += 1
+        if pull:
+            self._publish_sender_memory(binding, device)
         parts, flags, dst_ranges = [], [], []
         covered: set[int] = set()
         for m, g in (getattr(self, "_mc", {}) or {}).values():
@@ -398,6 +404,8 @@ class WeightSender:
             if ops is None:
                 ops = plan_pair(sphys, rphys, names=names)
                 self._ops_cache[ckey] = ops
+            if pull:                       # receivers load the copies; quantised blocks stay pushed
+                ops = [o for o in ops if o.kind == "quant"]
             parts.append(lower_ops(ops, lambda a: 0, imp.base, item_bytes=cfg.item_bytes))
             falloc, foff, _w = info["flags"]
             flags.append(imp.base(falloc) + foff + 8 * self.rank)
@@ -411,6 +419,9 @@ class WeightSender:
             for f in flags:
                 _check_flag(f, dst_ranges)
         from ..ops.executor import HostProgram, LaunchConfig, TransferProgram
+        if not len(tables):                # pull mode without quantised blocks: nothing to push
+            self._program = None
+            return
         if device.type == "cpu":
             if any(self._rinfo[r].get("device", 0) >= 0 for r in self.targets):
                 raise TransferError("a CPU sender cannot store into GPU receivers; use cpu_direct")
@@ -421,6 +432,19 @@ class WeightSender:
         self._program = TransferProgram(tables, device, flags, lc)
         self._stream = torch.cuda.Stream(device)
         self._ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+
+    def _publish_sender_memory(self, binding, device) -> None:
+        """Pull direction: export this sender's parameter memory for its receivers."""
+        info = {"version": self._bind_version, "pid": os.getpid(), "host": socket.gethostname()}
+        if device.type == "cuda":
+            from ..parallel.ipc import ExportTable
+            export = ExportTable(device)
+            phys = phys_binding(binding, export.locate)        # locates (and exports) every allocation
+            info.update({"allocs": export.to_json(), "binding": phys.to_json()})
+            self._export = export
+        else:                              # host memory: readable only inside this process
+            info.update({"allocs": [], "binding": phys_binding(binding).to_json()})
+        self.session.set_json(f"sendbind/{self.rank}", info)
 
     def _compile_wire(self, state_dict) -> None:
         """Wire modes: pack every target's overlap into one buffer per target (the C++
@@ -561,29 +585,43 @@ class WeightSender:
                 for w in works:
                     w.wait()
             st.bytes_written = sum(w.numel() for w, _t in self._wires.values())
-        elif self.targets and self._program.device.type == "cpu":
-            t2 = time.perf_counter()
-            self._program.launch(epoch)
-            st.device_ms = (time.perf_counter() - t2) * 1e3
-            st.bytes_read, st.bytes_written = self._program.bytes_read, self._program.bytes_written
-            sess.multi_set([f"done/{self.rank}/{r}/{epoch}" for r in self.targets], ["0"] * len(self.targets))
         elif self.targets:
             prog = self._program
-            cur = torch.cuda.current_stream(prog.device)
-            self._stream.wait_stream(cur)
-            e0, e1 = self._ev
-            with nvtx_range("wbridge.send/transfer"):
-                e0.record(self._stream)
-                prog.launch(epoch, self._stream)
-                e1.record(self._stream)
-                e1.synchronize()
-            st.device_ms = e0.elapsed_time(e1)
-            st.status = prog.read_status()
-            st.bytes_read, st.bytes_written = prog.bytes_read, prog.bytes_written
-            sess.multi_set([f"done/{self.rank}/{r}/{epoch}" for r in self.targets], [str(st.status)] * len(self.targets))
+            pushed = prog is not None and len(prog.tables) > 0
+            if pushed and prog.device.type == "cpu":
+                t2 = time.perf_counter()
+                prog.launch(epoch)
+                st.device_ms = (time.perf_counter() - t2) * 1e3
+            elif pushed:
+                cur = torch.cuda.current_stream(prog.device)
+                self._stream.wait_stream(cur)
+                e0, e1 = self._ev
+                with nvtx_range("wbridge.send/transfer"):
+                    e0.record(self._stream)
+                    prog.launch(epoch, self._stream)
+                    e1.record(self._stream)
+                    e1.synchronize()
+                st.device_ms = e0.elapsed_time(e1)
+                st.status = prog.read_status()
+            elif torch.cuda.is_available():
+                torch.cuda.current_stream().synchronize()   # the receivers pull: parameters must be final
+            if prog is not None:
+                st.bytes_read, st.bytes_written = prog.bytes_read, prog.bytes_written
+            done = f"{st.status}:{self._bind_version}:{int(pushed)}"
+            sess.multi_set([f"done/{self.rank}/{r}/{epoch}" for r in self.targets], [done] * len(self.targets))
             if st.status:
                 prog.clear_status()
                 raise TransferError(f"transfer kernel reported status {st.status:#x} at epoch {epoch}")
+            if cfg.mode == "gpu_direct" and cfg.direction == "pull":
+                # parameters stay untouched until every target has pulled its share
+                try:
+                    vals = sess.wait_checked([f"pulled/{r}/{epoch}" for r in self.targets], cfg.sync_timeout_s,
+                                             f"receivers {sorted(self.targets)} to pull epoch {epoch}")
+                except (SessionTimeout, PeerError) as e:
+                    raise TransferError(str(e)) from None
+                bad = {r: int(v) for r, v in zip(sorted(self.targets), vals) if int(v)}
+                if bad:
+                    raise TransferError(f"receivers reported pull status {bad} at epoch {epoch}")
         self.epoch = epoch
         st.host_ms = (time.perf_counter() - t0) * 1e3
         self.history.append(st)

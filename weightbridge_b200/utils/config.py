@@ -44,9 +44,12 @@ class TransferConfig:
     verify_flags: bool = True             # receiver checks every sender's epoch flag
     load_balance: bool = True             # spread replicated shards over senders
     validate_plan: bool = True            # check every work row against registered memory before upload
+    direction: str = "push"               # gpu_direct: push (senders store) | pull (receivers load copies)
 
     def __post_init__(self):
         self.mode = normalize_mode(self.mode)
+        if self.direction not in ("push", "pull"):
+            raise ValueError(f"direction must be 'push' or 'pull', not {self.direction!r}")
 
     @staticmethod
     def from_env(**overrides) -> "TransferConfig":
