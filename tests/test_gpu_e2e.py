@@ -23,3 +23,9 @@ def test_colocated_ipc_reference_style_late_binding():
     """Receiver created with metadata only; tensors handed over at request_update."""
     run("tiny-qwen3", "gpu_direct", [dict(tp=1)], dict(tp=2, tp_rank=1), device="cuda:0",
         dtype=torch.bfloat16, late=True)
+
+
+def test_colocated_ipc_pull_direction():
+    """The receiver maps the senders' memory (CUDA IPC) and runs the pull kernel itself."""
+    run("tiny-llama", "gpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)], dict(tp=1),
+        device="cuda:0", dtype=torch.bfloat16, direction="pull")
