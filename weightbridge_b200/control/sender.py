@@ -63,9 +63,22 @@ class SyncStats:
     bytes_written: int = 0
     receivers: list[int] = field(default_factory=list)
     status: int = 0
+    link_gbs: float = 770.0         # bandwidth the fraction below is taken against
+
+    @property
+    def gbs(self) -> float:
+        """Bytes written per second of device time (GB/s)."""
+        return self.bytes_written / (self.device_ms * 1e6) if self.device_ms > 0 else 0.0
+
+    @property
+    def link_fraction(self) -> float:
+        """Achieved share of the per-GPU link bandwidth ``link_gbs``."""
+        return self.gbs / self.link_gbs if self.link_gbs else 0.0
 
     def to_dict(self) -> dict:
-        return dict(self.__dict__)
+        d = dict(self.__dict__)
+        d["gbs"], d["link_fraction"] = round(self.gbs, 2), round(self.link_fraction, 4)
+        return d
 
 
 _HTTP = None
@@ -541,7 +554,7 @@ class WeightSender:
                         raise TransferError(f"receiver {url} refused the sync: {resp.json()}")
         epoch = self.epoch + 1
         sess = self.session
-        st = SyncStats(epoch=epoch, receivers=sorted(self.targets))
+        st = SyncStats(epoch=epoch, receivers=sorted(self.targets), link_gbs=cfg.link_gbs)
         t1 = time.perf_counter()
         try:
             with nvtx_range("wbridge.send/ready"):

@@ -45,6 +45,7 @@ class TransferConfig:
     load_balance: bool = True             # spread replicated shards over senders
     validate_plan: bool = True            # check every work row against registered memory before upload
     direction: str = "push"               # gpu_direct: push (senders store) | pull (receivers load copies)
+    link_gbs: float = 770.0               # per-GPU link bandwidth for the stats' fraction (measured peer copy)
 
     def __post_init__(self):
         self.mode = normalize_mode(self.mode)
