@@ -226,7 +226,11 @@ class WeightSender:
             counts.append(len(workers))
             base += len(workers)
         world = self.world_size + sum(counts)
-        addr = cfg.master_address if cfg.master_address not in ("", "auto") else local_address()
+        addr = cfg.master_address
+        if addr in ("", "auto"):
+            from urllib.parse import urlparse
+            hosts = {urlparse(u).hostname for u in self.receiver_urls}
+            addr = "127.0.0.1" if hosts <= {"127.0.0.1", "localhost", "::1"} else local_address()
         self.session = Session(addr, cfg.master_port, is_master=True, timeout_s=cfg.connect_timeout_s)
         sess = self.session
         smeta_objs = [WeightData(m) for m in metas]

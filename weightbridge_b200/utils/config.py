@@ -31,7 +31,8 @@ def normalize_mode(mode: str) -> str:
 @dataclass
 class TransferConfig:
     mode: str = "gpu_direct"
-    master_address: str = "127.0.0.1"     # address of the session store (sender rank 0)
+    master_address: str = "auto"          # session store address (sender rank 0); auto: loopback when
+                                          # every receiver URL is local, else this host's address
     master_port: int = 0                  # 0: let the OS pick a free port
     connect_timeout_s: float = 120.0      # rendezvous, metadata exchange, plan agreement
     sync_timeout_s: float = 300.0         # one send()/request_update() round
