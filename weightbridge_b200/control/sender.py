@@ -26,6 +26,7 @@ from __future__ import annotations
 import logging
 import os
 import socket
+import threading
 import time
 import uuid
 from dataclasses import dataclass, field
@@ -181,6 +182,7 @@ class WeightSender:
         mine = assignment.get(str(self.rank), {})
         self.targets = {int(r): names for r, names in mine.items() if names}
         rmetas = {int(k): WeightData(v) for k, v in info["receivers"].items()}
+        self._all_receivers = set(rmetas)
         self.overlaps = {r: WeightData.compute_overlap(restrict(sender_metadata, names), rmetas[r])
                          for r, names in self.targets.items()}
         # receivers publish their memory tables once they joined the store
@@ -530,6 +532,32 @@ class WeightSender:
         """The compiled transfer program (tables, grid, byte counts), once compiled."""
         return self._program
 
+    def _arm(self, epoch: int) -> threading.Thread:
+        """POST ``/wbridge/receive`` to every rollout server from a helper thread.  Only the
+        request reaching the workers is on the critical path (they then report ready through
+        the session); the responses are checked after the ready wait.  A failed arm is written
+        into every receiver's ready key, so all senders stop waiting at once."""
+        self._arm_error = None
+        urls, timeout = list(self.receiver_urls), self.config.http_timeout_s
+        receivers = sorted(self._all_receivers)
+
+        def run():
+            try:
+                http = _http()
+                with nvtx_range("wbridge.send/arm"):
+                    for url in urls:
+                        resp = http.post(f"{url}/wbridge/receive", timeout=timeout)
+                        resp.raise_for_status()
+                        if resp.json().get("status") != "success":
+                            raise TransferError(f"receiver {url} refused the sync: {resp.json()}")
+            except Exception as e:
+                self._arm_error = f"arming the rollout side failed: {type(e).__name__}: {e}"
+                self.session.set_error([f"ready/{r}/{epoch}" for r in receivers], self._arm_error)
+
+        th = threading.Thread(target=run, name="wbridge-arm", daemon=True)
+        th.start()
+        return th
+
     def _fail_epoch(self, epoch: int, message: str) -> None:
         """Tell this epoch's receivers that no data is coming (they stop waiting at once)."""
         if self.session is not None:
@@ -548,16 +576,9 @@ class WeightSender:
             raise RuntimeError("WeightSender.send requires connect() first")
         cfg = self.config
         t0 = time.perf_counter()
-        if self.rank == 0:
-            http = _http()
-            with nvtx_range("wbridge.send/arm"):
-                for url in self.receiver_urls:
-                    resp = http.post(f"{url}/wbridge/receive", timeout=cfg.http_timeout_s)
-                    resp.raise_for_status()
-                    if resp.json().get("status") != "success":
-                        raise TransferError(f"receiver {url} refused the sync: {resp.json()}")
         epoch = self.epoch + 1
         sess = self.session
+        arm = self._arm(epoch) if self.rank == 0 else None
         st = SyncStats(epoch=epoch, receivers=sorted(self.targets), link_gbs=cfg.link_gbs)
         t1 = time.perf_counter()
         try:
@@ -568,6 +589,11 @@ class WeightSender:
             self._fail_epoch(epoch, str(e))
             raise TransferError(str(e)) from None
         st.wait_ready_ms = (time.perf_counter() - t1) * 1e3
+        if arm is not None:
+            arm.join()
+            if self._arm_error is not None:
+                self._fail_epoch(epoch, self._arm_error)
+                raise TransferError(self._arm_error)
         try:
             key = self._key(state_dict)
             if cfg.mode not in WIRE_MODES and self._resolve_late():
