@@ -2,6 +2,7 @@
 worker) and N trainer processes (torch.distributed gloo group), all through the public API.
 Used by the CPU (gloo transport) and GPU (CUDA IPC, colocated on one GPU) tests."""
 import multiprocessing as mp
+import os
 import queue
 import socket
 import time
@@ -15,7 +16,8 @@ def _port():
         return s.getsockname()[1]
 
 
-def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype, late=False, direction="push"):
+def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype, late=False, direction="push",
+                 exit_after=None):
     import threading
     import uvicorn
     from fastapi import FastAPI
@@ -41,6 +43,9 @@ def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype, late=Fal
         q.put(("serving", None, None))
         results = []
         for i in range(n_syncs):
+            if exit_after is not None and i == exit_after:
+                q.put(("rollout-exit", i, None))
+                os._exit(0)           # leave between syncs: nothing of ours is in flight
             ok = recv.request_update(views if late else None, timeout=60)
             exp = lay.allocate(device=device, dtype=dtype, fill=True, seed=i)
             same = all(torch.equal(params[n].view(torch.uint8) if params[n].dtype == torch.float8_e4m3fn else params[n],

@@ -36,3 +36,57 @@ def test_two_gpus_nccl_wire_mode():
     _need(2)
     run("tiny-qwen2", "nccl", [dict(tp=1)], dict(tp=1), device="cuda:1", dtype=torch.bfloat16,
         trainer_devices=["cuda:0"])
+
+
+def _leaving_trainer(tport, url, q):
+    import torch.distributed as dist
+    from weightbridge_b200 import TransferConfig, WeightSender
+    from weightbridge_b200.control.sender import TransferError
+    from weightbridge_b200.models.arch import get_arch
+    from weightbridge_b200.parallel.megatron import MegatronLayout
+    torch.cuda.set_device(0)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{tport}", rank=0, world_size=1)
+    lay = MegatronLayout(get_arch("tiny-llama"), tp=1)
+    params = lay.allocate(device="cuda:0", dtype=torch.bfloat16)
+    meta, views = lay.to_wb(params)
+    cfg = TransferConfig(mode="gpu_direct", connect_timeout_s=60, sync_timeout_s=5, http_timeout_s=5)
+    s = WeightSender("gpu_direct", [url], config=cfg)
+    s.connect(meta)
+    s.send(views)
+    q.put(("first-sync", True, None))
+    import time
+    t0 = time.time()
+    try:
+        s.send(views)
+        q.put(("second-sync", "no error", time.time() - t0))
+    except (TransferError, Exception) as e:
+        q.put(("second-sync", type(e).__name__, time.time() - t0))
+
+
+def test_receiver_leaving_between_syncs_fails_the_next_send():
+    """A rollout process exits between two syncs (nothing in flight); the trainer's next send
+    reports an error within its deadline instead of hanging, and launches no kernel into the
+    departed receiver's memory (the launch waits for the receiver's ready key)."""
+    import multiprocessing as mp
+    import os
+    _need(2)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from tests.e2e_harness import _port, rollout_proc
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    hport, tport = _port(), _port()
+    roll = ctx.Process(target=rollout_proc, args=(hport, q, 2, "tiny-llama", "gpu_direct", "cuda:1", dict(tp=1),
+                                                  torch.bfloat16, False, "push", 1))
+    roll.start()
+    assert q.get(timeout=120)[0] == "serving"
+    tr = ctx.Process(target=_leaving_trainer, args=(tport, f"http://127.0.0.1:{hport}", q))
+    tr.start()
+    got = {}
+    for _ in range(3):
+        k, v, t = q.get(timeout=120)
+        got[k] = (v, t)
+    tr.join(30)
+    roll.join(30)
+    assert got["first-sync"][0] is True
+    assert got["second-sync"][0] != "no error"
+    assert got["second-sync"][1] < 30

@@ -19,15 +19,15 @@ def __getattr__(name):
     if name == "MegatronLayout":
         from .parallel.megatron import MegatronLayout
         return MegatronLayout
-    if name == "SGLangLayout":
-        from .parallel.sglang import SGLangLayout
-        return SGLangLayout
+    if name in ("SGLangLayout", "VLLMLayout"):
+        from .parallel import sglang
+        return getattr(sglang, name)
     raise AttributeError(name)
 
 
 __all__ = [
     "WeightData", "WeightSender", "WeightReceiver", "WeightReceiverController", "TransferConfig",
     "check_shard_compatibility", "shards_iterator", "original_total_numel", "dtype_str_to_torch",
-    "dtype_to_str", "MegatronLayout", "SGLangLayout",
+    "dtype_to_str", "MegatronLayout", "SGLangLayout", "VLLMLayout",
 ]
 __version__ = "0.1.0"

@@ -363,3 +363,10 @@ def convert_to_wb_and_views(model_config: Any, state_dict, tp_rank, tp_size, att
     layout = SGLangLayout(arch, tp=tp_size, tp_rank=tp_rank, attn_tp=attn_tp_size,
                           attn_tp_rank=attn_tp_rank, moe_ep=moe_ep, quant=quant)
     return layout.to_wb(state_dict)
+
+
+# vLLM keeps the same fused parameter layout for these families (QKVParallelLinear
+# ``[q; k; v]``, MergedColumnParallelLinear ``[gate; up]``, VocabParallelEmbedding padded to a
+# multiple of 64, FusedMoE ``w13_weight`` / ``w2_weight``, block-fp8 ``*_weight_scale_inv``),
+# so a vLLM rollout binds its parameters with the same layout class.
+VLLMLayout = SGLangLayout
