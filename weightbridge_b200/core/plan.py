@@ -286,6 +286,9 @@ def _split_rows(src, dst, sp, dp, row_bytes, rows, op, drb, item_bytes, out: lis
 def lower_ops(ops: Sequence[Op], src_base: Callable[[int], int], dst_base: Callable[[int], int],
               item_bytes: int = DEFAULT_ITEM_BYTES, multicast: bool = False) -> Tables:
     """Resolve allocation indices to addresses and cut ops into device work rows."""
+    if item_bytes < 16:
+        raise ValueError("item_bytes must be at least 16")
+    item_bytes = min(int(item_bytes), 1 << 30)      # row_bytes / rows are 32-bit in the work rows
     items: list[tuple] = []
     qdescs: list[tuple] = []
     qwork: list[np.ndarray] = []
