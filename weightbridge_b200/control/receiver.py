@@ -118,7 +118,10 @@ class WeightReceiver:
         """Receive the pending weights into the bound state_dict.
 
         Returns False when no sync is pending (the controller has not armed this worker);
-        with ``timeout`` the call first waits up to that many seconds for the arm.
+        with ``timeout`` the call first waits up to that many seconds for the arm.  A sync
+        that started and then failed (a sender's error, a stale flag, a deadline) raises
+        ``ReceiveError`` instead of returning False: the parameters may hold a mix of old and
+        new values, which the caller must not mistake for "no update".
         """
         if state_dict is not None and state_dict is not self.state_dict:
             if getattr(self, "_bound", False):
