@@ -141,6 +141,28 @@ def scenario(config: str, n: int) -> tuple[str, list[Role], str]:
     raise SystemExit(f"unknown config {config}")
 
 
+def _measured_peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def _roofline(value_gbs: float, links: float, colocated: bool, bytes_read: float, payload: float, ms: float) -> dict:
+    """Achieved fraction of the resource that bounds the sync: HBM copy bandwidth when every
+    transfer stays on one GPU (reads + writes), else NVLink per active link (measured peer copy)."""
+    if colocated and links <= 1:
+        peak = float(_measured_peaks().get("hbm_gbs", 6650.0))
+        achieved = (bytes_read + payload) / (ms / 1e3) / 1e9
+        return {"bound": "hbm copy (read + write)", "peak_gbs": peak, "achieved_gbs": round(achieved, 1),
+                "fraction_of_measured": round(achieved / peak, 3)}
+    peak = 770.0
+    per_link = value_gbs / max(links, 1.0)
+    return {"bound": "nvlink, per sending link", "peak_gbs": peak, "achieved_gbs": round(per_link, 1),
+            "fraction_of_measured": round(per_link / peak, 3)}
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -380,6 +402,8 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                        "rollout_params": "separate allocations" if args.no_pool else "one pooled allocation per rank",
                        "transfer": args.transfer, "direction": args.direction},
             "latency_s": round(lat, 6),
+            "roofline": _roofline(value, float(G[:, 7].sum()), colocated=len({r.device for r in roles}) < len(roles),
+                                  bytes_read=float(G[:, 3].sum()), payload=payload_total, ms=ms),
             "gbs_per_gpu": round(value / ngpu, 2),
             "gbs_per_sender": round(value / max(1.0, float(G[:, 7].sum())), 2),
             "e2e": None if args.no_e2e else {
