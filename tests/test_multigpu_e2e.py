@@ -82,11 +82,15 @@ def test_receiver_leaving_between_syncs_fails_the_next_send():
     tr = ctx.Process(target=_leaving_trainer, args=(tport, f"http://127.0.0.1:{hport}", q))
     tr.start()
     got = {}
-    for _ in range(3):
-        k, v, t = q.get(timeout=120)
-        got[k] = (v, t)
-    tr.join(30)
-    roll.join(30)
+    try:
+        for _ in range(3):
+            k, v, t = q.get(timeout=120)
+            got[k] = (v, t)
+    finally:
+        for p in (tr, roll):
+            p.join(30)
+            if p.is_alive():
+                p.kill()
     assert got["first-sync"][0] is True
     assert got["second-sync"][0] != "no error"
     assert got["second-sync"][1] < 30
