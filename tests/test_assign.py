@@ -1,0 +1,79 @@
+"""Source assignment: replica groups, overlap rules and load balancing."""
+import pytest
+import torch
+
+from weightbridge_b200 import WeightData
+from weightbridge_b200.control.assign import assign_sources, expected_senders, replica_groups
+from weightbridge_b200.core.shard import box_copy
+from weightbridge_b200.models.arch import get_arch
+from weightbridge_b200.parallel.megatron import MegatronLayout
+from weightbridge_b200.parallel.sglang import SGLangLayout
+
+
+def _meta(lay, param_specs):
+    params = {n: torch.empty(s, dtype=torch.bfloat16, device="meta") for n, s in param_specs.items()}
+    return lay.to_wb(params)[0]
+
+
+def _bytes(plan, smetas, rmetas):
+    out = {}
+    for s, rs in plan.items():
+        n = 0
+        for r, names in rs.items():
+            for name in names:
+                for a in smetas[s].shards(name):
+                    for b in rmetas[r].shards(name):
+                        bc = box_copy(a, b)
+                        if bc is not None:
+                            n += bc.numel * 2
+        out[s] = n
+    return out
+
+
+def test_ep4_to_tp4_dense_weights_spread_over_senders():
+    arch = get_arch("qwen3-30b-a3b").with_(num_layers=4)
+    smetas = []
+    for r in range(4):
+        lay = MegatronLayout(arch, ep=4, ep_rank=r)
+        smetas.append(_meta(lay, lay.param_shapes()))
+    rmetas = {}
+    for r in range(4):
+        lay = SGLangLayout(arch, tp=4, tp_rank=r, moe_ep=4)
+        rmetas[4 + r] = _meta(lay, {n: s for n, (s, _k) in lay.param_specs().items()})
+    plan = assign_sources(smetas, rmetas)
+    loads = _bytes(plan, smetas, rmetas)
+    assert len(loads) == 4
+    assert max(loads.values()) / min(loads.values()) < 1.05, loads
+    # experts come only from their EP owner
+    for s, rs in plan.items():
+        for r, names in rs.items():
+            for n in names:
+                if ".experts." in n:
+                    e = int(n.split(".experts.")[1].split(".")[0])
+                    assert e // 32 == s
+    # lowest-rank-wins is available for comparison
+    low = assign_sources(smetas, rmetas, load_balance=False)
+    assert max(_bytes(low, smetas, rmetas).values()) > max(loads.values())
+
+
+def test_partial_overlap_between_senders_raises():
+    a = WeightData({"w": {"shard": [(0, 3, 4), (0, 4, 4)], "dtype": "float32"}})
+    b = WeightData({"w": {"shard": [(2, 4, 4), (0, 4, 4)], "dtype": "float32"}})
+    r = WeightData({"w": {"shard": [(0, 4, 4), (0, 4, 4)], "dtype": "float32"}})
+    with pytest.raises(ValueError, match="Partial shard overlap"):
+        assign_sources([a, b], {2: r})
+
+
+def test_replicas_and_expected_senders():
+    full = {"w": {"shard": [(0, 4, 4), (0, 4, 4)], "dtype": "float32"}}
+    halves = [WeightData({"v": {"shard": [(0, 2, 4)], "dtype": "float32"}, **full}),
+              WeightData({"v": {"shard": [(2, 4, 4)], "dtype": "float32"}, **full})]
+    groups = replica_groups(halves)
+    assert groups["w"] == [[0, 1]] and groups["v"] == [[0], [1]]
+    recv = {2: WeightData({"w": full["w"], "v": {"shard": [(0, 4, 4)], "dtype": "float32"}}),
+            3: WeightData({"w": full["w"]})}
+    plan = assign_sources(halves, recv)
+    # receiver 2 needs both halves of v: both senders; w goes to one of them each
+    assert expected_senders(plan, 2) == [0, 1]
+    w_senders = [s for s in plan for r in plan[s] for n in plan[s][r] if n == "w"]
+    assert sorted(w_senders) == [0, 1]      # the two copies of w spread over the two replicas

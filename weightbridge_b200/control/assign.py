@@ -2,9 +2,10 @@
 
 Senders whose shards of an entry are identical are replicas (trainer DP, or the dense part
 of an EP-only layout); shards of different replica groups must not overlap.  For every
-receiver entry and every replica group that overlaps it, one member of the group is chosen:
-the least loaded one by bytes assigned so far (ties: lowest rank), so replicated weights
-spread over every sender's NVLink egress.
+receiver entry and every replica group that overlaps it, one member of the group sends it.
+Entries a single sender holds are fixed; replicated entries are then placed largest first on
+the least-loaded member (ties: lowest rank), so every sender's NVLink egress carries about
+the same bytes and the slowest link, which sets the sync time, is as short as possible.
 
 Parity: the reference deduplicates identical shards by keeping the lowest rank and raises
 on partial overlap (``wbridge/backend/direct_sender.py:31-71``); the overlap rule is the
@@ -63,10 +64,16 @@ def _overlap_bytes(s_shards, r_shards, itemsize: int) -> int:
 
 def assign_sources(sender_metas: list[WeightData], receiver_metas: dict[int, WeightData],
                    load_balance: bool = True) -> dict[int, dict[int, list[str]]]:
-    """``plan[sender][receiver] = [entry names]`` (both as indices into the inputs)."""
+    """``plan[sender][receiver] = [entry names]`` (both as indices into the inputs).
+
+    Two passes: entries only one replica group can serve are assigned first (their load is
+    fixed), then replicated entries, largest first, each to the least-loaded member of its
+    group (longest-processing-time greedy), so every sender ends with about the same bytes.
+    """
     groups = replica_groups(sender_metas)
     load = [0] * len(sender_metas)
     plan: dict[int, dict[int, list[str]]] = defaultdict(lambda: defaultdict(list))
+    flexible: list[tuple[int, int, str, list[int]]] = []      # (bytes, receiver, name, group)
     for r in sorted(receiver_metas):
         rmeta = receiver_metas[r]
         for name, r_shards, r_dtype in rmeta:
@@ -78,12 +85,22 @@ def assign_sources(sender_metas: list[WeightData], receiver_metas: dict[int, Wei
                 nbytes = _overlap_bytes(s_shards, r_shards, r_dtype.itemsize)
                 if nbytes == 0:
                     continue
-                if load_balance:
-                    s = min(group, key=lambda x: (load[x], x))
-                else:
+                if len(group) == 1 or not load_balance:
                     s = min(group)
-                load[s] += nbytes
-                plan[s][r].append(name)
+                    load[s] += nbytes
+                    plan[s][r].append(name)
+                else:
+                    flexible.append((nbytes, r, name, group))
+    flexible.sort(key=lambda t: (-t[0], t[1], t[2]))
+    for nbytes, r, name, group in flexible:
+        s = min(group, key=lambda x: (load[x], x))
+        load[s] += nbytes
+        plan[s][r].append(name)
+    # keep each receiver's names in its metadata order (deterministic, cache friendly)
+    order = {r: {n: i for i, n in enumerate(m.names())} for r, m in receiver_metas.items()}
+    for s in plan:
+        for r in plan[s]:
+            plan[s][r].sort(key=lambda n: order[r][n])
     return {s: dict(v) for s, v in plan.items()}
 
 
