@@ -294,9 +294,10 @@ class WeightSender:
             for gid, reps in enumerate(replica_groups(allinfo)):
                 senders = [s for s, rs in plan.items()
                            if all(r in rs for r in reps) and all(rs[r] == rs[reps[0]] for r in reps)]
-                devs = {allinfo[r]["device"] for r in reps} | {self._sender_devices[s] for s in senders}
-                if not senders or not nvls_supported(dev0):
-                    continue
+                members = [allinfo[r]["device"] for r in reps] + [self._sender_devices[s] for s in senders]
+                devs = set(members)
+                if not senders or not nvls_supported(dev0) or len(devs) != len(members):
+                    continue        # unicast: no senders, no NVLS, or two members on one GPU
                 size = int(allinfo[reps[0]]["pool"]["size"])
                 m = McMember(gid, size, dev0)
                 m.create(num_devices=len(devs))
