@@ -36,7 +36,7 @@ from dataclasses import dataclass, field
 ROOT = os.path.dirname(os.path.abspath(__file__))
 
 METRIC = "full weight-sync latency (s, device-timed, max over ranks) + effective GB/s/GPU"
-BASELINE_PUBLISHED = None   # the reference publishes no number
+BASELINE_PUBLISHED = None   # the reference publishes no throughput or latency number
 
 
 def parse(argv=None):
