@@ -374,8 +374,10 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     items = len(sender.program.tables.items) if (sender is not None and sender.program is not None) else 0
     grid = sender.program.grid() if (sender is not None and sender.program is not None) else 0
     kmode = sender.program.config.mode if (sender is not None and sender.program is not None) else -1
-    stats = torch.tensor([my_ms, e2e_ms, payload, read, ok, h2d, d2h, active, items, grid, setup_s, kmode],
-                         dtype=torch.float64)
+    hist = sender.history[-args.steps:] if (sender is not None and not args.no_e2e) else []
+    avg = lambda f: sum(getattr(h, f) for h in hist) / len(hist) if hist else 0.0
+    stats = torch.tensor([my_ms, e2e_ms, payload, read, ok, h2d, d2h, active, items, grid, setup_s, kmode,
+                          avg("wait_ready_ms"), avg("device_ms"), avg("host_ms")], dtype=torch.float64)
     gathered = [torch.zeros_like(stats) for _ in range(nprocs)]
     dist.all_gather(gathered, stats)
     G = torch.stack(gathered)
@@ -410,7 +412,10 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                 "value": round(payload_total / (e2e / 1e3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e, 4), "latency_s": round(e2e / 1e3, 6),
                 "h2d_bytes_per_step": int(G[:, 5].sum()), "d2h_bytes_per_step": int(G[:, 6].sum()),
-                "path": "WeightSender.send + WeightReceiver.request_update (HTTP arm, store handshake, IPC peer stores)"},
+                "path": "WeightSender.send + WeightReceiver.request_update (HTTP arm, store handshake, IPC peer stores)",
+                "sender_breakdown_ms": {"wait_ready": round(float(G[:, 12].max()), 3),
+                                        "transfer_kernel": round(float(G[:, 13].max()), 3),
+                                        "send_total": round(float(G[:, 14].max()), 3)}},
             "gpu_launches": int(args.steps * G[:, 7].sum()),
             "clocks": clk.summary() if clk else None,
             "verified": bool(G[:, 4].min() == 1) if not args.no_verify else None,
