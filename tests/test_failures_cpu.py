@@ -320,3 +320,55 @@ def test_pull_direction_with_pushed_fp8_blocks():
         recv.stop()
         server.should_exit = True
         ctl.close()
+
+
+@pytest.mark.parametrize("arm", ["direct", "http"])
+@pytest.mark.parametrize("mode", ["cpu_direct", "gpu_direct"])
+def test_both_arm_channels_sync(mode, arm):
+    """A sync is armed either by one ZMQ message per worker (default) or by the reference's
+    POST /wbridge/receive; both land the same weights and the controller sees the epochs."""
+    cfg = _cfg(mode=mode, arm=arm)
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender(mode, [ro.url], config=cfg)
+        s.connect(meta)
+        assert (s._arm_sock is not None) == (arm == "direct")
+        for step in range(3):
+            lay.fill(params, seed=step)
+            th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+            th.start()
+            st = s.send(views)
+            th.join(20)
+            assert st.epoch == step + 1
+            exp = ro.lay.allocate(dtype=torch.float32, fill=True, seed=step)
+            assert all(torch.equal(ro.params[n], exp[n]) for n in exp), step
+        assert ro.ctl.get_stats()[0]["epoch"] == 3
+        # a repeated arm of the pending epoch is harmless
+        if arm == "direct":
+            s._arm(4)
+            s._arm(4)
+            time.sleep(0.2)
+            assert ro.recv.state.value == "awaiting_scheduler_update"
+    finally:
+        ro.close()
+
+
+def test_direct_arm_to_a_stopped_worker_fails_fast():
+    """The worker's process side is gone (its sockets closed): the arm is unroutable and the
+    sync fails at once instead of waiting for the ready deadline."""
+    cfg = _cfg(mode="gpu_direct", sync_timeout_s=20.0)
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender("gpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        ro.recv.stop()
+        ro.recv = None
+        time.sleep(0.5)              # the sender's connection sees the peer close
+        t0 = time.time()
+        with pytest.raises(TransferError, match="unreachable"):
+            s.send(views)
+        assert time.time() - t0 < 5
+    finally:
+        ro.close()

@@ -1,9 +1,10 @@
 """Rollout-side receiver worker (one per rollout GPU / scheduler process).
 
-A daemon thread serves two ZMQ sockets: a DEALER to the controller (metadata, connect,
-receive, stats) and a REP for the scheduler's ``request_update``.  State machine:
+A daemon thread serves three ZMQ sockets: a DEALER to the controller (metadata, connect,
+receive, stats), a REP for the scheduler's ``request_update`` and, while in a session, a
+DEALER bound on TCP through which the first sender arms each sync directly.  State machine:
 DISCONNECTED -> CONNECTED (after joining a session) -> AWAITING_SCHEDULER_UPDATE (armed by
-``/wbridge/receive``) -> CONNECTED (after the update).
+``/wbridge/receive`` or by the direct arm message) -> CONNECTED (after the update).
 
 On connect (``gpu_direct``) the worker exports the allocations holding its parameters as
 CUDA IPC handles, publishes them with the physical binding of every entry and a flag word
@@ -70,6 +71,8 @@ class WeightReceiver:
         self.session: Session | None = None
         self._pending_update: dict | None = None
         self._garbage: list[str] = []
+        self._arm_sock = None
+        self._poller: zmq.Poller | None = None
         fd, path = tempfile.mkstemp(prefix=f"wbridge_sched_{rank}_")
         os.close(fd)
         os.unlink(path)
@@ -178,6 +181,7 @@ class WeightReceiver:
         poller = zmq.Poller()
         poller.register(ctl, zmq.POLLIN)
         poller.register(rep, zmq.POLLIN)
+        self._poller = poller
         if self.device.type == "cuda":
             torch.cuda.set_device(self.device)
         self._started.set()
@@ -187,6 +191,9 @@ class WeightReceiver:
                 if ctl in socks:
                     data = json.loads(ctl.recv_string())
                     self._on_controller(ctl, data)
+                arm = self._arm_sock
+                if arm is not None and arm in socks:
+                    self._on_arm(json.loads(arm.recv_string()))
                 if rep in socks:
                     msg = json.loads(rep.recv_string())
                     self._on_scheduler(rep, msg)
@@ -239,6 +246,42 @@ class WeightReceiver:
             self._stop.set()
         else:
             self._reply(sock, data, {"status": "error", "detail": f"unknown message type {t!r}"})
+
+    def _on_arm(self, msg: dict) -> None:
+        """A sender armed sync ``epoch`` directly (same transition as ``/wbridge/receive``).
+        A worker that cannot take it writes the reason into its ready key, where every
+        sender of the session is waiting."""
+        if "epoch" not in msg or self.session is None:
+            return                                   # connection probe
+        epoch = int(msg["epoch"])
+        ok_states = (ReceiverState.CONNECTED, ReceiverState.AWAITING_SCHEDULER_UPDATE)   # re-arm: no-op
+        if self._state in ok_states and epoch == self.epoch + 1:
+            self._state = ReceiverState.AWAITING_SCHEDULER_UPDATE
+            return
+        why = (f"receiver {self.global_rank} cannot take sync {epoch}: state {self._state.value}, "
+               f"last epoch {self.epoch}")
+        self.session.set_error([f"ready/{self.global_rank}/{epoch}"], why)
+
+    def _open_arm_socket(self, master_address: str) -> str:
+        """Bind the direct-arm DEALER on an OS-chosen TCP port; returns its endpoint."""
+        from .session import local_address
+        loopback = master_address in ("127.0.0.1", "localhost", "::1")
+        sock = self._ctx.socket(zmq.DEALER)
+        sock.setsockopt(zmq.LINGER, 0)
+        sock.setsockopt(zmq.IDENTITY, f"wbarm-{self.global_rank}".encode())
+        port = sock.bind_to_random_port("tcp://127.0.0.1" if loopback else "tcp://*")
+        self._arm_sock = sock
+        self._poller.register(sock, zmq.POLLIN)
+        return f"tcp://{'127.0.0.1' if loopback else local_address()}:{port}"
+
+    def _close_arm_socket(self) -> None:
+        sock, self._arm_sock = self._arm_sock, None
+        if sock is not None:
+            try:
+                self._poller.unregister(sock)
+            except KeyError:
+                pass
+            sock.close(0)
 
     def _on_scheduler(self, sock, msg: dict) -> None:
         if msg.get("type") != UPDATE_REQUEST:
@@ -293,7 +336,7 @@ class WeightReceiver:
                        timeout_s=self.config.connect_timeout_s)
         self.session = sess
         info: dict[str, Any] = {"rank": gr, "worker": self.rank, "pid": os.getpid(), "host": socket.gethostname(),
-                                "mode": mode}
+                                "mode": mode, "arm": self._open_arm_socket(data["master_address"])}
         self._W = W
         self._bound = False
         if self.state_dict is not None:
@@ -590,6 +633,7 @@ class WeightReceiver:
             sess.delete(self._garbage.pop())
 
     def _teardown(self) -> None:
+        self._close_arm_socket()
         for imp in (getattr(self, "_pull_imports", None) or {}).values():
             try:
                 imp.close()

@@ -138,6 +138,9 @@ class WeightSender:
         self._rinfo: dict[int, dict] = {}
         self._ops_cache: dict[tuple, list] = {}     # plan ops per (receiver, bindings, names)
         self._bind_version = 0                       # bumped whenever the bound tensors change
+        self._arm_sock = None                        # rank 0, arm="direct": ROUTER to every receiver worker
+        self._arm_idents: dict[int, bytes] = {}
+        self._arm_error: str | None = None
 
     # -- collectives on the trainer group (no-ops for a single sender) -------------------
     def _all_gather(self, obj):
@@ -257,8 +260,50 @@ class WeightSender:
             if resp.json().get("status") != "success":
                 return {"error": f"receiver {url} refused connect: {resp.json()}"}
             base += count
+        if cfg.arm == "direct":
+            self._open_arm_channel(sorted(receivers))
         return {"address": addr, "port": sess.port, "world_size": world,
                 "receivers": {str(r): m for r, m in receivers.items()}, "session": session_id}
+
+    def _open_arm_channel(self, receivers: list[int]) -> None:
+        """``arm="direct"``: connect one ROUTER to every receiver worker's arm socket (their
+        endpoints are in the session) and wait until each connection is up, so that a later
+        arm either reaches the worker or fails at once (``ROUTER_MANDATORY``: a worker whose
+        process is gone is unroutable) instead of queueing."""
+        import zmq
+        cfg = self.config
+        self._close_arm_channel()
+        sock = zmq.Context.instance().socket(zmq.ROUTER)
+        sock.setsockopt(zmq.LINGER, 0)
+        sock.setsockopt(zmq.ROUTER_MANDATORY, 1)
+        sock.setsockopt(zmq.IMMEDIATE, 1)          # a route exists only while its connection is up
+        try:
+            idents = {}
+            for r in receivers:
+                info = self.session.get_json(f"recv/{r}", cfg.connect_timeout_s)
+                sock.connect(info["arm"])
+                idents[r] = f"wbarm-{r}".encode()
+            pending, deadline = set(receivers), time.monotonic() + cfg.connect_timeout_s
+            while pending:
+                for r in sorted(pending):
+                    try:
+                        sock.send_multipart([idents[r], b"{}"], zmq.NOBLOCK)     # probe, ignored by the worker
+                        pending.discard(r)
+                    except zmq.ZMQError:
+                        pass
+                if pending and time.monotonic() > deadline:
+                    raise TransferError(f"receivers {sorted(pending)} unreachable on their arm sockets")
+                if pending:
+                    time.sleep(0.002)
+        except BaseException:
+            sock.close(0)
+            raise
+        self._arm_sock, self._arm_idents = sock, idents
+
+    def _close_arm_channel(self) -> None:
+        sock, self._arm_sock, self._arm_idents = self._arm_sock, None, {}
+        if sock is not None:
+            sock.close(0)
 
     def _open_receivers(self) -> None:
         from ..parallel.ipc import ImportTable
@@ -370,6 +415,7 @@ class WeightSender:
         self.connect(self.metadata)
 
     def disconnect(self) -> None:
+        self._close_arm_channel()
         self._teardown_multicast()
         for imp in self._imports.values():
             imp.close()
@@ -533,14 +579,30 @@ class WeightSender:
         """The compiled transfer program (tables, grid, byte counts), once compiled."""
         return self._program
 
-    def _arm(self, epoch: int) -> threading.Thread:
-        """POST ``/wbridge/receive`` to every rollout server from a helper thread.  Only the
-        request reaching the workers is on the critical path (they then report ready through
-        the session); the responses are checked after the ready wait.  A failed arm is written
-        into every receiver's ready key, so all senders stop waiting at once."""
+    def _arm(self, epoch: int) -> threading.Thread | None:
+        """Arm sync ``epoch`` on every receiver worker (rank 0 only).  A failed arm is written
+        into every receiver's ready key, so all senders stop waiting at once.
+
+        ``arm="direct"``: one ZMQ message per worker on the connections opened at connect; a
+        worker that cannot take the sync writes why into its own ready key.
+        ``arm="http"`` (the reference's protocol): POST ``/wbridge/receive`` to every rollout
+        server from a helper thread.  Only the request reaching the workers is on the critical
+        path (they then report ready through the session); the responses are checked after
+        the ready wait."""
         self._arm_error = None
-        urls, timeout = list(self.receiver_urls), self.config.http_timeout_s
         receivers = sorted(self._all_receivers)
+        if self._arm_sock is not None:
+            import zmq
+            payload = f'{{"epoch":{epoch}}}'.encode()
+            for r, ident in self._arm_idents.items():
+                try:
+                    self._arm_sock.send_multipart([ident, payload], zmq.NOBLOCK)
+                except zmq.ZMQError as e:
+                    self._arm_error = f"arming the rollout side failed: receiver {r} unreachable ({e})"
+                    self.session.set_error([f"ready/{x}/{epoch}" for x in receivers], self._arm_error)
+                    break
+            return None
+        urls, timeout = list(self.receiver_urls), self.config.http_timeout_s
 
         def run():
             try:
@@ -592,9 +654,9 @@ class WeightSender:
         st.wait_ready_ms = (time.perf_counter() - t1) * 1e3
         if arm is not None:
             arm.join()
-            if self._arm_error is not None:
-                self._fail_epoch(epoch, self._arm_error)
-                raise TransferError(self._arm_error)
+        if self.rank == 0 and self._arm_error is not None:
+            self._fail_epoch(epoch, self._arm_error)
+            raise TransferError(self._arm_error)
         try:
             key = self._key(state_dict)
             if cfg.mode not in WIRE_MODES and self._resolve_late():

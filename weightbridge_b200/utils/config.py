@@ -47,11 +47,15 @@ class TransferConfig:
     validate_plan: bool = True            # check every work row against registered memory before upload
     direction: str = "push"               # gpu_direct: push (senders store) | pull (receivers load copies)
     link_gbs: float = 770.0               # per-GPU link bandwidth for the stats' fraction (measured peer copy)
+    arm: str = "direct"                   # how each sync is armed: direct (one ZMQ message from sender rank 0
+                                          # to every receiver worker) | http (POST /wbridge/receive per sync)
 
     def __post_init__(self):
         self.mode = normalize_mode(self.mode)
         if self.direction not in ("push", "pull"):
             raise ValueError(f"direction must be 'push' or 'pull', not {self.direction!r}")
+        if self.arm not in ("direct", "http"):
+            raise ValueError(f"arm must be 'direct' or 'http', not {self.arm!r}")
 
     @staticmethod
     def from_env(**overrides) -> "TransferConfig":
