@@ -43,7 +43,7 @@ from ..utils.trace import nvtx_range
 from .assign import expected_senders, restrict
 from .protocol import (CONNECT_REQUEST, METADATA_REQUEST, RECEIVE_REQUEST, STATS_REQUEST, STOP_REQUEST,
                        UPDATE_REQUEST, ReceiverState, b64)
-from .session import PeerError, Session, SessionTimeout
+from .session import Janitor, PeerError, Session, SessionTimeout
 
 logger = logging.getLogger(__name__)
 
@@ -73,6 +73,7 @@ class WeightReceiver:
         self._garbage: list[str] = []
         self._arm_sock = None
         self._poller: zmq.Poller | None = None
+        self._janitor: Janitor | None = None
         fd, path = tempfile.mkstemp(prefix=f"wbridge_sched_{rank}_")
         os.close(fd)
         os.unlink(path)
@@ -335,6 +336,7 @@ class WeightReceiver:
         sess = Session(data["master_address"], int(data["master_port"]), is_master=False,
                        timeout_s=self.config.connect_timeout_s)
         self.session = sess
+        self._janitor = Janitor(data["master_address"], int(data["master_port"]), self.config.connect_timeout_s)
         info: dict[str, Any] = {"rank": gr, "worker": self.rank, "pid": os.getpid(), "host": socket.gethostname(),
                                 "mode": mode, "arm": self._open_arm_socket(data["master_address"])}
         self._W = W
@@ -628,12 +630,15 @@ class WeightReceiver:
             self._mc = None
 
     def _collect_garbage(self) -> None:
-        sess = self.session
-        while self._garbage and sess is not None:
-            sess.delete(self._garbage.pop())
+        if self._garbage and self._janitor is not None:
+            self._janitor.delete(self._garbage)
+        self._garbage = []
 
     def _teardown(self) -> None:
         self._close_arm_socket()
+        if self._janitor is not None:
+            self._janitor.close()
+            self._janitor = None
         for imp in (getattr(self, "_pull_imports", None) or {}).values():
             try:
                 imp.close()

@@ -38,7 +38,9 @@ class Session:
                                   wait_for_workers=False)
         self.port = self._tcp.port
         self.host = host
+        self.prefix = prefix
         self.store = dist.PrefixStore(prefix, self._tcp)
+        self._cur_timeout = timeout_s
 
     def set(self, key: str, value: bytes | str) -> None:
         self.store.set(key, value)
@@ -85,8 +87,14 @@ class Session:
         keys = list(keys)
         if not keys:
             return []
-        self.wait(keys, timeout_s, what)
-        vals = self.store.multi_get(keys) if len(keys) > 1 else [self.store.get(keys[0])]
+        t = timeout_s if timeout_s is not None else self.timeout_s
+        if t != self._cur_timeout:          # multi_get blocks until every key exists, up to this
+            self.store.set_timeout(timedelta(seconds=t))
+            self._cur_timeout = t
+        try:
+            vals = self.store.multi_get(keys)   # one round trip: wait and read
+        except Exception as e:
+            raise SessionTimeout(f"timed out after {t:.1f}s waiting for {what or keys[:4]}: {e}") from None
         for k, v in zip(keys, vals):
             if v.startswith(ERROR_PREFIX):
                 raise PeerError(v[len(ERROR_PREFIX):].decode(errors="replace"))
@@ -115,6 +123,42 @@ class Session:
             self.store.delete_key(key)
         except Exception:
             pass
+
+
+class Janitor:
+    """Deletes finished handshake keys from a thread of its own, over its own store client, so
+    the deletes (one round trip each) stay off the next sync's critical path."""
+
+    def __init__(self, host: str, port: int, timeout_s: float, prefix: str = "wbridge"):
+        import queue
+        import threading
+        self._args = (host, port, timeout_s, prefix)
+        self._q: "queue.SimpleQueue[list[str] | None]" = queue.SimpleQueue()
+        self._thread = threading.Thread(target=self._run, name="wbridge-janitor", daemon=True)
+        self._thread.start()
+
+    def delete(self, keys: list[str]) -> None:
+        if keys:
+            self._q.put(list(keys))
+
+    def _run(self) -> None:
+        sess = None
+        while True:
+            keys = self._q.get()
+            if keys is None:
+                return
+            try:
+                if sess is None:
+                    host, port, timeout_s, prefix = self._args
+                    sess = Session(host, port, is_master=False, timeout_s=timeout_s, prefix=prefix)
+                for k in keys:
+                    sess.delete(k)
+            except Exception:
+                pass             # the session is gone: nothing left to clean
+
+    def close(self, timeout_s: float = 2.0) -> None:
+        self._q.put(None)
+        self._thread.join(timeout_s)
 
 
 def free_port() -> int:
