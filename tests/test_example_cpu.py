@@ -1,4 +1,4 @@
-"""The single-node example runs end to end on CPU (gloo path)."""
+"""The examples run end to end on CPU (gloo path)."""
 import os
 import subprocess
 import sys
@@ -11,3 +11,12 @@ def test_single_node_example_cpu():
                           "--steps", "2", "--workers", "2"], capture_output=True, text=True, timeout=300)
     assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-3000:]
     assert "all syncs verified" in out.stdout
+
+
+def test_raw_shards_example_cpu():
+    """The reference example's scenario: uneven row split, column split and a duplicated
+    tensor on two trainer ranks, two rollout workers holding row halves in flat buffers."""
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "examples", "raw_shards.py"), "--device", "cpu",
+                          "--steps", "2"], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-3000:]
+    assert out.stdout.strip().splitlines()[-1].startswith("OK")

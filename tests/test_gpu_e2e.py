@@ -29,3 +29,16 @@ def test_colocated_ipc_pull_direction():
     """The receiver maps the senders' memory (CUDA IPC) and runs the pull kernel itself."""
     run("tiny-llama", "gpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)], dict(tp=1),
         device="cuda:0", dtype=torch.bfloat16, direction="pull")
+
+
+def test_raw_shards_example_on_one_gpu():
+    """Hand-built metadata (uneven rows, column split, duplicated tensor), flat receiver
+    buffers bound at request_update, two trainer and two worker processes on cuda:0."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, os.path.join(root, "examples", "raw_shards.py"), "--device", "cuda",
+                          "--steps", "2"], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-3000:]
+    assert out.stdout.strip().splitlines()[-1].startswith("OK")
