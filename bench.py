@@ -55,6 +55,8 @@ def parse(argv=None):
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--direction", default="push", choices=["push", "pull"],
                    help="gpu_direct: senders store (push) or receivers load the copies (pull)")
+    p.add_argument("--arm", default="direct", choices=["direct", "http"],
+                   help="how each sync is armed: one ZMQ message per worker, or POST /wbridge/receive")
     p.add_argument("--transfer", default="gpu_direct", choices=["gpu_direct", "nvls"],
                    help="nvls: rollout pools in VMM memory, multicast stores to replica groups")
     p.add_argument("--no-pool", action="store_true",
@@ -243,7 +245,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     trainer_ranks = [i for i, r in enumerate(roles) if r.kind == "trainer"]
     tgroup = dist.new_group(trainer_ranks, backend="gloo")
     cfg = TransferConfig.from_env(mode=args.transfer, connect_timeout_s=120, sync_timeout_s=60,
-                                  direction=args.direction)
+                                  direction=args.direction, arm=args.arm)
     if args.mode is not None:
         cfg.kernel_mode = args.mode
     if args.piece is not None:
@@ -402,7 +404,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                        "item_bytes": cfg.item_bytes, "work_items_max": int(G[:, 8].max()),
                        "grid": int(G[:, 9].max()), "processes": nprocs,
                        "rollout_params": "separate allocations" if args.no_pool else "one pooled allocation per rank",
-                       "transfer": args.transfer, "direction": args.direction},
+                       "transfer": args.transfer, "direction": args.direction, "arm": args.arm},
             "latency_s": round(lat, 6),
             "roofline": _roofline(value, float(G[:, 7].sum()), colocated=len({r.device for r in roles}) < len(roles),
                                   bytes_read=float(G[:, 3].sum()), payload=payload_total, ms=ms),
