@@ -1,7 +1,6 @@
 """Coverage checks: receivers are poisoned (NaN) before a sync; afterwards no bound element
 may still hold the poison, and padding outside the bound entries must still hold it (nothing
 writes where it should not).  Random layout pairs come from Hypothesis."""
-import pytest
 import torch
 from hypothesis import given, settings, strategies as st
 

@@ -8,7 +8,6 @@ ST_FLAG_TIMEOUT, and the context must stay usable.
 import random
 import time
 
-import numpy as np
 import pytest
 import torch
 

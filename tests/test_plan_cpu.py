@@ -1,5 +1,4 @@
 """Planner + C++ CPU executor: direct (address to address) and wire (pack / unpack) paths."""
-import numpy as np
 import pytest
 import torch
 

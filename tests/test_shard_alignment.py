@@ -13,7 +13,7 @@ import torch
 from weightbridge_b200 import WeightData
 from weightbridge_b200.core.binding import bind, pack_into, unpack_from, strided
 from weightbridge_b200.core.shard import (align_shards, box_copy, check_shard_compatibility,
-                                          coalesce, shard_extents)
+                                          coalesce)
 
 # (sender, receiver, expected aligned sender, expected aligned receiver); None = incompatible
 CASES = {

@@ -16,8 +16,8 @@ from dataclasses import dataclass, field
 import torch
 import torch.distributed as dist
 
-from ..control.assign import assign_sources, expected_senders, restrict
-from ..core.binding import Binding, bind, pack_into, unpack_from
+from ..control.assign import assign_sources, restrict
+from ..core.binding import Binding, pack_into, unpack_from
 from ..core.shard import WeightData
 
 

@@ -16,7 +16,7 @@ from __future__ import annotations
 import json
 from collections import defaultdict
 
-from ..core.shard import WeightData, box_copy, shard_numel
+from ..core.shard import WeightData, box_copy
 
 
 def _key(shards) -> str:

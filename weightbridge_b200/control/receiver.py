@@ -29,7 +29,6 @@ import tempfile
 import threading
 import time
 from collections import deque
-from datetime import timedelta
 from typing import Any
 
 import torch

@@ -10,7 +10,6 @@ from __future__ import annotations
 import json
 import os
 import socket
-import time
 import zlib
 from datetime import timedelta
 from typing import Any, Iterable

@@ -22,12 +22,12 @@ import hashlib
 import json
 import math
 from dataclasses import dataclass, field
-from typing import Any, Callable, Iterable, Sequence
+from typing import Callable, Iterable, Sequence
 
 import numpy as np
 import torch
 
-from ..utils.dtypes import FLOAT_CAST_DTYPES, as_dtype, dtype_code, dtype_to_str
+from ..utils.dtypes import FLOAT_CAST_DTYPES, dtype_code, dtype_to_str
 from .binding import Binding
 from .shard import Shard, WeightData, box_copy, coalesce, contiguous_strides, shard_extents, shard_numel
 

@@ -13,7 +13,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from ..core.plan import ITEM_DTYPE, OP_COPY, QDESC_DTYPE, QWORK_DTYPE, Tables
+from ..core.plan import OP_COPY, Tables
 from ._ext import ext
 
 # TMA pipeline modes of the kernel (stages x piece bytes of shared memory per CTA).

@@ -8,7 +8,7 @@ Here every wait has a deadline and the rendezvous port is chosen by the OS unles
 from __future__ import annotations
 
 import os
-from dataclasses import dataclass, field, fields
+from dataclasses import dataclass, fields
 
 MODE_ALIASES = {
     "gpu_direct": "gpu_direct", "p2p": "gpu_direct", "ipc": "gpu_direct", "ipc_local": "gpu_direct",
