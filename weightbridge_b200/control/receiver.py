@@ -538,7 +538,8 @@ class WeightReceiver:
             imp = ImportTable(sb["allocs"], same_process=same)
             self._pull_imports[s] = imp
             sphys = PhysBinding.from_json(sb["binding"])
-            ops = [o for o in plan_pair(sphys, self._rphys_abs, names=self._names[s]) if o.kind != "quant"]
+            ops = [o for o in plan_pair(sphys, self._rphys_abs, names=self._names[s])
+                   if o.kind not in ("quant", "squant")]
             parts.append(lower_ops(ops, imp.base, lambda a: 0, item_bytes=self.config.item_bytes))
             if sb["allocs"]:
                 src_ranges += [(imp.base(i), imp.base(i) + int(a["size"])) for i, a in enumerate(sb["allocs"])]

@@ -138,6 +138,8 @@ class WeightSender:
         self._rinfo: dict[int, dict] = {}
         self._ops_cache: dict[tuple, list] = {}     # plan ops per (receiver, bindings, names)
         self._bind_version = 0                       # bumped whenever the bound tensors change
+        self._xchg = None                            # split fp8 blocks shared with other senders
+        self._piece_pos = np.zeros(0, dtype=np.int64)
         self._arm_sock = None                        # rank 0, arm="direct": ROUTER to every receiver worker
         self._arm_idents: dict[int, bytes] = {}
         self._arm_error: str | None = None
@@ -188,6 +190,7 @@ class WeightSender:
         self._all_receivers = set(rmetas)
         self.overlaps = {r: WeightData.compute_overlap(restrict(sender_metadata, names), rmetas[r])
                          for r, names in self.targets.items()}
+        self._xchg = self._exchange_plan(metas, assignment, rmetas)
         # receivers publish their memory tables once they joined the store
         for r in self.targets:
             try:
@@ -216,6 +219,30 @@ class WeightSender:
         self._program_key = None
         self.connected = True
         logger.info("sender %d connected: %d receiver targets, mode=%s", self.rank, len(self.targets), cfg.mode)
+
+    def _exchange_plan(self, metas: list[dict], assignment: dict, rmetas: dict[int, WeightData]):
+        """The split fp8 blocks this sender shares with other senders (``core/splitq.py``),
+        or ``None``: nothing to exchange before a launch."""
+        from ..core.splitq import exchange_plan
+        if not any(any((m.quant(n) or {}).get("format") == "fp8_block" for n in m.names()) for m in rmetas.values()):
+            return None
+        plan = {int(s): {int(r): n for r, n in rs.items()} for s, rs in assignment.items()}
+        x = exchange_plan(self.rank, [WeightData(m) for m in metas], plan, rmetas)
+        return x if x is not None and x.keys else None
+
+    def _split_amax(self, epoch: int, partial: np.ndarray) -> np.ndarray:
+        """Split blocks: publish this sender's per-block amax, merge the co-owners' and return
+        the block amax of every piece.  Raises ``SessionTimeout`` / ``PeerError``."""
+        x, sess = self._xchg, self.session
+        vals = x.local(partial, self._piece_pos)
+        sess.set(f"amax/{self.rank}/{epoch}", vals.tobytes())
+        if x.co_owners:
+            blobs = sess.wait_checked([f"amax/{s}/{epoch}" for s in x.co_owners], self.config.sync_timeout_s,
+                                      f"senders {x.co_owners} to share the amax of split fp8 blocks")
+            vals = x.merge(vals, {s: np.frombuffer(b, dtype=np.float32) for s, b in zip(x.co_owners, blobs)})
+        if epoch > 1:        # every co-owner published this epoch's key, so read the previous one
+            sess.delete(f"amax/{self.rank}/{epoch - 1}")
+        return vals[self._piece_pos]
 
     def _connect_rank0(self, metas: list[dict]) -> dict:
         cfg = self.config
@@ -454,7 +481,7 @@ class WeightSender:
             for r in reps:
                 info, imp = self._rinfo[r], self._imports[r]
                 if uni_ops:          # casts, quantised blocks, unaligned copies: one store per replica
-                    parts.append(lower_ops(uni_ops, lambda a: 0, imp.base, item_bytes=cfg.item_bytes))
+                    parts.append(lower_ops(uni_ops, lambda a: 0, imp.base, item_bytes=cfg.item_bytes, receiver=r))
                 falloc, foff, _w = info["flags"]
                 flags.append(imp.base(falloc) + foff + 8 * self.rank)
                 dst_ranges += [(imp.base(i), imp.base(i) + int(a["size"])) for i, a in enumerate(info["allocs"])]
@@ -471,8 +498,8 @@ class WeightSender:
                 ops = plan_pair(sphys, rphys, names=names)
                 self._ops_cache[ckey] = ops
             if pull:                       # receivers load the copies; quantised blocks stay pushed
-                ops = [o for o in ops if o.kind == "quant"]
-            parts.append(lower_ops(ops, lambda a: 0, imp.base, item_bytes=cfg.item_bytes))
+                ops = [o for o in ops if o.kind in ("quant", "squant")]
+            parts.append(lower_ops(ops, lambda a: 0, imp.base, item_bytes=cfg.item_bytes, receiver=r))
             falloc, foff, _w = info["flags"]
             flags.append(imp.base(falloc) + foff + 8 * self.rank)
             if info["allocs"]:
@@ -480,6 +507,7 @@ class WeightSender:
             else:                          # host memory of this process: the bound regions themselves
                 dst_ranges += _phys_extents(rphys) + [(foff, foff + 8 * int(_w))]
         tables = _interleave(parts)
+        self._piece_pos = self._positions(tables)
         if cfg.validate_plan:
             validate_tables(tables, storage_ranges(state_dict.values()), dst_ranges)
             for f in flags:
@@ -529,11 +557,13 @@ class WeightSender:
             ov = self.overlaps[r]
             wire = torch.empty(ov.total_nbytes(), dtype=torch.uint8, device=dev)
             tables = lower_ops(plan_pair(sphys, wire_binding(ov, base=wire.data_ptr()), names=names, overlap_meta=ov),
-                               lambda a: 0, lambda a: 0, item_bytes=cfg.item_bytes)
+                               lambda a: 0, lambda a: 0, item_bytes=cfg.item_bytes, receiver=r)
             if cfg.validate_plan:
                 validate_tables(tables, storage_ranges(state_dict.values()), storage_ranges([wire]))
             self._wires[r] = (wire, tables)
             parts.append(tables)
+        self._wire_all = Tables.concat(parts)       # host path: split-block pieces of every wire, in order
+        self._piece_pos = self._positions(self._wire_all)
         self._program = None
         if dev.type == "cuda" and parts:
             torch.cuda.set_device(dev)
@@ -542,6 +572,13 @@ class WeightSender:
                                                          grid=cfg.grid or None))
             self._stream = torch.cuda.Stream(dev)
             self._ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+
+    def _positions(self, tables: Tables) -> np.ndarray:
+        if not len(tables.pieces):
+            return np.zeros(0, dtype=np.int64)
+        if self._xchg is None:
+            raise TransferError("the plan has split fp8 blocks but the exchange plan has none")
+        return self._xchg.positions(tables.piece_keys)
 
     def _key(self, state_dict) -> tuple:
         out = []
@@ -622,10 +659,13 @@ class WeightSender:
         return th
 
     def _fail_epoch(self, epoch: int, message: str) -> None:
-        """Tell this epoch's receivers that no data is coming (they stop waiting at once)."""
+        """Tell this epoch's receivers (and the senders sharing split fp8 blocks with this
+        one) that no data is coming: they stop waiting at once."""
         if self.session is not None:
-            self.session.set_error([f"done/{self.rank}/{r}/{epoch}" for r in self.targets],
-                                   f"sender {self.rank}: {message}")
+            keys = [f"done/{self.rank}/{r}/{epoch}" for r in self.targets]
+            if self._xchg is not None:
+                keys.append(f"amax/{self.rank}/{epoch}")
+            self.session.set_error(keys, f"sender {self.rank}: {message}")
 
     def send(self, state_dict: dict[str, Any]) -> SyncStats:
         """One full sync: arm the rollout side, wait until every target receiver is ready,
@@ -667,6 +707,18 @@ class WeightSender:
         except Exception as e:
             self._fail_epoch(epoch, f"{type(e).__name__}: {e}")
             raise
+        piece_amax = None
+        if len(self._piece_pos):          # split fp8 blocks: amax of every piece, then the exchange
+            try:
+                prog = self._program
+                if prog is not None:
+                    prog.set_piece_amax(self._split_amax(epoch, prog.piece_amax(getattr(self, "_stream", None))))
+                else:
+                    from ..ops.executor import cpu_piece_amax
+                    piece_amax = self._split_amax(epoch, cpu_piece_amax(self._wire_all))
+            except (SessionTimeout, PeerError, ValueError) as e:
+                self._fail_epoch(epoch, str(e))
+                raise TransferError(str(e)) from None
         if cfg.mode in WIRE_MODES:
             from ..ops.executor import cpu_execute
             works = []
@@ -685,8 +737,11 @@ class WeightSender:
                 st.device_ms = e0.elapsed_time(e1)
                 st.bytes_read = self._program.bytes_read
             else:
+                first = 0
                 for r, (wire, tables) in self._wires.items():
-                    cpu_execute(tables)
+                    n = len(tables.pieces)
+                    cpu_execute(tables, piece_amax[first:first + n] if n else None)
+                    first += n
                     works.append(self._pg.send([wire], r, epoch))
                 for w in works:
                     w.wait()

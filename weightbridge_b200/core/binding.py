@@ -133,6 +133,10 @@ def pack_into(binding: Binding, overlap: WeightData, out: torch.Tensor) -> None:
             seg = out[off:off + n * dtype.itemsize].view(dtype)
             local, packed = _region_views(binding, name, box, seg)
             if q:
+                from .splitq import block_split
+                if block_split(box, q["block"])[1]:
+                    raise ValueError(f"{name}: region {box} cuts through {list(q['block'])} blocks; their "
+                                     "scales need every sender's amax (WeightSender exchanges them)")
                 qv, sv = block_quant_fp8_ref(local.reshape(shard_extents(box)), tuple(q["block"]))
                 packed.copy_(qv.view(packed.shape))
                 sbox = overlap.shards(q["scale"])[bi]

@@ -8,7 +8,9 @@ both, every overlap becomes one op:
 * ``copy``  - same dtype, N-d strided copy (coalesced to as few dims as possible);
 * ``cast``  - float -> float elementwise conversion (fp32 <-> bf16 <-> fp16);
 * ``quant`` - a block-aligned 2-D region quantised to fp8 e4m3 with fp32 block scales
-  written to the receiver's scale tensor.
+  written to the receiver's scale tensor;
+* ``squant`` - one sender's part of a block that several senders share (``core/splitq.py``):
+  quantised with the block amax the senders exchange before the launch.
 
 Ops are lowered to the work tables the sm_100a kernel and the C++ CPU executor walk:
 ``ITEM`` rows (one 2-D copy/cast of at most ``item_bytes``) and ``QDESC`` rows (one
@@ -42,7 +44,12 @@ QDESC_DTYPE = np.dtype([
     ("bn", "<u2"), ("bk", "<u2"),
 ])
 QWORK_DTYPE = np.dtype([("desc", "<u4"), ("block", "<u4")])
+SPIECE_DTYPE = np.dtype([
+    ("src", "<u8"), ("dst", "<u8"), ("scale", "<u8"), ("src_pitch", "<i8"), ("dst_pitch", "<i8"),
+    ("rows", "<u4"), ("cols", "<u4"), ("src_code", "<u4"), ("reserved", "<u4", (3,)),
+])
 assert ITEM_DTYPE.itemsize == 48 and QDESC_DTYPE.itemsize == 64 and QWORK_DTYPE.itemsize == 8
+assert SPIECE_DTYPE.itemsize == 64
 
 OP_COPY, OP_CAST, OP_COPY_MC = 0, 1, 2
 DEFAULT_ITEM_BYTES = 1 << 19
@@ -135,6 +142,7 @@ class Op:
     scale: tuple[int, int] | None = None      # quant: scale tensor start (alloc, byte offset)
     scale_strides: list[int] | None = None    # quant: element strides of the scale grid
     block: tuple[int, int] | None = None
+    key: tuple | None = None                  # squant: (name, block row, block col) of the split block
 
     @property
     def src_bytes(self) -> int:
@@ -146,6 +154,8 @@ class Op:
         if self.kind == "quant":
             bn, bk = self.block
             n += math.ceil(self.extents[0] / bn) * math.ceil(self.extents[1] / bk) * 4
+        elif self.kind == "squant":
+            n += 4
         return n
 
 
@@ -183,7 +193,7 @@ def plan_pair(src: PhysBinding, dst: PhysBinding, names: Iterable[str] | None = 
                 src_at = _shift(sp, bc.src_offset * s_dtype.itemsize)
                 dst_at = _shift(dp, bc.dst_offset * d_dtype.itemsize)
                 if quant:
-                    ops.append(_quant_op(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst, di, qsrc))
+                    ops += _quant_ops(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst)
                     continue
                 e, ss, ds = coalesce(bc.extents, bc.src_strides, bc.dst_strides)
                 ops.append(Op("copy" if s_dtype == d_dtype else "cast", name, src_at, dst_at, e, ss, ds,
@@ -191,7 +201,21 @@ def plan_pair(src: PhysBinding, dst: PhysBinding, names: Iterable[str] | None = 
     return ops
 
 
-def _quant_op(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst: PhysBinding, di: int, qmeta: WeightData) -> Op:
+def _scale_cell(dst: PhysBinding, sname: str, name: str, bi: int, bj: int) -> tuple[tuple[int, int], list[int]]:
+    """(alloc, byte offset) of block (bi, bj)'s scale cell on the destination, and the scale
+    grid's element strides."""
+    for sp in dst.entries[sname]:
+        (a0, a1, _), (b0, b1, _) = sp.shard
+        if a0 <= bi < a1 and b0 <= bj < b1:
+            off = (bi - a0) * sp.strides[0] + (bj - b0) * sp.strides[1]
+            return (sp.alloc, sp.offset + off * 4), list(sp.strides)
+    raise ValueError(f"{name}: destination has no scale cell for block ({bi}, {bj})")
+
+
+def _quant_ops(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst: PhysBinding) -> list[Op]:
+    """The quantised ops of one overlap: its whole blocks as one ``quant`` op, and one
+    ``squant`` op per block it shares with other senders (``core/splitq.py``)."""
+    from .splitq import block_split
     if len(bc.extents) != 2:
         raise ValueError(f"{name}: a block-quantised overlap must be a 2-D region, got {bc.region}")
     if bc.src_strides[1] != 1 or bc.dst_strides[1] != 1:
@@ -199,22 +223,25 @@ def _quant_op(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst: PhysBinding, d
     block = tuple(int(b) for b in q["block"])
     sname = q["scale"]
     (r0, _r1, _), (c0, _c1, _) = bc.region
-    for (l, r, w), b in zip(bc.region, block):
-        if l % b or (r % b and r != w):
-            raise ValueError(f"{name}: overlap {bc.region} not aligned to {list(block)} blocks")
-    # locate the scale tensor cell of the region's first block on the destination side
-    sregion = [(r0 // block[0], r0 // block[0] + 1, 0), (c0 // block[1], c0 // block[1] + 1, 0)]
-    scale_at, sstr = None, None
-    for sp in dst.entries[sname]:
-        (a0, a1, _), (b0, b1, _) = sp.shard
-        if a0 <= sregion[0][0] < a1 and b0 <= sregion[1][0] < b1:
-            off = (sregion[0][0] - a0) * sp.strides[0] + (sregion[1][0] - b0) * sp.strides[1]
-            scale_at, sstr = (sp.alloc, sp.offset + off * 4), list(sp.strides)
-            break
-    if scale_at is None:
-        raise ValueError(f"{name}: destination has no scale cell for region {bc.region}")
-    return Op("quant", name, src_at, dst_at, list(bc.extents), list(bc.src_strides), list(bc.dst_strides),
-              s_dtype, d_dtype, scale_at, sstr, block)
+    se, de = s_dtype.itemsize, d_dtype.itemsize
+    core, pieces = block_split(bc.region, block)
+
+    def at(base, rr, cc, strides, es):
+        return (base[0], base[1] + ((rr - r0) * strides[0] + (cc - c0) * strides[1]) * es)
+
+    out = []
+    if core is not None:
+        (cr0, cr1), (cc0, cc1) = core
+        scale_at, sstr = _scale_cell(dst, sname, name, cr0 // block[0], cc0 // block[1])
+        out.append(Op("quant", name, at(src_at, cr0, cc0, bc.src_strides, se), at(dst_at, cr0, cc0, bc.dst_strides, de),
+                      [cr1 - cr0, cc1 - cc0], list(bc.src_strides), list(bc.dst_strides), s_dtype, d_dtype,
+                      scale_at, sstr, block))
+    for (bi, bj), (pr0, pr1), (pc0, pc1) in pieces:
+        scale_at, sstr = _scale_cell(dst, sname, name, bi, bj)
+        out.append(Op("squant", name, at(src_at, pr0, pc0, bc.src_strides, se), at(dst_at, pr0, pc0, bc.dst_strides, de),
+                      [pr1 - pr0, pc1 - pc0], list(bc.src_strides), list(bc.dst_strides), s_dtype, d_dtype,
+                      scale_at, sstr, block, key=(name, bi, bj)))
+    return out
 
 
 def plan_digest(ops: Sequence[Op] | WeightData) -> str:
@@ -236,6 +263,8 @@ class Tables:
     qwork: np.ndarray                 # QWORK_DTYPE
     bytes_read: int = 0
     bytes_written: int = 0
+    pieces: np.ndarray = field(default_factory=lambda: np.zeros(0, SPIECE_DTYPE))   # split-block parts
+    piece_keys: list = field(default_factory=list)      # (receiver, name, bi, bj) per piece
 
     @staticmethod
     def empty() -> "Tables":
@@ -254,10 +283,11 @@ class Tables:
             qw.append(w)
             off += len(t.qdescs)
         return Tables(np.concatenate([t.items for t in ts]), np.concatenate(qd), np.concatenate(qw),
-                      sum(t.bytes_read for t in ts), sum(t.bytes_written for t in ts))
+                      sum(t.bytes_read for t in ts), sum(t.bytes_written for t in ts),
+                      np.concatenate([t.pieces for t in ts]), [k for t in ts for k in t.piece_keys])
 
     def __len__(self) -> int:
-        return len(self.items) + len(self.qwork)
+        return len(self.items) + len(self.qwork) + len(self.pieces)
 
 
 def _split_rows(src, dst, sp, dp, row_bytes, rows, op, drb, item_bytes, out: list):
@@ -284,14 +314,17 @@ def _split_rows(src, dst, sp, dp, row_bytes, rows, op, drb, item_bytes, out: lis
 
 
 def lower_ops(ops: Sequence[Op], src_base: Callable[[int], int], dst_base: Callable[[int], int],
-              item_bytes: int = DEFAULT_ITEM_BYTES, multicast: bool = False) -> Tables:
-    """Resolve allocation indices to addresses and cut ops into device work rows."""
+              item_bytes: int = DEFAULT_ITEM_BYTES, multicast: bool = False, receiver: int = -1) -> Tables:
+    """Resolve allocation indices to addresses and cut ops into device work rows.
+    ``receiver`` prefixes the split-block keys of ``squant`` ops."""
     if item_bytes < 16:
         raise ValueError("item_bytes must be at least 16")
     item_bytes = min(int(item_bytes), 1 << 30)      # row_bytes / rows are 32-bit in the work rows
     items: list[tuple] = []
     qdescs: list[tuple] = []
     qwork: list[np.ndarray] = []
+    pieces: list[tuple] = []
+    keys: list[tuple] = []
     rd = wr = 0
     for o in ops:
         s_addr = src_base(o.src[0]) + o.src[1]
@@ -312,6 +345,15 @@ def lower_ops(ops: Sequence[Op], src_base: Callable[[int], int], dst_base: Calla
             w["desc"] = len(qdescs) - 1
             w["block"] = np.arange(nb, dtype=np.uint32)
             qwork.append(w)
+            continue
+        if o.kind == "squant":
+            if multicast:
+                raise ValueError(f"{o.name}: quantised blocks are stored per receiver, not multicast")
+            rows, cols = o.extents
+            sc = dst_base(o.scale[0]) + o.scale[1]
+            pieces.append((s_addr, d_addr, sc, o.src_strides[0] * se, o.dst_strides[0] * de, rows, cols,
+                           dtype_code(o.src_dtype), (0, 0, 0)))
+            keys.append((receiver,) + tuple(o.key))
             continue
         kind = OP_COPY if o.kind == "copy" else OP_CAST
         if multicast:
@@ -339,7 +381,8 @@ def lower_ops(ops: Sequence[Op], src_base: Callable[[int], int], dst_base: Calla
     it = np.array(items, dtype=ITEM_DTYPE) if items else np.zeros(0, ITEM_DTYPE)
     qd = np.array(qdescs, dtype=QDESC_DTYPE) if qdescs else np.zeros(0, QDESC_DTYPE)
     qw = np.concatenate(qwork) if qwork else np.zeros(0, QWORK_DTYPE)
-    return Tables(it, qd, qw, rd, wr)
+    pc = np.array(pieces, dtype=SPIECE_DTYPE) if pieces else np.zeros(0, SPIECE_DTYPE)
+    return Tables(it, qd, qw, rd, wr, pc, keys)
 
 
 # -- validation -----------------------------------------------------------------------------
@@ -407,6 +450,17 @@ def validate_tables(tables: Tables, src_ranges: Sequence[tuple[int, int]],
         nbc = (cols + bk - np.uint64(1)) // bk
         _check(q["scale"], q["scale"] + (nbr - np.uint64(1)) * q["scale_pitch"].astype(np.uint64) + nbc * np.uint64(4),
                dst_ranges, "scale write")
+    p = tables.pieces
+    if len(p):
+        from ..utils.dtypes import CODE_DTYPES
+        if (p["src_pitch"] < 0).any() or (p["dst_pitch"] < 0).any():
+            raise PlanBoundsError("negative row pitch in a split-block piece")
+        es = np.array([CODE_DTYPES[int(c)].itemsize for c in p["src_code"]], dtype=np.uint64)
+        last = np.maximum(p["rows"].astype(np.uint64), 1) - np.uint64(1)
+        cols = p["cols"].astype(np.uint64)
+        _check(p["src"], p["src"] + last * p["src_pitch"].astype(np.uint64) + cols * es, src_ranges, "piece read")
+        _check(p["dst"], p["dst"] + last * p["dst_pitch"].astype(np.uint64) + cols, dst_ranges, "piece write")
+        _check(p["scale"], p["scale"] + np.uint64(4), dst_ranges, "piece scale write")
 
 
 def storage_ranges(tensors) -> list[tuple[int, int]]:

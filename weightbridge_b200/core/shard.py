@@ -241,16 +241,12 @@ def box_copy(src_shard: Shard, dst_shard: Shard,
 
 
 def scale_box(region: Shard, block: Sequence[int], name: str = "") -> Shard:
-    """Block-scale coordinates of a block-aligned 2-D region of a quantised tensor."""
+    """Block-scale cells a 2-D region of a quantised tensor touches.  A cell of a block the
+    region only partly covers is shared with the other senders of that block (they all
+    write the same scale, see ``core/splitq.py``)."""
     if len(region) != 2:
         raise ValueError(f"{name}: a block-quantised overlap must be 2-D, got {region}")
-    out = []
-    for (l, r, w), b in zip(region, block):
-        if l % b or (r % b and r != w):
-            raise ValueError(f"{name}: overlap {region} is not aligned to the {list(block)} blocks; "
-                             f"each block must come from one sender")
-        out.append((l // b, (r + b - 1) // b, (w + b - 1) // b))
-    return out
+    return [(l // b, (r + b - 1) // b, (w + b - 1) // b) for (l, r, w), b in zip(region, block)]
 
 
 def coalesce(extents: Sequence[int], src_strides: Sequence[int], dst_strides: Sequence[int]

@@ -11,6 +11,7 @@
 #include "wb_common.h"
 #include "wb_cpu.h"
 #include "wb_ipc.h"
+#include "wb_splitq.h"
 #include "wb_transfer.h"
 
 namespace py = pybind11;
@@ -63,6 +64,28 @@ void cpu_execute(uint64_t items, size_t n_items, uint64_t qdescs, uint64_t qwork
                   n_qwork);
 }
 
+void split_amax(uint64_t pieces, uint32_t n, uint64_t partial, uint64_t stream) {
+  check(wb::launch_split_amax(P<const wb::SplitPiece>(pieces), n, P<float>(partial),
+                              reinterpret_cast<cudaStream_t>(stream)),
+        "split_amax launch");
+}
+
+void split_quant(uint64_t pieces, uint32_t n, uint64_t amax, uint64_t stream) {
+  check(wb::launch_split_quant(P<const wb::SplitPiece>(pieces), n, P<const float>(amax),
+                               reinterpret_cast<cudaStream_t>(stream)),
+        "split_quant launch");
+}
+
+void cpu_split_amax(uint64_t pieces, size_t n, uint64_t partial) {
+  py::gil_scoped_release nogil;
+  wb::cpu_split_amax(P<const wb::SplitPiece>(pieces), n, P<float>(partial));
+}
+
+void cpu_split_quant(uint64_t pieces, size_t n, uint64_t amax) {
+  py::gil_scoped_release nogil;
+  wb::cpu_split_quant(P<const wb::SplitPiece>(pieces), n, P<const float>(amax));
+}
+
 int num_sms(int device) {
   int v = 0;
   check(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device), "cudaDeviceGetAttribute");
@@ -79,6 +102,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("wait_flags", &wait_flags, "launch a bounded wait on flag words");
   m.def("bulk_stages", &wb::bulk_stages);
   m.def("cpu_execute", &cpu_execute, "run work tables on the host");
+  m.def("split_amax", &split_amax, "launch the per-piece amax kernel of split fp8 blocks");
+  m.def("split_quant", &split_quant, "launch the quantisation kernel of split fp8 blocks");
+  m.def("cpu_split_amax", &cpu_split_amax, "per-piece amax of split fp8 blocks on the host");
+  m.def("cpu_split_quant", &cpu_split_quant, "quantise split fp8 block pieces on the host");
   m.def("num_sms", &num_sms);
   m.def("addr_range", [](uint64_t p) {
     auto r = wb::addr_range(p);
@@ -107,6 +134,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("ITEM_SIZE") = (int)sizeof(wb::Item);
   m.attr("QDESC_SIZE") = (int)sizeof(wb::QuantDesc);
   m.attr("QWORK_SIZE") = (int)sizeof(wb::QuantWork);
+  m.attr("SPIECE_SIZE") = (int)sizeof(wb::SplitPiece);
   m.attr("ST_MBAR_TIMEOUT") = (int)wb::ST_MBAR_TIMEOUT;
   m.attr("ST_FLAG_TIMEOUT") = (int)wb::ST_FLAG_TIMEOUT;
   m.attr("ST_FLAG_STALE") = (int)wb::ST_FLAG_STALE;

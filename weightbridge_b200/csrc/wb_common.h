@@ -59,6 +59,23 @@ struct QuantWork {
 };
 static_assert(sizeof(QuantWork) == 8, "QuantWork layout");
 
+// One sender's part of a 128 x 128 quantisation block whose rows or columns are spread over
+// several senders (a "split block"): the block's scale needs the amax of every part, so the
+// senders first reduce their parts (split_amax), exchange the maxima on the host, then
+// quantise their parts with the common amax (split_quant).
+struct alignas(16) SplitPiece {
+  uint64_t src;
+  uint64_t dst;            // e4m3 destination of the part
+  uint64_t scale;          // the block's fp32 scale cell
+  int64_t src_pitch;       // bytes
+  int64_t dst_pitch;       // bytes
+  uint32_t rows;           // at most one block
+  uint32_t cols;
+  uint32_t src_code;       // DT_BF16 / DT_F16 / DT_F32
+  uint32_t reserved[3];
+};
+static_assert(sizeof(SplitPiece) == 64, "SplitPiece layout");
+
 // Status bits a kernel reports through its status word.
 enum Status : uint32_t {
   ST_OK = 0,

@@ -87,7 +87,46 @@ void run_quant(const QuantDesc& q, uint32_t block) {
   *sp = scale;
 }
 
+float piece_amax(const SplitPiece& p) {
+  const uint32_t es = dsize(p.src_code);
+  if (!es) throw std::invalid_argument("split piece with unsupported dtype");
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(p.src);
+  float amax = 0.f;
+  for (uint32_t r = 0; r < p.rows; ++r)
+    for (uint32_t c = 0; c < p.cols; ++c)
+      amax = std::max(amax, std::fabs(load_f(src + (int64_t)r * p.src_pitch + (uint64_t)c * es, p.src_code)));
+  return amax;
+}
+
+void piece_quant(const SplitPiece& p, float amax) {
+  const uint32_t es = dsize(p.src_code);
+  if (!es) throw std::invalid_argument("split piece with unsupported dtype");
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(p.src);
+  uint8_t* dst = reinterpret_cast<uint8_t*>(p.dst);
+  const float scale = amax > 0.f ? amax / kE4M3Max : 1.f;
+  const float inv = 1.f / scale;
+  for (uint32_t r = 0; r < p.rows; ++r)
+    for (uint32_t c = 0; c < p.cols; ++c) {
+      float x = load_f(src + (int64_t)r * p.src_pitch + (uint64_t)c * es, p.src_code) * inv;
+      x = std::min(std::max(x, -kE4M3Max), kE4M3Max);
+      dst[(int64_t)r * p.dst_pitch + c] = c10::Float8_e4m3fn(x).x;
+    }
+  std::memcpy(reinterpret_cast<void*>(p.scale), &scale, 4);
+}
+
 }  // namespace
+
+void cpu_split_amax(const SplitPiece* pieces, size_t n, float* partial) {
+  at::parallel_for(0, (int64_t)n, 4, [&](int64_t b, int64_t e) {
+    for (int64_t i = b; i < e; ++i) partial[i] = piece_amax(pieces[i]);
+  });
+}
+
+void cpu_split_quant(const SplitPiece* pieces, size_t n, const float* amax) {
+  at::parallel_for(0, (int64_t)n, 4, [&](int64_t b, int64_t e) {
+    for (int64_t i = b; i < e; ++i) piece_quant(pieces[i], amax[i]);
+  });
+}
 
 void cpu_execute(const Item* items, size_t n_items, const QuantDesc* qdescs, const QuantWork* qwork,
                  size_t n_qwork) {

@@ -37,13 +37,29 @@ def bulk_eligible(items: np.ndarray) -> np.ndarray:
     return ((items["op"] & 0xFF) == OP_COPY) & ((bits & np.uint64(15)) == 0)
 
 
-def cpu_execute(tables: Tables) -> None:
-    """Run work tables on the host (addresses are host pointers)."""
+def cpu_execute(tables: Tables, piece_amax: np.ndarray | None = None) -> None:
+    """Run work tables on the host (addresses are host pointers).  Split-block pieces are
+    quantised with ``piece_amax`` (one block amax per piece), which they need."""
+    if len(tables.pieces):
+        if piece_amax is None or len(piece_amax) != len(tables.pieces):
+            raise ValueError("split-block pieces need their block amax (one value per piece)")
+        pc = np.ascontiguousarray(tables.pieces)
+        am = np.ascontiguousarray(piece_amax, dtype=np.float32)
+        ext().cpu_split_quant(pc.ctypes.data, len(pc), am.ctypes.data)
     it = np.ascontiguousarray(tables.items)
     qd = np.ascontiguousarray(tables.qdescs)
     qw = np.ascontiguousarray(tables.qwork)
     ext().cpu_execute(it.ctypes.data if len(it) else 0, len(it), qd.ctypes.data if len(qd) else 0,
                       qw.ctypes.data if len(qw) else 0, len(qw))
+
+
+def cpu_piece_amax(tables: Tables) -> np.ndarray:
+    """Split blocks, first step on the host: max |x| over every piece."""
+    out = np.zeros(len(tables.pieces), dtype=np.float32)
+    if len(out):
+        pc = np.ascontiguousarray(tables.pieces)
+        ext().cpu_split_amax(pc.ctypes.data, len(pc), out.ctypes.data)
+    return out
 
 
 @dataclass
@@ -94,6 +110,29 @@ class TransferProgram:
         self.epoch_host = torch.zeros(1, dtype=torch.int64, pin_memory=True)
         self.n_sms = ext().num_sms(dev.index if dev.index is not None else torch.cuda.current_device())
         self.launches = 0
+        # split-block pieces: amax per piece (device, pinned copy) and the exchanged block amax
+        self.n_pieces = len(tables.pieces)
+        if self.n_pieces:
+            self.pieces = _np_to_tensor(tables.pieces, dev)
+            self.partial = torch.zeros(self.n_pieces, dtype=torch.float32, device=dev)
+            self.amax = torch.zeros(self.n_pieces, dtype=torch.float32, device=dev)
+            self.partial_host = torch.zeros(self.n_pieces, dtype=torch.float32, pin_memory=True)
+            self.amax_host = torch.zeros(self.n_pieces, dtype=torch.float32, pin_memory=True)
+
+    def piece_amax(self, stream: torch.cuda.Stream | None = None) -> np.ndarray:
+        """Split blocks, first step: max |x| over every piece (launch, copy back, wait)."""
+        if not self.n_pieces:
+            return np.zeros(0, dtype=np.float32)
+        stream = stream or torch.cuda.current_stream(self.device)
+        with torch.cuda.stream(stream):
+            ext().split_amax(self.pieces.data_ptr(), self.n_pieces, self.partial.data_ptr(), stream.cuda_stream)
+            self.partial_host.copy_(self.partial, non_blocking=True)
+        stream.synchronize()
+        return self.partial_host.numpy().copy()
+
+    def set_piece_amax(self, values: np.ndarray) -> None:
+        """The block amax of every piece for the next launches (after the senders' exchange)."""
+        self.amax_host.numpy()[:] = values
 
     @property
     def bytes_read(self) -> int:
@@ -124,6 +163,9 @@ class TransferProgram:
             if signal:
                 self.epoch_host[0] = epoch
                 self.epoch_dev.copy_(self.epoch_host, non_blocking=True)
+            if self.n_pieces:       # before the transfer kernel, whose last CTA publishes the flags
+                self.amax.copy_(self.amax_host, non_blocking=True)
+                ext().split_quant(self.pieces.data_ptr(), self.n_pieces, self.amax.data_ptr(), stream.cuda_stream)
             ext().transfer(
                 self.items.data_ptr(), len(self.items_np), self.bulk.data_ptr(), len(self.bulk_np),
                 self.qdescs.data_ptr(), self.qwork.data_ptr(), len(self.tables.qwork),
@@ -150,6 +192,14 @@ class HostProgram:
         self.flag_addrs = list(flag_addrs or [])
         self.device = torch.device("cpu")
         self.launches = 0
+        self.n_pieces = len(tables.pieces)
+        self._amax = np.zeros(self.n_pieces, dtype=np.float32)
+
+    def piece_amax(self, stream=None) -> np.ndarray:
+        return cpu_piece_amax(self.tables)
+
+    def set_piece_amax(self, values: np.ndarray) -> None:
+        self._amax = np.asarray(values, dtype=np.float32).copy()
 
     bytes_read = property(lambda self: self.tables.bytes_read)
     bytes_written = property(lambda self: self.tables.bytes_written)
@@ -159,7 +209,7 @@ class HostProgram:
 
     def launch(self, epoch: int, stream=None, signal: bool = True) -> None:
         import ctypes
-        cpu_execute(self.tables)
+        cpu_execute(self.tables, self._amax)
         if signal:
             for a in self.flag_addrs:
                 ctypes.c_int64.from_address(a).value = epoch
