@@ -271,3 +271,15 @@ def test_host_reshard_fp8_experts():
         for n in params:
             assert torch.equal(params[n].view(torch.uint8) if params[n].dtype == torch.float8_e4m3fn else params[n],
                                expected[n].view(torch.uint8) if expected[n].dtype == torch.float8_e4m3fn else expected[n]), n
+
+
+def test_sglang_fp8_qkv_rejects_a_kv_part_inside_a_block():
+    """Scales of the fused qkv_proj are per 128-row block of the fused tensor; a k/v part that
+    starts inside a block would share its scale with q, which per-entry scales cannot express."""
+    import dataclasses
+    from weightbridge_b200.models.arch import get_arch
+    from weightbridge_b200.parallel.sglang import SGLangLayout
+    arch = dataclasses.replace(get_arch("tiny-llama"), num_heads=3, num_kv_heads=1, head_dim=64, ffn=512)
+    lay = SGLangLayout(arch, tp=1, quant="fp8_linear")
+    with pytest.raises(ValueError, match="inside an fp8 block"):
+        lay.to_wb(lay.allocate(dtype=torch.bfloat16, fill=False))

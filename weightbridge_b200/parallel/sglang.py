@@ -243,6 +243,8 @@ class SGLangLayout:
                 b2 = [box, (0, H, H)]
                 sv = sb = None
                 if scale is not None:
+                    if r0 % bn:
+                        raise ValueError(f"qkv_proj: {nm} starts at row {r0}, inside an fp8 block of {bn} rows")
                     sb = block_box(b2)
                     sv = scale[r0 // bn:(r0 + n + bn - 1) // bn]
                 out += with_scale(f"{p}self_attn.{nm}.weight", param[r0:r0 + n], b2, sv, sb)
