@@ -202,6 +202,23 @@ def test_receive_request_rejected_before_connect():
         ro.close()
 
 
+def test_connect_from_another_protocol_version_is_refused():
+    """A sender of another protocol version (here: one that sends none) is refused at
+    connect, before any session state is touched."""
+    cfg = _cfg()
+    ro = Rollout(cfg)
+    try:
+        import requests
+        r = requests.post(f"{ro.url}/wbridge/connect", timeout=5, json={
+            "master_address": "127.0.0.1", "master_port": 1, "base_rank": 1, "world_size": 2,
+            "group_name": "wbridge", "sender_world_size": 1, "backend": "cpu_direct"})
+        body = r.json()
+        assert body["status"] == "error" and "protocol" in body["detail"][0]
+        assert ro.recv.state.value == "disconnected"
+    finally:
+        ro.close()
+
+
 @pytest.mark.parametrize("mode", ["cpu_direct", "gpu_direct"])
 def test_resume_after_receiver_restart(mode):
     """A rollout worker restarts (new process state, new tensors): the sender reconnects and

@@ -134,7 +134,7 @@ class WeightReceiverController:
                          "master_port": request.master_port, "rank": request.base_rank + idx,
                          "world_size": request.world_size, "group_name": request.group_name,
                          "sender_world_size": request.sender_world_size, "backend": request.backend,
-                         "session": request.session})
+                         "session": request.session, "protocol": request.protocol})
         replies = self._request(msgs)
         ok = all(r.get("status") == "ack" for r in replies)
         return {"status": "success" if ok else "error",

@@ -20,6 +20,10 @@ STATS_REQUEST = "stats_request"
 UPDATE_REQUEST = "update_request"
 STOP_REQUEST = "stop_request"
 
+# Version of the sender <-> receiver session protocol (session keys, arm channel, split-block
+# amax exchange).  A receiver refuses a connect from a sender speaking another version.
+PROTOCOL_VERSION = 2
+
 
 class ReceiverState(str, Enum):
     DISCONNECTED = "disconnected"
@@ -38,6 +42,7 @@ class ConnectRequest(BaseModel):
     sender_world_size: int
     backend: str = "gpu_direct"          # transfer mode: gpu_direct | nvls | nccl | cpu_direct ("gloo" = cpu_direct)
     session: Optional[str] = None
+    protocol: int = 1                    # PROTOCOL_VERSION of the sender (absent: an older sender)
 
 
 def b64(data: bytes) -> str:

@@ -40,8 +40,8 @@ from ..core.shard import WeightData
 from ..utils.config import WIRE_MODES, TransferConfig, normalize_mode
 from ..utils.trace import nvtx_range
 from .assign import expected_senders, restrict
-from .protocol import (CONNECT_REQUEST, METADATA_REQUEST, RECEIVE_REQUEST, STATS_REQUEST, STOP_REQUEST,
-                       UPDATE_REQUEST, ReceiverState, b64)
+from .protocol import (CONNECT_REQUEST, METADATA_REQUEST, PROTOCOL_VERSION, RECEIVE_REQUEST, STATS_REQUEST,
+                       STOP_REQUEST, UPDATE_REQUEST, ReceiverState, b64)
 from .session import Janitor, PeerError, Session, SessionTimeout
 
 logger = logging.getLogger(__name__)
@@ -217,6 +217,10 @@ class WeightReceiver:
         elif t == CONNECT_REQUEST:
             if self._state == ReceiverState.AWAITING_SCHEDULER_UPDATE:
                 self._reply(sock, data, {"status": "error", "detail": "cannot connect while awaiting scheduler update"})
+                return
+            if int(data.get("protocol", 1)) != PROTOCOL_VERSION:
+                self._reply(sock, data, {"status": "error", "detail": f"sender speaks protocol {data.get('protocol', 1)}, "
+                                                                      f"this receiver {PROTOCOL_VERSION}"})
                 return
             self._reply(sock, data, {"status": "ack"})
             self._state = ReceiverState.CONNECTING

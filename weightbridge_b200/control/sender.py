@@ -45,6 +45,7 @@ from ..core.shard import WeightData
 from ..utils.config import WIRE_MODES, TransferConfig, normalize_mode
 from .assign import assign_sources, restrict
 from ..utils.trace import nvtx_range
+from .protocol import PROTOCOL_VERSION
 from .session import PeerError, Session, SessionTimeout, local_address
 
 logger = logging.getLogger(__name__)
@@ -282,7 +283,7 @@ class WeightSender:
             resp = http.post(f"{url}/wbridge/connect", timeout=cfg.http_timeout_s, json={
                 "master_address": addr, "master_port": sess.port, "base_rank": base, "world_size": world,
                 "group_name": "wbridge", "sender_world_size": self.world_size, "backend": backend,
-                "session": session_id})
+                "session": session_id, "protocol": PROTOCOL_VERSION})
             resp.raise_for_status()
             if resp.json().get("status") != "success":
                 return {"error": f"receiver {url} refused connect: {resp.json()}"}
