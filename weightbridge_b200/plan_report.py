@@ -1,0 +1,133 @@
+"""Dry-run planner: what a sync between two layouts moves, without allocating a byte.
+
+    python -m weightbridge_b200.plan_report --model qwen3-30b-a3b --trainer ep=4 \\
+        --rollout tp=4,moe_ep=4,quant=fp8_experts
+    python -m weightbridge_b200.plan_report --model llama3-8b --trainer tp=2,pp=2 --rollout tp=1 --replicas 4 --json
+
+Builds both layouts on the ``meta`` device, runs the source assignment and the planner for
+every (sender, receiver) pair, and reports per-sender and per-receiver bytes, work rows,
+quantised blocks and split-block pieces, plus the sync time the busiest link allows.  Trainer
+ranks are enumerated as pipeline stage x expert-parallel rank x max(tp, etp) with
+``tp_rank = t % tp`` and ``etp_rank = t % etp``; rollout workers as replica x tp rank.
+The reference has no equivalent (it plans inside ``connect``, ``wbridge/backend/direct_sender.py:74-168``).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+
+import torch
+
+from .control.assign import assign_sources, restrict
+from .core.binding import bind
+from .core.plan import lower_ops, phys_binding, plan_pair
+from .core.shard import WeightData
+from .models.arch import get_arch
+from .parallel.megatron import MegatronLayout
+from .parallel.sglang import SGLangLayout
+
+_ABS = lambda _alloc: 0      # noqa: E731  (meta tensors: every address is 0)
+
+
+def _kv(spec: str) -> dict:
+    out: dict = {}
+    for part in filter(None, (p.strip() for p in spec.split(","))):
+        k, _, v = part.partition("=")
+        out[k] = int(v) if v.lstrip("-").isdigit() else (None if v in ("", "none") else v)
+    return out
+
+
+def trainer_layouts(arch, spec: dict) -> list[MegatronLayout]:
+    tp, pp, ep, etp = (int(spec.get(k, 1)) for k in ("tp", "pp", "ep", "etp"))
+    extra = {k: v for k, v in spec.items() if k not in ("tp", "pp", "ep", "etp")}
+    return [MegatronLayout(arch, tp=tp, pp=pp, ep=ep, etp=etp, tp_rank=t % tp, pp_rank=p, ep_rank=e,
+                           etp_rank=t % etp, **extra)
+            for p in range(pp) for e in range(ep) for t in range(max(tp, etp))]
+
+
+def rollout_layouts(arch, spec: dict, replicas: int) -> list[SGLangLayout]:
+    tp = int(spec.get("tp", 1))
+    extra = {k: v for k, v in spec.items() if k != "tp"}
+    return [SGLangLayout(arch, tp=tp, tp_rank=t, **extra) for _ in range(replicas) for t in range(tp)]
+
+
+def _meta_binding(lay):
+    params = lay.allocate(device="meta", dtype=torch.bfloat16, fill=False)
+    meta, views = lay.to_wb(params)
+    return meta, phys_binding(bind(meta, views))
+
+
+def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs: float = 770.0) -> dict:
+    arch = get_arch(model)
+    senders = [_meta_binding(l) for l in trainer_layouts(arch, trainer)]
+    receivers = [_meta_binding(l) for l in rollout_layouts(arch, rollout, replicas)]
+    smetas = [m for m, _ in senders]
+    rmetas = {r: m for r, (m, _) in enumerate(receivers)}
+    plan = assign_sources(smetas, rmetas)
+    srows, ingress = [], [0] * len(receivers)
+    for s, (smeta, sphys) in enumerate(senders):
+        row = {"sender": s, "targets": 0, "bytes_read": 0, "bytes_written": 0, "items": 0,
+               "quant_blocks": 0, "split_pieces": 0}
+        for r, names in sorted(plan.get(s, {}).items()):
+            if not names:
+                continue
+            t = lower_ops(plan_pair(sphys, receivers[r][1], names=names), _ABS, _ABS, receiver=r)
+            row["targets"] += 1
+            row["bytes_read"] += t.bytes_read
+            row["bytes_written"] += t.bytes_written
+            row["items"] += len(t.items)
+            row["quant_blocks"] += len(t.qwork)
+            row["split_pieces"] += len(t.pieces)
+            ingress[r] += t.bytes_written
+        srows.append(row)
+    egress = max((r["bytes_written"] for r in srows), default=0)
+    inmax = max(ingress, default=0)
+    return {
+        "model": model, "trainer": trainer, "rollout": rollout, "replicas": replicas,
+        "senders": srows,
+        "receivers": [{"receiver": r, "ingress_bytes": b,
+                       "senders": sorted(s for s, t in plan.items() if t.get(r))} for r, b in enumerate(ingress)],
+        "total_written_bytes": sum(ingress),
+        "busiest_sender_bytes": egress, "busiest_receiver_bytes": inmax,
+        "link_gbs": link_gbs,
+        "link_bound_ms": max(egress, inmax) / (link_gbs * 1e9) * 1e3,
+        "note": "link-bound estimate for senders and receivers on different GPUs; a colocated pair "
+                "moves its bytes through HBM instead",
+    }
+
+
+def _gb(n: int) -> str:
+    return f"{n / 1e9:.3f}"
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--model", required=True)
+    ap.add_argument("--trainer", default="", help="Megatron layout, e.g. tp=2,pp=2 or ep=4,etp=2")
+    ap.add_argument("--rollout", default="", help="SGLang layout, e.g. tp=4,moe_ep=4,quant=fp8_experts")
+    ap.add_argument("--replicas", type=int, default=1, help="rollout replicas (each with the rollout layout)")
+    ap.add_argument("--link-gbs", type=float, default=770.0, help="per-GPU link bandwidth for the estimate")
+    ap.add_argument("--json", action="store_true")
+    a = ap.parse_args(argv)
+    rep = report(a.model, _kv(a.trainer), _kv(a.rollout), a.replicas, a.link_gbs)
+    if a.json:
+        print(json.dumps(rep))
+        return 0
+    print(f"{a.model}: trainer {a.trainer or 'tp=1'} ({len(rep['senders'])} ranks) -> rollout "
+          f"{a.rollout or 'tp=1'} x{a.replicas} ({len(rep['receivers'])} workers)")
+    print(f"{'sender':>6} {'targets':>7} {'read GB':>9} {'written GB':>10} {'items':>8} {'quant blk':>9} {'split pcs':>9}")
+    for r in rep["senders"]:
+        print(f"{r['sender']:>6} {r['targets']:>7} {_gb(r['bytes_read']):>9} {_gb(r['bytes_written']):>10} "
+              f"{r['items']:>8} {r['quant_blocks']:>9} {r['split_pieces']:>9}")
+    print(f"{'worker':>6} {'ingress GB':>10}  senders")
+    for r in rep["receivers"]:
+        print(f"{r['receiver']:>6} {_gb(r['ingress_bytes']):>10}  {r['senders']}")
+    print(f"total written {_gb(rep['total_written_bytes'])} GB; busiest sender {_gb(rep['busiest_sender_bytes'])} GB, "
+          f"busiest worker {_gb(rep['busiest_receiver_bytes'])} GB -> {rep['link_bound_ms']:.2f} ms at "
+          f"{rep['link_gbs']:.0f} GB/s per link")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
