@@ -17,7 +17,7 @@ def _port():
 
 
 def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype, late=False, direction="push",
-                 exit_after=None):
+                 exit_after=None, cfg_extra=None):
     import threading
     import uvicorn
     from fastapi import FastAPI
@@ -32,7 +32,7 @@ def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype, late=Fal
         lay = SGLangLayout(get_arch(model), **rlayout)
         params = lay.allocate(device=device, dtype=dtype)
         meta, views = lay.to_wb(params)
-        cfg = TransferConfig(mode=mode, connect_timeout_s=60, sync_timeout_s=60)
+        cfg = TransferConfig(mode=mode, connect_timeout_s=60, sync_timeout_s=60, **(cfg_extra or {}))
         # late: the reference's flow, tensors handed over at request_update
         recv = WeightReceiver(ctl.ipc_name, 0, meta, state_dict=None if late else views, config=cfg)
         server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="warning"))
@@ -62,7 +62,8 @@ def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype, late=Fal
         q.put(("error", traceback.format_exc(), None))
 
 
-def trainer_proc(rank, world, tport, url, q, n_syncs, model, mode, device, layouts, dtype, direction="push"):
+def trainer_proc(rank, world, tport, url, q, n_syncs, model, mode, device, layouts, dtype, direction="push",
+                 cfg_extra=None):
     import torch.distributed as dist
     from weightbridge_b200 import TransferConfig, WeightSender
     from weightbridge_b200.models.arch import get_arch
@@ -74,7 +75,7 @@ def trainer_proc(rank, world, tport, url, q, n_syncs, model, mode, device, layou
         lay = MegatronLayout(get_arch(model), **layouts[rank])
         params = lay.allocate(device=device, dtype=dtype, seed=0)
         meta, views = lay.to_wb(params)
-        cfg = TransferConfig(mode=mode, connect_timeout_s=60, sync_timeout_s=60, direction=direction)
+        cfg = TransferConfig(mode=mode, connect_timeout_s=60, sync_timeout_s=60, direction=direction, **(cfg_extra or {}))
         sender = WeightSender(mode, [url], config=cfg)
         sender.connect(meta)
         for i in range(n_syncs):
@@ -89,17 +90,18 @@ def trainer_proc(rank, world, tport, url, q, n_syncs, model, mode, device, layou
 
 
 def run(model, mode, trainer_layouts, rollout_layout, device="cpu", dtype=torch.float32, n_syncs=3, timeout=240,
-        trainer_devices=None, late=False, direction="push"):
+        trainer_devices=None, late=False, direction="push", cfg_extra=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     hport, tport = _port(), _port()
     url = f"http://127.0.0.1:{hport}"
     world = len(trainer_layouts)
     procs = [ctx.Process(target=rollout_proc, args=(hport, q, n_syncs, model, mode, device, rollout_layout, dtype,
-                                                    late, direction))]
+                                                    late, direction, None, cfg_extra))]
     tdev = trainer_devices or [device] * world
     procs += [ctx.Process(target=trainer_proc, args=(r, world, tport, url, q, n_syncs, model, mode, tdev[r],
-                                                      trainer_layouts, dtype, direction)) for r in range(world)]
+                                                      trainer_layouts, dtype, direction, cfg_extra))
+              for r in range(world)]
     procs[0].start()
     deadline = time.time() + timeout
     first = q.get(timeout=120)

@@ -359,6 +359,7 @@ class WeightReceiver:
         self.expected = expected_senders(plan, gr)
         self._names = {s: plan[s][gr] for s in self.expected}
         self.direction = sess.wait_checked(["direction"])[0].decode() if mode == "gpu_direct" else "push"
+        self._wire_chunk = int(sess.wait_checked(["wire_chunk"])[0]) if mode in WIRE_MODES else 0
         self._pull_versions, self._pull_prog, self._pull_imports = None, None, {}
         self.expected_bytes = 0
         self.overlaps: dict[int, WeightData] = {}
@@ -415,22 +416,15 @@ class WeightReceiver:
         return info
 
     def _setup_wires(self) -> None:
-        """Wire modes: one receive buffer per expected sender and the unpack tables."""
-        from ..core.plan import Tables
-        from ..ops.executor import LaunchConfig, TransferProgram
+        """Wire modes: per expected sender, the chunked receive buffers and unpack tables
+        (``control/wires.py``)."""
+        from ..core.plan import storage_ranges
+        from .wires import WireSet
         if (self.mode == "nccl") != (self.device.type == "cuda"):
             raise ReceiveError(f"mode {self.mode} does not take tensors on {self.device}")
-        self._wires, parts = {}, []
-        for s, ov in self.overlaps.items():
-            wire = torch.empty(ov.total_nbytes(), dtype=torch.uint8, device=self.device)
-            tables = lower_ops(plan_pair(wire_binding(ov, base=wire.data_ptr()), self._rphys),
-                               lambda a: 0, lambda a: 0, item_bytes=self.config.item_bytes)
-            self._wires[s] = (wire, tables)
-            parts.append(tables)
-        self._unpack = None
-        if self.device.type == "cuda" and parts:
-            self._unpack = TransferProgram(Tables.concat(parts), self.device, [],
-                                           LaunchConfig(mode=self.config.kernel_mode))
+        self._wires = WireSet.for_receiver(self._rphys, self.overlaps, self.device, self.config,
+                                           storage_ranges(self.state_dict.values()), self._wire_chunk)
+        if self.device.type == "cuda":
             self._stream = torch.cuda.Stream(self.device)
 
     def _late_bind(self) -> None:
@@ -455,21 +449,14 @@ class WeightReceiver:
         if not self._bound:
             self._late_bind()
         if self.mode in WIRE_MODES:
-            from ..ops.executor import cpu_execute
             sess.set(f"ready/{gr}/{epoch}", "1")
-            if self._unpack is not None:     # device wires: NCCL receives, then one unpack launch
+            ws = self._wires
+            if ws.device.type == "cuda":     # NCCL receives and unpack launches, ordered on one stream
                 with torch.cuda.stream(self._stream):
-                    works = [self._pg.recv([wire], s, epoch) for s, (wire, _t) in self._wires.items()]
-                    for w in works:
-                        w.wait()
-                    self._unpack.launch(epoch, self._stream, signal=False)
+                    ws.recv(self._pg, epoch, self._stream)
                 self._stream.synchronize()
             else:
-                works = [self._pg.recv([wire], s, epoch) for s, (wire, _t) in self._wires.items()]
-                for w in works:
-                    w.wait()
-                for s, (wire, tables) in self._wires.items():
-                    cpu_execute(tables)
+                ws.recv(self._pg, epoch)
         else:
             sess.set(f"ready/{gr}/{epoch}", "1")
             keys = [f"done/{s}/{gr}/{epoch}" for s in self.expected]

@@ -271,6 +271,7 @@ class WeightSender:
         plan = assign_sources(smeta_objs, rmeta_objs, cfg.load_balance)
         sess.set_json("senders/meta", metas)
         sess.set("direction", cfg.direction if cfg.mode == "gpu_direct" else "push")
+        sess.set("wire_chunk", str(int(cfg.wire_chunk_bytes)))      # receivers cut their wires alike
         sess.set_json("assign", {str(s): {str(r): n for r, n in rs.items()} for s, rs in plan.items()})
         for s, rs in plan.items():
             for r, names in rs.items():
@@ -542,9 +543,10 @@ class WeightSender:
         self.session.set_json(f"sendbind/{self.rank}", info)
 
     def _compile_wire(self, state_dict) -> None:
-        """Wire modes: pack every target's overlap into one buffer per target (the C++
-        executor for host tensors, one transfer-kernel launch for device tensors)."""
-        from ..ops.executor import LaunchConfig, TransferProgram
+        """Wire modes: every target's overlap cut into chunks with two buffers per target
+        (``control/wires.py``), packed by the C++ executor for host tensors and by one
+        transfer-kernel launch per chunk for device tensors."""
+        from .wires import WireSet
         cfg = self.config
         binding = bind(self.metadata, state_dict)
         dev = binding.device
@@ -552,25 +554,13 @@ class WeightSender:
             raise TransferError("cpu_direct sends host tensors; use nccl or gpu_direct for device tensors")
         if cfg.mode == "nccl" and dev.type != "cuda":
             raise TransferError("nccl mode sends device tensors; use cpu_direct for host tensors")
-        sphys = phys_binding(binding)
-        self._wires, parts = {}, []
-        for r, names in sorted(self.targets.items()):
-            ov = self.overlaps[r]
-            wire = torch.empty(ov.total_nbytes(), dtype=torch.uint8, device=dev)
-            tables = lower_ops(plan_pair(sphys, wire_binding(ov, base=wire.data_ptr()), names=names, overlap_meta=ov),
-                               lambda a: 0, lambda a: 0, item_bytes=cfg.item_bytes, receiver=r)
-            if cfg.validate_plan:
-                validate_tables(tables, storage_ranges(state_dict.values()), storage_ranges([wire]))
-            self._wires[r] = (wire, tables)
-            parts.append(tables)
-        self._wire_all = Tables.concat(parts)       # host path: split-block pieces of every wire, in order
-        self._piece_pos = self._positions(self._wire_all)
-        self._program = None
-        if dev.type == "cuda" and parts:
+        if dev.type == "cuda":
             torch.cuda.set_device(dev)
-            self._program = TransferProgram(Tables.concat(parts), dev, [],
-                                            LaunchConfig(mode=cfg.kernel_mode, piece_bytes=cfg.piece_bytes,
-                                                         grid=cfg.grid or None))
+        self._wires = WireSet.for_sender(phys_binding(binding), self.overlaps, self.targets, dev, cfg,
+                                         storage_ranges(state_dict.values()))
+        self._piece_pos = self._positions(self._wires.all_tables)
+        self._program = None
+        if dev.type == "cuda":
             self._stream = torch.cuda.Stream(dev)
             self._ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
 
@@ -708,45 +698,28 @@ class WeightSender:
         except Exception as e:
             self._fail_epoch(epoch, f"{type(e).__name__}: {e}")
             raise
-        piece_amax = None
         if len(self._piece_pos):          # split fp8 blocks: amax of every piece, then the exchange
             try:
-                prog = self._program
-                if prog is not None:
-                    prog.set_piece_amax(self._split_amax(epoch, prog.piece_amax(getattr(self, "_stream", None))))
-                else:
-                    from ..ops.executor import cpu_piece_amax
-                    piece_amax = self._split_amax(epoch, cpu_piece_amax(self._wire_all))
+                src = self._wires if cfg.mode in WIRE_MODES else self._program
+                src.set_piece_amax(self._split_amax(epoch, src.piece_amax(getattr(self, "_stream", None))))
             except (SessionTimeout, PeerError, ValueError) as e:
                 self._fail_epoch(epoch, str(e))
                 raise TransferError(str(e)) from None
         if cfg.mode in WIRE_MODES:
-            from ..ops.executor import cpu_execute
-            works = []
-            if self._program is not None:        # device tensors: one pack launch, then NCCL sends
+            ws = self._wires
+            if ws.device.type == "cuda":          # pack launches and NCCL sends, ordered on one stream
                 e0, e1 = self._ev
                 with torch.cuda.stream(self._stream):
-                    self._stream.wait_stream(torch.cuda.current_stream(self._program.device))
+                    self._stream.wait_stream(torch.cuda.current_stream(ws.device))
                     e0.record(self._stream)
-                    self._program.launch(epoch, self._stream, signal=False)
-                    for r, (wire, _t) in self._wires.items():
-                        works.append(self._pg.send([wire], r, epoch))
-                    for w in works:
-                        w.wait()
+                    ws.send(self._pg, epoch, self._stream)
                     e1.record(self._stream)
                 e1.synchronize()
                 st.device_ms = e0.elapsed_time(e1)
-                st.bytes_read = self._program.bytes_read
             else:
-                first = 0
-                for r, (wire, tables) in self._wires.items():
-                    n = len(tables.pieces)
-                    cpu_execute(tables, piece_amax[first:first + n] if n else None)
-                    first += n
-                    works.append(self._pg.send([wire], r, epoch))
-                for w in works:
-                    w.wait()
-            st.bytes_written = sum(w.numel() for w, _t in self._wires.values())
+                ws.send(self._pg, epoch)
+            st.bytes_read = ws.bytes_read
+            st.bytes_written = ws.bytes_on_wire
         elif self.targets:
             prog = self._program
             pushed = prog is not None and len(prog.tables) > 0

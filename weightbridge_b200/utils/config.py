@@ -41,6 +41,7 @@ class TransferConfig:
     kernel_mode: int = -1                 # -1 auto, 0 vector, 1/2/3 TMA bulk pipeline depths
     piece_bytes: int = 16384
     item_bytes: int = 1 << 19
+    wire_chunk_bytes: int = 256 << 20     # wire modes: message size per peer (two buffers of it per peer); 0: whole overlap
     grid: int = 0                         # 0: sized from the SM count
     verify_flags: bool = True             # receiver checks every sender's epoch flag
     load_balance: bool = True             # spread replicated shards over senders
