@@ -585,7 +585,8 @@ class WeightSender:
         """Enqueue this sender's transfer kernel on ``stream`` with no HTTP arm, no handshake
         and no host synchronisation.  For callers that already know the rollout side is
         idle (and for device-timed benchmarks): the receivers' epoch flags are not touched,
-        so a later ``send`` still pairs with ``request_update``."""
+        so a later ``send`` still pairs with ``request_update``.  Blocks split across senders
+        are quantised with the block amax exchanged by the last ``send``."""
         if not self.connected:
             raise RuntimeError("WeightSender.launch requires connect() first")
         if self.config.mode in WIRE_MODES:
