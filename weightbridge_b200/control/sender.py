@@ -61,6 +61,7 @@ class SyncStats:
     device_ms: float = 0.0          # transfer kernel, CUDA events on the transfer stream
     host_ms: float = 0.0            # whole send() call
     wait_ready_ms: float = 0.0
+    exchange_ms: float = 0.0        # split fp8 blocks: amax pass and the exchange between senders
     bytes_read: int = 0
     bytes_written: int = 0
     receivers: list[int] = field(default_factory=list)
@@ -701,8 +702,10 @@ class WeightSender:
             raise
         if len(self._piece_pos):          # split fp8 blocks: amax of every piece, then the exchange
             try:
+                tx = time.perf_counter()
                 src = self._wires if cfg.mode in WIRE_MODES else self._program
                 src.set_piece_amax(self._split_amax(epoch, src.piece_amax(getattr(self, "_stream", None))))
+                st.exchange_ms = (time.perf_counter() - tx) * 1e3
             except (SessionTimeout, PeerError, ValueError) as e:
                 self._fail_epoch(epoch, str(e))
                 raise TransferError(str(e)) from None
