@@ -389,3 +389,28 @@ def test_direct_arm_to_a_stopped_worker_fails_fast():
         assert time.time() - t0 < 5
     finally:
         ro.close()
+
+
+def test_sync_over_this_hosts_address():
+    """The session store and the arm channel on the host's routable address instead of
+    loopback (the disaggregated set-up: the receivers publish that address for their arm
+    sockets, bound on every interface)."""
+    from weightbridge_b200.control.session import local_address
+    addr = local_address()
+    if addr.startswith("127."):
+        pytest.skip("no routable address on this host")
+    cfg = _cfg(mode="cpu_direct", master_address=addr)
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender("cpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+        th.start()
+        s.send(views)
+        th.join(20)
+        assert ro.recv._arm_sock.getsockopt_string(__import__("zmq").LAST_ENDPOINT).startswith("tcp://0.0.0.0:")
+        exp = ro.lay.allocate(dtype=torch.float32, fill=True)
+        assert all(torch.equal(ro.params[n], exp[n]) for n in exp)
+    finally:
+        ro.close()
