@@ -414,3 +414,82 @@ def test_sync_over_this_hosts_address():
         assert all(torch.equal(ro.params[n], exp[n]) for n in exp)
     finally:
         ro.close()
+
+
+def _cut(watch):
+    """A process dying: its liveness connections close without the orderly bye."""
+    import socket as _s
+    watch._stop.set()
+    watch._thread.join(2)
+    for sock in list(watch._conns):
+        try:
+            sock.shutdown(_s.SHUT_RDWR)
+        except OSError:
+            pass
+        sock.close()
+
+
+def test_sender_dying_mid_sync_fails_the_receiver_at_once():
+    """The receiver is waiting for a sender's done key when the sender's process goes away:
+    the liveness connection closes without a bye and the wait ends with an error in well
+    under the 30 s sync deadline."""
+    from weightbridge_b200.control.receiver import ReceiveError
+    cfg = _cfg(mode="gpu_direct", sync_timeout_s=30.0)
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender("gpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        out = {}
+
+        def update():
+            t0 = time.time()
+            try:
+                ro.recv.request_update(timeout=20)
+                out["r"] = ("ok", time.time() - t0)
+            except ReceiveError as e:
+                out["r"] = (str(e), time.time() - t0)
+
+        th = threading.Thread(target=update)
+        th.start()
+        s._arm(1)                                    # armed; the sender never launches
+        s.session.wait([f"ready/{min(s.targets)}/1"], 10)
+        _cut(s._watch)
+        th.join(20)
+        msg, dt = out["r"]
+        assert "left the session" in msg and dt < 10, out
+    finally:
+        ro.close()
+
+
+def test_receiver_dying_while_a_sender_waits_for_ready():
+    """The sender waits for a worker's ready key when the worker's process goes away: the
+    send fails at once instead of at the 30 s deadline."""
+    cfg = _cfg(mode="gpu_direct", sync_timeout_s=30.0)
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender("gpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        threading.Timer(0.5, lambda: _cut(ro.recv._watch)).start()   # nobody calls request_update
+        t0 = time.time()
+        with pytest.raises(TransferError, match="left the session"):
+            s.send(views)
+        assert time.time() - t0 < 10
+    finally:
+        ro.close()
+
+
+def test_orderly_disconnect_is_not_a_loss():
+    cfg = _cfg(mode="gpu_direct")
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender("gpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        watch = ro.recv._watch
+        s.disconnect()
+        time.sleep(0.5)
+        assert watch.lost == []
+    finally:
+        ro.close()

@@ -73,6 +73,7 @@ class WeightReceiver:
         self._arm_sock = None
         self._poller: zmq.Poller | None = None
         self._janitor: Janitor | None = None
+        self._watch = None
         fd, path = tempfile.mkstemp(prefix=f"wbridge_sched_{rank}_")
         os.close(fd)
         os.unlink(path)
@@ -278,6 +279,22 @@ class WeightReceiver:
         self._poller.register(sock, zmq.POLLIN)
         return f"tcp://{'127.0.0.1' if loopback else local_address()}:{port}"
 
+    def _open_watch(self, master_address: str):
+        """Accept the senders' liveness connections (``control/liveness.py``)."""
+        from .liveness import PeerWatch
+        from .session import local_address
+        loopback = master_address in ("127.0.0.1", "localhost", "::1")
+        lsock, port = PeerWatch.listen("127.0.0.1" if loopback else "0.0.0.0")
+        self._live_addr = ["127.0.0.1" if loopback else local_address(), port]
+        return PeerWatch(self._sender_lost, lsock)
+
+    def _sender_lost(self, s: int) -> None:
+        """A sender's process is gone: fail the wait for its ``done`` key now, not at the deadline."""
+        janitor, gr = self._janitor, self.global_rank
+        if janitor is not None and s in getattr(self, "expected", []):
+            janitor.set_error([f"done/{s}/{gr}/{self.epoch + 1}"],
+                              f"sender {s} left the session (its connection to receiver {gr} closed)")
+
     def _close_arm_socket(self) -> None:
         sock, self._arm_sock = self._arm_sock, None
         if sock is not None:
@@ -340,8 +357,10 @@ class WeightReceiver:
                        timeout_s=self.config.connect_timeout_s)
         self.session = sess
         self._janitor = Janitor(data["master_address"], int(data["master_port"]), self.config.connect_timeout_s)
+        self._watch = self._open_watch(data["master_address"])
         info: dict[str, Any] = {"rank": gr, "worker": self.rank, "pid": os.getpid(), "host": socket.gethostname(),
-                                "mode": mode, "arm": self._open_arm_socket(data["master_address"])}
+                                "mode": mode, "arm": self._open_arm_socket(data["master_address"]),
+                                "live": self._live_addr}
         self._W = W
         self._bound = False
         if self.state_dict is not None:
@@ -627,6 +646,9 @@ class WeightReceiver:
 
     def _teardown(self) -> None:
         self._close_arm_socket()
+        if self._watch is not None:
+            self._watch.close()
+            self._watch = None
         if self._janitor is not None:
             self._janitor.close()
             self._janitor = None

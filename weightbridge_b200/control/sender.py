@@ -46,7 +46,7 @@ from ..utils.config import WIRE_MODES, TransferConfig, normalize_mode
 from .assign import assign_sources, restrict
 from ..utils.trace import nvtx_range
 from .protocol import PROTOCOL_VERSION
-from .session import PeerError, Session, SessionTimeout, local_address
+from .session import Janitor, PeerError, Session, SessionTimeout, local_address
 
 logger = logging.getLogger(__name__)
 
@@ -216,11 +216,39 @@ class WeightSender:
             sess.wait_checked([f"joined/{r}" for r in self.targets], cfg.connect_timeout_s, "receivers to join")
         except (SessionTimeout, PeerError) as e:
             raise TransferError(str(e)) from None
+        self._open_watch(addr, port)
         self.epoch = 0
         self._program = None
         self._program_key = None
         self.connected = True
         logger.info("sender %d connected: %d receiver targets, mode=%s", self.rank, len(self.targets), cfg.mode)
+
+    def _open_watch(self, addr: str, port: int) -> None:
+        """Liveness connections to every target worker (``control/liveness.py``) and a side
+        channel to publish a lost worker's error while this thread waits on the session."""
+        from .liveness import PeerWatch
+        self._side = Janitor(addr, port, self.config.connect_timeout_s)
+        self._watch = PeerWatch(self._receiver_lost)
+        for r in sorted(self.targets):
+            host, lport = self._rinfo[r]["live"]
+            try:
+                self._watch.add(PeerWatch.connect(host, int(lport), self.rank, self.config.connect_timeout_s), r)
+            except OSError as e:
+                raise TransferError(f"cannot reach receiver {r}'s liveness port {host}:{lport}: {e}") from None
+
+    def _receiver_lost(self, r: int) -> None:
+        """A target worker's process is gone: fail the waits for its keys now."""
+        e = self.epoch + 1
+        self._side.set_error([f"ready/{r}/{e}", f"pulled/{r}/{e}"],
+                             f"receiver {r} left the session (its connection to sender {self.rank} closed)")
+
+    def _close_watch(self) -> None:
+        if getattr(self, "_watch", None) is not None:
+            self._watch.close()
+            self._watch = None
+        if getattr(self, "_side", None) is not None:
+            self._side.close()
+            self._side = None
 
     def _exchange_plan(self, metas: list[dict], assignment: dict, rmetas: dict[int, WeightData]):
         """The split fp8 blocks this sender shares with other senders (``core/splitq.py``),
@@ -445,6 +473,7 @@ class WeightSender:
         self.connect(self.metadata)
 
     def disconnect(self) -> None:
+        self._close_watch()
         self._close_arm_channel()
         self._teardown_multicast()
         for imp in self._imports.values():

@@ -125,35 +125,45 @@ class Session:
 
 
 class Janitor:
-    """Deletes finished handshake keys from a thread of its own, over its own store client, so
-    the deletes (one round trip each) stay off the next sync's critical path."""
+    """A thread with a store client of its own for work that must not wait behind (or block)
+    the main client: deleting finished handshake keys (one round trip each, kept off the next
+    sync's critical path) and publishing errors while the main thread may be blocked in a
+    wait on the same session."""
 
     def __init__(self, host: str, port: int, timeout_s: float, prefix: str = "wbridge"):
         import queue
         import threading
         self._args = (host, port, timeout_s, prefix)
-        self._q: "queue.SimpleQueue[list[str] | None]" = queue.SimpleQueue()
+        self._q: "queue.SimpleQueue[tuple | None]" = queue.SimpleQueue()
         self._thread = threading.Thread(target=self._run, name="wbridge-janitor", daemon=True)
         self._thread.start()
 
     def delete(self, keys: list[str]) -> None:
         if keys:
-            self._q.put(list(keys))
+            self._q.put(("delete", list(keys), None))
+
+    def set_error(self, keys: list[str], message: str) -> None:
+        if keys:
+            self._q.put(("error", list(keys), message))
 
     def _run(self) -> None:
         sess = None
         while True:
-            keys = self._q.get()
-            if keys is None:
+            job = self._q.get()
+            if job is None:
                 return
+            kind, keys, message = job
             try:
                 if sess is None:
                     host, port, timeout_s, prefix = self._args
                     sess = Session(host, port, is_master=False, timeout_s=timeout_s, prefix=prefix)
-                for k in keys:
-                    sess.delete(k)
+                if kind == "delete":
+                    for k in keys:
+                        sess.delete(k)
+                else:
+                    sess.set_error(keys, message)
             except Exception:
-                pass             # the session is gone: nothing left to clean
+                pass             # the session is gone: nothing left to clean or tell
 
     def close(self, timeout_s: float = 2.0) -> None:
         self._q.put(None)
