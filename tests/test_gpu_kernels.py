@@ -195,3 +195,41 @@ def test_repeated_launches_reset_counter():
         assert int(flag.item()) == e
         assert int(prog.counter.item()) == 0
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("etp,dtype", [(4, torch.bfloat16), (8, torch.bfloat16), (4, torch.float32)])
+def test_gpu_split_blocks_match_whole_tensor_oracle(etp, dtype):
+    """fp8 blocks split across senders (expert TP slices of 64 / 32 rows): split_amax on every
+    sender's pieces, the block amax merged over the senders on the host, split_quant plus the
+    transfer kernel; the receiver equals the oracle's quantisation of the whole tensor.  The
+    down_proj pieces (64 / 32 columns) take the element path, gate/up pieces with bf16 sources
+    the vector path."""
+    import numpy as np
+    dev = torch.device("cuda", 0)
+    arch = get_arch("tiny-qwen3-moe")
+    lay = SGLangLayout(arch, tp=1, quant="fp8_experts")
+    rparams = lay.allocate(device=dev, dtype=dtype)
+    rmeta, rviews = lay.to_wb(rparams)
+    rphys = phys_binding(bind(rmeta, rviews))
+    progs, keep = [], []
+    for i in range(etp):
+        meg = MegatronLayout(arch, etp=etp, etp_rank=i)
+        sp = meg.allocate(device=dev, dtype=dtype)
+        keep.append(sp)
+        smeta, sviews = meg.to_wb(sp)
+        t = lower_ops(plan_pair(phys_binding(bind(smeta, sviews)), rphys), ABS, ABS, receiver=0)
+        assert len(t.pieces)
+        progs.append(TransferProgram(t, dev, [], LaunchConfig(mode=MODE_VECTOR)))
+    block = {}
+    partials = [p.piece_amax() for p in progs]
+    for p, part in zip(progs, partials):
+        for k, a in zip(p.tables.piece_keys, part):
+            block[k] = max(block.get(k, 0.0), float(a))
+    for p in progs:
+        p.set_piece_amax(np.array([block[k] for k in p.tables.piece_keys], dtype=np.float32))
+        p.launch(epoch=1, signal=False)
+    torch.cuda.synchronize()
+    assert all(p.read_status() == 0 for p in progs)
+    expected = lay.allocate(device=dev, dtype=dtype, fill=True)
+    for n in rparams:
+        assert torch.equal(_u8(rparams[n]), _u8(expected[n])), n

@@ -171,10 +171,13 @@ class SGLangLayout:
         else:
             params = {n: torch.zeros(s, dtype=dt, device=device) for n, s, dt in specs}
         if fill:
-            self.fill_expected(params, seed)
+            self.fill_expected(params, seed, src_dtype=dtype)
         return params
 
-    def fill_expected(self, params: dict[str, torch.Tensor], seed: int = 0) -> None:
+    def fill_expected(self, params: dict[str, torch.Tensor], seed: int = 0,
+                      src_dtype: torch.dtype = torch.bfloat16) -> None:
+        """Write the synthetic weights; fp8 entries are the block quantisation of the
+        ``src_dtype`` weights a trainer would send."""
         meta, views = self.to_wb(params)
         for name, shards, dtype in meta:
             q = meta.quant(name)
@@ -182,7 +185,7 @@ class SGLangLayout:
                 continue
             box = shards[0]
             if q:
-                src = torch.empty([r - l for l, r, _ in box], dtype=torch.bfloat16, device=views[name].device)
+                src = torch.empty([r - l for l, r, _ in box], dtype=src_dtype, device=views[name].device)
                 synth_fill(src, name, box, seed=seed)
                 qv, sv = block_quant_fp8_ref(src, tuple(q["block"]))
                 views[name].copy_(qv)
