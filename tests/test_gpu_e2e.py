@@ -25,6 +25,14 @@ def test_colocated_ipc_reference_style_late_binding():
         dtype=torch.bfloat16, late=True)
 
 
+def test_colocated_ipc_split_fp8_blocks():
+    """Expert TP 4 (64-row slices): every expert block is split over two senders, which
+    exchange the block amax through the session before their kernels store into the
+    receiver's fp8 weights over CUDA IPC."""
+    run("tiny-qwen3-moe", "gpu_direct", [dict(etp=4, etp_rank=i) for i in range(4)],
+        dict(tp=1, quant="fp8_experts"), device="cuda:0", dtype=torch.bfloat16, n_syncs=2)
+
+
 def test_colocated_ipc_pull_direction():
     """The receiver maps the senders' memory (CUDA IPC) and runs the pull kernel itself."""
     run("tiny-llama", "gpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)], dict(tp=1),
