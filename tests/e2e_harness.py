@@ -63,7 +63,7 @@ def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype, late=Fal
 
 
 def trainer_proc(rank, world, tport, url, q, n_syncs, model, mode, device, layouts, dtype, direction="push",
-                 cfg_extra=None):
+                 cfg_extra=None, trainer="megatron"):
     import torch.distributed as dist
     from weightbridge_b200 import TransferConfig, WeightSender
     from weightbridge_b200.models.arch import get_arch
@@ -72,7 +72,11 @@ def trainer_proc(rank, world, tport, url, q, n_syncs, model, mode, device, layou
         if device != "cpu":
             torch.cuda.set_device(torch.device(device))
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{tport}", rank=rank, world_size=world)
-        lay = MegatronLayout(get_arch(model), **layouts[rank])
+        if trainer == "fsdp":
+            from weightbridge_b200.parallel.fsdp import FSDPLayout
+            lay = FSDPLayout(get_arch(model), **layouts[rank])
+        else:
+            lay = MegatronLayout(get_arch(model), **layouts[rank])
         params = lay.allocate(device=device, dtype=dtype, seed=0)
         meta, views = lay.to_wb(params)
         cfg = TransferConfig(mode=mode, connect_timeout_s=60, sync_timeout_s=60, direction=direction, **(cfg_extra or {}))
@@ -90,7 +94,7 @@ def trainer_proc(rank, world, tport, url, q, n_syncs, model, mode, device, layou
 
 
 def run(model, mode, trainer_layouts, rollout_layout, device="cpu", dtype=torch.float32, n_syncs=3, timeout=240,
-        trainer_devices=None, late=False, direction="push", cfg_extra=None):
+        trainer_devices=None, late=False, direction="push", cfg_extra=None, trainer="megatron"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     hport, tport = _port(), _port()
@@ -100,7 +104,7 @@ def run(model, mode, trainer_layouts, rollout_layout, device="cpu", dtype=torch.
                                                     late, direction, None, cfg_extra))]
     tdev = trainer_devices or [device] * world
     procs += [ctx.Process(target=trainer_proc, args=(r, world, tport, url, q, n_syncs, model, mode, tdev[r],
-                                                      trainer_layouts, dtype, direction, cfg_extra))
+                                                      trainer_layouts, dtype, direction, cfg_extra, trainer))
               for r in range(world)]
     procs[0].start()
     deadline = time.time() + timeout

@@ -1,0 +1,122 @@
+"""FSDP / DTensor trainer layout (parallel/fsdp.py): torch.chunk shard boxes, resharding into
+SGLang layouts (bf16 and fp8 with blocks split across FSDP ranks), DTensor conversion."""
+import multiprocessing as mp
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from weightbridge_b200.core.binding import bind
+from weightbridge_b200.core.plan import lower_ops, phys_binding, plan_pair
+from weightbridge_b200.models.arch import get_arch
+from weightbridge_b200.ops.executor import cpu_execute, cpu_piece_amax
+from weightbridge_b200.parallel.fsdp import FSDPLayout, chunk_rows, shard_box
+from weightbridge_b200.parallel.sglang import SGLangLayout
+
+ABS = lambda _a: 0
+
+
+def _u8(t):
+    return t.view(torch.uint8) if t.dtype == torch.float8_e4m3fn else t
+
+
+@pytest.mark.parametrize("n", [1, 5, 7, 128, 171, 1000])
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_chunk_rows_match_torch_chunk(n, world):
+    parts = torch.arange(n).chunk(world)
+    for r in range(world):
+        l, h = chunk_rows(n, world, r)
+        got = list(range(l, h))
+        want = parts[r].tolist() if r < len(parts) else []
+        assert got == want
+        assert (shard_box((n, 4), world, r) is None) == (not want)
+
+
+def _reshard(world, rollout, dtype):
+    arch = get_arch("tiny-llama-fp8")
+    senders = []
+    for i in range(world):
+        lay = FSDPLayout(arch, world=world, rank=i)
+        p = lay.allocate(dtype=dtype)
+        meta, views = lay.to_wb(p)
+        senders.append((p, phys_binding(bind(meta, views))))
+    out = []
+    for rl in rollout:
+        rp = rl.allocate(dtype=dtype)
+        rmeta, rviews = rl.to_wb(rp)
+        rphys = phys_binding(bind(rmeta, rviews))
+        tables = [lower_ops(plan_pair(sphys, rphys), ABS, ABS, receiver=0) for _p, sphys in senders]
+        block = {}
+        for t in tables:
+            for k, a in zip(t.piece_keys, cpu_piece_amax(t)):
+                block[k] = max(block.get(k, 0.0), float(a))
+        for t in tables:
+            cpu_execute(t, np.array([block[k] for k in t.piece_keys], dtype=np.float32))
+        out.append((rl, rp, sum(len(t.pieces) for t in tables)))
+    return out
+
+
+def test_fsdp_world3_to_sglang_tp2_bf16():
+    arch = get_arch("tiny-llama-fp8")
+    for rl, rp, _n in _reshard(3, [SGLangLayout(arch, tp=2, tp_rank=i) for i in range(2)], torch.bfloat16):
+        exp = rl.allocate(dtype=torch.bfloat16, fill=True)
+        assert all(torch.equal(rp[n], exp[n]) for n in rp)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fsdp_world3_to_sglang_fp8_linear_split_blocks(dtype):
+    """171-row FSDP shards cut the 128-row blocks of every fp8 linear layer."""
+    arch = get_arch("tiny-llama-fp8")
+    (rl, rp, pieces), = _reshard(3, [SGLangLayout(arch, tp=1, quant="fp8_linear")], dtype)
+    assert pieces > 0
+    exp = rl.allocate(dtype=dtype, fill=True)
+    for n in rp:
+        assert torch.equal(_u8(rp[n]), _u8(exp[n])), n
+
+
+def test_fsdp_to_fp8_rollout_over_gloo():
+    """Three FSDP ranks, one fp8_linear rollout worker, through the public API."""
+    from tests.e2e_harness import run
+    run("tiny-llama-fp8", "cpu_direct", [dict(world=3, rank=i) for i in range(3)],
+        dict(tp=1, quant="fp8_linear"), dtype=torch.bfloat16, n_syncs=2, trainer="fsdp")
+
+
+def _dtensor_rank(rank, port, q):
+    import torch.distributed as dist
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import Replicate, Shard, distribute_tensor
+    from weightbridge_b200.parallel.fsdp import convert_to_wb
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2)
+    mesh = init_device_mesh("cpu", (2,))
+    w = torch.arange(20, dtype=torch.float32).view(5, 4)
+    named = {"a.weight": distribute_tensor(w, mesh, [Shard(0)]),
+             "b.weight": distribute_tensor(w.t().contiguous(), mesh, [Shard(1)]),
+             "c.weight": distribute_tensor(w, mesh, [Replicate()]),
+             "d.bias": torch.ones(3)}
+    meta, views = convert_to_wb(named)
+    q.put((rank, {n: meta.shards(n)[0] for n in meta.names()},
+           {n: views[n].tolist() for n in views}))
+    dist.destroy_process_group()
+
+
+def test_dtensor_conversion_two_ranks():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_dtensor_rank, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    got = dict((r, (b, v)) for r, b, v in (q.get(timeout=120) for _ in range(2)))
+    for p in ps:
+        p.join(10)
+    w = torch.arange(20, dtype=torch.float32).view(5, 4)
+    b0, v0 = got[0]
+    b1, v1 = got[1]
+    assert b0["a.weight"] == [(0, 3, 5), (0, 4, 4)] and b1["a.weight"] == [(3, 5, 5), (0, 4, 4)]
+    assert v0["a.weight"] == w[:3].tolist() and v1["a.weight"] == w[3:].tolist()
+    assert b0["b.weight"] == [(0, 4, 4), (0, 3, 5)] and b1["b.weight"] == [(0, 4, 4), (3, 5, 5)]
+    assert b0["c.weight"] == [(0, 5, 5), (0, 4, 4)] == b1["c.weight"]
+    assert b0["d.bias"] == [(0, 3, 3)]

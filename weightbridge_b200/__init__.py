@@ -3,7 +3,7 @@
 Public API (the names of the reference package ``wbridge``, ``wbridge/__init__.py:3-17``):
 ``WeightSender``, ``WeightReceiver``, ``WeightReceiverController``, ``WeightData``,
 ``dtype_str_to_torch``, ``dtype_to_str``; plus ``TransferConfig`` and the layout adapters
-``MegatronLayout`` / ``SGLangLayout``.
+``MegatronLayout`` / ``FSDPLayout`` (trainers) and ``SGLangLayout`` (rollout).
 """
 from .core.shard import (WeightData, check_shard_compatibility, original_total_numel,
                          shards_iterator)
@@ -19,6 +19,9 @@ def __getattr__(name):
     if name == "MegatronLayout":
         from .parallel.megatron import MegatronLayout
         return MegatronLayout
+    if name == "FSDPLayout":
+        from .parallel.fsdp import FSDPLayout
+        return FSDPLayout
     if name in ("SGLangLayout", "VLLMLayout"):
         from .parallel import sglang
         return getattr(sglang, name)
@@ -28,6 +31,6 @@ def __getattr__(name):
 __all__ = [
     "WeightData", "WeightSender", "WeightReceiver", "WeightReceiverController", "TransferConfig",
     "check_shard_compatibility", "shards_iterator", "original_total_numel", "dtype_str_to_torch",
-    "dtype_to_str", "MegatronLayout", "SGLangLayout", "VLLMLayout",
+    "dtype_to_str", "MegatronLayout", "FSDPLayout", "SGLangLayout", "VLLMLayout",
 ]
 __version__ = "0.1.0"

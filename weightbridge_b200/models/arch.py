@@ -141,6 +141,8 @@ PRESETS: dict[str, ModelArch] = {
                                num_experts=128, moe_ffn=768, top_k=8),
     # small test models of every family
     "tiny-qwen2": ModelArch("tiny-qwen2", "qwen2", 2, 128, 4, 2, 32, 256, 512),
+    # head dim and FFN in multiples of 128: every linear layer block-quantisable (fp8_linear)
+    "tiny-llama-fp8": ModelArch("tiny-llama-fp8", "llama", 2, 256, 4, 2, 128, 512, 1024),
     "tiny-qwen3": ModelArch("tiny-qwen3", "qwen3", 2, 128, 8, 2, 32, 256, 520),
     "tiny-qwen3-moe": ModelArch("tiny-qwen3-moe", "qwen3_moe", 2, 256, 4, 2, 64, 0, 1000,
                                 num_experts=8, moe_ffn=256, top_k=2),
