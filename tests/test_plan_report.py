@@ -29,3 +29,8 @@ def test_report_cli_json():
     assert out.returncode == 0, out.stderr[-2000:]
     rep = json.loads(out.stdout)
     assert rep["model"] == "tiny-qwen3" and len(rep["senders"]) == 2
+
+
+def test_report_fsdp_trainer_counts_split_pieces():
+    rep = report("tiny-llama-fp8", {"world": 3}, {"tp": 1, "quant": "fp8_linear"}, trainer_kind="fsdp")
+    assert len(rep["senders"]) == 3 and sum(s["split_pieces"] for s in rep["senders"]) > 0

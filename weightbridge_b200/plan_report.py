@@ -8,7 +8,8 @@ Builds both layouts on the ``meta`` device, runs the source assignment and the p
 every (sender, receiver) pair, and reports per-sender and per-receiver bytes, work rows,
 quantised blocks and split-block pieces, plus the sync time the busiest link allows.  Trainer
 ranks are enumerated as pipeline stage x expert-parallel rank x max(tp, etp) with
-``tp_rank = t % tp`` and ``etp_rank = t % etp``; rollout workers as replica x tp rank.
+``tp_rank = t % tp`` and ``etp_rank = t % etp`` (``--trainer-kind fsdp``: ``world`` ranks of
+an FSDP-sharded model); rollout workers as replica x tp rank.
 The reference has no equivalent (it plans inside ``connect``, ``wbridge/backend/direct_sender.py:74-168``).
 """
 from __future__ import annotations
@@ -38,7 +39,11 @@ def _kv(spec: str) -> dict:
     return out
 
 
-def trainer_layouts(arch, spec: dict) -> list[MegatronLayout]:
+def trainer_layouts(arch, spec: dict, kind: str = "megatron") -> list:
+    if kind == "fsdp":
+        from .parallel.fsdp import FSDPLayout
+        world = int(spec.get("world", 1))
+        return [FSDPLayout(arch, world=world, rank=i, dim=int(spec.get("dim", 0))) for i in range(world)]
     tp, pp, ep, etp = (int(spec.get(k, 1)) for k in ("tp", "pp", "ep", "etp"))
     extra = {k: v for k, v in spec.items() if k not in ("tp", "pp", "ep", "etp")}
     return [MegatronLayout(arch, tp=tp, pp=pp, ep=ep, etp=etp, tp_rank=t % tp, pp_rank=p, ep_rank=e,
@@ -58,9 +63,10 @@ def _meta_binding(lay):
     return meta, phys_binding(bind(meta, views))
 
 
-def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs: float = 770.0) -> dict:
+def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs: float = 770.0,
+           trainer_kind: str = "megatron") -> dict:
     arch = get_arch(model)
-    senders = [_meta_binding(l) for l in trainer_layouts(arch, trainer)]
+    senders = [_meta_binding(l) for l in trainer_layouts(arch, trainer, trainer_kind)]
     receivers = [_meta_binding(l) for l in rollout_layouts(arch, rollout, replicas)]
     smetas = [m for m, _ in senders]
     rmetas = {r: m for r, (m, _) in enumerate(receivers)}
@@ -84,7 +90,7 @@ def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs
     egress = max((r["bytes_written"] for r in srows), default=0)
     inmax = max(ingress, default=0)
     return {
-        "model": model, "trainer": trainer, "rollout": rollout, "replicas": replicas,
+        "model": model, "trainer_kind": trainer_kind, "trainer": trainer, "rollout": rollout, "replicas": replicas,
         "senders": srows,
         "receivers": [{"receiver": r, "ingress_bytes": b,
                        "senders": sorted(s for s, t in plan.items() if t.get(r))} for r, b in enumerate(ingress)],
@@ -104,13 +110,14 @@ def _gb(n: int) -> str:
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--model", required=True)
-    ap.add_argument("--trainer", default="", help="Megatron layout, e.g. tp=2,pp=2 or ep=4,etp=2")
+    ap.add_argument("--trainer", default="", help="Megatron layout, e.g. tp=2,pp=2 or ep=4,etp=2; FSDP: world=8")
+    ap.add_argument("--trainer-kind", default="megatron", choices=["megatron", "fsdp"])
     ap.add_argument("--rollout", default="", help="SGLang layout, e.g. tp=4,moe_ep=4,quant=fp8_experts")
     ap.add_argument("--replicas", type=int, default=1, help="rollout replicas (each with the rollout layout)")
     ap.add_argument("--link-gbs", type=float, default=770.0, help="per-GPU link bandwidth for the estimate")
     ap.add_argument("--json", action="store_true")
     a = ap.parse_args(argv)
-    rep = report(a.model, _kv(a.trainer), _kv(a.rollout), a.replicas, a.link_gbs)
+    rep = report(a.model, _kv(a.trainer), _kv(a.rollout), a.replicas, a.link_gbs, a.trainer_kind)
     if a.json:
         print(json.dumps(rep))
         return 0
