@@ -31,11 +31,13 @@ def test_three_gpus_two_senders_one_receiver():
         dtype=torch.bfloat16, trainer_devices=["cuda:0", "cuda:1"])
 
 
-def test_two_gpus_nccl_wire_mode():
-    """Cross-node capable path: pack kernel -> NCCL send/recv -> unpack kernel."""
+@pytest.mark.parametrize("chunk", [0, 64 << 10])
+def test_two_gpus_nccl_wire_mode(chunk):
+    """Cross-node capable path: pack kernel -> NCCL send/recv -> unpack kernel, as one message
+    per peer (chunk 0) or as many 64 KiB chunks through two buffers per peer."""
     _need(2)
     run("tiny-qwen2", "nccl", [dict(tp=1)], dict(tp=1), device="cuda:1", dtype=torch.bfloat16,
-        trainer_devices=["cuda:0"])
+        trainer_devices=["cuda:0"], cfg_extra={"wire_chunk_bytes": chunk})
 
 
 def _leaving_trainer(tport, url, q):
