@@ -11,6 +11,7 @@ Process layout (the shape of a real RL job, without Ray):
     python examples/single_node.py --device cpu                 # gloo payload path, any machine
     python examples/single_node.py --device cuda                # CUDA IPC + sm_100a kernel, colocated on GPU 0
     python examples/single_node.py --device cuda --disaggregated  # trainers and workers on different GPUs
+    python examples/single_node.py --trainer fsdp --trainers 3    # an FSDP-sharded trainer instead
 
 Weights are synthetic (the tiny Llama-style model by default); every worker checks after
 each update that it holds exactly the trainer's weights of that step.
@@ -99,7 +100,11 @@ def trainer(args, rank: int, dist_port: int, url: str, results):
         torch.cuda.set_device(torch.device(dev))
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{dist_port}", rank=rank,
                             world_size=args.trainers)
-    lay = MegatronLayout(get_arch(args.model), tp=args.trainers, tp_rank=rank)
+    if args.trainer == "fsdp":              # FSDP2 / DTensor trainer: Shard(0) rows per rank
+        from weightbridge_b200 import FSDPLayout
+        lay = FSDPLayout(get_arch(args.model), world=args.trainers, rank=rank)
+    else:
+        lay = MegatronLayout(get_arch(args.model), tp=args.trainers, tp_rank=rank)
     params = lay.allocate(device=dev, dtype=args.dtype, seed=0)
     meta, views = lay.to_wb(params)          # HF-named boxes bound to views of the params
     sender = WeightSender(args.mode, [url], config=TransferConfig(mode=args.mode))
@@ -119,6 +124,8 @@ def main(argv=None):
     p.add_argument("--disaggregated", action="store_true")
     p.add_argument("--model", default="tiny-llama")
     p.add_argument("--trainers", type=int, default=2)
+    p.add_argument("--trainer", default="megatron", choices=["megatron", "fsdp"],
+                   help="trainer layout: Megatron TP over the trainer ranks, or FSDP rows")
     p.add_argument("--workers", type=int, default=1)
     p.add_argument("--steps", type=int, default=3)
     args = p.parse_args(argv)

@@ -13,6 +13,14 @@ def test_single_node_example_cpu():
     assert "all syncs verified" in out.stdout
 
 
+def test_single_node_example_fsdp_trainer_cpu():
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "examples", "single_node.py"), "--device", "cpu",
+                          "--steps", "2", "--workers", "2", "--trainers", "3", "--trainer", "fsdp"],
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-3000:]
+    assert "all syncs verified" in out.stdout
+
+
 def test_raw_shards_example_cpu():
     """The reference example's scenario: uneven row split, column split and a duplicated
     tensor on two trainer ranks, two rollout workers holding row halves in flat buffers."""
