@@ -283,3 +283,32 @@ def test_sglang_fp8_qkv_rejects_a_kv_part_inside_a_block():
     lay = SGLangLayout(arch, tp=1, quant="fp8_linear")
     with pytest.raises(ValueError, match="inside an fp8 block"):
         lay.to_wb(lay.allocate(dtype=torch.bfloat16, fill=False))
+
+
+def test_megatron_virtual_pipeline_chunks_cover_the_model_once():
+    """PP 2 x VPP 2 (interleaved schedule): chunk v of stage p holds the (v * 2 + p)-th quarter
+    of the layers; all chunks of all stages resharded into one SGLang rank give the model."""
+    from weightbridge_b200.core.plan import lower_ops, phys_binding, plan_pair
+    from weightbridge_b200.models.arch import get_arch
+    from weightbridge_b200.ops.executor import cpu_execute
+    from weightbridge_b200.parallel.megatron import MegatronLayout
+    from weightbridge_b200.parallel.sglang import SGLangLayout
+    arch = get_arch("tiny-llama").with_(num_layers=4)
+    seen = []
+    rl = SGLangLayout(arch, tp=1)
+    rp = rl.allocate(dtype=torch.float32)
+    rmeta, rviews = rl.to_wb(rp)
+    rphys = phys_binding(bind(rmeta, rviews))
+    keep = []
+    for pp_rank in range(2):
+        for lay in MegatronLayout(arch, pp=2, pp_rank=pp_rank, vpp=2).chunks():
+            p = lay.allocate(dtype=torch.float32)
+            keep.append(p)
+            meta, views = lay.to_wb(p)
+            seen += meta.names()
+            cpu_execute(lower_ops(plan_pair(phys_binding(bind(meta, views)), rphys), lambda a: 0, lambda a: 0))
+    assert len(seen) == len(set(seen)) == len(arch.hf_tensors())
+    layers = {pp: MegatronLayout(arch, pp=2, pp_rank=pp, vpp=2).chunks() for pp in range(2)}
+    assert [c.layer_offset for c in layers[0]] == [0, 2] and [c.layer_offset for c in layers[1]] == [1, 3]
+    exp = rl.allocate(dtype=torch.float32, fill=True)
+    assert all(torch.equal(rp[n], exp[n]) for n in exp)

@@ -1,6 +1,7 @@
 """Megatron-Core trainer layout -> logical HF boxes bound to strided views of the params.
 
-Covers TP (column/row parallel), PP (layer offset per stage), EP and expert-TP for MoE,
+Covers TP (column/row parallel), PP (layer offset per stage, virtual pipeline chunks of the
+interleaved schedule), EP and expert-TP for MoE,
 grouped-interleaved fused QKV (``[G, q_per_group + 2, head_dim, H]`` per rank), fused
 ``linear_fc1`` (``[gate; up]`` per rank), QKV bias, q/k layernorm and vocab-parallel
 embedding/output layer with vocab padding.
@@ -44,6 +45,8 @@ class MegatronLayout:
     vocab_pad_multiple: int = 128          # Megatron's make_vocab_size_divisible_by
     layers_per_stage: tuple[int, ...] | None = None
     expert_naming: str = "grouped"         # grouped: experts.linear_fc1.weight{e}; sequential: local_experts.{e}.
+    vpp: int = 1                           # virtual pipeline (interleaved schedule): model chunks per stage
+    vpp_rank: int = 0                      # the model chunk this layout describes
 
     def __post_init__(self):
         a = self.arch
@@ -55,6 +58,13 @@ class MegatronLayout:
             raise ValueError("ffn not divisible by TP")
         if a.is_moe and (a.num_experts % self.ep or a.moe_ffn % self.etp):
             raise ValueError("experts not divisible by EP (or expert FFN by ETP)")
+        if self.vpp > 1:
+            even = tuple([a.num_layers // self.pp] * self.pp)
+            if a.num_layers % (self.pp * self.vpp) or self.layers_per_stage not in (None, even):
+                raise ValueError("virtual pipeline stages need num_layers divisible by PP x VPP "
+                                 "(and even stages)")
+            if not 0 <= self.vpp_rank < self.vpp:
+                raise ValueError("vpp_rank out of range")
         if self.layers_per_stage is None:
             if a.num_layers % self.pp:
                 raise ValueError("num_layers not divisible by PP; pass layers_per_stage")
@@ -70,19 +80,28 @@ class MegatronLayout:
 
     @property
     def layer_offset(self) -> int:
+        if self.vpp > 1:       # chunk v of stage p: the (v * PP + p)-th run of L / (PP * VPP) layers
+            return (self.vpp_rank * self.pp + self.pp_rank) * self.num_local_layers
         return sum(self.layers_per_stage[: self.pp_rank])
 
     @property
     def num_local_layers(self) -> int:
+        if self.vpp > 1:
+            return self.arch.num_layers // (self.pp * self.vpp)
         return self.layers_per_stage[self.pp_rank]
 
     @property
     def first_stage(self) -> bool:
-        return self.pp_rank == 0
+        return self.pp_rank == 0 and self.vpp_rank == 0
 
     @property
     def last_stage(self) -> bool:
-        return self.pp_rank == self.pp - 1
+        return self.pp_rank == self.pp - 1 and self.vpp_rank == self.vpp - 1
+
+    def chunks(self) -> list["MegatronLayout"]:
+        """The layouts of every model chunk this rank holds (one without virtual pipeline)."""
+        from dataclasses import replace
+        return [replace(self, vpp_rank=v) for v in range(self.vpp)]
 
     def param_shapes(self) -> dict[str, tuple[int, ...]]:
         """Megatron parameter name (local layer numbering) -> local shape."""
@@ -246,10 +265,11 @@ class MegatronLayout:
 
 def convert_to_wb(args: Any, model_name: str, named_tensors, *, tp_rank: int | None = None,
                   tp_size: int | None = None, pp_rank: int = 0, pp_size: int = 1,
-                  ep_rank: int = 0, ep_size: int = 1, quantization_config=None
-                  ) -> tuple[WeightData, dict[str, torch.Tensor]]:
+                  ep_rank: int = 0, ep_size: int = 1, vpp_rank: int = 0, vpp_size: int = 1,
+                  quantization_config=None) -> tuple[WeightData, dict[str, torch.Tensor]]:
     """Megatron ``args`` + named params -> (WeightData, views); the reference's entry point
-    (``wbridge/utils/megatron_utils/__init__.py:11-19``) with explicit parallel ranks.
+    (``wbridge/utils/megatron_utils/__init__.py:11-19``) with explicit parallel ranks.  With
+    the interleaved schedule, call it once per model chunk (``vpp_rank``) and merge.
     When ranks are omitted they are read from ``megatron.core.mpu`` if it is importable."""
     if tp_rank is None or tp_size is None:
         try:
@@ -259,6 +279,8 @@ def convert_to_wb(args: Any, model_name: str, named_tensors, *, tp_rank: int | N
         tp_rank, tp_size = mpu.get_tensor_model_parallel_rank(), mpu.get_tensor_model_parallel_world_size()
         pp_rank, pp_size = mpu.get_pipeline_model_parallel_rank(), mpu.get_pipeline_model_parallel_world_size()
         ep_rank, ep_size = mpu.get_expert_model_parallel_rank(), mpu.get_expert_model_parallel_world_size()
+        vpp_size = mpu.get_virtual_pipeline_model_parallel_world_size() or 1
+        vpp_rank = (mpu.get_virtual_pipeline_model_parallel_rank() or 0) if vpp_size > 1 else 0
     name = model_name.lower()
     family = ("qwen3_moe" if "moe" in name else "qwen3" if "qwen3" in name else
               "qwen2" if "qwen2" in name else "llama" if "llama" in name else None)
@@ -266,6 +288,6 @@ def convert_to_wb(args: Any, model_name: str, named_tensors, *, tp_rank: int | N
         raise ValueError(f"unsupported model for convert_to_wb: {model_name}")
     arch = ModelArch.from_megatron_args(args, family=family, name=model_name)
     layout = MegatronLayout(arch, tp=tp_size, pp=pp_size, ep=ep_size, tp_rank=tp_rank,
-                            pp_rank=pp_rank, ep_rank=ep_rank,
+                            pp_rank=pp_rank, ep_rank=ep_rank, vpp=vpp_size, vpp_rank=vpp_rank,
                             vocab_pad_multiple=int(getattr(args, "make_vocab_size_divisible_by", 128)))
     return layout.to_wb(named_tensors)
