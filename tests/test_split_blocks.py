@@ -116,3 +116,28 @@ def test_split_blocks_expert_tp4_to_tp1_fp8_gloo():
     from tests.e2e_harness import run
     run("tiny-qwen3-moe", "cpu_direct", [dict(etp=4, etp_rank=i) for i in range(4)],
         dict(tp=1, quant="fp8_experts"), dtype=torch.bfloat16, n_syncs=2)
+
+
+@settings(max_examples=12, deadline=None)
+@given(world=st.integers(1, 7), tp=st.sampled_from([1, 2]), dim=st.sampled_from([0, 1]),
+       f32=st.booleans())
+def test_split_blocks_random_fsdp_shardings(world, tp, dim, f32):
+    """Random FSDP-style shardings (any world size, rows or columns) into fp8 SGLang ranks:
+    whole blocks, split blocks and their exchange reproduce the oracle bit for bit."""
+    from weightbridge_b200.parallel.fsdp import FSDPLayout
+    dtype = torch.float32 if f32 else torch.bfloat16
+    arch = get_arch("tiny-llama-fp8")
+    senders = make_senders([FSDPLayout(arch, world=world, rank=i, dim=dim) for i in range(world)], dtype)
+    for r in range(tp):
+        lay = SGLangLayout(arch, tp=tp, tp_rank=r, quant="fp8_linear")
+        params, _rmeta, rphys = make_receiver(lay, dtype)
+        tables = [lower_ops(plan_pair(sphys, rphys), ABS, ABS, receiver=r) for _p, _m, sphys in senders]
+        block: dict = {}
+        for t in tables:
+            for k, a in zip(t.piece_keys, cpu_piece_amax(t)):
+                block[k] = max(block.get(k, 0.0), float(a))
+        for t in tables:
+            cpu_execute(t, np.array([block[k] for k in t.piece_keys], dtype=np.float32))
+        expected = lay.allocate(dtype=dtype, fill=True)
+        for n in params:
+            assert torch.equal(_u8(params[n]), _u8(expected[n])), (n, world, tp, dim)

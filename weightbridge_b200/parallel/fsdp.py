@@ -29,8 +29,11 @@ def chunk_rows(n: int, world: int, rank: int) -> tuple[int, int]:
 
 
 def shard_box(shape: tuple[int, ...], world: int, rank: int, dim: int = 0) -> list[tuple[int, int, int]] | None:
-    """Box of ``rank``'s shard of a tensor of ``shape`` sharded on ``dim`` (None: empty shard)."""
+    """Box of ``rank``'s shard of a tensor of ``shape`` sharded on ``dim`` (None: empty shard);
+    a tensor with fewer dimensions is sharded on dim 0."""
     box = [(0, d, d) for d in shape]
+    if dim >= len(shape):
+        dim = 0
     if world > 1 and shape:
         l, r = chunk_rows(shape[dim], world, rank)
         if l >= r:
