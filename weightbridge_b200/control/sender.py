@@ -5,16 +5,19 @@ connect (once, or to reshard):
   2. sender rank 0 queries ``/wbridge/metadata`` of every rollout URL, hosts the session
      store (OS-chosen port), computes the load-balanced source assignment and the plan
      digest of every (sender, receiver) pair, and POSTs ``/wbridge/connect``;
-  3. every sender joins the store, reads the receivers' exported memory tables and opens
-     the CUDA IPC handles of the receivers it writes to.
+  3. every sender joins the store, reads the receivers' exported memory tables, opens
+     the CUDA IPC handles of the receivers it writes to and a liveness connection to each;
+     rank 0 connects its arm channel to every worker.
 send (each sync):
-  1. rank 0 POSTs ``/wbridge/receive`` (arms the workers; the schedulers call
-     ``request_update`` when they can take new weights);
+  1. rank 0 arms the workers: one ZMQ message each (``arm="direct"``) or a POST of
+     ``/wbridge/receive`` per rollout server (``arm="http"``); the schedulers call
+     ``request_update`` when they can take new weights;
   2. the first send binds the state_dict, compiles the plan against the receivers'
      addresses and uploads the work tables; later sends reuse them;
-  3. wait for every target's ``ready`` key, launch ONE transfer kernel (peer stores +
-     fused layout transform / fp8 quantisation + epoch flags), wait for it, publish
-     ``done`` with the kernel's status.
+  3. wait for every target's ``ready`` key; senders sharing split fp8 blocks exchange the
+     blocks' amax; launch ONE transfer kernel (peer stores + fused layout transform / fp8
+     quantisation + epoch flags), wait for it, publish ``done`` with the kernel's status.
+     The wire modes pack and send chunk by chunk instead (``control/wires.py``).
 
 Parity: ``wbridge/frontend/sender.py:7-26`` and ``wbridge/backend/direct_sender.py:16-211``
 (``transfer_mode`` ``gpu_direct`` / ``cpu_direct``, rank-0 HTTP control, dedup).  The
