@@ -49,6 +49,8 @@ class WireSet:
         ws = WireSet(device)
         for r, names in sorted(targets.items()):
             chunks = wire_chunks(overlaps[r], cfg.wire_chunk_bytes)
+            if not chunks:
+                continue
             bufs = ws._buffers(chunks)
             items = []
             for k, ov in enumerate(chunks):
@@ -68,6 +70,8 @@ class WireSet:
         ws = WireSet(device)
         for s, ov_all in sorted(overlaps.items()):
             chunks = wire_chunks(ov_all, chunk_bytes)
+            if not chunks:
+                continue
             bufs = ws._buffers(chunks)
             items = []
             for k, ov in enumerate(chunks):
