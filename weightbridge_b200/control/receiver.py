@@ -52,6 +52,16 @@ class ReceiveError(RuntimeError):
 
 
 class WeightReceiver:
+    """One rollout worker's side of the weight sync (one per GPU worker process).
+
+    ``controller_ipc_name``: ``WeightReceiverController.ipc_name`` of the rollout server;
+    ``rank``: the worker's index among the controller's ``worker_num`` workers;
+    ``metadata``: the worker's shards as logical HF boxes; ``state_dict``: the tensors (or
+    views into fused parameters) the senders write into, bound at connect, or ``None`` to
+    hand them over at the first ``request_update``; ``device`` defaults to the tensors'.
+    The scheduler calls ``request_update(timeout=...)`` between batches.
+    """
+
     def __init__(self, controller_ipc_name: str, rank: int, metadata: WeightData,
                  state_dict: dict[str, Any] | None = None, device: torch.device | int | str | None = None,
                  config: TransferConfig | None = None):

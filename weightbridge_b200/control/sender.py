@@ -118,6 +118,19 @@ def _get_with_retry(http, url: str, timeout_s: float):
 
 
 class WeightSender:
+    """One trainer rank's side of the weight sync.
+
+    ``transfer_mode``: ``gpu_direct`` (aliases ``p2p``, ``ipc``), ``nvls``, ``nccl`` or
+    ``cpu_direct`` (``cpu``, ``gloo``).  ``receiver_urls``: the rollout servers hosting a
+    ``WeightReceiverController``.  ``group``: the trainer process group whose ranks all send
+    (default: the default group, or a single sender without torch.distributed).  ``config``:
+    a ``TransferConfig`` (default: from ``WBRIDGE_*`` environment variables).
+
+    Every rank calls ``connect(metadata)`` once and ``send(state_dict)`` after each update;
+    ``metadata`` describes the rank's shards as logical HF boxes and ``state_dict`` holds
+    tensors or views of them (``MegatronLayout.to_wb`` / ``FSDPLayout.to_wb`` give both).
+    """
+
     def __init__(self, transfer_mode: str, receiver_urls: list[str], group: Any = None,
                  config: TransferConfig | None = None):
         self.transfer_mode = transfer_mode
