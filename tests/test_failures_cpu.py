@@ -355,12 +355,14 @@ def test_both_arm_channels_sync(mode, arm):
             lay.fill(params, seed=step)
             th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
             th.start()
-            st = s.send(views)
+            st = s.send(views, version=100 + step)
             th.join(20)
             assert st.epoch == step + 1
+            assert ro.recv.weights_version == 100 + step          # the tag travels with the weights
             exp = ro.lay.allocate(dtype=torch.float32, fill=True, seed=step)
             assert all(torch.equal(ro.params[n], exp[n]) for n in exp), step
-        assert ro.ctl.get_stats()[0]["epoch"] == 3
+        stats = ro.ctl.get_stats()[0]
+        assert stats["epoch"] == 3 and stats["weights_version"] == 102
         # a repeated arm of the pending epoch is harmless
         if arm == "direct":
             s._arm(4)

@@ -77,6 +77,7 @@ class WeightReceiver:
         self._started = threading.Event()
         self.stats: deque = deque(maxlen=64)
         self.epoch = 0
+        self.weights_version: int | None = None       # the tag of the last weights received (send(version=))
         self.session: Session | None = None
         self._pending_update: dict | None = None
         self._garbage: list[str] = []
@@ -255,7 +256,8 @@ class WeightReceiver:
             self._reply(sock, data, {"status": "ack"})
         elif t == STATS_REQUEST:
             self._reply(sock, data, {"rank": self.rank, "state": self._state.value, "epoch": self.epoch,
-                                     "error": self._error, "syncs": list(self.stats)})
+                                     "weights_version": self.weights_version, "error": self._error,
+                                     "syncs": list(self.stats)})
         elif t == STOP_REQUEST:
             self._reply(sock, data, {"status": "ack"})
             self._stop.set()
@@ -486,6 +488,10 @@ class WeightReceiver:
                 self._stream.synchronize()
             else:
                 ws.recv(self._pg, epoch)
+            try:
+                version = int(sess.wait_checked([f"ver/{epoch}"], self.config.sync_timeout_s)[0])
+            except (SessionTimeout, PeerError) as e:
+                raise ReceiveError(str(e)) from None
         else:
             sess.set(f"ready/{gr}/{epoch}", "1")
             keys = [f"done/{s}/{gr}/{epoch}" for s in self.expected]
@@ -494,11 +500,12 @@ class WeightReceiver:
                                          what=f"senders {self.expected} to finish epoch {epoch}")
             except (SessionTimeout, PeerError) as e:
                 raise ReceiveError(str(e)) from None
-            done = [v.decode().split(":") for v in vals]          # status:binding-version:pushed
+            done = [v.decode().split(":") for v in vals]          # status:binding-version:pushed:tag
             bad = {s: int(d[0]) for s, d in zip(self.expected, done) if int(d[0])}
             if bad:
                 raise ReceiveError(f"senders reported kernel status {bad} for epoch {epoch}")
             pushed = [s for s, d in zip(self.expected, done) if len(d) < 3 or d[2] == "1"]
+            version = max((int(d[3]) for d in done if len(d) > 3), default=-1)
             if self.direction == "pull":
                 self._pull(epoch, {s: int(d[1]) for s, d in zip(self.expected, done)})
             if self.config.verify_flags and pushed:
@@ -511,8 +518,9 @@ class WeightReceiver:
             if epoch > 1:
                 self._garbage.append(f"ready/{gr}/{epoch - 1}")
         self.epoch = epoch
-        return {"epoch": epoch, "host_ms": (time.perf_counter() - t0) * 1e3, "bytes": self.expected_bytes,
-                "senders": self.expected}
+        self.weights_version = None if version < 0 else version
+        return {"epoch": epoch, "version": self.weights_version, "host_ms": (time.perf_counter() - t0) * 1e3,
+                "bytes": self.expected_bytes, "senders": self.expected}
 
     # -- pull direction --------------------------------------------------------------------
     def _pull(self, epoch: int, versions: dict[int, int]) -> None:

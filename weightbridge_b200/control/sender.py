@@ -705,20 +705,25 @@ class WeightSender:
                 keys.append(f"amax/{self.rank}/{epoch}")
             self.session.set_error(keys, f"sender {self.rank}: {message}")
 
-    def send(self, state_dict: dict[str, Any]) -> SyncStats:
+    def send(self, state_dict: dict[str, Any], version: int | None = None) -> SyncStats:
         """One full sync: arm the rollout side, wait until every target receiver is ready,
-        launch the transfer kernel, wait for it and report completion.  NVTX ranges mark
-        the phases (``wbridge.send/arm``, ``/ready``, ``/transfer``)."""
+        launch the transfer kernel, wait for it and report completion.  ``version`` (e.g. the
+        training step) tags the weights: workers report it as ``weights_version``.  NVTX
+        ranges mark the phases (``wbridge.send/arm``, ``/ready``, ``/transfer``)."""
         with nvtx_range("wbridge.send"):
-            return self._send(state_dict)
+            return self._send(state_dict, -1 if version is None else int(version))
 
-    def _send(self, state_dict: dict[str, Any]) -> SyncStats:
+    def _send(self, state_dict: dict[str, Any], version: int = -1) -> SyncStats:
         if not self.connected or self.metadata is None:
             raise RuntimeError("WeightSender.send requires connect() first")
         cfg = self.config
         t0 = time.perf_counter()
         epoch = self.epoch + 1
         sess = self.session
+        if self.rank == 0 and cfg.mode in WIRE_MODES:     # no done keys there: the tag has its own
+            sess.set(f"ver/{epoch}", str(version))
+            if epoch > 16:
+                sess.delete(f"ver/{epoch - 16}")
         arm = self._arm(epoch) if self.rank == 0 else None
         st = SyncStats(epoch=epoch, receivers=sorted(self.targets), link_gbs=cfg.link_gbs)
         t1 = time.perf_counter()
@@ -791,7 +796,7 @@ class WeightSender:
                 torch.cuda.current_stream().synchronize()   # the receivers pull: parameters must be final
             if prog is not None:
                 st.bytes_read, st.bytes_written = prog.bytes_read, prog.bytes_written
-            done = f"{st.status}:{self._bind_version}:{int(pushed)}"
+            done = f"{st.status}:{self._bind_version}:{int(pushed)}:{version}"
             sess.multi_set([f"done/{self.rank}/{r}/{epoch}" for r in self.targets], [done] * len(self.targets))
             if st.status:
                 prog.clear_status()
