@@ -495,3 +495,44 @@ def test_orderly_disconnect_is_not_a_loss():
         assert watch.lost == []
     finally:
         ro.close()
+
+
+def test_partial_sync_of_named_entries():
+    """send(names=...) moves only those entries (here: layer 0); the rest keeps the previous
+    weights.  Alternating partial and full syncs reuses both compiled programs."""
+    cfg = _cfg(mode="gpu_direct")
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender("gpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        compiles = []
+        orig = s._compile
+        s._compile = lambda sd, sub=None: (compiles.append(sub), orig(sd, sub))[1]
+
+        def sync(**kw):
+            th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+            th.start()
+            s.send(views, **kw)
+            th.join(20)
+
+        sync()                                                   # everything at seed 0
+        lay.fill(params, seed=1)
+        layer0 = [n for n in meta.names() if n.startswith("model.layers.0.")]
+        sync(names=layer0)
+        exp0 = ro.lay.allocate(dtype=torch.float32, fill=True, seed=0)
+        exp1 = ro.lay.allocate(dtype=torch.float32, fill=True, seed=1)
+        # SGLang parameters of layer 0 (fused qkv / gate_up included) hold seed 1, the rest seed 0
+        for n in exp0:
+            want = exp1 if n.startswith("model.layers.0.") else exp0
+            assert torch.equal(ro.params[n], want[n]), n
+        lay.fill(params, seed=2)
+        sync()
+        sync(names=layer0)
+        exp2 = ro.lay.allocate(dtype=torch.float32, fill=True, seed=2)
+        assert all(torch.equal(ro.params[n], exp2[n]) for n in exp2)
+        assert len(compiles) == 2                               # full + layer 0, each once
+        with pytest.raises(ValueError):
+            WeightSender("cpu_direct", [ro.url], config=_cfg(mode="cpu_direct")).send(views, names=layer0)
+    finally:
+        ro.close()

@@ -34,7 +34,7 @@ import time
 import uuid
 from dataclasses import dataclass, field
 from datetime import timedelta
-from typing import Any
+from typing import Any, Iterable
 
 import numpy as np
 import torch
@@ -152,6 +152,7 @@ class WeightSender:
         self.history: list[SyncStats] = []
         self._program = None
         self._program_key = None
+        self._progs: dict[tuple, tuple] = {}        # compiled programs by (bound tensors, entry subset)
         self._imports: dict[int, Any] = {}
         self._rinfo: dict[int, dict] = {}
         self._ops_cache: dict[tuple, list] = {}     # plan ops per (receiver, bindings, names)
@@ -236,6 +237,7 @@ class WeightSender:
         self.epoch = 0
         self._program = None
         self._program_key = None
+        self._progs = {}
         self.connected = True
         logger.info("sender %d connected: %d receiver targets, mode=%s", self.rank, len(self.targets), cfg.mode)
 
@@ -500,7 +502,8 @@ class WeightSender:
         self.connected = False
 
     # -- send ----------------------------------------------------------------------------------
-    def _compile(self, state_dict) -> None:
+    def _compile(self, state_dict, subset: frozenset | None = None) -> None:
+        """Compile the push program for ``state_dict`` (entries restricted to ``subset``)."""
         cfg = self.config
         if not self.targets:
             self._program = None
@@ -518,7 +521,7 @@ class WeightSender:
         for m, g in (getattr(self, "_mc", {}) or {}).values():
             reps = g["replicas"]
             rep = reps[0]
-            names = self.targets[rep]
+            names = [n for n in self.targets[rep] if subset is None or n in subset]
             rphys = PhysBinding.from_json(self._rinfo[rep]["binding"])
             ops = plan_pair(sphys, rphys, names=names)
             mc_base = lambda a, va=m.va: va
@@ -537,6 +540,8 @@ class WeightSender:
         for r, names in sorted(self.targets.items()):
             if r in covered:
                 continue
+            if subset is not None:
+                names = [n for n in names if n in subset]
             info = self._rinfo[r]
             imp = self._imports[r]
             ckey = (r, _digest(info["binding"]), skey, tuple(names))
@@ -610,6 +615,23 @@ class WeightSender:
             self._stream = torch.cuda.Stream(dev)
             self._ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
 
+    def _select(self, state_dict, subset: frozenset | None) -> None:
+        """Make the program for (bound tensors, entry subset) current, compiling it on first
+        use; the last few stay compiled, so alternating full and partial syncs do not
+        recompile."""
+        key = (self._key(state_dict), subset)
+        if key == self._program_key:
+            return
+        hit = self._progs.pop(key, None)
+        if hit is None:
+            self._compile(state_dict, subset)
+            hit = (self._program, self._piece_pos)
+        self._progs[key] = hit
+        while len(self._progs) > 4:
+            self._progs.pop(next(iter(self._progs)))
+        self._program, self._piece_pos = hit
+        self._program_key = key
+
     def _positions(self, tables: Tables) -> np.ndarray:
         if not len(tables.pieces):
             return np.zeros(0, dtype=np.int64)
@@ -639,10 +661,7 @@ class WeightSender:
             raise RuntimeError("launch() stores into receiver memory; wire modes use send()")
         if any(info.get("late") and r not in self._imports for r, info in self._rinfo.items()):
             raise RuntimeError("launch() needs every receiver's memory; run one send() first")
-        key = self._key(state_dict)
-        if self._program_key != key:
-            self._compile(state_dict)
-            self._program_key = key
+        self._select(state_dict, None)
         if self._program is not None and len(self._program.tables):
             if self._program.device.type == "cpu":
                 self._program.launch(0, signal=False)
@@ -705,15 +724,22 @@ class WeightSender:
                 keys.append(f"amax/{self.rank}/{epoch}")
             self.session.set_error(keys, f"sender {self.rank}: {message}")
 
-    def send(self, state_dict: dict[str, Any], version: int | None = None) -> SyncStats:
+    def send(self, state_dict: dict[str, Any], version: int | None = None,
+             names: Iterable[str] | None = None) -> SyncStats:
         """One full sync: arm the rollout side, wait until every target receiver is ready,
         launch the transfer kernel, wait for it and report completion.  ``version`` (e.g. the
-        training step) tags the weights: workers report it as ``weights_version``.  NVTX
+        training step) tags the weights: workers report it as ``weights_version``.  ``names``
+        restricts the sync to those HF entries (e.g. skip frozen layers); every sender rank
+        must pass the same set (push direction of ``gpu_direct`` and ``nvls`` only).  NVTX
         ranges mark the phases (``wbridge.send/arm``, ``/ready``, ``/transfer``)."""
+        subset = None if names is None else frozenset(names)
+        if subset is not None and (self.config.mode in WIRE_MODES or self.config.direction == "pull"):
+            raise ValueError("names= needs the push direction of gpu_direct or nvls: the wire modes and "
+                             "pulling receivers move every entry they expect")
         with nvtx_range("wbridge.send"):
-            return self._send(state_dict, -1 if version is None else int(version))
+            return self._send(state_dict, -1 if version is None else int(version), subset)
 
-    def _send(self, state_dict: dict[str, Any], version: int = -1) -> SyncStats:
+    def _send(self, state_dict: dict[str, Any], version: int = -1, subset: frozenset | None = None) -> SyncStats:
         if not self.connected or self.metadata is None:
             raise RuntimeError("WeightSender.send requires connect() first")
         cfg = self.config
@@ -741,12 +767,16 @@ class WeightSender:
             self._fail_epoch(epoch, self._arm_error)
             raise TransferError(self._arm_error)
         try:
-            key = self._key(state_dict)
-            if cfg.mode not in WIRE_MODES and self._resolve_late():
-                self._program_key = None
-            if self._program_key != key:
-                (self._compile_wire if cfg.mode in WIRE_MODES else self._compile)(state_dict)
-                self._program_key = key
+            if cfg.mode in WIRE_MODES:
+                key = (self._key(state_dict), None)
+                if self._program_key != key:
+                    self._compile_wire(state_dict)
+                    self._program_key = key
+            else:
+                if self._resolve_late():
+                    self._progs.clear()
+                    self._program_key = None
+                self._select(state_dict, subset)
         except Exception as e:
             self._fail_epoch(epoch, f"{type(e).__name__}: {e}")
             raise
