@@ -12,13 +12,15 @@ Configurations (strong scaling: the model, hence the bytes moved per sync, is fi
                      N=2: TP1 -> 1 replica, N=4: PP2 -> 2 replicas
   qwen3-moe-fp8      Qwen3-30B-A3B, trainer EP4 -> rollout TP4 (EP4 experts), experts quantised
                      to fp8 e4m3 with 128x128 fp32 block scales in the transfer kernel (N=8)
+  qwen3-moe-fp8-etp  the same with trainer expert TP 4 instead of EP (192-row expert slices): every
+                     expert fp8 block is split over two senders, which exchange its amax (N=8)
   llama70b-colocated Llama-3-70B, trainer TP8 on GPUs 0-7 -> two rollout replicas at TP4 in
                      separate processes on GPUs 0-3 and 4-7 (N=8, 16 processes)
 
 Two timed phases, both after W warm-up syncs through the public API:
   value: K back-to-back transfer launches per sender (WeightSender.launch) bracketed by CUDA
          events on the transfer stream, barrier + synchronize on both sides, max over ranks;
-  e2e:   K full syncs through the public API (HTTP arm, ready/done handshake, epoch H2D from
+  e2e:   K full syncs through the public API (arm message, ready/done handshake, epoch H2D from
          pinned memory, kernel, status / flag words D2H), wall clock, max over ranks.
 Inputs are larger than L2 (GBs per sync), so no L2 flush is needed between iterations.
 """
@@ -45,7 +47,8 @@ def parse(argv=None):
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--config", default="llama8b",
-                   choices=["llama8b", "llama8b-fanout", "qwen3-moe-fp8", "llama70b-colocated"])
+                   choices=["llama8b", "llama8b-fanout", "qwen3-moe-fp8", "qwen3-moe-fp8-etp",
+                            "llama70b-colocated"])
     p.add_argument("--impl", default="wbridge", choices=["wbridge", "reference", "torch-p2p"],
                    help="torch-p2p: the reference's algorithm (per-box torch copies + NCCL isend/irecv)")
     p.add_argument("--mode", type=int, default=None, help="kernel mode: 0 vector, 1/2/3 TMA bulk")
@@ -134,6 +137,14 @@ def scenario(config: str, n: int) -> tuple[str, list[Role], str]:
         roles += [Role("rollout", t + i, dict(tp=t, tp_rank=i, moe_ep=t, quant="fp8_experts"), 0, i, i == 0)
                   for i in range(t)]
         return "qwen3-30b-a3b", roles, f"ep{t}->tp{t} (ep{t} experts, fp8 e4m3 128x128 blocks)"
+    if config == "qwen3-moe-fp8-etp":
+        if n not in (4, 8):
+            raise SystemExit("qwen3-moe-fp8-etp runs on 4 or 8 GPUs")
+        t = n // 2
+        roles = [Role("trainer", i, dict(etp=t, etp_rank=i)) for i in range(t)]
+        roles += [Role("rollout", t + i, dict(tp=t, tp_rank=i, moe_ep=t, quant="fp8_experts"), 0, i, i == 0)
+                  for i in range(t)]
+        return "qwen3-30b-a3b", roles, f"etp{t}->tp{t} (expert slices of {768 // t} rows: split fp8 blocks)"
     if config == "llama70b-colocated":
         if n != 8:
             raise SystemExit("llama70b-colocated runs on 8 GPUs")
@@ -379,7 +390,8 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     hist = sender.history[-args.steps:] if (sender is not None and not args.no_e2e) else []
     avg = lambda f: sum(getattr(h, f) for h in hist) / len(hist) if hist else 0.0
     stats = torch.tensor([my_ms, e2e_ms, payload, read, ok, h2d, d2h, active, items, grid, setup_s, kmode,
-                          avg("wait_ready_ms"), avg("device_ms"), avg("host_ms")], dtype=torch.float64)
+                          avg("wait_ready_ms"), avg("device_ms"), avg("host_ms"), avg("exchange_ms")],
+                         dtype=torch.float64)
     gathered = [torch.zeros_like(stats) for _ in range(nprocs)]
     dist.all_gather(gathered, stats)
     G = torch.stack(gathered)
@@ -417,7 +429,8 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                 "path": "WeightSender.send + WeightReceiver.request_update (HTTP arm, store handshake, IPC peer stores)",
                 "sender_breakdown_ms": {"wait_ready": round(float(G[:, 12].max()), 3),
                                         "transfer_kernel": round(float(G[:, 13].max()), 3),
-                                        "send_total": round(float(G[:, 14].max()), 3)}},
+                                        "send_total": round(float(G[:, 14].max()), 3),
+                                        "split_block_exchange": round(float(G[:, 15].max()), 3)}},
             "gpu_launches": int(args.steps * G[:, 7].sum()),
             "clocks": clk.summary() if clk else None,
             "verified": bool(G[:, 4].min() == 1) if not args.no_verify else None,
