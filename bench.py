@@ -380,6 +380,9 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     read = sender.program.bytes_read if (sender is not None and sender.program is not None) else 0
     active = 1 if (sender is not None and sender.program is not None and len(sender.program.tables)) else 0
     active += 1 if (recv is not None and recv.pull_program is not None and len(recv.pull_program.tables)) else 0
+    # kernels per timed launch: the transfer kernel, plus the split-block quantiser when there are pieces
+    kernels = active + (1 if (sender is not None and sender.program is not None
+                              and getattr(sender.program, "n_pieces", 0)) else 0)
     pushed = 1 if (sender is not None and sender.program is not None and len(sender.program.tables)) else 0
     pulled = 1 if (recv is not None and recv.pull_program is not None and len(recv.pull_program.tables)) else 0
     h2d = 8 * pushed                                  # the epoch word, from pinned memory
@@ -390,7 +393,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     hist = sender.history[-args.steps:] if (sender is not None and not args.no_e2e) else []
     avg = lambda f: sum(getattr(h, f) for h in hist) / len(hist) if hist else 0.0
     stats = torch.tensor([my_ms, e2e_ms, payload, read, ok, h2d, d2h, active, items, grid, setup_s, kmode,
-                          avg("wait_ready_ms"), avg("device_ms"), avg("host_ms"), avg("exchange_ms")],
+                          avg("wait_ready_ms"), avg("device_ms"), avg("host_ms"), avg("exchange_ms"), kernels],
                          dtype=torch.float64)
     gathered = [torch.zeros_like(stats) for _ in range(nprocs)]
     dist.all_gather(gathered, stats)
@@ -431,7 +434,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                                         "transfer_kernel": round(float(G[:, 13].max()), 3),
                                         "send_total": round(float(G[:, 14].max()), 3),
                                         "split_block_exchange": round(float(G[:, 15].max()), 3)}},
-            "gpu_launches": int(args.steps * G[:, 7].sum()),
+            "gpu_launches": int(args.steps * G[:, 16].sum()),
             "clocks": clk.summary() if clk else None,
             "verified": bool(G[:, 4].min() == 1) if not args.no_verify else None,
             "setup_s": round(float(G[:, 10].max()), 1),
