@@ -387,6 +387,9 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     pulled = 1 if (recv is not None and recv.pull_program is not None and len(recv.pull_program.tables)) else 0
     h2d = 8 * pushed                                  # the epoch word, from pinned memory
     d2h = 4 * (pushed + pulled) + (int(recv.flags.nbytes) if recv is not None and cfg.verify_flags else 0)
+    npieces = getattr(sender.program, "n_pieces", 0) if (sender is not None and sender.program is not None) else 0
+    h2d += 4 * npieces                                # split blocks: the exchanged amax of every piece
+    d2h += 4 * npieces                                # ... and each piece's own amax, read back first
     items = len(sender.program.tables.items) if (sender is not None and sender.program is not None) else 0
     grid = sender.program.grid() if (sender is not None and sender.program is not None) else 0
     kmode = sender.program.config.mode if (sender is not None and sender.program is not None) else -1
