@@ -1,0 +1,66 @@
+"""The benchmark's configurations are valid on CPU: every (config, N) builds its layouts
+(on the meta device), the assignment covers every rollout worker's entries exactly, and the
+devices and engines are consistent; the roofline arithmetic and the reference arm's line."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+import bench  # noqa: E402
+
+from weightbridge_b200 import WeightData  # noqa: E402
+from weightbridge_b200.control.assign import assign_sources, restrict  # noqa: E402
+from weightbridge_b200.models.arch import get_arch  # noqa: E402
+from weightbridge_b200.parallel.megatron import MegatronLayout  # noqa: E402
+from weightbridge_b200.parallel.sglang import SGLangLayout  # noqa: E402
+
+CASES = [("llama8b", 1), ("llama8b", 2), ("llama8b", 4), ("llama8b", 8), ("llama8b-fanout", 8),
+         ("qwen3-moe-fp8", 8), ("qwen3-moe-fp8-etp", 8), ("llama70b-colocated", 8)]
+
+
+def _meta(lay):
+    return lay.to_wb(lay.allocate(device="meta", dtype=torch.bfloat16, fill=False))[0]
+
+
+@pytest.mark.parametrize("config,n", CASES)
+def test_bench_scenario_is_consistent(config, n):
+    model, roles, desc = bench.scenario(config, n)
+    arch = get_arch(model)
+    assert all(0 <= r.device < n for r in roles) and {r.device for r in roles} == set(range(n))
+    hosts = [r for r in roles if r.kind == "rollout" and r.host]
+    assert {r.engine for r in hosts} == {r.engine for r in roles if r.kind == "rollout"}
+    smetas = [_meta(MegatronLayout(arch, **r.layout)) for r in roles if r.kind == "trainer"]
+    rmetas = {i: _meta(SGLangLayout(arch, **r.layout)) for i, r in enumerate(roles) if r.kind == "rollout"}
+    plan = assign_sources(smetas, rmetas)
+    for r, meta in rmetas.items():
+        # every element of every (non-scale) entry arrives from exactly one sender
+        weights = [n for n in meta.names() if (meta.quant(n) or {}).get("role") != "scale"]
+        got = 0
+        for s, targets in plan.items():
+            names = targets.get(r, [])
+            if names:
+                ov = WeightData.compute_overlap(restrict(smetas[s], names), meta)
+                got += sum(b - a for a, b, n, _sh, _dt in ov.iter_with_intv() if n in names)
+        want = sum(b - a for a, b, n, _sh, _dt in meta.iter_with_intv() if n in weights)
+        assert got == want, (config, n, r, got, want)
+
+
+def test_roofline_fractions():
+    rf = bench._roofline(1540.0, 2.0, colocated=False, bytes_read=7.7e9, payload=7.7e9, ms=5.0)
+    assert rf["bound"].startswith("nvlink") and rf["fraction_of_measured"] == 1.0
+    hbm = bench._measured_peaks().get("hbm_gbs", 6650.0)
+    rf = bench._roofline(0.0, 1.0, colocated=True, bytes_read=hbm * 1e9 / 2, payload=hbm * 1e9 / 2, ms=1000.0)
+    assert rf["bound"].startswith("hbm") and rf["fraction_of_measured"] == 1.0
+
+
+def test_reference_arm_prints_one_json_line():
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference"],
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and ("unavailable" in line or "value" in line)
