@@ -8,10 +8,10 @@
 // the block writes the same value).  The arithmetic matches the transfer kernel's quant
 // path: scale = amax / 448 (IEEE division), inv = RN(1 / scale), q = satfinite_e4m3(x * inv).
 //
-// One CTA per piece.  A piece 128 columns wide with 16-bit source and 16-byte aligned rows
-// (an expert-TP slice cutting block rows) takes the vector path of the transfer kernel's quant
-// blocks: 8 threads span a row, 32-byte loads, one 16-byte store per row; other pieces go
-// element by element.  Nothing waits on another kernel or rank.
+// One CTA per piece.  A piece with 16-bit source, a multiple of 16 columns and 16-byte aligned
+// rows (expert-TP or FSDP slices cutting block rows or columns) takes the vector path of the
+// transfer kernel's quant blocks: cols / 16 threads span a row, 32-byte loads, 16-byte stores;
+// other pieces go element by element.  Nothing waits on another kernel or rank.
 #include "wb_splitq.h"
 
 #include <cuda_bf16.h>
@@ -44,9 +44,10 @@ __device__ __forceinline__ void st16(void* p, uint4 v) {
   asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
 }
 
-// The vector path: 16-bit source, 128 columns, 16-byte aligned rows on both sides.
+// The vector path: 16-bit source, a multiple of 16 columns (at most 128), 16-byte aligned rows
+// on both sides.  cols / 16 threads span a row (32 source bytes, 16 e4m3 bytes each).
 __device__ __forceinline__ bool vec_ok(const SplitPiece& p) {
-  return (p.src_code == DT_BF16 || p.src_code == DT_F16) && p.cols == 128 && p.rows <= 128 &&
+  return (p.src_code == DT_BF16 || p.src_code == DT_F16) && p.cols % 16 == 0 && p.cols >= 16 && p.cols <= 128 &&
          ((p.src | p.dst | (uint64_t)p.src_pitch | (uint64_t)p.dst_pitch) & 15) == 0;
 }
 
@@ -108,10 +109,13 @@ __global__ void __launch_bounds__(kThreads) split_amax_kernel(const SplitPiece* 
     float m = 0.f;
     if (vec_ok(p)) {
       const bool bf16 = p.src_code == DT_BF16;
-      const uint32_t col = threadIdx.x & 7;
-      for (uint32_t r = threadIdx.x >> 3; r < p.rows; r += kThreads / 8) {
-        const uint8_t* q = src + (int64_t)r * p.src_pitch + col * 32u;
-        m = fmaxf(m, fmaxf(amax8(ld16(q), bf16), amax8(ld16(q + 16), bf16)));
+      const uint32_t tpr = p.cols / 16, rpp = kThreads / tpr;    // threads per row, rows per pass
+      if (threadIdx.x < tpr * rpp) {
+        const uint32_t col = threadIdx.x % tpr;
+        for (uint32_t r = threadIdx.x / tpr; r < p.rows; r += rpp) {
+          const uint8_t* q = src + (int64_t)r * p.src_pitch + col * 32u;
+          m = fmaxf(m, fmaxf(amax8(ld16(q), bf16), amax8(ld16(q + 16), bf16)));
+        }
       }
     } else {
       const uint32_t total = es ? p.rows * p.cols : 0u;
@@ -138,11 +142,14 @@ __global__ void __launch_bounds__(kThreads) split_quant_kernel(const SplitPiece*
     uint8_t* dst = reinterpret_cast<uint8_t*>(p.dst);
     if (vec_ok(p)) {
       const bool bf16 = p.src_code == DT_BF16;
-      const uint32_t col = threadIdx.x & 7;
-      for (uint32_t r = threadIdx.x >> 3; r < p.rows; r += kThreads / 8) {
-        const uint8_t* q = src + (int64_t)r * p.src_pitch + col * 32u;
-        const uint2 lo = quant8(ld16(q), bf16, inv), hi = quant8(ld16(q + 16), bf16, inv);
-        st16(dst + (int64_t)r * p.dst_pitch + col * 16u, make_uint4(lo.x, lo.y, hi.x, hi.y));
+      const uint32_t tpr = p.cols / 16, rpp = kThreads / tpr;
+      if (threadIdx.x < tpr * rpp) {
+        const uint32_t col = threadIdx.x % tpr;
+        for (uint32_t r = threadIdx.x / tpr; r < p.rows; r += rpp) {
+          const uint8_t* q = src + (int64_t)r * p.src_pitch + col * 32u;
+          const uint2 lo = quant8(ld16(q), bf16, inv), hi = quant8(ld16(q + 16), bf16, inv);
+          st16(dst + (int64_t)r * p.dst_pitch + col * 16u, make_uint4(lo.x, lo.y, hi.x, hi.y));
+        }
       }
     } else {
       const uint32_t total = p.rows * p.cols;
