@@ -192,3 +192,15 @@ def test_multicast_lowering_rules():
            (0, 0), [1, 1], (128, 128))
     with pytest.raises(ValueError):
         lower_ops([q], lambda x: 0, lambda x: 0, multicast=True)
+
+
+def test_data_ptrs_key_detects_rebinding():
+    """The sender's binding key: equal for the same tensors, different when a tensor (or a
+    view inside a multi-shard list) is replaced."""
+    from weightbridge_b200.ops._ext import ext
+    a, b, c = torch.zeros(4), torch.zeros(4), torch.zeros(4)
+    k1 = ext().data_ptrs([a, [a, b]])
+    assert k1 == ext().data_ptrs([a, [a, b]])
+    assert k1 != ext().data_ptrs([a, [a, c]])
+    assert k1 != ext().data_ptrs([a, [a], b])
+    assert len(ext().data_ptrs([None, a[1:]])) == 16

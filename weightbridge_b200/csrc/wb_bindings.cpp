@@ -5,6 +5,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cstring>
 #include <stdexcept>
 #include <string>
 
@@ -86,6 +87,27 @@ void cpu_split_quant(uint64_t pieces, size_t n, uint64_t amax) {
   wb::cpu_split_quant(P<const wb::SplitPiece>(pieces), n, P<const float>(amax));
 }
 
+// Data pointers of a list of tensors (lists / tuples of tensors flattened in order) as one
+// bytes object, 8 bytes each and 0 for anything else: the sender's cheap exact check that a
+// state_dict still holds the tensors its plan was compiled for.
+void append_ptrs(const py::handle& h, std::string& out, int depth) {
+  uint64_t p = 0;
+  if (THPVariable_Check(h.ptr())) {
+    p = reinterpret_cast<uint64_t>(THPVariable_Unpack(h.ptr()).data_ptr());
+  } else if (depth == 0 && (py::isinstance<py::list>(h) || py::isinstance<py::tuple>(h))) {
+    for (const auto& e : py::reinterpret_borrow<py::sequence>(h)) append_ptrs(e, out, 1);
+    p = ~uint64_t(0);  // end of a list
+  }
+  out.append(reinterpret_cast<const char*>(&p), 8);
+}
+
+py::bytes data_ptrs(const py::list& tensors) {
+  std::string out;
+  out.reserve(tensors.size() * 8);
+  for (const auto& h : tensors) append_ptrs(h, out, 0);
+  return py::bytes(out);
+}
+
 int num_sms(int device) {
   int v = 0;
   check(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device), "cudaDeviceGetAttribute");
@@ -107,6 +129,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cpu_split_amax", &cpu_split_amax, "per-piece amax of split fp8 blocks on the host");
   m.def("cpu_split_quant", &cpu_split_quant, "quantise split fp8 block pieces on the host");
   m.def("num_sms", &num_sms);
+  m.def("data_ptrs", &data_ptrs, "data pointers of a list of tensors, 8 bytes each");
   m.def("addr_range", [](uint64_t p) {
     auto r = wb::addr_range(p);
     return py::make_tuple(r.base, r.size);
