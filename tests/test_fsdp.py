@@ -120,3 +120,43 @@ def test_dtensor_conversion_two_ranks():
     assert b0["b.weight"] == [(0, 4, 4), (0, 3, 5)] and b1["b.weight"] == [(0, 4, 4), (3, 5, 5)]
     assert b0["c.weight"] == [(0, 5, 5), (0, 4, 4)] == b1["c.weight"]
     assert b0["d.bias"] == [(0, 3, 3)]
+
+
+def _dtensor_2d_rank(rank, port, q):
+    import torch.distributed as dist
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import Replicate, Shard, distribute_tensor
+    from weightbridge_b200.parallel.fsdp import convert_to_wb
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=4)
+    mesh = init_device_mesh("cpu", (2, 2))
+    w = torch.arange(7 * 6, dtype=torch.float32).view(7, 6)
+    named = {"hsdp": distribute_tensor(w, mesh, [Replicate(), Shard(0)]),
+             "two_dims": distribute_tensor(w, mesh, [Shard(0), Shard(1)]),
+             "nested": distribute_tensor(w, mesh, [Shard(0), Shard(0)])}
+    meta, views = convert_to_wb(named)
+    out = {}
+    for n in meta.names():
+        box = meta.shards(n)[0]
+        out[n] = (box, torch.equal(views[n], w[tuple(slice(l, r) for l, r, _ in box)]))
+    q.put((rank, out))
+    dist.destroy_process_group()
+
+
+def test_dtensor_conversion_2d_mesh():
+    """(Replicate, Shard(0)), (Shard(0), Shard(1)) and nested (Shard(0), Shard(0)) on a 2 x 2
+    mesh: every rank's box selects exactly its local tensor."""
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_dtensor_2d_rank, args=(r, port, q)) for r in range(4)]
+    for p in ps:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(4))
+    for p in ps:
+        p.join(10)
+    for r, out in got.items():
+        assert all(ok for _box, ok in out.values()), (r, out)
+    # nested: rows 0-3 split 2-2 within the first mesh row, rows 4-6 split 2-1 in the second
+    assert sorted(got[r]["nested"][0][0] for r in range(4)) == [(0, 2, 7), (2, 4, 7), (4, 6, 7), (6, 7, 7)]

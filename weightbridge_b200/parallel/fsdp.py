@@ -80,7 +80,8 @@ class FSDPLayout:
 def convert_to_wb(named_tensors: Iterable[tuple[str, Any]] | dict[str, Any]
                   ) -> tuple[WeightData, dict[str, torch.Tensor]]:
     """Metadata and local views of HF-named trainer tensors: ``DTensor``s with ``Shard(d)`` /
-    ``Replicate`` placements (one mesh dimension), or plain tensors (the whole tensor)."""
+    ``Replicate`` placements on any number of mesh dimensions (FSDP2, HSDP, FSDP x TP), or
+    plain tensors (the whole tensor)."""
     items = named_tensors.items() if isinstance(named_tensors, dict) else named_tensors
     meta, views = {}, {}
     for name, t in items:
@@ -93,25 +94,30 @@ def convert_to_wb(named_tensors: Iterable[tuple[str, Any]] | dict[str, Any]
 
 
 def _local_and_box(t):
+    """A DTensor's local tensor and its box: placements apply in mesh-dimension order, each
+    ``Shard(d)`` cutting the current extent of tensor dim ``d`` like ``torch.chunk`` (HSDP is
+    ``(Replicate(), Shard(0))``, 2-D FSDP x TP e.g. ``(Shard(0), Shard(1))``)."""
     try:
         from torch.distributed.tensor import DTensor, Replicate, Shard
     except ImportError:              # torch without DTensor: plain tensors only
         DTensor = None
     if DTensor is None or not isinstance(t, DTensor):
         return t, [(0, d, d) for d in t.shape]
-    if len(t.placements) != 1:
-        raise ValueError("only one-dimensional device meshes are supported")
-    p = t.placements[0]
     mesh = t.device_mesh
+    coord = mesh.get_coordinate()
     local = t.to_local()
-    shape = tuple(t.shape)
-    if isinstance(p, Replicate):
-        return local, [(0, d, d) for d in shape]
-    if isinstance(p, Shard):
-        box = shard_box(shape, mesh.size(), mesh.get_local_rank(), p.dim)
-        if box is None:
+    box = [[0, d, d] for d in t.shape]
+    for i, p in enumerate(t.placements):
+        if isinstance(p, Replicate):
+            continue
+        if type(p) is not Shard:     # _StridedShard and partial placements: not a plain box
+            raise ValueError(f"unsupported placement {p} (plain Shard / Replicate only)")
+        l, r, w = box[p.dim]
+        a, b = chunk_rows(r - l, mesh.size(i), coord[i])
+        if a >= b:
             return local, None
-        if tuple(local.shape) != tuple(r - l for l, r, _w in box):
-            raise ValueError(f"DTensor local shape {tuple(local.shape)} is not torch.chunk's shard {box}")
-        return local, box
-    raise ValueError(f"unsupported placement {p}")
+        box[p.dim] = [l + a, l + b, w]
+    box = [tuple(x) for x in box]
+    if tuple(local.shape) != tuple(r - l for l, r, _w in box):
+        raise ValueError(f"DTensor local shape {tuple(local.shape)} does not match its shard {box}")
+    return local, box
