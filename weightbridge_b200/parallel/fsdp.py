@@ -80,8 +80,9 @@ class FSDPLayout:
 def convert_to_wb(named_tensors: Iterable[tuple[str, Any]] | dict[str, Any]
                   ) -> tuple[WeightData, dict[str, torch.Tensor]]:
     """Metadata and local views of HF-named trainer tensors: ``DTensor``s with ``Shard(d)`` /
-    ``Replicate`` placements on any number of mesh dimensions (FSDP2, HSDP, FSDP x TP), or
-    plain tensors (the whole tensor)."""
+    ``Replicate`` placements on any number of mesh dimensions (FSDP2, HSDP, FSDP x TP on
+    different tensor dims; the strided shards of FSDP x TP on one dim are refused), or plain
+    tensors (the whole tensor)."""
     items = named_tensors.items() if isinstance(named_tensors, dict) else named_tensors
     meta, views = {}, {}
     for name, t in items:
