@@ -130,21 +130,26 @@ def _dtensor_2d_rank(rank, port, q):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=4)
     mesh = init_device_mesh("cpu", (2, 2))
     w = torch.arange(7 * 6, dtype=torch.float32).view(7, 6)
+    from torch.distributed.tensor.placement_types import _StridedShard
+    w8 = torch.arange(8 * 6, dtype=torch.float32).view(8, 6)
     named = {"hsdp": distribute_tensor(w, mesh, [Replicate(), Shard(0)]),
              "two_dims": distribute_tensor(w, mesh, [Shard(0), Shard(1)]),
-             "nested": distribute_tensor(w, mesh, [Shard(0), Shard(0)])}
+             "nested": distribute_tensor(w, mesh, [Shard(0), Shard(0)]),
+             "fsdp_on_tp": distribute_tensor(w8, mesh, [_StridedShard(0, split_factor=2), Shard(0)])}
     meta, views = convert_to_wb(named)
     out = {}
     for n in meta.names():
         box = meta.shards(n)[0]
-        out[n] = (box, torch.equal(views[n], w[tuple(slice(l, r) for l, r, _ in box)]))
+        ref = w8 if n == "fsdp_on_tp" else w
+        out[n] = (box, torch.equal(views[n], ref[tuple(slice(l, r) for l, r, _ in box)]))
     q.put((rank, out))
     dist.destroy_process_group()
 
 
 def test_dtensor_conversion_2d_mesh():
-    """(Replicate, Shard(0)), (Shard(0), Shard(1)) and nested (Shard(0), Shard(0)) on a 2 x 2
-    mesh: every rank's box selects exactly its local tensor."""
+    """(Replicate, Shard(0)), (Shard(0), Shard(1)), nested (Shard(0), Shard(0)) and FSDP's
+    (_StridedShard(0), Shard(0)) on a 2 x 2 mesh: every rank's box selects exactly its local
+    tensor."""
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
@@ -160,3 +165,5 @@ def test_dtensor_conversion_2d_mesh():
         assert all(ok for _box, ok in out.values()), (r, out)
     # nested: rows 0-3 split 2-2 within the first mesh row, rows 4-6 split 2-1 in the second
     assert sorted(got[r]["nested"][0][0] for r in range(4)) == [(0, 2, 7), (2, 4, 7), (4, 6, 7), (6, 7, 7)]
+    # FSDP (strided, mesh dim 0) on top of TP (mesh dim 1): TP halves first, then FSDP halves
+    assert got[1]["fsdp_on_tp"][0][0] == (4, 6, 8) and got[2]["fsdp_on_tp"][0][0] == (2, 4, 8)

@@ -80,9 +80,8 @@ class FSDPLayout:
 def convert_to_wb(named_tensors: Iterable[tuple[str, Any]] | dict[str, Any]
                   ) -> tuple[WeightData, dict[str, torch.Tensor]]:
     """Metadata and local views of HF-named trainer tensors: ``DTensor``s with ``Shard(d)`` /
-    ``Replicate`` placements on any number of mesh dimensions (FSDP2, HSDP, FSDP x TP on
-    different tensor dims; the strided shards of FSDP x TP on one dim are refused), or plain
-    tensors (the whole tensor)."""
+    ``Replicate`` placements on any number of mesh dimensions (FSDP2, HSDP, FSDP x TP,
+    including FSDP's strided shards on top of TP), or plain tensors (the whole tensor)."""
     items = named_tensors.items() if isinstance(named_tensors, dict) else named_tensors
     meta, views = {}, {}
     for name, t in items:
@@ -95,9 +94,10 @@ def convert_to_wb(named_tensors: Iterable[tuple[str, Any]] | dict[str, Any]
 
 
 def _local_and_box(t):
-    """A DTensor's local tensor and its box: placements apply in mesh-dimension order, each
-    ``Shard(d)`` cutting the current extent of tensor dim ``d`` like ``torch.chunk`` (HSDP is
-    ``(Replicate(), Shard(0))``, 2-D FSDP x TP e.g. ``(Shard(0), Shard(1))``)."""
+    """A DTensor's local tensor and its box.  Plain ``Shard(d)`` placements apply in
+    mesh-dimension order, each cutting the current extent of tensor dim ``d`` like
+    ``torch.chunk``; ``_StridedShard`` placements (FSDP2 on top of TP on the same dim) cut the
+    chunk the plain shards left, after them.  HSDP is ``(Replicate(), Shard(0))``."""
     try:
         from torch.distributed.tensor import DTensor, Replicate, Shard
     except ImportError:              # torch without DTensor: plain tensors only
@@ -108,11 +108,24 @@ def _local_and_box(t):
     coord = mesh.get_coordinate()
     local = t.to_local()
     box = [[0, d, d] for d in t.shape]
+    plain, strided = [], []
     for i, p in enumerate(t.placements):
         if isinstance(p, Replicate):
             continue
-        if type(p) is not Shard:     # _StridedShard and partial placements: not a plain box
-            raise ValueError(f"unsupported placement {p} (plain Shard / Replicate only)")
+        if type(p) is Shard:
+            plain.append((i, p))
+        elif type(p).__name__ == "_StridedShard":
+            strided.append((i, p))
+        else:
+            raise ValueError(f"unsupported placement {p} (Shard / Replicate / _StridedShard only)")
+    for i, p in strided:
+        inner = 1
+        for j, q in plain:
+            if q.dim == p.dim:
+                inner *= mesh.size(j)
+        if getattr(p, "split_factor", inner) != inner:
+            raise ValueError(f"{p}: split factor {p.split_factor} is not the {inner} plain shards of dim {p.dim}")
+    for i, p in plain + strided:
         l, r, w = box[p.dim]
         a, b = chunk_rows(r - l, mesh.size(i), coord[i])
         if a >= b:
