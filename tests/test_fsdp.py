@@ -123,6 +123,14 @@ def test_dtensor_conversion_two_ranks():
 
 
 def _dtensor_2d_rank(rank, port, q):
+    try:
+        _dtensor_2d_body(rank, port, q)
+    except Exception:
+        import traceback
+        q.put((rank, {"error": (None, traceback.format_exc())}))
+
+
+def _dtensor_2d_body(rank, port, q):
     import torch.distributed as dist
     from torch.distributed.device_mesh import init_device_mesh
     from torch.distributed.tensor import Replicate, Shard, distribute_tensor
@@ -162,6 +170,7 @@ def test_dtensor_conversion_2d_mesh():
     for p in ps:
         p.join(10)
     for r, out in got.items():
+        assert "error" not in out, out.get("error")
         assert all(ok for _box, ok in out.values()), (r, out)
     # nested: rows 0-3 split 2-2 within the first mesh row, rows 4-6 split 2-1 in the second
     assert sorted(got[r]["nested"][0][0] for r in range(4)) == [(0, 2, 7), (2, 4, 7), (4, 6, 7), (6, 7, 7)]
