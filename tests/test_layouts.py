@@ -312,3 +312,15 @@ def test_megatron_virtual_pipeline_chunks_cover_the_model_once():
     assert [c.layer_offset for c in layers[0]] == [0, 2] and [c.layer_offset for c in layers[1]] == [1, 3]
     exp = rl.allocate(dtype=torch.float32, fill=True)
     assert all(torch.equal(rp[n], exp[n]) for n in exp)
+
+
+def test_megatron_to_wb_strict_and_lenient():
+    from weightbridge_b200.models.arch import get_arch
+    from weightbridge_b200.parallel.megatron import MegatronLayout, UnknownParameter
+    lay = MegatronLayout(get_arch("tiny-llama"))
+    params = lay.allocate(dtype=torch.float32, fill=False)
+    params["decoder.layers.0.self_attention.linear_qkv.lora_A.weight"] = torch.zeros(8, 256)
+    with pytest.raises(UnknownParameter):
+        lay.to_wb(params)
+    meta, views = lay.to_wb(params, strict=False)
+    assert len(meta.names()) == len(get_arch("tiny-llama").hf_tensors())

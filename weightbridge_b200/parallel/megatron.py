@@ -25,6 +25,10 @@ from ..models.arch import ModelArch
 from ..models.synthetic import synth_fill
 
 
+class UnknownParameter(ValueError):
+    """A parameter name without a HuggingFace counterpart in this layout."""
+
+
 def _strip(name: str) -> str:
     while name.startswith("module."):
         name = name[len("module."):]
@@ -183,7 +187,7 @@ class MegatronLayout:
 
         m = re.match(r"decoder\.layers\.(\d+)\.(.+)", n)
         if not m:
-            raise ValueError(f"unknown Megatron parameter {name!r}")
+            raise UnknownParameter(f"unknown Megatron parameter {name!r}")
         li = int(m.group(1))
         rest = m.group(2)
         g = li + self.layer_offset
@@ -247,17 +251,24 @@ class MegatronLayout:
                 return [(q + "gate_proj.weight", param[:i_loc], [ibox, (0, H, H)]),
                         (q + "up_proj.weight", param[i_loc:], [ibox, (0, H, H)])]
             return [(q + "down_proj.weight", param, [(0, H, H), ibox])]
-        raise ValueError(f"unknown Megatron parameter {name!r}")
+        raise UnknownParameter(f"unknown Megatron parameter {name!r}")
 
-    def to_wb(self, named_params: dict[str, torch.Tensor] | Iterable[tuple[str, torch.Tensor]]
-              ) -> tuple[WeightData, dict[str, torch.Tensor]]:
-        """(metadata, HF name -> strided view) for this rank's parameters."""
+    def to_wb(self, named_params: dict[str, torch.Tensor] | Iterable[tuple[str, torch.Tensor]],
+              strict: bool = True) -> tuple[WeightData, dict[str, torch.Tensor]]:
+        """(metadata, HF name -> strided view) for this rank's parameters.  ``strict=False``
+        skips parameters without an HF counterpart (adapters, extra heads) instead of raising."""
         items = named_params.items() if isinstance(named_params, dict) else named_params
         meta: dict[str, dict[str, Any]] = {}
         views: dict[str, torch.Tensor] = {}
         for name, param in items:
             t = param.data if isinstance(param, torch.nn.Parameter) else param
-            for hf, view, box in self.split_param(name, t):
+            try:
+                parts = self.split_param(name, t)
+            except UnknownParameter:
+                if strict:
+                    raise
+                continue
+            for hf, view, box in parts:
                 meta[hf] = {"shard": box, "dtype": view.dtype}
                 views[hf] = view
         return WeightData(meta), views
