@@ -26,6 +26,7 @@ from ..core.shard import WeightData
 from ..models.arch import ModelArch
 from ..models.synthetic import synth_fill
 from ..ops.quant_ref import block_quant_fp8_ref
+from .megatron import UnknownParameter
 
 SKIP_PATTERNS = ("inv_freq", "cos_cached", "sin_cached", "projector", "vision_tower")
 
@@ -229,7 +230,7 @@ class SGLangLayout:
             return [(name, param, full(param.shape), None)]
         m = re.match(r"model\.layers\.(\d+)\.(.+)", name)
         if not m:
-            raise ValueError(f"unknown SGLang parameter {name!r}")
+            raise UnknownParameter(f"unknown SGLang parameter {name!r}")
         p = f"model.layers.{m.group(1)}."
         rest = m.group(2)
         q_loc = a.num_heads // self.attn_tp * hd
@@ -303,9 +304,10 @@ class SGLangLayout:
         # replicated tensors: norms, router, q/k norm
         return [(name, param, full(param.shape), None)]
 
-    def to_wb(self, params: dict[str, torch.Tensor]) -> tuple[WeightData, dict[str, torch.Tensor]]:
+    def to_wb(self, params: dict[str, torch.Tensor], strict: bool = True) -> tuple[WeightData, dict[str, torch.Tensor]]:
         """(metadata, HF name -> view) for this rank's SGLang parameters.  fp8 entries carry
-        ``quant`` and their scale views appear as ``<name>_scale_inv`` entries."""
+        ``quant`` and their scale views appear as ``<name>_scale_inv`` entries.
+        ``strict=False`` skips parameters this layout does not know instead of raising."""
         meta: dict[str, dict[str, Any]] = {}
         views: dict[str, torch.Tensor] = {}
         for name, param in params.items():
@@ -315,7 +317,13 @@ class SGLangLayout:
                 continue
             t = param.data if isinstance(param, torch.nn.Parameter) else param
             scale = params.get(name + "_scale_inv")
-            for hf, view, box, q in self.split_param(name, t, scale):
+            try:
+                parts = self.split_param(name, t, scale)
+            except UnknownParameter:
+                if strict:
+                    raise
+                continue
+            for hf, view, box, q in parts:
                 entry = {"shard": box, "dtype": view.dtype}
                 if q:
                     entry["quant"] = q
