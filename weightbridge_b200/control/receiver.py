@@ -479,6 +479,10 @@ class WeightReceiver:
         t0 = time.perf_counter()
         if not self._bound:
             self._late_bind()
+        if self.device.type == "cuda":
+            # the engine's last batch may still be running on its streams, reading these
+            # parameters: only an idle device may be written by the senders
+            torch.cuda.synchronize(self.device)
         if self.mode in WIRE_MODES:
             sess.set(f"ready/{gr}/{epoch}", "1")
             ws = self._wires
