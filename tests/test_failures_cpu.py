@@ -536,3 +536,23 @@ def test_partial_sync_of_named_entries():
             WeightSender("cpu_direct", [ro.url], config=_cfg(mode="cpu_direct")).send(views, names=layer0)
     finally:
         ro.close()
+
+
+def test_auto_transfer_mode_picks_cpu_direct_for_host_tensors():
+    """transfer_mode="auto": rank 0 picks the mode from where the tensors live (here: host
+    tensors, so cpu_direct) and every rank uses it."""
+    cfg = _cfg(mode="cpu_direct")
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender("auto", [ro.url], config=_cfg(mode="auto"))
+        s.connect(meta)
+        assert s.config.mode == "cpu_direct"
+        th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+        th.start()
+        s.send(views)
+        th.join(20)
+        exp = ro.lay.allocate(dtype=torch.float32, fill=True)
+        assert all(torch.equal(ro.params[n], exp[n]) for n in exp)
+    finally:
+        ro.close()

@@ -188,6 +188,7 @@ class WeightSender:
         cfg = self.config
         metas = self._all_gather(sender_metadata.to_jsonable())
         self._sender_devices = self._all_gather(torch.cuda.current_device() if torch.cuda.is_available() else -1)
+        self._sender_hosts = self._all_gather(socket.gethostname())
         info = None
         if self.rank == 0:
             try:
@@ -197,6 +198,7 @@ class WeightSender:
         info = self._broadcast(info)
         if info.get("error"):
             raise TransferError(info["error"])
+        cfg.mode = info["mode"]                      # resolved by rank 0 when it was "auto"
         addr, port, world = info["address"], info["port"], info["world_size"]
         if self.rank != 0:
             self.session = Session(addr, port, is_master=False, timeout_s=cfg.connect_timeout_s)
@@ -298,13 +300,17 @@ class WeightSender:
         receivers: dict[int, dict] = {}
         counts = []
         base = self.world_size
+        where = []                                   # (host, device) of every worker
         for url in self.receiver_urls:
             resp = _get_with_retry(http, f"{url}/wbridge/metadata", cfg.http_timeout_s)
             workers = sorted(resp.json(), key=lambda w: w["rank"])
             for i, w in enumerate(workers):
                 receivers[base + i] = w["metadata"]
+                where.append((w.get("host"), str(w.get("device", ""))))
             counts.append(len(workers))
             base += len(workers)
+        if cfg.mode == "auto":
+            cfg.mode = self._auto_mode(where)
         world = self.world_size + sum(counts)
         addr = cfg.master_address
         if addr in ("", "auto"):
@@ -338,8 +344,18 @@ class WeightSender:
             base += count
         if cfg.arm == "direct":
             self._open_arm_channel(sorted(receivers))
-        return {"address": addr, "port": sess.port, "world_size": world,
+        return {"address": addr, "port": sess.port, "world_size": world, "mode": cfg.mode,
                 "receivers": {str(r): m for r, m in receivers.items()}, "session": session_id}
+
+    def _auto_mode(self, where: list[tuple[str | None, str]]) -> str:
+        """``transfer_mode="auto"``: ``gpu_direct`` when every sender and worker holds CUDA
+        tensors on one host, ``nccl`` when they are on GPUs of several hosts, else
+        ``cpu_direct``."""
+        gpus = all(d >= 0 for d in self._sender_devices) and all(dev.startswith("cuda") for _h, dev in where)
+        hosts = set(self._sender_hosts) | {h for h, _d in where}
+        mode = ("gpu_direct" if len(hosts) == 1 else "nccl") if gpus else "cpu_direct"
+        logger.info("transfer_mode auto -> %s (hosts %s)", mode, sorted(h for h in hosts if h))
+        return mode
 
     def _open_arm_channel(self, receivers: list[int]) -> None:
         """``arm="direct"``: connect one ROUTER to every receiver worker's arm socket (their

@@ -15,6 +15,7 @@ MODE_ALIASES = {
     "cpu_direct": "cpu_direct", "cpu": "cpu_direct", "gloo": "cpu_direct",
     "nvls": "nvls", "multicast": "nvls",
     "nccl": "nccl", "nccl_wire": "nccl",
+    "auto": "auto",          # chosen at connect: gpu_direct, nccl or cpu_direct (see WeightSender)
 }
 
 # modes whose payload travels as packed wire buffers over a process group
