@@ -149,7 +149,31 @@ class WeightReceiverController:
     def get_stats(self):
         return self._broadcast({"type": STATS_REQUEST})
 
+    def serve(self, host: str = "127.0.0.1", port: int = 0, timeout_s: float = 30.0) -> str:
+        """Serve the routes from a uvicorn server on a daemon thread (for rollout processes
+        without a FastAPI app of their own); returns the URL the senders use."""
+        import socket as _socket
+        import uvicorn
+        from fastapi import FastAPI
+        if port == 0:
+            with _socket.socket() as s:
+                s.bind((host, 0))
+                port = s.getsockname()[1]
+        app = FastAPI()
+        self.attach(app)
+        self._server = uvicorn.Server(uvicorn.Config(app, host=host, port=port, log_level="warning"))
+        threading.Thread(target=self._server.run, name="wbridge-http", daemon=True).start()
+        deadline = time.monotonic() + timeout_s
+        while not self._server.started:
+            if time.monotonic() > deadline:
+                raise ControllerError(f"HTTP server on {host}:{port} did not start within {timeout_s}s")
+            time.sleep(0.02)
+        return f"http://{host}:{port}"
+
     def close(self) -> None:
+        server = getattr(self, "_server", None)
+        if server is not None:
+            server.should_exit = True
         self._sock.close(0)
         self._ctx.term()
         try:
