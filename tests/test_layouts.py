@@ -53,15 +53,16 @@ def megatron_oracle(arch, lay: MegatronLayout, hf):
         out[p + "self_attention.linear_proj.weight"] = hf[m + "self_attn.o_proj.weight"].chunk(tp, 1)[r]
         if arch.is_moe:
             out[p + "pre_mlp_layernorm.weight"] = hf[m + "post_attention_layernorm.weight"]
-            out[p + "mlp.router.weight"] = hf[m + "mlp.gate.weight"]
+            mb, (gn, un, dn) = arch.moe_block, arch.expert_projs
+            out[p + "mlp.router.weight"] = hf[m + f"{mb}.gate.weight"]
             E_loc = arch.num_experts // lay.ep
             for e in range(E_loc):
                 eg = lay.ep_rank * E_loc + e
-                x = f"{m}mlp.experts.{eg}."
-                gate = hf[x + "gate_proj.weight"].chunk(lay.etp, 0)[lay.etp_rank]
-                up = hf[x + "up_proj.weight"].chunk(lay.etp, 0)[lay.etp_rank]
+                x = f"{m}{mb}.experts.{eg}."
+                gate = hf[x + f"{gn}.weight"].chunk(lay.etp, 0)[lay.etp_rank]
+                up = hf[x + f"{un}.weight"].chunk(lay.etp, 0)[lay.etp_rank]
                 out[lay._expert_name(i, e, 1)] = torch.cat([gate, up])
-                out[lay._expert_name(i, e, 2)] = hf[x + "down_proj.weight"].chunk(lay.etp, 1)[lay.etp_rank]
+                out[lay._expert_name(i, e, 2)] = hf[x + f"{dn}.weight"].chunk(lay.etp, 1)[lay.etp_rank]
         else:
             out[p + "mlp.linear_fc1.layer_norm_weight"] = hf[m + "post_attention_layernorm.weight"]
             out[p + "mlp.linear_fc1.weight"] = torch.cat([hf[m + "mlp.gate_proj.weight"].chunk(tp)[r],
@@ -81,6 +82,7 @@ MEGATRON_CASES = [
     ("tiny-qwen3", dict(tp=2, pp=2)),
     ("tiny-qwen3-moe", dict(tp=1, ep=2)),
     ("tiny-qwen3-moe", dict(tp=2, ep=2, etp=2, expert_naming="sequential")),
+    ("tiny-mixtral", dict(tp=2, ep=2)),
 ]
 
 
@@ -149,18 +151,19 @@ def sglang_oracle(arch, lay: SGLangLayout, hf):
             out[m + "self_attn.q_norm.weight"] = hf[m + "self_attn.q_norm.weight"]
             out[m + "self_attn.k_norm.weight"] = hf[m + "self_attn.k_norm.weight"]
         if arch.is_moe:
-            out[m + "mlp.gate.weight"] = hf[m + "mlp.gate.weight"]
+            mb, (gn, un, dn) = arch.moe_block, arch.expert_projs
+            out[m + f"{mb}.gate.weight"] = hf[m + f"{mb}.gate.weight"]
             E_loc = arch.num_experts // lay.moe_ep
             w13, w2 = [], []
             for e in range(E_loc):
                 eg = lay.moe_ep_rank * E_loc + e
-                x = f"{m}mlp.experts.{eg}."
+                x = f"{m}{mb}.experts.{eg}."
                 t = lay.moe_tp_rank
-                w13.append(torch.cat([hf[x + "gate_proj.weight"].chunk(lay.moe_tp)[t],
-                                      hf[x + "up_proj.weight"].chunk(lay.moe_tp)[t]]))
-                w2.append(hf[x + "down_proj.weight"].chunk(lay.moe_tp, 1)[t])
-            out[m + "mlp.experts.w13_weight"] = torch.stack(w13)
-            out[m + "mlp.experts.w2_weight"] = torch.stack(w2)
+                w13.append(torch.cat([hf[x + f"{gn}.weight"].chunk(lay.moe_tp)[t],
+                                      hf[x + f"{un}.weight"].chunk(lay.moe_tp)[t]]))
+                w2.append(hf[x + f"{dn}.weight"].chunk(lay.moe_tp, 1)[t])
+            out[m + f"{mb}.experts.w13_weight"] = torch.stack(w13)
+            out[m + f"{mb}.experts.w2_weight"] = torch.stack(w2)
         else:
             out[m + "mlp.gate_up_proj.weight"] = torch.cat([hf[m + "mlp.gate_proj.weight"].chunk(tp)[r],
                                                             hf[m + "mlp.up_proj.weight"].chunk(tp)[r]])
@@ -178,6 +181,7 @@ SGLANG_CASES = [
     ("tiny-qwen3", dict(tp=2, attn_tp=1)),      # DP-attention style: attention unsharded
     ("tiny-qwen3-moe", dict(tp=2)),
     ("tiny-qwen3-moe", dict(tp=2, moe_ep=2)),
+    ("tiny-mixtral", dict(tp=2, moe_ep=2)),
 ]
 
 
@@ -230,6 +234,7 @@ SYNC_CASES = [
     ("tiny-qwen3", [dict(tp=1)], [dict(tp=2, tp_rank=i, attn_tp=1, attn_tp_rank=0) for i in range(2)]),
     ("tiny-qwen3-moe", [dict(ep=2, ep_rank=i) for i in range(2)], [dict(tp=2, tp_rank=i) for i in range(2)]),
     ("tiny-qwen3-moe", [dict(ep=2, ep_rank=i) for i in range(2)], [dict(tp=2, tp_rank=i, moe_ep=2) for i in range(2)]),
+    ("tiny-mixtral", [dict(ep=2, ep_rank=i) for i in range(2)], [dict(tp=2, tp_rank=i, moe_ep=2) for i in range(2)]),
 ]
 
 

@@ -38,6 +38,7 @@ CASES = [
     ("tiny-llama", [dict(pp=2, pp_rank=i) for i in range(2)], [dict(tp=4, tp_rank=i) for i in range(4)], torch.bfloat16),
     ("tiny-qwen2", [dict(tp=2, tp_rank=i) for i in range(2)], [dict(tp=2, tp_rank=i) for i in range(2)], torch.bfloat16),
     ("tiny-qwen3-moe", [dict(ep=2, ep_rank=i) for i in range(2)], [dict(tp=2, tp_rank=i) for i in range(2)], torch.bfloat16),
+    ("tiny-mixtral", [dict(ep=2, ep_rank=i) for i in range(2)], [dict(tp=1)], torch.bfloat16),
 ]
 
 
@@ -204,3 +205,25 @@ def test_data_ptrs_key_detects_rebinding():
     assert k1 != ext().data_ptrs([a, [a, c]])
     assert k1 != ext().data_ptrs([a, [a], b])
     assert len(ext().data_ptrs([None, a[1:]])) == 16
+
+
+def test_mixtral_fp8_experts_plan_cpu():
+    """Mixtral names (block_sparse_moe, w1/w3/w2) through the fp8 expert path."""
+    arch = get_arch("tiny-mixtral")
+    senders = make_senders([MegatronLayout(arch, ep=2, ep_rank=i) for i in range(2)], torch.bfloat16)
+    lay = SGLangLayout(arch, tp=1, quant="fp8_experts")
+    params, meta, rphys = make_receiver(lay, torch.bfloat16)
+    assert any(".block_sparse_moe.experts.3.w2.weight" in n for n in meta.names())
+    for _p, _sm, sphys in senders:
+        cpu_execute(lower_ops(plan_pair(sphys, rphys), ABS, ABS))
+    expected = lay.allocate(dtype=torch.bfloat16, fill=True)
+    for n in params:
+        assert torch.equal(_u8(params[n]), _u8(expected[n])), n
+
+
+def test_mixtral_from_hf_config():
+    from weightbridge_b200.models.arch import ModelArch
+    a = ModelArch.from_hf_config({"model_type": "mixtral", "hidden_size": 4096, "num_attention_heads": 32,
+                                  "num_key_value_heads": 8, "num_hidden_layers": 32, "intermediate_size": 14336,
+                                  "vocab_size": 32000, "num_local_experts": 8, "num_experts_per_tok": 2})
+    assert a == get_arch("mixtral-8x7b").with_(name="mixtral")

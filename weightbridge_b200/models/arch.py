@@ -1,7 +1,8 @@
 """Architecture descriptors and the HF-named logical tensors of each model family.
 
-Families: ``llama`` (Llama-2/3), ``qwen2`` (q/k/v bias), ``qwen3`` (q/k RMSNorm), and
-``qwen3_moe`` (Qwen3 attention + a routed-expert MLP in every layer).  The reference
+Families: ``llama`` (Llama-2/3), ``qwen2`` (q/k/v bias), ``qwen3`` (q/k RMSNorm),
+``qwen3_moe`` (Qwen3 attention + a routed-expert MLP in every layer) and ``mixtral`` (Llama
+attention + ``block_sparse_moe`` experts named ``w1`` / ``w3`` / ``w2``).  The reference
 covers Qwen2/Qwen3 dense only (``wbridge/utils/megatron_utils/qwen2.py:13-80``,
 ``wbridge/utils/sglang_utils/qwen2.py:24-119``); Llama and the MoE family are new here.
 """
@@ -40,6 +41,16 @@ class ModelArch:
         return self.num_experts > 0
 
     @property
+    def moe_block(self) -> str:
+        """HF module holding the router and the experts of a MoE layer."""
+        return "block_sparse_moe" if self.family == "mixtral" else "mlp"
+
+    @property
+    def expert_projs(self) -> tuple[str, str, str]:
+        """HF names of an expert's gate, up and down projections."""
+        return ("w1", "w3", "w2") if self.family == "mixtral" else ("gate_proj", "up_proj", "down_proj")
+
+    @property
     def q_per_group(self) -> int:
         return self.num_heads // self.num_kv_heads
 
@@ -64,13 +75,14 @@ class ModelArch:
         yield p + "self_attn.o_proj.weight", (H, self.num_heads * hd)
         yield p + "post_attention_layernorm.weight", (H,)
         if self.is_moe:
-            I = self.moe_ffn
-            yield p + "mlp.gate.weight", (self.num_experts, H)
+            I, mb = self.moe_ffn, self.moe_block
+            g, u, d = self.expert_projs
+            yield p + f"{mb}.gate.weight", (self.num_experts, H)
             for e in range(self.num_experts):
-                q = f"{p}mlp.experts.{e}."
-                yield q + "gate_proj.weight", (I, H)
-                yield q + "up_proj.weight", (I, H)
-                yield q + "down_proj.weight", (H, I)
+                q = f"{p}{mb}.experts.{e}."
+                yield q + f"{g}.weight", (I, H)
+                yield q + f"{u}.weight", (I, H)
+                yield q + f"{d}.weight", (H, I)
         else:
             yield p + "mlp.gate_proj.weight", (self.ffn, H)
             yield p + "mlp.up_proj.weight", (self.ffn, H)
@@ -102,7 +114,7 @@ class ModelArch:
         g = (lambda k, d=None: cfg.get(k, d)) if isinstance(cfg, dict) else (lambda k, d=None: getattr(cfg, k, d))
         mt = str(g("model_type", "llama")).lower()
         fam = {"llama": "llama", "mistral": "llama", "qwen2": "qwen2", "qwen3": "qwen3",
-               "qwen3_moe": "qwen3_moe"}.get(mt)
+               "qwen3_moe": "qwen3_moe", "mixtral": "mixtral"}.get(mt)
         if fam is None:
             raise ValueError(f"unsupported model_type {mt!r}")
         H, nh = int(g("hidden_size")), int(g("num_attention_heads"))
@@ -110,10 +122,10 @@ class ModelArch:
             name=name or mt, family=fam, num_layers=int(g("num_hidden_layers")), hidden=H,
             num_heads=nh, num_kv_heads=int(g("num_key_value_heads", nh) or nh),
             head_dim=int(g("head_dim", None) or H // nh),
-            ffn=int(g("intermediate_size", 0) or 0), vocab=int(g("vocab_size")),
+            ffn=0 if fam == "mixtral" else int(g("intermediate_size", 0) or 0), vocab=int(g("vocab_size")),
             tie_embeddings=bool(g("tie_word_embeddings", False)),
-            num_experts=int(g("num_experts", 0) or 0),
-            moe_ffn=int(g("moe_intermediate_size", 0) or 0),
+            num_experts=int(g("num_local_experts" if fam == "mixtral" else "num_experts", 0) or 0),
+            moe_ffn=int(g("intermediate_size" if fam == "mixtral" else "moe_intermediate_size", 0) or 0),
             top_k=int(g("num_experts_per_tok", 0) or 0))
 
     @staticmethod
@@ -146,6 +158,10 @@ PRESETS: dict[str, ModelArch] = {
     "tiny-qwen3": ModelArch("tiny-qwen3", "qwen3", 2, 128, 8, 2, 32, 256, 520),
     "tiny-qwen3-moe": ModelArch("tiny-qwen3-moe", "qwen3_moe", 2, 256, 4, 2, 64, 0, 1000,
                                 num_experts=8, moe_ffn=256, top_k=2),
+    "tiny-mixtral": ModelArch("tiny-mixtral", "mixtral", 2, 256, 4, 2, 64, 0, 1000,
+                              num_experts=4, moe_ffn=256, top_k=2),
+    "mixtral-8x7b": ModelArch("mixtral-8x7b", "mixtral", 32, 4096, 32, 8, 128, 0, 32000,
+                              num_experts=8, moe_ffn=14336, top_k=2),
 }
 
 

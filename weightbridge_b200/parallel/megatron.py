@@ -233,7 +233,7 @@ class MegatronLayout:
             f = F // tp
             return [(p + "mlp.down_proj.weight", param, [(0, H, H), (r * f, (r + 1) * f, F)])]
         if rest == "mlp.router.weight":
-            return [(p + "mlp.gate.weight", param, full(param.shape))]
+            return [(p + f"{a.moe_block}.gate.weight", param, full(param.shape))]
         em = (re.match(r"mlp\.experts\.linear_fc([12])\.weight(\d+)$", rest)
               or re.match(r"mlp\.experts\.local_experts\.(?P<e>\d+)\.linear_fc(?P<fc>[12])\.weight$", rest))
         if em:
@@ -246,11 +246,12 @@ class MegatronLayout:
             I = a.moe_ffn
             i_loc = I // self.etp
             ibox = (self.etp_rank * i_loc, (self.etp_rank + 1) * i_loc, I)
-            q = f"{p}mlp.experts.{eg}."
+            q = f"{p}{a.moe_block}.experts.{eg}."
+            gn, un, dn = a.expert_projs
             if fc == 1:
-                return [(q + "gate_proj.weight", param[:i_loc], [ibox, (0, H, H)]),
-                        (q + "up_proj.weight", param[i_loc:], [ibox, (0, H, H)])]
-            return [(q + "down_proj.weight", param, [(0, H, H), ibox])]
+                return [(q + f"{gn}.weight", param[:i_loc], [ibox, (0, H, H)]),
+                        (q + f"{un}.weight", param[i_loc:], [ibox, (0, H, H)])]
+            return [(q + f"{dn}.weight", param, [(0, H, H), ibox])]
         raise UnknownParameter(f"unknown Megatron parameter {name!r}")
 
     def to_wb(self, named_params: dict[str, torch.Tensor] | Iterable[tuple[str, torch.Tensor]],
@@ -293,7 +294,7 @@ def convert_to_wb(args: Any, model_name: str, named_tensors, *, tp_rank: int | N
         vpp_size = mpu.get_virtual_pipeline_model_parallel_world_size() or 1
         vpp_rank = (mpu.get_virtual_pipeline_model_parallel_rank() or 0) if vpp_size > 1 else 0
     name = model_name.lower()
-    family = ("qwen3_moe" if "moe" in name else "qwen3" if "qwen3" in name else
+    family = ("mixtral" if "mixtral" in name else "qwen3_moe" if "moe" in name else "qwen3" if "qwen3" in name else
               "qwen2" if "qwen2" in name else "llama" if "llama" in name else None)
     if family is None:
         raise ValueError(f"unsupported model for convert_to_wb: {model_name}")

@@ -126,9 +126,10 @@ class SGLangLayout:
             if a.is_moe:
                 E_loc = a.num_experts // self.moe_ep
                 I_loc = a.moe_ffn // self.moe_tp
-                out[p + "mlp.gate.weight"] = ((a.num_experts, H), "other")
-                out[p + "mlp.experts.w13_weight"] = ((E_loc, 2 * I_loc, H), "expert")
-                out[p + "mlp.experts.w2_weight"] = ((E_loc, H, I_loc), "expert")
+                mb = a.moe_block
+                out[p + f"{mb}.gate.weight"] = ((a.num_experts, H), "other")
+                out[p + f"{mb}.experts.w13_weight"] = ((E_loc, 2 * I_loc, H), "expert")
+                out[p + f"{mb}.experts.w2_weight"] = ((E_loc, H, I_loc), "expert")
             else:
                 F_loc = a.ffn // self.tp
                 out[p + "mlp.gate_up_proj.weight"] = ((2 * F_loc, H), "linear")
@@ -278,7 +279,7 @@ class SGLangLayout:
             f = a.ffn // self.tp
             box = [(0, H, H), (self.tp_rank * f, (self.tp_rank + 1) * f, a.ffn)]
             return with_scale(name, param, box, scale, block_box(box) if scale is not None else None)
-        if rest in ("mlp.experts.w13_weight", "mlp.experts.w2_weight"):
+        if rest in (f"{a.moe_block}.experts.w13_weight", f"{a.moe_block}.experts.w2_weight"):
             E_loc = a.num_experts // self.moe_ep
             I = a.moe_ffn
             i_loc = I // self.moe_tp
@@ -286,18 +287,19 @@ class SGLangLayout:
             out = []
             for e in range(E_loc):
                 eg = self.moe_ep_rank * E_loc + e
-                q = f"{p}mlp.experts.{eg}."
+                q = f"{p}{a.moe_block}.experts.{eg}."
+                gn, un, dn = a.expert_projs
                 if rest.endswith("w13_weight"):
                     if scale is not None and i_loc % bn:
                         raise ValueError("w13 gate/up split not aligned with the fp8 block")
-                    for j, nm in enumerate(("gate_proj", "up_proj")):
+                    for j, nm in enumerate((gn, un)):
                         box = [ibox, (0, H, H)]
                         sv = scale[e, j * i_loc // bn:(j + 1) * i_loc // bn] if scale is not None else None
                         out += with_scale(q + nm + ".weight", param[e, j * i_loc:(j + 1) * i_loc], box, sv,
                                           block_box(box) if scale is not None else None)
                 else:
                     box = [(0, H, H), ibox]
-                    out += with_scale(q + "down_proj.weight", param[e], box,
+                    out += with_scale(q + f"{dn}.weight", param[e], box,
                                       scale[e] if scale is not None else None,
                                       block_box(box) if scale is not None else None)
             return out
