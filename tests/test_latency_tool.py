@@ -1,0 +1,8 @@
+"""The control-plane latency tool runs and reports every field."""
+from weightbridge_b200.control.latency import measure
+
+
+def test_latency_tool_direct_arm():
+    r = measure("direct", syncs=24)
+    assert r["payload_bytes"] > 0
+    assert all(r[k] is not None and r[k] > 0 for k in ("send_ms", "wait_ready_ms", "copy_ms", "request_update_ms"))
