@@ -582,3 +582,14 @@ def test_controller_serves_its_own_http_server():
     finally:
         recv.stop()
         ctl.close()
+
+
+def test_worker_endpoints_use_the_host_address_not_the_master_override(monkeypatch):
+    """WBRIDGE_MASTER_ADDRESS names the sender's session store; a worker publishes its own
+    address (WBRIDGE_HOST_ADDRESS) for its arm and liveness endpoints."""
+    from weightbridge_b200.control.session import host_address, local_address
+    monkeypatch.setenv("WBRIDGE_MASTER_ADDRESS", "10.1.2.3")
+    monkeypatch.setenv("WBRIDGE_HOST_ADDRESS", "10.9.9.9")
+    assert local_address() == "10.1.2.3" and host_address() == "10.9.9.9"
+    monkeypatch.delenv("WBRIDGE_MASTER_ADDRESS")
+    assert local_address() == "10.9.9.9"

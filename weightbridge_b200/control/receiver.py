@@ -281,7 +281,7 @@ class WeightReceiver:
 
     def _open_arm_socket(self, master_address: str) -> str:
         """Bind the direct-arm DEALER on an OS-chosen TCP port; returns its endpoint."""
-        from .session import local_address
+        from .session import host_address
         loopback = master_address in ("127.0.0.1", "localhost", "::1")
         sock = self._ctx.socket(zmq.DEALER)
         sock.setsockopt(zmq.LINGER, 0)
@@ -289,15 +289,15 @@ class WeightReceiver:
         port = sock.bind_to_random_port("tcp://127.0.0.1" if loopback else "tcp://*")
         self._arm_sock = sock
         self._poller.register(sock, zmq.POLLIN)
-        return f"tcp://{'127.0.0.1' if loopback else local_address()}:{port}"
+        return f"tcp://{'127.0.0.1' if loopback else host_address()}:{port}"
 
     def _open_watch(self, master_address: str):
         """Accept the senders' liveness connections (``control/liveness.py``)."""
         from .liveness import PeerWatch
-        from .session import local_address
+        from .session import host_address
         loopback = master_address in ("127.0.0.1", "localhost", "::1")
         lsock, port = PeerWatch.listen("127.0.0.1" if loopback else "0.0.0.0")
-        self._live_addr = ["127.0.0.1" if loopback else local_address(), port]
+        self._live_addr = ["127.0.0.1" if loopback else host_address(), port]
         return PeerWatch(self._sender_lost, lsock)
 
     def _sender_lost(self, s: int) -> None:

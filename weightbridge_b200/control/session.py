@@ -176,10 +176,10 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def local_address() -> str:
-    """This host's address for the session store: ``WBRIDGE_MASTER_ADDRESS`` if set, else
-    the address of the default route, else loopback."""
-    env = os.environ.get("WBRIDGE_MASTER_ADDRESS")
+def host_address() -> str:
+    """The address other hosts reach this one at: ``WBRIDGE_HOST_ADDRESS`` if set, else the
+    address of the default route, else loopback."""
+    env = os.environ.get("WBRIDGE_HOST_ADDRESS")
     if env:
         return env
     try:
@@ -188,3 +188,10 @@ def local_address() -> str:
             return s.getsockname()[0]
     except OSError:
         return "127.0.0.1"
+
+
+def local_address() -> str:
+    """The session store's address on sender rank 0: ``WBRIDGE_MASTER_ADDRESS`` if set, else
+    this host's address (``host_address``)."""
+    env = os.environ.get("WBRIDGE_MASTER_ADDRESS")
+    return env if env else host_address()
