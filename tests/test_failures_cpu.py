@@ -562,26 +562,22 @@ def test_controller_serves_its_own_http_server():
     """WeightReceiverController.serve(): a rollout process without a FastAPI app of its own."""
     from weightbridge_b200 import WeightReceiverController
     cfg = _cfg(mode="cpu_direct")
-    ctl = WeightReceiverController(worker_num=1, timeout_s=5)
-    url = ctl.serve()
     arch = get_arch("tiny-llama")
     lay = SGLangLayout(arch, tp=1)
     params = lay.allocate(dtype=torch.float32)
     meta, views = lay.to_wb(params)
-    recv = WeightReceiver(ctl.ipc_name, 0, meta, state_dict=views, config=cfg)
-    try:
-        _l, sp, smeta, sviews = _sender(cfg)
-        s = WeightSender("cpu_direct", [url], config=cfg)
-        s.connect(smeta)
-        th = threading.Thread(target=lambda: recv.request_update(timeout=20))
-        th.start()
-        s.send(sviews)
-        th.join(20)
-        exp = lay.allocate(dtype=torch.float32, fill=True)
-        assert all(torch.equal(params[n], exp[n]) for n in exp)
-    finally:
-        recv.stop()
-        ctl.close()
+    with WeightReceiverController(worker_num=1, timeout_s=5) as ctl:
+        url = ctl.serve()
+        with WeightReceiver(ctl.ipc_name, 0, meta, state_dict=views, config=cfg) as recv:
+            _l, sp, smeta, sviews = _sender(cfg)
+            with WeightSender("cpu_direct", [url], config=cfg) as s:
+                s.connect(smeta)
+                th = threading.Thread(target=lambda: recv.request_update(timeout=20))
+                th.start()
+                s.send(sviews)
+                th.join(20)
+    exp = lay.allocate(dtype=torch.float32, fill=True)
+    assert all(torch.equal(params[n], exp[n]) for n in exp)
 
 
 def test_worker_endpoints_use_the_host_address_not_the_master_override(monkeypatch):

@@ -170,6 +170,12 @@ class WeightReceiverController:
             time.sleep(0.02)
         return f"http://{host}:{port}"
 
+    def __enter__(self) -> "WeightReceiverController":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
     def close(self) -> None:
         server = getattr(self, "_server", None)
         if server is not None:

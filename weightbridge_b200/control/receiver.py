@@ -165,6 +165,12 @@ class WeightReceiver:
                 return False
         return True
 
+    def __enter__(self) -> "WeightReceiver":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.stop()
+
     def stop(self) -> None:
         """Stop the worker thread and release the session."""
         self._stop.set()

@@ -506,7 +506,14 @@ class WeightSender:
             raise RuntimeError("reconnect() needs a previous connect()")
         self.connect(self.metadata)
 
+    def __enter__(self) -> "WeightSender":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.disconnect()
+
     def disconnect(self) -> None:
+        """Leave the session (liveness connections say bye, IPC mappings close)."""
         self._close_watch()
         self._close_arm_channel()
         self._teardown_multicast()
