@@ -7,6 +7,8 @@
 copy:    one contiguous bf16 buffer -> another (HBM read + write), 16-byte aligned;
 strided: column block of a row-major matrix -> contiguous (TP column split), 2-D items;
 quant:   bf16 [E, 768, 2048] expert stack -> fp8 e4m3 + 128x128 fp32 block scales;
+split:   the same stack as split-block pieces (half of every block: rows 64-127 of each block
+         row), quantised by split_quant with an amax from split_amax (pass timed on the host);
 peer-push / peer-pull / peer-quant (two GPUs, one process, peer access enabled): the kernel
          runs on GPU 0 and stores into GPU 1 (push), or runs on GPU 1 and loads from GPU 0
          (pull; plain and bulk loads from a peer, no cluster multicast), or quantises on
@@ -60,6 +62,23 @@ def build(case: str, gbytes: float, dev, item_bytes: int):
         ops = [Op("quant", "x", (-1, a[i].data_ptr()), (-1, q[i].data_ptr()), [r, c], [c, 1], [c, 1], a.dtype,
                   q.dtype, (-1, s[i].data_ptr()), [c // 128, 1], (128, 128)) for i in range(e)]
         keep, traffic = (a, q, s), a.nbytes + q.nbytes + s.nbytes
+    elif case == "split":
+        # expert-TP-like pieces: rows [64, 128) of every 128-row block row of a bf16 [E, 768, 2048]
+        # stack (half of each block), one piece per 128 x 128 block, quantised with a given amax
+        r, c = 768, 2048
+        e = max(1, n // (r * c))
+        a = torch.randn(e, r, c, device=dev, dtype=torch.bfloat16)
+        q = torch.empty(e, r, c, device=dev, dtype=torch.float8_e4m3fn)
+        s = torch.empty(e, r // 128, c // 128, device=dev, dtype=torch.float32)
+        ops = []
+        for i in range(e):
+            for bi in range(r // 128):
+                for bj in range(c // 128):
+                    r0, c0 = bi * 128 + 64, bj * 128
+                    ops.append(Op("squant", "x", (-1, a[i].data_ptr() + (r0 * c + c0) * 2),
+                                  (-1, q[i].data_ptr() + r0 * c + c0), [64, 128], [c, 1], [c, 1], a.dtype, q.dtype,
+                                  (-1, s[i, bi, bj].data_ptr()), [c // 128, 1], (128, 128), key=("x", i, bi, bj)))
+        keep, traffic = (a, q, s), e * r * c                # half the source (2 B) and half the fp8 (1 B)
     elif case in ("peer-push", "peer-pull", "peer-quant"):
         from ._ext import ext
         if torch.cuda.device_count() < 2:
@@ -90,7 +109,7 @@ def build(case: str, gbytes: float, dev, item_bytes: int):
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--case", default="copy",
-                   choices=["copy", "strided", "quant", "peer-push", "peer-pull", "peer-quant"])
+                   choices=["copy", "strided", "quant", "split", "peer-push", "peer-pull", "peer-quant"])
     p.add_argument("--gbytes", type=float, default=1.0)
     p.add_argument("--mode", type=int, default=-1)
     p.add_argument("--piece", type=int, default=16384)
@@ -103,6 +122,13 @@ def main(argv=None):
     torch.cuda.set_device(dev)
     tables, keep, traffic = build(a.case, a.gbytes, dev, a.item_bytes)
     prog = TransferProgram(tables, dev, [], LaunchConfig(mode=a.mode, piece_bytes=a.piece, grid=a.grid or None))
+    if prog.n_pieces:          # split pieces: a real amax pass first, timed separately
+        import numpy as np
+        import time
+        t0 = time.perf_counter()
+        part = prog.piece_amax()
+        amax_ms = (time.perf_counter() - t0) * 1e3
+        prog.set_piece_amax(np.asarray(part, dtype=np.float32))
     for _ in range(a.warmup):
         prog.launch(0, signal=False)
     torch.cuda.synchronize()
@@ -116,7 +142,8 @@ def main(argv=None):
     gbs = traffic / (ms / 1e3) / 1e9
     peak = 770.0 if a.case.startswith("peer") else _peak_gbs()   # measured peer copy vs HBM copy
     print(json.dumps({"case": a.case, "gbytes": a.gbytes, "mode": prog.config.mode, "piece": a.piece, "grid": prog.grid(),
-                      "items": len(tables.items), "qwork": len(tables.qwork), "ms": round(ms, 4),
+                      "items": len(tables.items), "qwork": len(tables.qwork), "pieces": len(tables.pieces),
+                      "amax_pass_ms_host": round(amax_ms, 3) if prog.n_pieces else None, "ms": round(ms, 4),
                       "traffic_bytes": traffic, "gbs": round(gbs, 1),
                       "frac_of_measured": round(gbs / peak, 3) if peak else None,
                       "status": prog.read_status()}))
