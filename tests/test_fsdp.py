@@ -176,3 +176,25 @@ def test_dtensor_conversion_2d_mesh():
     assert sorted(got[r]["nested"][0][0] for r in range(4)) == [(0, 2, 7), (2, 4, 7), (4, 6, 7), (6, 7, 7)]
     # FSDP (strided, mesh dim 0) on top of TP (mesh dim 1): TP halves first, then FSDP halves
     assert got[1]["fsdp_on_tp"][0][0] == (4, 6, 8) and got[2]["fsdp_on_tp"][0][0] == (2, 4, 8)
+
+
+def test_hf_layout_receives_from_megatron():
+    """A rollout holding the plain HF state_dict (HFLayout) from Megatron TP2 shards."""
+    from weightbridge_b200 import HFLayout
+    from weightbridge_b200.parallel.megatron import MegatronLayout
+    arch = get_arch("tiny-qwen2")
+    senders = []
+    for i in range(2):
+        lay = MegatronLayout(arch, tp=2, tp_rank=i)
+        p = lay.allocate(dtype=torch.float32)
+        meta, views = lay.to_wb(p)
+        senders.append((p, phys_binding(bind(meta, views))))
+    hl = HFLayout(arch)
+    hp = hl.allocate(dtype=torch.float32, fill=False)
+    hmeta, hviews = hl.to_wb(hp)
+    rphys = phys_binding(bind(hmeta, hviews))
+    for _p, sphys in senders:
+        cpu_execute(lower_ops(plan_pair(sphys, rphys), ABS, ABS))
+    exp = hl.allocate(dtype=torch.float32, fill=True)
+    assert set(hp) == {n for n, _s in arch.hf_tensors()}
+    assert all(torch.equal(hp[n], exp[n]) for n in exp)

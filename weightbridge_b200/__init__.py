@@ -19,9 +19,9 @@ def __getattr__(name):
     if name == "MegatronLayout":
         from .parallel.megatron import MegatronLayout
         return MegatronLayout
-    if name == "FSDPLayout":
-        from .parallel.fsdp import FSDPLayout
-        return FSDPLayout
+    if name in ("FSDPLayout", "HFLayout"):
+        from .parallel import fsdp
+        return getattr(fsdp, name)
     if name in ("SGLangLayout", "VLLMLayout"):
         from .parallel import sglang
         return getattr(sglang, name)
@@ -31,6 +31,6 @@ def __getattr__(name):
 __all__ = [
     "WeightData", "WeightSender", "WeightReceiver", "WeightReceiverController", "TransferConfig",
     "check_shard_compatibility", "shards_iterator", "original_total_numel", "dtype_str_to_torch",
-    "dtype_to_str", "MegatronLayout", "FSDPLayout", "SGLangLayout", "VLLMLayout",
+    "dtype_to_str", "MegatronLayout", "FSDPLayout", "HFLayout", "SGLangLayout", "VLLMLayout",
 ]
 __version__ = "0.1.0"

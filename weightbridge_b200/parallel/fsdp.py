@@ -77,6 +77,12 @@ class FSDPLayout:
         return WeightData(meta), {n: params[n] for n in boxes}
 
 
+def HFLayout(arch: ModelArch) -> FSDPLayout:
+    """An unsharded HuggingFace model (trainer or rollout holding the plain HF state_dict,
+    e.g. a transformers-based generator): every tensor whole, HF names."""
+    return FSDPLayout(arch, world=1, rank=0)
+
+
 def convert_to_wb(named_tensors: Iterable[tuple[str, Any]] | dict[str, Any]
                   ) -> tuple[WeightData, dict[str, torch.Tensor]]:
     """Metadata and local views of HF-named trainer tensors: ``DTensor``s with ``Shard(d)`` /
