@@ -645,6 +645,8 @@ class WeightSender:
         key = (self._key(state_dict), subset)
         if key == self._program_key:
             return
+        if self.config.direction == "pull":     # the receivers pull from the last published memory:
+            self._progs.clear()                 # a switch of tensors must publish again (compile)
         hit = self._progs.pop(key, None)
         if hit is None:
             self._compile(state_dict, subset)
