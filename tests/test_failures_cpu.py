@@ -297,6 +297,17 @@ def test_pull_direction_in_process():
             exp = ro.lay.allocate(dtype=torch.float32, fill=True, seed=step)
             assert all(torch.equal(ro.params[n], exp[n]) for n in exp), step
         assert ro.recv.pull_program is not None and len(ro.recv.pull_program.tables) > 0
+        # other tensors (a second copy of the weights), then the first ones again: each switch
+        # publishes the sender's memory anew and the receiver pulls from the right one
+        params2 = lay.allocate(dtype=torch.float32, seed=7)
+        _m2, views2 = lay.to_wb(params2)
+        for vs, seed in ((views2, 7), (views, 1)):
+            th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+            th.start()
+            s.send(vs)
+            th.join(20)
+            exp = ro.lay.allocate(dtype=torch.float32, fill=True, seed=seed)
+            assert all(torch.equal(ro.params[n], exp[n]) for n in exp), seed
     finally:
         ro.close()
 
