@@ -600,3 +600,29 @@ def test_worker_endpoints_use_the_host_address_not_the_master_override(monkeypat
     assert local_address() == "10.1.2.3" and host_address() == "10.9.9.9"
     monkeypatch.delenv("WBRIDGE_MASTER_ADDRESS")
     assert local_address() == "10.9.9.9"
+
+
+def test_push_alternating_tensor_sets_uses_cached_programs():
+    """Two sets of trainer tensors sent alternately: each send moves the set it is given, and
+    each set's program is compiled once."""
+    cfg = _cfg(mode="gpu_direct")
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        params2 = lay.allocate(dtype=torch.float32, seed=7)
+        _m2, views2 = lay.to_wb(params2)
+        s = WeightSender("gpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        compiles = []
+        orig = s._compile
+        s._compile = lambda sd, sub=None: (compiles.append(1), orig(sd, sub))[1]
+        for vs, seed in ((views, 0), (views2, 7), (views, 0), (views2, 7)):
+            th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+            th.start()
+            s.send(vs)
+            th.join(20)
+            exp = ro.lay.allocate(dtype=torch.float32, fill=True, seed=seed)
+            assert all(torch.equal(ro.params[n], exp[n]) for n in exp), seed
+        assert len(compiles) == 2
+    finally:
+        ro.close()
