@@ -18,3 +18,10 @@ def test_tiny_qwen3_moe_ep2_to_tp1_fp8_gloo():
     """fp8 block quantisation on the sender side of the gloo path."""
     run("tiny-qwen3-moe", "cpu_direct", [dict(ep=2, ep_rank=0), dict(ep=2, ep_rank=1)],
         dict(tp=1, quant="fp8_experts"), dtype=torch.bfloat16, n_syncs=2)
+
+
+def test_megatron_tp2_to_fp8_linear_gloo():
+    """fp8 on every linear layer from Megatron's grouped QKV: 64-row KV groups are half a
+    block, so each K/V block is shared by the two TP ranks, which exchange its amax."""
+    run("tiny-qwen2-moe", "cpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)],
+        dict(tp=1, quant="fp8_linear"), dtype=torch.bfloat16, n_syncs=2)

@@ -63,6 +63,12 @@ def megatron_oracle(arch, lay: MegatronLayout, hf):
                 up = hf[x + f"{un}.weight"].chunk(lay.etp, 0)[lay.etp_rank]
                 out[lay._expert_name(i, e, 1)] = torch.cat([gate, up])
                 out[lay._expert_name(i, e, 2)] = hf[x + f"{dn}.weight"].chunk(lay.etp, 1)[lay.etp_rank]
+            if arch.shared_ffn:
+                y = m + "mlp.shared_expert."
+                out[p + "mlp.shared_experts.linear_fc1.weight"] = torch.cat(
+                    [hf[y + "gate_proj.weight"].chunk(tp)[r], hf[y + "up_proj.weight"].chunk(tp)[r]])
+                out[p + "mlp.shared_experts.linear_fc2.weight"] = hf[y + "down_proj.weight"].chunk(tp, 1)[r]
+                out[p + "mlp.shared_experts.gate_weight"] = hf[m + "mlp.shared_expert_gate.weight"]
         else:
             out[p + "mlp.linear_fc1.layer_norm_weight"] = hf[m + "post_attention_layernorm.weight"]
             out[p + "mlp.linear_fc1.weight"] = torch.cat([hf[m + "mlp.gate_proj.weight"].chunk(tp)[r],
@@ -83,6 +89,7 @@ MEGATRON_CASES = [
     ("tiny-qwen3-moe", dict(tp=1, ep=2)),
     ("tiny-qwen3-moe", dict(tp=2, ep=2, etp=2, expert_naming="sequential")),
     ("tiny-mixtral", dict(tp=2, ep=2)),
+    ("tiny-qwen2-moe", dict(tp=2, ep=2)),
 ]
 
 
@@ -164,6 +171,12 @@ def sglang_oracle(arch, lay: SGLangLayout, hf):
                 w2.append(hf[x + f"{dn}.weight"].chunk(lay.moe_tp, 1)[t])
             out[m + f"{mb}.experts.w13_weight"] = torch.stack(w13)
             out[m + f"{mb}.experts.w2_weight"] = torch.stack(w2)
+            if arch.shared_ffn:
+                y = m + "mlp.shared_expert."
+                out[y + "gate_up_proj.weight"] = torch.cat([hf[y + "gate_proj.weight"].chunk(tp)[r],
+                                                            hf[y + "up_proj.weight"].chunk(tp)[r]])
+                out[y + "down_proj.weight"] = hf[y + "down_proj.weight"].chunk(tp, 1)[r]
+                out[m + "mlp.shared_expert_gate.weight"] = hf[m + "mlp.shared_expert_gate.weight"]
         else:
             out[m + "mlp.gate_up_proj.weight"] = torch.cat([hf[m + "mlp.gate_proj.weight"].chunk(tp)[r],
                                                             hf[m + "mlp.up_proj.weight"].chunk(tp)[r]])
@@ -182,6 +195,7 @@ SGLANG_CASES = [
     ("tiny-qwen3-moe", dict(tp=2)),
     ("tiny-qwen3-moe", dict(tp=2, moe_ep=2)),
     ("tiny-mixtral", dict(tp=2, moe_ep=2)),
+    ("tiny-qwen2-moe", dict(tp=2, moe_ep=2)),
 ]
 
 
@@ -235,6 +249,8 @@ SYNC_CASES = [
     ("tiny-qwen3-moe", [dict(ep=2, ep_rank=i) for i in range(2)], [dict(tp=2, tp_rank=i) for i in range(2)]),
     ("tiny-qwen3-moe", [dict(ep=2, ep_rank=i) for i in range(2)], [dict(tp=2, tp_rank=i, moe_ep=2) for i in range(2)]),
     ("tiny-mixtral", [dict(ep=2, ep_rank=i) for i in range(2)], [dict(tp=2, tp_rank=i, moe_ep=2) for i in range(2)]),
+    ("tiny-qwen2-moe", [dict(tp=2, ep=2, tp_rank=i % 2, ep_rank=i // 2) for i in range(4)],
+     [dict(tp=2, tp_rank=i, moe_ep=2) for i in range(2)]),
 ]
 
 

@@ -1,4 +1,5 @@
 """Planner + C++ CPU executor: direct (address to address) and wire (pack / unpack) paths."""
+import numpy as np
 import pytest
 import torch
 
@@ -7,7 +8,7 @@ from weightbridge_b200.core.binding import bind
 from weightbridge_b200.core.plan import (ITEM_DTYPE, lower_ops, phys_binding, plan_pair, wire_binding,
                                          plan_digest)
 from weightbridge_b200.models.arch import get_arch
-from weightbridge_b200.ops.executor import cpu_execute
+from weightbridge_b200.ops.executor import cpu_execute, cpu_piece_amax
 from weightbridge_b200.parallel.megatron import MegatronLayout
 from weightbridge_b200.parallel.sglang import SGLangLayout
 
@@ -227,3 +228,35 @@ def test_mixtral_from_hf_config():
                                   "num_key_value_heads": 8, "num_hidden_layers": 32, "intermediate_size": 14336,
                                   "vocab_size": 32000, "num_local_experts": 8, "num_experts_per_tok": 2})
     assert a == get_arch("mixtral-8x7b").with_(name="mixtral")
+
+
+@pytest.mark.parametrize("quant", ["fp8_experts", "fp8_linear"])
+def test_qwen2_moe_shared_expert_fp8_plan_cpu(quant):
+    """Qwen2-MoE: routed experts, the gated shared expert (a TP-split dense MLP) and q/k/v
+    bias; fp8 on the experts only or on every linear layer."""
+    arch = get_arch("tiny-qwen2-moe")
+    senders = make_senders([MegatronLayout(arch, tp=2, tp_rank=i) for i in range(2)], torch.bfloat16)
+    lay = SGLangLayout(arch, tp=1, quant=quant)
+    params, meta, rphys = make_receiver(lay, torch.bfloat16)
+    assert "model.layers.1.mlp.shared_expert.gate_up_proj.weight" in params
+    # fp8_linear: k/v of one 64-row KV group are half a block, so blocks span the two TP ranks
+    tables = [lower_ops(plan_pair(sphys, rphys), ABS, ABS, receiver=0) for _p, _sm, sphys in senders]
+    assert (quant == "fp8_linear") == any(len(t.pieces) for t in tables)
+    block = {}
+    for t in tables:
+        for k, a in zip(t.piece_keys, cpu_piece_amax(t)):
+            block[k] = max(block.get(k, 0.0), float(a))
+    for t in tables:
+        cpu_execute(t, np.array([block[k] for k in t.piece_keys], dtype=np.float32))
+    expected = lay.allocate(dtype=torch.bfloat16, fill=True)
+    for n in params:
+        assert torch.equal(_u8(params[n]), _u8(expected[n])), n
+
+
+def test_qwen2_moe_from_hf_config():
+    from weightbridge_b200.models.arch import ModelArch
+    a = ModelArch.from_hf_config({"model_type": "qwen2_moe", "hidden_size": 2048, "num_attention_heads": 16,
+                                  "num_key_value_heads": 16, "num_hidden_layers": 24, "intermediate_size": 5632,
+                                  "moe_intermediate_size": 1408, "shared_expert_intermediate_size": 5632,
+                                  "vocab_size": 151936, "num_experts": 60, "num_experts_per_tok": 4})
+    assert a.family == "qwen2_moe" and a.ffn == 0 and a.shared_ffn == 5632 and a.qkv_bias and a.is_moe

@@ -213,34 +213,44 @@ def _scale_cell(dst: PhysBinding, sname: str, name: str, bi: int, bj: int) -> tu
 
 
 def _quant_ops(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst: PhysBinding) -> list[Op]:
-    """The quantised ops of one overlap: its whole blocks as one ``quant`` op, and one
-    ``squant`` op per block it shares with other senders (``core/splitq.py``)."""
-    from .splitq import block_split
-    if len(bc.extents) != 2:
-        raise ValueError(f"{name}: a block-quantised overlap must be a 2-D region, got {bc.region}")
-    if bc.src_strides[1] != 1 or bc.dst_strides[1] != 1:
+    """The quantised ops of one overlap: per 2-D row sub-region (``core/splitq.py:
+    row_subregions``; a refined row dimension such as Megatron's QKV groups gives several),
+    its whole blocks as one ``quant`` op and one ``squant`` op per block it shares with other
+    sub-regions or senders."""
+    from .splitq import block_split, row_subregions
+    if len(bc.extents) < 2:
+        raise ValueError(f"{name}: a block-quantised overlap needs rows and columns, got {bc.region}")
+    if bc.src_strides[-1] != 1 or bc.dst_strides[-1] != 1:
         raise ValueError(f"{name}: quantised rows must be contiguous on both sides")
     block = tuple(int(b) for b in q["block"])
     sname = q["scale"]
-    (r0, _r1, _), (c0, _c1, _) = bc.region
     se, de = s_dtype.itemsize, d_dtype.itemsize
-    core, pieces = block_split(bc.region, block)
-
-    def at(base, rr, cc, strides, es):
-        return (base[0], base[1] + ((rr - r0) * strides[0] + (cc - c0) * strides[1]) * es)
-
+    lows = [l for l, _r, _w in bc.region[:-2]]
     out = []
-    if core is not None:
-        (cr0, cr1), (cc0, cc1) = core
-        scale_at, sstr = _scale_cell(dst, sname, name, cr0 // block[0], cc0 // block[1])
-        out.append(Op("quant", name, at(src_at, cr0, cc0, bc.src_strides, se), at(dst_at, cr0, cc0, bc.dst_strides, de),
-                      [cr1 - cr0, cc1 - cc0], list(bc.src_strides), list(bc.dst_strides), s_dtype, d_dtype,
-                      scale_at, sstr, block))
-    for (bi, bj), (pr0, pr1), (pc0, pc1) in pieces:
-        scale_at, sstr = _scale_cell(dst, sname, name, bi, bj)
-        out.append(Op("squant", name, at(src_at, pr0, pc0, bc.src_strides, se), at(dst_at, pr0, pc0, bc.dst_strides, de),
-                      [pr1 - pr0, pc1 - pc0], list(bc.src_strides), list(bc.dst_strides), s_dtype, d_dtype,
-                      scale_at, sstr, block, key=(name, bi, bj)))
+    for outer, rows, cols in row_subregions(bc.region):
+        # element offsets of this sub-region's first row on both sides
+        so = sum((i - l) * st for i, l, st in zip(outer, lows, bc.src_strides))
+        do = sum((i - l) * st for i, l, st in zip(outer, lows, bc.dst_strides))
+        src_sub = (src_at[0], src_at[1] + so * se)
+        dst_sub = (dst_at[0], dst_at[1] + do * de)
+        sst = [bc.src_strides[-2], bc.src_strides[-1]]
+        dst_ = [bc.dst_strides[-2], bc.dst_strides[-1]]
+        r0, c0 = rows[0], cols[0]
+        core, pieces = block_split([rows, cols], block)
+
+        def at(base, rr, cc, strides, es, r0=r0, c0=c0):
+            return (base[0], base[1] + ((rr - r0) * strides[0] + (cc - c0) * strides[1]) * es)
+
+        if core is not None:
+            (cr0, cr1), (cc0, cc1) = core
+            scale_at, sstr = _scale_cell(dst, sname, name, cr0 // block[0], cc0 // block[1])
+            out.append(Op("quant", name, at(src_sub, cr0, cc0, sst, se), at(dst_sub, cr0, cc0, dst_, de),
+                          [cr1 - cr0, cc1 - cc0], sst, dst_, s_dtype, d_dtype, scale_at, sstr, block))
+        for (bi, bj), (pr0, pr1), (pc0, pc1) in pieces:
+            scale_at, sstr = _scale_cell(dst, sname, name, bi, bj)
+            out.append(Op("squant", name, at(src_sub, pr0, pc0, sst, se), at(dst_sub, pr0, pc0, dst_, de),
+                          [pr1 - pr0, pc1 - pc0], sst, dst_, s_dtype, d_dtype, scale_at, sstr, block,
+                          key=(name, bi, bj)))
     return out
 
 

@@ -244,8 +244,11 @@ def scale_box(region: Shard, block: Sequence[int], name: str = "") -> Shard:
     """Block-scale cells a 2-D region of a quantised tensor touches.  A cell of a block the
     region only partly covers is shared with the other senders of that block (they all
     write the same scale, see ``core/splitq.py``)."""
+    if len(region) > 2:          # a refined row dimension: the logical rows it covers
+        from .splitq import region_rows
+        region = [region_rows(region), region[-1]]
     if len(region) != 2:
-        raise ValueError(f"{name}: a block-quantised overlap must be 2-D, got {region}")
+        raise ValueError(f"{name}: a block-quantised overlap needs rows and columns, got {region}")
     return [(l // b, (r + b - 1) // b, (w + b - 1) // b) for (l, r, w), b in zip(region, block)]
 
 

@@ -63,6 +63,42 @@ def block_split(region: Region, block: Sequence[int]):
     return core, pieces
 
 
+def row_subregions(region: Region):
+    """2-D pieces of a refined region of a 2-D logical tensor.
+
+    The shard algebra may refine the row dimension into several (a Megatron QKV shard is
+    ``[(groups), (rows per group), (cols)]``); a block-quantised op needs a uniform row pitch.
+    Yields ``(outer, rows, cols)`` per index tuple ``outer`` of the refined row dims before the
+    last one: ``rows = (l, r, W)`` in logical rows of the whole tensor, ``cols`` the last dim.
+    A 2-D region yields itself with ``outer == ()``."""
+    if len(region) < 2:
+        raise ValueError(f"a block-quantised region needs rows and columns, got {region}")
+    import itertools
+    *rowdims, cols = [tuple(int(x) for x in d) for d in region]
+    widths = [w for _l, _r, w in rowdims]
+    W = 1
+    for w in widths:
+        W *= w
+    inner_l, inner_r, inner_w = rowdims[-1]
+    outer_dims = rowdims[:-1]
+    for outer in itertools.product(*(range(l, r) for l, r, _w in outer_dims)):
+        base, mult = 0, inner_w
+        for idx, (_l, _r, w) in zip(reversed(outer), reversed(outer_dims)):
+            base += idx * mult
+            mult *= w
+        yield outer, (base + inner_l, base + inner_r, W), cols
+
+
+def region_rows(region: Region) -> tuple[int, int, int]:
+    """The logical row range ``(l, r, W)`` a region covers; raises if it is not contiguous
+    (the inner refined row dims must be whole)."""
+    subs = list(row_subregions(region))
+    lo, hi = subs[0][1][0], subs[-1][1][1]
+    if sum(r - l for _o, (l, r, _w), _c in subs) != hi - lo:
+        raise ValueError(f"region {region} covers non-contiguous rows of a block-quantised tensor")
+    return lo, hi, subs[0][1][2]
+
+
 def split_keys(sender: WeightData, receiver: WeightData, names: Iterable[str] | None = None) -> list[tuple]:
     """Sorted ``(name, bi, bj)`` of the split blocks ``sender`` sends to ``receiver``: the
     blocks of the receiver's quantised entries that the sender's regions touch without
@@ -78,10 +114,11 @@ def split_keys(sender: WeightData, receiver: WeightData, names: Iterable[str] | 
         for ss in s_shards:
             for rs in receiver.shards(name):
                 bc = box_copy(ss, rs)
-                if bc is None or len(bc.region) != 2:
+                if bc is None or len(bc.region) < 2:
                     continue
-                for (bi, bj), _pr, _pc in block_split(bc.region, q["block"])[1]:
-                    keys.add((name, bi, bj))
+                for _outer, rows, cols in row_subregions(bc.region):
+                    for (bi, bj), _pr, _pc in block_split([rows, cols], q["block"])[1]:
+                        keys.add((name, bi, bj))
     return sorted(keys)
 
 

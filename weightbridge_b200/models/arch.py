@@ -1,8 +1,9 @@
 """Architecture descriptors and the HF-named logical tensors of each model family.
 
 Families: ``llama`` (Llama-2/3), ``qwen2`` (q/k/v bias), ``qwen3`` (q/k RMSNorm),
-``qwen3_moe`` (Qwen3 attention + a routed-expert MLP in every layer) and ``mixtral`` (Llama
-attention + ``block_sparse_moe`` experts named ``w1`` / ``w3`` / ``w2``).  The reference
+``qwen3_moe`` (Qwen3 attention + a routed-expert MLP in every layer), ``qwen2_moe`` (Qwen2
+attention + routed experts + a gated shared expert) and ``mixtral`` (Llama attention +
+``block_sparse_moe`` experts named ``w1`` / ``w3`` / ``w2``).  The reference
 covers Qwen2/Qwen3 dense only (``wbridge/utils/megatron_utils/qwen2.py:13-80``,
 ``wbridge/utils/sglang_utils/qwen2.py:24-119``); Llama and the MoE family are new here.
 """
@@ -15,7 +16,7 @@ from typing import Any, Iterator
 @dataclass(frozen=True)
 class ModelArch:
     name: str
-    family: str                   # llama | qwen2 | qwen3 | qwen3_moe
+    family: str                   # llama | qwen2 | qwen3 | qwen3_moe | qwen2_moe | mixtral
     num_layers: int
     hidden: int
     num_heads: int
@@ -27,10 +28,11 @@ class ModelArch:
     num_experts: int = 0
     moe_ffn: int = 0              # per-expert intermediate width
     top_k: int = 0
+    shared_ffn: int = 0           # shared expert's intermediate width (qwen2_moe), 0: none
 
     @property
     def qkv_bias(self) -> bool:
-        return self.family == "qwen2"
+        return self.family in ("qwen2", "qwen2_moe")
 
     @property
     def qk_norm(self) -> bool:
@@ -83,6 +85,12 @@ class ModelArch:
                 yield q + f"{g}.weight", (I, H)
                 yield q + f"{u}.weight", (I, H)
                 yield q + f"{d}.weight", (H, I)
+            if self.shared_ffn:
+                S = self.shared_ffn
+                yield p + "mlp.shared_expert.gate_proj.weight", (S, H)
+                yield p + "mlp.shared_expert.up_proj.weight", (S, H)
+                yield p + "mlp.shared_expert.down_proj.weight", (H, S)
+                yield p + "mlp.shared_expert_gate.weight", (1, H)
         else:
             yield p + "mlp.gate_proj.weight", (self.ffn, H)
             yield p + "mlp.up_proj.weight", (self.ffn, H)
@@ -114,7 +122,7 @@ class ModelArch:
         g = (lambda k, d=None: cfg.get(k, d)) if isinstance(cfg, dict) else (lambda k, d=None: getattr(cfg, k, d))
         mt = str(g("model_type", "llama")).lower()
         fam = {"llama": "llama", "mistral": "llama", "qwen2": "qwen2", "qwen3": "qwen3",
-               "qwen3_moe": "qwen3_moe", "mixtral": "mixtral"}.get(mt)
+               "qwen3_moe": "qwen3_moe", "qwen2_moe": "qwen2_moe", "mixtral": "mixtral"}.get(mt)
         if fam is None:
             raise ValueError(f"unsupported model_type {mt!r}")
         H, nh = int(g("hidden_size")), int(g("num_attention_heads"))
@@ -122,11 +130,13 @@ class ModelArch:
             name=name or mt, family=fam, num_layers=int(g("num_hidden_layers")), hidden=H,
             num_heads=nh, num_kv_heads=int(g("num_key_value_heads", nh) or nh),
             head_dim=int(g("head_dim", None) or H // nh),
-            ffn=0 if fam == "mixtral" else int(g("intermediate_size", 0) or 0), vocab=int(g("vocab_size")),
+            ffn=0 if fam in ("mixtral", "qwen2_moe") else int(g("intermediate_size", 0) or 0),
+            vocab=int(g("vocab_size")),
             tie_embeddings=bool(g("tie_word_embeddings", False)),
             num_experts=int(g("num_local_experts" if fam == "mixtral" else "num_experts", 0) or 0),
             moe_ffn=int(g("intermediate_size" if fam == "mixtral" else "moe_intermediate_size", 0) or 0),
-            top_k=int(g("num_experts_per_tok", 0) or 0))
+            top_k=int(g("num_experts_per_tok", 0) or 0),
+            shared_ffn=int(g("shared_expert_intermediate_size", 0) or 0) if fam == "qwen2_moe" else 0)
 
     @staticmethod
     def from_megatron_args(args: Any, family: str = "qwen2", name: str | None = None) -> "ModelArch":
@@ -141,7 +151,8 @@ class ModelArch:
             tie_embeddings=not bool(getattr(args, "untie_embeddings_and_output_weights", True)),
             num_experts=int(getattr(args, "num_experts", 0) or 0),
             moe_ffn=int(getattr(args, "moe_ffn_hidden_size", 0) or 0),
-            top_k=int(getattr(args, "moe_router_topk", 0) or 0))
+            top_k=int(getattr(args, "moe_router_topk", 0) or 0),
+            shared_ffn=int(getattr(args, "moe_shared_expert_intermediate_size", 0) or 0))
 
 
 PRESETS: dict[str, ModelArch] = {
@@ -160,6 +171,8 @@ PRESETS: dict[str, ModelArch] = {
                                 num_experts=8, moe_ffn=256, top_k=2),
     "tiny-mixtral": ModelArch("tiny-mixtral", "mixtral", 2, 256, 4, 2, 64, 0, 1000,
                               num_experts=4, moe_ffn=256, top_k=2),
+    "tiny-qwen2-moe": ModelArch("tiny-qwen2-moe", "qwen2_moe", 2, 256, 4, 2, 64, 0, 1000,
+                                num_experts=4, moe_ffn=128, top_k=2, shared_ffn=512),
     "mixtral-8x7b": ModelArch("mixtral-8x7b", "mixtral", 32, 4096, 32, 8, 128, 0, 32000,
                               num_experts=8, moe_ffn=14336, top_k=2),
 }

@@ -62,6 +62,8 @@ class MegatronLayout:
             raise ValueError("ffn not divisible by TP")
         if a.is_moe and (a.num_experts % self.ep or a.moe_ffn % self.etp):
             raise ValueError("experts not divisible by EP (or expert FFN by ETP)")
+        if a.shared_ffn % self.tp:
+            raise ValueError("shared expert FFN not divisible by TP")
         if self.vpp > 1:
             even = tuple([a.num_layers // self.pp] * self.pp)
             if a.num_layers % (self.pp * self.vpp) or self.layers_per_stage not in (None, even):
@@ -133,6 +135,11 @@ class MegatronLayout:
                 for e in range(E_loc):
                     out[self._expert_name(i, e, 1)] = (2 * I_loc, H)
                     out[self._expert_name(i, e, 2)] = (H, I_loc)
+                if a.shared_ffn:                       # shared expert: TP-split like a dense MLP
+                    S_loc = a.shared_ffn // tp
+                    out[p + "mlp.shared_experts.linear_fc1.weight"] = (2 * S_loc, H)
+                    out[p + "mlp.shared_experts.linear_fc2.weight"] = (H, S_loc)
+                    out[p + "mlp.shared_experts.gate_weight"] = (1, H)
             else:
                 F_loc = a.ffn // tp
                 out[p + "mlp.linear_fc1.layer_norm_weight"] = (H,)
@@ -232,6 +239,18 @@ class MegatronLayout:
             F = a.ffn
             f = F // tp
             return [(p + "mlp.down_proj.weight", param, [(0, H, H), (r * f, (r + 1) * f, F)])]
+        if rest == "mlp.shared_experts.linear_fc1.weight":
+            S = a.shared_ffn
+            sl = S // tp
+            box = [(r * sl, (r + 1) * sl, S), (0, H, H)]
+            return [(p + "mlp.shared_expert.gate_proj.weight", param[:sl], box),
+                    (p + "mlp.shared_expert.up_proj.weight", param[sl:], box)]
+        if rest == "mlp.shared_experts.linear_fc2.weight":
+            S = a.shared_ffn
+            sl = S // tp
+            return [(p + "mlp.shared_expert.down_proj.weight", param, [(0, H, H), (r * sl, (r + 1) * sl, S)])]
+        if rest == "mlp.shared_experts.gate_weight":
+            return [(p + "mlp.shared_expert_gate.weight", param, full(param.shape))]
         if rest == "mlp.router.weight":
             return [(p + f"{a.moe_block}.gate.weight", param, full(param.shape))]
         em = (re.match(r"mlp\.experts\.linear_fc([12])\.weight(\d+)$", rest)
@@ -294,7 +313,8 @@ def convert_to_wb(args: Any, model_name: str, named_tensors, *, tp_rank: int | N
         vpp_size = mpu.get_virtual_pipeline_model_parallel_world_size() or 1
         vpp_rank = (mpu.get_virtual_pipeline_model_parallel_rank() or 0) if vpp_size > 1 else 0
     name = model_name.lower()
-    family = ("mixtral" if "mixtral" in name else "qwen3_moe" if "moe" in name else "qwen3" if "qwen3" in name else
+    family = ("mixtral" if "mixtral" in name else "qwen2_moe" if "qwen2" in name and "moe" in name else
+              "qwen3_moe" if "moe" in name else "qwen3" if "qwen3" in name else
               "qwen2" if "qwen2" in name else "llama" if "llama" in name else None)
     if family is None:
         raise ValueError(f"unsupported model for convert_to_wb: {model_name}")

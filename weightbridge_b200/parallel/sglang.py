@@ -130,6 +130,11 @@ class SGLangLayout:
                 out[p + f"{mb}.gate.weight"] = ((a.num_experts, H), "other")
                 out[p + f"{mb}.experts.w13_weight"] = ((E_loc, 2 * I_loc, H), "expert")
                 out[p + f"{mb}.experts.w2_weight"] = ((E_loc, H, I_loc), "expert")
+                if a.shared_ffn:                       # shared expert: a TP-split dense MLP + its gate
+                    S_loc = a.shared_ffn // self.tp
+                    out[p + "mlp.shared_expert.gate_up_proj.weight"] = ((2 * S_loc, H), "linear")
+                    out[p + "mlp.shared_expert.down_proj.weight"] = ((H, S_loc), "linear")
+                    out[p + "mlp.shared_expert_gate.weight"] = ((1, H), "other")
             else:
                 F_loc = a.ffn // self.tp
                 out[p + "mlp.gate_up_proj.weight"] = ((2 * F_loc, H), "linear")
@@ -261,9 +266,12 @@ class SGLangLayout:
         if rest == "self_attn.o_proj.weight":
             box = [(0, H, H), qbox]
             return with_scale(name, param, box, scale, block_box(box) if scale is not None else None)
-        if rest == "mlp.gate_up_proj.weight":
-            f = a.ffn // self.tp
-            fbox = (self.tp_rank * f, (self.tp_rank + 1) * f, a.ffn)
+        if rest in ("mlp.gate_up_proj.weight", "mlp.shared_expert.gate_up_proj.weight"):
+            shared = rest.startswith("mlp.shared_expert.")
+            F = a.shared_ffn if shared else a.ffn
+            mod = "mlp.shared_expert." if shared else "mlp."
+            f = F // self.tp
+            fbox = (self.tp_rank * f, (self.tp_rank + 1) * f, F)
             box = [fbox, (0, H, H)]
             out = []
             for j, nm in enumerate(("gate_proj", "up_proj")):
@@ -273,11 +281,12 @@ class SGLangLayout:
                     if f % bn:
                         raise ValueError("gate/up split not aligned with the fp8 block")
                     sv = scale[j * f // bn:(j + 1) * f // bn]
-                out += with_scale(f"{p}mlp.{nm}.weight", param[j * f:(j + 1) * f], box, sv, sb)
+                out += with_scale(f"{p}{mod}{nm}.weight", param[j * f:(j + 1) * f], box, sv, sb)
             return out
-        if rest == "mlp.down_proj.weight":
-            f = a.ffn // self.tp
-            box = [(0, H, H), (self.tp_rank * f, (self.tp_rank + 1) * f, a.ffn)]
+        if rest in ("mlp.down_proj.weight", "mlp.shared_expert.down_proj.weight"):
+            F = a.shared_ffn if rest.startswith("mlp.shared_expert.") else a.ffn
+            f = F // self.tp
+            box = [(0, H, H), (self.tp_rank * f, (self.tp_rank + 1) * f, F)]
             return with_scale(name, param, box, scale, block_box(box) if scale is not None else None)
         if rest in (f"{a.moe_block}.experts.w13_weight", f"{a.moe_block}.experts.w2_weight"):
             E_loc = a.num_experts // self.moe_ep
