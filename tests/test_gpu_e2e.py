@@ -33,6 +33,13 @@ def test_colocated_ipc_split_fp8_blocks():
         dict(tp=1, quant="fp8_experts"), device="cuda:0", dtype=torch.bfloat16, n_syncs=2)
 
 
+def test_colocated_ipc_fp8_linear_from_grouped_qkv():
+    """fp8 on every linear layer from Megatron TP 2: grouped-QKV overlaps cut per KV group,
+    K/V blocks split between the two ranks (amax exchanged), stores over CUDA IPC."""
+    run("tiny-qwen2-moe", "gpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)],
+        dict(tp=1, quant="fp8_linear"), device="cuda:0", dtype=torch.bfloat16, n_syncs=2)
+
+
 def test_colocated_ipc_pull_direction():
     """The receiver maps the senders' memory (CUDA IPC) and runs the pull kernel itself."""
     run("tiny-llama", "gpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)], dict(tp=1),
