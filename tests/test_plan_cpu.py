@@ -260,3 +260,21 @@ def test_qwen2_moe_from_hf_config():
                                   "moe_intermediate_size": 1408, "shared_expert_intermediate_size": 5632,
                                   "vocab_size": 151936, "num_experts": 60, "num_experts_per_tok": 4})
     assert a.family == "qwen2_moe" and a.ffn == 0 and a.shared_ffn == 5632 and a.qkv_bias and a.is_moe
+
+
+def test_pack_for_fp8_linear_from_grouped_qkv():
+    """The host pack path (WeightData.pack_for) on refined-row regions whose groups hold whole
+    blocks (128-row KV heads): the same bytes as quantising the whole tensors."""
+    from weightbridge_b200.core.binding import unpack_from
+    arch = get_arch("tiny-llama-fp8")
+    r = SGLangLayout(arch, tp=1, quant="fp8_linear")
+    rp = r.allocate(dtype=torch.bfloat16)
+    rm, rv = r.to_wb(rp)
+    for i in range(2):
+        s = MegatronLayout(arch, tp=2, tp_rank=i)
+        sp = s.allocate(dtype=torch.bfloat16)
+        sm, sv = s.to_wb(sp)
+        ov = WeightData.compute_overlap(sm, rm)
+        unpack_from(bind(rm, rv), ov, WeightData.pack_for(sm, sv, ov))
+    exp = r.allocate(dtype=torch.bfloat16, fill=True)
+    assert all(torch.equal(_u8(rp[n]), _u8(exp[n])) for n in exp)

@@ -133,8 +133,8 @@ def pack_into(binding: Binding, overlap: WeightData, out: torch.Tensor) -> None:
             seg = out[off:off + n * dtype.itemsize].view(dtype)
             local, packed = _region_views(binding, name, box, seg)
             if q:
-                from .splitq import block_split
-                if block_split(box, q["block"])[1]:
+                from .splitq import block_split, row_subregions
+                if any(block_split([rows, cols], q["block"])[1] for _o, rows, cols in row_subregions(box)):
                     raise ValueError(f"{name}: region {box} cuts through {list(q['block'])} blocks; their "
                                      "scales need every sender's amax (WeightSender exchanges them)")
                 qv, sv = block_quant_fp8_ref(local.reshape(shard_extents(box)), tuple(q["block"]))
