@@ -626,3 +626,33 @@ def test_push_alternating_tensor_sets_uses_cached_programs():
         assert len(compiles) == 2
     finally:
         ro.close()
+
+
+def test_send_async_overlaps_and_serialises():
+    """send_async returns at once; the future yields the sync's stats; two async sends run
+    one after the other in call order; disconnect waits for the one in flight."""
+    cfg = _cfg(mode="gpu_direct")
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender("gpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        got = []
+
+        def worker():
+            for _ in range(2):
+                ro.recv.request_update(timeout=20)
+                got.append(ro.recv.weights_version)
+
+        th = threading.Thread(target=worker)
+        th.start()
+        f1 = s.send_async(views, version=1)
+        f2 = s.send_async(views, version=2)
+        assert f1.result(timeout=20).epoch == 1 and f2.result(timeout=20).epoch == 2
+        th.join(20)
+        assert got == [1, 2]
+        exp = ro.lay.allocate(dtype=torch.float32, fill=True)
+        assert all(torch.equal(ro.params[n], exp[n]) for n in exp)
+        s.disconnect()
+    finally:
+        ro.close()

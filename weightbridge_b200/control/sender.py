@@ -513,7 +513,12 @@ class WeightSender:
         self.disconnect()
 
     def disconnect(self) -> None:
-        """Leave the session (liveness connections say bye, IPC mappings close)."""
+        """Leave the session (liveness connections say bye, IPC mappings close); waits for a
+        sync started with ``send_async``."""
+        pool = getattr(self, "_pool", None)
+        if pool is not None:
+            pool.shutdown(wait=True)
+            self._pool = None
         self._close_watch()
         self._close_arm_channel()
         self._teardown_multicast()
@@ -754,14 +759,46 @@ class WeightSender:
         restricts the sync to those HF entries (e.g. skip frozen layers); every sender rank
         must pass the same set (push direction of ``gpu_direct`` and ``nvls`` only).  NVTX
         ranges mark the phases (``wbridge.send/arm``, ``/ready``, ``/transfer``)."""
+        subset = self._subset(names)
+        with nvtx_range("wbridge.send"):
+            return self._send(state_dict, -1 if version is None else int(version), subset)
+
+    def send_async(self, state_dict: dict[str, Any], version: int | None = None,
+                   names: Iterable[str] | None = None):
+        """Start a sync and return at once with a ``concurrent.futures.Future`` of its
+        ``SyncStats``: the handshake and the transfer run on a helper thread while the caller
+        goes on (the next forward and backward only read the parameters).  The parameters
+        must stay unchanged until ``future.result()`` returns - call it before the next
+        optimizer step.  Syncs of one sender run one at a time, in call order.  The transfer
+        is ordered after the work already enqueued on the caller's current stream."""
+        subset = self._subset(names)
+        after = device = None
+        if torch.cuda.is_available():
+            after, device = torch.cuda.current_stream(), torch.cuda.current_device()
+        if getattr(self, "_pool", None) is None:
+            from concurrent.futures import ThreadPoolExecutor
+            self._pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="wbridge-send")
+        tag = -1 if version is None else int(version)
+
+        def run():
+            if device is not None:
+                torch.cuda.set_device(device)         # the helper thread starts on device 0
+            with nvtx_range("wbridge.send"):
+                return self._send(state_dict, tag, subset, after)
+
+        return self._pool.submit(run)
+
+    def _subset(self, names) -> frozenset | None:
         subset = None if names is None else frozenset(names)
         if subset is not None and (self.config.mode in WIRE_MODES or self.config.direction == "pull"):
             raise ValueError("names= needs the push direction of gpu_direct or nvls: the wire modes and "
                              "pulling receivers move every entry they expect")
-        with nvtx_range("wbridge.send"):
-            return self._send(state_dict, -1 if version is None else int(version), subset)
+        return subset
 
-    def _send(self, state_dict: dict[str, Any], version: int = -1, subset: frozenset | None = None) -> SyncStats:
+    def _send(self, state_dict: dict[str, Any], version: int = -1, subset: frozenset | None = None,
+              after: Any = None) -> SyncStats:
+        """``after``: the stream whose enqueued work the transfer must follow (default: this
+        thread's current stream on the transfer's device)."""
         if not self.connected or self.metadata is None:
             raise RuntimeError("WeightSender.send requires connect() first")
         cfg = self.config
@@ -816,7 +853,7 @@ class WeightSender:
             if ws.device.type == "cuda":          # pack launches and NCCL sends, ordered on one stream
                 e0, e1 = self._ev
                 with torch.cuda.stream(self._stream):
-                    self._stream.wait_stream(torch.cuda.current_stream(ws.device))
+                    self._stream.wait_stream(after if after is not None else torch.cuda.current_stream(ws.device))
                     e0.record(self._stream)
                     ws.send(self._pg, epoch, self._stream)
                     e1.record(self._stream)
@@ -834,7 +871,7 @@ class WeightSender:
                 prog.launch(epoch)
                 st.device_ms = (time.perf_counter() - t2) * 1e3
             elif pushed:
-                cur = torch.cuda.current_stream(prog.device)
+                cur = after if after is not None else torch.cuda.current_stream(prog.device)
                 self._stream.wait_stream(cur)
                 e0, e1 = self._ev
                 with nvtx_range("wbridge.send/transfer"):
@@ -845,7 +882,8 @@ class WeightSender:
                 st.device_ms = e0.elapsed_time(e1)
                 st.status = prog.read_status()
             elif torch.cuda.is_available():
-                torch.cuda.current_stream().synchronize()   # the receivers pull: parameters must be final
+                (after if after is not None else torch.cuda.current_stream()).synchronize()   # the receivers
+                # pull: the parameters must be final
             if prog is not None:
                 st.bytes_read, st.bytes_written = prog.bytes_read, prog.bytes_written
             done = f"{st.status}:{self._bind_version}:{int(pushed)}:{version}"
