@@ -57,3 +57,34 @@ def test_raw_shards_example_on_one_gpu():
                           "--steps", "2"], capture_output=True, text=True, timeout=300)
     assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-3000:]
     assert out.stdout.strip().splitlines()[-1].startswith("OK")
+
+
+def test_inprocess_send_async_on_gpu():
+    """Sender, controller and receiver in one process on cuda:0 (the sender uses the
+    receiver's addresses directly); send_async overlaps with the caller and tags the weights."""
+    import threading
+    from weightbridge_b200 import TransferConfig, WeightReceiver, WeightReceiverController, WeightSender
+    from weightbridge_b200.models.arch import get_arch
+    from weightbridge_b200.parallel.megatron import MegatronLayout
+    from weightbridge_b200.parallel.sglang import SGLangLayout
+    torch.cuda.set_device(0)
+    arch = get_arch("tiny-llama")
+    cfg = TransferConfig(mode="gpu_direct", connect_timeout_s=60, sync_timeout_s=60)
+    with WeightReceiverController(worker_num=1, timeout_s=30) as ctl:
+        url = ctl.serve()
+        rl = SGLangLayout(arch, tp=1)
+        rp = rl.allocate(device="cuda:0", dtype=torch.bfloat16)
+        rm, rv = rl.to_wb(rp)
+        with WeightReceiver(ctl.ipc_name, 0, rm, state_dict=rv, config=cfg) as recv:
+            sl = MegatronLayout(arch, tp=1)
+            sp = sl.allocate(device="cuda:0", dtype=torch.bfloat16, seed=3)
+            sm, sv = sl.to_wb(sp)
+            with WeightSender("gpu_direct", [url], config=cfg) as s:
+                s.connect(sm)
+                th = threading.Thread(target=lambda: recv.request_update(timeout=30))
+                th.start()
+                st = s.send_async(sv, version=3).result(timeout=60)
+                th.join(30)
+                assert st.status == 0 and recv.weights_version == 3
+    exp = rl.allocate(device="cuda:0", dtype=torch.bfloat16, fill=True, seed=3)
+    assert all(torch.equal(rp[n], exp[n]) for n in exp)
