@@ -759,6 +759,8 @@ class WeightSender:
         restricts the sync to those HF entries (e.g. skip frozen layers); every sender rank
         must pass the same set (push direction of ``gpu_direct`` and ``nvls`` only).  NVTX
         ranges mark the phases (``wbridge.send/arm``, ``/ready``, ``/transfer``)."""
+        if getattr(self, "_pool", None) is not None:     # after send_async: keep the call order
+            return self.send_async(state_dict, version, names).result()
         subset = self._subset(names)
         with nvtx_range("wbridge.send"):
             return self._send(state_dict, -1 if version is None else int(version), subset)
