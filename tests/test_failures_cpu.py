@@ -656,3 +656,25 @@ def test_send_async_overlaps_and_serialises():
         s.disconnect()
     finally:
         ro.close()
+
+
+def test_uncovered_rollout_entries_warn_or_fail():
+    """A rollout entry that no sender holds (here: lm_head, the trainer ties its embeddings)
+    is reported at connect; require_full_coverage turns the warning into an error."""
+    import dataclasses
+    cfg = _cfg(mode="cpu_direct")
+    ro = Rollout(cfg)
+    try:
+        tied = dataclasses.replace(get_arch("tiny-llama"), tie_embeddings=True)
+        lay = MegatronLayout(tied, tp=1)
+        params = lay.allocate(dtype=torch.float32)
+        meta, views = lay.to_wb(params)
+        s = WeightSender("cpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        assert s.uncovered == {1: ["lm_head.weight"]}
+        s.disconnect()
+        strict = _cfg(mode="cpu_direct", require_full_coverage=True)
+        with pytest.raises(TransferError, match="lm_head"):
+            WeightSender("cpu_direct", [ro.url], config=strict).connect(meta)
+    finally:
+        ro.close()

@@ -157,6 +157,7 @@ class WeightSender:
         self._rinfo: dict[int, dict] = {}
         self._ops_cache: dict[tuple, list] = {}     # plan ops per (receiver, bindings, names)
         self._bind_version = 0                       # bumped whenever the bound tensors change
+        self.uncovered: dict[int, list[str]] = {}    # rank 0, after connect: worker -> entries no sender fills
         self._xchg = None                            # split fp8 blocks shared with other senders
         self._piece_pos = np.zeros(0, dtype=np.int64)
         self._arm_sock = None                        # rank 0, arm="direct": ROUTER to every receiver worker
@@ -326,10 +327,19 @@ class WeightSender:
         sess.set("direction", cfg.direction if cfg.mode == "gpu_direct" else "push")
         sess.set("wire_chunk", str(int(cfg.wire_chunk_bytes)))      # receivers cut their wires alike
         sess.set_json("assign", {str(s): {str(r): n for r, n in rs.items()} for s, rs in plan.items()})
+        covered: dict[tuple[int, str], int] = {}
         for s, rs in plan.items():
             for r, names in rs.items():
                 ov = WeightData.compute_overlap(restrict(smeta_objs[s], names), rmeta_objs[r])
                 sess.set(f"digest/{s}/{r}", plan_digest(ov))
+                for a, b, n, _sh, _dt in ov.iter_with_intv():
+                    covered[(r, n)] = covered.get((r, n), 0) + (b - a)
+        self.uncovered = _uncovered(rmeta_objs, covered)
+        if self.uncovered:
+            msg = ", ".join(f"worker {r}: {len(v)} entries (e.g. {v[0]})" for r, v in sorted(self.uncovered.items()))
+            if cfg.require_full_coverage:
+                raise TransferError(f"no sender holds some of the rollout's weights: {msg}")
+            logger.warning("no sender holds some of the rollout's weights (they keep their values): %s", msg)
         session_id = uuid.uuid4().hex
         backend = cfg.mode
         base = self.world_size
@@ -909,6 +919,18 @@ class WeightSender:
         if len(self.history) > 256:
             del self.history[:128]
         return st
+
+
+def _uncovered(rmetas: dict[int, WeightData], covered: dict[tuple[int, str], int]) -> dict[int, list[str]]:
+    """Per worker, the entries (scales aside) that the senders' overlaps do not fill."""
+    out: dict[int, list[str]] = {}
+    for r, meta in rmetas.items():
+        for a, b, n, _sh, _dt in meta.iter_with_intv():
+            if (meta.quant(n) or {}).get("role") == "scale":
+                continue
+            if covered.get((r, n), 0) < b - a:
+                out.setdefault(r, []).append(n)
+    return out
 
 
 def _digest(obj) -> str:

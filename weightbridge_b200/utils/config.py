@@ -47,6 +47,7 @@ class TransferConfig:
     verify_flags: bool = True             # receiver checks every sender's epoch flag
     load_balance: bool = True             # spread replicated shards over senders
     validate_plan: bool = True            # check every work row against registered memory before upload
+    require_full_coverage: bool = False   # connect fails (instead of warning) if a rollout entry has no sender
     direction: str = "push"               # gpu_direct: push (senders store) | pull (receivers load copies)
     link_gbs: float = 770.0               # per-GPU link bandwidth for the stats' fraction (measured peer copy)
     arm: str = "direct"                   # how each sync is armed: direct (one ZMQ message from sender rank 0
