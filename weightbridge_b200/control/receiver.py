@@ -357,9 +357,9 @@ class WeightReceiver:
             logger.exception("receiver %d update failed", self.rank)
             self._error = f"{type(e).__name__}: {e}"
             self._state = ReceiverState.FAILED
-            if self.session is not None:
-                self.session.set_error([f"ready/{self.global_rank}/{self.epoch + 1}"],
-                                       f"receiver {self.global_rank}: {self._error}")
+            if self._janitor is not None:        # off this thread: the store may be gone with its host
+                self._janitor.set_error([f"ready/{self.global_rank}/{self.epoch + 1}"],
+                                        f"receiver {self.global_rank}: {self._error}")
             sock.send_string(json.dumps({"success": False, "message": self._error, "error": self._error}))
 
     # -- session -----------------------------------------------------------------------
