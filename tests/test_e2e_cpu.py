@@ -25,3 +25,10 @@ def test_megatron_tp2_to_fp8_linear_gloo():
     block, so each K/V block is shared by the two TP ranks, which exchange its amax."""
     run("tiny-qwen2-moe", "cpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)],
         dict(tp=1, quant="fp8_linear"), dtype=torch.bfloat16, n_syncs=2)
+
+
+def test_redundant_expert_slots_fp8_gloo():
+    """A rollout worker with redundant expert slots (SGLang EPLB placement), fp8 experts."""
+    run("tiny-qwen3-moe", "cpu_direct", [dict(ep=2, ep_rank=0), dict(ep=2, ep_rank=1)],
+        dict(tp=1, quant="fp8_experts", expert_slots=[0, 5, 2, 5, 7, 1, 3, 6, 4]),
+        dtype=torch.bfloat16, n_syncs=2)

@@ -278,3 +278,27 @@ def test_pack_for_fp8_linear_from_grouped_qkv():
         unpack_from(bind(rm, rv), ov, WeightData.pack_for(sm, sv, ov))
     exp = r.allocate(dtype=torch.bfloat16, fill=True)
     assert all(torch.equal(_u8(rp[n]), _u8(exp[n])) for n in exp)
+
+
+@pytest.mark.parametrize("quant", [None, "fp8_experts"])
+def test_redundant_expert_slots(quant):
+    """SGLang EPLB-style placement: physical slots naming logical experts, one of them twice
+    (and a per-layer map): every slot receives its expert, the duplicate included, with its
+    own block scales under fp8."""
+    arch = get_arch("tiny-qwen3-moe")
+    senders = make_senders([MegatronLayout(arch, ep=2, ep_rank=i) for i in range(2)], torch.bfloat16)
+    slots = [[0, 5, 2, 5, 7], [1, 1, 3, 6, 4]]          # layer 0, layer 1
+    lay = SGLangLayout(arch, tp=1, quant=quant, expert_slots=slots)
+    params, meta, rphys = make_receiver(lay, torch.bfloat16)
+    assert params["model.layers.0.mlp.experts.w13_weight"].shape[0] == 5
+    assert len(meta.shards("model.layers.0.mlp.experts.5.gate_proj.weight")) == 2
+    for _p, _sm, sphys in senders:
+        cpu_execute(lower_ops(plan_pair(sphys, rphys), ABS, ABS))
+    expected = lay.allocate(dtype=torch.bfloat16, fill=True)
+    for n in params:
+        assert torch.equal(_u8(params[n]), _u8(expected[n])), n
+    w = params["model.layers.0.mlp.experts.w13_weight"]
+    assert torch.equal(_u8(w[1]), _u8(w[3]))                # both slots of expert 5
+    if quant:
+        sc = params["model.layers.0.mlp.experts.w13_weight_scale_inv"]
+        assert torch.equal(sc[1], sc[3]) and not torch.equal(sc[0], sc[1])

@@ -193,7 +193,7 @@ def plan_pair(src: PhysBinding, dst: PhysBinding, names: Iterable[str] | None = 
                 src_at = _shift(sp, bc.src_offset * s_dtype.itemsize)
                 dst_at = _shift(dp, bc.dst_offset * d_dtype.itemsize)
                 if quant:
-                    ops += _quant_ops(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst)
+                    ops += _quant_ops(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst, di)
                     continue
                 e, ss, ds = coalesce(bc.extents, bc.src_strides, bc.dst_strides)
                 ops.append(Op("copy" if s_dtype == d_dtype else "cast", name, src_at, dst_at, e, ss, ds,
@@ -201,10 +201,16 @@ def plan_pair(src: PhysBinding, dst: PhysBinding, names: Iterable[str] | None = 
     return ops
 
 
-def _scale_cell(dst: PhysBinding, sname: str, name: str, bi: int, bj: int) -> tuple[tuple[int, int], list[int]]:
+def _scale_cell(dst: PhysBinding, sname: str, name: str, bi: int, bj: int,
+                shard: int | None = None) -> tuple[tuple[int, int], list[int]]:
     """(alloc, byte offset) of block (bi, bj)'s scale cell on the destination, and the scale
-    grid's element strides."""
-    for sp in dst.entries[sname]:
+    grid's element strides.  When the scale entry has one shard per weight shard (always, for
+    layouts with repeated shards such as redundant expert slots), the cell is taken from the
+    weight shard's own scale shard ``shard``."""
+    cands = dst.entries[sname]
+    if shard is not None and len(cands) == len(dst.entries[name]):
+        cands = [cands[shard]]
+    for sp in cands:
         (a0, a1, _), (b0, b1, _) = sp.shard
         if a0 <= bi < a1 and b0 <= bj < b1:
             off = (bi - a0) * sp.strides[0] + (bj - b0) * sp.strides[1]
@@ -212,7 +218,7 @@ def _scale_cell(dst: PhysBinding, sname: str, name: str, bi: int, bj: int) -> tu
     raise ValueError(f"{name}: destination has no scale cell for block ({bi}, {bj})")
 
 
-def _quant_ops(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst: PhysBinding) -> list[Op]:
+def _quant_ops(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst: PhysBinding, di: int | None = None) -> list[Op]:
     """The quantised ops of one overlap: per 2-D row sub-region (``core/splitq.py:
     row_subregions``; a refined row dimension such as Megatron's QKV groups gives several),
     its whole blocks as one ``quant`` op and one ``squant`` op per block it shares with other
@@ -243,11 +249,11 @@ def _quant_ops(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst: PhysBinding) 
 
         if core is not None:
             (cr0, cr1), (cc0, cc1) = core
-            scale_at, sstr = _scale_cell(dst, sname, name, cr0 // block[0], cc0 // block[1])
+            scale_at, sstr = _scale_cell(dst, sname, name, cr0 // block[0], cc0 // block[1], di)
             out.append(Op("quant", name, at(src_sub, cr0, cc0, sst, se), at(dst_sub, cr0, cc0, dst_, de),
                           [cr1 - cr0, cc1 - cc0], sst, dst_, s_dtype, d_dtype, scale_at, sstr, block))
         for (bi, bj), (pr0, pr1), (pc0, pc1) in pieces:
-            scale_at, sstr = _scale_cell(dst, sname, name, bi, bj)
+            scale_at, sstr = _scale_cell(dst, sname, name, bi, bj, di)
             out.append(Op("squant", name, at(src_sub, pr0, pc0, sst, se), at(dst_sub, pr0, pc0, dst_, de),
                           [pr1 - pr0, pc1 - pc0], sst, dst_, s_dtype, d_dtype, scale_at, sstr, block,
                           key=(name, bi, bj)))

@@ -42,6 +42,10 @@ class SGLangLayout:
     quant: str | None = None             # None | "fp8_experts" | "fp8_linear"
     block: tuple[int, int] = (128, 128)
     vocab_pad_multiple: int = 64
+    # expert placement with redundant slots (SGLang EPLB): the logical expert held by each of
+    # this rank's physical slots, one list for every layer or a list of lists per layer;
+    # None: the contiguous split of the experts over the moe_ep ranks
+    expert_slots: tuple | list | None = None
 
     def __post_init__(self):
         if self.attn_tp is None:
@@ -62,6 +66,23 @@ class SGLangLayout:
                 raise ValueError("expert FFN not divisible by the MoE TP size")
         if self.quant not in (None, "fp8_experts", "fp8_linear"):
             raise ValueError(f"unknown quant mode {self.quant!r}")
+        if self.expert_slots is not None:
+            per_layer = list(self.expert_slots)
+            if per_layer and not isinstance(per_layer[0], (list, tuple)):
+                per_layer = [per_layer] * a.num_layers
+            if len(per_layer) != a.num_layers:
+                raise ValueError("expert_slots needs one slot list per layer (or one for all)")
+            for slots in per_layer:
+                if any(not 0 <= int(e) < a.num_experts for e in slots):
+                    raise ValueError(f"expert_slots names an expert outside 0..{a.num_experts - 1}")
+            self.expert_slots = tuple(tuple(int(e) for e in slots) for slots in per_layer)
+
+    def local_experts(self, layer: int) -> list[int]:
+        """The logical expert of each local physical slot of ``layer``."""
+        if self.expert_slots is not None:
+            return list(self.expert_slots[layer])
+        E_loc = self.arch.num_experts // self.moe_ep
+        return [self.moe_ep_rank * E_loc + e for e in range(E_loc)]
 
     # -- sizes ------------------------------------------------------------------------
     @property
@@ -124,7 +145,7 @@ class SGLangLayout:
             out[p + "self_attn.o_proj.weight"] = ((H, q_loc), "linear")
             out[p + "post_attention_layernorm.weight"] = ((H,), "other")
             if a.is_moe:
-                E_loc = a.num_experts // self.moe_ep
+                E_loc = len(self.local_experts(i))
                 I_loc = a.moe_ffn // self.moe_tp
                 mb = a.moe_block
                 out[p + f"{mb}.gate.weight"] = ((a.num_experts, H), "other")
@@ -186,19 +207,21 @@ class SGLangLayout:
         """Write the synthetic weights; fp8 entries are the block quantisation of the
         ``src_dtype`` weights a trainer would send."""
         meta, views = self.to_wb(params)
+        as_list = lambda v: v if isinstance(v, list) else [v]      # noqa: E731  (redundant slots)
         for name, shards, dtype in meta:
             q = meta.quant(name)
             if q and q.get("role") == "scale":
                 continue
-            box = shards[0]
-            if q:
-                src = torch.empty([r - l for l, r, _ in box], dtype=src_dtype, device=views[name].device)
-                synth_fill(src, name, box, seed=seed)
-                qv, sv = block_quant_fp8_ref(src, tuple(q["block"]))
-                views[name].copy_(qv)
-                views[q["scale"]].copy_(sv)
-            else:
-                synth_fill(views[name], name, box, seed=seed)
+            for box, view, sview in zip(shards, as_list(views[name]),
+                                        as_list(views[q["scale"]]) if q else [None] * len(shards)):
+                if q:
+                    src = torch.empty([r - l for l, r, _ in box], dtype=src_dtype, device=view.device)
+                    synth_fill(src, name, box, seed=seed)
+                    qv, sv = block_quant_fp8_ref(src, tuple(q["block"]))
+                    view.copy_(qv)
+                    sview.copy_(sv)
+                else:
+                    synth_fill(view, name, box, seed=seed)
 
     # -- conversion ------------------------------------------------------------------------
     def split_param(self, name: str, param: torch.Tensor, scale: torch.Tensor | None = None
@@ -289,13 +312,11 @@ class SGLangLayout:
             box = [(0, H, H), (self.tp_rank * f, (self.tp_rank + 1) * f, F)]
             return with_scale(name, param, box, scale, block_box(box) if scale is not None else None)
         if rest in (f"{a.moe_block}.experts.w13_weight", f"{a.moe_block}.experts.w2_weight"):
-            E_loc = a.num_experts // self.moe_ep
             I = a.moe_ffn
             i_loc = I // self.moe_tp
             ibox = (self.moe_tp_rank * i_loc, (self.moe_tp_rank + 1) * i_loc, I)
             out = []
-            for e in range(E_loc):
-                eg = self.moe_ep_rank * E_loc + e
+            for e, eg in enumerate(self.local_experts(int(m.group(1)))):
                 q = f"{p}{a.moe_block}.experts.{eg}."
                 gn, un, dn = a.expert_projs
                 if rest.endswith("w13_weight"):
@@ -335,6 +356,13 @@ class SGLangLayout:
                     raise
                 continue
             for hf, view, box, q in parts:
+                if hf in meta:           # a redundant expert slot: one more shard (and view) of it
+                    e = meta[hf]
+                    if not isinstance(views[hf], list):
+                        e["shard"], views[hf] = [e["shard"]], [views[hf]]
+                    e["shard"].append(box)
+                    views[hf].append(view)
+                    continue
                 entry = {"shard": box, "dtype": view.dtype}
                 if q:
                     entry["quant"] = q
