@@ -42,6 +42,12 @@ def free_port() -> int:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
+def share_cores(args) -> None:
+    """All the example's processes run on this host: split the cores between their intra-op
+    thread pools instead of letting every process start one thread per core."""
+    torch.set_num_threads(max(1, (os.cpu_count() or 2) // (5)))
+
+
 
 def full_tensor(name: str, step: int) -> torch.Tensor:
     """The logical [4, 8] tensor of ``name`` after training step ``step``."""
@@ -73,6 +79,7 @@ def local_slice(t: torch.Tensor, box) -> torch.Tensor:
 
 # -- rollout side --------------------------------------------------------------------------
 def worker(args, ipc_name: str, rank: int, results):
+    share_cores(args)
     from weightbridge_b200 import TransferConfig, WeightReceiver
     from weightbridge_b200.core.shard import shard_numel
     dev = "cpu" if args.device == "cpu" else "cuda:0"
@@ -125,6 +132,7 @@ def rollout_engine(args, port: int, results, ready):
 
 # -- trainer side --------------------------------------------------------------------------
 def trainer(args, rank: int, dist_port: int, url: str, results):
+    share_cores(args)
     import torch.distributed as dist
     from weightbridge_b200 import TransferConfig, WeightSender
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{dist_port}", rank=rank, world_size=2)

@@ -38,6 +38,12 @@ def free_port() -> int:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
+def share_cores(args) -> None:
+    """All the example's processes run on this host: split the cores between their intra-op
+    thread pools instead of letting every process start one thread per core."""
+    torch.set_num_threads(max(1, (os.cpu_count() or 2) // (args.trainers + args.workers + 1)))
+
+
 
 def device_for(args, role: str, rank: int) -> str:
     if args.device == "cpu":
@@ -49,6 +55,7 @@ def device_for(args, role: str, rank: int) -> str:
 
 # -- rollout side --------------------------------------------------------------------------
 def worker(args, ipc_name: str, rank: int, results):
+    share_cores(args)
     """One rollout worker: owns its shard of the SGLang parameters, takes updates."""
     from weightbridge_b200 import SGLangLayout, TransferConfig, WeightReceiver
     from weightbridge_b200.models.arch import get_arch
@@ -92,6 +99,7 @@ def rollout_engine(args, port: int, results):
 
 # -- trainer side --------------------------------------------------------------------------
 def trainer(args, rank: int, dist_port: int, url: str, results):
+    share_cores(args)
     import torch.distributed as dist
     from weightbridge_b200 import MegatronLayout, TransferConfig, WeightSender
     from weightbridge_b200.models.arch import get_arch

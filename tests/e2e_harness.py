@@ -16,8 +16,14 @@ def _port():
         return s.getsockname()[1]
 
 
+def _share_cores(nprocs: int) -> None:
+    """Several processes on one host: split the cores between their intra-op thread pools
+    (oversubscribed OpenMP teams spin against each other and slow every host op a hundredfold)."""
+    torch.set_num_threads(max(1, (os.cpu_count() or 2) // max(1, nprocs)))
+
+
 def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype, late=False, direction="push",
-                 exit_after=None, cfg_extra=None):
+                 exit_after=None, cfg_extra=None, nprocs=3):
     import threading
     import uvicorn
     from fastapi import FastAPI
@@ -25,6 +31,7 @@ def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype, late=Fal
     from weightbridge_b200.models.arch import get_arch
     from weightbridge_b200.parallel.sglang import SGLangLayout
     try:
+        _share_cores(nprocs)
         if device != "cpu":
             torch.cuda.set_device(torch.device(device))
         app = FastAPI()
@@ -69,6 +76,7 @@ def trainer_proc(rank, world, tport, url, q, n_syncs, model, mode, device, layou
     from weightbridge_b200.models.arch import get_arch
     from weightbridge_b200.parallel.megatron import MegatronLayout
     try:
+        _share_cores(world + 1)
         if device != "cpu":
             torch.cuda.set_device(torch.device(device))
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{tport}", rank=rank, world_size=world)
@@ -101,7 +109,7 @@ def run(model, mode, trainer_layouts, rollout_layout, device="cpu", dtype=torch.
     url = f"http://127.0.0.1:{hport}"
     world = len(trainer_layouts)
     procs = [ctx.Process(target=rollout_proc, args=(hport, q, n_syncs, model, mode, device, rollout_layout, dtype,
-                                                    late, direction, None, cfg_extra))]
+                                                    late, direction, None, cfg_extra, world + 1))]
     tdev = trainer_devices or [device] * world
     procs += [ctx.Process(target=trainer_proc, args=(r, world, tport, url, q, n_syncs, model, mode, tdev[r],
                                                       trainer_layouts, dtype, direction, cfg_extra, trainer))

@@ -20,6 +20,7 @@ def _port():
 
 
 def _trainer(rank, tport, url, q):
+    torch.set_num_threads(2)            # three processes share the host's cores
     import torch.distributed as dist
     from weightbridge_b200 import TransferConfig, WeightSender
     from weightbridge_b200.models.arch import get_arch
@@ -43,6 +44,7 @@ def _trainer(rank, tport, url, q):
 
 
 def _rollout(port, q):
+    torch.set_num_threads(2)
     import threading
     import uvicorn
     from fastapi import FastAPI
