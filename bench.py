@@ -240,6 +240,8 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     import faulthandler
     faulthandler.dump_traceback_later(args.stall_dump_s, exit=False)
     t_start = time.time()
+    # every role of the box is a process of this host: split the cores between their thread pools
+    torch.set_num_threads(max(1, (os.cpu_count() or 2) // max(1, nprocs)))
 
     def phase(msg):
         if idx == 0 or roles[idx].host:
