@@ -4,7 +4,7 @@ Produces ``weightbridge_b200/_C*.so`` (sm_100a kernels, CPU executor, IPC/VMM/mu
 """
 import os
 
-from setuptools import setup
+from setuptools import find_packages, setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -19,7 +19,7 @@ NVCC_FLAGS = [
 setup(
     name="weightbridge_b200",
     version="0.1.0",
-    packages=["weightbridge_b200"],
+    packages=find_packages(include=["weightbridge_b200", "weightbridge_b200.*"]),
     ext_modules=[
         CUDAExtension(
             name="weightbridge_b200._C",
