@@ -678,3 +678,37 @@ def test_uncovered_rollout_entries_warn_or_fail():
             WeightSender("cpu_direct", [ro.url], config=strict).connect(meta)
     finally:
         ro.close()
+
+
+@pytest.mark.parametrize("mode", ["gpu_direct", "cpu_direct"])
+def test_receiver_rebind_without_reconnect(mode):
+    """The engine reallocates its parameters: rebind() hands the worker new tensors, the next
+    update binds them and the senders follow (a new binding generation in the ready key)."""
+    cfg = _cfg(mode=mode)
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender(mode, [ro.url], config=cfg)
+        s.connect(meta)
+
+        def sync(seed):
+            lay.fill(params, seed=seed)
+            th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+            th.start()
+            s.send(views)
+            th.join(20)
+
+        sync(0)
+        old = {n: t.clone() for n, t in ro.params.items()}
+        fresh = ro.lay.allocate(dtype=torch.float32)
+        _m, fviews = ro.lay.to_wb(fresh)
+        ro.recv.rebind(fviews)
+        sync(4)
+        exp4 = ro.lay.allocate(dtype=torch.float32, fill=True, seed=4)
+        assert all(torch.equal(fresh[n], exp4[n]) for n in exp4)            # new tensors got sync 2
+        assert all(torch.equal(ro.params[n], old[n]) for n in old)          # old ones untouched
+        sync(5)
+        exp5 = ro.lay.allocate(dtype=torch.float32, fill=True, seed=5)
+        assert all(torch.equal(fresh[n], exp5[n]) for n in exp5)
+    finally:
+        ro.close()

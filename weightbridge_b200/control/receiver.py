@@ -85,6 +85,9 @@ class WeightReceiver:
         self._poller: zmq.Poller | None = None
         self._janitor: Janitor | None = None
         self._watch = None
+        self._bind_gen = 0                            # bumped at every (re)binding of the tensors
+        self._rebind_to = None                        # tensors handed to rebind(), bound at the next update
+        self._rebind_lock = threading.Lock()
         fd, path = tempfile.mkstemp(prefix=f"wbridge_sched_{rank}_")
         os.close(fd)
         os.unlink(path)
@@ -127,6 +130,15 @@ class WeightReceiver:
         """Tensors (or views) the senders write into; bound at the next connect."""
         self.state_dict = state_dict
         self.device = self._infer_device(None, state_dict)
+
+    def rebind(self, state_dict: dict[str, Any]) -> None:
+        """Receive into other tensors from the next update on (the engine reallocated its
+        parameters): the worker binds and exports them at that update and the senders pick
+        the new memory up when they see its ready key, without a reconnect."""
+        if self.mode == "nvls":
+            raise ReceiveError("rebind is not supported in mode 'nvls' (its memory is a fixed VmmPool)")
+        with self._rebind_lock:
+            self._rebind_to = state_dict
 
     # -- scheduler side ----------------------------------------------------------------
     def request_update(self, state_dict: dict[str, Any] | None = None, timeout: float | None = None) -> bool:
@@ -450,6 +462,8 @@ class WeightReceiver:
         else:
             self._rphys = phys_binding(binding)
         self._bound = True
+        self._bind_gen += 1
+        info["gen"] = self._bind_gen
         return info
 
     def _setup_wires(self) -> None:
@@ -471,6 +485,7 @@ class WeightReceiver:
         if self.device.type == "cuda":
             torch.cuda.set_device(self.device)
         extra = self._bind()
+        self._pull_versions = None                # the pull program writes into the old tensors
         if self.mode in WIRE_MODES:
             self._setup_wires()
         else:
@@ -483,6 +498,11 @@ class WeightReceiver:
         epoch = self.epoch + 1
         gr = self.global_rank
         t0 = time.perf_counter()
+        with self._rebind_lock:
+            target, self._rebind_to = self._rebind_to, None
+        if target is not None:
+            self.set_state_dict(target)
+            self._bound = False
         if not self._bound:
             self._late_bind()
         if self.device.type == "cuda":
@@ -503,7 +523,7 @@ class WeightReceiver:
             except (SessionTimeout, PeerError) as e:
                 raise ReceiveError(str(e)) from None
         else:
-            sess.set(f"ready/{gr}/{epoch}", "1")
+            sess.set(f"ready/{gr}/{epoch}", str(self._bind_gen))     # senders rebind on a new generation
             keys = [f"done/{s}/{gr}/{epoch}" for s in self.expected]
             try:
                 vals = sess.wait_checked(keys, self.config.sync_timeout_s,

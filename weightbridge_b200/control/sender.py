@@ -414,7 +414,7 @@ class WeightSender:
             if info.get("mode") not in ("gpu_direct", "nvls"):
                 raise TransferError(f"receiver {r} joined in mode {info.get('mode')}")
             if info.get("late"):
-                continue            # bound at its first update; opened in _resolve_late
+                continue            # bound at its first update; opened in _resolve_bindings
             if info["host"] != host:
                 raise TransferError(f"receiver {r} is on host {info['host']}: gpu_direct needs one node")
             if info.get("device", 0) < 0 and info["pid"] != pid:
@@ -492,18 +492,25 @@ class WeightSender:
                 m.teardown_binding()
         self._mc, self._mc_created = {}, []
 
-    def _resolve_late(self) -> bool:
-        """Receivers that joined without tensors publish their memory at their first update
-        (before they mark themselves ready); open it now.  True if anything changed."""
+    def _resolve_bindings(self, ready: dict[int, bytes]) -> bool:
+        """Open the memory of workers that bound tensors after connect: late binders at their
+        first update, and workers that called ``rebind`` (their ready key carries a new binding
+        generation).  Both publish ``recvbind/<rank>`` before marking ready.  True if any
+        changed (the compiled programs then refer to old memory)."""
         from ..parallel.ipc import ImportTable
         changed = False
         for r, info in self._rinfo.items():
-            if not info.get("late") or r in self._imports:
+            gen = int(ready[r]) if r in ready and ready[r].isdigit() else info.get("gen", 1)
+            stale = info.get("late") and r not in self._imports
+            if not stale and gen == info.get("gen", 1):
                 continue
             try:
                 info.update(self.session.get_json(f"recvbind/{r}", self.config.sync_timeout_s))
             except (SessionTimeout, PeerError) as e:
                 raise TransferError(str(e)) from None
+            old = self._imports.pop(r, None)
+            if old is not None:
+                old.close()
             self._imports[r] = ImportTable(info["allocs"], same_process=(info["pid"] == os.getpid()))
             changed = True
         return changed
@@ -826,8 +833,8 @@ class WeightSender:
         t1 = time.perf_counter()
         try:
             with nvtx_range("wbridge.send/ready"):
-                sess.wait_checked([f"ready/{r}/{epoch}" for r in self.targets], cfg.sync_timeout_s,
-                                  f"receivers {sorted(self.targets)} to be ready for epoch {epoch}")
+                ready = sess.wait_checked([f"ready/{r}/{epoch}" for r in self.targets], cfg.sync_timeout_s,
+                                          f"receivers {sorted(self.targets)} to be ready for epoch {epoch}")
         except (SessionTimeout, PeerError) as e:
             self._fail_epoch(epoch, str(e))
             raise TransferError(str(e)) from None
@@ -844,7 +851,7 @@ class WeightSender:
                     self._compile_wire(state_dict)
                     self._program_key = key
             else:
-                if self._resolve_late():
+                if self._resolve_bindings(dict(zip(self.targets, ready))):
                     self._progs.clear()
                     self._program_key = None
                 self._select(state_dict, subset)
