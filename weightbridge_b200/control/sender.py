@@ -698,7 +698,9 @@ class WeightSender:
         and no host synchronisation.  For callers that already know the rollout side is
         idle (and for device-timed benchmarks): the receivers' epoch flags are not touched,
         so a later ``send`` still pairs with ``request_update``.  Blocks split across senders
-        are quantised with the block amax exchanged by the last ``send``."""
+        are quantised with the block amax exchanged by the last ``send``, and the receivers'
+        memory is the one known at the last ``send`` (after a worker's ``rebind``, run a
+        ``send`` first)."""
         if not self.connected:
             raise RuntimeError("WeightSender.launch requires connect() first")
         if self.config.mode in WIRE_MODES:
