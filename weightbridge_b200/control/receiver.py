@@ -35,7 +35,7 @@ import torch
 import zmq
 
 from ..core.binding import bind
-from ..core.plan import lower_ops, phys_binding, plan_digest, plan_pair, wire_binding
+from ..core.plan import lower_ops, phys_binding, plan_digest, plan_pair
 from ..core.shard import WeightData
 from ..utils.config import WIRE_MODES, TransferConfig, normalize_mode
 from ..utils.trace import nvtx_range

@@ -42,8 +42,7 @@ import torch.distributed as dist
 
 from ..core.binding import bind
 from ..core.plan import (PhysBinding, PlanBoundsError, Tables, lower_ops, multicast_ok, phys_binding, plan_digest,
-                         plan_pair,
-                         storage_ranges, validate_tables, wire_binding)
+                         plan_pair, storage_ranges, validate_tables)
 from ..core.shard import WeightData
 from ..utils.config import WIRE_MODES, TransferConfig, normalize_mode
 from .assign import assign_sources, restrict

@@ -20,10 +20,9 @@ import sys
 
 import torch
 
-from .control.assign import assign_sources, restrict
+from .control.assign import assign_sources
 from .core.binding import bind
 from .core.plan import lower_ops, phys_binding, plan_pair
-from .core.shard import WeightData
 from .models.arch import get_arch
 from .parallel.megatron import MegatronLayout
 from .parallel.sglang import SGLangLayout
