@@ -141,3 +141,33 @@ def test_split_blocks_random_fsdp_shardings(world, tp, dim, f32):
         expected = lay.allocate(dtype=dtype, fill=True)
         for n in params:
             assert torch.equal(_u8(params[n]), _u8(expected[n])), (n, world, tp, dim)
+
+
+@settings(max_examples=12, deadline=None)
+@given(model=st.sampled_from(["tiny-llama-fp8", "tiny-qwen2-moe"]), mtp=st.sampled_from([1, 2]),
+       mpp=st.sampled_from([1, 2]), rtp=st.sampled_from([1, 2]), f32=st.booleans())
+def test_random_megatron_to_fp8_linear(model, mtp, mpp, rtp, f32):
+    """Random Megatron TP x PP layouts into fp8 SGLang ranks (every linear layer quantised):
+    grouped-QKV regions cut per KV group, blocks split between ranks merged by amax."""
+    dtype = torch.float32 if f32 else torch.bfloat16
+    arch = get_arch(model)
+    if arch.num_kv_heads % mtp:
+        return
+    megs = [MegatronLayout(arch, tp=mtp, pp=mpp, tp_rank=t, pp_rank=p) for t in range(mtp) for p in range(mpp)]
+    senders = make_senders(megs, dtype)
+    for r in range(rtp):
+        try:
+            lay = SGLangLayout(arch, tp=rtp, tp_rank=r, quant="fp8_linear", moe_ep=rtp if arch.is_moe else 1)
+            params, _rmeta, rphys = make_receiver(lay, dtype)
+        except ValueError:            # a TP split the fp8 layout itself refuses (block-misaligned)
+            return
+        tables = [lower_ops(plan_pair(sphys, rphys), ABS, ABS, receiver=r) for _p, _m, sphys in senders]
+        block: dict = {}
+        for t in tables:
+            for k, a in zip(t.piece_keys, cpu_piece_amax(t)):
+                block[k] = max(block.get(k, 0.0), float(a))
+        for t in tables:
+            cpu_execute(t, np.array([block[k] for k in t.piece_keys], dtype=np.float32))
+        expected = lay.allocate(dtype=dtype, fill=True)
+        for n in params:
+            assert torch.equal(_u8(params[n]), _u8(expected[n])), (n, model, mtp, mpp, rtp)
