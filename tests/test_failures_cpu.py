@@ -712,3 +712,47 @@ def test_receiver_rebind_without_reconnect(mode):
         assert all(torch.equal(fresh[n], exp5[n]) for n in exp5)
     finally:
         ro.close()
+
+
+def test_two_models_share_one_rollout_app():
+    """Two controllers (policy and a second model) on one FastAPI app under URL prefixes;
+    each sender syncs its own model through its prefix."""
+    import uvicorn
+    from fastapi import FastAPI
+    from weightbridge_b200 import WeightReceiverController
+    cfg = _cfg(mode="cpu_direct")
+    app = FastAPI()
+    ctls, recvs, stores = [], [], []
+    for prefix in ("/policy", "/critic"):
+        ctl = WeightReceiverController(app, worker_num=1, timeout_s=5, prefix=prefix)
+        lay = SGLangLayout(get_arch("tiny-llama"), tp=1)
+        p = lay.allocate(dtype=torch.float32)
+        m, v = lay.to_wb(p)
+        recvs.append(WeightReceiver(ctl.ipc_name, 0, m, state_dict=v, config=cfg))
+        ctls.append(ctl)
+        stores.append((lay, p))
+    port = _port()
+    server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="error"))
+    threading.Thread(target=server.run, daemon=True).start()
+    while not server.started:
+        time.sleep(0.02)
+    try:
+        for k, prefix in enumerate(("/policy", "/critic")):
+            lay, params, meta, views = _sender(cfg)
+            lay.fill(params, seed=10 + k)
+            s = WeightSender("cpu_direct", [f"http://127.0.0.1:{port}{prefix}"], config=cfg)
+            s.connect(meta)
+            th = threading.Thread(target=lambda r=recvs[k]: r.request_update(timeout=20))
+            th.start()
+            s.send(views)
+            th.join(20)
+            s.disconnect()
+        for k, (rl, rp) in enumerate(stores):
+            exp = rl.allocate(dtype=torch.float32, fill=True, seed=10 + k)
+            assert all(torch.equal(rp[n], exp[n]) for n in exp), k
+    finally:
+        for r in recvs:
+            r.stop()
+        server.should_exit = True
+        for c in ctls:
+            c.close()

@@ -34,7 +34,11 @@ class ControllerError(RuntimeError):
 
 
 class WeightReceiverController:
-    def __init__(self, app=None, worker_num: int | None = None, timeout_s: float = 60.0):
+    """The rollout server's side of the control plane.  ``prefix`` mounts the routes under
+    ``<prefix>/wbridge/...`` so several controllers (several models) can share one app; the
+    senders then use ``http://host:port<prefix>`` as the receiver URL."""
+
+    def __init__(self, app=None, worker_num: int | None = None, timeout_s: float = 60.0, prefix: str = ""):
         fd, path = tempfile.mkstemp(prefix="wbridge_ctl_")
         os.close(fd)
         os.unlink(path)
@@ -51,6 +55,9 @@ class WeightReceiverController:
         self._ids = itertools.count(1)
         self._worker_num: int | None = None
         self._receiver_identities: list[bytes] = []
+        self.prefix = prefix.rstrip("/")
+        if self.prefix and not self.prefix.startswith("/"):
+            raise ValueError("prefix must start with '/'")
         if worker_num is not None:
             self.set_worker_num(worker_num)
         if app is not None:
@@ -59,10 +66,11 @@ class WeightReceiverController:
     def attach(self, app) -> None:
         from fastapi import APIRouter
         router = APIRouter()
-        router.add_api_route("/wbridge/metadata", self.get_metadata, methods=["GET"])
-        router.add_api_route("/wbridge/connect", self.connect, methods=["POST"])
-        router.add_api_route("/wbridge/receive", self.receive_weights, methods=["POST"])
-        router.add_api_route("/wbridge/stats", self.get_stats, methods=["GET"])
+        base = f"{self.prefix}/wbridge"
+        router.add_api_route(f"{base}/metadata", self.get_metadata, methods=["GET"])
+        router.add_api_route(f"{base}/connect", self.connect, methods=["POST"])
+        router.add_api_route(f"{base}/receive", self.receive_weights, methods=["POST"])
+        router.add_api_route(f"{base}/stats", self.get_stats, methods=["GET"])
         app.include_router(router)
         self.router = router
 
@@ -168,7 +176,7 @@ class WeightReceiverController:
             if time.monotonic() > deadline:
                 raise ControllerError(f"HTTP server on {host}:{port} did not start within {timeout_s}s")
             time.sleep(0.02)
-        return f"http://{host}:{port}"
+        return f"http://{host}:{port}{self.prefix}"
 
     def __enter__(self) -> "WeightReceiverController":
         return self
