@@ -23,6 +23,9 @@ from weightbridge_b200.parallel.megatron import MegatronLayout
 from weightbridge_b200.parallel.sglang import SGLangLayout
 
 pytestmark = pytest.mark.gpu
+# Written since the last run on a B200: they run and report, but a failure does not stop the
+# rest of the GPU suite (pytest -x) before the tests that have passed there.
+FIRST_RUN = pytest.mark.xfail(reason="first run on a B200 pending", strict=False)
 ABS = lambda _a: 0
 MODES = [MODE_VECTOR, MODE_BULK8, MODE_BULK12, MODE_BULK4]
 
@@ -198,6 +201,7 @@ def test_repeated_launches_reset_counter():
 
 
 @pytest.mark.parametrize("etp,dtype", [(4, torch.bfloat16), (8, torch.bfloat16), (4, torch.float32)])
+@FIRST_RUN
 def test_gpu_split_blocks_match_whole_tensor_oracle(etp, dtype):
     """fp8 blocks split across senders (expert TP slices of 64 / 32 rows): split_amax on every
     sender's pieces, the block amax merged over the senders on the host, split_quant plus the
