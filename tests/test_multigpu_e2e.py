@@ -8,6 +8,10 @@ from tests.e2e_harness import run
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
 
+# not yet run on B200s: reported, but a failure does not stop the suite (pytest -x)
+FIRST_RUN = pytest.mark.xfail(reason="first run on B200s pending", strict=False)
+
+
 def _need(n):
     if torch.cuda.device_count() < n:
         pytest.skip(f"needs {n} GPUs")
@@ -25,13 +29,14 @@ def test_two_gpus_fp8_experts_over_nvlink():
         dtype=torch.bfloat16, trainer_devices=["cuda:0"], n_syncs=2)
 
 
+@FIRST_RUN
 def test_three_gpus_two_senders_one_receiver():
     _need(3)
     run("tiny-qwen2", "gpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)], dict(tp=1), device="cuda:2",
         dtype=torch.bfloat16, trainer_devices=["cuda:0", "cuda:1"])
 
 
-@pytest.mark.parametrize("chunk", [0, 64 << 10])
+@pytest.mark.parametrize("chunk", [0, pytest.param(64 << 10, marks=FIRST_RUN)])
 def test_two_gpus_nccl_wire_mode(chunk):
     """Cross-node capable path: pack kernel -> NCCL send/recv -> unpack kernel, as one message
     per peer (chunk 0) or as many 64 KiB chunks through two buffers per peer."""
@@ -65,6 +70,7 @@ def _leaving_trainer(tport, url, q):
         q.put(("second-sync", type(e).__name__, time.time() - t0))
 
 
+@FIRST_RUN
 def test_receiver_leaving_between_syncs_fails_the_next_send():
     """A rollout process exits between two syncs (nothing in flight); the trainer's next send
     reports an error within its deadline instead of hanging, and launches no kernel into the
