@@ -658,6 +658,42 @@ def test_send_async_overlaps_and_serialises():
         ro.close()
 
 
+def test_send_async_snapshot_lets_the_caller_update_at_once():
+    """send_async(snapshot=True) syncs a copy taken at the call: the trainer overwrites its
+    parameters right after the call and the worker still receives the old values; the
+    snapshot buffers are reused while the tensors stay the same."""
+    cfg = _cfg(mode="gpu_direct")
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender("gpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        got = []
+
+        def worker():
+            for _ in range(2):
+                ro.recv.request_update(timeout=20)
+                got.append((ro.recv.weights_version, {n: t.clone() for n, t in ro.params.items()}))
+
+        th = threading.Thread(target=worker)
+        th.start()
+        f1 = s.send_async(views, version=1, snapshot=True)
+        buf = s._snap
+        lay.fill(params, seed=9)                  # the optimizer step, before the sync ran
+        f2 = s.send_async(views, version=2, snapshot=True)
+        lay.fill(params, seed=4)
+        assert f1.result(timeout=20).epoch == 1 and f2.result(timeout=20).epoch == 2
+        th.join(20)
+        assert s._snap is buf
+        assert [v for v, _p in got] == [1, 2]
+        for (_v, recvd), seed in zip(got, (0, 9)):
+            exp = ro.lay.allocate(dtype=torch.float32, fill=True, seed=seed)
+            assert all(torch.equal(recvd[n], exp[n]) for n in exp), seed
+        s.disconnect()
+    finally:
+        ro.close()
+
+
 def test_uncovered_rollout_entries_warn_or_fail():
     """A rollout entry that no sender holds (here: lm_head, the trainer ties its embeddings)
     is reported at connect; require_full_coverage turns the warning into an error."""

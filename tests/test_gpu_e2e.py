@@ -96,3 +96,38 @@ def test_inprocess_send_async_on_gpu():
                 assert st.status == 0 and recv.weights_version == 3
     exp = rl.allocate(device="cuda:0", dtype=torch.bfloat16, fill=True, seed=3)
     assert all(torch.equal(rp[n], exp[n]) for n in exp)
+
+
+@FIRST_RUN
+def test_inprocess_send_async_snapshot_on_gpu():
+    """send_async(snapshot=True) on cuda:0: the copy is enqueued on the caller's stream, the
+    caller overwrites its parameters right away (the next optimizer step) and the worker
+    still receives the values of the call."""
+    import threading
+    from weightbridge_b200 import TransferConfig, WeightReceiver, WeightReceiverController, WeightSender
+    from weightbridge_b200.models.arch import get_arch
+    from weightbridge_b200.parallel.megatron import MegatronLayout
+    from weightbridge_b200.parallel.sglang import SGLangLayout
+    torch.cuda.set_device(0)
+    arch = get_arch("tiny-llama")
+    cfg = TransferConfig(mode="gpu_direct", connect_timeout_s=60, sync_timeout_s=60)
+    with WeightReceiverController(worker_num=1, timeout_s=30) as ctl:
+        url = ctl.serve()
+        rl = SGLangLayout(arch, tp=1)
+        rp = rl.allocate(device="cuda:0", dtype=torch.bfloat16)
+        rm, rv = rl.to_wb(rp)
+        with WeightReceiver(ctl.ipc_name, 0, rm, state_dict=rv, config=cfg) as recv:
+            sl = MegatronLayout(arch, tp=1)
+            sp = sl.allocate(device="cuda:0", dtype=torch.bfloat16, seed=3)
+            sm, sv = sl.to_wb(sp)
+            with WeightSender("gpu_direct", [url], config=cfg) as s:
+                s.connect(sm)
+                th = threading.Thread(target=lambda: recv.request_update(timeout=30))
+                th.start()
+                fut = s.send_async(sv, version=4, snapshot=True)
+                torch._foreach_add_(list(sp.values()), 1.0)
+                st = fut.result(timeout=60)
+                th.join(30)
+                assert st.status == 0 and recv.weights_version == 4
+    exp = rl.allocate(device="cuda:0", dtype=torch.bfloat16, fill=True, seed=3)
+    assert all(torch.equal(rp[n], exp[n]) for n in exp)

@@ -535,6 +535,7 @@ class WeightSender:
         if pool is not None:
             pool.shutdown(wait=True)
             self._pool = None
+        self._snap = self._snap_key = self._snap_future = None
         self._close_watch()
         self._close_arm_channel()
         self._teardown_multicast()
@@ -784,17 +785,29 @@ class WeightSender:
             return self._send(state_dict, -1 if version is None else int(version), subset)
 
     def send_async(self, state_dict: dict[str, Any], version: int | None = None,
-                   names: Iterable[str] | None = None):
+                   names: Iterable[str] | None = None, snapshot: bool = False):
         """Start a sync and return at once with a ``concurrent.futures.Future`` of its
         ``SyncStats``: the handshake and the transfer run on a helper thread while the caller
         goes on (the next forward and backward only read the parameters).  The parameters
         must stay unchanged until ``future.result()`` returns - call it before the next
         optimizer step.  Syncs of one sender run one at a time, in call order.  The transfer
-        is ordered after the work already enqueued on the caller's current stream."""
+        is ordered after the work enqueued on the caller's current stream before this call.
+
+        ``snapshot=True`` first copies the tensors (on the caller's current stream, into
+        buffers this sender keeps: the memory of its shard once more) and syncs the copy, so
+        the caller may update its parameters at once.  The copy waits for the previous
+        snapshot sync to be done with the buffers."""
         subset = self._subset(names)
+        if snapshot:
+            prev = getattr(self, "_snap_future", None)
+            if prev is not None:
+                prev.exception()              # wait; its error is its own future's
+            state_dict = self._take_snapshot(state_dict)
         after = device = None
         if torch.cuda.is_available():
-            after, device = torch.cuda.current_stream(), torch.cuda.current_device()
+            device = torch.cuda.current_device()
+            after = torch.cuda.Event()
+            after.record(torch.cuda.current_stream(device))
         if getattr(self, "_pool", None) is None:
             from concurrent.futures import ThreadPoolExecutor
             self._pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="wbridge-send")
@@ -806,7 +819,38 @@ class WeightSender:
             with nvtx_range("wbridge.send"):
                 return self._send(state_dict, tag, subset, after)
 
-        return self._pool.submit(run)
+        fut = self._pool.submit(run)
+        if snapshot:
+            self._snap_future = fut
+        return fut
+
+    def _take_snapshot(self, state_dict: dict[str, Any]) -> dict[str, Any]:
+        """Copy ``state_dict``'s tensors (lists of views included) into this sender's snapshot
+        buffers, allocated on first use and again when the tensors change."""
+        key = self._key(state_dict)
+        if getattr(self, "_snap_key", None) != key:
+            self._snap = {n: [torch.empty_like(t) for t in v] if isinstance(v, (list, tuple)) else torch.empty_like(v)
+                          for n, v in state_dict.items()}
+            self._snap_key = key
+        src, dst = [], []
+        for n, v in state_dict.items():
+            if isinstance(v, (list, tuple)):
+                src += list(v)
+                dst += self._snap[n]
+            else:
+                src.append(v)
+                dst.append(self._snap[n])
+        torch._foreach_copy_(dst, src)
+        return self._snap
+
+    @staticmethod
+    def _wait_after(stream, after, device) -> None:
+        """Order ``stream`` after ``after`` (an event recorded by the caller, or a stream;
+        ``None``: this thread's current stream on ``device``)."""
+        if isinstance(after, torch.cuda.Event):
+            stream.wait_event(after)
+        else:
+            stream.wait_stream(after if after is not None else torch.cuda.current_stream(device))
 
     def _subset(self, names) -> frozenset | None:
         subset = None if names is None else frozenset(names)
@@ -817,7 +861,7 @@ class WeightSender:
 
     def _send(self, state_dict: dict[str, Any], version: int = -1, subset: frozenset | None = None,
               after: Any = None) -> SyncStats:
-        """``after``: the stream whose enqueued work the transfer must follow (default: this
+        """``after``: the event or stream whose work the transfer must follow (default: this
         thread's current stream on the transfer's device)."""
         if not self.connected or self.metadata is None:
             raise RuntimeError("WeightSender.send requires connect() first")
@@ -873,7 +917,7 @@ class WeightSender:
             if ws.device.type == "cuda":          # pack launches and NCCL sends, ordered on one stream
                 e0, e1 = self._ev
                 with torch.cuda.stream(self._stream):
-                    self._stream.wait_stream(after if after is not None else torch.cuda.current_stream(ws.device))
+                    self._wait_after(self._stream, after, ws.device)
                     e0.record(self._stream)
                     ws.send(self._pg, epoch, self._stream)
                     e1.record(self._stream)
@@ -891,8 +935,7 @@ class WeightSender:
                 prog.launch(epoch)
                 st.device_ms = (time.perf_counter() - t2) * 1e3
             elif pushed:
-                cur = after if after is not None else torch.cuda.current_stream(prog.device)
-                self._stream.wait_stream(cur)
+                self._wait_after(self._stream, after, prog.device)
                 e0, e1 = self._ev
                 with nvtx_range("wbridge.send/transfer"):
                     e0.record(self._stream)
