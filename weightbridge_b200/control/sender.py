@@ -907,7 +907,11 @@ class WeightSender:
             try:
                 tx = time.perf_counter()
                 src = self._wires if cfg.mode in WIRE_MODES else self._program
-                src.set_piece_amax(self._split_amax(epoch, src.piece_amax(getattr(self, "_stream", None))))
+                stream = None
+                if src.device.type == "cuda":     # the amax pass reads what the caller's work wrote
+                    stream = self._stream
+                    self._wait_after(stream, after, src.device)
+                src.set_piece_amax(self._split_amax(epoch, src.piece_amax(stream)))
                 st.exchange_ms = (time.perf_counter() - tx) * 1e3
             except (SessionTimeout, PeerError, ValueError) as e:
                 self._fail_epoch(epoch, str(e))
