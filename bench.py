@@ -434,7 +434,8 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                 "value": round(payload_total / (e2e / 1e3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e, 4), "latency_s": round(e2e / 1e3, 6),
                 "h2d_bytes_per_step": int(G[:, 5].sum()), "d2h_bytes_per_step": int(G[:, 6].sum()),
-                "path": "WeightSender.send + WeightReceiver.request_update (HTTP arm, store handshake, IPC peer stores)",
+                "path": (f"WeightSender.send + WeightReceiver.request_update ({args.arm} arm, store handshake, "
+                         f"{'IPC peer loads' if args.direction == 'pull' else 'IPC peer stores'})"),
                 "sender_breakdown_ms": {"wait_ready": round(float(G[:, 12].max()), 3),
                                         "transfer_kernel": round(float(G[:, 13].max()), 3),
                                         "send_total": round(float(G[:, 14].max()), 3),
