@@ -43,6 +43,7 @@ import torch.distributed as dist
 from ..core.binding import bind
 from ..core.plan import (PhysBinding, PlanBoundsError, Tables, lower_ops, multicast_ok, phys_binding, plan_digest,
                          plan_pair, storage_ranges, validate_tables)
+from ..core.plancache import PlanCache, plan_key, relative_binding
 from ..core.shard import WeightData
 from ..utils.config import WIRE_MODES, TransferConfig, normalize_mode
 from .assign import assign_sources, restrict
@@ -155,6 +156,7 @@ class WeightSender:
         self._imports: dict[int, Any] = {}
         self._rinfo: dict[int, dict] = {}
         self._ops_cache: dict[tuple, list] = {}     # plan ops per (receiver, bindings, names)
+        self._plan_cache = PlanCache(self.config.plan_cache_dir) if self.config.plan_cache_dir else None
         self._bind_version = 0                       # bumped whenever the bound tensors change
         self.uncovered: dict[int, list[str]] = {}    # rank 0, after connect: worker -> entries no sender fills
         self._xchg = None                            # split fp8 blocks shared with other senders
@@ -555,8 +557,10 @@ class WeightSender:
             return
         binding = bind(self.metadata, state_dict)
         device = binding.device
-        sphys = phys_binding(binding)
-        skey = _digest(sphys.to_json())
+        sphys, ptrs = relative_binding(binding)      # address-free: plans survive reallocation
+        src_base = ptrs.__getitem__
+        sjson = sphys.to_json()
+        skey = _digest(sjson)
         pull = cfg.mode == "gpu_direct" and cfg.direction == "pull"
         self._bind_version += 1
         if pull:
@@ -570,14 +574,14 @@ class WeightSender:
             rphys = PhysBinding.from_json(self._rinfo[rep]["binding"])
             ops = plan_pair(sphys, rphys, names=names)
             mc_base = lambda a, va=m.va: va
-            mc_ops = [o for o in ops if multicast_ok(o, lambda a: 0, mc_base)]
-            uni_ops = [o for o in ops if not multicast_ok(o, lambda a: 0, mc_base)]
-            parts.append(lower_ops(mc_ops, lambda a: 0, mc_base, item_bytes=cfg.item_bytes, multicast=True))
+            mc_ops = [o for o in ops if multicast_ok(o, src_base, mc_base)]
+            uni_ops = [o for o in ops if not multicast_ok(o, src_base, mc_base)]
+            parts.append(lower_ops(mc_ops, src_base, mc_base, item_bytes=cfg.item_bytes, multicast=True))
             dst_ranges.append((m.va, m.va + m.size))
             for r in reps:
                 info, imp = self._rinfo[r], self._imports[r]
                 if uni_ops:          # casts, quantised blocks, unaligned copies: one store per replica
-                    parts.append(lower_ops(uni_ops, lambda a: 0, imp.base, item_bytes=cfg.item_bytes, receiver=r))
+                    parts.append(lower_ops(uni_ops, src_base, imp.base, item_bytes=cfg.item_bytes, receiver=r))
                 falloc, foff, _w = info["flags"]
                 flags.append(imp.base(falloc) + foff + 8 * self.rank)
                 dst_ranges += [(imp.base(i), imp.base(i) + int(a["size"])) for i, a in enumerate(info["allocs"])]
@@ -592,12 +596,19 @@ class WeightSender:
             ckey = (r, _digest(info["binding"]), skey, tuple(names))
             ops = self._ops_cache.get(ckey)
             rphys = PhysBinding.from_json(info["binding"])
+            if ops is None and self._plan_cache is not None:
+                dkey = plan_key(sjson, info["binding"], names)
+                ops = self._plan_cache.get(dkey)
+                if ops is None:
+                    ops = plan_pair(sphys, rphys, names=names)
+                    self._plan_cache.put(dkey, ops)
+                self._ops_cache[ckey] = ops
             if ops is None:
                 ops = plan_pair(sphys, rphys, names=names)
                 self._ops_cache[ckey] = ops
             if pull:                       # receivers load the copies; quantised blocks stay pushed
                 ops = [o for o in ops if o.kind in ("quant", "squant")]
-            parts.append(lower_ops(ops, lambda a: 0, imp.base, item_bytes=cfg.item_bytes, receiver=r))
+            parts.append(lower_ops(ops, src_base, imp.base, item_bytes=cfg.item_bytes, receiver=r))
             falloc, foff, _w = info["flags"]
             flags.append(imp.base(falloc) + foff + 8 * self.rank)
             if info["allocs"]:

@@ -52,6 +52,7 @@ class TransferConfig:
     link_gbs: float = 770.0               # per-GPU link bandwidth for the stats' fraction (measured peer copy)
     arm: str = "direct"                   # how each sync is armed: direct (one ZMQ message from sender rank 0
                                           # to every receiver worker) | http (POST /wbridge/receive per sync)
+    plan_cache_dir: str = ""              # senders keep their planned ops here across restarts ("": memory only)
 
     def __post_init__(self):
         self.mode = normalize_mode(self.mode)
