@@ -88,6 +88,11 @@ class WeightReceiver:
         self._bind_gen = 0                            # bumped at every (re)binding of the tensors
         self._rebind_to = None                        # tensors handed to rebind(), bound at the next update
         self._rebind_lock = threading.Lock()
+        self._bound = False                           # tensors bound and exported for this session
+        self._pull_versions, self._pull_prog, self._pull_imports = None, None, {}   # pull direction
+        self._pull_stream = None
+        self._mc = None                               # nvls: (multicast object, replica group)
+        self._fd_server = None                        # nvls: serves the pool's file descriptor
         fd, path = tempfile.mkstemp(prefix=f"wbridge_sched_{rank}_")
         os.close(fd)
         os.unlink(path)
@@ -151,7 +156,7 @@ class WeightReceiver:
         new values, which the caller must not mistake for "no update".
         """
         if state_dict is not None and state_dict is not self.state_dict:
-            if getattr(self, "_bound", False):
+            if self._bound:
                 if not self._same_tensors(state_dict):
                     raise ReceiveError("request_update got tensors other than the ones bound at connect; "
                                        "reconnect the sender to rebind")
@@ -617,7 +622,7 @@ class WeightReceiver:
         """Pull direction: enqueue this worker's pull kernel on ``stream`` with no handshake
         (for callers that know the senders' memory is stable, e.g. device-timed benchmarks).
         Needs one completed ``request_update`` (which compiles the pull program)."""
-        prog = getattr(self, "_pull_prog", None)
+        prog = self._pull_prog
         if prog is None:
             raise RuntimeError("no pull program: the receiver is not in the pull direction or has not synced yet")
         if len(prog.tables):
@@ -628,7 +633,7 @@ class WeightReceiver:
 
     @property
     def pull_program(self):
-        return getattr(self, "_pull_prog", None)
+        return self._pull_prog
 
     # -- NVLink multicast (mode "nvls") -----------------------------------------------------
     def _join_nvls_export(self, binding, info: dict, W: int) -> None:
@@ -675,7 +680,7 @@ class WeightReceiver:
 
     def _leave_nvls(self) -> None:
         """Unbind only once every sender of the group unmapped the object (bounded wait)."""
-        mc = getattr(self, "_mc", None)
+        mc = self._mc
         if not mc:
             return
         m, g = mc
@@ -700,7 +705,7 @@ class WeightReceiver:
         if self._janitor is not None:
             self._janitor.close()
             self._janitor = None
-        for imp in (getattr(self, "_pull_imports", None) or {}).values():
+        for imp in self._pull_imports.values():
             try:
                 imp.close()
             except Exception:
@@ -710,7 +715,7 @@ class WeightReceiver:
             self._leave_nvls()
         except Exception:
             logger.exception("receiver %d: multicast teardown", self.rank)
-        srv = getattr(self, "_fd_server", None)
+        srv = self._fd_server
         if srv is not None:
             srv.close()
             self._fd_server = None

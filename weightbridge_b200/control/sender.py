@@ -164,6 +164,13 @@ class WeightSender:
         self._arm_sock = None                        # rank 0, arm="direct": ROUTER to every receiver worker
         self._arm_idents: dict[int, bytes] = {}
         self._arm_error: str | None = None
+        self._watch = None                           # liveness connections to the workers
+        self._side = None                            # janitor: deletes and error writes off the critical path
+        self._mc: dict = {}                          # nvls: multicast objects by replica group
+        self._mc_created: list = []
+        self._stream = self._ev = None               # transfer stream and its timing events (device tensors)
+        self._pool = None                            # send_async's single worker thread
+        self._snap = self._snap_key = self._snap_future = None   # send_async(snapshot=True) buffers
 
     # -- collectives on the trainer group (no-ops for a single sender) -------------------
     def _all_gather(self, obj):
@@ -265,10 +272,10 @@ class WeightSender:
                              f"receiver {r} left the session (its connection to sender {self.rank} closed)")
 
     def _close_watch(self) -> None:
-        if getattr(self, "_watch", None) is not None:
+        if self._watch is not None:
             self._watch.close()
             self._watch = None
-        if getattr(self, "_side", None) is not None:
+        if self._side is not None:
             self._side.close()
             self._side = None
 
@@ -476,7 +483,7 @@ class WeightSender:
         logger.info("sender %d: %d multicast group(s)", self.rank, len(self._mc))
 
     def _teardown_multicast(self) -> None:
-        mc = getattr(self, "_mc", {}) or {}
+        mc = self._mc
         sess = self.session
         for m, g in mc.values():
             m.teardown_mapping()
@@ -488,7 +495,7 @@ class WeightSender:
                     sess.wait([f"nvls/{g['id']}/unmapped/{x}" for x in g["senders"]], self.config.connect_timeout_s)
             finally:
                 m.teardown_binding()
-        for m in getattr(self, "_mc_created", []):
+        for m in self._mc_created:
             if all(m is not x for x, _g in mc.values()):
                 m.teardown_binding()
         self._mc, self._mc_created = {}, []
@@ -533,7 +540,7 @@ class WeightSender:
     def disconnect(self) -> None:
         """Leave the session (liveness connections say bye, IPC mappings close); waits for a
         sync started with ``send_async``."""
-        pool = getattr(self, "_pool", None)
+        pool = self._pool
         if pool is not None:
             pool.shutdown(wait=True)
             self._pool = None
@@ -567,7 +574,7 @@ class WeightSender:
             self._publish_sender_memory(binding, device)
         parts, flags, dst_ranges = [], [], []
         covered: set[int] = set()
-        for m, g in (getattr(self, "_mc", {}) or {}).values():
+        for m, g in self._mc.values():
             reps = g["replicas"]
             rep = reps[0]
             names = [n for n in self.targets[rep] if subset is None or n in subset]
@@ -789,7 +796,7 @@ class WeightSender:
         restricts the sync to those HF entries (e.g. skip frozen layers); every sender rank
         must pass the same set (push direction of ``gpu_direct`` and ``nvls`` only).  NVTX
         ranges mark the phases (``wbridge.send/arm``, ``/ready``, ``/transfer``)."""
-        if getattr(self, "_pool", None) is not None:     # after send_async: keep the call order
+        if self._pool is not None:     # after send_async: keep the call order
             return self.send_async(state_dict, version, names).result()
         subset = self._subset(names)
         with nvtx_range("wbridge.send"):
@@ -810,7 +817,7 @@ class WeightSender:
         snapshot sync to be done with the buffers."""
         subset = self._subset(names)
         if snapshot:
-            prev = getattr(self, "_snap_future", None)
+            prev = self._snap_future
             if prev is not None:
                 prev.exception()              # wait; its error is its own future's
             state_dict = self._take_snapshot(state_dict)
@@ -819,7 +826,7 @@ class WeightSender:
             device = torch.cuda.current_device()
             after = torch.cuda.Event()
             after.record(torch.cuda.current_stream(device))
-        if getattr(self, "_pool", None) is None:
+        if self._pool is None:
             from concurrent.futures import ThreadPoolExecutor
             self._pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="wbridge-send")
         tag = -1 if version is None else int(version)
@@ -839,7 +846,7 @@ class WeightSender:
         """Copy ``state_dict``'s tensors (lists of views included) into this sender's snapshot
         buffers, allocated on first use and again when the tensors change."""
         key = self._key(state_dict)
-        if getattr(self, "_snap_key", None) != key:
+        if self._snap_key != key:
             self._snap = {n: [torch.empty_like(t) for t in v] if isinstance(v, (list, tuple)) else torch.empty_like(v)
                           for n, v in state_dict.items()}
             self._snap_key = key
