@@ -58,3 +58,38 @@ def test_hf_config_dict_and_unknown_type():
     assert a.family == "llama" and a.head_dim == 16
     with pytest.raises(ValueError):
         ModelArch.from_hf_config(dict(cfg, model_type="mamba"))
+
+
+def test_deepseek_configs_and_converters():
+    """DeepSeek-V3 from a HF config dict and from Megatron MLA args, and the two entry points
+    on its parameters (including SGLang's derived w_kc / w_vc, passed by name)."""
+    arch = get_arch("tiny-deepseek-v3")
+    hf = {"model_type": "deepseek_v3", "hidden_size": arch.hidden, "num_attention_heads": arch.num_heads,
+          "num_key_value_heads": arch.num_heads, "num_hidden_layers": arch.num_layers, "vocab_size": arch.vocab,
+          "intermediate_size": arch.ffn, "moe_intermediate_size": arch.moe_ffn, "n_routed_experts": arch.num_experts,
+          "n_shared_experts": 1, "num_experts_per_tok": arch.top_k, "first_k_dense_replace": 1,
+          "q_lora_rank": arch.q_lora_rank, "kv_lora_rank": arch.kv_lora_rank, "qk_nope_head_dim": arch.qk_nope_dim,
+          "qk_rope_head_dim": arch.qk_rope_dim, "v_head_dim": arch.v_head_dim, "topk_method": "noaux_tc"}
+    assert ModelArch.from_hf_config(hf, name=arch.name) == arch
+    lite = get_arch("tiny-deepseek-v2-lite")
+    hf2 = dict(hf, model_type="deepseek_v2", q_lora_rank=None, num_hidden_layers=2, moe_intermediate_size=128,
+               n_routed_experts=4, n_shared_experts=2, intermediate_size=256, kv_lora_rank=128,
+               qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128, topk_method="greedy")
+    assert ModelArch.from_hf_config(hf2, name=lite.name) == lite
+    args = SimpleNamespace(hidden_size=arch.hidden, num_attention_heads=arch.num_heads, num_layers=arch.num_layers,
+                           ffn_hidden_size=arch.ffn, vocab_size=arch.vocab, num_experts=arch.num_experts,
+                           moe_ffn_hidden_size=arch.moe_ffn, moe_router_topk=arch.top_k,
+                           moe_shared_expert_intermediate_size=arch.shared_ffn, q_lora_rank=arch.q_lora_rank,
+                           kv_lora_rank=arch.kv_lora_rank, qk_head_dim=arch.qk_nope_dim,
+                           qk_pos_emb_head_dim=arch.qk_rope_dim, v_head_dim=arch.v_head_dim,
+                           moe_layer_freq=[0, 1, 1], moe_router_enable_expert_bias=True)
+    assert ModelArch.from_megatron_args(args, family="deepseek_v3", name=arch.name) == arch
+    lay = MegatronLayout(arch, tp=2, tp_rank=1)
+    params = lay.allocate(dtype=torch.float32, fill=False)
+    meta, _v = megatron_to_wb(args, "deepseek-v3", list(params.items()), tp_rank=1, tp_size=2)
+    assert meta == lay.to_wb(params)[0]
+    slay = SGLangLayout(arch, tp=2, tp_rank=0)
+    sparams = slay.allocate(dtype=torch.bfloat16)
+    smeta = sglang_to_wb(SimpleNamespace(hf_config=SimpleNamespace(**hf)), sparams, tp_rank=0, tp_size=2)
+    assert smeta == slay.to_wb(sparams)[0]
+    assert len(smeta.shards("model.layers.2.self_attn.kv_b_proj.weight")) == 3

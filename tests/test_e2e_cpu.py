@@ -32,3 +32,40 @@ def test_redundant_expert_slots_fp8_gloo():
     run("tiny-qwen3-moe", "cpu_direct", [dict(ep=2, ep_rank=0), dict(ep=2, ep_rank=1)],
         dict(tp=1, quant="fp8_experts", expert_slots=[0, 5, 2, 5, 7, 1, 3, 6, 4]),
         dtype=torch.bfloat16, n_syncs=2)
+
+
+def test_deepseek_mla_tp2_ep2_to_tp1_fp8_experts_gloo():
+    """DeepSeek-style model: MLA attention (the worker's derived w_kc / w_vc written with
+    kv_b_proj), dense first layer, shared experts, router bias, fp8 routed experts; four
+    Megatron ranks (TP 2 x EP 2) into one SGLang worker over the wire path."""
+    run("tiny-deepseek-v3", "cpu_direct", [dict(tp=2, ep=2, tp_rank=i % 2, ep_rank=i // 2) for i in range(4)],
+        dict(tp=1, quant="fp8_experts"), dtype=torch.bfloat16, n_syncs=2)
+
+
+def test_deepseek_mla_gpu_direct_protocol_on_host():
+    """The same model through the gpu_direct protocol in one process (work tables run by the
+    C++ executor, host addresses): one op per destination shard, so w_kc / w_vc are written
+    with their transposed strides straight from the trainer's kv up projection."""
+    import threading
+    from weightbridge_b200 import WeightSender
+    from weightbridge_b200.models.arch import get_arch
+    from weightbridge_b200.parallel.megatron import MegatronLayout
+    from tests.test_failures_cpu import Rollout, _cfg
+    cfg = _cfg(mode="gpu_direct")
+    ro = Rollout(cfg, model="tiny-deepseek-v3", layout=dict(tp=1))
+    try:
+        lay = MegatronLayout(get_arch("tiny-deepseek-v3"), tp=1)
+        params = lay.allocate(dtype=torch.float32)
+        meta, views = lay.to_wb(params)
+        with WeightSender("gpu_direct", [ro.url], config=cfg) as s:
+            s.connect(meta)
+            for seed in (3, 4):
+                lay.fill(params, seed=seed)
+                th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+                th.start()
+                s.send(views)
+                th.join(20)
+                exp = ro.lay.allocate(dtype=torch.float32, fill=True, seed=seed)
+                assert all(torch.equal(ro.params[n], exp[n]) for n in exp), seed
+    finally:
+        ro.close()

@@ -29,11 +29,12 @@ def _port():
 class Rollout:
     """FastAPI server + controller + one receiver worker, in this process."""
 
-    def __init__(self, cfg, state_dict=None, meta=None, workers=1, make_receiver=True):
+    def __init__(self, cfg, state_dict=None, meta=None, workers=1, make_receiver=True, model="tiny-llama",
+                 layout=None):
         import uvicorn
         from fastapi import FastAPI
-        arch = get_arch("tiny-llama")
-        self.lay = SGLangLayout(arch, tp=1)
+        arch = get_arch(model)
+        self.lay = SGLangLayout(arch, **(layout or dict(tp=1)))
         self.params = self.lay.allocate(dtype=torch.float32)
         m, views = self.lay.to_wb(self.params)
         self.meta = meta or m

@@ -37,24 +37,40 @@ def megatron_oracle(arch, lay: MegatronLayout, hf):
     for i in range(lay.num_local_layers):
         g = i + lay.layer_offset
         p, m = f"decoder.layers.{i}.", f"model.layers.{g}."
-        q = hf[m + "self_attn.q_proj.weight"].view(G, qpg * hd, H)
-        k = hf[m + "self_attn.k_proj.weight"].view(G, hd, H)
-        v = hf[m + "self_attn.v_proj.weight"].view(G, hd, H)
-        out[p + "self_attention.linear_qkv.weight"] = torch.cat([q, k, v], 1)[r * G_loc:(r + 1) * G_loc].reshape(-1, H)
-        if arch.qkv_bias:
-            qb = hf[m + "self_attn.q_proj.bias"].view(G, qpg * hd)
-            kb = hf[m + "self_attn.k_proj.bias"].view(G, hd)
-            vb = hf[m + "self_attn.v_proj.bias"].view(G, hd)
-            out[p + "self_attention.linear_qkv.bias"] = torch.cat([qb, kb, vb], 1)[r * G_loc:(r + 1) * G_loc].reshape(-1)
-        out[p + "self_attention.linear_qkv.layer_norm_weight"] = hf[m + "input_layernorm.weight"]
-        if arch.qk_norm:
-            out[p + "self_attention.q_layernorm.weight"] = hf[m + "self_attn.q_norm.weight"]
-            out[p + "self_attention.k_layernorm.weight"] = hf[m + "self_attn.k_norm.weight"]
-        out[p + "self_attention.linear_proj.weight"] = hf[m + "self_attn.o_proj.weight"].chunk(tp, 1)[r]
-        if arch.is_moe:
+        if arch.is_mla:                  # head-contiguous up projections: plain row chunks per TP rank
+            a = p + "self_attention."
+            out[p + "input_layernorm.weight"] = hf[m + "input_layernorm.weight"]
+            if arch.q_lora_rank:
+                out[a + "linear_q_down_proj.weight"] = hf[m + "self_attn.q_a_proj.weight"]
+                out[a + "linear_q_up_proj.layer_norm_weight"] = hf[m + "self_attn.q_a_layernorm.weight"]
+                out[a + "linear_q_up_proj.weight"] = hf[m + "self_attn.q_b_proj.weight"].chunk(tp)[r]
+            else:
+                out[a + "linear_q_proj.weight"] = hf[m + "self_attn.q_proj.weight"].chunk(tp)[r]
+            out[a + "linear_kv_down_proj.weight"] = hf[m + "self_attn.kv_a_proj_with_mqa.weight"]
+            out[a + "linear_kv_up_proj.layer_norm_weight"] = hf[m + "self_attn.kv_a_layernorm.weight"]
+            out[a + "linear_kv_up_proj.weight"] = hf[m + "self_attn.kv_b_proj.weight"].chunk(tp)[r]
+            out[a + "linear_proj.weight"] = hf[m + "self_attn.o_proj.weight"].chunk(tp, 1)[r]
+        else:
+            q = hf[m + "self_attn.q_proj.weight"].view(G, qpg * hd, H)
+            k = hf[m + "self_attn.k_proj.weight"].view(G, hd, H)
+            v = hf[m + "self_attn.v_proj.weight"].view(G, hd, H)
+            out[p + "self_attention.linear_qkv.weight"] = torch.cat([q, k, v], 1)[r * G_loc:(r + 1) * G_loc].reshape(-1, H)
+            if arch.qkv_bias:
+                qb = hf[m + "self_attn.q_proj.bias"].view(G, qpg * hd)
+                kb = hf[m + "self_attn.k_proj.bias"].view(G, hd)
+                vb = hf[m + "self_attn.v_proj.bias"].view(G, hd)
+                out[p + "self_attention.linear_qkv.bias"] = torch.cat([qb, kb, vb], 1)[r * G_loc:(r + 1) * G_loc].reshape(-1)
+            out[p + "self_attention.linear_qkv.layer_norm_weight"] = hf[m + "input_layernorm.weight"]
+            if arch.qk_norm:
+                out[p + "self_attention.q_layernorm.weight"] = hf[m + "self_attn.q_norm.weight"]
+                out[p + "self_attention.k_layernorm.weight"] = hf[m + "self_attn.k_norm.weight"]
+            out[p + "self_attention.linear_proj.weight"] = hf[m + "self_attn.o_proj.weight"].chunk(tp, 1)[r]
+        if arch.moe_layer(g):
             out[p + "pre_mlp_layernorm.weight"] = hf[m + "post_attention_layernorm.weight"]
             mb, (gn, un, dn) = arch.moe_block, arch.expert_projs
             out[p + "mlp.router.weight"] = hf[m + f"{mb}.gate.weight"]
+            if arch.router_bias:
+                out[p + "mlp.router.expert_bias"] = hf[m + f"{mb}.gate.e_score_correction_bias"]
             E_loc = arch.num_experts // lay.ep
             for e in range(E_loc):
                 eg = lay.ep_rank * E_loc + e
@@ -64,11 +80,12 @@ def megatron_oracle(arch, lay: MegatronLayout, hf):
                 out[lay._expert_name(i, e, 1)] = torch.cat([gate, up])
                 out[lay._expert_name(i, e, 2)] = hf[x + f"{dn}.weight"].chunk(lay.etp, 1)[lay.etp_rank]
             if arch.shared_ffn:
-                y = m + "mlp.shared_expert."
+                y = m + ("mlp.shared_experts." if arch.is_mla else "mlp.shared_expert.")
                 out[p + "mlp.shared_experts.linear_fc1.weight"] = torch.cat(
                     [hf[y + "gate_proj.weight"].chunk(tp)[r], hf[y + "up_proj.weight"].chunk(tp)[r]])
                 out[p + "mlp.shared_experts.linear_fc2.weight"] = hf[y + "down_proj.weight"].chunk(tp, 1)[r]
-                out[p + "mlp.shared_experts.gate_weight"] = hf[m + "mlp.shared_expert_gate.weight"]
+                if not arch.is_mla:
+                    out[p + "mlp.shared_experts.gate_weight"] = hf[m + "mlp.shared_expert_gate.weight"]
         else:
             out[p + "mlp.linear_fc1.layer_norm_weight"] = hf[m + "post_attention_layernorm.weight"]
             out[p + "mlp.linear_fc1.weight"] = torch.cat([hf[m + "mlp.gate_proj.weight"].chunk(tp)[r],
@@ -90,6 +107,8 @@ MEGATRON_CASES = [
     ("tiny-qwen3-moe", dict(tp=2, ep=2, etp=2, expert_naming="sequential")),
     ("tiny-mixtral", dict(tp=2, ep=2)),
     ("tiny-qwen2-moe", dict(tp=2, ep=2)),
+    ("tiny-deepseek-v3", dict(tp=2, ep=2)),
+    ("tiny-deepseek-v2-lite", dict(tp=2, pp=2)),
 ]
 
 
@@ -142,24 +161,45 @@ def sglang_oracle(arch, lay: SGLangLayout, hf):
     kv0 = lay.kv_head0
     for i in range(arch.num_layers):
         m = f"model.layers.{i}."
-        q = hf[m + "self_attn.q_proj.weight"].chunk(atp)[ar]
-        k = hf[m + "self_attn.k_proj.weight"][kv0 * hd:(kv0 + lay.kv_local) * hd]
-        v = hf[m + "self_attn.v_proj.weight"][kv0 * hd:(kv0 + lay.kv_local) * hd]
-        out[m + "self_attn.qkv_proj.weight"] = torch.cat([q, k, v])
-        if arch.qkv_bias:
-            out[m + "self_attn.qkv_proj.bias"] = torch.cat([
-                hf[m + "self_attn.q_proj.bias"].chunk(atp)[ar],
-                hf[m + "self_attn.k_proj.bias"][kv0 * hd:(kv0 + lay.kv_local) * hd],
-                hf[m + "self_attn.v_proj.bias"][kv0 * hd:(kv0 + lay.kv_local) * hd]])
-        out[m + "self_attn.o_proj.weight"] = hf[m + "self_attn.o_proj.weight"].chunk(atp, 1)[ar]
+        if arch.is_mla:
+            a = m + "self_attn."
+            if arch.q_lora_rank:
+                out[a + "fused_qkv_a_proj_with_mqa.weight"] = torch.cat([hf[a + "q_a_proj.weight"],
+                                                                         hf[a + "kv_a_proj_with_mqa.weight"]])
+                out[a + "q_a_layernorm.weight"] = hf[a + "q_a_layernorm.weight"]
+                out[a + "q_b_proj.weight"] = hf[a + "q_b_proj.weight"].chunk(atp)[ar]
+            else:
+                out[a + "q_proj.weight"] = hf[a + "q_proj.weight"].chunk(atp)[ar]
+                out[a + "kv_a_proj_with_mqa.weight"] = hf[a + "kv_a_proj_with_mqa.weight"]
+            out[a + "kv_a_layernorm.weight"] = hf[a + "kv_a_layernorm.weight"]
+            kvb = hf[a + "kv_b_proj.weight"].chunk(atp)[ar]
+            out[a + "kv_b_proj.weight"] = kvb
+            # what SGLang derives after loading (absorbed MLA): per head, k_nope rows and v rows
+            w = kvb.view(arch.num_heads // atp, arch.qk_nope_dim + arch.v_head_dim, arch.kv_lora_rank)
+            out[a + "w_kc"] = w[:, :arch.qk_nope_dim]
+            out[a + "w_vc"] = w[:, arch.qk_nope_dim:].transpose(1, 2)
+            out[a + "o_proj.weight"] = hf[a + "o_proj.weight"].chunk(atp, 1)[ar]
+        else:
+            q = hf[m + "self_attn.q_proj.weight"].chunk(atp)[ar]
+            k = hf[m + "self_attn.k_proj.weight"][kv0 * hd:(kv0 + lay.kv_local) * hd]
+            v = hf[m + "self_attn.v_proj.weight"][kv0 * hd:(kv0 + lay.kv_local) * hd]
+            out[m + "self_attn.qkv_proj.weight"] = torch.cat([q, k, v])
+            if arch.qkv_bias:
+                out[m + "self_attn.qkv_proj.bias"] = torch.cat([
+                    hf[m + "self_attn.q_proj.bias"].chunk(atp)[ar],
+                    hf[m + "self_attn.k_proj.bias"][kv0 * hd:(kv0 + lay.kv_local) * hd],
+                    hf[m + "self_attn.v_proj.bias"][kv0 * hd:(kv0 + lay.kv_local) * hd]])
+            out[m + "self_attn.o_proj.weight"] = hf[m + "self_attn.o_proj.weight"].chunk(atp, 1)[ar]
         for n in ("input_layernorm.weight", "post_attention_layernorm.weight"):
             out[m + n] = hf[m + n]
         if arch.qk_norm:
             out[m + "self_attn.q_norm.weight"] = hf[m + "self_attn.q_norm.weight"]
             out[m + "self_attn.k_norm.weight"] = hf[m + "self_attn.k_norm.weight"]
-        if arch.is_moe:
+        if arch.moe_layer(i):
             mb, (gn, un, dn) = arch.moe_block, arch.expert_projs
             out[m + f"{mb}.gate.weight"] = hf[m + f"{mb}.gate.weight"]
+            if arch.router_bias:
+                out[m + f"{mb}.gate.e_score_correction_bias"] = hf[m + f"{mb}.gate.e_score_correction_bias"]
             E_loc = arch.num_experts // lay.moe_ep
             w13, w2 = [], []
             for e in range(E_loc):
@@ -172,11 +212,12 @@ def sglang_oracle(arch, lay: SGLangLayout, hf):
             out[m + f"{mb}.experts.w13_weight"] = torch.stack(w13)
             out[m + f"{mb}.experts.w2_weight"] = torch.stack(w2)
             if arch.shared_ffn:
-                y = m + "mlp.shared_expert."
+                y = m + ("mlp.shared_experts." if arch.is_mla else "mlp.shared_expert.")
                 out[y + "gate_up_proj.weight"] = torch.cat([hf[y + "gate_proj.weight"].chunk(tp)[r],
                                                             hf[y + "up_proj.weight"].chunk(tp)[r]])
                 out[y + "down_proj.weight"] = hf[y + "down_proj.weight"].chunk(tp, 1)[r]
-                out[m + "mlp.shared_expert_gate.weight"] = hf[m + "mlp.shared_expert_gate.weight"]
+                if not arch.is_mla:
+                    out[m + "mlp.shared_expert_gate.weight"] = hf[m + "mlp.shared_expert_gate.weight"]
         else:
             out[m + "mlp.gate_up_proj.weight"] = torch.cat([hf[m + "mlp.gate_proj.weight"].chunk(tp)[r],
                                                             hf[m + "mlp.up_proj.weight"].chunk(tp)[r]])
@@ -196,6 +237,9 @@ SGLANG_CASES = [
     ("tiny-qwen3-moe", dict(tp=2, moe_ep=2)),
     ("tiny-mixtral", dict(tp=2, moe_ep=2)),
     ("tiny-qwen2-moe", dict(tp=2, moe_ep=2)),
+    ("tiny-deepseek-v3", dict(tp=2, moe_ep=2)),
+    ("tiny-deepseek-v3", dict(tp=4, attn_tp=1, moe_ep=4)),   # DP-attention: MLA unsharded
+    ("tiny-deepseek-v2-lite", dict(tp=2)),
 ]
 
 
@@ -251,6 +295,12 @@ SYNC_CASES = [
     ("tiny-mixtral", [dict(ep=2, ep_rank=i) for i in range(2)], [dict(tp=2, tp_rank=i, moe_ep=2) for i in range(2)]),
     ("tiny-qwen2-moe", [dict(tp=2, ep=2, tp_rank=i % 2, ep_rank=i // 2) for i in range(4)],
      [dict(tp=2, tp_rank=i, moe_ep=2) for i in range(2)]),
+    ("tiny-deepseek-v3", [dict(tp=2, ep=2, tp_rank=i % 2, ep_rank=i // 2) for i in range(4)],
+     [dict(tp=2, tp_rank=i, moe_ep=2) for i in range(2)]),
+    ("tiny-deepseek-v3", [dict(tp=4, ep=2, etp=2, tp_rank=i, ep_rank=i // 2, etp_rank=i % 2) for i in range(4)],
+     [dict(tp=4, tp_rank=i, attn_tp=1, attn_tp_rank=0, moe_ep=2) for i in range(4)]),
+    ("tiny-deepseek-v2-lite", [dict(tp=1, pp=2, pp_rank=i) for i in range(2)],
+     [dict(tp=4, tp_rank=i) for i in range(4)]),
 ]
 
 
@@ -345,3 +395,35 @@ def test_megatron_to_wb_strict_and_lenient():
         lay.to_wb(params)
     meta, views = lay.to_wb(params, strict=False)
     assert len(meta.names()) == len(get_arch("tiny-llama").hf_tensors())
+
+
+def test_sglang_mla_derived_tensors_are_strided_destinations():
+    """w_kc / w_vc keep SGLang's transposed storage and are extra destination shards of
+    kv_b_proj (its k_nope rows and its v rows of each local head)."""
+    arch = get_arch("tiny-deepseek-v3")
+    lay = SGLangLayout(arch, tp=2, tp_rank=1)
+    params = lay.allocate(dtype=torch.bfloat16)
+    a = "model.layers.0.self_attn."
+    kc, vc = params[a + "w_kc"], params[a + "w_vc"]
+    assert tuple(kc.shape) == (2, 32, 128) and kc.stride() == (128 * 32, 1, 32)
+    assert tuple(vc.shape) == (2, 128, 32) and vc.stride() == (32 * 128, 1, 128)
+    meta, views = lay.to_wb(params)
+    assert meta.shards(a + "kv_b_proj.weight") == [[(128, 256, 256), (0, 128, 128)],
+                                                   [(2, 4, 4), (0, 32, 64), (0, 128, 128)],
+                                                   [(2, 4, 4), (32, 64, 64), (0, 128, 128)]]
+    assert views[a + "kv_b_proj.weight"][1].data_ptr() == kc.data_ptr()
+    with pytest.raises(ValueError, match="fp8_linear"):
+        SGLangLayout(arch, tp=1, quant="fp8_linear")
+
+
+def test_host_reshard_deepseek_fp8_experts():
+    """bf16 Megatron TP2 x EP2 -> SGLang TP2 (EP2) DeepSeek-style: fp8 routed experts, bf16
+    MLA with the derived w_kc / w_vc, dense first layer, shared experts, router bias."""
+    arch = get_arch("tiny-deepseek-v3")
+    meg = [MegatronLayout(arch, tp=2, ep=2, tp_rank=i % 2, ep_rank=i // 2) for i in range(4)]
+    sgl = [SGLangLayout(arch, tp=2, tp_rank=i, moe_ep=2, quant="fp8_experts") for i in range(2)]
+    for params, expected, done, meta in _host_sync(meg, sgl, torch.bfloat16):
+        assert done == set(meta.names())
+        for n in params:
+            assert torch.equal(params[n].view(torch.uint8) if params[n].dtype == torch.float8_e4m3fn else params[n],
+                               expected[n].view(torch.uint8) if expected[n].dtype == torch.float8_e4m3fn else expected[n]), n

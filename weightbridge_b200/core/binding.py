@@ -37,15 +37,24 @@ class Binding:
     device: torch.device = torch.device("cpu")
 
     def find(self, name: str, box: Shard):
-        """(bound shard, BoxCopy) of the local shard that fully contains ``box``."""
+        """(bound shard, BoxCopy) of the first local shard that fully contains ``box``."""
+        found = self.find_all(name, box)
+        if not found:
+            raise ValueError(f"no local shard of {name} contains {box}")
+        return found[0]
+
+    def find_all(self, name: str, box: Shard) -> list:
+        """Every (bound shard, BoxCopy) that fully contains ``box``: several when an entry's
+        shards overlap (redundant expert slots, MLA's ``w_kc`` / ``w_vc`` inside ``kv_b_proj``)."""
+        out = []
         for bs in self.entries[name]:
             try:
                 bc = box_copy(bs.shard, box, bs.strides, None)
             except ValueError:
                 continue
             if bc is not None and bc.numel == shard_numel(box):
-                return bs, bc
-        raise ValueError(f"no local shard of {name} contains {box}")
+                out.append((bs, bc))
+        return out
 
 
 def _as_box_view(t: torch.Tensor, shard: Shard, name: str) -> BoundShard:
@@ -108,8 +117,9 @@ def strided(t: torch.Tensor, offset: int, extents: Sequence[int], strides: Seque
     return torch.as_strided(t, list(extents), list(strides), t.storage_offset() + offset)
 
 
-def _region_views(binding: Binding, name: str, box: Shard, wire: torch.Tensor):
-    bs, bc = binding.find(name, box)
+def _region_views(binding: Binding, name: str, box: Shard, wire: torch.Tensor, bs=None):
+    if bs is None:
+        bs, _bc = binding.find(name, box)
     # wire side: the box packed contiguously; align its strides with the refinement
     wire_bc = box_copy(bs.shard, box, bs.strides, contiguous_strides(shard_extents(box)))
     assert wire_bc is not None
@@ -160,6 +170,10 @@ def unpack_from(binding: Binding, overlap: WeightData, chunk: torch.Tensor) -> N
         for box in shards:
             n = shard_numel(box)
             seg = chunk[off:off + n * dtype.itemsize].view(dtype)
-            local, packed = _region_views(binding, name, box, seg)
-            local.copy_(packed)
+            found = binding.find_all(name, box)
+            if not found:
+                raise ValueError(f"no local shard of {name} contains {box}")
+            for bs, _bc in found:            # every destination holding the region
+                local, packed = _region_views(binding, name, box, seg, bs)
+                local.copy_(packed)
             off += n * dtype.itemsize

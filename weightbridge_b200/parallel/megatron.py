@@ -4,7 +4,11 @@ Covers TP (column/row parallel), PP (layer offset per stage, virtual pipeline ch
 interleaved schedule), EP and expert-TP for MoE,
 grouped-interleaved fused QKV (``[G, q_per_group + 2, head_dim, H]`` per rank), fused
 ``linear_fc1`` (``[gate; up]`` per rank), QKV bias, q/k layernorm and vocab-parallel
-embedding/output layer with vocab padding.
+embedding/output layer with vocab padding.  Multi-head latent attention (``deepseek_v3``):
+the down projections ``linear_q_down_proj`` / ``linear_kv_down_proj`` are replicated, the up
+projections ``linear_q_up_proj`` / ``linear_kv_up_proj`` (with their fused q / kv layernorms)
+are column-parallel over heads, and each head's rows are already HF's ``[nope | rope]`` and
+``[k_nope | v]``, so a rank's shard is one row range of the HF tensor.
 
 Parity: name mapping and un-fusing follow ``wbridge/utils/megatron_utils/qwen2.py:13-80``;
 shard boxes follow ``qwen2.py:83-115`` (box on ``partition_dim`` from the TP rank, vocab
@@ -58,7 +62,7 @@ class MegatronLayout:
             raise ValueError(f"num_kv_heads {a.num_kv_heads} not divisible by TP {self.tp}")
         if a.num_heads % self.tp:
             raise ValueError("num_heads not divisible by TP")
-        if not a.is_moe and a.ffn % self.tp:
+        if (not a.is_moe or a.first_dense_layers) and a.ffn % self.tp:
             raise ValueError("ffn not divisible by TP")
         if a.is_moe and (a.num_experts % self.ep or a.moe_ffn % self.etp):
             raise ValueError("experts not divisible by EP (or expert FFN by ETP)")
@@ -120,18 +124,35 @@ class MegatronLayout:
             out["embedding.word_embeddings.weight"] = (self.padded_vocab // tp, H)
         for i in range(self.num_local_layers):
             p = f"decoder.layers.{i}."
-            out[p + "self_attention.linear_qkv.layer_norm_weight"] = (H,)
-            out[p + "self_attention.linear_qkv.weight"] = (qkv_rows, H)
-            if a.qkv_bias:
-                out[p + "self_attention.linear_qkv.bias"] = (qkv_rows,)
-            if a.qk_norm:
-                out[p + "self_attention.q_layernorm.weight"] = (hd,)
-                out[p + "self_attention.k_layernorm.weight"] = (hd,)
-            out[p + "self_attention.linear_proj.weight"] = (H, a.num_heads * hd // tp)
-            if a.is_moe:
+            if a.is_mla:
+                nh_loc = a.num_heads // tp
+                out[p + "input_layernorm.weight"] = (H,)
+                if a.q_lora_rank:
+                    out[p + "self_attention.linear_q_down_proj.weight"] = (a.q_lora_rank, H)
+                    out[p + "self_attention.linear_q_up_proj.layer_norm_weight"] = (a.q_lora_rank,)
+                    out[p + "self_attention.linear_q_up_proj.weight"] = (nh_loc * hd, a.q_lora_rank)
+                else:
+                    out[p + "self_attention.linear_q_proj.weight"] = (nh_loc * hd, H)
+                out[p + "self_attention.linear_kv_down_proj.weight"] = (a.kv_lora_rank + a.qk_rope_dim, H)
+                out[p + "self_attention.linear_kv_up_proj.layer_norm_weight"] = (a.kv_lora_rank,)
+                out[p + "self_attention.linear_kv_up_proj.weight"] = (nh_loc * (a.qk_nope_dim + a.v_head_dim),
+                                                                       a.kv_lora_rank)
+                out[p + "self_attention.linear_proj.weight"] = (H, nh_loc * a.v_head_dim)
+            else:
+                out[p + "self_attention.linear_qkv.layer_norm_weight"] = (H,)
+                out[p + "self_attention.linear_qkv.weight"] = (qkv_rows, H)
+                if a.qkv_bias:
+                    out[p + "self_attention.linear_qkv.bias"] = (qkv_rows,)
+                if a.qk_norm:
+                    out[p + "self_attention.q_layernorm.weight"] = (hd,)
+                    out[p + "self_attention.k_layernorm.weight"] = (hd,)
+                out[p + "self_attention.linear_proj.weight"] = (H, a.num_heads * hd // tp)
+            if a.moe_layer(i + self.layer_offset):
                 E_loc, I_loc = a.num_experts // self.ep, a.moe_ffn // self.etp
                 out[p + "pre_mlp_layernorm.weight"] = (H,)
                 out[p + "mlp.router.weight"] = (a.num_experts, H)
+                if a.router_bias:
+                    out[p + "mlp.router.expert_bias"] = (a.num_experts,)
                 for e in range(E_loc):
                     out[self._expert_name(i, e, 1)] = (2 * I_loc, H)
                     out[self._expert_name(i, e, 2)] = (H, I_loc)
@@ -139,7 +160,8 @@ class MegatronLayout:
                     S_loc = a.shared_ffn // tp
                     out[p + "mlp.shared_experts.linear_fc1.weight"] = (2 * S_loc, H)
                     out[p + "mlp.shared_experts.linear_fc2.weight"] = (H, S_loc)
-                    out[p + "mlp.shared_experts.gate_weight"] = (1, H)
+                    if not a.is_mla:                   # qwen2_moe gates its shared expert
+                        out[p + "mlp.shared_experts.gate_weight"] = (1, H)
             else:
                 F_loc = a.ffn // tp
                 out[p + "mlp.linear_fc1.layer_norm_weight"] = (H,)
@@ -203,6 +225,10 @@ class MegatronLayout:
         G_loc = G // tp
         gbox = (r * G_loc, (r + 1) * G_loc, G)
 
+        if a.is_mla:
+            got = self._split_mla(rest, param, p)
+            if got is not None:
+                return got
         if rest == "self_attention.linear_qkv.weight":
             v = param.view(G_loc, (qpg + 2) * hd, H)
             return [
@@ -240,19 +266,21 @@ class MegatronLayout:
             f = F // tp
             return [(p + "mlp.down_proj.weight", param, [(0, H, H), (r * f, (r + 1) * f, F)])]
         if rest == "mlp.shared_experts.linear_fc1.weight":
-            S = a.shared_ffn
+            S, sp = a.shared_ffn, p + a.shared_prefix
             sl = S // tp
             box = [(r * sl, (r + 1) * sl, S), (0, H, H)]
-            return [(p + "mlp.shared_expert.gate_proj.weight", param[:sl], box),
-                    (p + "mlp.shared_expert.up_proj.weight", param[sl:], box)]
+            return [(sp + "gate_proj.weight", param[:sl], box),
+                    (sp + "up_proj.weight", param[sl:], box)]
         if rest == "mlp.shared_experts.linear_fc2.weight":
-            S = a.shared_ffn
+            S, sp = a.shared_ffn, p + a.shared_prefix
             sl = S // tp
-            return [(p + "mlp.shared_expert.down_proj.weight", param, [(0, H, H), (r * sl, (r + 1) * sl, S)])]
+            return [(sp + "down_proj.weight", param, [(0, H, H), (r * sl, (r + 1) * sl, S)])]
         if rest == "mlp.shared_experts.gate_weight":
             return [(p + "mlp.shared_expert_gate.weight", param, full(param.shape))]
         if rest == "mlp.router.weight":
             return [(p + f"{a.moe_block}.gate.weight", param, full(param.shape))]
+        if rest == "mlp.router.expert_bias":
+            return [(p + f"{a.moe_block}.gate.e_score_correction_bias", param, full(param.shape))]
         em = (re.match(r"mlp\.experts\.linear_fc([12])\.weight(\d+)$", rest)
               or re.match(r"mlp\.experts\.local_experts\.(?P<e>\d+)\.linear_fc(?P<fc>[12])\.weight$", rest))
         if em:
@@ -272,6 +300,37 @@ class MegatronLayout:
                         (q + f"{un}.weight", param[i_loc:], [ibox, (0, H, H)])]
             return [(q + f"{dn}.weight", param, [(0, H, H), ibox])]
         raise UnknownParameter(f"unknown Megatron parameter {name!r}")
+
+    def _split_mla(self, rest: str, param: torch.Tensor, p: str) -> list | None:
+        """The MLA attention params of one layer (``None``: not an MLA attention param)."""
+        a, tp, r = self.arch, self.tp, self.tp_rank
+        H, nh = a.hidden, a.num_heads
+        nh_loc = nh // tp
+        full = lambda shape: [(0, d, d) for d in shape]         # noqa: E731
+
+        def heads(rows_per_head: int, cols: int):              # column-parallel over heads
+            R = nh * rows_per_head
+            return [(r * nh_loc * rows_per_head, (r + 1) * nh_loc * rows_per_head, R), (0, cols, cols)]
+
+        if rest == "self_attention.linear_q_down_proj.weight":
+            return [(p + "self_attn.q_a_proj.weight", param, full(param.shape))]
+        if rest in ("self_attention.linear_q_up_proj.layer_norm_weight", "self_attention.q_layernorm.weight"):
+            return [(p + "self_attn.q_a_layernorm.weight", param, full(param.shape))]
+        if rest == "self_attention.linear_q_up_proj.weight":
+            return [(p + "self_attn.q_b_proj.weight", param, heads(a.head_dim, a.q_lora_rank))]
+        if rest == "self_attention.linear_q_proj.weight":
+            return [(p + "self_attn.q_proj.weight", param, heads(a.head_dim, H))]
+        if rest == "self_attention.linear_kv_down_proj.weight":
+            return [(p + "self_attn.kv_a_proj_with_mqa.weight", param, full(param.shape))]
+        if rest in ("self_attention.linear_kv_up_proj.layer_norm_weight", "self_attention.kv_layernorm.weight"):
+            return [(p + "self_attn.kv_a_layernorm.weight", param, full(param.shape))]
+        if rest == "self_attention.linear_kv_up_proj.weight":
+            return [(p + "self_attn.kv_b_proj.weight", param, heads(a.qk_nope_dim + a.v_head_dim, a.kv_lora_rank))]
+        if rest == "self_attention.linear_proj.weight":
+            K = nh * a.v_head_dim
+            k = K // tp
+            return [(p + "self_attn.o_proj.weight", param, [(0, H, H), (r * k, (r + 1) * k, K)])]
+        return None
 
     def to_wb(self, named_params: dict[str, torch.Tensor] | Iterable[tuple[str, torch.Tensor]],
               strict: bool = True) -> tuple[WeightData, dict[str, torch.Tensor]]:
@@ -313,7 +372,8 @@ def convert_to_wb(args: Any, model_name: str, named_tensors, *, tp_rank: int | N
         vpp_size = mpu.get_virtual_pipeline_model_parallel_world_size() or 1
         vpp_rank = (mpu.get_virtual_pipeline_model_parallel_rank() or 0) if vpp_size > 1 else 0
     name = model_name.lower()
-    family = ("mixtral" if "mixtral" in name else "qwen2_moe" if "qwen2" in name and "moe" in name else
+    family = ("deepseek_v3" if "deepseek" in name else
+              "mixtral" if "mixtral" in name else "qwen2_moe" if "qwen2" in name and "moe" in name else
               "qwen3_moe" if "moe" in name else "qwen3" if "qwen3" in name else
               "qwen2" if "qwen2" in name else "llama" if "llama" in name else None)
     if family is None:

@@ -8,6 +8,13 @@ weights are ``float8_e4m3fn`` and each has an fp32 ``*_scale_inv`` of 128 x 128 
 scales.  Attention may use its own TP size (DP-attention); when TP exceeds the KV-head
 count each rank holds one replicated KV head.
 
+Multi-head latent attention (``deepseek_v3``): ``fused_qkv_a_proj_with_mqa`` is
+``[q_a_proj; kv_a_proj_with_mqa]`` (replicated), ``q_b_proj`` / ``kv_b_proj`` are split over
+heads, and the absorbed-attention copies of ``kv_b_proj`` that SGLang derives after loading
+are refreshed by the same sync: ``self_attn.w_kc`` (``[heads, nope, kv_lora]``, stored
+transposed) and ``self_attn.w_vc`` (``[heads, kv_lora, v]``, a transposed view of
+``[heads, v, kv_lora]``) are extra destination shards of ``kv_b_proj``.
+
 Parity: the routing and the column/row partition rules follow
 ``wbridge/utils/sglang_utils/qwen2.py:1-173`` and ``sglang_utils/__init__.py:15-52``.
 Differences: the q/k/v split uses SGLang's ``[q; k; v]`` order rather than a grouped
@@ -29,6 +36,8 @@ from ..ops.quant_ref import block_quant_fp8_ref
 from .megatron import UnknownParameter
 
 SKIP_PATTERNS = ("inv_freq", "cos_cached", "sin_cached", "projector", "vision_tower")
+# MLA tensors SGLang keeps with transposed storage: allocated as [..., b, a], viewed as [..., a, b]
+TRANSPOSED = ("self_attn.w_kc", "self_attn.w_vc")
 
 
 @dataclass
@@ -66,6 +75,9 @@ class SGLangLayout:
                 raise ValueError("expert FFN not divisible by the MoE TP size")
         if self.quant not in (None, "fp8_experts", "fp8_linear"):
             raise ValueError(f"unknown quant mode {self.quant!r}")
+        if self.quant == "fp8_linear" and a.is_mla:
+            raise ValueError("fp8_linear: MLA attention stays bf16 here (w_kc / w_vc are bf16 copies of "
+                             "kv_b_proj); use quant='fp8_experts'")
         if self.expert_slots is not None:
             per_layer = list(self.expert_slots)
             if per_layer and not isinstance(per_layer[0], (list, tuple)):
@@ -136,26 +148,32 @@ class SGLangLayout:
         for i in range(a.num_layers):
             p = f"model.layers.{i}."
             out[p + "input_layernorm.weight"] = ((H,), "other")
-            out[p + "self_attn.qkv_proj.weight"] = ((q_loc + 2 * kv_loc, H), "linear")
-            if a.qkv_bias:
-                out[p + "self_attn.qkv_proj.bias"] = ((q_loc + 2 * kv_loc,), "other")
-            if a.qk_norm:
-                out[p + "self_attn.q_norm.weight"] = ((hd,), "other")
-                out[p + "self_attn.k_norm.weight"] = ((hd,), "other")
-            out[p + "self_attn.o_proj.weight"] = ((H, q_loc), "linear")
+            if a.is_mla:
+                out.update(self._mla_specs(p))
+            else:
+                out[p + "self_attn.qkv_proj.weight"] = ((q_loc + 2 * kv_loc, H), "linear")
+                if a.qkv_bias:
+                    out[p + "self_attn.qkv_proj.bias"] = ((q_loc + 2 * kv_loc,), "other")
+                if a.qk_norm:
+                    out[p + "self_attn.q_norm.weight"] = ((hd,), "other")
+                    out[p + "self_attn.k_norm.weight"] = ((hd,), "other")
+                out[p + "self_attn.o_proj.weight"] = ((H, q_loc), "linear")
             out[p + "post_attention_layernorm.weight"] = ((H,), "other")
-            if a.is_moe:
+            if a.moe_layer(i):
                 E_loc = len(self.local_experts(i))
                 I_loc = a.moe_ffn // self.moe_tp
                 mb = a.moe_block
                 out[p + f"{mb}.gate.weight"] = ((a.num_experts, H), "other")
+                if a.router_bias:
+                    out[p + f"{mb}.gate.e_score_correction_bias"] = ((a.num_experts,), "other")
                 out[p + f"{mb}.experts.w13_weight"] = ((E_loc, 2 * I_loc, H), "expert")
                 out[p + f"{mb}.experts.w2_weight"] = ((E_loc, H, I_loc), "expert")
-                if a.shared_ffn:                       # shared expert: a TP-split dense MLP + its gate
-                    S_loc = a.shared_ffn // self.tp
-                    out[p + "mlp.shared_expert.gate_up_proj.weight"] = ((2 * S_loc, H), "linear")
-                    out[p + "mlp.shared_expert.down_proj.weight"] = ((H, S_loc), "linear")
-                    out[p + "mlp.shared_expert_gate.weight"] = ((1, H), "other")
+                if a.shared_ffn:                       # shared experts: a TP-split dense MLP (+ a gate)
+                    S_loc, sp = a.shared_ffn // self.tp, p + a.shared_prefix
+                    out[sp + "gate_up_proj.weight"] = ((2 * S_loc, H), "linear")
+                    out[sp + "down_proj.weight"] = ((H, S_loc), "linear")
+                    if not a.is_mla:
+                        out[p + "mlp.shared_expert_gate.weight"] = ((1, H), "other")
             else:
                 F_loc = a.ffn // self.tp
                 out[p + "mlp.gate_up_proj.weight"] = ((2 * F_loc, H), "linear")
@@ -167,6 +185,25 @@ class SGLangLayout:
             if self._fp8(kind):
                 lead, (r, c) = shape[:-2], shape[-2:]
                 out[name + "_scale_inv"] = (tuple(lead) + self._scales(r, c), "scale")
+        return out
+
+    def _mla_specs(self, p: str) -> dict[str, tuple[tuple[int, ...], str]]:
+        """One layer's MLA attention parameters: name -> (local shape, kind)."""
+        a = self.arch
+        H, nh_loc, kvl = a.hidden, a.num_heads // self.attn_tp, a.kv_lora_rank
+        out = {}
+        if a.q_lora_rank:
+            out[p + "self_attn.fused_qkv_a_proj_with_mqa.weight"] = ((a.q_lora_rank + kvl + a.qk_rope_dim, H), "other")
+            out[p + "self_attn.q_a_layernorm.weight"] = ((a.q_lora_rank,), "other")
+            out[p + "self_attn.q_b_proj.weight"] = ((nh_loc * a.head_dim, a.q_lora_rank), "linear")
+        else:
+            out[p + "self_attn.q_proj.weight"] = ((nh_loc * a.head_dim, H), "linear")
+            out[p + "self_attn.kv_a_proj_with_mqa.weight"] = ((kvl + a.qk_rope_dim, H), "other")
+        out[p + "self_attn.kv_a_layernorm.weight"] = ((kvl,), "other")
+        out[p + "self_attn.kv_b_proj.weight"] = ((nh_loc * (a.qk_nope_dim + a.v_head_dim), kvl), "linear")
+        out[p + "self_attn.o_proj.weight"] = ((a.hidden, nh_loc * a.v_head_dim), "linear")
+        out[p + "self_attn.w_kc"] = ((nh_loc, a.qk_nope_dim, kvl), "derived")
+        out[p + "self_attn.w_vc"] = ((nh_loc, kvl, a.v_head_dim), "derived")
         return out
 
     def param_dtype(self, name: str, kind: str, dtype: torch.dtype) -> torch.dtype:
@@ -193,11 +230,14 @@ class SGLangLayout:
         weights (quantised where the layout is fp8), i.e. what a sync should produce.
         ``pool`` places every parameter in one allocation (one CUDA IPC handle to export
         instead of one per parameter), each start aligned to 256 bytes."""
-        specs = [(n, s, self.param_dtype(n, k, dtype)) for n, (s, k) in self.param_specs().items()]
+        specs = [(n, _storage_shape(n, s), self.param_dtype(n, k, dtype)) for n, (s, k) in self.param_specs().items()]
         if pool or buffer is not None:
             params = pooled_zeros(specs, device, buffer=buffer)
         else:
             params = {n: torch.zeros(s, dtype=dt, device=device) for n, s, dt in specs}
+        for n in params:
+            if n.endswith(TRANSPOSED):
+                params[n] = params[n].transpose(-1, -2)
         if fill:
             self.fill_expected(params, seed, src_dtype=dtype)
         return params
@@ -262,6 +302,10 @@ class SGLangLayout:
             raise UnknownParameter(f"unknown SGLang parameter {name!r}")
         p = f"model.layers.{m.group(1)}."
         rest = m.group(2)
+        if a.is_mla:
+            got = self._split_mla(rest, param, p)
+            if got is not None:
+                return got
         q_loc = a.num_heads // self.attn_tp * hd
         kv_loc = self.kv_local * hd
         ar = self.attn_tp_rank
@@ -289,10 +333,10 @@ class SGLangLayout:
         if rest == "self_attn.o_proj.weight":
             box = [(0, H, H), qbox]
             return with_scale(name, param, box, scale, block_box(box) if scale is not None else None)
-        if rest in ("mlp.gate_up_proj.weight", "mlp.shared_expert.gate_up_proj.weight"):
-            shared = rest.startswith("mlp.shared_expert.")
+        if rest in ("mlp.gate_up_proj.weight", a.shared_prefix + "gate_up_proj.weight"):
+            shared = rest != "mlp.gate_up_proj.weight"
             F = a.shared_ffn if shared else a.ffn
-            mod = "mlp.shared_expert." if shared else "mlp."
+            mod = a.shared_prefix if shared else "mlp."
             f = F // self.tp
             fbox = (self.tp_rank * f, (self.tp_rank + 1) * f, F)
             box = [fbox, (0, H, H)]
@@ -306,8 +350,8 @@ class SGLangLayout:
                     sv = scale[j * f // bn:(j + 1) * f // bn]
                 out += with_scale(f"{p}{mod}{nm}.weight", param[j * f:(j + 1) * f], box, sv, sb)
             return out
-        if rest in ("mlp.down_proj.weight", "mlp.shared_expert.down_proj.weight"):
-            F = a.shared_ffn if rest.startswith("mlp.shared_expert.") else a.ffn
+        if rest in ("mlp.down_proj.weight", a.shared_prefix + "down_proj.weight"):
+            F = a.shared_ffn if rest != "mlp.down_proj.weight" else a.ffn
             f = F // self.tp
             box = [(0, H, H), (self.tp_rank * f, (self.tp_rank + 1) * f, F)]
             return with_scale(name, param, box, scale, block_box(box) if scale is not None else None)
@@ -335,6 +379,39 @@ class SGLangLayout:
             return out
         # replicated tensors: norms, router, q/k norm
         return [(name, param, full(param.shape), None)]
+
+    def _split_mla(self, rest: str, param: torch.Tensor, p: str) -> list | None:
+        """The MLA attention params of one layer (``None``: not one of them, or replicated
+        under its HF name)."""
+        a = self.arch
+        H, nh = a.hidden, a.num_heads
+        nh_loc, ar = nh // self.attn_tp, self.attn_tp_rank
+        nope, v, kvl = a.qk_nope_dim, a.v_head_dim, a.kv_lora_rank
+        full = lambda shape: [(0, d, d) for d in shape]         # noqa: E731
+        hbox = (ar * nh_loc, (ar + 1) * nh_loc, nh)
+
+        def heads(rows_per_head: int, cols: int):
+            return [(ar * nh_loc * rows_per_head, (ar + 1) * nh_loc * rows_per_head, nh * rows_per_head),
+                    (0, cols, cols)]
+
+        if rest == "self_attn.fused_qkv_a_proj_with_mqa.weight":
+            ql = a.q_lora_rank
+            return [(p + "self_attn.q_a_proj.weight", param[:ql], full((ql, H)), None),
+                    (p + "self_attn.kv_a_proj_with_mqa.weight", param[ql:], full((kvl + a.qk_rope_dim, H)), None)]
+        if rest == "self_attn.q_b_proj.weight":
+            return [(p + rest, param, heads(a.head_dim, a.q_lora_rank), None)]
+        if rest == "self_attn.q_proj.weight":
+            return [(p + rest, param, heads(a.head_dim, H), None)]
+        if rest == "self_attn.kv_b_proj.weight":
+            return [(p + rest, param, heads(nope + v, kvl), None)]
+        if rest == "self_attn.o_proj.weight":
+            return [(p + rest, param, [(0, H, H), (ar * nh_loc * v, (ar + 1) * nh_loc * v, nh * v)], None)]
+        if rest == "self_attn.w_kc":          # [heads, nope, kv_lora]: the k_nope rows of each head
+            return [(p + "self_attn.kv_b_proj.weight", param, [hbox, (0, nope, nope + v), (0, kvl, kvl)], None)]
+        if rest == "self_attn.w_vc":          # [heads, kv_lora, v]: the v rows of each head, transposed
+            return [(p + "self_attn.kv_b_proj.weight", param.transpose(-1, -2),
+                     [hbox, (nope, nope + v, nope + v), (0, kvl, kvl)], None)]
+        return None
 
     def to_wb(self, params: dict[str, torch.Tensor], strict: bool = True) -> tuple[WeightData, dict[str, torch.Tensor]]:
         """(metadata, HF name -> view) for this rank's SGLang parameters.  fp8 entries carry
@@ -371,6 +448,12 @@ class SGLangLayout:
         return WeightData(meta), views
 
 
+def _storage_shape(name: str, shape: tuple[int, ...]) -> tuple[int, ...]:
+    if name.endswith(TRANSPOSED):
+        return tuple(shape[:-2]) + (shape[-1], shape[-2])
+    return tuple(shape)
+
+
 def pooled_zeros(specs, device, align: int = 256, buffer: torch.Tensor | None = None) -> dict[str, torch.Tensor]:
     """Zero tensors of the given (name, shape, dtype) carved out of one allocation (a new
     one, or ``buffer``: a uint8 tensor such as a VmmPool's parameter region)."""
@@ -403,7 +486,9 @@ def convert_to_wb(model_config: Any, state_dict: dict[str, torch.Tensor], tp_ran
                   moe_ep: int = 1, quant: str | None = None) -> WeightData:
     """SGLang state_dict -> WeightData (the reference's signature,
     ``wbridge/utils/sglang_utils/__init__.py:15-52``); ``convert_to_wb_and_views`` also
-    returns the views the receiver binds."""
+    returns the views the receiver binds.  MLA models (DeepSeek-V2/V3): SGLang keeps
+    ``self_attn.w_kc`` / ``self_attn.w_vc`` as attributes, not parameters; add them to
+    ``state_dict`` under those names so the sync refreshes them with ``kv_b_proj``."""
     return convert_to_wb_and_views(model_config, state_dict, tp_rank, tp_size, attn_tp_rank,
                                    attn_tp_size, moe_ep, quant)[0]
 
