@@ -125,3 +125,53 @@ def test_random_fsdp_shardings_cover_exactly(model, world, dim, rtp, rrank):
             assert torch.isnan(rp[n][valid:]).all()
         else:
             assert torch.equal(rp[n], exp[n]), n
+
+
+@settings(max_examples=20, deadline=None)
+@given(mtp=st.sampled_from([1, 2, 4]), mpp=st.sampled_from([1, 3]), ep=st.sampled_from([1, 2]),
+       etp=st.sampled_from([1, 2]), rtp=st.sampled_from([1, 2, 4]), attn_dp=st.booleans(),
+       fp8=st.booleans(), rrank=st.integers(0, 3))
+def test_random_mla_moe_layouts_cover_exactly(mtp, mpp, ep, etp, rtp, attn_dp, fp8, rrank):
+    """DeepSeek-style layouts (MLA, dense first layer, shared experts, router bias) from random
+    Megatron TP x PP x EP x ETP into a random SGLang rank, fp8 experts or not: every bound
+    element (the derived w_kc / w_vc included) gets its value, vocab padding stays poisoned.
+    Expert slices that cut fp8 blocks are quantised with the block amax merged over senders."""
+    import numpy as np
+    from weightbridge_b200.ops.executor import cpu_piece_amax
+    arch = get_arch("tiny-deepseek-v3")
+    sgl = dict(tp=rtp, tp_rank=rrank % rtp, moe_ep=rtp if fp8 else 1, quant="fp8_experts" if fp8 else None)
+    if attn_dp:
+        sgl.update(attn_tp=1, attn_tp_rank=0)
+    rl = SGLangLayout(arch, **sgl)
+    rp = rl.allocate(dtype=torch.bfloat16, pool=True)
+    pool = torch.empty(0, dtype=torch.uint8).set_(next(iter(rp.values())).untyped_storage())
+    pool.fill_(0xFF)                       # one allocation: poison it whole (w_kc / w_vc are transposed views)
+    rmeta, rviews = rl.to_wb(rp)
+    rphys = phys_binding(bind(rmeta, rviews))
+    keep, tables = [], []
+    for p in range(mpp):
+        for e in range(ep):
+            for t in range(max(mtp, etp)):
+                lay = MegatronLayout(arch, tp=mtp, pp=mpp, ep=ep, etp=etp, tp_rank=t % mtp, pp_rank=p,
+                                     ep_rank=e, etp_rank=t % etp)
+                prm = lay.allocate(dtype=torch.bfloat16)
+                keep.append(prm)
+                tables.append(lower_ops(plan_pair(phys_binding(bind(*lay.to_wb(prm))), rphys), ABS, ABS,
+                                        item_bytes=4096, receiver=0))
+    block_amax = {}
+    for tb in tables:                      # the senders' amax exchange, in one process
+        for k, v in zip(tb.piece_keys, cpu_piece_amax(tb)):
+            block_amax[k] = max(block_amax.get(k, 0.0), float(v))
+    for tb in tables:
+        cpu_execute(tb, np.array([block_amax[k] for k in tb.piece_keys], dtype=np.float32))
+    exp = rl.allocate(dtype=torch.bfloat16, fill=True)
+    for n in rp:
+        a, b = rp[n], exp[n]
+        if a.dtype == torch.float8_e4m3fn:
+            a, b = a.view(torch.uint8), b.view(torch.uint8)
+        if "embed_tokens" in n or "lm_head" in n:
+            rows = rl.padded_vocab // rl.tp
+            valid = max(0, min(rows, arch.vocab - rl.tp_rank * rows))
+            assert torch.isnan(rp[n][valid:]).all()
+            a, b = a[:valid], b[:valid]
+        assert torch.equal(a, b), n
