@@ -12,7 +12,7 @@ import torch
 
 from weightbridge_b200 import WeightData
 from weightbridge_b200.core.binding import bind, pack_into, unpack_from, strided
-from weightbridge_b200.core.shard import (align_shards, box_copy, check_shard_compatibility,
+from weightbridge_b200.core.shard import (align_shards, box_copies, box_copy, check_shard_compatibility,
                                           coalesce)
 
 # (sender, receiver, expected aligned sender, expected aligned receiver); None = incompatible
@@ -117,8 +117,28 @@ def test_overlap_disjoint_is_empty():
 
 
 def test_overlap_incompatible_raises():
-    with pytest.raises(ValueError):
-        WeightData.compute_overlap(_meta([(5, 13, 24)]), _meta([(0, 4, 4), (0, 6, 6)]))
+    with pytest.raises(ValueError):             # 4 x 6 against 6 x 4: no common refinement
+        WeightData.compute_overlap(_meta([(0, 4, 4), (0, 6, 6)]), _meta([(0, 6, 6), (0, 4, 4)]))
+    with pytest.raises(ValueError):             # different logical sizes
+        WeightData.compute_overlap(_meta([(0, 24, 24)]), _meta([(0, 5, 5), (0, 5, 5)]))
+
+
+def test_overlap_cuts_a_range_through_rows_into_rectangles():
+    """A flat range that starts and ends inside rows of the other side's 4 x 6 box has no
+    single rectangular overlap; it is cut at the row boundaries (the pair-form check keeps
+    the reference's answer, no common refinement)."""
+    assert check_shard_compatibility([(5, 13, 24)], [(0, 4, 4), (0, 6, 6)]) is None
+    ov = WeightData.compute_overlap(_meta([(5, 13, 24)]), _meta([(0, 4, 4), (0, 6, 6)]))
+    assert ov.shards("weight") == [[(0, 1, 4), (5, 6, 6)], [(1, 2, 4), (0, 6, 6)], [(2, 3, 4), (0, 1, 6)]]
+    assert ov.total_nbytes() == 8 * 4
+    flat = torch.arange(24, dtype=torch.float32)
+    s = _meta([(5, 13, 24)])
+    packed = WeightData.pack_for(s, {"weight": flat[5:13]}, ov)
+    got = torch.full((4, 6), -1.0)
+    unpack_from(bind(_meta([(0, 4, 4), (0, 6, 6)]), {"weight": got}), ov, packed)
+    exp = torch.full((24,), -1.0)
+    exp[5:13] = flat[5:13]
+    assert torch.equal(got.reshape(-1), exp)
 
 
 def test_pack_for_roundtrip():
@@ -283,3 +303,37 @@ def test_pack_unpack_multi_receiver(seed):
             pack_into(b, ov, buf)
             unpack_from(bind(rm, {"w": r_tensors[ri]}), ov, buf)
     assert torch.equal(torch.cat(r_tensors), full.reshape(-1))
+
+
+@pytest.mark.parametrize("seed", range(80))
+def test_box_copies_cut_ranges_against_dense_oracle(seed):
+    """A flat range (an FSDP-style row range) against a partial N-d box of the same tensor,
+    either side as the source: the pieces write every element of the intersection exactly
+    once, with the right value, and nothing else."""
+    import math
+    rng = random.Random(seed)
+    shape = [rng.choice([2, 3, 4, 6]) for _ in range(rng.choice([2, 3]))]
+    n = math.prod(shape)
+    a = rng.randrange(n)
+    b = rng.randrange(a + 1, n + 1)
+    flat, box = [(a, b, n)], _random_box(rng, shape)
+    logical = torch.arange(1, n + 1, dtype=torch.float64)
+    in_box = logical.reshape(shape)[_logical_region(box)]          # values = logical index + 1
+    in_range = ((in_box - 1) >= a) & ((in_box - 1) < b)
+    if rng.random() < 0.5:                                          # flat source, box destination
+        src, dst = logical[a:b].clone(), torch.zeros(in_box.shape, dtype=torch.float64)
+        bcs = box_copies(flat, box)
+        expect = torch.where(in_range, in_box, torch.zeros_like(in_box))
+    else:                                                           # box source, flat destination
+        src, dst = in_box.contiguous(), torch.zeros(b - a, dtype=torch.float64)
+        bcs = box_copies(box, flat)
+        full = torch.zeros(n, dtype=torch.float64)
+        full[(in_box[in_range] - 1).long()] = in_box[in_range]
+        expect = full[a:b]
+    count = torch.zeros_like(dst)
+    for bc in bcs:
+        strided(dst, bc.dst_offset, bc.extents, bc.dst_strides).copy_(
+            strided(src, bc.src_offset, bc.extents, bc.src_strides))
+        strided(count, bc.dst_offset, bc.extents, bc.dst_strides).add_(1)
+    assert torch.equal(dst, expect)
+    assert (count <= 1).all() and int(count.sum()) == int(in_range.sum())

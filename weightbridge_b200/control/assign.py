@@ -16,7 +16,7 @@ from __future__ import annotations
 import json
 from collections import defaultdict
 
-from ..core.shard import WeightData, box_copy
+from ..core.shard import WeightData, box_copies
 
 
 def _key(shards) -> str:
@@ -41,10 +41,10 @@ def replica_groups(sender_metas: list[WeightData]) -> dict[str, list[list[int]]]
                 for sa in a:
                     for sb in b:
                         try:
-                            bc = box_copy(sa, sb)
+                            bcs = box_copies(sa, sb)
                         except ValueError:
                             raise ValueError(f"senders {glist[i]} and {glist[j]} hold incompatible shards of {name!r}")
-                        if bc is not None:
+                        if bcs:
                             raise ValueError(
                                 f"Partial shard overlap for {name!r} between sender ranks {glist[i][0]} and "
                                 f"{glist[j][0]}: senders must have identical or non-overlapping shards")
@@ -56,9 +56,7 @@ def _overlap_bytes(s_shards, r_shards, itemsize: int) -> int:
     n = 0
     for a in s_shards:
         for b in r_shards:
-            bc = box_copy(a, b)
-            if bc is not None:
-                n += bc.numel
+            n += sum(bc.numel for bc in box_copies(a, b))
     return n * itemsize
 
 

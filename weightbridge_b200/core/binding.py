@@ -19,7 +19,7 @@ from typing import Any, Sequence
 
 import torch
 
-from .shard import (Shard, WeightData, box_copy, contiguous_strides, shard_extents,
+from .shard import (Shard, WeightData, box_copies, contiguous_strides, shard_extents,
                     shard_numel)
 
 
@@ -49,11 +49,11 @@ class Binding:
         out = []
         for bs in self.entries[name]:
             try:
-                bc = box_copy(bs.shard, box, bs.strides, None)
+                bcs = box_copies(bs.shard, box, bs.strides, None)
             except ValueError:
                 continue
-            if bc is not None and bc.numel == shard_numel(box):
-                out.append((bs, bc))
+            if len(bcs) == 1 and bcs[0].numel == shard_numel(box):
+                out.append((bs, bcs[0]))
         return out
 
 
@@ -121,8 +121,9 @@ def _region_views(binding: Binding, name: str, box: Shard, wire: torch.Tensor, b
     if bs is None:
         bs, _bc = binding.find(name, box)
     # wire side: the box packed contiguously; align its strides with the refinement
-    wire_bc = box_copy(bs.shard, box, bs.strides, contiguous_strides(shard_extents(box)))
-    assert wire_bc is not None
+    bcs = box_copies(bs.shard, box, bs.strides, contiguous_strides(shard_extents(box)))
+    assert len(bcs) == 1, (name, box)
+    wire_bc = bcs[0]
     local = strided(bs.tensor, wire_bc.src_offset, wire_bc.extents, wire_bc.src_strides)
     packed = strided(wire, wire_bc.dst_offset, wire_bc.extents, wire_bc.dst_strides)
     return local, packed

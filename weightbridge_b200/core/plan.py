@@ -31,7 +31,7 @@ import torch
 
 from ..utils.dtypes import FLOAT_CAST_DTYPES, dtype_code, dtype_to_str
 from .binding import Binding
-from .shard import Shard, WeightData, box_copy, coalesce, contiguous_strides, shard_extents, shard_numel
+from .shard import Shard, WeightData, box_copies, coalesce, contiguous_strides, shard_extents, shard_numel
 
 # -- device table layouts (csrc/wb_common.h declares the same structs) ----------------------
 ITEM_DTYPE = np.dtype([
@@ -184,20 +184,19 @@ def plan_pair(src: PhysBinding, dst: PhysBinding, names: Iterable[str] | None = 
         for sp in src.entries[name]:
             for di, dp in enumerate(dst.entries[name]):
                 try:
-                    bc = box_copy(sp.shard, dp.shard, sp.strides, dp.strides)
+                    bcs = box_copies(sp.shard, dp.shard, sp.strides, dp.strides)
                 except ValueError:
                     raise ValueError(f"shard compatibility check failed for {name}: "
                                      f"{sp.shard} vs {dp.shard}") from None
-                if bc is None:
-                    continue
-                src_at = _shift(sp, bc.src_offset * s_dtype.itemsize)
-                dst_at = _shift(dp, bc.dst_offset * d_dtype.itemsize)
-                if quant:
-                    ops += _quant_ops(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst, di)
-                    continue
-                e, ss, ds = coalesce(bc.extents, bc.src_strides, bc.dst_strides)
-                ops.append(Op("copy" if s_dtype == d_dtype else "cast", name, src_at, dst_at, e, ss, ds,
-                              s_dtype, d_dtype))
+                for bc in bcs:
+                    src_at = _shift(sp, bc.src_offset * s_dtype.itemsize)
+                    dst_at = _shift(dp, bc.dst_offset * d_dtype.itemsize)
+                    if quant:
+                        ops += _quant_ops(name, q, bc, src_at, dst_at, s_dtype, d_dtype, dst, di)
+                        continue
+                    e, ss, ds = coalesce(bc.extents, bc.src_strides, bc.dst_strides)
+                    ops.append(Op("copy" if s_dtype == d_dtype else "cast", name, src_at, dst_at, e, ss, ds,
+                                  s_dtype, d_dtype))
     return ops
 
 

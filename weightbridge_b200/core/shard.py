@@ -240,6 +240,79 @@ def box_copy(src_shard: Shard, dst_shard: Shard,
     return BoxCopy(src_off, dst_off, ext, ss, ds, region)
 
 
+def _logical_strides(shard: Shard) -> list[int]:
+    """Elements of the logical tensor between consecutive indices of each box dimension."""
+    out = [1] * len(shard)
+    for d in range(len(shard) - 2, -1, -1):
+        out[d] = out[d + 1] * int(shard[d + 1][2])
+    return out
+
+
+def _cut_sizes(shard: Shard, other: Shard) -> list[list[int]]:
+    """Per dimension of ``shard``: the block sizes (in units of that dimension, largest first)
+    of ``other``'s dimensions nested inside it, i.e. where ``other``'s factorisation puts
+    boundaries that a range of this dimension may have to be cut at."""
+    L, M = _logical_strides(shard), _logical_strides(other)
+    out = []
+    for (_l, _r, w), li in zip(shard, L):
+        out.append(sorted({m // li for m in M if m % li == 0 and li < m < li * int(w)}, reverse=True))
+    return out
+
+
+def _split_range(l: int, r: int, sizes: Sequence[int]) -> list[tuple[int, int]]:
+    """Cut ``[l, r)`` into pieces that are whole blocks of ``sizes[0]`` or lie inside one such
+    block, recursively for the smaller sizes."""
+    if not sizes:
+        return [(l, r)]
+    q, rest = sizes[0], sizes[1:]
+    a, b = -(-l // q) * q, (r // q) * q
+    if a >= b:
+        if l // q == (r - 1) // q:
+            return _split_range(l, r, rest)
+        return _split_range(l, a, rest) + _split_range(a, r, rest)
+    out = _split_range(l, a, rest) if l < a else []
+    out.append((a, b))
+    if b < r:
+        out += _split_range(b, r, rest)
+    return out
+
+
+def _pieces(shard: Shard, strides: Sequence[int], other: Shard):
+    """``(piece, element offset)`` of ``shard`` cut so that each piece aligns with ``other``."""
+    import itertools
+    per_dim = [_split_range(int(l), int(r), q) for (l, r, _w), q in zip(shard, _cut_sizes(shard, other))]
+    for combo in itertools.product(*per_dim):
+        off = sum((a - int(l)) * int(st) for (a, _b), (l, _r, _w), st in zip(combo, shard, strides))
+        yield [(a, b, int(w)) for (a, b), (_l, _r, w) in zip(combo, shard)], off
+
+
+def box_copies(src_shard: Shard, dst_shard: Shard,
+               src_strides: Sequence[int] | None = None,
+               dst_strides: Sequence[int] | None = None) -> list[BoxCopy]:
+    """The intersection of two boxes as strided copies: one when the two factorisations
+    align, else one per pair of aligned pieces.  A range that cuts through a block of the
+    other side's refinement (an FSDP row range ending inside an attention head, against a
+    per-head box) is cut at those block boundaries first; the pieces are rectangles in the
+    common refinement.  Raises ``ValueError`` when even the pieces cannot be aligned."""
+    try:
+        bc = box_copy(src_shard, dst_shard, src_strides, dst_strides)
+        return [] if bc is None else [bc]
+    except ValueError:
+        pass
+    ss = list(src_strides) if src_strides is not None else contiguous_strides(shard_extents(src_shard))
+    ds = list(dst_strides) if dst_strides is not None else contiguous_strides(shard_extents(dst_shard))
+    out = []
+    dst_pieces = list(_pieces(dst_shard, ds, src_shard))
+    for sp, soff in _pieces(src_shard, ss, dst_shard):
+        for dp, doff in dst_pieces:
+            bc = box_copy(sp, dp, ss, ds)
+            if bc is not None:
+                bc.src_offset += soff
+                bc.dst_offset += doff
+                out.append(bc)
+    return out
+
+
 def scale_box(region: Shard, block: Sequence[int], name: str = "") -> Shard:
     """Block-scale cells a 2-D region of a quantised tensor touches.  A cell of a block the
     region only partly covers is shared with the other senders of that block (they all
@@ -407,12 +480,11 @@ class WeightData:
             for ss in s_shards:
                 for rs in receiver.shards(name):
                     try:
-                        bc = box_copy(ss, rs)
+                        bcs = box_copies(ss, rs)
                     except ValueError:
                         raise ValueError(f"shard compatibility check failed for {name}: "
                                          f"{ss} vs {rs}") from None
-                    if bc is not None:
-                        boxes.append(bc.region)
+                    boxes += [bc.region for bc in bcs]
             if boxes:
                 entry: dict[str, Any] = {"shard": boxes, "dtype": s_dtype}
                 if r_dtype != s_dtype:

@@ -19,7 +19,7 @@ from typing import Iterable, Sequence
 
 import numpy as np
 
-from .shard import WeightData, box_copy
+from .shard import WeightData, box_copies
 
 Region = Sequence[tuple[int, int, int]]          # [(l, r, w), (l, r, w)]
 BlockKey = tuple                                 # (receiver, name, block row, block col)
@@ -113,12 +113,12 @@ def split_keys(sender: WeightData, receiver: WeightData, names: Iterable[str] | 
             continue
         for ss in s_shards:
             for rs in receiver.shards(name):
-                bc = box_copy(ss, rs)
-                if bc is None or len(bc.region) < 2:
-                    continue
-                for _outer, rows, cols in row_subregions(bc.region):
-                    for (bi, bj), _pr, _pc in block_split([rows, cols], q["block"])[1]:
-                        keys.add((name, bi, bj))
+                for bc in box_copies(ss, rs):
+                    if len(bc.region) < 2:
+                        continue
+                    for _outer, rows, cols in row_subregions(bc.region):
+                        for (bi, bj), _pr, _pc in block_split([rows, cols], q["block"])[1]:
+                            keys.add((name, bi, bj))
     return sorted(keys)
 
 
