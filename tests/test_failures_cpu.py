@@ -793,3 +793,37 @@ def test_two_models_share_one_rollout_app():
         server.should_exit = True
         for c in ctls:
             c.close()
+
+
+def test_metrics_route_counts_syncs_and_failures():
+    """GET /wbridge/metrics: Prometheus text with per-worker counters (syncs, failures,
+    bytes) and gauges (epoch, weights version, state) that follow the syncs."""
+    import requests
+    cfg = _cfg(mode="gpu_direct")
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender("gpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        for v in (5, 6):
+            th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+            th.start()
+            s.send(views, version=v)
+            th.join(20)
+        r = requests.get(f"{ro.url}/wbridge/metrics", timeout=5)
+        assert r.status_code == 200 and r.headers["content-type"].startswith("text/plain")
+        vals = {}
+        for line in r.text.splitlines():
+            if line and not line.startswith("#"):
+                key, val = line.rsplit(" ", 1)
+                vals[key] = float(val)
+        assert vals['wbridge_receiver_syncs_total{worker="0"}'] == 2
+        assert vals['wbridge_receiver_sync_failures_total{worker="0"}'] == 0
+        assert vals['wbridge_receiver_bytes_total{worker="0"}'] == 2 * ro.recv.expected_bytes > 0
+        assert vals['wbridge_receiver_epoch{worker="0"}'] == 2
+        assert vals['wbridge_receiver_weights_version{worker="0"}'] == 6
+        assert vals['wbridge_receiver_state{worker="0",state="connected"}'] == 1
+        assert "# TYPE wbridge_receiver_syncs_total counter" in r.text
+        s.disconnect()
+    finally:
+        ro.close()

@@ -1,7 +1,8 @@
 """Rollout-side HTTP control plane: FastAPI routes that fan out to the receiver workers.
 
 Routes (on the user's FastAPI app): ``GET /wbridge/metadata``, ``POST /wbridge/connect``,
-``POST /wbridge/receive`` and ``GET /wbridge/stats``.  The controller talks to the
+``POST /wbridge/receive``, ``GET /wbridge/stats`` (JSON) and ``GET /wbridge/metrics``
+(Prometheus text format).  The controller talks to the
 ``WeightReceiver`` workers over a ZMQ ROUTER bound at an ``ipc://`` path; each request
 carries an id and replies are matched by (worker, id), with a deadline on every gather.
 
@@ -71,6 +72,7 @@ class WeightReceiverController:
         router.add_api_route(f"{base}/connect", self.connect, methods=["POST"])
         router.add_api_route(f"{base}/receive", self.receive_weights, methods=["POST"])
         router.add_api_route(f"{base}/stats", self.get_stats, methods=["GET"])
+        router.add_api_route(f"{base}/metrics", self.get_metrics, methods=["GET"])
         app.include_router(router)
         self.router = router
 
@@ -157,6 +159,12 @@ class WeightReceiverController:
     def get_stats(self):
         return self._broadcast({"type": STATS_REQUEST})
 
+    def get_metrics(self):
+        """Every worker's counters and gauges in the Prometheus text exposition format."""
+        from fastapi.responses import PlainTextResponse
+        return PlainTextResponse(metrics_text(self.get_stats(), self.prefix),
+                                 media_type="text/plain; version=0.0.4")
+
     def serve(self, host: str = "127.0.0.1", port: int = 0, timeout_s: float = 30.0) -> str:
         """Serve the routes from a uvicorn server on a daemon thread (for rollout processes
         without a FastAPI app of their own); returns the URL the senders use."""
@@ -194,3 +202,32 @@ class WeightReceiverController:
             os.unlink(self._ipc_path)
         except OSError:
             pass
+
+
+_METRICS = (
+    ("wbridge_receiver_syncs_total", "counter", "Weight updates the worker completed.",
+     lambda w: w.get("totals", {}).get("syncs", 0)),
+    ("wbridge_receiver_sync_failures_total", "counter", "Weight updates that failed on the worker.",
+     lambda w: w.get("totals", {}).get("failures", 0)),
+    ("wbridge_receiver_bytes_total", "counter", "Bytes the worker received.",
+     lambda w: w.get("totals", {}).get("bytes", 0)),
+    ("wbridge_receiver_epoch", "gauge", "Sync epoch of the worker's current weights.",
+     lambda w: w.get("epoch", 0)),
+    ("wbridge_receiver_weights_version", "gauge", "Trainer version tag of the current weights (-1: none).",
+     lambda w: -1 if w.get("weights_version") is None else w["weights_version"]),
+    ("wbridge_receiver_last_update_seconds", "gauge", "Host time of the worker's last update.",
+     lambda w: (w.get("syncs") or [{}])[-1].get("host_ms", 0.0) / 1e3),
+)
+
+
+def metrics_text(stats: list[dict], prefix: str = "") -> str:
+    """Prometheus exposition text of the workers' ``/wbridge/stats`` replies."""
+    extra = f',prefix="{prefix}"' if prefix else ""
+    lines = []
+    for name, kind, help_, get in _METRICS:
+        lines += [f"# HELP {name} {help_}", f"# TYPE {name} {kind}"]
+        lines += [f'{name}{{worker="{w.get("rank")}"{extra}}} {get(w)}' for w in stats]
+    lines += ["# HELP wbridge_receiver_state Worker state (1 for the current one).",
+              "# TYPE wbridge_receiver_state gauge"]
+    lines += [f'wbridge_receiver_state{{worker="{w.get("rank")}",state="{w.get("state")}"{extra}}} 1' for w in stats]
+    return "\n".join(lines) + "\n"

@@ -76,6 +76,7 @@ class WeightReceiver:
         self._stop = threading.Event()
         self._started = threading.Event()
         self.stats: deque = deque(maxlen=64)
+        self.totals = {"syncs": 0, "failures": 0, "bytes": 0}     # since construction (metrics counters)
         self.epoch = 0
         self.weights_version: int | None = None       # the tag of the last weights received (send(version=))
         self.session: Session | None = None
@@ -280,7 +281,7 @@ class WeightReceiver:
         elif t == STATS_REQUEST:
             self._reply(sock, data, {"rank": self.rank, "state": self._state.value, "epoch": self.epoch,
                                      "weights_version": self.weights_version, "error": self._error,
-                                     "syncs": list(self.stats)})
+                                     "syncs": list(self.stats), "totals": dict(self.totals)})
         elif t == STOP_REQUEST:
             self._reply(sock, data, {"status": "ack"})
             self._stop.set()
@@ -367,11 +368,14 @@ class WeightReceiver:
             with nvtx_range("wbridge.receive"):
                 rec = self._receive()
             self.stats.append(rec)
+            self.totals["syncs"] += 1
+            self.totals["bytes"] += int(rec.get("bytes") or 0)
             self._state = ReceiverState.CONNECTED
             sock.send_string(json.dumps({"success": True, "epoch": self.epoch, "stats": rec}))
             self._collect_garbage()
         except Exception as e:
             logger.exception("receiver %d update failed", self.rank)
+            self.totals["failures"] += 1
             self._error = f"{type(e).__name__}: {e}"
             self._state = ReceiverState.FAILED
             if self._janitor is not None:        # off this thread: the store may be gone with its host
