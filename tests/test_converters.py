@@ -93,3 +93,19 @@ def test_deepseek_configs_and_converters():
     smeta = sglang_to_wb(SimpleNamespace(hf_config=SimpleNamespace(**hf)), sparams, tp_rank=0, tp_size=2)
     assert smeta == slay.to_wb(sparams)[0]
     assert len(smeta.shards("model.layers.2.self_attn.kv_b_proj.weight")) == 3
+
+
+def test_glm4_moe_config():
+    arch = get_arch("tiny-glm4-moe")
+    hf = {"model_type": "glm4_moe", "hidden_size": arch.hidden, "num_attention_heads": arch.num_heads,
+          "num_key_value_heads": arch.num_kv_heads, "head_dim": arch.head_dim, "num_hidden_layers": arch.num_layers,
+          "vocab_size": arch.vocab, "intermediate_size": arch.ffn, "moe_intermediate_size": arch.moe_ffn,
+          "n_routed_experts": arch.num_experts, "n_shared_experts": 1, "num_experts_per_tok": arch.top_k,
+          "first_k_dense_replace": 1, "attention_bias": True, "use_qk_norm": False}
+    assert ModelArch.from_hf_config(hf, name=arch.name) == arch
+    names = {n for n, _s in arch.hf_tensors()}
+    assert "model.layers.0.mlp.gate_proj.weight" in names and "model.layers.1.mlp.gate.e_score_correction_bias" in names
+    assert "model.layers.1.mlp.shared_experts.up_proj.weight" in names and "model.layers.1.self_attn.k_proj.bias" in names
+    import pytest
+    with pytest.raises(ValueError, match="use_qk_norm"):
+        ModelArch.from_hf_config(dict(hf, use_qk_norm=True))

@@ -69,3 +69,10 @@ def test_deepseek_mla_gpu_direct_protocol_on_host():
                 assert all(torch.equal(ro.params[n], exp[n]) for n in exp), seed
     finally:
         ro.close()
+
+
+def test_glm4_moe_tp2_ep2_to_tp2_fp8_experts_gloo():
+    """GLM-4.5 style (GQA with q/k/v bias, dense first layer, ungated shared experts, router
+    bias): Megatron TP 2 x EP 2 into an SGLang worker with fp8 experts."""
+    run("tiny-glm4-moe", "cpu_direct", [dict(tp=2, ep=2, tp_rank=i % 2, ep_rank=i // 2) for i in range(4)],
+        dict(tp=1, quant="fp8_experts"), dtype=torch.bfloat16, n_syncs=2)

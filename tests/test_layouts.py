@@ -80,11 +80,11 @@ def megatron_oracle(arch, lay: MegatronLayout, hf):
                 out[lay._expert_name(i, e, 1)] = torch.cat([gate, up])
                 out[lay._expert_name(i, e, 2)] = hf[x + f"{dn}.weight"].chunk(lay.etp, 1)[lay.etp_rank]
             if arch.shared_ffn:
-                y = m + ("mlp.shared_experts." if arch.is_mla else "mlp.shared_expert.")
+                y = m + ("mlp.shared_expert." if arch.family == "qwen2_moe" else "mlp.shared_experts.")
                 out[p + "mlp.shared_experts.linear_fc1.weight"] = torch.cat(
                     [hf[y + "gate_proj.weight"].chunk(tp)[r], hf[y + "up_proj.weight"].chunk(tp)[r]])
                 out[p + "mlp.shared_experts.linear_fc2.weight"] = hf[y + "down_proj.weight"].chunk(tp, 1)[r]
-                if not arch.is_mla:
+                if arch.family == "qwen2_moe":
                     out[p + "mlp.shared_experts.gate_weight"] = hf[m + "mlp.shared_expert_gate.weight"]
         else:
             out[p + "mlp.linear_fc1.layer_norm_weight"] = hf[m + "post_attention_layernorm.weight"]
@@ -109,6 +109,7 @@ MEGATRON_CASES = [
     ("tiny-qwen2-moe", dict(tp=2, ep=2)),
     ("tiny-deepseek-v3", dict(tp=2, ep=2)),
     ("tiny-deepseek-v2-lite", dict(tp=2, pp=2)),
+    ("tiny-glm4-moe", dict(tp=2, ep=2)),
 ]
 
 
@@ -212,11 +213,11 @@ def sglang_oracle(arch, lay: SGLangLayout, hf):
             out[m + f"{mb}.experts.w13_weight"] = torch.stack(w13)
             out[m + f"{mb}.experts.w2_weight"] = torch.stack(w2)
             if arch.shared_ffn:
-                y = m + ("mlp.shared_experts." if arch.is_mla else "mlp.shared_expert.")
+                y = m + ("mlp.shared_expert." if arch.family == "qwen2_moe" else "mlp.shared_experts.")
                 out[y + "gate_up_proj.weight"] = torch.cat([hf[y + "gate_proj.weight"].chunk(tp)[r],
                                                             hf[y + "up_proj.weight"].chunk(tp)[r]])
                 out[y + "down_proj.weight"] = hf[y + "down_proj.weight"].chunk(tp, 1)[r]
-                if not arch.is_mla:
+                if arch.family == "qwen2_moe":
                     out[m + "mlp.shared_expert_gate.weight"] = hf[m + "mlp.shared_expert_gate.weight"]
         else:
             out[m + "mlp.gate_up_proj.weight"] = torch.cat([hf[m + "mlp.gate_proj.weight"].chunk(tp)[r],
@@ -240,6 +241,7 @@ SGLANG_CASES = [
     ("tiny-deepseek-v3", dict(tp=2, moe_ep=2)),
     ("tiny-deepseek-v3", dict(tp=4, attn_tp=1, moe_ep=4)),   # DP-attention: MLA unsharded
     ("tiny-deepseek-v2-lite", dict(tp=2)),
+    ("tiny-glm4-moe", dict(tp=2, moe_ep=2)),
 ]
 
 
@@ -301,6 +303,8 @@ SYNC_CASES = [
      [dict(tp=4, tp_rank=i, attn_tp=1, attn_tp_rank=0, moe_ep=2) for i in range(4)]),
     ("tiny-deepseek-v2-lite", [dict(tp=1, pp=2, pp_rank=i) for i in range(2)],
      [dict(tp=4, tp_rank=i) for i in range(4)]),
+    ("tiny-glm4-moe", [dict(tp=2, ep=2, tp_rank=i % 2, ep_rank=i // 2) for i in range(4)],
+     [dict(tp=2, tp_rank=i, moe_ep=2) for i in range(2)]),
 ]
 
 

@@ -6,7 +6,8 @@ attention + routed experts + a gated shared expert), ``mixtral`` (Llama attentio
 ``block_sparse_moe`` experts named ``w1`` / ``w3`` / ``w2``) and ``deepseek_v3`` (multi-head
 latent attention: low-rank q and kv projections, per-head ``[nope | rope]`` queries and
 ``[k_nope | v]`` keys/values; dense MLPs in the first layers, then routed experts with
-ungated shared experts and a router score-correction bias).  The reference
+ungated shared experts and a router score-correction bias) and ``glm4_moe`` (GLM-4.5: GQA
+attention with q/k/v bias and the same MoE layout as ``deepseek_v3``).  The reference
 covers Qwen2/Qwen3 dense only (``wbridge/utils/megatron_utils/qwen2.py:13-80``,
 ``wbridge/utils/sglang_utils/qwen2.py:24-119``); Llama, the MoE families and MLA are new here.
 """
@@ -19,7 +20,7 @@ from typing import Any, Iterator
 @dataclass(frozen=True)
 class ModelArch:
     name: str
-    family: str                   # llama | qwen2 | qwen3 | qwen3_moe | qwen2_moe | mixtral | deepseek_v3
+    family: str                   # llama | qwen2 | qwen3 | qwen3_moe | qwen2_moe | mixtral | deepseek_v3 | glm4_moe
     num_layers: int
     hidden: int
     num_heads: int
@@ -43,7 +44,7 @@ class ModelArch:
 
     @property
     def qkv_bias(self) -> bool:
-        return self.family in ("qwen2", "qwen2_moe")
+        return self.family in ("qwen2", "qwen2_moe", "glm4_moe")
 
     @property
     def qk_norm(self) -> bool:
@@ -64,7 +65,12 @@ class ModelArch:
     @property
     def shared_prefix(self) -> str:
         """HF module of the shared experts: one gated expert (qwen2_moe) or ungated ones."""
-        return "mlp.shared_experts." if self.is_mla else "mlp.shared_expert."
+        return "mlp.shared_expert." if self.shared_gate else "mlp.shared_experts."
+
+    @property
+    def shared_gate(self) -> bool:
+        """Whether the shared expert's output is gated (``mlp.shared_expert_gate``)."""
+        return self.family == "qwen2_moe"
 
     @property
     def moe_block(self) -> str:
@@ -133,7 +139,7 @@ class ModelArch:
                 yield sp + "gate_proj.weight", (S, H)
                 yield sp + "up_proj.weight", (S, H)
                 yield sp + "down_proj.weight", (H, S)
-                if not self.is_mla:                  # qwen2_moe gates its shared expert
+                if self.shared_gate:
                     yield p + "mlp.shared_expert_gate.weight", (1, H)
         else:
             yield p + "mlp.gate_proj.weight", (self.ffn, H)
@@ -163,15 +169,28 @@ class ModelArch:
     @staticmethod
     def from_hf_config(cfg: Any, name: str | None = None) -> "ModelArch":
         """From a HuggingFace config object or dict (model_type llama / mistral / qwen2 / qwen3 /
-        qwen3_moe / qwen2_moe / mixtral / deepseek_v2 / deepseek_v3)."""
+        qwen3_moe / qwen2_moe / mixtral / deepseek_v2 / deepseek_v3 / glm4_moe)."""
         g = (lambda k, d=None: cfg.get(k, d)) if isinstance(cfg, dict) else (lambda k, d=None: getattr(cfg, k, d))
         mt = str(g("model_type", "llama")).lower()
         fam = {"llama": "llama", "mistral": "llama", "qwen2": "qwen2", "qwen3": "qwen3",
                "qwen3_moe": "qwen3_moe", "qwen2_moe": "qwen2_moe", "mixtral": "mixtral",
-               "deepseek_v2": "deepseek_v3", "deepseek_v3": "deepseek_v3"}.get(mt)
+               "deepseek_v2": "deepseek_v3", "deepseek_v3": "deepseek_v3", "glm4_moe": "glm4_moe"}.get(mt)
         if fam is None:
             raise ValueError(f"unsupported model_type {mt!r}")
         H, nh = int(g("hidden_size")), int(g("num_attention_heads"))
+        if fam == "glm4_moe":
+            if g("use_qk_norm", False):
+                raise ValueError("glm4_moe with use_qk_norm is not supported")
+            moe_ffn = int(g("moe_intermediate_size", 0) or 0)
+            return ModelArch(
+                name=name or mt, family=fam, num_layers=int(g("num_hidden_layers")), hidden=H,
+                num_heads=nh, num_kv_heads=int(g("num_key_value_heads", nh) or nh),
+                head_dim=int(g("head_dim", None) or H // nh), ffn=int(g("intermediate_size", 0) or 0),
+                vocab=int(g("vocab_size")), tie_embeddings=bool(g("tie_word_embeddings", False)),
+                num_experts=int(g("n_routed_experts", 0) or 0), moe_ffn=moe_ffn,
+                top_k=int(g("num_experts_per_tok", 0) or 0),
+                shared_ffn=int(g("n_shared_experts", 0) or 0) * moe_ffn,
+                first_dense_layers=int(g("first_k_dense_replace", 0) or 0), router_bias=True)
         if fam == "deepseek_v3":
             nope, rope = int(g("qk_nope_head_dim")), int(g("qk_rope_head_dim"))
             moe_ffn = int(g("moe_intermediate_size", 0) or 0)
@@ -225,6 +244,8 @@ class ModelArch:
                 router_bias=bool(getattr(args, "moe_router_enable_expert_bias", False)))
         kv = getattr(args, "num_query_groups", None) or nh
         hd = getattr(args, "kv_channels", None) or H // nh
+        freq = getattr(args, "moe_layer_freq", 1)
+        first = next((i for i, f in enumerate(freq) if f), len(freq)) if isinstance(freq, (list, tuple)) else 0
         return ModelArch(
             name=name or family, family=family, num_layers=int(args.num_layers), hidden=H,
             num_heads=nh, num_kv_heads=int(kv), head_dim=int(hd),
@@ -233,7 +254,8 @@ class ModelArch:
             num_experts=int(getattr(args, "num_experts", 0) or 0),
             moe_ffn=int(getattr(args, "moe_ffn_hidden_size", 0) or 0),
             top_k=int(getattr(args, "moe_router_topk", 0) or 0),
-            shared_ffn=int(getattr(args, "moe_shared_expert_intermediate_size", 0) or 0))
+            shared_ffn=int(getattr(args, "moe_shared_expert_intermediate_size", 0) or 0),
+            first_dense_layers=first, router_bias=bool(getattr(args, "moe_router_enable_expert_bias", False)))
 
 
 PRESETS: dict[str, ModelArch] = {
@@ -265,6 +287,11 @@ PRESETS: dict[str, ModelArch] = {
     "tiny-deepseek-v2-lite": ModelArch("tiny-deepseek-v2-lite", "deepseek_v3", 2, 256, 4, 4, 192, 256, 1000,
                                        num_experts=4, moe_ffn=128, top_k=2, shared_ffn=256, kv_lora_rank=128,
                                        qk_nope_dim=128, qk_rope_dim=64, v_head_dim=128, first_dense_layers=1),
+    # GLM-4.5 style: GQA with q/k/v bias, a dense first layer, routed + ungated shared experts
+    "tiny-glm4-moe": ModelArch("tiny-glm4-moe", "glm4_moe", 2, 256, 4, 2, 64, 512, 1000, num_experts=8,
+                               moe_ffn=128, top_k=2, shared_ffn=128, first_dense_layers=1, router_bias=True),
+    "glm-4.5-air": ModelArch("glm-4.5-air", "glm4_moe", 46, 4096, 96, 8, 128, 10944, 151552, num_experts=128,
+                             moe_ffn=1408, top_k=8, shared_ffn=1408, first_dense_layers=1, router_bias=True),
     "deepseek-v3": ModelArch("deepseek-v3", "deepseek_v3", 61, 7168, 128, 128, 192, 18432, 129280,
                              num_experts=256, moe_ffn=2048, top_k=8, shared_ffn=2048, q_lora_rank=1536,
                              kv_lora_rank=512, qk_nope_dim=128, qk_rope_dim=64, v_head_dim=128,

@@ -160,7 +160,7 @@ class MegatronLayout:
                     S_loc = a.shared_ffn // tp
                     out[p + "mlp.shared_experts.linear_fc1.weight"] = (2 * S_loc, H)
                     out[p + "mlp.shared_experts.linear_fc2.weight"] = (H, S_loc)
-                    if not a.is_mla:                   # qwen2_moe gates its shared expert
+                    if a.shared_gate:                  # qwen2_moe gates its shared expert
                         out[p + "mlp.shared_experts.gate_weight"] = (1, H)
             else:
                 F_loc = a.ffn // tp
@@ -372,7 +372,7 @@ def convert_to_wb(args: Any, model_name: str, named_tensors, *, tp_rank: int | N
         vpp_size = mpu.get_virtual_pipeline_model_parallel_world_size() or 1
         vpp_rank = (mpu.get_virtual_pipeline_model_parallel_rank() or 0) if vpp_size > 1 else 0
     name = model_name.lower()
-    family = ("deepseek_v3" if "deepseek" in name else
+    family = ("deepseek_v3" if "deepseek" in name else "glm4_moe" if "glm" in name else
               "mixtral" if "mixtral" in name else "qwen2_moe" if "qwen2" in name and "moe" in name else
               "qwen3_moe" if "moe" in name else "qwen3" if "qwen3" in name else
               "qwen2" if "qwen2" in name else "llama" if "llama" in name else None)

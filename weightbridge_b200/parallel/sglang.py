@@ -172,7 +172,7 @@ class SGLangLayout:
                     S_loc, sp = a.shared_ffn // self.tp, p + a.shared_prefix
                     out[sp + "gate_up_proj.weight"] = ((2 * S_loc, H), "linear")
                     out[sp + "down_proj.weight"] = ((H, S_loc), "linear")
-                    if not a.is_mla:
+                    if a.shared_gate:
                         out[p + "mlp.shared_expert_gate.weight"] = ((1, H), "other")
             else:
                 F_loc = a.ffn // self.tp
