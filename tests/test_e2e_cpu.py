@@ -76,3 +76,12 @@ def test_glm4_moe_tp2_ep2_to_tp2_fp8_experts_gloo():
     bias): Megatron TP 2 x EP 2 into an SGLang worker with fp8 experts."""
     run("tiny-glm4-moe", "cpu_direct", [dict(tp=2, ep=2, tp_rank=i % 2, ep_rank=i // 2) for i in range(4)],
         dict(tp=1, quant="fp8_experts"), dtype=torch.bfloat16, n_syncs=2)
+
+
+def test_deepseek_fused_shared_expert_slot_fp8_gloo():
+    """The shared expert kept as a fifth slot of each layer's fp8 FusedMoE tensors: the two
+    Megatron TP ranks each hold half of its rows, so its fp8 blocks are split between them
+    (amax exchanged) and land in the fused slot."""
+    slots = [[]] + [[0, 1, 2, 3, 4, 5, 6, 7, -1]] * 2
+    run("tiny-deepseek-v3", "cpu_direct", [dict(tp=2, tp_rank=i) for i in range(2)],
+        dict(tp=1, quant="fp8_experts", expert_slots=slots), dtype=torch.bfloat16, n_syncs=2)

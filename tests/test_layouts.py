@@ -431,3 +431,29 @@ def test_host_reshard_deepseek_fp8_experts():
         for n in params:
             assert torch.equal(params[n].view(torch.uint8) if params[n].dtype == torch.float8_e4m3fn else params[n],
                                expected[n].view(torch.uint8) if expected[n].dtype == torch.float8_e4m3fn else expected[n]), n
+
+
+def test_sglang_fused_shared_expert_slot_and_slot_count_guard():
+    """A worker that keeps DeepSeek's shared expert as one more slot of w13 / w2 (expert_slots
+    value -1) receives it there from the trainer's shared_experts; a FusedMoE tensor whose
+    slot count the layout does not expect is an error, not a slot left stale."""
+    arch = get_arch("tiny-deepseek-v3")
+    sl = lambda r: [[]] + [[4 * r + e for e in range(4)] + [-1]] * (arch.num_layers - 1)   # noqa: E731
+    meg = [MegatronLayout(arch, tp=2, ep=2, tp_rank=i % 2, ep_rank=i // 2) for i in range(4)]
+    sgl = [SGLangLayout(arch, tp=2, tp_rank=r, moe_ep=2, expert_slots=sl(r)) for r in range(2)]
+    assert "model.layers.1.mlp.shared_experts.gate_up_proj.weight" not in sgl[0].param_specs()
+    assert sgl[0].param_specs()["model.layers.1.mlp.experts.w13_weight"][0][0] == 5
+    for params, expected, done, meta in _host_sync(meg, sgl, torch.bfloat16):
+        assert done == set(meta.names())
+        assert "model.layers.1.mlp.shared_experts.down_proj.weight" in meta
+        for n in params:
+            a, b = params[n], expected[n]
+            if a.dtype == torch.float8_e4m3fn:
+                a, b = a.view(torch.uint8), b.view(torch.uint8)
+            assert torch.equal(a, b), n
+    plain = SGLangLayout(arch, tp=2, tp_rank=0, moe_ep=2)
+    fused = sgl[0].allocate(dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="expert slots"):
+        plain.to_wb({n: t for n, t in fused.items() if not n.endswith("_scale_inv")})
+    with pytest.raises(ValueError, match="shared expert"):
+        SGLangLayout(get_arch("tiny-qwen2-moe"), tp=1, expert_slots=[[0, 1, 2, 3, -1]] * 2)

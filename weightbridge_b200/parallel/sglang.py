@@ -53,7 +53,9 @@ class SGLangLayout:
     vocab_pad_multiple: int = 64
     # expert placement with redundant slots (SGLang EPLB): the logical expert held by each of
     # this rank's physical slots, one list for every layer or a list of lists per layer;
-    # None: the contiguous split of the experts over the moe_ep ranks
+    # -1 is the shared expert fused into the routed-expert tensors (its own shared_experts
+    # parameters then do not exist on this rank); None: the contiguous split of the experts
+    # over the moe_ep ranks
     expert_slots: tuple | list | None = None
 
     def __post_init__(self):
@@ -85,8 +87,11 @@ class SGLangLayout:
             if len(per_layer) != a.num_layers:
                 raise ValueError("expert_slots needs one slot list per layer (or one for all)")
             for slots in per_layer:
-                if any(not 0 <= int(e) < a.num_experts for e in slots):
-                    raise ValueError(f"expert_slots names an expert outside 0..{a.num_experts - 1}")
+                if any(not -1 <= int(e) < a.num_experts for e in slots):
+                    raise ValueError(f"expert_slots names an expert outside 0..{a.num_experts - 1} (or -1)")
+                if -1 in slots and (not a.shared_ffn or a.shared_ffn != a.moe_ffn or a.shared_gate):
+                    raise ValueError("a fused shared-expert slot (-1) needs one ungated shared expert of the "
+                                     "routed experts' width")
             self.expert_slots = tuple(tuple(int(e) for e in slots) for slots in per_layer)
 
     def local_experts(self, layer: int) -> list[int]:
@@ -168,7 +173,7 @@ class SGLangLayout:
                     out[p + f"{mb}.gate.e_score_correction_bias"] = ((a.num_experts,), "other")
                 out[p + f"{mb}.experts.w13_weight"] = ((E_loc, 2 * I_loc, H), "expert")
                 out[p + f"{mb}.experts.w2_weight"] = ((E_loc, H, I_loc), "expert")
-                if a.shared_ffn:                       # shared experts: a TP-split dense MLP (+ a gate)
+                if a.shared_ffn and -1 not in self.local_experts(i):   # a TP-split dense MLP (+ a gate)
                     S_loc, sp = a.shared_ffn // self.tp, p + a.shared_prefix
                     out[sp + "gate_up_proj.weight"] = ((2 * S_loc, H), "linear")
                     out[sp + "down_proj.weight"] = ((H, S_loc), "linear")
@@ -360,9 +365,15 @@ class SGLangLayout:
             i_loc = I // self.moe_tp
             ibox = (self.moe_tp_rank * i_loc, (self.moe_tp_rank + 1) * i_loc, I)
             out = []
-            for e, eg in enumerate(self.local_experts(int(m.group(1)))):
+            slots = self.local_experts(int(m.group(1)))
+            if param.shape[0] != len(slots):
+                raise ValueError(f"{name} holds {param.shape[0]} expert slots, the layout expects {len(slots)}: "
+                                 "describe redundant or fused shared-expert slots with expert_slots=")
+            for e, eg in enumerate(slots):
                 q = f"{p}{a.moe_block}.experts.{eg}."
                 gn, un, dn = a.expert_projs
+                if eg == -1:                     # the fused shared expert
+                    q, (gn, un, dn) = p + a.shared_prefix, ("gate_proj", "up_proj", "down_proj")
                 if rest.endswith("w13_weight"):
                     if scale is not None and i_loc % bn:
                         raise ValueError("w13 gate/up split not aligned with the fp8 block")
