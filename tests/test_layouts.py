@@ -457,3 +457,9 @@ def test_sglang_fused_shared_expert_slot_and_slot_count_guard():
         plain.to_wb({n: t for n, t in fused.items() if not n.endswith("_scale_inv")})
     with pytest.raises(ValueError, match="shared expert"):
         SGLangLayout(get_arch("tiny-qwen2-moe"), tp=1, expert_slots=[[0, 1, 2, 3, -1]] * 2)
+
+
+def test_megatron_expert_index_beyond_local_count_is_an_error():
+    lay = MegatronLayout(get_arch("tiny-qwen3-moe"), ep=2, ep_rank=1)
+    with pytest.raises(ValueError, match="local expert 4 of 4"):
+        lay.split_param("decoder.layers.0.mlp.experts.linear_fc2.weight4", torch.zeros(256, 256))

@@ -289,6 +289,8 @@ class MegatronLayout:
             else:
                 fc, e = int(em.group(1)), int(em.group(2))
             E_loc = a.num_experts // self.ep
+            if e >= E_loc:
+                raise ValueError(f"{name}: local expert {e} of {E_loc} (num_experts {a.num_experts} / EP {self.ep})")
             eg = self.ep_rank * E_loc + e
             I = a.moe_ffn
             i_loc = I // self.etp
