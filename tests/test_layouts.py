@@ -463,3 +463,22 @@ def test_megatron_expert_index_beyond_local_count_is_an_error():
     lay = MegatronLayout(get_arch("tiny-qwen3-moe"), ep=2, ep_rank=1)
     with pytest.raises(ValueError, match="local expert 4 of 4"):
         lay.split_param("decoder.layers.0.mlp.experts.linear_fc2.weight4", torch.zeros(256, 256))
+
+
+def test_overlap_carries_elements_shared_by_overlapping_shards_once():
+    """Receiver shards that overlap (MLA's w_kc / w_vc inside kv_b_proj, a redundant expert
+    slot) do not multiply the overlap: it holds each element once, the receiver writes it into
+    every shard, and coverage still counts every destination shard as filled."""
+    from weightbridge_b200.core.shard import covered_numel, shard_numel
+    arch = get_arch("tiny-deepseek-v3")
+    smeta, _ = MegatronLayout(arch, tp=1).to_wb(MegatronLayout(arch, tp=1).allocate(fill=False))
+    rl = SGLangLayout(arch, tp=1, expert_slots=[[]] + [[0, 1, 2, 3, 4, 5, 6, 7, 3]] * 2)
+    rmeta, _ = rl.to_wb(rl.allocate(dtype=torch.bfloat16))
+    ov = WeightData.compute_overlap(smeta, rmeta)
+    kvb = "model.layers.0.self_attn.kv_b_proj.weight"
+    assert len(rmeta.shards(kvb)) == 3 and ov.shards(kvb) == [[(0, 256, 256), (0, 128, 128)]]
+    e3 = "model.layers.1.mlp.experts.3.up_proj.weight"
+    assert len(rmeta.shards(e3)) == 2 and len(ov.shards(e3)) == 1
+    for n in (kvb, e3):
+        full = sum(shard_numel(s) for s in rmeta.shards(n))
+        assert sum(covered_numel(reg, rmeta.shards(n)) for reg in ov.shards(n)) == full

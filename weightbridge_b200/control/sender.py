@@ -44,7 +44,7 @@ from ..core.binding import bind
 from ..core.plan import (PhysBinding, PlanBoundsError, Tables, lower_ops, multicast_ok, phys_binding, plan_digest,
                          plan_pair, storage_ranges, validate_tables)
 from ..core.plancache import PlanCache, plan_key, relative_binding
-from ..core.shard import WeightData
+from ..core.shard import WeightData, covered_numel, shard_numel
 from ..utils.config import WIRE_MODES, TransferConfig, normalize_mode
 from .assign import assign_sources, restrict
 from ..utils.trace import nvtx_range
@@ -340,8 +340,12 @@ class WeightSender:
             for r, names in rs.items():
                 ov = WeightData.compute_overlap(restrict(smeta_objs[s], names), rmeta_objs[r])
                 sess.set(f"digest/{s}/{r}", plan_digest(ov))
-                for a, b, n, _sh, _dt in ov.iter_with_intv():
-                    covered[(r, n)] = covered.get((r, n), 0) + (b - a)
+                rm = rmeta_objs[r]
+                for n, regions, _dt in ov:
+                    if (rm.quant(n) or {}).get("role") == "scale":
+                        continue
+                    k = sum(covered_numel(reg, rm.shards(n)) for reg in regions)
+                    covered[(r, n)] = covered.get((r, n), 0) + k
         self.uncovered = _uncovered(rmeta_objs, covered)
         if self.uncovered:
             msg = ", ".join(f"worker {r}: {len(v)} entries (e.g. {v[0]})" for r, v in sorted(self.uncovered.items()))
@@ -995,13 +999,14 @@ class WeightSender:
 
 
 def _uncovered(rmetas: dict[int, WeightData], covered: dict[tuple[int, str], int]) -> dict[int, list[str]]:
-    """Per worker, the entries (scales aside) that the senders' overlaps do not fill."""
+    """Per worker, the entries (scales aside) whose shards the senders' overlaps do not fill
+    (``covered``: elements written, counted per destination shard)."""
     out: dict[int, list[str]] = {}
     for r, meta in rmetas.items():
-        for a, b, n, _sh, _dt in meta.iter_with_intv():
+        for n, shards, _dt in meta:
             if (meta.quant(n) or {}).get("role") == "scale":
                 continue
-            if covered.get((r, n), 0) < b - a:
+            if covered.get((r, n), 0) < sum(shard_numel(sh) for sh in shards):
                 out.setdefault(r, []).append(n)
     return out
 

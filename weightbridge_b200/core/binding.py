@@ -162,7 +162,9 @@ def pack_into(binding: Binding, overlap: WeightData, out: torch.Tensor) -> None:
 
 
 def unpack_from(binding: Binding, overlap: WeightData, chunk: torch.Tensor) -> None:
-    """Scatter a packed ``chunk`` (``overlap`` layout) into the bound tensors."""
+    """Scatter a packed ``chunk`` (``overlap`` layout) into the bound tensors: each region
+    into every bound shard it intersects (an entry's shards may overlap, e.g. redundant
+    expert slots, and the overlap then carries their shared elements once)."""
     chunk = chunk.reshape(-1).view(torch.uint8)
     if chunk.device != binding.device:
         chunk = chunk.to(binding.device)
@@ -171,10 +173,13 @@ def unpack_from(binding: Binding, overlap: WeightData, chunk: torch.Tensor) -> N
         for box in shards:
             n = shard_numel(box)
             seg = chunk[off:off + n * dtype.itemsize].view(dtype)
-            found = binding.find_all(name, box)
-            if not found:
-                raise ValueError(f"no local shard of {name} contains {box}")
-            for bs, _bc in found:            # every destination holding the region
-                local, packed = _region_views(binding, name, box, seg, bs)
-                local.copy_(packed)
+            wire = contiguous_strides(shard_extents(box))
+            wrote = 0
+            for bs in binding.entries[name]:
+                for bc in box_copies(box, bs.shard, wire, bs.strides):
+                    strided(bs.tensor, bc.dst_offset, bc.extents, bc.dst_strides).copy_(
+                        strided(seg, bc.src_offset, bc.extents, bc.src_strides))
+                    wrote += bc.numel
+            if wrote < n:
+                raise ValueError(f"the local shards of {name} do not hold all of {box}")
             off += n * dtype.itemsize

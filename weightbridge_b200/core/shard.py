@@ -313,6 +313,38 @@ def box_copies(src_shard: Shard, dst_shard: Shard,
     return out
 
 
+def _drop_contained(boxes: list[Shard]) -> list[Shard]:
+    """The regions not contained in another one (of identical ones, the first).  A receiver
+    entry whose shards overlap (redundant expert slots, MLA's ``w_kc`` / ``w_vc`` inside
+    ``kv_b_proj``) would otherwise carry the shared elements once per shard; the receiver
+    writes a region into every shard it intersects, so one copy is enough."""
+    keep = []
+    for i, a in enumerate(boxes):
+        na = shard_numel(a)
+        inside = False
+        for j, b in enumerate(boxes):
+            if i == j:
+                continue
+            nb = shard_numel(b)
+            if nb < na or (nb == na and j > i):
+                continue
+            try:
+                k = sum(bc.numel for bc in box_copies(a, b))
+            except ValueError:
+                continue
+            if k == na:
+                inside = True
+                break
+        if not inside:
+            keep.append(a)
+    return keep
+
+
+def covered_numel(region: Shard, shards: Sequence[Shard]) -> int:
+    """Elements of ``shards`` (counted once per shard) that ``region`` fills."""
+    return sum(bc.numel for rs in shards for bc in box_copies(region, rs))
+
+
 def scale_box(region: Shard, block: Sequence[int], name: str = "") -> Shard:
     """Block-scale cells a 2-D region of a quantised tensor touches.  A cell of a block the
     region only partly covers is shared with the other senders of that block (they all
@@ -485,6 +517,8 @@ class WeightData:
                         raise ValueError(f"shard compatibility check failed for {name}: "
                                          f"{ss} vs {rs}") from None
                     boxes += [bc.region for bc in bcs]
+            if len(receiver.shards(name)) > 1:
+                boxes = _drop_contained(boxes)
             if boxes:
                 entry: dict[str, Any] = {"shard": boxes, "dtype": s_dtype}
                 if r_dtype != s_dtype:
