@@ -16,6 +16,9 @@ Configurations (strong scaling: the model, hence the bytes moved per sync, is fi
                      expert fp8 block is split over two senders, which exchange its amax (N=8)
   llama70b-colocated Llama-3-70B, trainer TP8 on GPUs 0-7 -> two rollout replicas at TP4 in
                      separate processes on GPUs 0-3 and 4-7 (N=8, 16 processes)
+  deepseek-lite-fp8  DeepSeek-V2-Lite (MLA + 64 routed and 2 shared experts), trainer TP2 x EP2 ->
+                     rollout TP4 (EP4 experts, fp8 e4m3 blocks), MLA's w_kc / w_vc written with
+                     kv_b_proj (N=8; N=4: TP2 -> TP2)
 
 Two timed phases, both after W warm-up syncs through the public API:
   value: K back-to-back transfer launches per sender (WeightSender.launch) bracketed by CUDA
@@ -48,7 +51,7 @@ def parse(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--config", default="llama8b",
                    choices=["llama8b", "llama8b-fanout", "qwen3-moe-fp8", "qwen3-moe-fp8-etp",
-                            "llama70b-colocated"])
+                            "llama70b-colocated", "deepseek-lite-fp8"])
     p.add_argument("--impl", default="wbridge", choices=["wbridge", "reference", "torch-p2p"],
                    help="torch-p2p: the reference's algorithm (per-box torch copies + NCCL isend/irecv)")
     p.add_argument("--mode", type=int, default=None, help="kernel mode: 0 vector, 1/2/3 TMA bulk")
@@ -151,6 +154,14 @@ def scenario(config: str, n: int) -> tuple[str, list[Role], str]:
         roles = [Role("trainer", i, dict(tp=8, tp_rank=i)) for i in range(8)]
         roles += [Role("rollout", i, dict(tp=4, tp_rank=i % 4), i // 4, i % 4, i % 4 == 0) for i in range(8)]
         return "llama3-70b", roles, "tp8 -> 2 replicas x tp4, colocated (16 processes)"
+    if config == "deepseek-lite-fp8":
+        if n not in (4, 8):
+            raise SystemExit("deepseek-lite-fp8 runs on 4 or 8 GPUs")
+        t = n // 2
+        roles = [Role("trainer", i, dict(tp=2, ep=t // 2, tp_rank=i % 2, ep_rank=i // 2)) for i in range(t)]
+        roles += [Role("rollout", t + i, dict(tp=t, tp_rank=i, moe_ep=t, quant="fp8_experts"), 0, i, i == 0)
+                  for i in range(t)]
+        return "deepseek-v2-lite", roles, f"tp2xep{t // 2}->tp{t} (MLA, ep{t} fp8 experts)"
     raise SystemExit(f"unknown config {config}")
 
 

@@ -15,12 +15,14 @@ import bench  # noqa: E402
 
 from weightbridge_b200 import WeightData  # noqa: E402
 from weightbridge_b200.control.assign import assign_sources, restrict  # noqa: E402
+from weightbridge_b200.core.shard import covered_numel, shard_numel  # noqa: E402
 from weightbridge_b200.models.arch import get_arch  # noqa: E402
 from weightbridge_b200.parallel.megatron import MegatronLayout  # noqa: E402
 from weightbridge_b200.parallel.sglang import SGLangLayout  # noqa: E402
 
 CASES = [("llama8b", 1), ("llama8b", 2), ("llama8b", 4), ("llama8b", 8), ("llama8b-fanout", 8),
-         ("qwen3-moe-fp8", 8), ("qwen3-moe-fp8-etp", 8), ("llama70b-colocated", 8)]
+         ("qwen3-moe-fp8", 8), ("qwen3-moe-fp8-etp", 8), ("llama70b-colocated", 8), ("deepseek-lite-fp8", 4),
+         ("deepseek-lite-fp8", 8)]
 
 
 def _meta(lay):
@@ -38,15 +40,15 @@ def test_bench_scenario_is_consistent(config, n):
     rmetas = {i: _meta(SGLangLayout(arch, **r.layout)) for i, r in enumerate(roles) if r.kind == "rollout"}
     plan = assign_sources(smetas, rmetas)
     for r, meta in rmetas.items():
-        # every element of every (non-scale) entry arrives from exactly one sender
+        # every element of every (non-scale) entry's shards arrives from exactly one sender
         weights = [n for n in meta.names() if (meta.quant(n) or {}).get("role") != "scale"]
         got = 0
         for s, targets in plan.items():
             names = targets.get(r, [])
             if names:
                 ov = WeightData.compute_overlap(restrict(smetas[s], names), meta)
-                got += sum(b - a for a, b, n, _sh, _dt in ov.iter_with_intv() if n in names)
-        want = sum(b - a for a, b, n, _sh, _dt in meta.iter_with_intv() if n in weights)
+                got += sum(covered_numel(reg, meta.shards(n)) for n, regs, _dt in ov if n in names for reg in regs)
+        want = sum(shard_numel(sh) for n in weights for sh in meta.shards(n))
         assert got == want, (config, n, r, got, want)
 
 
