@@ -545,7 +545,8 @@ def test_partial_sync_of_named_entries():
         assert all(torch.equal(ro.params[n], exp2[n]) for n in exp2)
         assert len(compiles) == 2                               # full + layer 0, each once
         with pytest.raises(ValueError):
-            WeightSender("cpu_direct", [ro.url], config=_cfg(mode="cpu_direct")).send(views, names=layer0)
+            WeightSender("gpu_direct", [ro.url], config=_cfg(mode="gpu_direct", direction="pull")).send(
+                views, names=layer0)
     finally:
         ro.close()
 
@@ -824,6 +825,45 @@ def test_metrics_route_counts_syncs_and_failures():
         assert vals['wbridge_receiver_weights_version{worker="0"}'] == 6
         assert vals['wbridge_receiver_state{worker="0",state="connected"}'] == 1
         assert "# TYPE wbridge_receiver_syncs_total counter" in r.text
+        s.disconnect()
+    finally:
+        ro.close()
+
+
+@pytest.mark.parametrize("chunk", [0, 48 << 10])
+def test_partial_syncs_over_the_wire(chunk):
+    """names= in a wire mode: the sender tags the epoch with the subset's digest, both sides cut
+    the subset's chunks alike (on the full set's buffers), and only those entries change."""
+    cfg = _cfg(mode="cpu_direct", wire_chunk_bytes=chunk)
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender("cpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        layer1 = [n for n in views if n.startswith("model.layers.1.")]
+
+        def sync(seed, names=None, version=None):
+            lay.fill(params, seed=seed)
+            th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
+            th.start()
+            s.send(views, names=names, version=version)
+            th.join(20)
+
+        sync(0)
+        sync(5, names=layer1, version=7)
+        in_l1 = lambda n: 5 if n.startswith("model.layers.1.") else 0      # noqa: E731
+        exp0, exp5 = (ro.lay.allocate(dtype=torch.float32, fill=True, seed=sd) for sd in (0, 5))
+        for n in ro.params:
+            assert torch.equal(ro.params[n], (exp5 if in_l1(n) == 5 else exp0)[n]), n
+        assert ro.recv.weights_version == 7
+        sync(6, names=layer1)                      # cached subset: no new wire set
+        sync(8)
+        exp8 = ro.lay.allocate(dtype=torch.float32, fill=True, seed=8)
+        assert all(torch.equal(ro.params[n], exp8[n]) for n in ro.params)
+        assert set(s._wire_sets) == {None, frozenset(layer1)} and len(ro.recv._wire_sets) == 2
+        full, part = s._wire_sets[None], s._wire_sets[frozenset(layer1)]
+        for p, (bufs, _items) in part.peers.items():
+            assert [b.data_ptr() for b in bufs] == [b.data_ptr() for b in full.peers[p][0][:len(bufs)]]
         s.disconnect()
     finally:
         ro.close()

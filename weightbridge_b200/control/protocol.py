@@ -22,7 +22,7 @@ STOP_REQUEST = "stop_request"
 
 # Version of the sender <-> receiver session protocol (session keys, arm channel, split-block
 # amax exchange).  A receiver refuses a connect from a sender speaking another version.
-PROTOCOL_VERSION = 2
+PROTOCOL_VERSION = 3
 
 
 class ReceiverState(str, Enum):

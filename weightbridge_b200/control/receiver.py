@@ -484,8 +484,27 @@ class WeightReceiver:
             raise ReceiveError(f"mode {self.mode} does not take tensors on {self.device}")
         self._wires = WireSet.for_receiver(self._rphys, self.overlaps, self.device, self.config,
                                            storage_ranges(self.state_dict.values()), self._wire_chunk)
+        self._wire_sets = {"": self._wires}        # by the digest of a partial sync's entry subset
         if self.device.type == "cuda":
             self._stream = torch.cuda.Stream(self.device)
+
+    def _wire_set(self, digest: str):
+        """The wire set of the entry subset ``digest`` names (``""``: every entry), cut like
+        the senders' from the same overlaps and on the full set's buffers."""
+        ws = self._wire_sets.get(digest)
+        if ws is None:
+            from ..core.plan import storage_ranges
+            from ..core.wire import restrict_overlap
+            from .wires import WireSet
+            names = self.session.get_json(f"subset/{digest}", self.config.sync_timeout_s)
+            overlaps = {s: restrict_overlap(ov, names) for s, ov in self.overlaps.items()}
+            ws = WireSet.for_receiver(self._rphys, overlaps, self.device, self.config,
+                                      storage_ranges(self.state_dict.values()), self._wire_chunk,
+                                      self._wire_sets[""].buffers())
+            if len(self._wire_sets) >= 8:
+                self._wire_sets.pop(next(k for k in self._wire_sets if k))
+            self._wire_sets[digest] = ws
+        return ws
 
     def _late_bind(self) -> None:
         """First update of a receiver that joined without tensors: bind, export, publish."""
@@ -519,18 +538,20 @@ class WeightReceiver:
             # parameters: only an idle device may be written by the senders
             torch.cuda.synchronize(self.device)
         if self.mode in WIRE_MODES:
+            try:     # sender rank 0 writes the tag and the entry subset before it arms the workers
+                tag, _sep, digest = sess.wait_checked([f"ver/{epoch}"], self.config.sync_timeout_s)[0] \
+                    .decode().partition("|")
+                ws = self._wire_set(digest)
+            except (SessionTimeout, PeerError) as e:
+                raise ReceiveError(str(e)) from None
+            version = int(tag)
             sess.set(f"ready/{gr}/{epoch}", "1")
-            ws = self._wires
             if ws.device.type == "cuda":     # NCCL receives and unpack launches, ordered on one stream
                 with torch.cuda.stream(self._stream):
                     ws.recv(self._pg, epoch, self._stream)
                 self._stream.synchronize()
             else:
                 ws.recv(self._pg, epoch)
-            try:
-                version = int(sess.wait_checked([f"ver/{epoch}"], self.config.sync_timeout_s)[0])
-            except (SessionTimeout, PeerError) as e:
-                raise ReceiveError(str(e)) from None
         else:
             sess.set(f"ready/{gr}/{epoch}", str(self._bind_gen))     # senders rebind on a new generation
             keys = [f"done/{s}/{gr}/{epoch}" for s in self.expected]

@@ -171,6 +171,8 @@ class WeightSender:
         self._stream = self._ev = None               # transfer stream and its timing events (device tensors)
         self._pool = None                            # send_async's single worker thread
         self._snap = self._snap_key = self._snap_future = None   # send_async(snapshot=True) buffers
+        self._wire_sets: dict = {}                   # wire modes: compiled wire sets by entry subset
+        self._subsets_published: set[str] = set()   # wire modes, rank 0: subset digests in the session
 
     # -- collectives on the trainer group (no-ops for a single sender) -------------------
     def _all_gather(self, obj):
@@ -249,6 +251,8 @@ class WeightSender:
         self._program = None
         self._program_key = None
         self._progs = {}
+        self._wire_sets = {}
+        self._subsets_published = set()              # a new session holds none of them
         self.connected = True
         logger.info("sender %d connected: %d receiver targets, mode=%s", self.rank, len(self.targets), cfg.mode)
 
@@ -660,10 +664,38 @@ class WeightSender:
             info.update({"allocs": [], "binding": phys_binding(binding).to_json()})
         self.session.set_json(f"sendbind/{self.rank}", info)
 
-    def _compile_wire(self, state_dict) -> None:
-        """Wire modes: every target's overlap cut into chunks with two buffers per target
-        (``control/wires.py``), packed by the C++ executor for host tensors and by one
-        transfer-kernel launch per chunk for device tensors."""
+    def _publish_subset(self, subset: frozenset | None) -> str:
+        """Wire modes, rank 0: the digest the receivers look a partial sync's entries up by
+        (``""``: every entry); each subset's names are written to the session once."""
+        if subset is None:
+            return ""
+        names = sorted(subset)
+        dg = _digest(names)[:16]
+        if dg not in self._subsets_published:
+            self.session.set_json(f"subset/{dg}", names)
+            self._subsets_published.add(dg)
+        return dg
+
+    def _select_wire(self, state_dict, subset: frozenset | None) -> None:
+        """Make the wire set of ``subset`` current (compiled on first use, on the full set's
+        buffers); the last few subsets stay compiled."""
+        ws = self._wire_sets.get(subset)
+        if ws is None:
+            if subset is not None and None not in self._wire_sets:
+                self._select_wire(state_dict, None)           # its buffers serve every subset
+            self._compile_wire(state_dict, subset)
+            ws = self._wires
+            if len(self._wire_sets) >= 8:
+                self._wire_sets.pop(next(k for k in self._wire_sets if k is not None))
+            self._wire_sets[subset] = ws
+        self._wires = ws
+        self._piece_pos = self._positions(ws.all_tables)
+
+    def _compile_wire(self, state_dict, subset: frozenset | None = None) -> None:
+        """Wire modes: every target's overlap (restricted to ``subset``) cut into chunks with
+        two buffers per target (``control/wires.py``), packed by the C++ executor for host
+        tensors and by one transfer-kernel launch per chunk for device tensors."""
+        from ..core.wire import restrict_overlap
         from .wires import WireSet
         cfg = self.config
         binding = bind(self.metadata, state_dict)
@@ -674,11 +706,18 @@ class WeightSender:
             raise TransferError("nccl mode sends device tensors; use cpu_direct for host tensors")
         if dev.type == "cuda":
             torch.cuda.set_device(dev)
-        self._wires = WireSet.for_sender(phys_binding(binding), self.overlaps, self.targets, dev, cfg,
-                                         storage_ranges(state_dict.values()))
+        overlaps, targets = self.overlaps, self.targets
+        shared = None
+        if subset is not None:
+            overlaps = {r: restrict_overlap(ov, subset) for r, ov in overlaps.items()}
+            targets = {r: [n for n in names if n in subset] for r, names in targets.items()}
+            full = self._wire_sets.get(None)
+            shared = full.buffers() if full is not None else None
+        self._wires = WireSet.for_sender(phys_binding(binding), overlaps, targets, dev, cfg,
+                                         storage_ranges(state_dict.values()), shared)
         self._piece_pos = self._positions(self._wires.all_tables)
         self._program = None
-        if dev.type == "cuda":
+        if dev.type == "cuda" and self._stream is None:
             self._stream = torch.cuda.Stream(dev)
             self._ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
 
@@ -876,9 +915,9 @@ class WeightSender:
 
     def _subset(self, names) -> frozenset | None:
         subset = None if names is None else frozenset(names)
-        if subset is not None and (self.config.mode in WIRE_MODES or self.config.direction == "pull"):
-            raise ValueError("names= needs the push direction of gpu_direct or nvls: the wire modes and "
-                             "pulling receivers move every entry they expect")
+        if subset is not None and self.config.mode == "gpu_direct" and self.config.direction == "pull":
+            raise ValueError("names= is not supported in the pull direction: pulling receivers load every "
+                             "entry they expect")
         return subset
 
     def _send(self, state_dict: dict[str, Any], version: int = -1, subset: frozenset | None = None,
@@ -891,8 +930,9 @@ class WeightSender:
         t0 = time.perf_counter()
         epoch = self.epoch + 1
         sess = self.session
-        if self.rank == 0 and cfg.mode in WIRE_MODES:     # no done keys there: the tag has its own
-            sess.set(f"ver/{epoch}", str(version))
+        if self.rank == 0 and cfg.mode in WIRE_MODES:     # no done keys there: the tag has its own,
+            dg = self._publish_subset(subset)              # with the entry subset the receivers cut by
+            sess.set(f"ver/{epoch}", f"{version}|{dg}")
             if epoch > 16:
                 sess.delete(f"ver/{epoch - 16}")
         arm = self._arm(epoch) if self.rank == 0 else None
@@ -913,10 +953,11 @@ class WeightSender:
             raise TransferError(self._arm_error)
         try:
             if cfg.mode in WIRE_MODES:
-                key = (self._key(state_dict), None)
+                key = self._key(state_dict)
                 if self._program_key != key:
-                    self._compile_wire(state_dict)
+                    self._wire_sets.clear()
                     self._program_key = key
+                self._select_wire(state_dict, subset)
             else:
                 if self._resolve_bindings(dict(zip(self.targets, ready))):
                     self._progs.clear()

@@ -18,7 +18,7 @@ import torch
 
 from ..core.plan import Tables, lower_ops, plan_pair, storage_ranges, validate_tables, wire_binding
 from ..core.shard import WeightData
-from ..core.wire import wire_chunks
+from ..core.wire import buffer_bytes, wire_chunks
 
 _ABS = lambda _alloc: 0     # noqa: E731  (wire and local bindings hold absolute addresses)
 
@@ -39,19 +39,32 @@ class WireSet:
         self._amax = np.zeros(0, dtype=np.float32)
 
     # -- construction --------------------------------------------------------------------
-    def _buffers(self, chunks: list[WeightData]) -> list[torch.Tensor]:
-        size = max(1, max(c.total_nbytes() for c in chunks))
-        return [torch.empty(size, dtype=torch.uint8, device=self.device) for _ in range(min(2, len(chunks)))]
+    def _buffers(self, peer: int, overlap: WeightData, chunks: list[WeightData], chunk_bytes: int,
+                 shared: dict[int, list[torch.Tensor]] | None) -> list[torch.Tensor]:
+        """Two buffers (one for a single chunk) that hold any chunk of ``overlap`` or of a
+        subset of it, so the wire sets of partial syncs reuse the full set's (``shared``)."""
+        n = min(2, len(chunks))
+        need = max(c.total_nbytes() for c in chunks)
+        have = (shared or {}).get(peer)
+        if have is not None and len(have) >= n and all(b.numel() >= need for b in have[:n]):
+            return have[:n]
+        size = max(need, buffer_bytes(overlap, chunk_bytes))
+        return [torch.empty(size, dtype=torch.uint8, device=self.device) for _ in range(n)]
+
+    def buffers(self) -> dict[int, list[torch.Tensor]]:
+        return {p: bufs for p, (bufs, _items) in self.peers.items()}
 
     @staticmethod
     def for_sender(sphys, overlaps: dict[int, WeightData], targets: dict[int, list[str]], device, cfg,
-                   src_ranges) -> "WireSet":
+                   src_ranges, shared: dict[int, list[torch.Tensor]] | None = None) -> "WireSet":
+        """``shared``: per peer, buffers of another wire set of the same peers (the full sync's,
+        when this one is a partial sync) to reuse where they are large enough."""
         ws = WireSet(device)
         for r, names in sorted(targets.items()):
             chunks = wire_chunks(overlaps[r], cfg.wire_chunk_bytes)
             if not chunks:
                 continue
-            bufs = ws._buffers(chunks)
+            bufs = ws._buffers(r, overlaps[r], chunks, cfg.wire_chunk_bytes, shared)
             items = []
             for k, ov in enumerate(chunks):
                 b = k % len(bufs)
@@ -65,14 +78,15 @@ class WireSet:
         return ws
 
     @staticmethod
-    def for_receiver(rphys, overlaps: dict[int, WeightData], device, cfg, dst_ranges, chunk_bytes: int) -> "WireSet":
+    def for_receiver(rphys, overlaps: dict[int, WeightData], device, cfg, dst_ranges, chunk_bytes: int,
+                     shared: dict[int, list[torch.Tensor]] | None = None) -> "WireSet":
         """``chunk_bytes`` is the senders' (the session carries it), so both sides cut alike."""
         ws = WireSet(device)
         for s, ov_all in sorted(overlaps.items()):
             chunks = wire_chunks(ov_all, chunk_bytes)
             if not chunks:
                 continue
-            bufs = ws._buffers(chunks)
+            bufs = ws._buffers(s, ov_all, chunks, chunk_bytes, shared)
             items = []
             for k, ov in enumerate(chunks):
                 b = k % len(bufs)

@@ -48,3 +48,33 @@ def wire_chunks(overlap: WeightData, chunk_bytes: int) -> list[WeightData]:
 def _entry_bytes(overlap: WeightData):
     for start, end, name, _shards, _dtype in overlap.iter_with_intv():
         yield name, end - start
+
+
+def restrict_overlap(overlap: WeightData, names) -> WeightData:
+    """``overlap`` limited to the entries ``names`` (a partial sync), with the scale entries of
+    the quantised ones."""
+    keep = set(names)
+    js = overlap.to_jsonable()
+    out = {}
+    for n, e in js.items():
+        q = e.get("quant") or {}
+        if n in keep or (q.get("role") == "scale" and q.get("of") in keep):
+            out[n] = e
+    return WeightData(out)
+
+
+def buffer_bytes(overlap: WeightData, chunk_bytes: int) -> int:
+    """Size of a wire buffer that holds any chunk of ``overlap`` or of any subset of its
+    entries: a chunk is at most ``chunk_bytes`` or one unit (an entry with its scales), and
+    never more than the whole overlap."""
+    total = overlap.total_nbytes()
+    if chunk_bytes <= 0:
+        return max(1, total)
+    sizes = {n: b for n, b in _entry_bytes(overlap)}
+    unit = 0
+    for name in overlap.names():
+        q = overlap.quant(name) or {}
+        if q.get("role") == "scale":
+            continue
+        unit = max(unit, sizes[name] + (sizes.get(q["scale"], 0) if q.get("scale") else 0))
+    return max(1, min(total, max(chunk_bytes, unit)))
