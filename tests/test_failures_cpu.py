@@ -509,10 +509,12 @@ def test_orderly_disconnect_is_not_a_loss():
         ro.close()
 
 
-def test_partial_sync_of_named_entries():
+@pytest.mark.parametrize("direction", ["push", "pull"])
+def test_partial_sync_of_named_entries(direction):
     """send(names=...) moves only those entries (here: layer 0); the rest keeps the previous
-    weights.  Alternating partial and full syncs reuses both compiled programs."""
-    cfg = _cfg(mode="gpu_direct")
+    weights.  Alternating partial and full syncs reuses both compiled programs (pull: the
+    worker's programs, selected by the subset digest in the senders' done values)."""
+    cfg = _cfg(mode="gpu_direct", direction=direction)
     ro = Rollout(cfg)
     try:
         lay, params, meta, views = _sender(cfg)
@@ -544,9 +546,8 @@ def test_partial_sync_of_named_entries():
         exp2 = ro.lay.allocate(dtype=torch.float32, fill=True, seed=2)
         assert all(torch.equal(ro.params[n], exp2[n]) for n in exp2)
         assert len(compiles) == 2                               # full + layer 0, each once
-        with pytest.raises(ValueError):
-            WeightSender("gpu_direct", [ro.url], config=_cfg(mode="gpu_direct", direction="pull")).send(
-                views, names=layer0)
+        if direction == "pull":
+            assert len(ro.recv._pull_progs) == 2
     finally:
         ro.close()
 

@@ -92,6 +92,9 @@ class WeightReceiver:
         self._bound = False                           # tensors bound and exported for this session
         self._pull_versions, self._pull_prog, self._pull_imports = None, None, {}   # pull direction
         self._pull_stream = None
+        self._pull_progs: dict = {}                   # pull programs by entry-subset digest
+        self._pull_src: dict = {}
+        self._pull_ranges: list = []
         self._mc = None                               # nvls: (multicast object, replica group)
         self._fd_server = None                        # nvls: serves the pool's file descriptor
         fd, path = tempfile.mkstemp(prefix=f"wbridge_sched_{rank}_")
@@ -560,14 +563,15 @@ class WeightReceiver:
                                          what=f"senders {self.expected} to finish epoch {epoch}")
             except (SessionTimeout, PeerError) as e:
                 raise ReceiveError(str(e)) from None
-            done = [v.decode().split(":") for v in vals]          # status:binding-version:pushed:tag
+            done = [v.decode().split(":") for v in vals]          # status:binding-version:pushed:tag:subset
             bad = {s: int(d[0]) for s, d in zip(self.expected, done) if int(d[0])}
             if bad:
                 raise ReceiveError(f"senders reported kernel status {bad} for epoch {epoch}")
             pushed = [s for s, d in zip(self.expected, done) if len(d) < 3 or d[2] == "1"]
             version = max((int(d[3]) for d in done if len(d) > 3), default=-1)
             if self.direction == "pull":
-                self._pull(epoch, {s: int(d[1]) for s, d in zip(self.expected, done)})
+                self._pull(epoch, {s: int(d[1]) for s, d in zip(self.expected, done)},
+                           done[0][4] if done and len(done[0]) > 4 else "")
             if self.config.verify_flags and pushed:
                 flags = self.flags.cpu()
                 stale = [s for s in pushed if int(flags[s]) != epoch]
@@ -583,13 +587,12 @@ class WeightReceiver:
                 "bytes": self.expected_bytes, "senders": self.expected}
 
     # -- pull direction --------------------------------------------------------------------
-    def _pull(self, epoch: int, versions: dict[int, int]) -> None:
+    def _pull(self, epoch: int, versions: dict[int, int], digest: str = "") -> None:
         """Load this worker's copies from the senders' memory (they keep it unchanged until
-        every receiver has reported ``pulled``)."""
+        every receiver has reported ``pulled``); ``digest`` names a partial sync's entries."""
         status = 0
         try:
-            if versions != self._pull_versions:
-                self._compile_pull(versions)
+            self._select_pull(versions, digest)
             prog = self._pull_prog
             if prog is not None and len(prog.tables):
                 if prog.device.type == "cpu":
@@ -608,14 +611,29 @@ class WeightReceiver:
         if status:
             raise ReceiveError(f"pull kernel reported status {status:#x} at epoch {epoch}")
 
-    def _compile_pull(self, versions: dict[int, int]) -> None:
-        from ..core.plan import PhysBinding, Tables, storage_ranges, validate_tables
-        from ..ops.executor import HostProgram, LaunchConfig, TransferProgram
+    def _select_pull(self, versions: dict[int, int], digest: str) -> None:
+        """Make the pull program of (the senders' memory versions, entry subset) current: the
+        senders' memory is opened again when a version changes, a subset's program is compiled
+        on first use."""
+        if versions != self._pull_versions:
+            self._open_senders(versions)
+        prog = self._pull_progs.get(digest)
+        if prog is None:
+            names = set(self.session.get_json(f"subset/{digest}", self.config.sync_timeout_s)) if digest else None
+            prog = self._compile_pull(names)
+            if len(self._pull_progs) >= 8:
+                self._pull_progs.pop(next(k for k in self._pull_progs if k))
+            self._pull_progs[digest] = prog
+        self._pull_prog = prog
+
+    def _open_senders(self, versions: dict[int, int]) -> None:
+        from ..core.plan import PhysBinding
         from ..parallel.ipc import ImportTable
         from .sender import _phys_extents
         for imp in self._pull_imports.values():
             imp.close()
-        self._pull_imports, parts, src_ranges = {}, [], []
+        self._pull_imports, self._pull_src, self._pull_ranges = {}, {}, []
+        self._pull_progs = {}
         for s in self.expected:
             sb = self.session.get_json(f"sendbind/{s}", self.config.sync_timeout_s)
             if sb["host"] != socket.gethostname():
@@ -626,22 +644,31 @@ class WeightReceiver:
             imp = ImportTable(sb["allocs"], same_process=same)
             self._pull_imports[s] = imp
             sphys = PhysBinding.from_json(sb["binding"])
-            ops = [o for o in plan_pair(sphys, self._rphys_abs, names=self._names[s])
-                   if o.kind not in ("quant", "squant")]
-            parts.append(lower_ops(ops, imp.base, lambda a: 0, item_bytes=self.config.item_bytes))
+            self._pull_src[s] = sphys
             if sb["allocs"]:
-                src_ranges += [(imp.base(i), imp.base(i) + int(a["size"])) for i, a in enumerate(sb["allocs"])]
+                self._pull_ranges += [(imp.base(i), imp.base(i) + int(a["size"])) for i, a in enumerate(sb["allocs"])]
             else:
-                src_ranges += _phys_extents(sphys)
+                self._pull_ranges += _phys_extents(sphys)
+        self._pull_versions = dict(versions)
+        if self.device.type != "cpu" and self._pull_stream is None:
+            self._pull_stream = torch.cuda.Stream(self.device)
+
+    def _compile_pull(self, names: set | None):
+        """The pull program of every expected sender's entries (restricted to ``names``)."""
+        from ..core.plan import Tables, storage_ranges, validate_tables
+        from ..ops.executor import HostProgram, LaunchConfig, TransferProgram
+        parts = []
+        for s in self.expected:
+            mine = self._names[s] if names is None else [n for n in self._names[s] if n in names]
+            ops = [o for o in plan_pair(self._pull_src[s], self._rphys_abs, names=mine)
+                   if o.kind not in ("quant", "squant")]
+            parts.append(lower_ops(ops, self._pull_imports[s].base, lambda a: 0, item_bytes=self.config.item_bytes))
         tables = Tables.concat(parts)
         if self.config.validate_plan:
-            validate_tables(tables, src_ranges, storage_ranges(self.state_dict.values()))
+            validate_tables(tables, self._pull_ranges, storage_ranges(self.state_dict.values()))
         if self.device.type == "cpu":
-            self._pull_prog = HostProgram(tables)
-        else:
-            self._pull_prog = TransferProgram(tables, self.device, [], LaunchConfig(mode=self.config.kernel_mode))
-            self._pull_stream = torch.cuda.Stream(self.device)
-        self._pull_versions = dict(versions)
+            return HostProgram(tables)
+        return TransferProgram(tables, self.device, [], LaunchConfig(mode=self.config.kernel_mode))
 
     def launch(self, stream: torch.cuda.Stream | None = None) -> None:
         """Pull direction: enqueue this worker's pull kernel on ``stream`` with no handshake

@@ -158,6 +158,7 @@ class WeightSender:
         self._ops_cache: dict[tuple, list] = {}     # plan ops per (receiver, bindings, names)
         self._plan_cache = PlanCache(self.config.plan_cache_dir) if self.config.plan_cache_dir else None
         self._bind_version = 0                       # bumped whenever the bound tensors change
+        self._published_key = None                   # pull: the tensors whose memory was last exported
         self.uncovered: dict[int, list[str]] = {}    # rank 0, after connect: worker -> entries no sender fills
         self._xchg = None                            # split fp8 blocks shared with other senders
         self._piece_pos = np.zeros(0, dtype=np.int64)
@@ -251,6 +252,7 @@ class WeightSender:
         self._program = None
         self._program_key = None
         self._progs = {}
+        self._published_key = None                   # the new session has no exported memory yet
         self._wire_sets = {}
         self._subsets_published = set()              # a new session holds none of them
         self.connected = True
@@ -577,9 +579,12 @@ class WeightSender:
         sjson = sphys.to_json()
         skey = _digest(sjson)
         pull = cfg.mode == "gpu_direct" and cfg.direction == "pull"
-        self._bind_version += 1
-        if pull:
+        if not pull:
+            self._bind_version += 1
+        elif self._published_key != self._key(state_dict):   # new tensors: export them again
+            self._bind_version += 1
             self._publish_sender_memory(binding, device)
+            self._published_key = self._key(state_dict)
         parts, flags, dst_ranges = [], [], []
         covered: set[int] = set()
         for m, g in self._mc.values():
@@ -729,7 +734,8 @@ class WeightSender:
         if key == self._program_key:
             return
         if self.config.direction == "pull":     # the receivers pull from the last published memory:
-            self._progs.clear()                 # a switch of tensors must publish again (compile)
+            # programs of other tensors are dropped (a switch of tensors publishes again)
+            self._progs = {k: v for k, v in self._progs.items() if k[0] == key[0]}
         hit = self._progs.pop(key, None)
         if hit is None:
             self._compile(state_dict, subset)
@@ -914,11 +920,7 @@ class WeightSender:
             stream.wait_stream(after if after is not None else torch.cuda.current_stream(device))
 
     def _subset(self, names) -> frozenset | None:
-        subset = None if names is None else frozenset(names)
-        if subset is not None and self.config.mode == "gpu_direct" and self.config.direction == "pull":
-            raise ValueError("names= is not supported in the pull direction: pulling receivers load every "
-                             "entry they expect")
-        return subset
+        return None if names is None else frozenset(names)
 
     def _send(self, state_dict: dict[str, Any], version: int = -1, subset: frozenset | None = None,
               after: Any = None) -> SyncStats:
@@ -1016,7 +1018,8 @@ class WeightSender:
                 # pull: the parameters must be final
             if prog is not None:
                 st.bytes_read, st.bytes_written = prog.bytes_read, prog.bytes_written
-            done = f"{st.status}:{self._bind_version}:{int(pushed)}:{version}"
+            dg = self._publish_subset(subset) if self.rank == 0 else (_digest(sorted(subset))[:16] if subset else "")
+            done = f"{st.status}:{self._bind_version}:{int(pushed)}:{version}:{dg}"
             sess.multi_set([f"done/{self.rank}/{r}/{epoch}" for r in self.targets], [done] * len(self.targets))
             if st.status:
                 prog.clear_status()
