@@ -924,21 +924,39 @@ class WeightSender:
 
     def _send(self, state_dict: dict[str, Any], version: int = -1, subset: frozenset | None = None,
               after: Any = None) -> SyncStats:
-        """``after``: the event or stream whose work the transfer must follow (default: this
+        """One sync: handshake, program selection, split-block exchange, transfer, completion.
+        ``after``: the event or stream whose work the transfer must follow (default: this
         thread's current stream on the transfer's device)."""
         if not self.connected or self.metadata is None:
             raise RuntimeError("WeightSender.send requires connect() first")
-        cfg = self.config
         t0 = time.perf_counter()
         epoch = self.epoch + 1
-        sess = self.session
+        st = SyncStats(epoch=epoch, receivers=sorted(self.targets), link_gbs=self.config.link_gbs)
+        ready = self._handshake(epoch, version, subset, st)
+        self._prepare(state_dict, subset, ready, epoch)
+        if len(self._piece_pos):          # split fp8 blocks: amax of every piece, then the exchange
+            self._exchange_split_amax(epoch, st, after)
+        if self.config.mode in WIRE_MODES:
+            self._transfer_wire(epoch, st, after)
+        elif self.targets:
+            self._transfer_direct(epoch, st, after, version, subset)
+        self.epoch = epoch
+        st.host_ms = (time.perf_counter() - t0) * 1e3
+        self.history.append(st)
+        if len(self.history) > 256:
+            del self.history[:128]
+        return st
+
+    def _handshake(self, epoch: int, version: int, subset: frozenset | None, st: SyncStats) -> list:
+        """Rank 0 tags the epoch (wire modes) and arms the workers; every rank waits until its
+        targets are ready.  Returns the targets' ready values (their binding generations)."""
+        cfg, sess = self.config, self.session
         if self.rank == 0 and cfg.mode in WIRE_MODES:     # no done keys there: the tag has its own,
             dg = self._publish_subset(subset)              # with the entry subset the receivers cut by
             sess.set(f"ver/{epoch}", f"{version}|{dg}")
             if epoch > 16:
                 sess.delete(f"ver/{epoch - 16}")
         arm = self._arm(epoch) if self.rank == 0 else None
-        st = SyncStats(epoch=epoch, receivers=sorted(self.targets), link_gbs=cfg.link_gbs)
         t1 = time.perf_counter()
         try:
             with nvtx_range("wbridge.send/ready"):
@@ -953,8 +971,13 @@ class WeightSender:
         if self.rank == 0 and self._arm_error is not None:
             self._fail_epoch(epoch, self._arm_error)
             raise TransferError(self._arm_error)
+        return ready
+
+    def _prepare(self, state_dict, subset: frozenset | None, ready: list, epoch: int) -> None:
+        """Make the program (or wire set) of these tensors and this subset current, opening
+        the memory of workers that bound new tensors first."""
         try:
-            if cfg.mode in WIRE_MODES:
+            if self.config.mode in WIRE_MODES:
                 key = self._key(state_dict)
                 if self._program_key != key:
                     self._wire_sets.clear()
@@ -968,79 +991,82 @@ class WeightSender:
         except Exception as e:
             self._fail_epoch(epoch, f"{type(e).__name__}: {e}")
             raise
-        if len(self._piece_pos):          # split fp8 blocks: amax of every piece, then the exchange
-            try:
-                tx = time.perf_counter()
-                src = self._wires if cfg.mode in WIRE_MODES else self._program
-                stream = None
-                if src.device.type == "cuda":     # the amax pass reads what the caller's work wrote
-                    stream = self._stream
-                    self._wait_after(stream, after, src.device)
-                src.set_piece_amax(self._split_amax(epoch, src.piece_amax(stream)))
-                st.exchange_ms = (time.perf_counter() - tx) * 1e3
-            except (SessionTimeout, PeerError, ValueError) as e:
-                self._fail_epoch(epoch, str(e))
-                raise TransferError(str(e)) from None
-        if cfg.mode in WIRE_MODES:
-            ws = self._wires
-            if ws.device.type == "cuda":          # pack launches and NCCL sends, ordered on one stream
-                e0, e1 = self._ev
-                with torch.cuda.stream(self._stream):
-                    self._wait_after(self._stream, after, ws.device)
-                    e0.record(self._stream)
-                    ws.send(self._pg, epoch, self._stream)
-                    e1.record(self._stream)
-                e1.synchronize()
-                st.device_ms = e0.elapsed_time(e1)
-            else:
-                ws.send(self._pg, epoch)
-            st.bytes_read = ws.bytes_read
-            st.bytes_written = ws.bytes_on_wire
-        elif self.targets:
-            prog = self._program
-            pushed = prog is not None and len(prog.tables) > 0
-            if pushed and prog.device.type == "cpu":
-                t2 = time.perf_counter()
-                prog.launch(epoch)
-                st.device_ms = (time.perf_counter() - t2) * 1e3
-            elif pushed:
-                self._wait_after(self._stream, after, prog.device)
-                e0, e1 = self._ev
-                with nvtx_range("wbridge.send/transfer"):
-                    e0.record(self._stream)
-                    prog.launch(epoch, self._stream)
-                    e1.record(self._stream)
-                    e1.synchronize()
-                st.device_ms = e0.elapsed_time(e1)
-                st.status = prog.read_status()
-            elif torch.cuda.is_available():
-                (after if after is not None else torch.cuda.current_stream()).synchronize()   # the receivers
-                # pull: the parameters must be final
-            if prog is not None:
-                st.bytes_read, st.bytes_written = prog.bytes_read, prog.bytes_written
-            dg = self._publish_subset(subset) if self.rank == 0 else (_digest(sorted(subset))[:16] if subset else "")
-            done = f"{st.status}:{self._bind_version}:{int(pushed)}:{version}:{dg}"
-            sess.multi_set([f"done/{self.rank}/{r}/{epoch}" for r in self.targets], [done] * len(self.targets))
-            if st.status:
-                prog.clear_status()
-                raise TransferError(f"transfer kernel reported status {st.status:#x} at epoch {epoch}")
-            if cfg.mode == "gpu_direct" and cfg.direction == "pull":
-                # parameters stay untouched until every target has pulled its share
-                try:
-                    vals = sess.wait_checked([f"pulled/{r}/{epoch}" for r in self.targets], cfg.sync_timeout_s,
-                                             f"receivers {sorted(self.targets)} to pull epoch {epoch}")
-                except (SessionTimeout, PeerError) as e:
-                    raise TransferError(str(e)) from None
-                bad = {r: int(v) for r, v in zip(sorted(self.targets), vals) if int(v)}
-                if bad:
-                    raise TransferError(f"receivers reported pull status {bad} at epoch {epoch}")
-        self.epoch = epoch
-        st.host_ms = (time.perf_counter() - t0) * 1e3
-        self.history.append(st)
-        if len(self.history) > 256:
-            del self.history[:128]
-        return st
 
+    def _exchange_split_amax(self, epoch: int, st: SyncStats, after: Any) -> None:
+        """Split fp8 blocks: the amax of every piece, exchanged with the blocks' co-owners."""
+        try:
+            tx = time.perf_counter()
+            src = self._wires if self.config.mode in WIRE_MODES else self._program
+            stream = None
+            if src.device.type == "cuda":     # the amax pass reads what the caller's work wrote
+                stream = self._stream
+                self._wait_after(stream, after, src.device)
+            src.set_piece_amax(self._split_amax(epoch, src.piece_amax(stream)))
+            st.exchange_ms = (time.perf_counter() - tx) * 1e3
+        except (SessionTimeout, PeerError, ValueError) as e:
+            self._fail_epoch(epoch, str(e))
+            raise TransferError(str(e)) from None
+
+    def _transfer_wire(self, epoch: int, st: SyncStats, after: Any) -> None:
+        """Wire modes: pack and send every chunk (device tensors: pack launches and NCCL sends
+        ordered on the transfer stream)."""
+        ws = self._wires
+        if ws.device.type == "cuda":
+            e0, e1 = self._ev
+            with torch.cuda.stream(self._stream):
+                self._wait_after(self._stream, after, ws.device)
+                e0.record(self._stream)
+                ws.send(self._pg, epoch, self._stream)
+                e1.record(self._stream)
+            e1.synchronize()
+            st.device_ms = e0.elapsed_time(e1)
+        else:
+            ws.send(self._pg, epoch)
+        st.bytes_read = ws.bytes_read
+        st.bytes_written = ws.bytes_on_wire
+
+    def _transfer_direct(self, epoch: int, st: SyncStats, after: Any, version: int,
+                         subset: frozenset | None) -> None:
+        """gpu_direct / nvls: launch the push program, publish completion (with the tag and
+        the subset), and in the pull direction wait until every target has pulled."""
+        cfg, sess = self.config, self.session
+        prog = self._program
+        pushed = prog is not None and len(prog.tables) > 0
+        if pushed and prog.device.type == "cpu":
+            t2 = time.perf_counter()
+            prog.launch(epoch)
+            st.device_ms = (time.perf_counter() - t2) * 1e3
+        elif pushed:
+            self._wait_after(self._stream, after, prog.device)
+            e0, e1 = self._ev
+            with nvtx_range("wbridge.send/transfer"):
+                e0.record(self._stream)
+                prog.launch(epoch, self._stream)
+                e1.record(self._stream)
+                e1.synchronize()
+            st.device_ms = e0.elapsed_time(e1)
+            st.status = prog.read_status()
+        elif torch.cuda.is_available():
+            (after if after is not None else torch.cuda.current_stream()).synchronize()   # the receivers
+            # pull: the parameters must be final
+        if prog is not None:
+            st.bytes_read, st.bytes_written = prog.bytes_read, prog.bytes_written
+        dg = self._publish_subset(subset) if self.rank == 0 else (_digest(sorted(subset))[:16] if subset else "")
+        done = f"{st.status}:{self._bind_version}:{int(pushed)}:{version}:{dg}"
+        sess.multi_set([f"done/{self.rank}/{r}/{epoch}" for r in self.targets], [done] * len(self.targets))
+        if st.status:
+            prog.clear_status()
+            raise TransferError(f"transfer kernel reported status {st.status:#x} at epoch {epoch}")
+        if cfg.mode == "gpu_direct" and cfg.direction == "pull":
+            # parameters stay untouched until every target has pulled its share
+            try:
+                vals = sess.wait_checked([f"pulled/{r}/{epoch}" for r in self.targets], cfg.sync_timeout_s,
+                                         f"receivers {sorted(self.targets)} to pull epoch {epoch}")
+            except (SessionTimeout, PeerError) as e:
+                raise TransferError(str(e)) from None
+            bad = {r: int(v) for r, v in zip(sorted(self.targets), vals) if int(v)}
+            if bad:
+                raise TransferError(f"receivers reported pull status {bad} at epoch {epoch}")
 
 def _uncovered(rmetas: dict[int, WeightData], covered: dict[tuple[int, str], int]) -> dict[int, list[str]]:
     """Per worker, the entries (scales aside) whose shards the senders' overlaps do not fill
