@@ -2,3 +2,5 @@
 from .controller import WeightReceiverController
 from .receiver import WeightReceiver
 from .sender import SyncStats, WeightSender
+
+__all__ = ["WeightReceiverController", "WeightReceiver", "SyncStats", "WeightSender"]

@@ -1,2 +1,4 @@
 """Model architecture descriptors and deterministic synthetic weights."""
 from .arch import PRESETS, ModelArch, get_arch
+
+__all__ = ["PRESETS", "ModelArch", "get_arch"]
