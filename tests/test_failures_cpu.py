@@ -868,3 +868,29 @@ def test_partial_syncs_over_the_wire(chunk):
         s.disconnect()
     finally:
         ro.close()
+
+
+def test_wait_for_version_takes_updates_until_the_tag():
+    """A scheduler that needs weights of at least step 3 takes the pending updates (versions
+    1..3) and returns; waiting for a version no sender produces ends at its deadline."""
+    from weightbridge_b200.control.receiver import ReceiveError
+    cfg = _cfg(mode="gpu_direct")
+    ro = Rollout(cfg)
+    try:
+        lay, params, meta, views = _sender(cfg)
+        s = WeightSender("gpu_direct", [ro.url], config=cfg)
+        s.connect(meta)
+        got = []
+        th = threading.Thread(target=lambda: got.append(ro.recv.wait_for_version(3, timeout=30, poll_s=0.5)))
+        th.start()
+        for v in (1, 2, 3):
+            s.send(views, version=v)
+        th.join(30)
+        assert got == [3] and ro.recv.weights_version == 3
+        t0 = time.time()
+        with pytest.raises(ReceiveError, match="waiting for 4"):
+            ro.recv.wait_for_version(4, timeout=1.0, poll_s=0.3)
+        assert time.time() - t0 < 5
+        s.disconnect()
+    finally:
+        ro.close()

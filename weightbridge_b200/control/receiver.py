@@ -179,6 +179,20 @@ class WeightReceiver:
             raise ReceiveError(reply["error"])
         return bool(reply["success"])
 
+    def wait_for_version(self, version: int, timeout: float, poll_s: float = 1.0) -> int:
+        """Take pending updates until the weights carry at least trainer version ``version``
+        (``send(version=...)``); returns the version reached.  For a scheduler that must not
+        generate with weights older than a given step.  Raises ``ReceiveError`` when the
+        deadline passes first (or an update fails)."""
+        deadline = time.monotonic() + timeout
+        while self.weights_version is None or self.weights_version < version:
+            left = deadline - time.monotonic()
+            if left <= 0:
+                raise ReceiveError(f"weights still at version {self.weights_version} after {timeout:.1f}s "
+                                   f"(waiting for {version})")
+            self.request_update(timeout=min(poll_s, left))
+        return self.weights_version
+
     def _same_tensors(self, state_dict) -> bool:
         for name in self.metadata.names():
             a, b = self.state_dict.get(name), state_dict.get(name)
