@@ -887,6 +887,9 @@ def test_wait_for_version_takes_updates_until_the_tag():
             s.send(views, version=v)
         th.join(30)
         assert got == [3] and ro.recv.weights_version == 3
+        sm = s.summary()
+        assert sm["syncs"] == 3 and sm["host_ms"]["p50"] > 0 and sm["bytes_written"] > 0
+        assert set(sm) >= {"device_ms", "wait_ready_ms", "gbs"}
         t0 = time.time()
         with pytest.raises(ReceiveError, match="waiting for 4"):
             ro.recv.wait_for_version(4, timeout=1.0, poll_s=0.3)

@@ -919,6 +919,19 @@ class WeightSender:
         else:
             stream.wait_stream(after if after is not None else torch.cuda.current_stream(device))
 
+    def summary(self, last: int = 100) -> dict:
+        """Median and 90th percentile of the last ``last`` syncs' host time, device time, wait
+        for the workers and GB/s (``SyncStats``), for periodic logging."""
+        hist = self.history[-last:]
+        out: dict = {"syncs": len(hist)}
+        if not hist:
+            return out
+        for f in ("host_ms", "device_ms", "wait_ready_ms", "exchange_ms", "gbs"):
+            v = np.sort(np.array([getattr(h, f) for h in hist], dtype=np.float64))
+            out[f] = {"p50": round(float(np.percentile(v, 50)), 3), "p90": round(float(np.percentile(v, 90)), 3)}
+        out["bytes_written"] = hist[-1].bytes_written
+        return out
+
     def _subset(self, names) -> frozenset | None:
         return None if names is None else frozenset(names)
 
