@@ -337,3 +337,41 @@ def test_box_copies_cut_ranges_against_dense_oracle(seed):
         strided(count, bc.dst_offset, bc.extents, bc.dst_strides).add_(1)
     assert torch.equal(dst, expect)
     assert (count <= 1).all() and int(count.sum()) == int(in_range.sum())
+
+
+@pytest.mark.parametrize("seed", range(120))
+def test_box_copies_random_factorisations_against_dense_oracle(seed):
+    """Two partial boxes of one tensor, each re-factorised at random: wherever box_copies
+    returns pieces they write exactly the intersection, once per element; it succeeds at least
+    whenever the single-rectangle box_copy does."""
+    rng = random.Random(1000 + seed)
+    shape = [rng.choice([2, 3, 4, 6, 8]) for _ in range(rng.choice([1, 2, 3]))]
+    logical = torch.arange(1, 1 + torch.tensor(shape).prod().item(), dtype=torch.float64).reshape(shape)
+    sb, rb = _random_box(rng, shape), _random_box(rng, shape)
+    s_repr, r_repr = _reshape_randomly(rng, sb, steps=4), _reshape_randomly(rng, rb, steps=4)
+    try:
+        single = box_copy(s_repr, r_repr)
+        single_ok = True
+    except ValueError:
+        single_ok = False
+    try:
+        bcs = box_copies(s_repr, r_repr)
+    except ValueError:
+        assert not single_ok
+        return
+    src = logical[_logical_region(sb)].contiguous()
+    dst = torch.zeros([r - l for l, r, _ in rb], dtype=torch.float64)
+    count = torch.zeros_like(dst)
+    for bc in bcs:
+        strided(dst, bc.dst_offset, bc.extents, bc.dst_strides).copy_(
+            strided(src, bc.src_offset, bc.extents, bc.src_strides))
+        strided(count, bc.dst_offset, bc.extents, bc.dst_strides).add_(1)
+    inter = [(max(a[0], b[0]), min(a[1], b[1])) for a, b in zip(sb, rb)]
+    expect = torch.zeros_like(dst)
+    if all(lo < hi for lo, hi in inter):
+        sub = logical[tuple(slice(lo, hi) for lo, hi in inter)]
+        expect[tuple(slice(lo - b[0], hi - b[0]) for (lo, hi), b in zip(inter, rb))] = sub
+    assert torch.equal(dst, expect)
+    assert (count <= 1).all() and int(count.sum()) == int((expect != 0).sum())
+    if single_ok:
+        assert (single is None) == (not bcs)
