@@ -301,6 +301,51 @@ def box_copies(src_shard: Shard, dst_shard: Shard,
         pass
     ss = list(src_strides) if src_strides is not None else contiguous_strides(shard_extents(src_shard))
     ds = list(dst_strides) if dst_strides is not None else contiguous_strides(shard_extents(dst_shard))
+    try:
+        return _cut_copies(src_shard, ss, dst_shard, ds)
+    except ValueError:
+        pass
+    # last resort: runs of the source with every leading index fixed (a single-row range aligns
+    # with any factorisation of the rest), each cut against the destination like above
+    try:
+        out = []
+        for run, roff in _runs(src_shard, ss):
+            got = _cut_copies(run, ss, dst_shard, ds)
+            for bc in got:
+                bc.src_offset += roff
+            out += got
+        return out
+    except ValueError:
+        pass
+    # any two factorisations of one tensor: runs along the source's last dimension, each a
+    # logically contiguous 1-D range with that dimension's stride
+    out = []
+    for run, roff, st in _flat_runs(src_shard, ss):
+        try:
+            got = _cut_copies(run, [st], dst_shard, ds)
+        except ValueError:
+            raise ValueError(f"shards {src_shard} and {dst_shard} cannot be aligned") from None
+        for bc in got:
+            bc.src_offset += roff
+        out += got
+    return out
+
+
+def _flat_runs(shard: Shard, strides: Sequence[int]):
+    """``(1-D box, element offset, stride)`` of every run along ``shard``'s last dimension."""
+    import itertools
+    n = 1
+    for _l, _r, w in shard:
+        n *= int(w)
+    L = _logical_strides(shard)
+    (ll, lr, _lw), st = shard[-1], int(strides[-1])
+    for idx in itertools.product(*[range(int(l), int(r)) for l, r, _w in shard[:-1]]):
+        base = sum(i * li for i, li in zip(idx, L))
+        off = sum((i - int(l)) * int(s_) for i, (l, _r, _w), s_ in zip(idx, shard, strides))
+        yield [(base + int(ll), base + int(lr), n)], off, st
+
+
+def _cut_copies(src_shard: Shard, ss: Sequence[int], dst_shard: Shard, ds: Sequence[int]) -> list[BoxCopy]:
     out = []
     dst_pieces = list(_pieces(dst_shard, ds, src_shard))
     for sp, soff in _pieces(src_shard, ss, dst_shard):
@@ -311,6 +356,19 @@ def box_copies(src_shard: Shard, dst_shard: Shard,
                 bc.dst_offset += doff
                 out.append(bc)
     return out
+
+
+def _runs(shard: Shard, strides: Sequence[int]):
+    """``(run, element offset)``: ``shard`` cut into boxes whose dims before the first one
+    that is followed only by whole dims are single indices (logically contiguous runs)."""
+    import itertools
+    k = len(shard) - 1
+    while k > 0 and all(int(l) == 0 and int(r) == int(w) for l, r, w in shard[k:]):
+        k -= 1
+    prefix = [range(int(l), int(r)) for l, r, _w in shard[:k]]
+    for idx in itertools.product(*prefix):
+        off = sum((i - int(l)) * int(st) for i, (l, _r, _w), st in zip(idx, shard, strides))
+        yield [(i, i + 1, int(w)) for i, (_l, _r, w) in zip(idx, shard)] + [tuple(int(x) for x in d) for d in shard[k:]], off
 
 
 def _drop_contained(boxes: list[Shard]) -> list[Shard]:
