@@ -12,8 +12,8 @@ import torch
 
 from weightbridge_b200 import WeightData
 from weightbridge_b200.core.binding import bind, pack_into, unpack_from, strided
-from weightbridge_b200.core.shard import (align_shards, box_copies, box_copy, check_shard_compatibility,
-                                          coalesce)
+from weightbridge_b200.core.shard import (_nested, align_shards, box_copies, box_copy,
+                                          check_shard_compatibility, coalesce)
 
 # (sender, receiver, expected aligned sender, expected aligned receiver); None = incompatible
 CASES = {
@@ -121,20 +121,11 @@ def test_overlap_incompatible_raises():
         WeightData.compute_overlap(_meta([(0, 24, 24)]), _meta([(0, 5, 5), (0, 5, 5)]))
 
 
-def test_overlap_of_cross_factorisations_is_cut_into_runs():
-    """4 x 6 against 6 x 4 of the same 24 elements (row-major): no common refinement (the
-    pair-form check says so, like the reference), but the overlap is still every element, cut
-    into runs that each align."""
-    s, r = [(0, 4, 4), (1, 6, 6)], [(0, 6, 6), (0, 4, 4)]
-    assert check_shard_compatibility(s, r) is None
-    ov = WeightData.compute_overlap(_meta(s), _meta(r))
-    assert ov.total_nbytes() == 4 * 5 * 4
-    flat = torch.arange(24, dtype=torch.float32)
-    got = torch.full((24,), -1.0)
-    unpack_from(bind(_meta(r), {"weight": got.view(6, 4)}), ov,
-                WeightData.pack_for(_meta(s), {"weight": flat.view(4, 6)[:, 1:].contiguous()}, ov))
-    exp = torch.where(torch.arange(24) % 6 == 0, torch.tensor(-1.0), flat)
-    assert torch.equal(got, exp)
+def test_cross_factorisations_are_refused():
+    """4 x 6 against 6 x 4 of the same 24 elements: not refinements of one shape, which in a
+    real layout means a transposed or mis-declared tensor, so the overlap is an error."""
+    with pytest.raises(ValueError, match="refinements of one shape"):
+        WeightData.compute_overlap(_meta([(0, 4, 4), (1, 6, 6)]), _meta([(0, 6, 6), (0, 4, 4)]))
 
 
 def test_overlap_cuts_a_range_through_rows_into_rectangles():
@@ -355,9 +346,10 @@ def test_box_copies_cut_ranges_against_dense_oracle(seed):
 
 @pytest.mark.parametrize("seed", range(300))
 def test_box_copies_random_factorisations_against_dense_oracle(seed):
-    """Two partial boxes of one tensor, each re-factorised at random: box_copies always
-    returns pieces, which write exactly the intersection, once per element, and agrees with
-    the single-rectangle box_copy on whether they intersect."""
+    """Two partial boxes of one tensor, each re-factorised at random: box_copies returns
+    pieces for every pair of refinements of one shape (and whenever box_copy aligns), which
+    write exactly the intersection, once per element, and agrees with box_copy on whether
+    they intersect; cross factorisations that box_copy refuses stay refused."""
     rng = random.Random(1000 + seed)
     shape = [rng.choice([2, 3, 4, 6, 8]) for _ in range(rng.choice([1, 2, 3]))]
     logical = torch.arange(1, 1 + torch.tensor(shape).prod().item(), dtype=torch.float64).reshape(shape)
@@ -368,7 +360,11 @@ def test_box_copies_random_factorisations_against_dense_oracle(seed):
         single_ok = True
     except ValueError:
         single_ok = False
-    bcs = box_copies(s_repr, r_repr)         # any two factorisations of one tensor align
+    try:
+        bcs = box_copies(s_repr, r_repr)     # every pair of refinements of one shape aligns
+    except ValueError:
+        assert not single_ok and not _nested(s_repr, r_repr)
+        return
     src = logical[_logical_region(sb)].contiguous()
     dst = torch.zeros([r - l for l, r, _ in rb], dtype=torch.float64)
     count = torch.zeros_like(dst)

@@ -185,9 +185,8 @@ def plan_pair(src: PhysBinding, dst: PhysBinding, names: Iterable[str] | None = 
             for di, dp in enumerate(dst.entries[name]):
                 try:
                     bcs = box_copies(sp.shard, dp.shard, sp.strides, dp.strides)
-                except ValueError:
-                    raise ValueError(f"shard compatibility check failed for {name}: "
-                                     f"{sp.shard} vs {dp.shard}") from None
+                except ValueError as e:
+                    raise ValueError(f"shard compatibility check failed for {name}: {e}") from None
                 for bc in bcs:
                     src_at = _shift(sp, bc.src_offset * s_dtype.itemsize)
                     dst_at = _shift(dp, bc.dst_offset * d_dtype.itemsize)

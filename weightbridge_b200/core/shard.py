@@ -292,37 +292,28 @@ def box_copies(src_shard: Shard, dst_shard: Shard,
     """The intersection of two boxes as strided copies: one when the two factorisations
     align, else one per pair of aligned pieces.  A range that cuts through a block of the
     other side's refinement (an FSDP row range ending inside an attention head, against a
-    per-head box) is cut at those block boundaries first; the pieces are rectangles in the
-    common refinement.  Raises ``ValueError`` when even the pieces cannot be aligned."""
+    per-head box) is cut at those block boundaries first, then, if needed, into runs with every
+    leading index fixed; the pieces are rectangles in the common refinement.  Raises
+    ``ValueError`` when the two boxes' dimensions are not refinements of one shape (4 x 6
+    against 6 x 4: most likely a transposed or mis-declared tensor) or the pieces do not align."""
     try:
         bc = box_copy(src_shard, dst_shard, src_strides, dst_strides)
         return [] if bc is None else [bc]
     except ValueError:
         pass
+    if not _nested(src_shard, dst_shard):
+        raise ValueError(f"shards {src_shard} and {dst_shard} cannot be aligned: their dimensions are not "
+                         "refinements of one shape (a transposed or mis-declared tensor?)")
     ss = list(src_strides) if src_strides is not None else contiguous_strides(shard_extents(src_shard))
     ds = list(dst_strides) if dst_strides is not None else contiguous_strides(shard_extents(dst_shard))
     try:
         return _cut_copies(src_shard, ss, dst_shard, ds)
     except ValueError:
         pass
-    # last resort: runs of the source with every leading index fixed (a single-row range aligns
-    # with any factorisation of the rest), each cut against the destination like above
-    try:
-        out = []
-        for run, roff in _runs(src_shard, ss):
-            got = _cut_copies(run, ss, dst_shard, ds)
-            for bc in got:
-                bc.src_offset += roff
-            out += got
-        return out
-    except ValueError:
-        pass
-    # any two factorisations of one tensor: runs along the source's last dimension, each a
-    # logically contiguous 1-D range with that dimension's stride
     out = []
-    for run, roff, st in _flat_runs(src_shard, ss):
+    for run, roff in _runs(src_shard, ss):
         try:
-            got = _cut_copies(run, [st], dst_shard, ds)
+            got = _cut_copies(run, ss, dst_shard, ds)
         except ValueError:
             raise ValueError(f"shards {src_shard} and {dst_shard} cannot be aligned") from None
         for bc in got:
@@ -331,18 +322,18 @@ def box_copies(src_shard: Shard, dst_shard: Shard,
     return out
 
 
-def _flat_runs(shard: Shard, strides: Sequence[int]):
-    """``(1-D box, element offset, stride)`` of every run along ``shard``'s last dimension."""
-    import itertools
-    n = 1
-    for _l, _r, w in shard:
-        n *= int(w)
-    L = _logical_strides(shard)
-    (ll, lr, _lw), st = shard[-1], int(strides[-1])
-    for idx in itertools.product(*[range(int(l), int(r)) for l, r, _w in shard[:-1]]):
-        base = sum(i * li for i, li in zip(idx, L))
-        off = sum((i - int(l)) * int(s_) for i, (l, _r, _w), s_ in zip(idx, shard, strides))
-        yield [(base + int(ll), base + int(lr), n)], off, st
+def _nested(a: Shard, b: Shard) -> bool:
+    """Whether two boxes' dimensions are refinements of one shape: the logical extents of all
+    their dimension suffixes form a chain under divisibility (4 x 6 and 2 x 2 x 6 do; 4 x 6
+    and 6 x 4 of the same 24 elements do not)."""
+    pts = set()
+    for box in (a, b):
+        m = 1
+        for _l, _r, w in reversed(box):
+            m *= int(w)
+            pts.add(m)
+    pts = sorted(pts)
+    return all(y % x == 0 for x, y in zip(pts, pts[1:]))
 
 
 def _cut_copies(src_shard: Shard, ss: Sequence[int], dst_shard: Shard, ds: Sequence[int]) -> list[BoxCopy]:
@@ -571,9 +562,8 @@ class WeightData:
                 for rs in receiver.shards(name):
                     try:
                         bcs = box_copies(ss, rs)
-                    except ValueError:
-                        raise ValueError(f"shard compatibility check failed for {name}: "
-                                         f"{ss} vs {rs}") from None
+                    except ValueError as e:
+                        raise ValueError(f"shard compatibility check failed for {name}: {e}") from None
                     boxes += [bc.region for bc in bcs]
             if len(receiver.shards(name)) > 1:
                 boxes = _drop_contained(boxes)
