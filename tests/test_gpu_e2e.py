@@ -131,3 +131,12 @@ def test_inprocess_send_async_snapshot_on_gpu():
                 assert st.status == 0 and recv.weights_version == 4
     exp = rl.allocate(device="cuda:0", dtype=torch.bfloat16, fill=True, seed=3)
     assert all(torch.equal(rp[n], exp[n]) for n in exp)
+
+
+@FIRST_RUN
+def test_colocated_ipc_deepseek_mla_fp8_experts():
+    """DeepSeek-style model from Megatron TP 2 over CUDA IPC: MLA with the worker's derived
+    w_kc / w_vc (transposed strided destinations), dense first layer, shared experts, router
+    bias, fp8 routed experts."""
+    run("tiny-deepseek-v3", "gpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)],
+        dict(tp=1, quant="fp8_experts"), device="cuda:0", dtype=torch.bfloat16, n_syncs=2)

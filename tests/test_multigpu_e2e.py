@@ -102,3 +102,11 @@ def test_receiver_leaving_between_syncs_fails_the_next_send():
     assert got["first-sync"][0] is True
     assert got["second-sync"][0] != "no error"
     assert got["second-sync"][1] < 30
+
+
+@FIRST_RUN
+def test_two_gpus_deepseek_mla_over_nvlink():
+    """MLA (w_kc / w_vc written with kv_b_proj) and fp8 experts, trainer on GPU 0, worker on GPU 1."""
+    _need(2)
+    run("tiny-deepseek-v3", "gpu_direct", [dict(tp=1)], dict(tp=1, quant="fp8_experts"), device="cuda:1",
+        dtype=torch.bfloat16, trainer_devices=["cuda:0"], n_syncs=2)
