@@ -49,3 +49,22 @@ def test_chunked_gloo_sync_split_fp8_blocks():
     from tests.e2e_harness import run
     run("tiny-qwen3-moe", "cpu_direct", [dict(etp=4, etp_rank=i) for i in range(4)],
         dict(tp=1, quant="fp8_experts"), dtype=torch.bfloat16, n_syncs=2, cfg_extra={"wire_chunk_bytes": 64 << 10})
+
+
+from hypothesis import given, settings, strategies as st  # noqa: E402
+
+
+@settings(max_examples=200, deadline=None)
+@given(sizes=st.lists(st.integers(1, 5000), min_size=1, max_size=12), chunk=st.integers(0, 8000),
+       pick=st.lists(st.booleans(), min_size=12, max_size=12))
+def test_buffer_size_holds_every_chunk_of_every_subset(sizes, chunk, pick):
+    """The wire sets of partial syncs reuse the full sync's buffers: a buffer of
+    buffer_bytes(full overlap) holds every chunk of any subset of its entries."""
+    import torch
+    from weightbridge_b200 import WeightData
+    from weightbridge_b200.core.wire import buffer_bytes, restrict_overlap, wire_chunks
+    ov = WeightData({f"e{i}": {"shard": [(0, n, n)], "dtype": torch.uint8} for i, n in enumerate(sizes)})
+    cap = buffer_bytes(ov, chunk)
+    names = [f"e{i}" for i in range(len(sizes)) if pick[i]] or ["e0"]
+    for sub in (ov, restrict_overlap(ov, names)):
+        assert all(c.total_nbytes() <= cap for c in wire_chunks(sub, chunk))
