@@ -23,7 +23,7 @@ def _share_cores(nprocs: int) -> None:
 
 
 def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype, late=False, direction="push",
-                 exit_after=None, cfg_extra=None, nprocs=3):
+                 exit_after=None, cfg_extra=None, nprocs=3, subset_prefix=None):
     import threading
     import uvicorn
     from fastapi import FastAPI
@@ -55,9 +55,18 @@ def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype, late=Fal
                 os._exit(0)           # leave between syncs: nothing of ours is in flight
             ok = recv.request_update(views if late else None, timeout=60)
             exp = lay.allocate(device=device, dtype=dtype, fill=True, seed=i)
-            same = all(torch.equal(params[n].view(torch.uint8) if params[n].dtype == torch.float8_e4m3fn else params[n],
-                                   exp[n].view(torch.uint8) if exp[n].dtype == torch.float8_e4m3fn else exp[n])
-                       for n in params)
+            if subset_prefix is not None and i % 2:      # a partial sync: other entries keep seed i - 1
+                prev = lay.allocate(device=device, dtype=dtype, fill=True, seed=i - 1)
+                _m, ev = lay.to_wb(exp)
+                _m, pv = lay.to_wb(prev)
+                as_list = lambda v: v if isinstance(v, list) else [v]      # noqa: E731
+                same = all(torch.equal(a.view(torch.uint8), b.view(torch.uint8))
+                           for n in views
+                           for a, b in zip(as_list(views[n]), as_list((ev if n.startswith(subset_prefix) else pv)[n])))
+            else:
+                same = all(torch.equal(params[n].view(torch.uint8) if params[n].dtype == torch.float8_e4m3fn else params[n],
+                                       exp[n].view(torch.uint8) if exp[n].dtype == torch.float8_e4m3fn else exp[n])
+                           for n in params)
             results.append(bool(ok) and same)
         stats = ctl.get_stats()
         q.put(("rollout", results, stats[0]["epoch"]))
@@ -70,7 +79,7 @@ def rollout_proc(port, q, n_syncs, model, mode, device, rlayout, dtype, late=Fal
 
 
 def trainer_proc(rank, world, tport, url, q, n_syncs, model, mode, device, layouts, dtype, direction="push",
-                 cfg_extra=None, trainer="megatron"):
+                 cfg_extra=None, trainer="megatron", subset_prefix=None):
     import torch.distributed as dist
     from weightbridge_b200 import TransferConfig, WeightSender
     from weightbridge_b200.models.arch import get_arch
@@ -93,7 +102,8 @@ def trainer_proc(rank, world, tport, url, q, n_syncs, model, mode, device, layou
         for i in range(n_syncs):
             if i:
                 lay.fill(params, seed=i)
-            sender.send(views)
+            partial = subset_prefix is not None and i % 2
+            sender.send(views, names=[n for n in views if n.startswith(subset_prefix)] if partial else None)
         q.put(("trainer", rank, sender.epoch))
         dist.destroy_process_group()
     except Exception:
@@ -102,17 +112,19 @@ def trainer_proc(rank, world, tport, url, q, n_syncs, model, mode, device, layou
 
 
 def run(model, mode, trainer_layouts, rollout_layout, device="cpu", dtype=torch.float32, n_syncs=3, timeout=240,
-        trainer_devices=None, late=False, direction="push", cfg_extra=None, trainer="megatron"):
+        trainer_devices=None, late=False, direction="push", cfg_extra=None, trainer="megatron", subset_prefix=None):
+    """``subset_prefix``: odd syncs send only the HF entries with that prefix (partial syncs)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     hport, tport = _port(), _port()
     url = f"http://127.0.0.1:{hport}"
     world = len(trainer_layouts)
     procs = [ctx.Process(target=rollout_proc, args=(hport, q, n_syncs, model, mode, device, rollout_layout, dtype,
-                                                    late, direction, None, cfg_extra, world + 1))]
+                                                    late, direction, None, cfg_extra, world + 1, subset_prefix))]
     tdev = trainer_devices or [device] * world
     procs += [ctx.Process(target=trainer_proc, args=(r, world, tport, url, q, n_syncs, model, mode, tdev[r],
-                                                      trainer_layouts, dtype, direction, cfg_extra, trainer))
+                                                      trainer_layouts, dtype, direction, cfg_extra, trainer,
+                                                      subset_prefix))
               for r in range(world)]
     procs[0].start()
     deadline = time.time() + timeout

@@ -85,3 +85,12 @@ def test_deepseek_fused_shared_expert_slot_fp8_gloo():
     slots = [[]] + [[0, 1, 2, 3, 4, 5, 6, 7, -1]] * 2
     run("tiny-deepseek-v3", "cpu_direct", [dict(tp=2, tp_rank=i) for i in range(2)],
         dict(tp=1, quant="fp8_experts", expert_slots=slots), dtype=torch.bfloat16, n_syncs=2)
+
+
+def test_partial_syncs_with_split_fp8_blocks_gloo():
+    """Odd syncs send layer 1 only: over the wire path, with K/V fp8 blocks split between the
+    two TP ranks (amax exchanged within the partial sync); the rest keeps the previous sync's
+    weights."""
+    run("tiny-qwen2-moe", "cpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)],
+        dict(tp=1, quant="fp8_linear"), dtype=torch.bfloat16, n_syncs=3, subset_prefix="model.layers.1.",
+        cfg_extra=dict(wire_chunk_bytes=64 << 10))
