@@ -140,3 +140,12 @@ def test_colocated_ipc_deepseek_mla_fp8_experts():
     bias, fp8 routed experts."""
     run("tiny-deepseek-v3", "gpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)],
         dict(tp=1, quant="fp8_experts"), device="cuda:0", dtype=torch.bfloat16, n_syncs=2)
+
+
+@FIRST_RUN
+def test_colocated_ipc_partial_syncs_with_split_fp8_blocks():
+    """Odd syncs send layer 1 only (names=): the split K/V fp8 blocks of that layer are
+    quantised with the exchanged amax, the other layers keep the previous weights."""
+    run("tiny-qwen2-moe", "gpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)],
+        dict(tp=1, quant="fp8_linear"), device="cuda:0", dtype=torch.bfloat16, n_syncs=3,
+        subset_prefix="model.layers.1.")
