@@ -7,9 +7,6 @@ import torch
 from tests.e2e_harness import run
 
 pytestmark = pytest.mark.gpu
-# Written since the last run on a B200: they run and report, but a failure does not stop the
-# rest of the GPU suite (pytest -x) before the tests that have passed there.
-FIRST_RUN = pytest.mark.xfail(reason="first run on a B200 pending", strict=False)
 
 
 def test_colocated_ipc_tiny_llama_tp2_to_tp1():
@@ -28,7 +25,6 @@ def test_colocated_ipc_reference_style_late_binding():
         dtype=torch.bfloat16, late=True)
 
 
-@FIRST_RUN
 def test_colocated_ipc_split_fp8_blocks():
     """Expert TP 4 (64-row slices): every expert block is split over two senders, which
     exchange the block amax through the session before their kernels store into the
@@ -37,7 +33,6 @@ def test_colocated_ipc_split_fp8_blocks():
         dict(tp=1, quant="fp8_experts"), device="cuda:0", dtype=torch.bfloat16, n_syncs=2)
 
 
-@FIRST_RUN
 def test_colocated_ipc_fp8_linear_from_grouped_qkv():
     """fp8 on every linear layer from Megatron TP 2: grouped-QKV overlaps cut per KV group,
     K/V blocks split between the two ranks (amax exchanged), stores over CUDA IPC."""
@@ -45,14 +40,12 @@ def test_colocated_ipc_fp8_linear_from_grouped_qkv():
         dict(tp=1, quant="fp8_linear"), device="cuda:0", dtype=torch.bfloat16, n_syncs=2)
 
 
-@FIRST_RUN
 def test_colocated_ipc_pull_direction():
     """The receiver maps the senders' memory (CUDA IPC) and runs the pull kernel itself."""
     run("tiny-llama", "gpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)], dict(tp=1),
         device="cuda:0", dtype=torch.bfloat16, direction="pull")
 
 
-@FIRST_RUN
 def test_raw_shards_example_on_one_gpu():
     """Hand-built metadata (uneven rows, column split, duplicated tensor), flat receiver
     buffers bound at request_update, two trainer and two worker processes on cuda:0."""
@@ -66,7 +59,6 @@ def test_raw_shards_example_on_one_gpu():
     assert out.stdout.strip().splitlines()[-1].startswith("OK")
 
 
-@FIRST_RUN
 def test_inprocess_send_async_on_gpu():
     """Sender, controller and receiver in one process on cuda:0 (the sender uses the
     receiver's addresses directly); send_async overlaps with the caller and tags the weights."""
@@ -98,7 +90,6 @@ def test_inprocess_send_async_on_gpu():
     assert all(torch.equal(rp[n], exp[n]) for n in exp)
 
 
-@FIRST_RUN
 def test_inprocess_send_async_snapshot_on_gpu():
     """send_async(snapshot=True) on cuda:0: the copy is enqueued on the caller's stream, the
     caller overwrites its parameters right away (the next optimizer step) and the worker
@@ -133,7 +124,6 @@ def test_inprocess_send_async_snapshot_on_gpu():
     assert all(torch.equal(rp[n], exp[n]) for n in exp)
 
 
-@FIRST_RUN
 def test_colocated_ipc_deepseek_mla_fp8_experts():
     """DeepSeek-style model from Megatron TP 2 over CUDA IPC: MLA with the worker's derived
     w_kc / w_vc (transposed strided destinations), dense first layer, shared experts, router
@@ -142,7 +132,6 @@ def test_colocated_ipc_deepseek_mla_fp8_experts():
         dict(tp=1, quant="fp8_experts"), device="cuda:0", dtype=torch.bfloat16, n_syncs=2)
 
 
-@FIRST_RUN
 def test_colocated_ipc_partial_syncs_with_split_fp8_blocks():
     """Odd syncs send layer 1 only (names=): the split K/V fp8 blocks of that layer are
     quantised with the exchanged amax, the other layers keep the previous weights."""

@@ -23,9 +23,6 @@ from weightbridge_b200.parallel.megatron import MegatronLayout
 from weightbridge_b200.parallel.sglang import SGLangLayout
 
 pytestmark = pytest.mark.gpu
-# Written since the last run on a B200: they run and report, but a failure does not stop the
-# rest of the GPU suite (pytest -x) before the tests that have passed there.
-FIRST_RUN = pytest.mark.xfail(reason="first run on a B200 pending", strict=False)
 ABS = lambda _a: 0
 MODES = [MODE_VECTOR, MODE_BULK8, MODE_BULK12, MODE_BULK4]
 
@@ -201,7 +198,6 @@ def test_repeated_launches_reset_counter():
 
 
 @pytest.mark.parametrize("etp,dtype", [(4, torch.bfloat16), (8, torch.bfloat16), (4, torch.float32)])
-@FIRST_RUN
 def test_gpu_split_blocks_match_whole_tensor_oracle(etp, dtype):
     """fp8 blocks split across senders (expert TP slices of 64 / 32 rows): split_amax on every
     sender's pieces, the block amax merged over the senders on the host, split_quant plus the
@@ -237,3 +233,22 @@ def test_gpu_split_blocks_match_whole_tensor_oracle(etp, dtype):
     expected = lay.allocate(device=dev, dtype=dtype, fill=True)
     for n in rparams:
         assert torch.equal(_u8(rparams[n]), _u8(expected[n])), n
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+def test_gpu_synth_fill_kernel_matches_torch_ops(dtype):
+    """The native fill kernel writes, into strided views, exactly the values the torch-op
+    statement of the same arithmetic produces on the GPU (boxes with offsets, 1-D to 3-D)."""
+    from weightbridge_b200.models.synthetic import synth_fill, synth_values
+    dev = torch.device("cuda", 0)
+    full = torch.zeros(96, 3 * 160, dtype=dtype, device=dev)
+    cases = [
+        ("w.col", full[:, 160:320], [(32, 128, 512), (160, 320, 480)]),          # column block, row offset
+        ("w.grp", full[:, :150].unflatten(1, (3, 50)), [(0, 96, 96), (1, 4, 7), (5, 55, 60)]),
+        ("w.flat", torch.zeros(4099, dtype=dtype, device=dev)[3:], [((1 << 33) + 5, (1 << 33) + 4101, 1 << 40)]),
+    ]
+    for name, view, box in cases:
+        synth_fill(view, name, box, seed=3)
+        ref = synth_values(name, box, dev, dtype, seed=3)
+        assert torch.equal(view.contiguous().view(torch.uint8 if dtype != torch.float32 else torch.int32),
+                           ref.contiguous().view(torch.uint8 if dtype != torch.float32 else torch.int32)), name
