@@ -10,7 +10,9 @@
 //   * bulk items     - 16-byte aligned copies moved by the TMA engine: one elected thread
 //                      streams pieces global -> shared (cp.async.bulk + mbarrier) and
 //                      shared -> destination (cp.async.bulk bulk_group), S stages deep.
-//                      No cluster multicast anywhere: every load reads this GPU's memory.
+//                      Bulk loads may read a peer GPU's memory (the pull direction runs
+//                      this kernel on the receiver with sources in the sender's IPC
+//                      mapping); no load or store here uses .multicast::cluster.
 //
 // Completion: every CTA fences at system scope and bumps a scratch counter; the last CTA
 // writes the epoch with st.release.sys to each flag and resets the counter.  Every wait in
