@@ -2,10 +2,12 @@
 
 It serves callers that cannot allocate GPU memory (an engine whose allocator already owns
 the free memory, or a C host without a tensor framework): they pass the work table in host
-memory and the library stages it into its fixed device scratch array.  This test checks that
+memory and the library stages it into its fixed device scratch array.  These tests check that
 it produces exactly what the regular entry point (``TransferProgram.launch``) produces, on
-two calls in a row with different weights, publishes the epoch to the flag, and rejects
-tables beyond its stated maximum without launching anything.
+two calls in a row with different weights (the work table in pinned memory that the caller
+overwrites as soon as each call returns), publishes the epoch to the flag, rejects tables
+beyond its stated maximum without launching anything, and that calls after the first leave
+the device's free memory and the caching allocator's counters unchanged.
 
 The file is named so that pytest collects it last.
 """
@@ -69,7 +71,11 @@ def test_noalloc_entry_matches_regular_entry_on_two_calls():
     flag_b = torch.zeros(1, dtype=torch.int64, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     prog_b = TransferProgram(tab_b, dev, [flag_b.data_ptr()], LaunchConfig(mode=MODE_VECTOR))
-    items = np.ascontiguousarray(tab_a.items)
+    # the work table sits in pinned host memory and is overwritten (with empty items) as soon as
+    # the call returns: the entry point must have taken its own copy by then
+    table = np.ascontiguousarray(tab_a.items).view(np.uint8)
+    pinned = torch.empty(table.nbytes, dtype=torch.uint8, pin_memory=True)
+    items = pinned.numpy()
     flags = np.array([flag_a.data_ptr()], dtype=np.uint64)
     stream = torch.cuda.current_stream(dev)
     for call, seed in ((1, 11), (2, 12)):
@@ -77,7 +83,10 @@ def test_noalloc_entry_matches_regular_entry_on_two_calls():
             lay.fill(sp, seed=seed)
         torch.cuda.synchronize()
         prog_b.launch(epoch=call)
-        rc = fn(items.ctypes.data, len(items), flags.ctypes.data, 1, call, status.data_ptr(), stream.cuda_stream)
+        items[:] = table
+        rc = fn(items.ctypes.data, len(tab_a.items), flags.ctypes.data, 1, call, status.data_ptr(),
+                stream.cuda_stream)
+        items[:] = 0
         assert rc == 0, rc
         torch.cuda.synchronize()
         assert int(status.item()) == 0 and prog_b.read_status() == 0
@@ -101,3 +110,27 @@ def test_noalloc_rejects_oversized_tables():
     assert fn(None, 0, flags.ctypes.data, 65, 1, None, stream.cuda_stream) == -2
     assert fn(None, 5, None, 0, 1, None, stream.cuda_stream) == -3
     torch.cuda.synchronize()
+
+
+def test_noalloc_calls_allocate_no_device_memory():
+    """After the first call on the device (which looks up the scratch array), further calls
+    leave the device's free memory and the caching allocator's counters unchanged."""
+    fn = _lib()
+    dev, _senders, _sparams, ((_rp_a, tab_a), _b) = _setup()
+    flag = torch.zeros(1, dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    items = np.ascontiguousarray(tab_a.items)
+    flags = np.array([flag.data_ptr()], dtype=np.uint64)
+    stream = torch.cuda.current_stream(dev)
+    assert fn(items.ctypes.data, len(items), flags.ctypes.data, 1, 1, status.data_ptr(), stream.cuda_stream) == 0
+    torch.cuda.synchronize()
+    free0, _total = torch.cuda.mem_get_info(dev)
+    keys = ("num_device_alloc", "num_device_free", "allocated_bytes.all.current", "reserved_bytes.all.current")
+    stats0 = {k: torch.cuda.memory_stats(dev).get(k) for k in keys}
+    for call in range(2, 7):
+        rc = fn(items.ctypes.data, len(items), flags.ctypes.data, 1, call, status.data_ptr(), stream.cuda_stream)
+        assert rc == 0, rc
+        torch.cuda.synchronize()
+    assert int(flag.item()) == 6 and int(status.item()) == 0
+    assert torch.cuda.mem_get_info(dev)[0] == free0
+    assert {k: torch.cuda.memory_stats(dev).get(k) for k in keys} == stats0

@@ -15,7 +15,8 @@
 //
 // The scratch array lives in device memory of every GPU that loads this library, from load
 // until process exit, whether or not this entry point is ever called.  Its size is fixed at
-// build time by the two limits below (about 400 KB).
+// build time by the two limits below (about 400 KB); a host staging block of the same size,
+// also part of the library, carries the arguments over.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -40,16 +41,21 @@ extern "C" {
 // Kernel errors set bits in *status (a device word owned by the caller; may be NULL).
 //
 // Allocates nothing: no cudaMalloc, cudaFree or allocating library call.  The work table,
-// flag table, epoch and completion counter are staged into the library's fixed device
-// scratch array with cudaMemcpyAsync/cudaMemsetAsync on `stream`; the host arrays may be
-// reused as soon as the call returns.
+// flag table and epoch are first copied into a fixed staging block in the library's own host
+// memory and then sent with ONE cudaMemcpyAsync on `stream` into the library's fixed device
+// scratch array (the same copy zeroes the completion counter).  Because that staging block is
+// ordinary pageable memory, the copy has read it before cudaMemcpyAsync returns, so the
+// caller's host arrays may be reused as soon as this call returns, whether they are pageable,
+// pinned or registered memory.  A host-to-device copy from pageable memory also waits for the
+// work already queued on `stream`: this call blocks the calling thread until that work is done.
 //
 // The first call on a device (with that device current) looks up the scratch array's device
-// address (cudaGetSymbolAddress) and caches it; make that first call before any stream
-// capture on the device.  All calls share the one scratch array and it keeps the contents
-// of the last call: the completion counter is cleared at the start of every call, and two
-// calls whose work overlaps on the GPU (different streams, or different host threads on
-// the same device) race on the scratch and must be serialised by the caller.
+// address (cudaGetSymbolAddress) and caches it per device and driver context; make that first
+// call before any stream capture on the device, and do not reset the device (cudaDeviceReset)
+// between calls.  All calls share the one scratch array and it keeps the contents of the last
+// call.  Calls from several host threads are serialised while they stage and enqueue, but two
+// calls whose work overlaps on the GPU (different streams, or the same device driven by
+// several threads without ordering) race on the scratch and must be serialised by the caller.
 //
 // Returns 0 on success, a WB_NOALLOC_ERR_* code for rejected arguments, or the cudaError_t
 // of the failing CUDA runtime call.
