@@ -8,11 +8,13 @@
 #include <cstring>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "wb_common.h"
 #include "wb_cpu.h"
 #include "wb_ipc.h"
 #include "wb_splitq.h"
+#include "wb_synth.h"
 #include "wb_transfer.h"
 
 namespace py = pybind11;
@@ -108,6 +110,28 @@ py::bytes data_ptrs(const py::list& tensors) {
   return py::bytes(out);
 }
 
+void synth_fill(uint64_t dst, uint32_t dtype, uint64_t key, double std, const std::vector<int64_t>& ext,
+                const std::vector<int64_t>& vstride, const std::vector<int64_t>& lo,
+                const std::vector<int64_t>& lstride, uint64_t stream) {
+  const size_t n = ext.size();
+  if (n < 1 || n > (size_t)wb::kSynthMaxDims || vstride.size() != n || lo.size() != n || lstride.size() != n)
+    throw std::invalid_argument("synth_fill: 1-8 dimensions with one extent, stride, start and logical stride each");
+  if (!wb::synth_dtype_supported(dtype)) throw std::invalid_argument("synth_fill: dtype code not supported");
+  wb::SynthDesc d{};
+  d.dst = dst;
+  d.ndim = (int32_t)n;
+  d.dtype = dtype;
+  d.key = key;
+  d.std = std;
+  for (size_t k = 0; k < n; ++k) {
+    d.ext[k] = ext[k];
+    d.vstride[k] = vstride[k];
+    d.lo[k] = lo[k];
+    d.lstride[k] = lstride[k];
+  }
+  check(wb::launch_synth_fill(d, reinterpret_cast<cudaStream_t>(stream)), "synth_fill launch");
+}
+
 int num_sms(int device) {
   int v = 0;
   check(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device), "cudaDeviceGetAttribute");
@@ -129,6 +153,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cpu_split_amax", &cpu_split_amax, "per-piece amax of split fp8 blocks on the host");
   m.def("cpu_split_quant", &cpu_split_quant, "quantise split fp8 block pieces on the host");
   m.def("num_sms", &num_sms);
+  m.def("synth_fill", &synth_fill, "fill a strided view with the synthetic weights");
+  m.def("synth_dtype_supported", &wb::synth_dtype_supported);
   m.def("data_ptrs", &data_ptrs, "data pointers of a list of tensors, 8 bytes each");
   m.def("addr_range", [](uint64_t p) {
     auto r = wb::addr_range(p);

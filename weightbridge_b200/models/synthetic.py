@@ -4,7 +4,9 @@ Every element of a logical HF tensor gets a value that depends only on (seed, te
 flat logical index), so each rank can fill its own shard (any box, any factorisation, any
 strided view) without materialising the full tensor, and a receiver can regenerate what it
 should have received and compare bit for bit.  Uses a 32-bit integer mixing hash and a
-Box-Muller transform in plain torch ops (same values on every device of one type).
+Box-Muller transform.  On a CUDA device one launch of the native fill kernel
+(``csrc/wb_synth.cu``) writes a whole view; ``synth_values`` states the same arithmetic in
+torch ops, which the host path runs and the GPU tests compare the kernel against bit for bit.
 """
 from __future__ import annotations
 
@@ -60,12 +62,33 @@ def synth_values(name: str, box: Shard, device, dtype=torch.float32, seed: int =
     return (z * std).to(dtype)
 
 
+def _native_fill(view: torch.Tensor, name: str, box: Shard, seed: int, std: float) -> bool:
+    """One launch of the fill kernel on the view's device and current stream; False when the
+    view's dtype is not one the kernel writes."""
+    from ..ops._ext import ext
+    from ..utils.dtypes import DTYPE_CODES
+    code = DTYPE_CODES.get(view.dtype)
+    if code is None or not ext().synth_dtype_supported(code) or len(box) > 8:
+        return False
+    widths = [w for _, _, w in box]
+    lstr = [1] * len(box)
+    for d in range(len(box) - 2, -1, -1):
+        lstr[d] = lstr[d + 1] * widths[d + 1]
+    stream = torch.cuda.current_stream(view.device).cuda_stream
+    with torch.cuda.device(view.device):
+        ext().synth_fill(view.data_ptr(), code, name_key(name, seed), float(std), list(view.shape),
+                         list(view.stride()), [l for l, _, _ in box], lstr, stream)
+    return True
+
+
 def synth_fill(view: torch.Tensor, name: str, box: Shard, seed: int = 0, std: float = 0.02,
                chunk_elems: int = 1 << 25) -> torch.Tensor:
     """Fill ``view`` (shape == box extents, any strides) with the synthetic values."""
     ext = [r - l for l, r, _ in box]
     if list(view.shape) != ext:
         view = view.view(ext)
+    if view.is_cuda and view.numel() and _native_fill(view, name, box, seed, std):
+        return view
     rows = ext[0]
     per_row = max(1, view.numel() // max(rows, 1))
     step = max(1, chunk_elems // per_row)
