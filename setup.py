@@ -19,7 +19,7 @@ NVCC_FLAGS = [
 setup(
     name="weightbridge_b200",
     version="0.1.0",
-    packages=find_packages(include=["weightbridge_b200", "weightbridge_b200.*"]),
+    packages=find_packages(include=["weightbridge_b200", "weightbridge_b200.*", "wbridge"]),
     ext_modules=[
         CUDAExtension(
             name="weightbridge_b200._C",
