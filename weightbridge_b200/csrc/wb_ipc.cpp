@@ -21,11 +21,16 @@ void check_rt(cudaError_t e, const char* what) {
   if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+// The ABI version every entry point is requested at: the one of the cuda.h these typedefs
+// were written against.  (A symbol newer than the requested version - the multicast API is
+// 12.1 - is reported as not found.)
+constexpr unsigned kDriverAbi = CUDA_VERSION;
+
 template <typename F>
 F entry(const char* name) {
   void* fn = nullptr;
   cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-  cudaError_t e = cudaGetDriverEntryPointByVersion(name, &fn, 12000, cudaEnableDefault, &q);
+  cudaError_t e = cudaGetDriverEntryPointByVersion(name, &fn, kDriverAbi, cudaEnableDefault, &q);
   if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
     throw std::runtime_error(std::string("driver entry point unavailable: ") + name);
   return reinterpret_cast<F>(fn);

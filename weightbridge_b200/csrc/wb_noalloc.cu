@@ -50,7 +50,7 @@ void* current_context() {
   static CtxGetCurrent fn = [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, CUDA_VERSION, cudaEnableDefault, &q) != cudaSuccess ||
         q != cudaDriverEntryPointSuccess)
       p = nullptr;
     return reinterpret_cast<CtxGetCurrent>(p);

@@ -51,6 +51,11 @@ __device__ __forceinline__ void st_mc16(void* p, uint4 v) {
 __device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+// release store of a flag word through an NVLink multicast address: every replica's copy of
+// the word receives it, ordered after this thread's earlier multimem stores
+__device__ __forceinline__ void st_mc_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("multimem.st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 __device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
   uint64_t v;
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -468,7 +473,11 @@ __device__ void signal_done(const Signal& sg, uint32_t* s_last) {
   if (*s_last && threadIdx.x == 0) {
     __threadfence_system();
     const uint64_t e = *reinterpret_cast<volatile const uint64_t*>(sg.epoch);
-    for (uint32_t i = 0; i < sg.n_flags; ++i) st_release_sys(reinterpret_cast<uint64_t*>(sg.flag_addrs[i]), e);
+    for (uint32_t i = 0; i < sg.n_flags; ++i) {
+      const uint64_t a = sg.flag_addrs[i];     // bit 0 set: a multicast address (replica group)
+      if (a & 1ull) st_mc_release_sys(reinterpret_cast<uint64_t*>(a & ~1ull), e);
+      else st_release_sys(reinterpret_cast<uint64_t*>(a), e);
+    }
     *reinterpret_cast<volatile uint32_t*>(sg.counter) = 0u;
     __threadfence();
   }

@@ -10,7 +10,8 @@ namespace wb {
 // Completion signal of one launch.
 struct Signal {
   uint32_t* counter;           // scratch word, zero between launches (the last CTA resets it)
-  const uint64_t* flag_addrs;  // device array: addresses of the flag words to publish to
+  const uint64_t* flag_addrs;  // device array: addresses of the flag words to publish to (bit 0
+                               // set: an NVLink multicast address, written with multimem.st)
   uint32_t n_flags;
   const uint64_t* epoch;       // device word holding this sync's epoch
   uint32_t* status;            // ST_* bits, or null

@@ -4,9 +4,10 @@ rollout replica through the NVSwitch.
 For a *replica group* (receivers with identical metadata and identical pool-relative
 bindings, e.g. several SGLang TP1 replicas), sender rank 0 creates one multicast object the
 size of a replica's VMM pool and shares it as a file descriptor.  Every participant adds its
-device; replicas bind their pool to it; senders bind a scratch pool of the same size (every
-device added to the object backs it with memory) and map the object.  Stores to
-``mc_base + offset`` then land at ``offset`` in every bound pool.  The transfer kernel writes
+device; replicas bind their pool to it; senders back it with scratch memory nobody reads
+(every device added to the object must back all of it: a sender binds one window of at most
+``SCRATCH_WINDOW`` bytes at every window offset, see ``McMember.bind_scratch``) and map the
+object.  Stores to ``mc_base + offset`` then land at ``offset`` in every bound pool.  The transfer kernel writes
 such items with ``multimem.st.relaxed.sys.global.v4.f32`` (16-byte aligned items only) and
 publishes the epoch to each replica's flag word with ordinary unicast stores.
 
@@ -23,15 +24,41 @@ import json
 import os
 from dataclasses import dataclass, field
 
+import logging
+
 from ..ops._ext import ext
 from .fdpass import FdServer, fetch_fd
 from .vmm import VmmPool
 
+logger = logging.getLogger(__name__)
+
+
+SCRATCH_WINDOW = 1 << 30          # a sender's backing of a multicast object: at most this much
+
+
+def scratch_window(size: int, device: int, window: int = SCRATCH_WINDOW) -> int:
+    """The largest multiple of the multicast granularity that divides ``size`` and is at most
+    ``window`` (at least one granule)."""
+    gran = max(ext().vmm_granularity(device, True), ext().vmm_granularity(device, False))
+    if size % gran:
+        return size
+    n = size // gran
+    best = 1
+    for k in range(1, n + 1):
+        if k * gran > window:
+            break
+        if n % k == 0:
+            best = k
+    return best * gran
+
 
 def nvls_supported(device_index: int) -> bool:
+    """Whether the device reports NVLink multicast support (a driver query that fails is
+    logged and counts as no support)."""
     try:
         return bool(ext().multicast_supported(device_index))
     except Exception:
+        logger.warning("multicast support query failed on device %d", device_index, exc_info=True)
         return False
 
 
@@ -86,11 +113,37 @@ class McMember:
         ext().mc_bind_mem(self.handle, 0, pool.handle, 0, self.size)
         self.bound = True
 
-    def bind_scratch(self) -> None:
+    def bind_scratch(self, window: int = SCRATCH_WINDOW) -> None:
+        """Back this (sender) device's share of the object with memory nobody reads.  Every
+        device added to a multicast object must back all of it, but a sender only issues the
+        stores: one ``window``-sized allocation is bound at every window offset of the object
+        (the multimem stores that land here overwrite each other), so the sender pays the
+        window instead of a whole replica.  If the driver refuses to bind one allocation at
+        several offsets, a scratch pool of the object's full size is used instead (noted)."""
+        w = scratch_window(self.size, self.device, window)
+        if w < self.size:
+            self.scratch = VmmPool(w, self.device, tail_bytes=0)
+            done = 0
+            try:
+                for off in range(0, self.size, w):
+                    ext().mc_bind_mem(self.handle, off, self.scratch.handle, 0, w)
+                    done += w
+                self.bound = True
+                return
+            except RuntimeError as e:
+                self.notes.append(f"windowed scratch refused after {done} bytes ({e}); binding {self.size} bytes")
+                if done:
+                    ext().mc_unbind(self.handle, self.device, 0, done)
+                self.scratch.free()
+                self.scratch = None
         self.scratch = VmmPool(self.size, self.device, tail_bytes=0)
         if self.scratch.size != self.size:
             raise ValueError("scratch pool size differs from the multicast object")
         self.bind(self.scratch)
+
+    @property
+    def scratch_bytes(self) -> int:
+        return self.scratch.size if self.scratch is not None else 0
 
     def map(self) -> int:
         self.mapped = ext().mc_map(self.handle, self.size, self.device)
