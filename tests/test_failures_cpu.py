@@ -72,11 +72,12 @@ def _cfg(**kw):
     return TransferConfig(**base)
 
 
-@pytest.mark.parametrize("mode", ["cpu_direct", "gpu_direct"])
-def test_sync_then_receiver_never_updates_times_out(mode):
+@pytest.mark.parametrize("mode,direction", [("cpu_direct", "push"), ("gpu_direct", "push"), ("gpu_direct", "pull")])
+def test_sync_then_receiver_never_updates_times_out(mode, direction):
     """gpu_direct with host tensors in one process runs the device protocol (work tables,
-    flags, ready/done, status) through the C++ executor."""
-    cfg = _cfg(sync_timeout_s=2.0, mode=mode)
+    flags, ready/done, status) through the C++ executor.  Pulling, the sender does not wait
+    for the worker to be ready; it fails waiting for the worker to pull."""
+    cfg = _cfg(sync_timeout_s=2.0, mode=mode, direction=direction)
     ro = Rollout(cfg)
     try:
         lay, params, meta, views = _sender(cfg)
@@ -91,19 +92,20 @@ def test_sync_then_receiver_never_updates_times_out(mode):
         assert all(torch.equal(ro.params[n], exp[n]) for n in exp)
         assert ro.recv.epoch == 1
         if mode == "gpu_direct":
-            assert int(ro.recv.flags[0]) == 1
+            pushed = direction == "push"      # pulling, the worker copies and no flag is written
+            assert int(ro.recv.flags[0]) == (1 if pushed else 0)
             # a second good sync with new weights
             lay.fill(params, seed=5)
             th = threading.Thread(target=lambda: ro.recv.request_update(timeout=20))
             th.start()
             st = s.send(views)
             th.join(20)
-            assert st.epoch == 2 and st.status == 0 and int(ro.recv.flags[0]) == 2
+            assert st.epoch == 2 and st.status == 0 and int(ro.recv.flags[0]) == (2 if pushed else 0)
             exp = ro.lay.allocate(dtype=torch.float32, fill=True, seed=5)
             assert all(torch.equal(ro.params[n], exp[n]) for n in exp)
         # now nobody calls request_update: send must fail by the deadline, not hang
         t0 = time.time()
-        with pytest.raises(TransferError, match="ready"):
+        with pytest.raises(TransferError, match="ready" if direction == "push" else "pull"):
             s.send(views)
         assert time.time() - t0 < 10
     finally:
@@ -313,8 +315,10 @@ def test_pull_direction_in_process():
         ro.close()
 
 
-def test_pull_direction_with_pushed_fp8_blocks():
-    """Hybrid sync: quantised expert blocks pushed by the sender, everything else pulled."""
+def test_pull_request_with_fp8_blocks_pushes_everything():
+    """A session whose workers hold fp8 block-quantised entries pushes every copy even when
+    pull was asked for: the sender quantises (halving the bytes on the link), and pulling the
+    plain copies could only start after its kernel stored the blocks."""
     import uvicorn
     from fastapi import FastAPI
     cfg = _cfg(mode="gpu_direct", direction="pull")
@@ -340,8 +344,9 @@ def test_pull_direction_with_pushed_fp8_blocks():
         th.start()
         s.send(sviews)
         th.join(20)
-        assert s.program is not None and len(s.program.tables.qwork) > 0 and len(s.program.tables.items) == 0
-        assert len(recv.pull_program.tables.items) > 0 and len(recv.pull_program.tables.qwork) == 0
+        assert s.direction == "push" and recv.direction == "push"
+        assert s.program is not None and len(s.program.tables.qwork) > 0 and len(s.program.tables.items) > 0
+        assert recv.pull_program is None
         exp = rl.allocate(dtype=torch.bfloat16, fill=True)
         u8 = lambda t: t.view(torch.uint8) if t.dtype == torch.float8_e4m3fn else t
         assert all(torch.equal(u8(rparams[n]), u8(exp[n])) for n in exp)
@@ -608,7 +613,7 @@ def test_worker_endpoints_use_the_host_address_not_the_master_override(monkeypat
 def test_push_alternating_tensor_sets_uses_cached_programs():
     """Two sets of trainer tensors sent alternately: each send moves the set it is given, and
     each set's program is compiled once."""
-    cfg = _cfg(mode="gpu_direct")
+    cfg = _cfg(mode="gpu_direct", direction="push")
     ro = Rollout(cfg)
     try:
         lay, params, meta, views = _sender(cfg)

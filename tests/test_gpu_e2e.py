@@ -9,14 +9,18 @@ from tests.e2e_harness import run
 pytestmark = pytest.mark.gpu
 
 
-def test_colocated_ipc_tiny_llama_tp2_to_tp1():
+@pytest.mark.parametrize("direction", ["pull", "push"])
+def test_colocated_ipc_tiny_llama_tp2_to_tp1(direction):
     run("tiny-llama", "gpu_direct", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)], dict(tp=1),
-        device="cuda:0", dtype=torch.bfloat16)
+        device="cuda:0", dtype=torch.bfloat16, direction=direction)
 
 
-def test_colocated_ipc_qwen3_moe_fp8_experts():
+@pytest.mark.parametrize("direction", ["pull", "push"])
+def test_colocated_ipc_qwen3_moe_fp8_experts(direction):
+    """pull: the receiver loads the bf16 copies while the senders quantise and push the fp8
+    expert blocks; push: the senders store everything."""
     run("tiny-qwen3-moe", "gpu_direct", [dict(ep=2, ep_rank=0), dict(ep=2, ep_rank=1)],
-        dict(tp=1, quant="fp8_experts"), device="cuda:0", dtype=torch.bfloat16, n_syncs=2)
+        dict(tp=1, quant="fp8_experts"), device="cuda:0", dtype=torch.bfloat16, n_syncs=2, direction=direction)
 
 
 def test_colocated_ipc_reference_style_late_binding():

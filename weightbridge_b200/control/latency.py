@@ -4,8 +4,10 @@ Runs a rollout server (FastAPI controller + one receiver worker thread) and a se
 process with host tensors of a tiny model (``gpu_direct`` protocol through the C++ executor:
 arm, ready / done handshakes, epoch flags), and reports per-sync medians: the whole
 ``send()``, the wait for the worker's ready key (the arm's round trip), the copy itself, and
-``request_update`` on the worker side.  The payload is ~8 MB, so the numbers are the control
-plane's own cost, the floor under every sync's end-to-end time.
+``request_update`` on the worker side.  ``--direction push`` (the default here) measures the
+protocol in which the sender copies; pulling, the worker copies and the sender waits for no
+ready key.  The payload is ~8 MB, so the numbers are the control plane's own cost, the floor
+under every sync's end-to-end time.
 """
 from __future__ import annotations
 
@@ -17,7 +19,7 @@ import threading
 import time
 
 
-def measure(arm: str = "direct", syncs: int = 200, model: str = "tiny-llama") -> dict:
+def measure(arm: str = "direct", syncs: int = 200, model: str = "tiny-llama", direction: str = "push") -> dict:
     import torch
     from ..models.arch import get_arch
     from ..parallel.megatron import MegatronLayout
@@ -27,7 +29,7 @@ def measure(arm: str = "direct", syncs: int = 200, model: str = "tiny-llama") ->
     from .receiver import WeightReceiver
     from .sender import WeightSender
 
-    cfg = TransferConfig(mode="gpu_direct", arm=arm, connect_timeout_s=60, sync_timeout_s=60)
+    cfg = TransferConfig(mode="gpu_direct", arm=arm, connect_timeout_s=60, sync_timeout_s=60, direction=direction)
     arch = get_arch(model)
     rl = SGLangLayout(arch, tp=1)
     rparams = rl.allocate(dtype=torch.float32)
@@ -66,7 +68,8 @@ def measure(arm: str = "direct", syncs: int = 200, model: str = "tiny-llama") ->
     tail = slice(min(20, syncs // 4), None)             # drop the first syncs (plan compile, caches)
     hist = sender.history[tail]
     med = lambda xs: round(statistics.median(xs), 3) if xs else None   # noqa: E731
-    return {"arm": arm, "syncs": syncs, "model": model, "payload_bytes": hist[-1].bytes_written if hist else 0,
+    return {"arm": arm, "direction": direction, "syncs": syncs, "model": model,
+            "payload_bytes": hist[-1].bytes_written if hist else 0,
             "send_ms": med(sends[tail]), "wait_ready_ms": med([h.wait_ready_ms for h in hist]),
             "copy_ms": med([h.device_ms for h in hist]), "request_update_ms": med(upd[tail]),
             "note": "one process, host tensors; separate processes add socket hops but no GIL contention"}
@@ -77,8 +80,9 @@ def main(argv=None) -> int:
     ap.add_argument("--arm", choices=["direct", "http"], default="direct")
     ap.add_argument("--syncs", type=int, default=200)
     ap.add_argument("--model", default="tiny-llama")
+    ap.add_argument("--direction", choices=["push", "pull"], default="push")
     a = ap.parse_args(argv)
-    print(json.dumps(measure(a.arm, a.syncs, a.model)))
+    print(json.dumps(measure(a.arm, a.syncs, a.model, a.direction)))
     return 0
 
 

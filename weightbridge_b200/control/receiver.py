@@ -210,7 +210,9 @@ class WeightReceiver:
         """Stop the worker thread and release the session."""
         self._stop.set()
         if self.receiver_thread.is_alive():
-            self.receiver_thread.join(timeout=10)
+            # a pool bound to a multicast object is unbound by the worker thread once the
+            # senders unmapped it (bounded wait): the process must not exit before that
+            self.receiver_thread.join(timeout=10 if self._mc is None else self.config.connect_timeout_s + 30)
         try:
             self._req.close(0)
         except Exception:
@@ -669,15 +671,18 @@ class WeightReceiver:
 
     def _compile_pull(self, names: set | None):
         """The pull program of every expected sender's entries (restricted to ``names``)."""
-        from ..core.plan import Tables, storage_ranges, validate_tables
+        from ..core.plan import storage_ranges, validate_tables
         from ..ops.executor import HostProgram, LaunchConfig, TransferProgram
+        from .sender import _interleave
         parts = []
         for s in self.expected:
             mine = self._names[s] if names is None else [n for n in self._names[s] if n in names]
             ops = [o for o in plan_pair(self._pull_src[s], self._rphys_abs, names=mine)
                    if o.kind not in ("quant", "squant")]
             parts.append(lower_ops(ops, self._pull_imports[s].base, lambda a: 0, item_bytes=self.config.item_bytes))
-        tables = Tables.concat(parts)
+        # round-robin over the senders, so the CTAs running at any moment load from every
+        # sender at once (one sender after the other would leave all but one egress idle)
+        tables = _interleave(parts)
         if self.config.validate_plan:
             validate_tables(tables, self._pull_ranges, storage_ranges(self.state_dict.values()))
         if self.device.type == "cpu":
@@ -734,9 +739,9 @@ class WeightReceiver:
             if gr not in g["replicas"]:
                 continue
             m = McMember(g["id"], g["size"], self.device.index)
+            self._mc = (m, g)                 # tracked from here on: teardown undoes every stage
             m.join(g["addr"])
             m.add_device()
-            self._mc = (m, g)
             everyone = g["replicas"] + g["senders"]
             sess.set(f"nvls/{g['id']}/added/{gr}", "1")
             sess.wait_checked([f"nvls/{g['id']}/added/{x}" for x in everyone], self.config.connect_timeout_s,

@@ -161,6 +161,8 @@ class WeightSender:
         self._published_key = None                   # pull: the tensors whose memory was last exported
         self.uncovered: dict[int, list[str]] = {}    # rank 0, after connect: worker -> entries no sender fills
         self._xchg = None                            # split fp8 blocks shared with other senders
+        self._writes_nothing = False                 # pull direction: senders store nothing
+        self.direction = "push"                      # resolved at connect (session_direction)
         self._piece_pos = np.zeros(0, dtype=np.int64)
         self._arm_sock = None                        # rank 0, arm="direct": ROUTER to every receiver worker
         self._arm_idents: dict[int, bytes] = {}
@@ -224,14 +226,24 @@ class WeightSender:
         self.overlaps = {r: WeightData.compute_overlap(restrict(sender_metadata, names), rmetas[r])
                          for r, names in self.targets.items()}
         self._xchg = self._exchange_plan(metas, assignment, rmetas)
+        self.direction = session_direction(cfg, rmetas.values())
+        # pulling, this sender never writes into its workers' memory, so a sync need not wait
+        # for them to be idle (each loads when it is)
+        self._writes_nothing = self.direction == "pull"
         # receivers publish their memory tables once they joined the store
         for r in self.targets:
             try:
                 self._rinfo[r] = sess.get_json(f"recv/{r}", cfg.connect_timeout_s)
             except (SessionTimeout, PeerError) as e:
                 raise TransferError(str(e)) from None
+        if any(i.get("late") for i in self._rinfo.values()):
+            self._writes_nothing = False           # late binders publish their memory with ready
         if cfg.mode == "nvls":
-            self._setup_multicast(sess, info, assignment)
+            try:
+                self._setup_multicast(sess, info, assignment)
+            except BaseException:
+                self._teardown_multicast()       # nothing of this process stays bound to an object
+                raise
         if cfg.mode in WIRE_MODES:
             # the group needs every rank: join it only once every receiver verified the plan
             everyone = sorted(rmetas)
@@ -338,7 +350,7 @@ class WeightSender:
         rmeta_objs = {r: WeightData(m) for r, m in receivers.items()}
         plan = assign_sources(smeta_objs, rmeta_objs, cfg.load_balance)
         sess.set_json("senders/meta", metas)
-        sess.set("direction", cfg.direction if cfg.mode == "gpu_direct" else "push")
+        sess.set("direction", session_direction(cfg, rmeta_objs.values()))
         sess.set("wire_chunk", str(int(cfg.wire_chunk_bytes)))      # receivers cut their wires alike
         sess.set_json("assign", {str(s): {str(r): n for r, n in rs.items()} for s, rs in plan.items()})
         covered: dict[tuple[int, str], int] = {}
@@ -462,7 +474,11 @@ class WeightSender:
                 members = [allinfo[r]["device"] for r in reps] + [self._sender_devices[s] for s in senders]
                 devs = set(members)
                 if not senders or not nvls_supported(dev0) or len(devs) != len(members):
-                    continue        # unicast: no senders, no NVLS, or two members on one GPU
+                    logger.warning("replica group %s goes unicast: %s", reps,
+                                   "no sender writes the same entries to all of it" if not senders else
+                                   "two members share a GPU" if len(devs) != len(members) else
+                                   "the GPU reports no NVLink multicast")
+                    continue
                 size = int(allinfo[reps[0]]["pool"]["size"])
                 m = McMember(gid, size, dev0)
                 m.create(num_devices=len(devs))
@@ -477,6 +493,7 @@ class WeightSender:
                 continue
             creator = next((m for m in self._mc_created if m.group == g["id"]), None)
             m = creator if creator is not None else McMember(g["id"], g["size"], dev)
+            self._mc[g["id"]] = (m, g)           # tracked from here on: teardown undoes every stage
             if creator is None:
                 m.join(g["addr"])
             m.add_device()
@@ -489,20 +506,30 @@ class WeightSender:
             sess.wait_checked([f"nvls/{g['id']}/bound/{x}" for x in members], cfg.connect_timeout_s,
                               "multicast members to bind memory")
             m.map()
-            self._mc[g["id"]] = (m, g)
         logger.info("sender %d: %d multicast group(s)", self.rank, len(self._mc))
 
     def _teardown_multicast(self) -> None:
+        """Unmap, tell the group, and unbind only once every sender of the group unmapped
+        (no multimem store can then reach this device's backing).  Also undoes a set-up that
+        stopped half way: members that never mapped still report ``unmapped``."""
         mc = self._mc
         sess = self.session
         for m, g in mc.values():
-            m.teardown_mapping()
-            if sess is not None:
-                sess.set(f"nvls/{g['id']}/unmapped/{self.rank}", "1")
+            try:
+                m.teardown_mapping()
+            finally:
+                if sess is not None:
+                    try:
+                        sess.set(f"nvls/{g['id']}/unmapped/{self.rank}", "1")
+                    except Exception:
+                        logger.exception("sender %d: could not report the multicast unmap", self.rank)
         for m, g in mc.values():
             try:
                 if sess is not None:
                     sess.wait([f"nvls/{g['id']}/unmapped/{x}" for x in g["senders"]], self.config.connect_timeout_s)
+            except Exception:
+                logger.exception("sender %d: multicast group %d: waiting for the other senders to unmap",
+                                 self.rank, g["id"])
             finally:
                 m.teardown_binding()
         for m in self._mc_created:
@@ -578,7 +605,7 @@ class WeightSender:
         src_base = ptrs.__getitem__
         sjson = sphys.to_json()
         skey = _digest(sjson)
-        pull = cfg.mode == "gpu_direct" and cfg.direction == "pull"
+        pull = self.direction == "pull"
         if not pull:
             self._bind_version += 1
         elif self._published_key != self._key(state_dict):   # new tensors: export them again
@@ -602,9 +629,11 @@ class WeightSender:
                 info, imp = self._rinfo[r], self._imports[r]
                 if uni_ops:          # casts, quantised blocks, unaligned copies: one store per replica
                     parts.append(lower_ops(uni_ops, src_base, imp.base, item_bytes=cfg.item_bytes, receiver=r))
-                falloc, foff, _w = info["flags"]
-                flags.append(imp.base(falloc) + foff + 8 * self.rank)
                 dst_ranges += [(imp.base(i), imp.base(i) + int(a["size"])) for i, a in enumerate(info["allocs"])]
+            # the replicas' pools are laid out alike, flag words included: one multicast release
+            # store (bit 0 marks the address as multicast) reaches every replica's word
+            _falloc, foff, _w = self._rinfo[rep]["flags"]
+            flags.append((m.va + foff + 8 * self.rank) | 1)
             covered |= set(reps)
         for r, names in sorted(self.targets.items()):
             if r in covered:
@@ -733,7 +762,7 @@ class WeightSender:
         key = (self._key(state_dict), subset)
         if key == self._program_key:
             return
-        if self.config.direction == "pull":     # the receivers pull from the last published memory:
+        if self.direction == "pull":            # the receivers pull from the last published memory:
             # programs of other tensors are dropped (a switch of tensors publishes again)
             self._progs = {k: v for k, v in self._progs.items() if k[0] == key[0]}
         hit = self._progs.pop(key, None)
@@ -806,7 +835,8 @@ class WeightSender:
                     self._arm_sock.send_multipart([ident, payload], zmq.NOBLOCK)
                 except zmq.ZMQError as e:
                     self._arm_error = f"arming the rollout side failed: receiver {r} unreachable ({e})"
-                    self.session.set_error([f"ready/{x}/{epoch}" for x in receivers], self._arm_error)
+                    self.session.set_error([f"{k}/{x}/{epoch}" for x in receivers for k in ("ready", "pulled")],
+                                           self._arm_error)
                     break
             return None
         urls, timeout = list(self.receiver_urls), self.config.http_timeout_s
@@ -822,7 +852,8 @@ class WeightSender:
                             raise TransferError(f"receiver {url} refused the sync: {resp.json()}")
             except Exception as e:
                 self._arm_error = f"arming the rollout side failed: {type(e).__name__}: {e}"
-                self.session.set_error([f"ready/{r}/{epoch}" for r in receivers], self._arm_error)
+                self.session.set_error([f"{k}/{r}/{epoch}" for r in receivers for k in ("ready", "pulled")],
+                                       self._arm_error)
 
         th = threading.Thread(target=run, name="wbridge-arm", daemon=True)
         th.start()
@@ -932,6 +963,11 @@ class WeightSender:
         out["bytes_written"] = hist[-1].bytes_written
         return out
 
+    def _overlap_bytes(self, subset: frozenset | None) -> int:
+        """Bytes of this sender's entries its targets receive (restricted to ``subset``)."""
+        return sum(end - start for ov in self.overlaps.values() for start, end, name, _sh, _dt in ov.iter_with_intv()
+                   if subset is None or name in subset)
+
     def _subset(self, names) -> frozenset | None:
         return None if names is None else frozenset(names)
 
@@ -970,6 +1006,13 @@ class WeightSender:
             if epoch > 16:
                 sess.delete(f"ver/{epoch - 16}")
         arm = self._arm(epoch) if self.rank == 0 else None
+        if self._writes_nothing:                  # nothing to wait for: publish done right away
+            if arm is not None:
+                arm.join()
+            if self.rank == 0 and self._arm_error is not None:
+                self._fail_epoch(epoch, self._arm_error)
+                raise TransferError(self._arm_error)
+            return []
         t1 = time.perf_counter()
         try:
             with nvtx_range("wbridge.send/ready"):
@@ -1064,13 +1107,15 @@ class WeightSender:
             # pull: the parameters must be final
         if prog is not None:
             st.bytes_read, st.bytes_written = prog.bytes_read, prog.bytes_written
+        elif self.direction == "pull":     # the workers move this sender's bytes
+            st.bytes_read = st.bytes_written = self._overlap_bytes(subset)
         dg = self._publish_subset(subset) if self.rank == 0 else (_digest(sorted(subset))[:16] if subset else "")
         done = f"{st.status}:{self._bind_version}:{int(pushed)}:{version}:{dg}"
         sess.multi_set([f"done/{self.rank}/{r}/{epoch}" for r in self.targets], [done] * len(self.targets))
         if st.status:
             prog.clear_status()
             raise TransferError(f"transfer kernel reported status {st.status:#x} at epoch {epoch}")
-        if cfg.mode == "gpu_direct" and cfg.direction == "pull":
+        if self.direction == "pull":
             # parameters stay untouched until every target has pulled its share
             try:
                 vals = sess.wait_checked([f"pulled/{r}/{epoch}" for r in self.targets], cfg.sync_timeout_s,
@@ -1112,8 +1157,23 @@ def _phys_extents(pb: PhysBinding) -> list[tuple[int, int]]:
 
 
 def _check_flag(addr: int, ranges) -> None:
+    addr &= ~1                          # bit 0 marks a multicast address
     if not any(lo <= addr and addr + 8 <= hi for lo, hi in ranges):
         raise PlanBoundsError(f"flag word {addr:#x} outside the receiver's registered memory")
+
+
+def session_direction(cfg: TransferConfig, receiver_metas) -> str:
+    """Who runs the copy program of a ``gpu_direct`` session: ``pull`` (each receiver loads its
+    copies from the senders' exported memory; the fastest way over NVLink measured here) when
+    asked for and no receiver holds block-quantised (fp8) entries; otherwise ``push`` (each sender
+    stores, fusing the quantisation, which halves the bytes on the link).  A session with fp8
+    entries pushes everything: pulling the plain copies would only start once the quantised
+    blocks are stored, after the push kernel."""
+    if cfg.mode != "gpu_direct" or cfg.direction != "pull":
+        return "push"
+    if any(m.quant(n) for m in receiver_metas for n in m.names()):
+        return "push"
+    return "pull"
 
 
 def wire_group(mode: str, sess: Session, rank: int, world: int, timeout_s: float, address: str):
@@ -1137,14 +1197,22 @@ def gloo_group(sess: Session, rank: int, world: int, timeout_s: float, address: 
     return dist.ProcessGroupGloo(dist.PrefixStore("gloo", sess.store), rank, world, opts)
 
 
+def _round_robin(lens: list[int]) -> np.ndarray:
+    """Order taking one row from each of the concatenated parts (of ``lens`` rows) in turn."""
+    k = len(lens)
+    keys = np.concatenate([np.arange(n, dtype=np.int64) * k + i for i, n in enumerate(lens)]) if lens else \
+        np.zeros(0, np.int64)
+    return np.argsort(keys, kind="stable")
+
+
 def _interleave(parts: list[Tables]) -> Tables:
-    """Concatenate per-receiver tables, interleaving items round-robin across receivers so
-    CTAs running at the same time store to different peers."""
+    """Concatenate per-peer tables, dealing the copy items and the quantised blocks round-robin
+    across the peers, so the CTAs running at any moment reach every peer: senders whose work
+    for peer 0 comes first would otherwise all meet at peer 0's link, then at peer 1's, ...
+    (split-block pieces keep their order: their positions index the exchanged amax)."""
     if len(parts) <= 1:
         return Tables.concat(parts)
     merged = Tables.concat(parts)
-    lens = [len(p.items) for p in parts]
-    keys = np.concatenate([np.arange(n) * len(parts) + i for i, n in enumerate(lens)]) if lens else np.zeros(0)
-    order = np.argsort(keys, kind="stable")
-    merged.items = merged.items[order]
+    merged.items = merged.items[_round_robin([len(p.items) for p in parts])]
+    merged.qwork = merged.qwork[_round_robin([len(p.qwork) for p in parts])]
     return merged

@@ -48,8 +48,9 @@ class TransferConfig:
     load_balance: bool = True             # spread replicated shards over senders
     validate_plan: bool = True            # check every work row against registered memory before upload
     require_full_coverage: bool = False   # connect fails (instead of warning) if a rollout entry has no sender
-    direction: str = "push"               # gpu_direct: push (senders store) | pull (receivers load copies)
-    link_gbs: float = 770.0               # per-GPU link bandwidth for the stats' fraction (measured peer copy)
+    direction: str = "pull"               # gpu_direct: pull (receivers load the copies; fp8 blocks are still
+                                          # quantised and pushed by the senders) | push (senders store all)
+    link_gbs: float = 788.0               # per-GPU link bandwidth for the stats' fraction (measured peer peak)
     arm: str = "direct"                   # how each sync is armed: direct (one ZMQ message from sender rank 0
                                           # to every receiver worker) | http (POST /wbridge/receive per sync)
     plan_cache_dir: str = ""              # senders keep their planned ops here across restarts ("": memory only)
