@@ -59,14 +59,16 @@ def parse(argv=None):
     p.add_argument("--item-bytes", type=int, default=None)
     p.add_argument("--no-verify", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--direction", default="push", choices=["push", "pull"],
-                   help="gpu_direct: senders store (push) or receivers load the copies (pull)")
+    p.add_argument("--direction", default="pull", choices=["push", "pull"],
+                   help="gpu_direct: receivers load the copies (pull, the default) or senders store them (push)")
     p.add_argument("--arm", default="direct", choices=["direct", "http"],
                    help="how each sync is armed: one ZMQ message per worker, or POST /wbridge/receive")
     p.add_argument("--transfer", default="gpu_direct", choices=["gpu_direct", "nvls"],
                    help="nvls: rollout pools in VMM memory, multicast stores to replica groups")
     p.add_argument("--no-pool", action="store_true",
                    help="allocate every rollout parameter separately (one IPC handle each)")
+    p.add_argument("--no-torch-p2p", action="store_true",
+                   help="skip the same-box comparison with the reference's algorithm (torch copies + NCCL P2P)")
     p.add_argument("--stall-dump-s", type=float, default=150.0,
                    help="dump every thread's stack to stderr if a process is still running after this long")
     return p.parse_args(argv)
@@ -85,7 +87,10 @@ def reference_arm(args):
     sys.path.insert(0, ref)
     try:
         import torch
-        from wbridge import WeightData  # the reference package
+        import wbridge  # the reference package
+        if not os.path.abspath(wbridge.__file__).startswith(os.path.abspath(ref)):
+            raise ImportError(f"'wbridge' resolved to {wbridge.__file__}, not the reference install in {ref}")
+        from wbridge import WeightData
         # the exact call GPUDirectSender.send makes (wbridge/backend/direct_sender.py:192):
         #   chunks = self.metadata(state_dict)[self.overlaps]
         meta = WeightData({"w": {"shard": [(0, 4, 4), (0, 8, 8)], "dtype": "bfloat16"}})
@@ -181,10 +186,22 @@ def _roofline(value_gbs: float, links: float, colocated: bool, bytes_read: float
         achieved = (bytes_read + payload) / (ms / 1e3) / 1e9
         return {"bound": "hbm copy (read + write)", "peak_gbs": peak, "achieved_gbs": round(achieved, 1),
                 "fraction_of_measured": round(achieved / peak, 3)}
-    peak = 770.0
+    peak, source = _peer_peak()
     per_link = value_gbs / max(links, 1.0)
-    return {"bound": "nvlink, per sending link", "peak_gbs": peak, "achieved_gbs": round(per_link, 1),
-            "fraction_of_measured": round(per_link / peak, 3)}
+    return {"bound": "nvlink, per sending link", "peak_gbs": peak, "peak_source": source,
+            "achieved_gbs": round(per_link, 1), "fraction_of_measured": round(per_link / peak, 3)}
+
+
+def _peer_peak() -> tuple[float, str]:
+    """GPU -> GPU peak: the largest of copy engine, push kernel and pull kernel measured on two
+    B200s of this pool (profiles/nvlink_peer_peak.json, written by
+    ``python -m weightbridge_b200.ops.microbench --case peer-peak``)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "nvlink_peer_peak.json")) as f:
+            d = json.load(f)
+        return float(d["best_gbs"]), "measured: profiles/nvlink_peer_peak.json (max of copy engine, push, pull)"
+    except (OSError, KeyError, ValueError):
+        return 770.0, "fallback: earlier peer-copy measurement (no profiles/nvlink_peer_peak.json)"
 
 
 def _free_port() -> int:
@@ -313,164 +330,251 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     dist.all_gather_object(infos, engine_info)
     engines = {e[0]: e for e in infos if e is not None}
     urls = [engines[k][1] for k in sorted(engines)]
-    if role.kind == "rollout":
-        recv = WeightReceiver(engines[role.engine][2], role.worker, meta, state_dict=views, device=dev, config=cfg)
-    dist.barrier()
-    phase("engines up")
-    if role.kind == "trainer":
-        sender = WeightSender(args.transfer, urls, group=tgroup, config=cfg)
-        sender.connect(meta)
-    dist.barrier()
-    phase("connected")
-    setup_s = time.time() - t_setup
-
-    def public_sync():
-        if sender is not None:
-            sender.send(views)
-        else:
-            ok = recv.request_update(timeout=cfg.sync_timeout_s)
-            if not ok:
-                raise RuntimeError("request_update returned False")
-
-    for _ in range(args.warmup):
-        public_sync()
-    torch.cuda.synchronize()
-    phase("warm-up syncs done")
-
-    # phase A: device-timed transfer launches
-    stream = torch.cuda.Stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clk = ClockSampler() if idx == 0 else None
-    dist.barrier()
-    torch.cuda.synchronize()
-    if clk:
-        clk.__enter__()
-    dist.barrier()
-    e0.record(stream)
-    pulls = recv is not None and recv.pull_program is not None and len(recv.pull_program.tables) > 0
-    if sender is not None:
-        for _ in range(args.steps):
-            sender.launch(views, stream)         # the pushed part (everything, unless pulling)
-    elif pulls:
-        for _ in range(args.steps):
-            recv.launch(stream)                  # pull direction: receivers load the copies
-    e1.record(stream)
-    torch.cuda.synchronize()
-    dist.barrier()
-    if clk:
-        clk.__exit__(None, None, None)
-    my_ms = e0.elapsed_time(e1) / args.steps if (sender is not None or pulls) else 0.0
-
-    # phase B: public API end to end
-    e2e_ms = 0.0
-    if not args.no_e2e:
+    # from here until the teardown every path ends in recv.stop() / sender.disconnect(): a
+    # process must not exit with memory still bound to a multicast object (mode nvls)
+    clean = False
+    try:
+        if role.kind == "rollout":
+            recv = WeightReceiver(engines[role.engine][2], role.worker, meta, state_dict=views, device=dev, config=cfg)
         dist.barrier()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
+        phase("engines up")
+        if role.kind == "trainer":
+            sender = WeightSender(args.transfer, urls, group=tgroup, config=cfg)
+            sender.connect(meta)
+        dist.barrier()
+        phase("connected")
+        setup_s = time.time() - t_setup
+
+        def public_sync():
+            if sender is not None:
+                sender.send(views)
+            else:
+                ok = recv.request_update(timeout=cfg.sync_timeout_s)
+                if not ok:
+                    raise RuntimeError("request_update returned False")
+
+        for _ in range(args.warmup):
             public_sync()
         torch.cuda.synchronize()
-        e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+        phase("warm-up syncs done")
+
+        # phase A: device-timed transfer launches
+        stream = torch.cuda.Stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clk = ClockSampler() if idx == 0 else None
         dist.barrier()
+        torch.cuda.synchronize()
+        if clk:
+            clk.__enter__()
+        dist.barrier()
+        e0.record(stream)
+        pulls = recv is not None and recv.pull_program is not None and len(recv.pull_program.tables) > 0
+        if sender is not None:
+            for _ in range(args.steps):
+                sender.launch(views, stream)         # the pushed part (everything, unless pulling)
+        elif pulls:
+            for _ in range(args.steps):
+                recv.launch(stream)                  # pull direction: receivers load the copies
+        e1.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        if clk:
+            clk.__exit__(None, None, None)
+        my_ms = e0.elapsed_time(e1) / args.steps if (sender is not None or pulls) else 0.0
 
-    phase("timed phases done")
-    ok = 1
-    if role.kind == "rollout" and not args.no_verify:
-        del_views = None
-        expected = lay.allocate(device=dev, dtype=torch.bfloat16, fill=True, pool=not args.no_pool)
-        for n in params:
-            a, b = params[n], expected[n]
-            if a.dtype == torch.float8_e4m3fn:
-                a, b = a.view(torch.uint8), b.view(torch.uint8)
-            if not torch.equal(a, b):
-                ok = 0
-                print(f"[rank {idx}] mismatch in {n}", flush=True)
-                break
-        del expected
-    payload = sender.program.bytes_written if (sender is not None and sender.program is not None) else 0
-    if recv is not None and recv.pull_program is not None:
-        payload += recv.pull_program.bytes_written
-    read = sender.program.bytes_read if (sender is not None and sender.program is not None) else 0
-    active = 1 if (sender is not None and sender.program is not None and len(sender.program.tables)) else 0
-    active += 1 if (recv is not None and recv.pull_program is not None and len(recv.pull_program.tables)) else 0
-    # kernels per timed launch: the transfer kernel, plus the split-block quantiser when there are pieces
-    kernels = active + (1 if (sender is not None and sender.program is not None
-                              and getattr(sender.program, "n_pieces", 0)) else 0)
-    pushed = 1 if (sender is not None and sender.program is not None and len(sender.program.tables)) else 0
-    pulled = 1 if (recv is not None and recv.pull_program is not None and len(recv.pull_program.tables)) else 0
-    h2d = 8 * pushed                                  # the epoch word, from pinned memory
-    d2h = 4 * (pushed + pulled) + (int(recv.flags.nbytes) if recv is not None and cfg.verify_flags else 0)
-    npieces = getattr(sender.program, "n_pieces", 0) if (sender is not None and sender.program is not None) else 0
-    h2d += 4 * npieces                                # split blocks: the exchanged amax of every piece
-    d2h += 4 * npieces                                # ... and each piece's own amax, read back first
-    items = len(sender.program.tables.items) if (sender is not None and sender.program is not None) else 0
-    grid = sender.program.grid() if (sender is not None and sender.program is not None) else 0
-    kmode = sender.program.config.mode if (sender is not None and sender.program is not None) else -1
-    hist = sender.history[-args.steps:] if (sender is not None and not args.no_e2e) else []
-    avg = lambda f: sum(getattr(h, f) for h in hist) / len(hist) if hist else 0.0
-    stats = torch.tensor([my_ms, e2e_ms, payload, read, ok, h2d, d2h, active, items, grid, setup_s, kmode,
-                          avg("wait_ready_ms"), avg("device_ms"), avg("host_ms"), avg("exchange_ms"), kernels],
-                         dtype=torch.float64)
-    gathered = [torch.zeros_like(stats) for _ in range(nprocs)]
-    dist.all_gather(gathered, stats)
-    G = torch.stack(gathered)
+        # phase B: public API end to end
+        e2e_ms = 0.0
+        if not args.no_e2e:
+            dist.barrier()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                public_sync()
+            torch.cuda.synchronize()
+            e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+            dist.barrier()
 
-    if idx == 0:
-        ms = float(G[:, 0].max())
-        e2e = float(G[:, 1].max())
-        payload_total = float(G[:, 2].sum())
-        ngpu = args.gpus
-        lat = ms / 1e3
-        value = payload_total / lat / 1e9
-        res = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ngpu, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: random-init N(0,0.02) weights of the architecture (hashed per element)",
-            "config": {"model": model, "config": args.config, "layout": desc, "global_batch": None, "seq_len": None,
-                       "parallelism": desc, "payload_bytes_per_sync": int(payload_total),
-                       "bytes_read_per_sync": int(G[:, 3].sum()),
-                       "l2": "inputs larger than L2 (GBs per sync); no flush needed",
-                       "kernel_mode": int(G[:, 11].max()), "piece_bytes": cfg.piece_bytes,
-                       "item_bytes": cfg.item_bytes, "work_items_max": int(G[:, 8].max()),
-                       "grid": int(G[:, 9].max()), "processes": nprocs,
-                       "rollout_params": "separate allocations" if args.no_pool else "one pooled allocation per rank",
-                       "transfer": args.transfer, "direction": args.direction, "arm": args.arm},
-            "latency_s": round(lat, 6),
-            "roofline": _roofline(value, float(G[:, 7].sum()), colocated=len({r.device for r in roles}) < len(roles),
-                                  bytes_read=float(G[:, 3].sum()), payload=payload_total, ms=ms),
-            "gbs_per_gpu": round(value / ngpu, 2),
-            "gbs_per_sender": round(value / max(1.0, float(G[:, 7].sum())), 2),
-            "e2e": None if args.no_e2e else {
-                "value": round(payload_total / (e2e / 1e3) / 1e9, 2), "unit": "GB/s",
-                "ms_per_step": round(e2e, 4), "latency_s": round(e2e / 1e3, 6),
-                "h2d_bytes_per_step": int(G[:, 5].sum()), "d2h_bytes_per_step": int(G[:, 6].sum()),
-                "path": (f"WeightSender.send + WeightReceiver.request_update ({args.arm} arm, store handshake, "
-                         f"{'IPC peer loads' if args.direction == 'pull' else 'IPC peer stores'})"),
-                "sender_breakdown_ms": {"wait_ready": round(float(G[:, 12].max()), 3),
-                                        "transfer_kernel": round(float(G[:, 13].max()), 3),
-                                        "send_total": round(float(G[:, 14].max()), 3),
-                                        "split_block_exchange": round(float(G[:, 15].max()), 3)}},
-            "gpu_launches": int(args.steps * G[:, 16].sum()),
-            "clocks": clk.summary() if clk else None,
-            "verified": bool(G[:, 4].min() == 1) if not args.no_verify else None,
-            "setup_s": round(float(G[:, 10].max()), 1),
-            "impl": "wbridge",
-        }
-        print(json.dumps(res), flush=True)
+        phase("timed phases done")
+        p2p = None
+        if not args.no_torch_p2p:
+            p2p = torch_p2p_phase(args, roles, idx, lay, meta, views, params, dev)
+            phase("reference-algorithm phase done")
+        ok = 1
+        if role.kind == "rollout" and not args.no_verify:
+            del_views = None
+            expected = lay.allocate(device=dev, dtype=torch.bfloat16, fill=True, pool=not args.no_pool)
+            for n in params:
+                a, b = params[n], expected[n]
+                if a.dtype == torch.float8_e4m3fn:
+                    a, b = a.view(torch.uint8), b.view(torch.uint8)
+                if not torch.equal(a, b):
+                    ok = 0
+                    print(f"[rank {idx}] mismatch in {n}", flush=True)
+                    break
+            del expected
+        sender_direction = sender.direction if sender is not None else None
+        sprog = sender.program if (sender is not None and sender.program is not None) else None
+        rprog = recv.pull_program if (recv is not None and recv.pull_program is not None
+                                      and len(recv.pull_program.tables)) else None
+        payload = (sprog.bytes_written if sprog else 0) + (rprog.bytes_written if rprog else 0)
+        read = (sprog.bytes_read if sprog else 0) + (rprog.bytes_read if rprog else 0)
+        active = 1 if (sender is not None and sender.program is not None and len(sender.program.tables)) else 0
+        active += 1 if (recv is not None and recv.pull_program is not None and len(recv.pull_program.tables)) else 0
+        # kernels per timed launch: the transfer kernel, plus the split-block quantiser when there are pieces
+        kernels = active + (1 if (sender is not None and sender.program is not None
+                                  and getattr(sender.program, "n_pieces", 0)) else 0)
+        pushed = 1 if (sender is not None and sender.program is not None and len(sender.program.tables)) else 0
+        pulled = 1 if (recv is not None and recv.pull_program is not None and len(recv.pull_program.tables)) else 0
+        h2d = 8 * pushed                                  # the epoch word, from pinned memory
+        # a worker reads the flag words back when some sender pushed (every copy in push; the
+        # fp8 blocks in pull)
+        any_push = args.direction == "push" or args.transfer != "gpu_direct" or any(meta.quant(n) for n in meta.names())
+        d2h = 4 * (pushed + pulled) + (int(recv.flags.nbytes) if recv is not None and cfg.verify_flags and any_push
+                                       else 0)
+        npieces = getattr(sender.program, "n_pieces", 0) if (sender is not None and sender.program is not None) else 0
+        h2d += 4 * npieces                                # split blocks: the exchanged amax of every piece
+        d2h += 4 * npieces                                # ... and each piece's own amax, read back first
+        progs = [p for p in (sprog, rprog) if p is not None and len(p.tables)]
+        items = max((len(p.tables.items) for p in progs), default=0)
+        grid = max((p.grid() for p in progs), default=0)
+        kmode = max((p.config.mode for p in progs), default=-1)
+        hist = sender.history[-args.steps:] if (sender is not None and not args.no_e2e) else []
+        avg = lambda f: sum(getattr(h, f) for h in hist) / len(hist) if hist else 0.0
+        p2p_ms, p2p_e2e, p2p_ok = (p2p or {}).get("ms", -1.0), (p2p or {}).get("e2e_ms", -1.0), (p2p or {}).get("ok", 1)
+        stats = torch.tensor([my_ms, e2e_ms, payload, read, ok, h2d, d2h, active, items, grid, setup_s, kmode,
+                              avg("wait_ready_ms"), avg("device_ms"), avg("host_ms"), avg("exchange_ms"), kernels,
+                              p2p_ms, p2p_e2e, p2p_ok, len(sender._mc) if sender is not None else 0],
+                             dtype=torch.float64)
+        gathered = [torch.zeros_like(stats) for _ in range(nprocs)]
+        dist.all_gather(gathered, stats)
+        G = torch.stack(gathered)
 
-    faulthandler.cancel_dump_traceback_later()
-    dist.barrier()
-    if recv is not None:
-        recv.stop()
-    if sender is not None:
-        sender.disconnect()
-    dist.barrier()
+        if idx == 0:
+            ms = float(G[:, 0].max())
+            e2e = float(G[:, 1].max())
+            payload_total = float(G[:, 2].sum())
+            ngpu = args.gpus
+            lat = ms / 1e3
+            value = payload_total / lat / 1e9
+            res = {
+                "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ngpu, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic: random-init N(0,0.02) weights of the architecture (hashed per element)",
+                "config": {"model": model, "config": args.config, "layout": desc, "global_batch": None, "seq_len": None,
+                           "parallelism": desc, "payload_bytes_per_sync": int(payload_total),
+                           "bytes_read_per_sync": int(G[:, 3].sum()),
+                           "l2": "inputs larger than L2 (GBs per sync); no flush needed",
+                           "kernel_mode": int(G[:, 11].max()), "piece_bytes": cfg.piece_bytes,
+                           "item_bytes": cfg.item_bytes, "work_items_max": int(G[:, 8].max()),
+                           "grid": int(G[:, 9].max()), "processes": nprocs,
+                           "rollout_params": "separate allocations" if args.no_pool else "one pooled allocation per rank",
+                           "transfer": args.transfer, "arm": args.arm,
+                           "direction": sender_direction if sender_direction else args.direction,
+                           "multicast_groups_per_sender_max": int(G[:, 20].max())},
+                "latency_s": round(lat, 6),
+                "roofline": _roofline(value, float(G[:, 7].sum()), colocated=len({r.device for r in roles}) < len(roles),
+                                      bytes_read=float(G[:, 3].sum()), payload=payload_total, ms=ms),
+                "gbs_per_gpu": round(value / ngpu, 2),
+                "gbs_per_sender": round(value / max(1.0, float(G[:, 7].sum())), 2),
+                "e2e": None if args.no_e2e else {
+                    "value": round(payload_total / (e2e / 1e3) / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(e2e, 4), "latency_s": round(e2e / 1e3, 6),
+                    "h2d_bytes_per_step": int(G[:, 5].sum()), "d2h_bytes_per_step": int(G[:, 6].sum()),
+                    "path": (f"WeightSender.send + WeightReceiver.request_update ({args.arm} arm, store handshake, "
+                             f"{'IPC peer loads' if args.direction == 'pull' else 'IPC peer stores'})"),
+                    "sender_breakdown_ms": {"wait_ready": round(float(G[:, 12].max()), 3),
+                                            "transfer_kernel": round(float(G[:, 13].max()), 3),
+                                            "send_total": round(float(G[:, 14].max()), 3),
+                                            "split_block_exchange": round(float(G[:, 15].max()), 3)}},
+                "vs_torch_p2p": _p2p_report(args, p2p, G, ms, e2e),
+                "gpu_launches": int(args.steps * G[:, 16].sum()),
+                "clocks": clk.summary() if clk else None,
+                "verified": bool(G[:, 4].min() == 1) if not args.no_verify else None,
+                "setup_s": round(float(G[:, 10].max()), 1),
+                "impl": "wbridge",
+            }
+            print(json.dumps(res), flush=True)
+
+        faulthandler.cancel_dump_traceback_later()
+        dist.barrier()
+        clean = True
+    finally:
+        if recv is not None:
+            recv.stop()
+        if sender is not None:
+            sender.disconnect()
+    if clean:
+        dist.barrier()
     if server is not None:
         server.should_exit = True
     if ctl is not None:
         ctl.close()
     dist.destroy_process_group()
+
+
+def torch_p2p_phase(args, roles, idx, lay, meta, views, params, dev) -> dict | None:
+    """The reference's data path (per-box torch copies into a wire buffer on the device, NCCL
+    isend / irecv, per-box unpack: ``baselines/torch_p2p.py``) on the same processes, layout,
+    weights, steps and warm-up as the library's phases, after them.  Every rank takes part (the
+    same collective steps in the same order); a layout with two ranks on one GPU has no NCCL
+    point-to-point path, which every rank sees alike and skips.  Returns this rank's device time
+    per sync (CUDA events on its stream), wall time per sync (host-driven syncs until the device
+    finished) and, on receivers, whether the weights are still bit-exact."""
+    import torch
+    import torch.distributed as dist
+    from weightbridge_b200.baselines.torch_p2p import build_plan, sync
+    from weightbridge_b200.core.binding import bind
+    if len({r.device for r in roles}) != len(roles):
+        return {"unavailable": "this layout puts two ranks on one GPU, which NCCL point-to-point does not support"}
+    nprocs = len(roles)
+    group = dist.new_group(list(range(nprocs)), backend="nccl")
+    try:
+        plan = build_plan(idx, nprocs, meta, roles[idx].kind == "trainer", dev)   # objects over gloo
+        binding = bind(meta, views)
+        for _ in range(args.warmup):
+            sync(plan, binding, group=group)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            sync(plan, binding, group=group)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            sync(plan, binding, group=group)
+        torch.cuda.synchronize()
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+        dist.barrier()
+        ok = 1
+        if roles[idx].kind == "rollout" and not args.no_verify:
+            exp = lay.allocate(device=dev, dtype=torch.bfloat16, fill=True)
+            u8 = lambda t: t.view(torch.uint8) if t.dtype == torch.float8_e4m3fn else t      # noqa: E731
+            ok = int(all(torch.equal(u8(params[n]), u8(exp[n])) for n in params))
+            del exp
+        plan.wires.clear()
+        return {"ms": ms, "e2e_ms": e2e_ms, "ok": ok}
+    finally:
+        torch.cuda.synchronize()
+        dist.destroy_process_group(group)
+
+
+def _p2p_report(args, p2p, G, ms, e2e) -> dict:
+    """The same-box comparison line: > 1 means this library's sync is that much faster."""
+    if args.no_torch_p2p:
+        return {"unavailable": "skipped (--no-torch-p2p)"}
+    if p2p is not None and "unavailable" in p2p:
+        return {"unavailable": p2p["unavailable"]}
+    p_ms, p_e2e = float(G[:, 17].max()), float(G[:, 18].max())
+    return {"ms_per_step": round(p_ms, 4), "e2e_ms_per_step": round(p_e2e, 4),
+            "ratio": round(p_ms / ms, 3), "e2e_ratio": round(p_e2e / e2e, 3) if e2e > 0 else None,
+            "verified": bool(G[:, 19].min() == 1) if not args.no_verify else None,
+            "path": "reference algorithm on the same processes: per-box torch copies into a device wire "
+                    "buffer, NCCL isend/irecv, per-box unpack (weightbridge_b200/baselines/torch_p2p.py)"}
 
 
 def torch_p2p_main(args):

@@ -53,7 +53,9 @@ def test_bench_scenario_is_consistent(config, n):
 
 
 def test_roofline_fractions():
-    rf = bench._roofline(1540.0, 2.0, colocated=False, bytes_read=7.7e9, payload=7.7e9, ms=5.0)
+    peak, source = bench._peer_peak()
+    assert source.startswith("measured") and 700 < peak < 900     # profiles/nvlink_peer_peak.json
+    rf = bench._roofline(2 * peak, 2.0, colocated=False, bytes_read=7.7e9, payload=7.7e9, ms=5.0)
     assert rf["bound"].startswith("nvlink") and rf["fraction_of_measured"] == 1.0
     hbm = bench._measured_peaks().get("hbm_gbs", 6650.0)
     rf = bench._roofline(0.0, 1.0, colocated=True, bytes_read=hbm * 1e9 / 2, payload=hbm * 1e9 / 2, ms=1000.0)

@@ -13,6 +13,8 @@ peer-push / peer-pull / peer-quant (two GPUs, one process, peer access enabled):
          runs on GPU 0 and stores into GPU 1 (push), or runs on GPU 1 and loads from GPU 0
          (pull; plain and bulk loads from a peer, no cluster multicast), or quantises on
          GPU 0 into GPU 1; bandwidth counts the bytes that cross NVLink.
+peer-peak: copy engine, push kernel and pull kernel GPU 0 -> GPU 1, best of --iters each;
+         the largest is the measured peer peak (--out writes it as JSON).
 Reports device time per launch (CUDA events, after warm-up) and achieved bandwidth against
 the measured copy peak in MEASURED_PEAKS.json when present.
 """
@@ -35,6 +37,19 @@ def _peak_gbs() -> float | None:
         return float(json.load(open(p))["hbm_gbs"])
     except (OSError, KeyError, ValueError):
         return None
+
+
+PEER_PEAK_FILE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "..", "profiles",
+                              "nvlink_peer_peak.json")
+FALLBACK_PEER_GBS = 770.0     # an earlier peer-copy measurement on B200s, used when no file exists
+
+
+def _peer_peak_gbs() -> float:
+    """The measured GPU -> GPU peak (largest of copy engine, push and pull kernels)."""
+    try:
+        return float(json.load(open(PEER_PEAK_FILE))["best_gbs"])
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_PEER_GBS
 
 
 def build(case: str, gbytes: float, dev, item_bytes: int):
@@ -106,10 +121,68 @@ def build(case: str, gbytes: float, dev, item_bytes: int):
     return lower_ops(ops, lambda x: 0, lambda x: 0, item_bytes=item_bytes), keep, traffic
 
 
+def _time_ms(fn, iters: int, warmup: int, stream=None) -> float:
+    """Best single-launch device time of ``fn`` over ``iters`` launches (CUDA events on the
+    launching stream, after ``warmup`` launches)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(iters):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    return best
+
+
+def peer_peak(gbytes: float, iters: int, warmup: int, item_bytes: int) -> dict:
+    """GPU 0 -> GPU 1 bandwidth of the three ways bytes can cross NVLink here: the copy engine
+    (a cross-device tensor copy: cudaMemcpyAsync between peers), this library's kernel storing
+    into the peer (push, TMA bulk mode), and the kernel on GPU 1 loading from GPU 0 (pull).
+    Best launch of ``iters`` each, CUDA events, clocks sampled during the timed region.  The
+    largest figure is the peer-bandwidth denominator of the benchmark's roofline."""
+    from ..utils.timing import ClockSampler
+    from ._ext import ext
+    if torch.cuda.device_count() < 2:
+        raise SystemExit("peer-peak needs two GPUs")
+    d0, d1 = torch.device("cuda", 0), torch.device("cuda", 1)
+    for a_, b_ in ((0, 1), (1, 0)):
+        with torch.cuda.device(a_):
+            ext().enable_peer_access(b_)
+    n = int(gbytes * (1 << 30)) // 2
+    a = torch.randn(n, device=d0, dtype=torch.bfloat16)
+    b = torch.empty(n, device=d1, dtype=torch.bfloat16)
+    ops = [Op("copy", "x", (-1, a.data_ptr()), (-1, b.data_ptr()), [n], [1], [1], a.dtype, a.dtype)]
+    tables = lower_ops(ops, lambda x: 0, lambda x: 0, item_bytes=item_bytes)
+    out = {"bytes": a.nbytes, "iters": iters, "warmup": warmup}
+    with ClockSampler() as clk:
+        with torch.cuda.device(d0):
+            s0 = torch.cuda.current_stream(d0)
+            out["copy_engine_ms"] = _time_ms(lambda: b.copy_(a, non_blocking=True), iters, warmup, s0)
+            push = TransferProgram(tables, d0, [], LaunchConfig(mode=1))
+            out["push_kernel_ms"] = _time_ms(lambda: push.launch(0, s0, signal=False), iters, warmup, s0)
+            assert push.read_status() == 0
+        with torch.cuda.device(d1):
+            s1 = torch.cuda.current_stream(d1)
+            pull = TransferProgram(tables, d1, [], LaunchConfig(mode=1))
+            out["pull_kernel_ms"] = _time_ms(lambda: pull.launch(0, s1, signal=False), iters, warmup, s1)
+            assert pull.read_status() == 0
+    assert torch.equal(a.to(d1), b)
+    for k in ("copy_engine", "push_kernel", "pull_kernel"):
+        out[k + "_gbs"] = round(a.nbytes / (out[k + "_ms"] / 1e3) / 1e9, 1)
+    out["best_gbs"] = max(out[k + "_gbs"] for k in ("copy_engine", "push_kernel", "pull_kernel"))
+    out["clocks"] = clk.summary()
+    out["device"] = torch.cuda.get_device_name(d0)
+    return out
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--case", default="copy",
-                   choices=["copy", "strided", "quant", "split", "peer-push", "peer-pull", "peer-quant"])
+                   choices=["copy", "strided", "quant", "split", "peer-push", "peer-pull", "peer-quant", "peer-peak"])
     p.add_argument("--gbytes", type=float, default=1.0)
     p.add_argument("--mode", type=int, default=-1)
     p.add_argument("--piece", type=int, default=16384)
@@ -117,7 +190,15 @@ def main(argv=None):
     p.add_argument("--item-bytes", type=int, default=1 << 19)
     p.add_argument("--iters", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--out", default=None, help="peer-peak: also write the JSON result to this file")
     a = p.parse_args(argv)
+    if a.case == "peer-peak":
+        res = peer_peak(a.gbytes, a.iters, a.warmup, a.item_bytes)
+        print(json.dumps(res))
+        if a.out:
+            with open(a.out, "w") as f:
+                json.dump(res, f, indent=1)
+        return
     dev = torch.device("cuda", 1 if a.case == "peer-pull" else 0)   # pull: the kernel runs on the reader
     torch.cuda.set_device(dev)
     tables, keep, traffic = build(a.case, a.gbytes, dev, a.item_bytes)
@@ -140,7 +221,7 @@ def main(argv=None):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.iters
     gbs = traffic / (ms / 1e3) / 1e9
-    peak = 770.0 if a.case.startswith("peer") else _peak_gbs()   # measured peer copy vs HBM copy
+    peak = _peer_peak_gbs() if a.case.startswith("peer") else _peak_gbs()   # measured peer vs HBM copy
     print(json.dumps({"case": a.case, "gbytes": a.gbytes, "mode": prog.config.mode, "piece": a.piece, "grid": prog.grid(),
                       "items": len(tables.items), "qwork": len(tables.qwork), "pieces": len(tables.pieces),
                       "amax_pass_ms_host": round(amax_ms, 3) if prog.n_pieces else None, "ms": round(ms, 4),
