@@ -252,3 +252,21 @@ def test_gpu_synth_fill_kernel_matches_torch_ops(dtype):
         ref = synth_values(name, box, dev, dtype, seed=3)
         assert torch.equal(view.contiguous().view(torch.uint8 if dtype != torch.float32 else torch.int32),
                            ref.contiguous().view(torch.uint8 if dtype != torch.float32 else torch.int32)), name
+
+
+@pytest.mark.parametrize("mode", [MODE_VECTOR, MODE_BULK8])
+@pytest.mark.parametrize("dtype,offs", [(torch.bfloat16, (0, 0)), (torch.bfloat16, (1, 3)), (torch.float32, (1, 0)),
+                                        (torch.uint8, (0, 5))])
+def test_gpu_transposed_destination(mode, dtype, offs):
+    """OP_TRANSPOSE work rows (a destination stored column-major, like MLA's w_kc): the
+    2-byte tile path (aligned and misaligned rows, edge tiles) and the element path write
+    exactly the transpose, in every kernel mode; nothing outside the destination changes."""
+    from tests.test_plan_cpu import _transpose_case
+    dev = torch.device("cuda", 0)
+    op, src, dst, store, es = _transpose_case(dtype, 3, 70, 130, src_off=offs[0], dst_off=offs[1], device=dev)
+    prog = TransferProgram(lower_ops([op], ABS, ABS, item_bytes=64 * 70 * es), dev, [], LaunchConfig(mode=mode))
+    prog.launch(1)
+    torch.cuda.synchronize()
+    assert prog.read_status() == 0
+    assert torch.equal(dst, src)
+    assert not store[:offs[1]].to(torch.float32).any()

@@ -302,3 +302,37 @@ def test_redundant_expert_slots(quant):
     if quant:
         sc = params["model.layers.0.mlp.experts.w13_weight_scale_inv"]
         assert torch.equal(sc[1], sc[3]) and not torch.equal(sc[0], sc[1])
+
+
+def _transpose_case(dtype, lead, R, C, src_off=0, dst_off=0, device="cpu"):
+    """A copy of ``[lead, R, C]`` (rows contiguous) into a destination that stores each
+    ``[R, C]`` matrix column-major (MLA's w_kc against kv_b_proj); offsets misalign rows."""
+    from weightbridge_b200.core.plan import Op
+    base = torch.arange(lead * R * C + src_off, dtype=torch.float64, device=device).to(dtype) \
+        if dtype.is_floating_point else torch.randint(0, 100, (lead * R * C + src_off,), device=device).to(dtype)
+    src = base[src_off:].view(lead, R, C)
+    dst_store = torch.zeros(lead * C * R + dst_off, dtype=dtype, device=device)
+    dst = dst_store[dst_off:].view(lead, C, R).transpose(1, 2)       # logical [lead, R, C]
+    es = src.element_size()
+    op = Op("copy", "w", (-1, src.data_ptr()), (-1, dst.data_ptr()), [lead, R, C], list(src.stride()),
+            list(dst.stride()), dtype, dtype)
+    return op, src, dst, dst_store, es
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.uint8])
+def test_transposed_destination_lowers_to_tiled_transposes(dtype):
+    """A destination contiguous along the source's rows lowers to OP_TRANSPOSE work rows (one
+    per matrix and column chunk), which the C++ executor writes exactly; the bounds check
+    covers the destination rows a transpose writes."""
+    from weightbridge_b200.core.plan import OP_TRANSPOSE, PlanBoundsError, validate_tables
+    op, src, dst, store, es = _transpose_case(dtype, 3, 70, 130, src_off=1, dst_off=3)
+    t = lower_ops([op], ABS, ABS, item_bytes=64 * 70 * es)
+    assert len(t.items) == 3 * 3 and ((t.items["op"] & 0xFF) == OP_TRANSPOSE).all()
+    srange = [(src.data_ptr(), src.data_ptr() + src.numel() * es)]
+    drange = [(store.data_ptr(), store.data_ptr() + store.numel() * es)]
+    validate_tables(t, srange, drange)
+    with pytest.raises(PlanBoundsError):
+        validate_tables(t, srange, [(drange[0][0], drange[0][1] - es)])
+    cpu_execute(t)
+    assert torch.equal(dst, src)
+    assert not store[:3].to(torch.float32).any()

@@ -51,7 +51,7 @@ SPIECE_DTYPE = np.dtype([
 assert ITEM_DTYPE.itemsize == 48 and QDESC_DTYPE.itemsize == 64 and QWORK_DTYPE.itemsize == 8
 assert SPIECE_DTYPE.itemsize == 64
 
-OP_COPY, OP_CAST, OP_COPY_MC = 0, 1, 2
+OP_COPY, OP_CAST, OP_COPY_MC, OP_TRANSPOSE = 0, 1, 2, 3
 DEFAULT_ITEM_BYTES = 1 << 19
 
 
@@ -327,6 +327,24 @@ def _split_rows(src, dst, sp, dp, row_bytes, rows, op, drb, item_bytes, out: lis
         out.append((src + r0 * sp, dst + r0 * dp, sp, dp, row_bytes, n, op, drb))
 
 
+def _lower_transpose(o: Op, s_addr: int, d_addr: int, ext, ss, ds, item_bytes: int, out: list) -> None:
+    """Work rows of OP_TRANSPOSE for a copy whose last source dimension is contiguous and whose
+    destination is contiguous along the second-to-last one: per outer index, R source rows by
+    chunks of the C columns (``item_bytes`` of destination each, at least 64 columns)."""
+    es = o.src_dtype.itemsize
+    R, C = ext[-2], ext[-1]
+    sp, dp = ss[-2] * es, ds[-1] * es
+    word = op_word(OP_TRANSPOSE, o.src_dtype, o.dst_dtype)
+    per = max(64, item_bytes // max(1, R * es))
+    outer = ext[:-2]
+    for idx in np.ndindex(*outer) if outer else [()]:
+        so = sum(i * st for i, st in zip(idx, ss[:-2])) * es
+        do = sum(i * st for i, st in zip(idx, ds[:-2])) * es
+        for c0 in range(0, C, per):
+            n = min(per, C - c0)
+            out.append((s_addr + so + c0 * es, d_addr + do + c0 * dp, sp, dp, n * es, R, word, R * es))
+
+
 def lower_ops(ops: Sequence[Op], src_base: Callable[[int], int], dst_base: Callable[[int], int],
               item_bytes: int = DEFAULT_ITEM_BYTES, multicast: bool = False, receiver: int = -1) -> Tables:
     """Resolve allocation indices to addresses and cut ops into device work rows.
@@ -376,6 +394,12 @@ def lower_ops(ops: Sequence[Op], src_base: Callable[[int], int], dst_base: Calla
             kind = OP_COPY_MC
         word = op_word(kind, o.src_dtype, o.dst_dtype)
         ext, ss, ds = list(o.extents), list(o.src_strides), list(o.dst_strides)
+        if (kind == OP_COPY and len(ext) >= 2 and ss[-1] == 1 and ds[-1] != 1 and ds[-2] == 1
+                and ext[-1] > 1 and ext[-2] > 1):
+            # the destination is contiguous along the source's rows: tiled transposes (one
+            # work row per outer index and column chunk) instead of one element per row
+            _lower_transpose(o, s_addr, d_addr, ext, ss, ds, item_bytes, items)
+            continue
         if ss[-1] == 1 and ds[-1] == 1:
             run = ext.pop()
             ss.pop(); ds.pop()
@@ -400,6 +424,12 @@ def lower_ops(ops: Sequence[Op], src_base: Callable[[int], int], dst_base: Calla
 
 
 # -- validation -----------------------------------------------------------------------------
+
+def _code_bytes(code: int) -> int:
+    from ..utils.dtypes import CODE_DTYPES
+    dt = CODE_DTYPES.get(code)
+    return dt.itemsize if dt is not None else 0
+
 
 class PlanBoundsError(ValueError):
     """A work row would read or write outside the memory registered for it."""
@@ -445,7 +475,13 @@ def validate_tables(tables: Tables, src_ranges: Sequence[tuple[int, int]],
         s0 = it["src"]
         s1 = s0 + last * it["src_pitch"].astype(np.uint64) + it["row_bytes"].astype(np.uint64)
         d0 = it["dst"]
-        d1 = d0 + last * it["dst_pitch"].astype(np.uint64) + it["dst_row_bytes"].astype(np.uint64)
+        # a transpose writes one destination row per source column
+        tp = (it["op"] & 0xFF) == OP_TRANSPOSE
+        dlast = last.copy()
+        if tp.any():
+            es = np.array([max(1, _code_bytes(int(c))) for c in (it["op"][tp] >> 8) & 0xFF], dtype=np.uint64)
+            dlast[tp] = np.maximum(it["row_bytes"][tp].astype(np.uint64) // es, 1) - np.uint64(1)
+        d1 = d0 + dlast * it["dst_pitch"].astype(np.uint64) + it["dst_row_bytes"].astype(np.uint64)
         if (it["src_pitch"] < 0).any() or (it["dst_pitch"] < 0).any():
             raise PlanBoundsError("negative row pitch in a work row")
         _check(s0, s1, src_ranges, "read")

@@ -18,11 +18,24 @@ enum DType : uint32_t {
 };
 
 // op word: bits 0-7 kind, 8-15 source dtype, 16-23 destination dtype
-enum OpKind : uint32_t { OP_COPY = 0, OP_CAST = 1, OP_COPY_MC = 2 };
+// OP_TRANSPOSE: `rows` source rows of `row_bytes` (same dtype both sides); destination row c
+// (at dst + c * dst_pitch, `dst_row_bytes` long) holds source column c.
+enum OpKind : uint32_t { OP_COPY = 0, OP_CAST = 1, OP_COPY_MC = 2, OP_TRANSPOSE = 3 };
 
 inline WB_HD uint32_t op_kind(uint32_t w) { return w & 0xffu; }
 inline WB_HD uint32_t op_src(uint32_t w) { return (w >> 8) & 0xffu; }
 inline WB_HD uint32_t op_dst(uint32_t w) { return (w >> 16) & 0xffu; }
+
+// bytes per element of a dtype code (0: unknown)
+inline WB_HD uint32_t dtype_bytes(uint32_t c) {
+  switch (c) {
+    case DT_U8: case DT_I8: case DT_E4M3: case DT_BOOL: case DT_E5M2: return 1u;
+    case DT_F16: case DT_BF16: case DT_I16: return 2u;
+    case DT_F32: case DT_I32: return 4u;
+    case DT_I64: case DT_F64: return 8u;
+    default: return 0u;
+  }
+}
 
 // One unit of copy work: `rows` rows of `row_bytes` source bytes.
 struct alignas(16) Item {

@@ -60,6 +60,16 @@ void run_item(const Item& it) {
     return;
   }
   if (k == OP_COPY_MC) throw std::invalid_argument("multicast items have no CPU execution");
+  if (k == OP_TRANSPOSE) {
+    const uint32_t es = dtype_bytes(op_src(it.op));
+    if (!es || it.row_bytes % es) throw std::invalid_argument("transpose item with unsupported dtype");
+    const uint32_t cols = it.row_bytes / es;
+    for (uint32_t r = 0; r < it.rows; ++r)
+      for (uint32_t c = 0; c < cols; ++c)
+        std::memcpy(d + c * it.dst_pitch + (uint64_t)r * es, s + r * it.src_pitch + (uint64_t)c * es, es);
+    return;
+  }
+  if (k != OP_COPY) throw std::invalid_argument("work row with an unknown op kind");
   for (uint32_t r = 0; r < it.rows; ++r) std::memcpy(d + r * it.dst_pitch, s + r * it.src_pitch, it.row_bytes);
 }
 

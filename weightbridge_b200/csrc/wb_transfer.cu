@@ -174,10 +174,78 @@ __device__ void cast_item(const Item& it, uint32_t* status) {
   }
 }
 
-__device__ void generic_item(const Item& it, uint32_t* status) {
+// ------------------------------------------------------------------------------------
+// generic items: transposes (a destination whose contiguous dimension is the source's rows,
+// e.g. MLA's w_kc written from kv_b_proj).  2-byte elements go through a 64 x 64 tile in
+// shared memory so that both the loads (along source rows) and the stores (along destination
+// rows) are coalesced 128-byte warp accesses; other sizes take an element loop.
+// ------------------------------------------------------------------------------------
+constexpr int kTp = 64;         // tile edge, elements
+constexpr int kTpPitch = 66;    // tile row pitch, elements (4-byte aligned rows, 2-way banks)
+
+__device__ void transpose_item(const Item& it, uint16_t* tile, uint32_t* status) {
+  const uint32_t es = dtype_bytes(op_src(it.op));
+  if (es == 0 || it.row_bytes % es) {
+    if (threadIdx.x == 0 && status) atomicOr(status, ST_BAD_ITEM);
+    return;
+  }
+  const uint32_t R = it.rows, C = it.row_bytes / es;
+  const uint8_t* s8 = reinterpret_cast<const uint8_t*>(it.src);
+  uint8_t* d8 = reinterpret_cast<uint8_t*>(it.dst);
+  if (es != 2) {
+    const uint64_t n = (uint64_t)R * C;
+    for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint32_t c = (uint32_t)(i / R), r = (uint32_t)(i - (uint64_t)c * R);   // r fastest: dst rows
+      const uint8_t* sp = s8 + r * it.src_pitch + (uint64_t)c * es;
+      uint8_t* dp = d8 + c * it.dst_pitch + (uint64_t)r * es;
+      for (uint32_t b = 0; b < es; ++b) dp[b] = sp[b];
+    }
+    return;
+  }
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (uint32_t r0 = 0; r0 < R; r0 += kTp) {
+    for (uint32_t c0 = 0; c0 < C; c0 += kTp) {
+      const uint32_t nr = min((uint32_t)kTp, R - r0), nc = min((uint32_t)kTp, C - c0);
+      __syncthreads();                      // the previous tile's stores have read the tile
+      // load: a warp takes one source row at a time, two elements per lane (128 bytes)
+      for (uint32_t r = warp; r < nr; r += nw) {
+        const uint8_t* row = s8 + (r0 + r) * it.src_pitch + (uint64_t)c0 * 2;
+        const uint32_t c = 2 * lane;
+        uint32_t v = 0;
+        if (c + 1 < nc && (reinterpret_cast<uint64_t>(row) & 3) == 0) {
+          v = __ldg(reinterpret_cast<const uint32_t*>(row) + lane);
+        } else {
+          if (c < nc) v = __ldg(reinterpret_cast<const uint16_t*>(row) + c);
+          if (c + 1 < nc) v |= (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(row) + c + 1) << 16;
+        }
+        *reinterpret_cast<uint32_t*>(tile + r * kTpPitch + c) = v;
+      }
+      __syncthreads();
+      // store: a warp takes one destination row (source column) at a time, two elements per lane
+      for (uint32_t c = warp; c < nc; c += nw) {
+        uint8_t* row = d8 + (c0 + c) * it.dst_pitch + (uint64_t)r0 * 2;
+        const uint32_t r = 2 * lane;
+        const uint16_t lo = r < nr ? tile[r * kTpPitch + c] : 0;
+        const uint16_t hi = r + 1 < nr ? tile[(r + 1) * kTpPitch + c] : 0;
+        if (r + 1 < nr && (reinterpret_cast<uint64_t>(row) & 3) == 0) {
+          reinterpret_cast<uint32_t*>(row)[lane] = (uint32_t)lo | ((uint32_t)hi << 16);
+        } else {
+          if (r < nr) reinterpret_cast<uint16_t*>(row)[r] = lo;
+          if (r + 1 < nr) reinterpret_cast<uint16_t*>(row)[r + 1] = hi;
+        }
+      }
+    }
+  }
+}
+
+__device__ void generic_item(const Item& it, uint16_t* tile, uint32_t* status) {
   const uint32_t k = op_kind(it.op);
   if (k == OP_CAST) {
     cast_item(it, status);
+    return;
+  }
+  if (k == OP_TRANSPOSE) {
+    transpose_item(it, tile, status);
     return;
   }
   const int g = item_granularity(it);
@@ -187,6 +255,10 @@ __device__ void generic_item(const Item& it, uint32_t* status) {
       return;
     }
     copy_item<16, true>(it);
+    return;
+  }
+  if (k != OP_COPY) {
+    if (threadIdx.x == 0 && status) atomicOr(status, ST_BAD_ITEM);
     return;
   }
   switch (g) {
@@ -492,6 +564,7 @@ template <bool BULK, int S, int KST>
 __global__ void __launch_bounds__(kThreads) transfer_kernel(TransferArgs a) {
   extern __shared__ __align__(1024) uint8_t dyn_smem[];
   __shared__ float red[33];
+  __shared__ __align__(16) uint16_t tile[kTp * kTpPitch];
   __shared__ uint32_t s_last;
   __shared__ uint64_t bars[S > 0 ? S : 1];
   __shared__ uint64_t ring_dst[S > 0 ? S : 1];
@@ -499,7 +572,7 @@ __global__ void __launch_bounds__(kThreads) transfer_kernel(TransferArgs a) {
 
   for (uint32_t i = blockIdx.x; i < a.n_items; i += gridDim.x) {
     const Item it = a.items[i];
-    generic_item(it, a.sig.status);
+    generic_item(it, tile, a.sig.status);
   }
   for (uint32_t i = blockIdx.x; i < a.n_qwork; i += gridDim.x) {
     const QuantWork w = a.qwork[i];
