@@ -425,12 +425,12 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                                   and getattr(sender.program, "n_pieces", 0)) else 0)
         pushed = 1 if (sender is not None and sender.program is not None and len(sender.program.tables)) else 0
         pulled = 1 if (recv is not None and recv.pull_program is not None and len(recv.pull_program.tables)) else 0
-        h2d = 8 * pushed                                  # the epoch word, from pinned memory
+        h2d = 8 * (pushed + pulled)                       # the epoch word of each launch, from pinned memory
         # a worker reads the flag words back when some sender pushed (every copy in push; the
         # fp8 blocks in pull)
         any_push = args.direction == "push" or args.transfer != "gpu_direct" or any(meta.quant(n) for n in meta.names())
-        d2h = 4 * (pushed + pulled) + (int(recv.flags.nbytes) if recv is not None and cfg.verify_flags and any_push
-                                       else 0)
+        d2h = 4 * (pushed + pulled) + 8 * pulled + (int(recv.flags.nbytes) if recv is not None and cfg.verify_flags
+                                                    and any_push else 0)     # status words, pull flag, flags
         npieces = getattr(sender.program, "n_pieces", 0) if (sender is not None and sender.program is not None) else 0
         h2d += 4 * npieces                                # split blocks: the exchanged amax of every piece
         d2h += 4 * npieces                                # ... and each piece's own amax, read back first
