@@ -336,3 +336,26 @@ def test_transposed_destination_lowers_to_tiled_transposes(dtype):
     cpu_execute(t)
     assert torch.equal(dst, src)
     assert not store[:3].to(torch.float32).any()
+
+
+def test_interleave_deals_items_and_blocks_round_robin():
+    """Per-peer tables are merged so that consecutive copy items and consecutive quantised
+    blocks go to different peers (no peer's work all comes first), every row kept once."""
+    import numpy as np
+    from weightbridge_b200.control.sender import _interleave
+    from weightbridge_b200.core.plan import ITEM_DTYPE, QDESC_DTYPE, QWORK_DTYPE, Tables
+    parts = []
+    for p, (ni, nq) in enumerate([(5, 4), (2, 6), (3, 0)]):
+        it = np.zeros(ni, ITEM_DTYPE)
+        it["dst"] = 1000 * p + np.arange(ni)
+        qd = np.zeros(1 if nq else 0, QDESC_DTYPE)
+        qw = np.zeros(nq, QWORK_DTYPE)
+        qw["block"] = 1000 * p + np.arange(nq)
+        parts.append(Tables(it, qd, qw))
+    t = _interleave(parts)
+    assert list(t.items["dst"] // 1000)[:6] == [0, 1, 2, 0, 1, 2]
+    assert sorted(t.items["dst"].tolist()) == sorted(np.concatenate([p.items["dst"] for p in parts]).tolist())
+    peers = (t.qwork["block"] // 1000).tolist()
+    assert peers[:4] == [0, 1, 0, 1] and sorted(t.qwork["block"].tolist()) == [0, 1, 2, 3] + [1000 + i for i in range(6)]
+    # each block still points at its own peer's descriptor
+    assert all(int(d) == (0 if b < 1000 else 1) for d, b in zip(t.qwork["desc"], t.qwork["block"]))

@@ -92,7 +92,6 @@ class WeightReceiver:
         self._bound = False                           # tensors bound and exported for this session
         self._pull_versions, self._pull_prog, self._pull_imports = None, None, {}   # pull direction
         self._pull_stream = None
-        self._pull_flag = None                        # device word each pull launch publishes its epoch to
         self._pull_progs: dict = {}                   # pull programs by entry-subset digest
         self._pull_src: dict = {}
         self._pull_ranges: list = []
@@ -620,8 +619,7 @@ class WeightReceiver:
                     with nvtx_range("wbridge.receive/pull"):
                         prog.launch(epoch, self._pull_stream, signal=True)
                         self._pull_stream.synchronize()
-                    status = prog.read_status()
-                    got = int(self._pull_flag.item())
+                    status, got = prog.read_status_and_flag()
                     if not status and got != epoch:
                         raise ReceiveError(f"pull kernel completed with flag {got}, expected epoch {epoch}")
         except Exception as e:
@@ -693,10 +691,7 @@ class WeightReceiver:
             validate_tables(tables, self._pull_ranges, storage_ranges(self.state_dict.values()))
         if self.device.type == "cpu":
             return HostProgram(tables)
-        if self._pull_flag is None:
-            self._pull_flag = torch.zeros(1, dtype=torch.int64, device=self.device)
-        return TransferProgram(tables, self.device, [self._pull_flag.data_ptr()],
-                               LaunchConfig(mode=self.config.kernel_mode))
+        return TransferProgram(tables, self.device, [], LaunchConfig(mode=self.config.kernel_mode), local_flag=True)
 
     def launch(self, stream: torch.cuda.Stream | None = None) -> None:
         """Pull direction: enqueue this worker's pull kernel on ``stream`` with no handshake

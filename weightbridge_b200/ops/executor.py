@@ -83,7 +83,10 @@ class TransferProgram:
     """Device-resident tables of one sender plus its completion signal."""
 
     def __init__(self, tables: Tables, device: torch.device | int | str,
-                 flag_addrs: list[int] | None = None, config: LaunchConfig | None = None):
+                 flag_addrs: list[int] | None = None, config: LaunchConfig | None = None,
+                 local_flag: bool = False):
+        """``local_flag``: the launch also publishes its epoch to a word of this program, next
+        to the status word, so one read returns both (``read_status_and_flag``)."""
         self.device = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
         self.config = config or LaunchConfig.from_env()
         if self.config.mode == MODE_AUTO:
@@ -102,10 +105,14 @@ class TransferProgram:
         self.qdescs = _np_to_tensor(tables.qdescs, dev)
         self.qwork = _np_to_tensor(tables.qwork, dev)
         flag_addrs = list(flag_addrs or [])
+        self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        # [status (low 4 bytes), local flag]: one 16-byte read returns both
+        self.status_flag = torch.zeros(2, dtype=torch.int64, device=dev)
+        self.status = self.status_flag[:1].view(torch.int32)[:1]
+        if local_flag:
+            flag_addrs.append(self.status_flag[1:].data_ptr())
         self.n_flags = len(flag_addrs)
         self.flags = torch.tensor(flag_addrs or [0], dtype=torch.int64, device=dev)
-        self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.epoch_dev = torch.zeros(1, dtype=torch.int64, device=dev)
         self.epoch_host = torch.zeros(1, dtype=torch.int64, pin_memory=True)
         self.n_sms = ext().num_sms(dev.index if dev.index is not None else torch.cuda.current_device())
@@ -177,6 +184,11 @@ class TransferProgram:
 
     def read_status(self) -> int:
         return int(self.status.item())
+
+    def read_status_and_flag(self) -> tuple[int, int]:
+        """The status bits and the local flag word (``local_flag=True``), in one read."""
+        v = self.status_flag.cpu()
+        return int(v[0]) & 0xFFFFFFFF, int(v[1])
 
     def clear_status(self) -> None:
         self.status.zero_()
