@@ -24,7 +24,7 @@ setup(
         CUDAExtension(
             name="weightbridge_b200._C",
             sources=[os.path.join(CSRC, f) for f in
-                     ("wb_bindings.cpp", "wb_transfer.cu", "wb_splitq.cu", "wb_noalloc.cu", "wb_synth.cu", "wb_ipc.cpp",
+                     ("wb_bindings.cpp", "wb_transfer.cu", "wb_splitq.cu", "wb_noalloc.cu", "wb_synth.cu", "wb_board.cpp", "wb_ipc.cpp",
                       "wb_cpu.cpp")],
             include_dirs=[os.path.join(HERE, CSRC)],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},

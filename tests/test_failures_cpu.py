@@ -472,7 +472,9 @@ def test_sender_dying_mid_sync_fails_the_receiver_at_once():
         th = threading.Thread(target=update)
         th.start()
         s._arm(1)                                    # armed; the sender never launches
-        s.session.wait([f"ready/{min(s.targets)}/1"], 10)
+        b = s._board                                 # peers on one host: the handshake words
+        assert b is not None
+        b.wait([b.ready_slot(min(s.targets))], 1, 10.0, lambda: None, "the worker's ready")
         _cut(s._watch)
         th.join(20)
         msg, dt = out["r"]

@@ -21,8 +21,9 @@ UPDATE_REQUEST = "update_request"
 STOP_REQUEST = "stop_request"
 
 # Version of the sender <-> receiver session protocol (session keys, arm channel, split-block
-# amax exchange).  A receiver refuses a connect from a sender speaking another version.
-PROTOCOL_VERSION = 3
+# amax exchange, the same-host handshake board, the pull direction's rules).  A receiver refuses
+# a connect from a sender speaking another version.
+PROTOCOL_VERSION = 4
 
 
 class ReceiverState(str, Enum):

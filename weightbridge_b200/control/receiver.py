@@ -43,6 +43,7 @@ from .assign import expected_senders, restrict
 from .protocol import (CONNECT_REQUEST, METADATA_REQUEST, PROTOCOL_VERSION, RECEIVE_REQUEST, STATS_REQUEST,
                        STOP_REQUEST, UPDATE_REQUEST, ReceiverState, b64)
 from .session import Janitor, PeerError, Session, SessionTimeout
+from .board import word_digest
 
 logger = logging.getLogger(__name__)
 
@@ -96,6 +97,7 @@ class WeightReceiver:
         self._pull_src: dict = {}
         self._pull_ranges: list = []
         self._mc = None                               # nvls: (multicast object, replica group)
+        self._board = None                            # same-host handshake words (control/board.py)
         self._fd_server = None                        # nvls: serves the pool's file descriptor
         fd, path = tempfile.mkstemp(prefix=f"wbridge_sched_{rank}_")
         os.close(fd)
@@ -436,6 +438,9 @@ class WeightReceiver:
         self.expected = expected_senders(plan, gr)
         self._names = {s: plan[s][gr] for s in self.expected}
         self.direction = sess.wait_checked(["direction"])[0].decode() if mode == "gpu_direct" else "push"
+        if mode in ("gpu_direct", "nvls"):
+            from .board import SyncBoard
+            self._board = SyncBoard.attach(sess.get_json("board", self.config.connect_timeout_s))
         self._wire_chunk = int(sess.wait_checked(["wire_chunk"])[0]) if mode in WIRE_MODES else 0
         self._pull_versions, self._pull_prog, self._pull_imports = None, None, {}
         self.expected_bytes = 0
@@ -572,14 +577,22 @@ class WeightReceiver:
             else:
                 ws.recv(self._pg, epoch)
         else:
-            sess.set(f"ready/{gr}/{epoch}", str(self._bind_gen))     # senders rebind on a new generation
+            b = self._board
             keys = [f"done/{s}/{gr}/{epoch}" for s in self.expected]
+            what = f"senders {self.expected} to finish epoch {epoch}"
             try:
-                vals = sess.wait_checked(keys, self.config.sync_timeout_s,
-                                         what=f"senders {self.expected} to finish epoch {epoch}")
+                if b is not None:
+                    b.publish(b.ready_slot(gr), [self._bind_gen], epoch)          # senders rebind on a new generation
+                    b.wait([b.done_slot(s, gr) for s in self.expected], epoch, self.config.sync_timeout_s,
+                           lambda: sess.raise_posted_error(keys), what)
+                    words = [b.read(b.done_slot(s, gr), 6) for s in self.expected]
+                    done = [[str(w[1]), str(w[2]), str(w[3]), str(w[4]), word_digest(w[5])] for w in words]
+                else:
+                    sess.set(f"ready/{gr}/{epoch}", str(self._bind_gen))
+                    vals = sess.wait_checked(keys, self.config.sync_timeout_s, what=what)
+                    done = [v.decode().split(":") for v in vals]          # status:binding-version:pushed:tag:subset
             except (SessionTimeout, PeerError) as e:
                 raise ReceiveError(str(e)) from None
-            done = [v.decode().split(":") for v in vals]          # status:binding-version:pushed:tag:subset
             bad = {s: int(d[0]) for s, d in zip(self.expected, done) if int(d[0])}
             if bad:
                 raise ReceiveError(f"senders reported kernel status {bad} for epoch {epoch}")
@@ -594,9 +607,10 @@ class WeightReceiver:
                 if stale:
                     raise ReceiveError(f"flags of senders {stale} do not hold epoch {epoch}: {flags.tolist()}")
             # handshake keys of this epoch are deleted after the reply (off the critical path)
-            self._garbage += [f"done/{s}/{gr}/{epoch}" for s in self.expected]
-            if epoch > 1:
-                self._garbage.append(f"ready/{gr}/{epoch - 1}")
+            if b is None:
+                self._garbage += [f"done/{s}/{gr}/{epoch}" for s in self.expected]
+                if epoch > 1:
+                    self._garbage.append(f"ready/{gr}/{epoch - 1}")
         self.epoch = epoch
         self.weights_version = None if version < 0 else version
         return {"epoch": epoch, "version": self.weights_version, "host_ms": (time.perf_counter() - t0) * 1e3,
@@ -625,9 +639,12 @@ class WeightReceiver:
         except Exception as e:
             self.session.set_error([f"pulled/{self.global_rank}/{epoch}"], f"receiver {self.global_rank}: {e}")
             raise
-        self.session.set(f"pulled/{self.global_rank}/{epoch}", str(status))
-        if epoch > 1:   # the senders read epoch e's key before this worker can reach epoch e + 1
-            self._garbage.append(f"pulled/{self.global_rank}/{epoch - 1}")
+        if self._board is not None:
+            self._board.publish(self._board.pulled_slot(self.global_rank), [status], epoch)
+        else:
+            self.session.set(f"pulled/{self.global_rank}/{epoch}", str(status))
+            if epoch > 1:   # the senders read epoch e's key before this worker can reach epoch e + 1
+                self._garbage.append(f"pulled/{self.global_rank}/{epoch - 1}")
         if status:
             raise ReceiveError(f"pull kernel reported status {status:#x} at epoch {epoch}")
 
@@ -794,6 +811,9 @@ class WeightReceiver:
         if srv is not None:
             srv.close()
             self._fd_server = None
+        if self._board is not None:
+            self._board.close()
+            self._board = None
         self.session = None
         self._pg = None
         self._garbage = []

@@ -50,6 +50,7 @@ from .assign import assign_sources, restrict
 from ..utils.trace import nvtx_range
 from .protocol import PROTOCOL_VERSION
 from .session import Janitor, PeerError, Session, SessionTimeout, local_address
+from .board import digest_word
 
 logger = logging.getLogger(__name__)
 
@@ -162,6 +163,7 @@ class WeightSender:
         self.uncovered: dict[int, list[str]] = {}    # rank 0, after connect: worker -> entries no sender fills
         self._xchg = None                            # split fp8 blocks shared with other senders
         self._writes_nothing = False                 # pull direction: senders store nothing
+        self._board = None                           # same-host handshake words (control/board.py)
         self.direction = "push"                      # resolved at connect (session_direction)
         self._piece_pos = np.zeros(0, dtype=np.int64)
         self._arm_sock = None                        # rank 0, arm="direct": ROUTER to every receiver worker
@@ -197,6 +199,9 @@ class WeightSender:
     def connect(self, sender_metadata: WeightData) -> None:
         if self.connected:
             self.disconnect()
+        if self._board is not None:
+            self._board.close()
+            self._board = None
         self.metadata = sender_metadata
         self._rinfo = {}
         cfg = self.config
@@ -218,6 +223,9 @@ class WeightSender:
             self.session = Session(addr, port, is_master=False, timeout_s=cfg.connect_timeout_s)
         self.world_total = world
         sess = self.session
+        if self.rank != 0:
+            from .board import SyncBoard
+            self._board = SyncBoard.attach(sess.get_json("board", cfg.connect_timeout_s))
         assignment = sess.get_json("assign")
         mine = assignment.get(str(self.rank), {})
         self.targets = {int(r): names for r, names in mine.items() if names}
@@ -371,6 +379,13 @@ class WeightSender:
                 raise TransferError(f"no sender holds some of the rollout's weights: {msg}")
             logger.warning("no sender holds some of the rollout's weights (they keep their values): %s", msg)
         session_id = uuid.uuid4().hex
+        # peers on one host: per-sync handshake words in shared memory (control/board.py)
+        me = socket.gethostname()
+        if cfg.mode in ("gpu_direct", "nvls") and all(h == me for h in self._sender_hosts) \
+                and all(h == me for h, _d in where):
+            from .board import SyncBoard
+            self._board = SyncBoard.create(session_id, self.world_size, sum(counts))
+        sess.set_json("board", self._board.describe() if self._board is not None else {})
         backend = cfg.mode
         base = self.world_size
         for url, count in zip(self.receiver_urls, counts):
@@ -588,6 +603,9 @@ class WeightSender:
         for imp in self._imports.values():
             imp.close()
         self._imports.clear()
+        if self._board is not None:
+            self._board.close()
+            self._board = None
         self._program = None
         self.session = None
         self.connected = False
@@ -782,12 +800,14 @@ class WeightSender:
             raise TransferError("the plan has split fp8 blocks but the exchange plan has none")
         return self._xchg.positions(tables.piece_keys)
 
-    def _key(self, state_dict) -> tuple:
-        """Identity of the bound tensors: the dict's names and the data pointers of its tensors
-        (lists of views included), so a rebound or reallocated tensor recompiles the plan.
-        One C++ pass over the values (about 25 ns per tensor) instead of a Python loop."""
+    def _key(self, state_dict) -> bytes:
+        """Identity of the bound tensors: per entry, in dict order, the name's hash and the data
+        pointers of its tensor (lists of views included), so a rebound or reallocated tensor
+        recompiles the plan.  One C++ pass over the dict (``state_key``)."""
         from ..ops._ext import ext
-        return tuple(state_dict), ext().data_ptrs(list(state_dict.values()))
+        if isinstance(state_dict, dict):
+            return ext().state_key(state_dict)
+        return ext().state_key(dict(state_dict))
 
     def launch(self, state_dict: dict[str, Any], stream: torch.cuda.Stream | None = None) -> None:
         """Enqueue this sender's transfer kernel on ``stream`` with no HTTP arm, no handshake
@@ -1016,8 +1036,15 @@ class WeightSender:
         t1 = time.perf_counter()
         try:
             with nvtx_range("wbridge.send/ready"):
-                ready = sess.wait_checked([f"ready/{r}/{epoch}" for r in self.targets], cfg.sync_timeout_s,
-                                          f"receivers {sorted(self.targets)} to be ready for epoch {epoch}")
+                what = f"receivers {sorted(self.targets)} to be ready for epoch {epoch}"
+                keys = [f"ready/{r}/{epoch}" for r in self.targets]
+                if self._board is not None:
+                    b = self._board
+                    b.wait([b.ready_slot(r) for r in self.targets], epoch, cfg.sync_timeout_s,
+                           lambda: sess.raise_posted_error(keys), what)
+                    ready = [str(b.read(b.ready_slot(r), 2)[1]).encode() for r in self.targets]
+                else:
+                    ready = sess.wait_checked(keys, cfg.sync_timeout_s, what)
         except (SessionTimeout, PeerError) as e:
             self._fail_epoch(epoch, str(e))
             raise TransferError(str(e)) from None
@@ -1110,16 +1137,29 @@ class WeightSender:
         elif self.direction == "pull":     # the workers move this sender's bytes
             st.bytes_read = st.bytes_written = self._overlap_bytes(subset)
         dg = self._publish_subset(subset) if self.rank == 0 else (_digest(sorted(subset))[:16] if subset else "")
-        done = f"{st.status}:{self._bind_version}:{int(pushed)}:{version}:{dg}"
-        sess.multi_set([f"done/{self.rank}/{r}/{epoch}" for r in self.targets], [done] * len(self.targets))
+        if self._board is not None:
+            b = self._board
+            for r in self.targets:
+                b.publish(b.done_slot(self.rank, r), [st.status, self._bind_version, int(pushed), version,
+                                                      digest_word(dg)], epoch)
+        else:
+            done = f"{st.status}:{self._bind_version}:{int(pushed)}:{version}:{dg}"
+            sess.multi_set([f"done/{self.rank}/{r}/{epoch}" for r in self.targets], [done] * len(self.targets))
         if st.status:
             prog.clear_status()
             raise TransferError(f"transfer kernel reported status {st.status:#x} at epoch {epoch}")
         if self.direction == "pull":
             # parameters stay untouched until every target has pulled its share
             try:
-                vals = sess.wait_checked([f"pulled/{r}/{epoch}" for r in self.targets], cfg.sync_timeout_s,
-                                         f"receivers {sorted(self.targets)} to pull epoch {epoch}")
+                what = f"receivers {sorted(self.targets)} to pull epoch {epoch}"
+                keys = [f"pulled/{r}/{epoch}" for r in self.targets]
+                if self._board is not None:
+                    b = self._board
+                    b.wait([b.pulled_slot(r) for r in self.targets], epoch, cfg.sync_timeout_s,
+                           lambda: sess.raise_posted_error(keys), what)
+                    vals = [str(b.read(b.pulled_slot(r), 2)[1]).encode() for r in sorted(self.targets)]
+                else:
+                    vals = sess.wait_checked(keys, cfg.sync_timeout_s, what)
             except (SessionTimeout, PeerError) as e:
                 raise TransferError(str(e)) from None
             bad = {r: int(v) for r, v in zip(sorted(self.targets), vals) if int(v)}

@@ -99,6 +99,15 @@ class Session:
                 raise PeerError(v[len(ERROR_PREFIX):].decode(errors="replace"))
         return vals
 
+    def raise_posted_error(self, keys: Iterable[str]) -> None:
+        """Raise ``PeerError`` if a peer posted an error in any of ``keys`` (non-blocking; a
+        key that does not exist yet is no error)."""
+        for k in keys:
+            if self.store.check([k]):
+                v = self.store.get(k)
+                if v.startswith(ERROR_PREFIX):
+                    raise PeerError(v[len(ERROR_PREFIX):].decode(errors="replace"))
+
     def set_error(self, keys: Iterable[str], message: str) -> None:
         """Publish a failure in the keys a peer is (or will be) waiting for."""
         for k in keys:

@@ -10,6 +10,7 @@
 #include <string>
 #include <vector>
 
+#include "wb_board.h"
 #include "wb_common.h"
 #include "wb_cpu.h"
 #include "wb_ipc.h"
@@ -103,6 +104,47 @@ void append_ptrs(const py::handle& h, std::string& out, int depth) {
   out.append(reinterpret_cast<const char*>(&p), 8);
 }
 
+// Fingerprint of a state_dict for the sender's per-sync check that it still holds the tensors
+// its program was compiled for: the entry count, then per entry (in dict order) the name's
+// hash and the data pointer(s) of its tensor or list of tensors.  One pass over the dict with
+// PyDict_Next; str hashes are cached by Python, and the tensor type check is skipped while the
+// type repeats.
+py::bytes state_key(const py::dict& d) {
+  std::string out;
+  out.reserve(16 * static_cast<size_t>(PyDict_Size(d.ptr())) + 8);
+  const uint64_t n = static_cast<uint64_t>(PyDict_Size(d.ptr()));
+  out.append(reinterpret_cast<const char*>(&n), 8);
+  PyObject *key = nullptr, *val = nullptr;
+  Py_ssize_t pos = 0;
+  PyTypeObject* tensor_type = nullptr;       // last type seen to be a tensor type
+  auto ptr_of = [&](PyObject* o) -> uint64_t {
+    if (Py_TYPE(o) != tensor_type) {
+      if (!THPVariable_Check(o)) return 0;
+      tensor_type = Py_TYPE(o);
+    }
+    return reinterpret_cast<uint64_t>(THPVariable_Unpack(o).data_ptr());
+  };
+  while (PyDict_Next(d.ptr(), &pos, &key, &val)) {
+    const Py_hash_t kh = PyObject_Hash(key);
+    if (kh == -1) throw py::error_already_set();
+    out.append(reinterpret_cast<const char*>(&kh), 8);
+    uint64_t p = 0;
+    if (PyList_Check(val) || PyTuple_Check(val)) {
+      const Py_ssize_t m = PySequence_Fast_GET_SIZE(val);
+      PyObject** items = PySequence_Fast_ITEMS(val);
+      for (Py_ssize_t i = 0; i < m; ++i) {
+        const uint64_t q = ptr_of(items[i]);
+        out.append(reinterpret_cast<const char*>(&q), 8);
+      }
+      p = ~uint64_t(0);  // end of a list
+    } else {
+      p = ptr_of(val);
+    }
+    out.append(reinterpret_cast<const char*>(&p), 8);
+  }
+  return py::bytes(out);
+}
+
 py::bytes data_ptrs(const py::list& tensors) {
   std::string out;
   out.reserve(tensors.size() * 8);
@@ -152,10 +194,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("split_quant", &split_quant, "launch the quantisation kernel of split fp8 blocks");
   m.def("cpu_split_amax", &cpu_split_amax, "per-piece amax of split fp8 blocks on the host");
   m.def("cpu_split_quant", &cpu_split_quant, "quantise split fp8 block pieces on the host");
+  m.def("board_publish", &wb::board_publish, "store a handshake slot's fields, then its epoch (release)");
+  m.def("board_wait", [](uint64_t base, const std::vector<int64_t>& offs, int64_t target, int64_t max_ns) {
+          py::gil_scoped_release nogil;
+          return wb::board_wait(base, offs, target, max_ns);
+        }, "wait until every slot's epoch reaches target (bounded; the GIL is released)");
+  m.def("board_read", &wb::board_read, "a handshake slot's epoch and fields");
   m.def("num_sms", &num_sms);
   m.def("synth_fill", &synth_fill, "fill a strided view with the synthetic weights");
   m.def("synth_dtype_supported", &wb::synth_dtype_supported);
   m.def("data_ptrs", &data_ptrs, "data pointers of a list of tensors, 8 bytes each");
+  m.def("state_key", &state_key, "fingerprint of a state_dict: entry names' hashes and tensor data pointers");
   m.def("addr_range", [](uint64_t p) {
     auto r = wb::addr_range(p);
     return py::make_tuple(r.base, r.size);
