@@ -62,8 +62,13 @@ def _meta_binding(lay):
     return meta, phys_binding(bind(meta, views))
 
 
-def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs: float = 770.0,
+def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs: float | None = None,
            trainer_kind: str = "megatron") -> dict:
+    """``link_gbs``: per-GPU link bandwidth of the estimate (default: the measured GPU -> GPU
+    peak, ``ops/microbench.py:peer_peak``)."""
+    if link_gbs is None:
+        from .ops.microbench import _peer_peak_gbs
+        link_gbs = _peer_peak_gbs()
     arch = get_arch(model)
     senders = [_meta_binding(l) for l in trainer_layouts(arch, trainer, trainer_kind)]
     receivers = [_meta_binding(l) for l in rollout_layouts(arch, rollout, replicas)]
@@ -113,7 +118,8 @@ def main(argv=None) -> int:
     ap.add_argument("--trainer-kind", default="megatron", choices=["megatron", "fsdp"])
     ap.add_argument("--rollout", default="", help="SGLang layout, e.g. tp=4,moe_ep=4,quant=fp8_experts")
     ap.add_argument("--replicas", type=int, default=1, help="rollout replicas (each with the rollout layout)")
-    ap.add_argument("--link-gbs", type=float, default=770.0, help="per-GPU link bandwidth for the estimate")
+    ap.add_argument("--link-gbs", type=float, default=None,
+                    help="per-GPU link bandwidth for the estimate (default: the measured peer peak)")
     ap.add_argument("--json", action="store_true")
     a = ap.parse_args(argv)
     rep = report(a.model, _kv(a.trainer), _kv(a.rollout), a.replicas, a.link_gbs, a.trainer_kind)
