@@ -6,6 +6,7 @@
 
 copy:    one contiguous bf16 buffer -> another (HBM read + write), 16-byte aligned;
 strided: column block of a row-major matrix -> contiguous (TP column split), 2-D items;
+transpose: [heads, 128, 512] bf16 -> each matrix stored column-major (MLA's w_kc), OP_TRANSPOSE rows;
 quant:   bf16 [E, 768, 2048] expert stack -> fp8 e4m3 + 128x128 fp32 block scales;
 split:   the same stack as split-block pieces (half of every block: rows 64-127 of each block
          row), quantised by split_quant with an amax from split_amax (pass timed on the host);
@@ -94,6 +95,16 @@ def build(case: str, gbytes: float, dev, item_bytes: int):
                                   (-1, q[i].data_ptr() + r0 * c + c0), [64, 128], [c, 1], [c, 1], a.dtype, q.dtype,
                                   (-1, s[i, bi, bj].data_ptr()), [c // 128, 1], (128, 128), key=("x", i, bi, bj)))
         keep, traffic = (a, q, s), e * r * c                # half the source (2 B) and half the fp8 (1 B)
+    elif case == "transpose":
+        # MLA's w_kc from kv_b_proj: per head a [128, 512] bf16 matrix stored column-major
+        r, c = 128, 512
+        m = max(1, n // (r * c))
+        a = torch.randn(m, r, c, device=dev, dtype=torch.bfloat16)
+        b = torch.empty(m, c, r, device=dev, dtype=torch.bfloat16)
+        bt = b.transpose(1, 2)                                    # logical [m, r, c]
+        ops = [Op("copy", "x", (-1, a.data_ptr()), (-1, b.data_ptr()), [m, r, c], list(a.stride()),
+                  list(bt.stride()), a.dtype, a.dtype)]
+        keep, traffic = (a, b), 2 * a.nbytes
     elif case in ("peer-push", "peer-pull", "peer-quant"):
         from ._ext import ext
         if torch.cuda.device_count() < 2:
@@ -182,7 +193,8 @@ def peer_peak(gbytes: float, iters: int, warmup: int, item_bytes: int) -> dict:
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--case", default="copy",
-                   choices=["copy", "strided", "quant", "split", "peer-push", "peer-pull", "peer-quant", "peer-peak"])
+                   choices=["copy", "strided", "transpose", "quant", "split", "peer-push", "peer-pull", "peer-quant",
+                            "peer-peak"])
     p.add_argument("--gbytes", type=float, default=1.0)
     p.add_argument("--mode", type=int, default=-1)
     p.add_argument("--piece", type=int, default=16384)
