@@ -439,6 +439,11 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
         grid = max((p.grid() for p in progs), default=0)
         kmode = max((p.config.mode for p in progs), default=-1)
         hist = sender.history[-args.steps:] if (sender is not None and not args.no_e2e) else []
+        rphases = {}
+        if recv is not None and not args.no_e2e:       # the worker's host steps during the e2e syncs
+            recs = [r.get("phases_ms", {}) for r in list(recv.stats)[-args.steps:]]
+            for k in sorted({k for r in recs for k in r}):
+                rphases[k] = round(sum(r.get(k, 0.0) for r in recs) / max(1, len(recs)), 4)
         avg = lambda f: sum(getattr(h, f) for h in hist) / len(hist) if hist else 0.0
         p2p_ms, p2p_e2e, p2p_ok = (p2p or {}).get("ms", -1.0), (p2p or {}).get("e2e_ms", -1.0), (p2p or {}).get("ok", 1)
         stats = torch.tensor([my_ms, e2e_ms, payload, read, ok, h2d, d2h, active, items, grid, setup_s, kmode,
@@ -448,6 +453,9 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
         gathered = [torch.zeros_like(stats) for _ in range(nprocs)]
         dist.all_gather(gathered, stats)
         G = torch.stack(gathered)
+        phase_lists = [None] * nprocs
+        dist.all_gather_object(phase_lists, rphases)
+        worker_phases = next((p for p in phase_lists if p), {})
 
         if idx == 0:
             ms = float(G[:, 0].max())
@@ -486,7 +494,8 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                     "sender_breakdown_ms": {"wait_ready": round(float(G[:, 12].max()), 3),
                                             "transfer_kernel": round(float(G[:, 13].max()), 3),
                                             "send_total": round(float(G[:, 14].max()), 3),
-                                            "split_block_exchange": round(float(G[:, 15].max()), 3)}},
+                                            "split_block_exchange": round(float(G[:, 15].max()), 3)},
+                "worker_host_steps_ms": worker_phases},
                 "vs_torch_p2p": _p2p_report(args, p2p, G, ms, e2e),
                 "gpu_launches": int(args.steps * G[:, 16].sum()),
                 "clocks": clk.summary() if clk else None,

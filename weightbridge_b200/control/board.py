@@ -5,10 +5,11 @@ notifications - a worker's ``ready`` (it is idle; in the push direction the send
 store into it), a sender's ``done`` (its kernel finished, or in the pull direction its
 parameters are final) and a worker's ``pulled`` - are words in one shared-memory file instead
 of session-store keys: a notification is a store of a few words ended by a release store of the
-epoch, and a wait polls the epoch words (``csrc/wb_board.cpp``, GIL released) instead of a
-TCP round trip to the store.  Errors still travel through the session store: a waiter checks
-the store keys of the notifications it waits for every few milliseconds, so an error a peer
-(or the liveness watcher) posted there ends the wait as before.
+epoch, and a wait polls the epoch words (``csrc/wb_board.cpp``: spinning, then yielding the
+core between polls, with the GIL released) instead of a TCP round trip to the store.  Errors
+still travel through the session store: a waiter checks the store keys of the notifications it
+waits for every few milliseconds, so an error a peer (or the liveness watcher) posted there
+ends the wait as before.
 
 Layout (int64 words): an 8-word header, then one 8-word slot per worker for ``ready``
 (epoch, binding generation), one per worker for ``pulled`` (epoch, status), and one per

@@ -98,6 +98,7 @@ class WeightReceiver:
         self._pull_ranges: list = []
         self._mc = None                               # nvls: (multicast object, replica group)
         self._board = None                            # same-host handshake words (control/board.py)
+        self._pull_phases: dict = {}                  # host time of the last pull's steps, ms
         self._fd_server = None                        # nvls: serves the pool's file descriptor
         fd, path = tempfile.mkstemp(prefix=f"wbridge_sched_{rank}_")
         os.close(fd)
@@ -561,6 +562,15 @@ class WeightReceiver:
             # the engine's last batch may still be running on its streams, reading these
             # parameters: only an idle device may be written by the senders
             torch.cuda.synchronize(self.device)
+        phases: dict[str, float] = {}             # host time of this update's steps, ms
+        mark = [t0]
+
+        def lap(name: str) -> None:
+            t = time.perf_counter()
+            phases[name] = round((t - mark[0]) * 1e3, 4)
+            mark[0] = t
+
+        lap("idle")
         if self.mode in WIRE_MODES:
             try:     # sender rank 0 writes the tag and the entry subset before it arms the workers
                 tag, _sep, digest = sess.wait_checked([f"ver/{epoch}"], self.config.sync_timeout_s)[0] \
@@ -585,6 +595,7 @@ class WeightReceiver:
                     b.publish(b.ready_slot(gr), [self._bind_gen], epoch)          # senders rebind on a new generation
                     b.wait([b.done_slot(s, gr) for s in self.expected], epoch, self.config.sync_timeout_s,
                            lambda: sess.raise_posted_error(keys), what)
+                    lap("ready")
                     words = [b.read(b.done_slot(s, gr), 6) for s in self.expected]
                     done = [[str(w[1]), str(w[2]), str(w[3]), str(w[4]), word_digest(w[5])] for w in words]
                 else:
@@ -598,9 +609,12 @@ class WeightReceiver:
                 raise ReceiveError(f"senders reported kernel status {bad} for epoch {epoch}")
             pushed = [s for s, d in zip(self.expected, done) if len(d) < 3 or d[2] == "1"]
             version = max((int(d[3]) for d in done if len(d) > 3), default=-1)
+            lap("done")
             if self.direction == "pull":
                 self._pull(epoch, {s: int(d[1]) for s, d in zip(self.expected, done)},
                            done[0][4] if done and len(done[0]) > 4 else "")
+                lap("pull")
+                phases.update(self._pull_phases)
             if self.config.verify_flags and pushed:
                 flags = self.flags.cpu()
                 stale = [s for s in pushed if int(flags[s]) != epoch]
@@ -613,8 +627,9 @@ class WeightReceiver:
                     self._garbage.append(f"ready/{gr}/{epoch - 1}")
         self.epoch = epoch
         self.weights_version = None if version < 0 else version
+        lap("finish")
         return {"epoch": epoch, "version": self.weights_version, "host_ms": (time.perf_counter() - t0) * 1e3,
-                "bytes": self.expected_bytes, "senders": self.expected}
+                "bytes": self.expected_bytes, "senders": self.expected, "phases_ms": phases}
 
     # -- pull direction --------------------------------------------------------------------
     def _pull(self, epoch: int, versions: dict[int, int], digest: str = "") -> None:
@@ -631,9 +646,15 @@ class WeightReceiver:
                     # the epoch goes down from pinned memory with the launch; the kernel's last
                     # CTA publishes it to this worker's pull flag, read back with the status
                     with nvtx_range("wbridge.receive/pull"):
+                        t0 = time.perf_counter()
                         prog.launch(epoch, self._pull_stream, signal=True)
+                        t1 = time.perf_counter()
                         self._pull_stream.synchronize()
+                        t2 = time.perf_counter()
                     status, got = prog.read_status_and_flag()
+                    self._pull_phases = {"pull_enqueue": round((t1 - t0) * 1e3, 4),
+                                         "pull_device_wait": round((t2 - t1) * 1e3, 4),
+                                         "pull_readback": round((time.perf_counter() - t2) * 1e3, 4)}
                     if not status and got != epoch:
                         raise ReceiveError(f"pull kernel completed with flag {got}, expected epoch {epoch}")
         except Exception as e:

@@ -1001,7 +1001,10 @@ class WeightSender:
         t0 = time.perf_counter()
         epoch = self.epoch + 1
         st = SyncStats(epoch=epoch, receivers=sorted(self.targets), link_gbs=self.config.link_gbs)
-        ready = self._handshake(epoch, version, subset, st)
+        if self._writes_nothing:          # pulling: done is published before the arm (_transfer_direct)
+            ready = []
+        else:
+            ready = self._handshake(epoch, version, subset, st)
         self._prepare(state_dict, subset, ready, epoch)
         if len(self._piece_pos):          # split fp8 blocks: amax of every piece, then the exchange
             self._exchange_split_amax(epoch, st, after)
@@ -1009,12 +1012,25 @@ class WeightSender:
             self._transfer_wire(epoch, st, after)
         elif self.targets:
             self._transfer_direct(epoch, st, after, version, subset)
+        elif self._writes_nothing:        # rank 0 arms every worker even when it sends nothing itself
+            self._arm_and_check(epoch)
         self.epoch = epoch
         st.host_ms = (time.perf_counter() - t0) * 1e3
         self.history.append(st)
         if len(self.history) > 256:
             del self.history[:128]
         return st
+
+    def _arm_and_check(self, epoch: int) -> None:
+        """Rank 0 arms the workers and fails the epoch if that did not reach all of them."""
+        if self.rank != 0:
+            return
+        arm = self._arm(epoch)
+        if arm is not None:
+            arm.join()
+        if self._arm_error is not None:
+            self._fail_epoch(epoch, self._arm_error)
+            raise TransferError(self._arm_error)
 
     def _handshake(self, epoch: int, version: int, subset: frozenset | None, st: SyncStats) -> list:
         """Rank 0 tags the epoch (wire modes) and arms the workers; every rank waits until its
@@ -1026,13 +1042,6 @@ class WeightSender:
             if epoch > 16:
                 sess.delete(f"ver/{epoch - 16}")
         arm = self._arm(epoch) if self.rank == 0 else None
-        if self._writes_nothing:                  # nothing to wait for: publish done right away
-            if arm is not None:
-                arm.join()
-            if self.rank == 0 and self._arm_error is not None:
-                self._fail_epoch(epoch, self._arm_error)
-                raise TransferError(self._arm_error)
-            return []
         t1 = time.perf_counter()
         try:
             with nvtx_range("wbridge.send/ready"):
@@ -1145,6 +1154,8 @@ class WeightSender:
         else:
             done = f"{st.status}:{self._bind_version}:{int(pushed)}:{version}:{dg}"
             sess.multi_set([f"done/{self.rank}/{r}/{epoch}" for r in self.targets], [done] * len(self.targets))
+        if self._writes_nothing:          # pulling: the workers find this done the moment they are armed
+            self._arm_and_check(epoch)
         if st.status:
             prog.clear_status()
             raise TransferError(f"transfer kernel reported status {st.status:#x} at epoch {epoch}")

@@ -55,6 +55,35 @@ void transfer(uint64_t items, uint32_t n_items, uint64_t bulk, uint32_t n_bulk, 
   check(wb::launch_transfer(a, mode, grid, reinterpret_cast<cudaStream_t>(stream)), "transfer launch");
 }
 
+// One call per launch for the per-sync path: with `epoch` >= 0 write it into the pinned host word
+// and copy it to the device epoch word on `stream`, then launch the kernel with the completion
+// signal; with `epoch` < 0 launch without a signal.  `a` holds the program's fixed arguments:
+// (items, n_items, bulk, n_bulk, qdescs, qwork, n_qwork, piece_bytes, spin_limit, counter,
+//  flags, n_flags, epoch_dev, status, mode, grid, epoch_host).
+void transfer_launch(const py::tuple& a, int64_t epoch, uint64_t stream) {
+  if (a.size() != 17) throw std::invalid_argument("transfer_launch: 17 fixed arguments expected");
+  auto u = [&](size_t i) { return a[i].cast<uint64_t>(); };
+  const bool sig = epoch >= 0;
+  const auto st = reinterpret_cast<cudaStream_t>(stream);
+  if (sig) {
+    int64_t* host = reinterpret_cast<int64_t*>(u(16));
+    *host = epoch;
+    check(cudaMemcpyAsync(reinterpret_cast<void*>(u(12)), host, 8, cudaMemcpyHostToDevice, st), "epoch copy");
+  }
+  transfer(u(0), (uint32_t)u(1), u(2), (uint32_t)u(3), u(4), u(5), (uint32_t)u(6), (uint32_t)u(7), (uint32_t)u(8),
+           sig ? u(9) : 0, u(10), sig ? (uint32_t)u(11) : 0, u(12), u(13), a[14].cast<int>(), a[15].cast<int>(), stream);
+}
+
+// Synchronous read of `n` 8-byte words of device memory through a pinned host buffer.
+py::list read_words(uint64_t dev, uint64_t host, int64_t n) {
+  check(cudaMemcpy(reinterpret_cast<void*>(host), reinterpret_cast<const void*>(dev), 8 * (size_t)n,
+                   cudaMemcpyDeviceToHost), "read_words");
+  py::list out;
+  const int64_t* h = reinterpret_cast<const int64_t*>(host);
+  for (int64_t i = 0; i < n; ++i) out.append(h[i]);
+  return out;
+}
+
 void wait_flags(uint64_t flags, uint32_t n, uint64_t epoch, uint64_t timeout_ns, uint64_t status, uint64_t where,
                 uint64_t stream) {
   check(wb::launch_wait_flags(P<const uint64_t>(flags), n, P<const uint64_t>(epoch), timeout_ns, P<uint32_t>(status),
@@ -187,6 +216,8 @@ py::tuple vmm_tuple(const wb::VmmAlloc& a) { return py::make_tuple(a.ptr, a.size
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "weightbridge_b200 native runtime: sm_100a transfer kernel, CPU executor, IPC/VMM/multicast";
   m.def("transfer", &transfer, "launch the persistent transfer kernel");
+  m.def("transfer_launch", &transfer_launch, "epoch copy and transfer launch of one program, in one call");
+  m.def("read_words", &read_words, "synchronous read of device words through a pinned buffer");
   m.def("wait_flags", &wait_flags, "launch a bounded wait on flag words");
   m.def("bulk_stages", &wb::bulk_stages);
   m.def("cpu_execute", &cpu_execute, "run work tables on the host");

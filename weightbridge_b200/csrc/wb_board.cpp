@@ -5,7 +5,7 @@
 // "pulled" or "ready" - which otherwise cost a session-store round trip each.  Here every
 // notification is a group of 64-bit words in one shared-memory file: the writer stores the
 // fields and then the epoch with release ordering; a waiter polls the epoch words with acquire
-// loads (spinning briefly, then sleeping in growing steps) until all of them reach the target,
+// loads (spinning, then yielding the core between polls) until all of them reach the target,
 // with the GIL released.  Errors do not travel here: they stay in the session store, which the
 // caller checks between bounded waits.
 #include "wb_board.h"
@@ -36,15 +36,13 @@ bool board_wait(uint64_t base, const std::vector<int64_t>& offs, int64_t target,
   const auto t0 = clock::now();
   const auto limit = std::chrono::nanoseconds(max_ns);
   size_t next = 0;
-  int64_t sleep_ns = 0;
   for (uint64_t polls = 0;; ++polls) {
     while (next < offs.size() && word(base, offs[next])->load(std::memory_order_acquire) >= target) ++next;
     if (next == offs.size()) return true;
     if ((polls & 63) == 0 && clock::now() - t0 >= limit) return false;
-    if (polls > 2048) {                       // ~tens of microseconds of spinning, then back off
-      sleep_ns = sleep_ns ? (sleep_ns < 50000 ? sleep_ns * 2 : 50000) : 1000;
-      std::this_thread::sleep_for(std::chrono::nanoseconds(sleep_ns));
-    }
+    // spin first; then yield the core between polls (a sleep would wake late: the kernel's
+    // timer slack rounds short sleeps up to ~50 us, which a sync would pay at every handshake)
+    if (polls > 4096) std::this_thread::yield();
   }
 }
 

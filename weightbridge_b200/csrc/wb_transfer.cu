@@ -181,7 +181,39 @@ __device__ void cast_item(const Item& it, uint32_t* status) {
 // rows) are coalesced 128-byte warp accesses; other sizes take an element loop.
 // ------------------------------------------------------------------------------------
 constexpr int kTp = 64;         // tile edge, elements
-constexpr int kTpPitch = 66;    // tile row pitch, elements (4-byte aligned rows, 2-way banks)
+constexpr int kTpPitch = 66;    // tile row pitch, elements: 33 words, so the 32-bit writes of a
+                                // warp (4 rows x 8 lanes) hit 32 banks and the column reads 2-way
+
+// One 64 x 64 tile of 2-byte elements: each of the 256 threads holds two 16-byte pieces of
+// source rows (eight lanes span a 128-byte row segment, a warp four rows), written to shared
+// memory as 32-bit words.  Loads of the next tile are issued before the current tile's
+// stores, so they overlap.
+struct TpRegs {
+  uint4 v[2];
+};
+
+__device__ __forceinline__ void tp_load(const uint8_t* s8, int64_t pitch, uint32_t R, uint32_t C, uint32_t r0,
+                                        uint32_t c0, TpRegs& g) {
+  #pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const uint32_t idx = threadIdx.x + 256u * k;          // 512 pieces of 8 elements
+    const uint32_t r = idx >> 3, c = (idx & 7) * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r0 + r < R) {
+      const uint8_t* p = s8 + (r0 + r) * pitch + (uint64_t)(c0 + c) * 2;
+      if (c0 + c + 8 <= C && (reinterpret_cast<uint64_t>(p) & 15) == 0) {
+        v = ld_nc16(p);
+      } else {
+        uint16_t e[8];
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) e[j] = (c0 + c + j < C) ? __ldg(reinterpret_cast<const uint16_t*>(p) + j) : 0;
+        v = make_uint4(e[0] | ((uint32_t)e[1] << 16), e[2] | ((uint32_t)e[3] << 16), e[4] | ((uint32_t)e[5] << 16),
+                       e[6] | ((uint32_t)e[7] << 16));
+      }
+    }
+    g.v[k] = v;
+  }
+}
 
 __device__ void transpose_item(const Item& it, uint16_t* tile, uint32_t* status) {
   const uint32_t es = dtype_bytes(op_src(it.op));
@@ -192,7 +224,7 @@ __device__ void transpose_item(const Item& it, uint16_t* tile, uint32_t* status)
   const uint32_t R = it.rows, C = it.row_bytes / es;
   const uint8_t* s8 = reinterpret_cast<const uint8_t*>(it.src);
   uint8_t* d8 = reinterpret_cast<uint8_t*>(it.dst);
-  if (es != 2) {
+  if (es != 2 || blockDim.x != 256) {
     const uint64_t n = (uint64_t)R * C;
     for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) {
       const uint32_t c = (uint32_t)(i / R), r = (uint32_t)(i - (uint64_t)c * R);   // r fastest: dst rows
@@ -202,37 +234,36 @@ __device__ void transpose_item(const Item& it, uint16_t* tile, uint32_t* status)
     }
     return;
   }
-  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (uint32_t r0 = 0; r0 < R; r0 += kTp) {
-    for (uint32_t c0 = 0; c0 < C; c0 += kTp) {
-      const uint32_t nr = min((uint32_t)kTp, R - r0), nc = min((uint32_t)kTp, C - c0);
-      __syncthreads();                      // the previous tile's stores have read the tile
-      // load: a warp takes one source row at a time, two elements per lane (128 bytes)
-      for (uint32_t r = warp; r < nr; r += nw) {
-        const uint8_t* row = s8 + (r0 + r) * it.src_pitch + (uint64_t)c0 * 2;
-        const uint32_t c = 2 * lane;
-        uint32_t v = 0;
-        if (c + 1 < nc && (reinterpret_cast<uint64_t>(row) & 3) == 0) {
-          v = __ldg(reinterpret_cast<const uint32_t*>(row) + lane);
-        } else {
-          if (c < nc) v = __ldg(reinterpret_cast<const uint16_t*>(row) + c);
-          if (c + 1 < nc) v |= (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(row) + c + 1) << 16;
-        }
-        *reinterpret_cast<uint32_t*>(tile + r * kTpPitch + c) = v;
-      }
-      __syncthreads();
-      // store: a warp takes one destination row (source column) at a time, two elements per lane
-      for (uint32_t c = warp; c < nc; c += nw) {
-        uint8_t* row = d8 + (c0 + c) * it.dst_pitch + (uint64_t)r0 * 2;
-        const uint32_t r = 2 * lane;
-        const uint16_t lo = r < nr ? tile[r * kTpPitch + c] : 0;
-        const uint16_t hi = r + 1 < nr ? tile[(r + 1) * kTpPitch + c] : 0;
-        if (r + 1 < nr && (reinterpret_cast<uint64_t>(row) & 3) == 0) {
-          reinterpret_cast<uint32_t*>(row)[lane] = (uint32_t)lo | ((uint32_t)hi << 16);
-        } else {
-          if (r < nr) reinterpret_cast<uint16_t*>(row)[r] = lo;
-          if (r + 1 < nr) reinterpret_cast<uint16_t*>(row)[r + 1] = hi;
-        }
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t tr = (R + kTp - 1) / kTp, tc = (C + kTp - 1) / kTp, nt = tr * tc;
+  TpRegs g;
+  tp_load(s8, it.src_pitch, R, C, 0, 0, g);
+  for (uint32_t t = 0; t < nt; ++t) {
+    const uint32_t r0 = (t / tc) * kTp, c0 = (t % tc) * kTp;
+    const uint32_t nr = min((uint32_t)kTp, R - r0), nc = min((uint32_t)kTp, C - c0);
+    __syncthreads();                        // the previous tile's stores have read the tile
+    #pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const uint32_t idx = threadIdx.x + 256u * k;
+      uint32_t* w = reinterpret_cast<uint32_t*>(tile + (idx >> 3) * kTpPitch + (idx & 7) * 8);
+      w[0] = g.v[k].x;
+      w[1] = g.v[k].y;
+      w[2] = g.v[k].z;
+      w[3] = g.v[k].w;
+    }
+    __syncthreads();
+    if (t + 1 < nt) tp_load(s8, it.src_pitch, R, C, ((t + 1) / tc) * kTp, ((t + 1) % tc) * kTp, g);
+    // store: a warp takes one destination row (source column) at a time, two elements per lane
+    for (uint32_t c = warp; c < nc; c += 8) {
+      uint8_t* row = d8 + (c0 + c) * it.dst_pitch + (uint64_t)r0 * 2;
+      const uint32_t r = 2 * lane;
+      const uint16_t lo = r < nr ? tile[r * kTpPitch + c] : 0;
+      const uint16_t hi = r + 1 < nr ? tile[(r + 1) * kTpPitch + c] : 0;
+      if (r + 1 < nr && (reinterpret_cast<uint64_t>(row) & 3) == 0) {
+        reinterpret_cast<uint32_t*>(row)[lane] = (uint32_t)lo | ((uint32_t)hi << 16);
+      } else {
+        if (r < nr) reinterpret_cast<uint16_t*>(row)[r] = lo;
+        if (r + 1 < nr) reinterpret_cast<uint16_t*>(row)[r + 1] = hi;
       }
     }
   }

@@ -117,6 +117,13 @@ class TransferProgram:
         self.epoch_host = torch.zeros(1, dtype=torch.int64, pin_memory=True)
         self.n_sms = ext().num_sms(dev.index if dev.index is not None else torch.cuda.current_device())
         self.launches = 0
+        self.status_host = torch.zeros(2, dtype=torch.int64, pin_memory=True)
+        launch_mode = self.config.mode if len(self.bulk_np) else MODE_VECTOR
+        self._fixed = (self.items.data_ptr(), len(self.items_np), self.bulk.data_ptr(), len(self.bulk_np),
+                       self.qdescs.data_ptr(), self.qwork.data_ptr(), len(tables.qwork), self.config.piece_bytes,
+                       self.config.spin_limit, self.counter.data_ptr(), self.flags.data_ptr() if self.n_flags else 0,
+                       self.n_flags, self.epoch_dev.data_ptr(), self.status.data_ptr(), launch_mode, self.grid(),
+                       self.epoch_host.data_ptr())
         # split-block pieces: amax per piece (device, pinned copy) and the exchanged block amax
         self.n_pieces = len(tables.pieces)
         if self.n_pieces:
@@ -154,7 +161,7 @@ class TransferProgram:
         if c.grid:
             return c.grid
         work = len(self.items_np) + len(self.tables.qwork) + len(self.bulk_np)
-        if c.mode == MODE_VECTOR:
+        if c.mode == MODE_VECTOR or not len(self.bulk_np):      # launched in vector mode
             per_sm = 4
         else:
             smem = ext().bulk_stages(c.mode) * c.piece_bytes
@@ -165,30 +172,21 @@ class TransferProgram:
         """Copy the epoch host->device and launch the kernel on ``stream``.  With
         ``signal=False`` the launch publishes no flags (ordering is the caller's job)."""
         stream = stream or torch.cuda.current_stream(self.device)
-        c = self.config
-        with torch.cuda.stream(stream):
-            if signal:
-                self.epoch_host[0] = epoch
-                self.epoch_dev.copy_(self.epoch_host, non_blocking=True)
-            if self.n_pieces:       # before the transfer kernel, whose last CTA publishes the flags
+        if self.n_pieces:           # before the transfer kernel, whose last CTA publishes the flags
+            with torch.cuda.stream(stream):
                 self.amax.copy_(self.amax_host, non_blocking=True)
                 ext().split_quant(self.pieces.data_ptr(), self.n_pieces, self.amax.data_ptr(), stream.cuda_stream)
-            ext().transfer(
-                self.items.data_ptr(), len(self.items_np), self.bulk.data_ptr(), len(self.bulk_np),
-                self.qdescs.data_ptr(), self.qwork.data_ptr(), len(self.tables.qwork),
-                c.piece_bytes, c.spin_limit, self.counter.data_ptr() if signal else 0,
-                self.flags.data_ptr() if self.n_flags else 0, self.n_flags if signal else 0,
-                self.epoch_dev.data_ptr(), self.status.data_ptr(), c.mode if len(self.bulk_np) else MODE_VECTOR,
-                self.grid(), stream.cuda_stream)
+        # one native call: the epoch (pinned host word -> device) and the launch
+        ext().transfer_launch(self._fixed, int(epoch) if signal else -1, stream.cuda_stream)
         self.launches += 1
 
     def read_status(self) -> int:
-        return int(self.status.item())
+        return ext().read_words(self.status_flag.data_ptr(), self.status_host.data_ptr(), 1)[0] & 0xFFFFFFFF
 
     def read_status_and_flag(self) -> tuple[int, int]:
         """The status bits and the local flag word (``local_flag=True``), in one read."""
-        v = self.status_flag.cpu()
-        return int(v[0]) & 0xFFFFFFFF, int(v[1])
+        v = ext().read_words(self.status_flag.data_ptr(), self.status_host.data_ptr(), 2)
+        return v[0] & 0xFFFFFFFF, v[1]
 
     def clear_status(self) -> None:
         self.status.zero_()
