@@ -456,6 +456,13 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
         phase_lists = [None] * nprocs
         dist.all_gather_object(phase_lists, rphases)
         worker_phases = next((p for p in phase_lists if p), {})
+        # the sync's critical path across processes (perf_counter is the host's monotonic clock)
+        my_marks = ({"sender": {h.epoch: h.marks for h in hist}} if sender is not None else
+                    {"worker": {r["epoch"]: r.get("marks", {}) for r in list(recv.stats)[-args.steps:]}}
+                    if recv is not None and not args.no_e2e else {})
+        mark_lists = [None] * nprocs
+        dist.all_gather_object(mark_lists, my_marks)
+        chain = _sync_chain(mark_lists)
 
         if idx == 0:
             ms = float(G[:, 0].max())
@@ -495,7 +502,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                                             "transfer_kernel": round(float(G[:, 13].max()), 3),
                                             "send_total": round(float(G[:, 14].max()), 3),
                                             "split_block_exchange": round(float(G[:, 15].max()), 3)},
-                "worker_host_steps_ms": worker_phases},
+                "worker_host_steps_ms": worker_phases, "sync_chain_ms": chain},
                 "vs_torch_p2p": _p2p_report(args, p2p, G, ms, e2e),
                 "gpu_launches": int(args.steps * G[:, 16].sum()),
                 "clocks": clk.summary() if clk else None,
@@ -520,6 +527,36 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
     if ctl is not None:
         ctl.close()
     dist.destroy_process_group()
+
+
+def _sync_chain(mark_lists: list) -> dict:
+    """Median host latencies along one sync between the first sender and the first worker that
+    recorded marks: sender start -> program selected -> stream synchronised -> done published ->
+    workers armed -> the worker's arm message
+    seen -> its update begins -> pulled published -> the sender's send returns."""
+    import statistics
+    snd = next((m["sender"] for m in mark_lists if m and "sender" in m), None)
+    wrk = next((m["worker"] for m in mark_lists if m and "worker" in m), None)
+    if not snd or not wrk:
+        return {}
+    steps = {"sender_start_to_prepared": ("s", "start", "s", "prepared"),
+             "prepared_to_synced": ("s", "prepared", "s", "synced"), "synced_to_done": ("s", "synced", "s", "done"),
+             "done_to_armed": ("s", "done", "s", "armed"),
+             "armed_to_worker_arm_seen": ("s", "armed", "w", "armed"),
+             "arm_seen_to_update_begin": ("w", "armed", "w", "begin"),
+             "worker_update": ("w", "begin", "w", "pulled"),
+             "pulled_to_sender_return": ("w", "pulled", "s", "end")}
+    out = {}
+    for name, (a, ka, b, kb) in steps.items():
+        vals = []
+        for e in set(snd) & set(wrk):
+            ma = snd[e] if a == "s" else wrk[e]
+            mb = snd[e] if b == "s" else wrk[e]
+            if ma.get(ka) and mb.get(kb):
+                vals.append((mb[kb] - ma[ka]) * 1e3)
+        if vals:
+            out[name] = round(statistics.median(vals), 4)
+    return out
 
 
 def torch_p2p_phase(args, roles, idx, lay, meta, views, params, dev) -> dict | None:

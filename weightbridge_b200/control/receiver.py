@@ -99,6 +99,8 @@ class WeightReceiver:
         self._mc = None                               # nvls: (multicast object, replica group)
         self._board = None                            # same-host handshake words (control/board.py)
         self._pull_phases: dict = {}                  # host time of the last pull's steps, ms
+        self._arm_t = 0.0                             # time.perf_counter() of the last direct arm
+        self._pulled_t = 0.0                          # ... and of the last pulled word
         self._fd_server = None                        # nvls: serves the pool's file descriptor
         fd, path = tempfile.mkstemp(prefix=f"wbridge_sched_{rank}_")
         os.close(fd)
@@ -320,6 +322,7 @@ class WeightReceiver:
         ok_states = (ReceiverState.CONNECTED, ReceiverState.AWAITING_SCHEDULER_UPDATE)   # re-arm: no-op
         if self._state in ok_states and epoch == self.epoch + 1:
             self._state = ReceiverState.AWAITING_SCHEDULER_UPDATE
+            self._arm_t = time.perf_counter()
             return
         why = (f"receiver {self.global_rank} cannot take sync {epoch}: state {self._state.value}, "
                f"last epoch {self.epoch}")
@@ -629,7 +632,8 @@ class WeightReceiver:
         self.weights_version = None if version < 0 else version
         lap("finish")
         return {"epoch": epoch, "version": self.weights_version, "host_ms": (time.perf_counter() - t0) * 1e3,
-                "bytes": self.expected_bytes, "senders": self.expected, "phases_ms": phases}
+                "bytes": self.expected_bytes, "senders": self.expected, "phases_ms": phases,
+                "marks": {"armed": self._arm_t, "begin": t0, "pulled": self._pulled_t, "end": mark[0]}}
 
     # -- pull direction --------------------------------------------------------------------
     def _pull(self, epoch: int, versions: dict[int, int], digest: str = "") -> None:
@@ -662,6 +666,7 @@ class WeightReceiver:
             raise
         if self._board is not None:
             self._board.publish(self._board.pulled_slot(self.global_rank), [status], epoch)
+            self._pulled_t = time.perf_counter()
         else:
             self.session.set(f"pulled/{self.global_rank}/{epoch}", str(status))
             if epoch > 1:   # the senders read epoch e's key before this worker can reach epoch e + 1

@@ -71,6 +71,7 @@ class SyncStats:
     receivers: list[int] = field(default_factory=list)
     status: int = 0
     link_gbs: float = 770.0         # bandwidth the fraction below is taken against
+    marks: dict = field(default_factory=dict)   # time.perf_counter() at the sync's steps (start, done, armed, end)
 
     @property
     def gbs(self) -> float:
@@ -163,6 +164,7 @@ class WeightSender:
         self.uncovered: dict[int, list[str]] = {}    # rank 0, after connect: worker -> entries no sender fills
         self._xchg = None                            # split fp8 blocks shared with other senders
         self._writes_nothing = False                 # pull direction: senders store nothing
+        self._overlap_nbytes: dict = {}              # bytes per entry subset (pull stats), per session
         self._board = None                           # same-host handshake words (control/board.py)
         self.direction = "push"                      # resolved at connect (session_direction)
         self._piece_pos = np.zeros(0, dtype=np.int64)
@@ -233,6 +235,7 @@ class WeightSender:
         self._all_receivers = set(rmetas)
         self.overlaps = {r: WeightData.compute_overlap(restrict(sender_metadata, names), rmetas[r])
                          for r, names in self.targets.items()}
+        self._overlap_nbytes = {}
         self._xchg = self._exchange_plan(metas, assignment, rmetas)
         self.direction = session_direction(cfg, rmetas.values())
         # pulling, this sender never writes into its workers' memory, so a sync need not wait
@@ -984,9 +987,14 @@ class WeightSender:
         return out
 
     def _overlap_bytes(self, subset: frozenset | None) -> int:
-        """Bytes of this sender's entries its targets receive (restricted to ``subset``)."""
-        return sum(end - start for ov in self.overlaps.values() for start, end, name, _sh, _dt in ov.iter_with_intv()
-                   if subset is None or name in subset)
+        """Bytes of this sender's entries its targets receive (restricted to ``subset``),
+        computed once per subset and session."""
+        n = self._overlap_nbytes.get(subset)
+        if n is None:
+            n = sum(end - start for ov in self.overlaps.values() for start, end, name, _sh, _dt in ov.iter_with_intv()
+                    if subset is None or name in subset)
+            self._overlap_nbytes[subset] = n
+        return n
 
     def _subset(self, names) -> frozenset | None:
         return None if names is None else frozenset(names)
@@ -1001,11 +1009,13 @@ class WeightSender:
         t0 = time.perf_counter()
         epoch = self.epoch + 1
         st = SyncStats(epoch=epoch, receivers=sorted(self.targets), link_gbs=self.config.link_gbs)
+        st.marks["start"] = t0
         if self._writes_nothing:          # pulling: done is published before the arm (_transfer_direct)
             ready = []
         else:
             ready = self._handshake(epoch, version, subset, st)
         self._prepare(state_dict, subset, ready, epoch)
+        st.marks["prepared"] = time.perf_counter()
         if len(self._piece_pos):          # split fp8 blocks: amax of every piece, then the exchange
             self._exchange_split_amax(epoch, st, after)
         if self.config.mode in WIRE_MODES:
@@ -1015,7 +1025,8 @@ class WeightSender:
         elif self._writes_nothing:        # rank 0 arms every worker even when it sends nothing itself
             self._arm_and_check(epoch)
         self.epoch = epoch
-        st.host_ms = (time.perf_counter() - t0) * 1e3
+        st.marks["end"] = time.perf_counter()
+        st.host_ms = (st.marks["end"] - t0) * 1e3
         self.history.append(st)
         if len(self.history) > 256:
             del self.history[:128]
@@ -1141,6 +1152,7 @@ class WeightSender:
         elif torch.cuda.is_available():
             (after if after is not None else torch.cuda.current_stream()).synchronize()   # the receivers
             # pull: the parameters must be final
+        st.marks["synced"] = time.perf_counter()
         if prog is not None:
             st.bytes_read, st.bytes_written = prog.bytes_read, prog.bytes_written
         elif self.direction == "pull":     # the workers move this sender's bytes
@@ -1154,8 +1166,10 @@ class WeightSender:
         else:
             done = f"{st.status}:{self._bind_version}:{int(pushed)}:{version}:{dg}"
             sess.multi_set([f"done/{self.rank}/{r}/{epoch}" for r in self.targets], [done] * len(self.targets))
+        st.marks["done"] = time.perf_counter()
         if self._writes_nothing:          # pulling: the workers find this done the moment they are armed
             self._arm_and_check(epoch)
+            st.marks["armed"] = time.perf_counter()
         if st.status:
             prog.clear_status()
             raise TransferError(f"transfer kernel reported status {st.status:#x} at epoch {epoch}")
