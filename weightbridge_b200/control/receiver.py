@@ -28,6 +28,7 @@ import socket
 import tempfile
 import threading
 import time
+import uuid
 from collections import deque
 from typing import Any
 
@@ -101,6 +102,7 @@ class WeightReceiver:
         self._pull_phases: dict = {}                  # host time of the last pull's steps, ms
         self._arm_t = 0.0                             # time.perf_counter() of the last direct arm
         self._pulled_t = 0.0                          # ... and of the last pulled word
+        self._arm_path = None                         # Unix socket file of a loopback arm endpoint
         self._fd_server = None                        # nvls: serves the pool's file descriptor
         fd, path = tempfile.mkstemp(prefix=f"wbridge_sched_{rank}_")
         os.close(fd)
@@ -326,19 +328,27 @@ class WeightReceiver:
             return
         why = (f"receiver {self.global_rank} cannot take sync {epoch}: state {self._state.value}, "
                f"last epoch {self.epoch}")
-        self.session.set_error([f"ready/{self.global_rank}/{epoch}"], why)
+        # senders wait for ready (push) or pulled (pull): both carry the reason
+        self.session.set_error([f"ready/{self.global_rank}/{epoch}", f"pulled/{self.global_rank}/{epoch}"], why)
 
     def _open_arm_socket(self, master_address: str) -> str:
-        """Bind the direct-arm DEALER on an OS-chosen TCP port; returns its endpoint."""
+        """Bind the direct-arm DEALER; returns its endpoint.  With a loopback session (every
+        sender on this host) a Unix-domain socket, which delivers an arm in about half the time
+        of a TCP loopback connection; otherwise an OS-chosen TCP port."""
         from .session import host_address
         loopback = master_address in ("127.0.0.1", "localhost", "::1")
         sock = self._ctx.socket(zmq.DEALER)
         sock.setsockopt(zmq.LINGER, 0)
         sock.setsockopt(zmq.IDENTITY, f"wbarm-{self.global_rank}".encode())
-        port = sock.bind_to_random_port("tcp://127.0.0.1" if loopback else "tcp://*")
         self._arm_sock = sock
         self._poller.register(sock, zmq.POLLIN)
-        return f"tcp://{'127.0.0.1' if loopback else host_address()}:{port}"
+        if loopback:
+            self._arm_path = os.path.join(tempfile.gettempdir(), f"wbridge-arm-{os.getpid()}-{uuid.uuid4().hex[:12]}")
+            endpoint = f"ipc://{self._arm_path}"
+            sock.bind(endpoint)
+            return endpoint
+        port = sock.bind_to_random_port("tcp://*")
+        return f"tcp://{host_address()}:{port}"
 
     def _open_watch(self, master_address: str):
         """Accept the senders' liveness connections (``control/liveness.py``)."""
@@ -364,6 +374,12 @@ class WeightReceiver:
             except KeyError:
                 pass
             sock.close(0)
+        path, self._arm_path = self._arm_path, None
+        if path:
+            try:
+                os.unlink(path)
+            except OSError:
+                pass
 
     def _on_scheduler(self, sock, msg: dict) -> None:
         if msg.get("type") != UPDATE_REQUEST:
