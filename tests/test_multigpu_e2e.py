@@ -137,3 +137,15 @@ def test_nvls_fanout_two_pipeline_stages_two_replicas():
     rep = run_fanout("tiny-llama", "nvls", [dict(tp=1, pp=2, pp_rank=0), dict(tp=1, pp=2, pp_rank=1)], dict(tp=1),
                      ["cuda:0", "cuda:1"], ["cuda:2", "cuda:3"])
     assert all(r["mc_groups"] == 1 and r["mc_items"] > 0 for r in rep.values())
+
+
+def test_nvls_fanout_sender_on_a_replica_gpu():
+    """Two GPUs: the sender shares GPU 0 with one replica (whose pool backs that device's share
+    of the multicast object), the other replica is on GPU 1; both verify bit for bit."""
+    _need(2)
+    from tests.e2e_harness import run_fanout
+    from weightbridge_b200.parallel.nvls import nvls_supported
+    if not nvls_supported(0):
+        pytest.skip("no NVLink multicast on this machine")
+    rep = run_fanout("tiny-llama", "nvls", [dict(tp=1)], dict(tp=1), ["cuda:0"], ["cuda:0", "cuda:1"])
+    assert rep[0]["mc_groups"] == 1 and rep[0]["mc_items"] > 0

@@ -472,7 +472,8 @@ class WeightSender:
     # -- NVLink multicast (mode "nvls") --------------------------------------------------------
     def _setup_multicast(self, sess: Session, info: dict, assignment: dict) -> None:
         """Rank 0 finds replica groups and creates one multicast object per group; every
-        sender of a group adds its device, backs the object with a scratch pool and maps it."""
+        sender of a group adds its device and backs the object with scratch (unless a replica on
+        its GPU already does), then maps it."""
         from ..parallel.nvls import McMember, nvls_supported, replica_groups
         cfg = self.config
         self._mc: dict[int, tuple] = {}
@@ -489,20 +490,24 @@ class WeightSender:
             for gid, reps in enumerate(replica_groups(allinfo)):
                 senders = [s for s, rs in plan.items()
                            if all(r in rs for r in reps) and all(rs[r] == rs[reps[0]] for r in reps)]
-                members = [allinfo[r]["device"] for r in reps] + [self._sender_devices[s] for s in senders]
-                devs = set(members)
-                if not senders or not nvls_supported(dev0) or len(devs) != len(members):
+                # a sender on a replica's GPU shares that device's membership (the replica's pool
+                # backs it); every other member needs a GPU of its own
+                rep_devs = [allinfo[r]["device"] for r in reps]
+                colocated = [s for s in senders if self._sender_devices[s] in rep_devs]
+                extra = [self._sender_devices[s] for s in senders if s not in colocated]
+                distinct = len(set(rep_devs)) == len(rep_devs) and len(set(extra)) == len(extra)
+                if not senders or not nvls_supported(dev0) or not distinct:
                     logger.warning("replica group %s goes unicast: %s", reps,
                                    "no sender writes the same entries to all of it" if not senders else
-                                   "two members share a GPU" if len(devs) != len(members) else
-                                   "the GPU reports no NVLink multicast")
+                                   "two replicas, or two senders off the replicas, share a GPU" if not distinct
+                                   else "the GPU reports no NVLink multicast")
                     continue
                 size = int(allinfo[reps[0]]["pool"]["size"])
                 m = McMember(gid, size, dev0)
-                m.create(num_devices=len(devs))
+                m.create(num_devices=len(rep_devs) + len(extra))
                 self._mc_created.append(m)
-                groups.append({"id": gid, "replicas": reps, "senders": senders, "size": size,
-                               "addr": m.server.address})
+                groups.append({"id": gid, "replicas": reps, "senders": senders, "colocated": colocated,
+                               "size": size, "addr": m.server.address})
             sess.set_json("nvls/plan", {"groups": groups})
         plan = sess.get_json("nvls/plan", cfg.connect_timeout_s)
         dev = torch.cuda.current_device()
@@ -514,12 +519,15 @@ class WeightSender:
             self._mc[g["id"]] = (m, g)           # tracked from here on: teardown undoes every stage
             if creator is None:
                 m.join(g["addr"])
-            m.add_device()
+            shared = self.rank in g.get("colocated", [])      # a replica on this GPU backs the object
+            if not shared:
+                m.add_device()
             sess.set(f"nvls/{g['id']}/added/{self.rank}", "1")
             members = g["replicas"] + g["senders"]
             sess.wait_checked([f"nvls/{g['id']}/added/{x}" for x in members], cfg.connect_timeout_s,
                               "multicast members to add their devices")
-            m.bind_scratch()
+            if not shared:
+                m.bind_scratch()
             sess.set(f"nvls/{g['id']}/bound/{self.rank}", "1")
             sess.wait_checked([f"nvls/{g['id']}/bound/{x}" for x in members], cfg.connect_timeout_s,
                               "multicast members to bind memory")
