@@ -10,6 +10,8 @@ Configurations (strong scaling: the model, hence the bytes moved per sync, is fi
                      processes); N=2: TP1 -> TP1; N=4: TP2 -> TP2; N=8: TP4 -> TP4 (disaggregated)
   llama8b-fanout     Llama-3-8B, trainer TP2 x PP2 -> 4 rollout replicas at TP1 (N=8);
                      N=2: TP1 -> 1 replica, N=4: PP2 -> 2 replicas
+  llama8b-broadcast  Llama-3-8B, one trainer GPU at TP1 -> N-1 rollout replicas at TP1 (replicas
+                     outnumber senders: the case NVLink multicast, --transfer nvls, is for)
   qwen3-moe-fp8      Qwen3-30B-A3B, trainer EP4 -> rollout TP4 (EP4 experts), experts quantised
                      to fp8 e4m3 with 128x128 fp32 block scales in the transfer kernel (N=8)
   qwen3-moe-fp8-etp  the same with trainer expert TP 4 instead of EP (192-row expert slices): every
@@ -50,7 +52,7 @@ def parse(argv=None):
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--config", default="llama8b",
-                   choices=["llama8b", "llama8b-fanout", "qwen3-moe-fp8", "qwen3-moe-fp8-etp",
+                   choices=["llama8b", "llama8b-fanout", "llama8b-broadcast", "qwen3-moe-fp8", "qwen3-moe-fp8-etp",
                             "llama70b-colocated", "deepseek-lite-fp8"])
     p.add_argument("--impl", default="wbridge", choices=["wbridge", "reference", "torch-p2p"],
                    help="torch-p2p: the reference's algorithm (per-box torch copies + NCCL isend/irecv)")
@@ -137,6 +139,12 @@ def scenario(config: str, n: int) -> tuple[str, list[Role], str]:
         reps = n - tp * pp
         roles += [Role("rollout", tp * pp + j, dict(tp=1), j, 0, True) for j in range(reps)]
         return "llama3-8b", roles, f"tp{tp}xpp{pp} -> {reps} replicas x tp1 (fan-out)"
+    if config == "llama8b-broadcast":
+        if n < 2:
+            raise SystemExit("llama8b-broadcast runs on 2 or more GPUs")
+        roles = [Role("trainer", 0, dict(tp=1))]
+        roles += [Role("rollout", j + 1, dict(tp=1), j, 0, True) for j in range(n - 1)]
+        return "llama3-8b", roles, f"tp1 -> {n - 1} replicas x tp1 (one sender, fan-out)"
     if config == "qwen3-moe-fp8":
         if n not in (2, 4, 8):
             raise SystemExit("qwen3-moe-fp8 runs on 2, 4 or 8 GPUs")
@@ -178,18 +186,66 @@ def _measured_peaks() -> dict:
         return {}
 
 
-def _roofline(value_gbs: float, links: float, colocated: bool, bytes_read: float, payload: float, ms: float) -> dict:
-    """Achieved fraction of the resource that bounds the sync: HBM copy bandwidth when every
-    transfer stays on one GPU (reads + writes), else NVLink per active link (measured peer copy)."""
-    if colocated and links <= 1:
+def _link_bytes(routes: list[dict]) -> tuple[dict, dict, dict, int]:
+    """Per-GPU NVLink bytes of one sync: unicast egress, multicast egress, ingress, and the bytes
+    that stay on one GPU.  A unicast route to its own GPU stays in HBM; a multicast store leaves
+    its sender's GPU once and the NVSwitch delivers it to every replica's GPU (its own included)."""
+    egress: dict[int, int] = {}
+    mc_egress: dict[int, int] = {}
+    ingress: dict[int, int] = {}
+    local = 0
+    for r in routes:
+        n, src = int(r["bytes"]), int(r["src"])
+        remote = list(r["dst"]) if r["multicast"] else [d for d in r["dst"] if d != src]
+        local += n * (len(r["dst"]) - len(remote))
+        if not remote:
+            continue
+        if r["multicast"]:
+            mc_egress[src] = mc_egress.get(src, 0) + n
+        else:
+            egress[src] = egress.get(src, 0) + n * len(remote)
+        for d in remote:
+            ingress[d] = ingress.get(d, 0) + n
+    return egress, mc_egress, ingress, local
+
+
+def _roofline(routes: list[dict], bytes_read: float, payload: float, ms: float) -> dict:
+    """Achieved fraction of the resource that bounds the sync: HBM copy bandwidth (reads +
+    writes) when every byte stays on its GPU; otherwise ideal time / measured time, where the
+    ideal time is the busiest GPU's NVLink egress or ingress: unicast bytes at the measured
+    GPU -> GPU peak, multicast stores at the measured multicast store peak."""
+    egress, mc_egress, ingress, _local = _link_bytes(routes)
+    if not egress and not mc_egress:
         peak = float(_measured_peaks().get("hbm_gbs", 6650.0))
         achieved = (bytes_read + payload) / (ms / 1e3) / 1e9
         return {"bound": "hbm copy (read + write)", "peak_gbs": peak, "achieved_gbs": round(achieved, 1),
                 "fraction_of_measured": round(achieved / peak, 3)}
     peak, source = _peer_peak()
-    per_link = value_gbs / max(links, 1.0)
-    return {"bound": "nvlink, per sending link", "peak_gbs": peak, "peak_source": source,
-            "achieved_gbs": round(per_link, 1), "fraction_of_measured": round(per_link / peak, 3)}
+    mc_peak, mc_source = _mc_peak(peak)
+    times = [(("egress", d), egress.get(d, 0) / peak + mc_egress.get(d, 0) / mc_peak)
+             for d in set(egress) | set(mc_egress)]
+    times += [(("ingress", d), b / peak) for d, b in ingress.items()]
+    (side, dev), t = max(times, key=lambda x: x[1])          # seconds * 1e9 (bytes / (GB/s))
+    ideal_ms = t / 1e6
+    out = {"bound": f"nvlink, busiest GPU ({side} of GPU {dev})", "ideal_ms": round(ideal_ms, 4),
+           "peak_gbs": peak, "peak_source": source, "fraction_of_measured": round(ideal_ms / ms, 3),
+           "egress_gb": {str(d): round(b / 1e9, 3) for d, b in sorted(egress.items())},
+           "ingress_gb": {str(d): round(b / 1e9, 3) for d, b in sorted(ingress.items())}}
+    if mc_egress:
+        out.update({"multicast_egress_gb": {str(d): round(b / 1e9, 3) for d, b in sorted(mc_egress.items())},
+                    "multicast_peak_gbs": mc_peak, "multicast_peak_source": mc_source})
+    return out
+
+
+def _mc_peak(fallback: float) -> tuple[float, str]:
+    """Multicast store bandwidth out of one GPU (``multimem.st`` through the NVSwitch), measured
+    on B200s of this pool (profiles/nvlink_multicast_store_peak.json, written by
+    ``python -m weightbridge_b200.ops.microbench --case mc-peak``)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "nvlink_multicast_store_peak.json")) as f:
+            return float(json.load(f)["best_gbs"]), "measured: profiles/nvlink_multicast_store_peak.json"
+    except (OSError, KeyError, ValueError):
+        return fallback, "fallback: the GPU -> GPU peak (no profiles/nvlink_multicast_store_peak.json)"
 
 
 def _peer_peak() -> tuple[float, str]:
@@ -416,7 +472,9 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
         sprog = sender.program if (sender is not None and sender.program is not None) else None
         rprog = recv.pull_program if (recv is not None and recv.pull_program is not None
                                       and len(recv.pull_program.tables)) else None
-        payload = (sprog.bytes_written if sprog else 0) + (rprog.bytes_written if rprog else 0)
+        my_routes = (sender.routes() if sender is not None else []) + (recv.routes() if recv is not None else [])
+        # bytes landed in receivers: a multicast store counts once per replica it reaches
+        payload = sum(r["bytes"] * len(r["dst"]) for r in my_routes)
         read = (sprog.bytes_read if sprog else 0) + (rprog.bytes_read if rprog else 0)
         active = 1 if (sender is not None and sender.program is not None and len(sender.program.tables)) else 0
         active += 1 if (recv is not None and recv.pull_program is not None and len(recv.pull_program.tables)) else 0
@@ -462,6 +520,8 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                     if recv is not None and not args.no_e2e else {})
         mark_lists = [None] * nprocs
         dist.all_gather_object(mark_lists, my_marks)
+        route_lists = [None] * nprocs
+        dist.all_gather_object(route_lists, my_routes)
         chain = _sync_chain(mark_lists)
 
         if idx == 0:
@@ -488,8 +548,8 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
                            "direction": sender_direction if sender_direction else args.direction,
                            "multicast_groups_per_sender_max": int(G[:, 20].max())},
                 "latency_s": round(lat, 6),
-                "roofline": _roofline(value, float(G[:, 7].sum()), colocated=len({r.device for r in roles}) < len(roles),
-                                      bytes_read=float(G[:, 3].sum()), payload=payload_total, ms=ms),
+                "roofline": _roofline([r for rs in route_lists for r in rs], bytes_read=float(G[:, 3].sum()),
+                                      payload=payload_total, ms=ms),
                 "gbs_per_gpu": round(value / ngpu, 2),
                 "gbs_per_sender": round(value / max(1.0, float(G[:, 7].sum())), 2),
                 "e2e": None if args.no_e2e else {

@@ -21,6 +21,7 @@ from weightbridge_b200.parallel.megatron import MegatronLayout  # noqa: E402
 from weightbridge_b200.parallel.sglang import SGLangLayout  # noqa: E402
 
 CASES = [("llama8b", 1), ("llama8b", 2), ("llama8b", 4), ("llama8b", 8), ("llama8b-fanout", 8),
+         ("llama8b-broadcast", 4), ("llama8b-broadcast", 8),
          ("qwen3-moe-fp8", 8), ("qwen3-moe-fp8-etp", 8), ("llama70b-colocated", 8), ("deepseek-lite-fp8", 4),
          ("deepseek-lite-fp8", 8)]
 
@@ -55,11 +56,35 @@ def test_bench_scenario_is_consistent(config, n):
 def test_roofline_fractions():
     peak, source = bench._peer_peak()
     assert source.startswith("measured") and 700 < peak < 900     # profiles/nvlink_peer_peak.json
-    rf = bench._roofline(2 * peak, 2.0, colocated=False, bytes_read=7.7e9, payload=7.7e9, ms=5.0)
+    # two TP pairs: each sender's link carries peak * 5 ms worth of bytes
+    n = int(peak * 1e9 * 5e-3)
+    routes = [{"src": 0, "dst": [2], "bytes": n, "multicast": False}, {"src": 1, "dst": [3], "bytes": n, "multicast": False}]
+    rf = bench._roofline(routes, bytes_read=2 * n, payload=2 * n, ms=5.0)
     assert rf["bound"].startswith("nvlink") and rf["fraction_of_measured"] == 1.0
     hbm = bench._measured_peaks().get("hbm_gbs", 6650.0)
-    rf = bench._roofline(0.0, 1.0, colocated=True, bytes_read=hbm * 1e9 / 2, payload=hbm * 1e9 / 2, ms=1000.0)
+    local = [{"src": 0, "dst": [0], "bytes": int(hbm * 1e9 / 2), "multicast": False}]
+    rf = bench._roofline(local, bytes_read=hbm * 1e9 / 2, payload=hbm * 1e9 / 2, ms=1000.0)
     assert rf["bound"].startswith("hbm") and rf["fraction_of_measured"] == 1.0
+
+
+def test_link_bytes_unicast_fanout_and_multicast():
+    """One sender to three replicas: unicast leaves the sender's GPU three times, multicast
+    once; each replica's GPU takes the bytes in once either way; a route to the sender's own
+    GPU stays in HBM."""
+    uni = [{"src": 0, "dst": [d], "bytes": 10, "multicast": False} for d in (1, 2, 3)]
+    eg, mc, ing, local = bench._link_bytes(uni + [{"src": 0, "dst": [0], "bytes": 7, "multicast": False}])
+    assert eg == {0: 30} and mc == {} and ing == {1: 10, 2: 10, 3: 10} and local == 7
+    mcr = [{"src": 0, "dst": [1, 2, 3], "bytes": 10, "multicast": True}]
+    eg, mc, ing, local = bench._link_bytes(mcr)
+    assert eg == {} and mc == {0: 10} and ing == {1: 10, 2: 10, 3: 10} and local == 0
+    peak, _ = bench._peer_peak()
+    n = int(peak * 1e6)                      # 1 ms of the peer peak
+    rf = bench._roofline([dict(r, bytes=n) for r in uni], bytes_read=3 * n, payload=3 * n, ms=3.0)
+    assert "egress of GPU 0" in rf["bound"] and rf["fraction_of_measured"] == 1.0
+    # multicast egress is divided by the multicast store peak (at most the peer peak)
+    mc_peak, _ = bench._mc_peak(peak)
+    rf = bench._roofline([dict(mcr[0], bytes=n)], bytes_read=n, payload=3 * n, ms=1.0)
+    assert rf["multicast_peak_gbs"] == mc_peak and abs(rf["ideal_ms"] - peak / mc_peak) < 1e-3
 
 
 def test_reference_arm_prints_one_json_line():

@@ -93,6 +93,7 @@ class WeightReceiver:
         self._rebind_lock = threading.Lock()
         self._bound = False                           # tensors bound and exported for this session
         self._pull_versions, self._pull_prog, self._pull_imports = None, None, {}   # pull direction
+        self._pull_devices: dict[int, int] = {}      # GPU ordinal of each sender pulled from
         self._pull_stream = None
         self._pull_progs: dict = {}                   # pull programs by entry-subset digest
         self._pull_src: dict = {}
@@ -712,6 +713,7 @@ class WeightReceiver:
         for imp in self._pull_imports.values():
             imp.close()
         self._pull_imports, self._pull_src, self._pull_ranges = {}, {}, []
+        self._pull_devices = {}
         self._pull_progs = {}
         for s in self.expected:
             sb = self.session.get_json(f"sendbind/{s}", self.config.sync_timeout_s)
@@ -722,6 +724,7 @@ class WeightReceiver:
                 raise ReceiveError(f"sender {s} holds host memory in another process")
             imp = ImportTable(sb["allocs"], same_process=same)
             self._pull_imports[s] = imp
+            self._pull_devices[s] = int(sb.get("device", -1))
             sphys = PhysBinding.from_json(sb["binding"])
             self._pull_src[s] = sphys
             if sb["allocs"]:
@@ -737,20 +740,27 @@ class WeightReceiver:
         from ..core.plan import storage_ranges, validate_tables
         from ..ops.executor import HostProgram, LaunchConfig, TransferProgram
         from .sender import _interleave
-        parts = []
+        parts, routes = [], []
+        me = self.device.index if self.device.type == "cuda" else -1
         for s in self.expected:
             mine = self._names[s] if names is None else [n for n in self._names[s] if n in names]
             ops = [o for o in plan_pair(self._pull_src[s], self._rphys_abs, names=mine)
                    if o.kind not in ("quant", "squant")]
             parts.append(lower_ops(ops, self._pull_imports[s].base, lambda a: 0, item_bytes=self.config.item_bytes))
+            if parts[-1].bytes_written:
+                routes.append({"src": self._pull_devices.get(s, -1), "dst": [me], "bytes": int(parts[-1].bytes_written),
+                               "multicast": False})
         # round-robin over the senders, so the CTAs running at any moment load from every
         # sender at once (one sender after the other would leave all but one egress idle)
         tables = _interleave(parts)
         if self.config.validate_plan:
             validate_tables(tables, self._pull_ranges, storage_ranges(self.state_dict.values()))
         if self.device.type == "cpu":
-            return HostProgram(tables)
-        return TransferProgram(tables, self.device, [], LaunchConfig(mode=self.config.kernel_mode), local_flag=True)
+            prog = HostProgram(tables)
+        else:
+            prog = TransferProgram(tables, self.device, [], LaunchConfig(mode=self.config.kernel_mode), local_flag=True)
+        prog.routes = routes
+        return prog
 
     def launch(self, stream: torch.cuda.Stream | None = None) -> None:
         """Pull direction: enqueue this worker's pull kernel on ``stream`` with no handshake
@@ -768,6 +778,11 @@ class WeightReceiver:
     @property
     def pull_program(self):
         return self._pull_prog
+
+    def routes(self) -> list[dict]:
+        """Where the current pull program's bytes come from: one record per sender, with the
+        GPU ordinals on both ends."""
+        return list(getattr(self._pull_prog, "routes", [])) if self._pull_prog is not None else []
 
     # -- NVLink multicast (mode "nvls") -----------------------------------------------------
     def _join_nvls_export(self, binding, info: dict, W: int) -> None:
@@ -822,6 +837,10 @@ class WeightReceiver:
             if self.session is not None:
                 self.session.wait([f"nvls/{g['id']}/unmapped/{x}" for x in g["senders"]],
                                   self.config.connect_timeout_s, "senders to unmap the multicast object")
+        except SessionTimeout as e:
+            # the store lives in sender rank 0, which closes it only after every sender of every
+            # group it created reported the unmap (or its own bounded wait for that ended)
+            logger.warning("receiver %d: multicast teardown without the senders' unmap keys: %s", self.rank, e)
         finally:
             m.teardown_binding()
             self._mc = None

@@ -154,6 +154,7 @@ class WeightSender:
         self.history: list[SyncStats] = []
         self._program = None
         self._program_key = None
+        self._routes: list[tuple[list[int], int]] = []   # (receivers one store reaches, bytes) of the program
         self._progs: dict[tuple, tuple] = {}        # compiled programs by (bound tensors, entry subset)
         self._imports: dict[int, Any] = {}
         self._rinfo: dict[int, dict] = {}
@@ -558,9 +559,25 @@ class WeightSender:
                                  self.rank, g["id"])
             finally:
                 m.teardown_binding()
+        plan = {}
+        if self._mc_created and sess is not None:
+            try:
+                plan = {g["id"]: g for g in sess.get_json("nvls/plan", 1.0)["groups"]}
+            except Exception:
+                logger.exception("sender %d: multicast plan unreadable at teardown", self.rank)
         for m in self._mc_created:
             if all(m is not x for x, _g in mc.values()):
-                m.teardown_binding()
+                # created here, written by others: the store (held by this rank) stays up until
+                # they unmapped, so the replicas can read the same keys before they unbind
+                g = plan.get(m.group)
+                try:
+                    if g is not None:
+                        sess.wait([f"nvls/{g['id']}/unmapped/{x}" for x in g["senders"]], self.config.connect_timeout_s)
+                except Exception:
+                    logger.exception("sender %d: multicast group %d: waiting for its senders to unmap", self.rank,
+                                     m.group)
+                finally:
+                    m.teardown_binding()
         self._mc, self._mc_created = {}, []
 
     def _resolve_bindings(self, ready: dict[int, bytes]) -> bool:
@@ -625,6 +642,7 @@ class WeightSender:
     def _compile(self, state_dict, subset: frozenset | None = None) -> None:
         """Compile the push program for ``state_dict`` (entries restricted to ``subset``)."""
         cfg = self.config
+        self._routes = []
         if not self.targets:
             self._program = None
             return
@@ -643,6 +661,7 @@ class WeightSender:
             self._published_key = self._key(state_dict)
         parts, flags, dst_ranges = [], [], []
         covered: set[int] = set()
+        routes: list[tuple[list[int], int]] = []
         for m, g in self._mc.values():
             reps = g["replicas"]
             rep = reps[0]
@@ -652,12 +671,15 @@ class WeightSender:
             mc_base = lambda a, va=m.va: va
             mc_ops = [o for o in ops if multicast_ok(o, src_base, mc_base)]
             uni_ops = [o for o in ops if not multicast_ok(o, src_base, mc_base)]
-            parts.append(lower_ops(mc_ops, src_base, mc_base, item_bytes=cfg.item_bytes, multicast=True))
+            mct = lower_ops(mc_ops, src_base, mc_base, item_bytes=cfg.item_bytes, multicast=True)
+            parts.append(mct)
+            routes.append((list(reps), mct.bytes_written))     # one multimem store reaches every replica
             dst_ranges.append((m.va, m.va + m.size))
             for r in reps:
                 info, imp = self._rinfo[r], self._imports[r]
                 if uni_ops:          # casts, quantised blocks, unaligned copies: one store per replica
                     parts.append(lower_ops(uni_ops, src_base, imp.base, item_bytes=cfg.item_bytes, receiver=r))
+                    routes.append(([r], parts[-1].bytes_written))
                 dst_ranges += [(imp.base(i), imp.base(i) + int(a["size"])) for i, a in enumerate(info["allocs"])]
             # the replicas' pools are laid out alike, flag words included: one multicast release
             # store (bit 0 marks the address as multicast) reaches every replica's word
@@ -687,6 +709,7 @@ class WeightSender:
             if pull:                       # receivers load the copies; quantised blocks stay pushed
                 ops = [o for o in ops if o.kind in ("quant", "squant")]
             parts.append(lower_ops(ops, src_base, imp.base, item_bytes=cfg.item_bytes, receiver=r))
+            routes.append(([r], parts[-1].bytes_written))
             falloc, foff, _w = info["flags"]
             flags.append(imp.base(falloc) + foff + 8 * self.rank)
             if info["allocs"]:
@@ -694,6 +717,7 @@ class WeightSender:
             else:                          # host memory of this process: the bound regions themselves
                 dst_ranges += _phys_extents(rphys) + [(foff, foff + 8 * int(_w))]
         tables = _interleave(parts)
+        self._routes = routes
         self._piece_pos = self._positions(tables)
         if cfg.validate_plan:
             validate_tables(tables, storage_ranges(state_dict.values()), dst_ranges)
@@ -716,7 +740,8 @@ class WeightSender:
 
     def _publish_sender_memory(self, binding, device) -> None:
         """Pull direction: export this sender's parameter memory for its receivers."""
-        info = {"version": self._bind_version, "pid": os.getpid(), "host": socket.gethostname()}
+        info = {"version": self._bind_version, "pid": os.getpid(), "host": socket.gethostname(),
+                "device": device.index if device.type == "cuda" else -1}
         if device.type == "cuda":
             from ..parallel.ipc import ExportTable
             export = ExportTable(device)
@@ -797,11 +822,11 @@ class WeightSender:
         hit = self._progs.pop(key, None)
         if hit is None:
             self._compile(state_dict, subset)
-            hit = (self._program, self._piece_pos)
+            hit = (self._program, self._piece_pos, self._routes)
         self._progs[key] = hit
         while len(self._progs) > 4:
             self._progs.pop(next(iter(self._progs)))
-        self._program, self._piece_pos = hit
+        self._program, self._piece_pos, self._routes = hit
         self._program_key = key
 
     def _positions(self, tables: Tables) -> np.ndarray:
@@ -845,6 +870,21 @@ class WeightSender:
     def program(self):
         """The compiled transfer program (tables, grid, byte counts), once compiled."""
         return self._program
+
+    @property
+    def delivered_bytes(self) -> int:
+        """Bytes the compiled push program lands in receivers per sync: a multicast store
+        counts once per replica it reaches."""
+        return sum(n * len(rs) for rs, n in self._routes) if self._program is not None else 0
+
+    def routes(self) -> list[dict]:
+        """Where the compiled push program's bytes go: one record per receiver (unicast) or per
+        replica group (multicast), with the GPU ordinals on both ends."""
+        if self._program is None:
+            return []
+        src = self._program.device.index if self._program.device.type == "cuda" else -1
+        return [{"src": src, "dst": [int(self._rinfo[r].get("device", -1)) for r in rs], "bytes": int(n),
+                 "multicast": len(rs) > 1} for rs, n in self._routes if n]
 
     def _arm(self, epoch: int) -> threading.Thread | None:
         """Arm sync ``epoch`` on every receiver worker (rank 0 only).  A failed arm is written

@@ -3,6 +3,7 @@
   python -m weightbridge_b200.ops.microbench --case copy  --gbytes 1 --mode 1
   python -m weightbridge_b200.ops.microbench --case quant --gbytes 1
   python -m weightbridge_b200.ops.microbench --case strided --gbytes 1
+  python -m weightbridge_b200.ops.microbench --case mc-peak --gbytes 2 --members 4   # >= 2 GPUs
 
 copy:    one contiguous bf16 buffer -> another (HBM read + write), 16-byte aligned;
 strided: column block of a row-major matrix -> contiguous (TP column split), 2-D items;
@@ -190,11 +191,83 @@ def peer_peak(gbytes: float, iters: int, warmup: int, item_bytes: int) -> dict:
     return out
 
 
+def mc_peak(gbytes: float, iters: int, warmup: int, item_bytes: int, members: int) -> dict:
+    """NVLink multicast store bandwidth out of GPU 0: one multicast object backed by a VMM
+    allocation on each of ``members`` GPUs (GPU 0 included), all in this process; the transfer
+    kernel on GPU 0 copies a local buffer to the object's address with ``multimem.st`` (OP_COPY_MC
+    items, vector mode), so every member receives the bytes once.  Best launch of ``iters``,
+    CUDA events, clocks sampled.  Beside it, the same kernel pushing plain copies to each other
+    member in turn (unicast fan-out).  Every member is verified.  The multicast figure is the
+    roofline denominator of a sender's multicast egress in the benchmark.
+
+    One process holds every member, so no process can exit while another's memory is bound;
+    the object is unmapped and unbound before the process ends, failure or not."""
+    from ..parallel.vmm import VmmPool
+    from ..utils.timing import ClockSampler
+    from ._ext import ext
+    k = min(members, torch.cuda.device_count())
+    if k < 2:
+        raise SystemExit("mc-peak needs two GPUs")
+    if not all(ext().multicast_supported(d) for d in range(k)):
+        raise SystemExit("a GPU reports no NVLink multicast")
+    d0 = torch.device("cuda", 0)
+    for d in range(1, k):
+        with torch.cuda.device(0):
+            ext().enable_peer_access(d)
+    want = int(gbytes * (1 << 30))
+    pools = [VmmPool(want, d, tail_bytes=0) for d in range(k)]
+    size = pools[0].size
+    out = {"bytes": size, "members": k, "iters": iters, "warmup": warmup}
+    h, bound, va = ext().mc_create(size, k), [], None
+    try:
+        for d in range(k):
+            ext().mc_add_device(h, d)
+        for d in range(k):
+            ext().mc_bind_mem(h, 0, pools[d].handle, 0, size)
+            bound.append(d)
+        va = ext().mc_map(h, size, 0)[0]
+        n = size // 2
+        a = torch.randn(n, device=d0, dtype=torch.bfloat16)
+        ops = [Op("copy", "x", (-1, a.data_ptr()), (-1, 0), [n], [1], [1], a.dtype, a.dtype)]
+        mc_tables = lower_ops(ops, lambda x: 0, lambda x: va, item_bytes=item_bytes, multicast=True)
+        uc_tables = lower_ops([Op("copy", "x", (-1, a.data_ptr()), (-1, pools[d].ptr), [n], [1], [1], a.dtype, a.dtype)
+                               for d in range(1, k)], lambda x: 0, lambda x: 0, item_bytes=item_bytes)
+        with ClockSampler() as clk, torch.cuda.device(d0):
+            s0 = torch.cuda.current_stream(d0)
+            mc = TransferProgram(mc_tables, d0, [], LaunchConfig(mode=0))
+            out["multicast_ms"] = _time_ms(lambda: mc.launch(0, s0, signal=False), iters, warmup, s0)
+            assert mc.read_status() == 0, mc.read_status()
+            torch.cuda.synchronize()
+            ok = [torch.equal(pools[d].tensor[: a.nbytes].view(torch.bfloat16).to(d0), a) for d in range(k)]
+            uc = TransferProgram(uc_tables, d0, [], LaunchConfig(mode=1))
+            out["unicast_fanout_ms"] = _time_ms(lambda: uc.launch(0, s0, signal=False), iters, warmup, s0)
+            assert uc.read_status() == 0, uc.read_status()
+        out["verified_members"] = ok
+        out["multicast_egress_gbs"] = round(a.nbytes / (out["multicast_ms"] / 1e3) / 1e9, 1)
+        out["unicast_fanout_egress_gbs"] = round(a.nbytes * (k - 1) / (out["unicast_fanout_ms"] / 1e3) / 1e9, 1)
+        out["best_gbs"] = out["multicast_egress_gbs"]
+        out["clocks"] = clk.summary()
+        out["device"] = torch.cuda.get_device_name(d0)
+        del mc, uc, a
+        torch.cuda.synchronize()
+    finally:
+        if va is not None:
+            ext().va_unmap(va, size)
+        for d in bound:
+            ext().mc_unbind(h, d, 0, size)
+        ext().mem_release(h)
+        for p_ in pools:
+            p_.free()
+    if not all(out.get("verified_members", [False])):
+        raise SystemExit(f"multicast copy mismatch: {out}")
+    return out
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--case", default="copy",
                    choices=["copy", "strided", "transpose", "quant", "split", "peer-push", "peer-pull", "peer-quant",
-                            "peer-peak"])
+                            "peer-peak", "mc-peak"])
     p.add_argument("--gbytes", type=float, default=1.0)
     p.add_argument("--mode", type=int, default=-1)
     p.add_argument("--piece", type=int, default=16384)
@@ -202,8 +275,16 @@ def main(argv=None):
     p.add_argument("--item-bytes", type=int, default=1 << 19)
     p.add_argument("--iters", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--out", default=None, help="peer-peak: also write the JSON result to this file")
+    p.add_argument("--out", default=None, help="peer-peak, mc-peak: also write the JSON result to this file")
+    p.add_argument("--members", type=int, default=4, help="mc-peak: GPUs in the multicast object")
     a = p.parse_args(argv)
+    if a.case == "mc-peak":
+        res = mc_peak(a.gbytes, a.iters, a.warmup, a.item_bytes, a.members)
+        print(json.dumps(res))
+        if a.out:
+            with open(a.out, "w") as f:
+                json.dump(res, f, indent=1)
+        return
     if a.case == "peer-peak":
         res = peer_peak(a.gbytes, a.iters, a.warmup, a.item_bytes)
         print(json.dumps(res))
