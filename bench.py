@@ -495,7 +495,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
         progs = [p for p in (sprog, rprog) if p is not None and len(p.tables)]
         items = max((len(p.tables.items) for p in progs), default=0)
         grid = max((p.grid() for p in progs), default=0)
-        kmode = max((p.config.mode for p in progs), default=-1)
+        kmode = max((getattr(p, "launch_mode", p.config.mode) for p in progs), default=-1)
         hist = sender.history[-args.steps:] if (sender is not None and not args.no_e2e) else []
         rphases = {}
         if recv is not None and not args.no_e2e:       # the worker's host steps during the e2e syncs

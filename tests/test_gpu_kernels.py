@@ -72,7 +72,7 @@ def test_gpu_layout_sync_bitwise(mode, model, meg, sgl):
             assert torch.equal(params[n], expected[n]), n
 
 
-@pytest.mark.parametrize("mode", [MODE_VECTOR, MODE_BULK8])
+@pytest.mark.parametrize("mode", MODES)
 def test_gpu_fp8_expert_quant_matches_oracle(mode):
     arch = get_arch("tiny-qwen3-moe")
     meg = [MegatronLayout(arch, ep=2, ep_rank=i) for i in range(2)]
@@ -83,23 +83,71 @@ def test_gpu_fp8_expert_quant_matches_oracle(mode):
             assert torch.equal(_u8(params[n]), _u8(expected[n])), n
 
 
-def test_gpu_quant_partial_blocks_and_fp32_source():
-    """Edge blocks (rows/cols not multiples of 128) and an fp32 source take the generic path."""
+def _quant_op(x, q, s):
+    n, k = x.shape
+    return Op("quant", "x", (-1, x.data_ptr()), (-1, q.data_ptr()), [n, k], [x.stride(0), 1], [q.stride(0), 1],
+              x.dtype, torch.float8_e4m3fn, (-1, s.data_ptr()), [s.stride(0), 1], (128, 128))
+
+
+def _quant_case(dev, src_dtype, n, k, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = (torch.randn(n, k, generator=g) * 3).to(src_dtype).to(dev)
+    q = torch.zeros(n, k, dtype=torch.float8_e4m3fn, device=dev)
+    s = torch.zeros((n + 127) // 128, (k + 127) // 128, dtype=torch.float32, device=dev)
+    return x, q, s
+
+
+def _check_quant(x, q, s):
+    qr, sr = block_quant_fp8_ref(x.cpu())
+    assert torch.equal(s.cpu(), sr)
+    assert torch.equal(q.cpu().view(torch.uint8), qr.view(torch.uint8))
+
+
+@pytest.mark.parametrize("mode", [MODE_VECTOR, MODE_BULK8, MODE_BULK4, MODE_BULK12])
+def test_gpu_quant_partial_blocks_and_fp32_source(mode):
+    """Edge blocks (rows/cols not multiples of 128), fp16 and fp32 sources, in every mode: in the
+    TMA modes bf16/fp16 matrices whose columns are a multiple of 8 arrive by tensor-map loads
+    (past-the-edge rows and columns read as zero), the others take the register path."""
     dev = torch.device("cuda", 0)
-    for src_dtype, (n, k) in [(torch.float32, (200, 300)), (torch.bfloat16, (130, 256)), (torch.float16, (64, 100))]:
-        x = (torch.randn(n, k, device=dev) * 3).to(src_dtype)
-        q = torch.zeros(n, k, dtype=torch.float8_e4m3fn, device=dev)
-        sn, sk = (n + 127) // 128, (k + 127) // 128
-        s = torch.zeros(sn, sk, dtype=torch.float32, device=dev)
-        op = Op("quant", "x", (-1, x.data_ptr()), (-1, q.data_ptr()), [n, k], [k, 1], [k, 1], src_dtype,
-                torch.float8_e4m3fn, (-1, s.data_ptr()), [sk, 1], (128, 128))
-        prog = TransferProgram(lower_ops([op], ABS, ABS), dev, [], LaunchConfig(mode=MODE_VECTOR))
+    cases = [(torch.float32, (200, 300), False), (torch.bfloat16, (130, 256), True), (torch.float16, (64, 100), False),
+             (torch.bfloat16, (257, 136), True), (torch.float16, (128, 384), True)]
+    for src_dtype, (n, k), tma in cases:
+        x, q, s = _quant_case(dev, src_dtype, n, k)
+        prog = TransferProgram(lower_ops([_quant_op(x, q, s)], ABS, ABS), dev, [], LaunchConfig(mode=mode))
+        nblocks = s.numel()
+        assert prog.n_tma_quant == (nblocks if tma and mode != MODE_VECTOR else 0), (src_dtype, n, k)
         prog.launch(1)
         torch.cuda.synchronize()
         assert prog.read_status() == 0
-        qr, sr = block_quant_fp8_ref(x.cpu())
-        assert torch.equal(s.cpu(), sr)
-        assert torch.equal(q.cpu().view(torch.uint8), qr.view(torch.uint8))
+        _check_quant(x, q, s)
+
+
+@pytest.mark.parametrize("mode", [MODE_BULK8, MODE_BULK4])
+def test_gpu_tma_quant_ring_wraps_and_mixes_with_register_blocks(mode):
+    """Two CTAs walk 128 TMA blocks each (the shared-memory ring of 2-4 stages wraps many times,
+    mbarrier parities flip) interleaved with register-path blocks of a matrix whose rows start
+    2 bytes off a 16-byte boundary, and with plain copies; three launches in a row."""
+    dev = torch.device("cuda", 0)
+    a, qa, sa = _quant_case(dev, torch.bfloat16, 1024, 4096, seed=1)          # 256 TMA blocks
+    buf = torch.zeros(300 * 257 + 1, dtype=torch.bfloat16, device=dev)
+    b = buf[1:].view(300, 257)[:, :256]                                         # misaligned rows: register path
+    b.copy_((torch.randn(300, 256) * 0.5).to(torch.bfloat16))
+    qb = torch.zeros(300, 256, dtype=torch.float8_e4m3fn, device=dev)
+    sb = torch.zeros(3, 2, dtype=torch.float32, device=dev)
+    c = torch.randn(4096, device=dev)
+    d = torch.zeros_like(c)
+    ops = [_quant_op(a, qa, sa), _quant_op(b, qb, sb),
+           Op("copy", "c", (-1, c.data_ptr()), (-1, d.data_ptr()), [4096], [1], [1], c.dtype, c.dtype)]
+    prog = TransferProgram(lower_ops(ops, ABS, ABS), dev, [], LaunchConfig(mode=mode, grid=2))
+    assert prog.n_tma_quant == 256 and prog.launch_mode == mode
+    for ep in range(1, 4):
+        qa.zero_(); sa.zero_(); qb.zero_(); sb.zero_(); d.zero_()
+        prog.launch(ep)
+        torch.cuda.synchronize()
+        assert prog.read_status() == 0
+        _check_quant(a, qa, sa)
+        _check_quant(b, qb, sb)
+        assert torch.equal(c, d)
 
 
 def _random_ops(rng, dev, count=12):

@@ -33,8 +33,11 @@ void check(cudaError_t e, const char* what) {
 
 void transfer(uint64_t items, uint32_t n_items, uint64_t bulk, uint32_t n_bulk, uint64_t qdescs, uint64_t qwork,
               uint32_t n_qwork, uint32_t piece_bytes, uint32_t spin_limit, uint64_t counter, uint64_t flags,
-              uint32_t n_flags, uint64_t epoch, uint64_t status, int mode, int grid, uint64_t stream) {
+              uint32_t n_flags, uint64_t epoch, uint64_t status, int mode, int grid, uint64_t stream,
+              uint64_t qmaps = 0, uint64_t qtma = 0) {
   if (mode == 0 && n_bulk) throw std::invalid_argument("bulk items need a TMA mode (1-3)");
+  if ((qmaps != 0) != (qtma != 0)) throw std::invalid_argument("quant tensor maps need their validity bytes");
+  if (qmaps % 64) throw std::invalid_argument("quant tensor maps must be 64-byte aligned");
   if (piece_bytes % 16) throw std::invalid_argument("piece_bytes must be a multiple of 16");
   wb::TransferArgs a{};
   a.items = P<const wb::Item>(items);
@@ -51,6 +54,8 @@ void transfer(uint64_t items, uint32_t n_items, uint64_t bulk, uint32_t n_bulk, 
   a.sig.n_flags = n_flags;
   a.sig.epoch = P<const uint64_t>(epoch);
   a.sig.status = P<uint32_t>(status);
+  a.qmaps = mode != 0 ? P<const uint8_t>(qmaps) : nullptr;      // the vector mode has no quant stages
+  a.qtma = mode != 0 ? P<const uint8_t>(qtma) : nullptr;
   if (a.sig.counter && !a.sig.epoch) throw std::invalid_argument("a completion signal needs an epoch word");
   check(wb::launch_transfer(a, mode, grid, reinterpret_cast<cudaStream_t>(stream)), "transfer launch");
 }
@@ -59,9 +64,9 @@ void transfer(uint64_t items, uint32_t n_items, uint64_t bulk, uint32_t n_bulk, 
 // and copy it to the device epoch word on `stream`, then launch the kernel with the completion
 // signal; with `epoch` < 0 launch without a signal.  `a` holds the program's fixed arguments:
 // (items, n_items, bulk, n_bulk, qdescs, qwork, n_qwork, piece_bytes, spin_limit, counter,
-//  flags, n_flags, epoch_dev, status, mode, grid, epoch_host).
+//  flags, n_flags, epoch_dev, status, mode, grid, epoch_host, qmaps, qtma).
 void transfer_launch(const py::tuple& a, int64_t epoch, uint64_t stream) {
-  if (a.size() != 17) throw std::invalid_argument("transfer_launch: 17 fixed arguments expected");
+  if (a.size() != 19) throw std::invalid_argument("transfer_launch: 19 fixed arguments expected");
   auto u = [&](size_t i) { return a[i].cast<uint64_t>(); };
   const bool sig = epoch >= 0;
   const auto st = reinterpret_cast<cudaStream_t>(stream);
@@ -71,7 +76,13 @@ void transfer_launch(const py::tuple& a, int64_t epoch, uint64_t stream) {
     check(cudaMemcpyAsync(reinterpret_cast<void*>(u(12)), host, 8, cudaMemcpyHostToDevice, st), "epoch copy");
   }
   transfer(u(0), (uint32_t)u(1), u(2), (uint32_t)u(3), u(4), u(5), (uint32_t)u(6), (uint32_t)u(7), (uint32_t)u(8),
-           sig ? u(9) : 0, u(10), sig ? (uint32_t)u(11) : 0, u(12), u(13), a[14].cast<int>(), a[15].cast<int>(), stream);
+           sig ? u(9) : 0, u(10), sig ? (uint32_t)u(11) : 0, u(12), u(13), a[14].cast<int>(), a[15].cast<int>(), stream,
+           u(17), u(18));
+}
+
+// Tensor maps of the quant descriptors (host arrays): returns how many qualified for the TMA path.
+uint32_t encode_quant_maps(uint64_t descs, uint32_t n, uint64_t maps, uint64_t valid) {
+  return wb::encode_quant_maps(P<const wb::QuantDesc>(descs), n, P<uint8_t>(maps), P<uint8_t>(valid));
 }
 
 // Synchronous read of `n` 8-byte words of device memory through a pinned host buffer.
@@ -215,7 +226,12 @@ py::tuple vmm_tuple(const wb::VmmAlloc& a) { return py::make_tuple(a.ptr, a.size
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "weightbridge_b200 native runtime: sm_100a transfer kernel, CPU executor, IPC/VMM/multicast";
-  m.def("transfer", &transfer, "launch the persistent transfer kernel");
+  m.def("transfer", &transfer, "launch the persistent transfer kernel", py::arg("items"), py::arg("n_items"),
+        py::arg("bulk"), py::arg("n_bulk"), py::arg("qdescs"), py::arg("qwork"), py::arg("n_qwork"),
+        py::arg("piece_bytes"), py::arg("spin_limit"), py::arg("counter"), py::arg("flags"), py::arg("n_flags"),
+        py::arg("epoch"), py::arg("status"), py::arg("mode"), py::arg("grid"), py::arg("stream"),
+        py::arg("qmaps") = 0, py::arg("qtma") = 0);
+  m.def("encode_quant_maps", &encode_quant_maps, "tensor maps of the quant descriptors the TMA path can load");
   m.def("transfer_launch", &transfer_launch, "epoch copy and transfer launch of one program, in one call");
   m.def("read_words", &read_words, "synchronous read of device words through a pinned buffer");
   m.def("wait_flags", &wait_flags, "launch a bounded wait on flag words");

@@ -5,6 +5,7 @@
 // so the extension links only against the CUDA runtime and imports on machines without a
 // GPU driver.
 #include "wb_ipc.h"
+#include "wb_driver.h"
 
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -21,31 +22,9 @@ void check_rt(cudaError_t e, const char* what) {
   if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-// The ABI version every entry point is requested at: the one of the cuda.h these typedefs
-// were written against.  (A symbol newer than the requested version - the multicast API is
-// 12.1 - is reported as not found.)
-constexpr unsigned kDriverAbi = CUDA_VERSION;
+using drv::entry;
 
-template <typename F>
-F entry(const char* name) {
-  void* fn = nullptr;
-  cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-  cudaError_t e = cudaGetDriverEntryPointByVersion(name, &fn, kDriverAbi, cudaEnableDefault, &q);
-  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
-    throw std::runtime_error(std::string("driver entry point unavailable: ") + name);
-  return reinterpret_cast<F>(fn);
-}
-
-void check_drv(CUresult r, const char* what) {
-  if (r == CUDA_SUCCESS) return;
-  using GetErr = CUresult (*)(CUresult, const char**);
-  const char* msg = nullptr;
-  try {
-    entry<GetErr>("cuGetErrorString")(r, &msg);
-  } catch (...) {
-  }
-  throw std::runtime_error(std::string(what) + ": CUresult " + std::to_string((int)r) + (msg ? std::string(" ") + msg : ""));
-}
+void check_drv(CUresult r, const char* what) { drv::check(r, what); }
 
 }  // namespace
 

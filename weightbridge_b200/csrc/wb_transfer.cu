@@ -6,7 +6,10 @@
 // Three kinds of work share the launch:
 //   * generic items  - 2-D strided copies / float casts, all threads, widest aligned vector;
 //   * quant blocks   - 128 x 128 bf16/fp16/fp32 -> e4m3 with an fp32 block scale, fused with
-//                      the (peer) store of the quantised block and its scale;
+//                      the (peer) store of the quantised block and its scale.  In the TMA
+//                      modes a block whose matrix has a tensor map arrives in shared memory
+//                      with one cp.async.bulk.tensor.2d load (a ring of 32 KiB stages, loads
+//                      issued ahead by one thread); others are loaded into registers;
 //   * bulk items     - 16-byte aligned copies moved by the TMA engine: one elected thread
 //                      streams pieces global -> shared (cp.async.bulk + mbarrier) and
 //                      shared -> destination (cp.async.bulk bulk_group), S stages deep.
@@ -23,11 +26,15 @@
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <cstdint>
+#include <cstring>
 
 #include "wb_common.h"
+#include "wb_driver.h"
 #include "wb_transfer.h"
 
 namespace wb {
+
+constexpr int kThreads = 256;     // threads per CTA of the transfer kernel
 
 // ------------------------------------------------------------------------------------
 // memory helpers
@@ -433,6 +440,57 @@ __device__ void quant_block(const QuantDesc& d, uint32_t block, float* red, uint
 }
 
 // ------------------------------------------------------------------------------------
+// quant blocks from shared memory (TMA modes): the 128 x 128 source block was loaded by one
+// tensor-map copy (rows at a 256-byte pitch; rows and columns past the matrix read as zero,
+// which leaves the amax unchanged).  Thread t holds elements [8c, 8c + 8) and [64 + 8c, 72 + 8c)
+// of rows t / 8 + 32k (c = t % 8): each quarter-warp reads 128 contiguous bytes, no bank
+// conflicts.  Same arithmetic as quant_block, so the output is identical.
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ void st8(void* p, uint2 v) {
+  asm volatile("st.global.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
+}
+
+__device__ void quant_block_smem(const QuantDesc& d, uint32_t block, const uint8_t* tile, float* red) {
+  const uint32_t nbc = (d.cols + 127u) / 128u;
+  const uint32_t br = block / nbc, bc = block - br * nbc;
+  const uint32_t r0 = br * 128u, c0 = bc * 128u;
+  const uint32_t nr = min(128u, d.rows - r0), nc = min(128u, d.cols - c0);
+  const bool bf16 = d.src_code == DT_BF16;
+  const uint32_t cc = threadIdx.x & 7u, rg = threadIdx.x >> 3;
+  uint4 v[4][2];
+  #pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint4* p = reinterpret_cast<const uint4*>(tile + (rg + 32u * k) * 256u + cc * 16u);
+    v[k][0] = p[0];
+    v[k][1] = p[8];
+  }
+  float amax = 0.f;
+  #pragma unroll
+  for (int k = 0; k < 4; ++k) amax = fmaxf(amax, fmaxf(amax8(v[k][0], bf16), amax8(v[k][1], bf16)));
+  // block max with one barrier: every warp posts its max, every thread folds the eight
+  // (the caller's barrier after the previous block guards `red` against reuse)
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31u) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  #pragma unroll
+  for (int w = 0; w < kThreads / 32; ++w) amax = fmaxf(amax, red[w]);
+  const float scale = amax > 0.f ? __fdiv_rn(amax, kE4M3Max) : 1.f;
+  const float inv = __frcp_rn(scale);
+  uint8_t* dst = reinterpret_cast<uint8_t*>(d.dst) + r0 * d.dst_pitch + c0;
+  #pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t r = rg + 32u * k;
+    if (r >= nr) continue;
+    uint8_t* row = dst + r * d.dst_pitch;
+    if (cc * 8u < nc) st8(row + cc * 8u, quant8(v[k][0], bf16, inv));
+    if (64u + cc * 8u < nc) st8(row + 64u + cc * 8u, quant8(v[k][1], bf16, inv));
+  }
+  if (threadIdx.x == 0)
+    *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(d.scale) + br * d.scale_pitch + bc * 4u) = scale;
+}
+
+// ------------------------------------------------------------------------------------
 // bulk items: TMA pipeline driven by one thread
 // ------------------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -562,6 +620,80 @@ __device__ void bulk_pipeline(const Item* items, uint32_t n_items, uint8_t* stag
 }
 
 // ------------------------------------------------------------------------------------
+// quant phase of the TMA modes: the dynamic shared memory is a ring of `qs` block stages.
+// Thread 0 keeps `qs` tensor-map loads in flight (the CTA's next TMA-eligible blocks, in the
+// order the consumers take them); all 256 threads wait on a stage's mbarrier, quantise it
+// from shared memory, and after a barrier thread 0 refills the stage.  Blocks without a valid
+// map take the register path in the same walk.  A wait that runs out of polls sets
+// ST_MBAR_TIMEOUT; the CTA then lets its loads in flight land (bounded) and skips its
+// remaining blocks.
+// ------------------------------------------------------------------------------------
+constexpr int kMaxQStages = 8;
+
+__device__ __forceinline__ void tma_load_2d(void* smem, const void* tmap, int32_t x, int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(smem)),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ void quant_tma_phase(const TransferArgs& a, uint8_t* smem, uint32_t qs, uint64_t* qbars, float* red) {
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < qs; ++s) mbar_init(&qbars[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  uint32_t pi = blockIdx.x, issued = 0;      // producer cursor (thread 0)
+  auto issue_next = [&]() {
+    while (pi < a.n_qwork) {
+      const QuantWork w = a.qwork[pi];
+      pi += gridDim.x;
+      if (!a.qtma[w.desc]) continue;
+      const uint32_t cols = a.qdescs[w.desc].cols;
+      const uint32_t nbc = (cols + 127u) / 128u;
+      const uint32_t br = w.block / nbc, bc = w.block - br * nbc;
+      const uint32_t s = issued % qs;
+      mbar_expect_tx(&qbars[s], kQBlockBytes);
+      tma_load_2d(smem + (size_t)s * kQBlockBytes, a.qmaps + (size_t)w.desc * 128u, (int32_t)(bc * 128u),
+                  (int32_t)(br * 128u), &qbars[s]);
+      ++issued;
+      return;
+    }
+  };
+  if (threadIdx.x == 0) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    for (uint32_t k = 0; k < qs; ++k) issue_next();
+  }
+  uint32_t consumed = 0;
+  for (uint32_t i = blockIdx.x; i < a.n_qwork; i += gridDim.x) {
+    const QuantWork w = a.qwork[i];
+    const QuantDesc d = a.qdescs[w.desc];
+    if (!a.qtma[w.desc]) {
+      quant_block(d, w.block, red, a.sig.status);
+      continue;
+    }
+    const uint32_t s = consumed % qs;
+    const bool ok = mbar_wait_bounded(&qbars[s], (consumed / qs) & 1u, a.mbar_spin_limit);
+    if (__syncthreads_or(!ok)) {
+      if (threadIdx.x == 0) {
+        if (a.sig.status) atomicOr(a.sig.status, ST_MBAR_TIMEOUT);
+        for (uint32_t k = consumed; k < issued; ++k) mbar_wait_bounded(&qbars[k % qs], (k / qs) & 1u, a.mbar_spin_limit);
+      }
+      __syncthreads();
+      return;
+    }
+    quant_block_smem(d, w.block, smem + (size_t)s * kQBlockBytes, red);
+    __syncthreads();                       // every thread is done reading stage s
+    if (threadIdx.x == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue_next();
+    }
+    ++consumed;
+  }
+}
+
+// ------------------------------------------------------------------------------------
 // completion signal
 // ------------------------------------------------------------------------------------
 __device__ void signal_done(const Signal& sg, uint32_t* s_last) {
@@ -589,7 +721,6 @@ __device__ void signal_done(const Signal& sg, uint32_t* s_last) {
 // ------------------------------------------------------------------------------------
 // kernels
 // ------------------------------------------------------------------------------------
-constexpr int kThreads = 256;
 
 template <bool BULK, int S, int KST>
 __global__ void __launch_bounds__(kThreads) transfer_kernel(TransferArgs a) {
@@ -600,15 +731,25 @@ __global__ void __launch_bounds__(kThreads) transfer_kernel(TransferArgs a) {
   __shared__ uint64_t bars[S > 0 ? S : 1];
   __shared__ uint64_t ring_dst[S > 0 ? S : 1];
   __shared__ uint32_t ring_bytes[S > 0 ? S : 1];
+  __shared__ uint64_t qbars[BULK ? kMaxQStages : 1];
 
   for (uint32_t i = blockIdx.x; i < a.n_items; i += gridDim.x) {
     const Item it = a.items[i];
     generic_item(it, tile, a.sig.status);
   }
-  for (uint32_t i = blockIdx.x; i < a.n_qwork; i += gridDim.x) {
-    const QuantWork w = a.qwork[i];
-    const QuantDesc d = a.qdescs[w.desc];
-    quant_block(d, w.block, red, a.sig.status);
+  uint32_t qs = 0;                          // quant stages in shared memory (TMA modes)
+  if constexpr (BULK) {
+    if (a.qmaps != nullptr && a.qtma != nullptr)
+      qs = min((uint32_t)kMaxQStages, (uint32_t)(((uint64_t)S * a.piece_bytes) / kQBlockBytes));
+  }
+  if (qs > 0 && a.n_qwork > 0) {
+    if constexpr (BULK) quant_tma_phase(a, dyn_smem, qs, qbars, red);
+  } else {
+    for (uint32_t i = blockIdx.x; i < a.n_qwork; i += gridDim.x) {
+      const QuantWork w = a.qwork[i];
+      const QuantDesc d = a.qdescs[w.desc];
+      quant_block(d, w.block, red, a.sig.status);
+    }
   }
   if constexpr (BULK) {
     if (a.n_bulk > 0 && threadIdx.x == 0)
@@ -678,6 +819,39 @@ cudaError_t launch_wait_flags(const uint64_t* flags, uint32_t n, const uint64_t*
                               uint32_t* status, uint32_t* where, cudaStream_t stream) {
   wait_flags_kernel<<<1, 32, 0, stream>>>(flags, n, epoch, timeout_ns, status, where);
   return cudaGetLastError();
+}
+
+uint32_t encode_quant_maps(const QuantDesc* descs, uint32_t n, uint8_t* maps, uint8_t* valid) {
+  using Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static Encode encode = drv::entry<Encode>("cuTensorMapEncodeTiled");
+  static_assert(sizeof(CUtensorMap) == 128, "tensor map size");
+  uint32_t ok = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    const QuantDesc& d = descs[i];
+    CUtensorMap* m = reinterpret_cast<CUtensorMap*>(maps + (size_t)i * 128u);
+    std::memset(m, 0, sizeof(CUtensorMap));
+    valid[i] = 0;
+    const bool fits = (d.src_code == DT_BF16 || d.src_code == DT_F16) && d.bn == 128 && d.bk == 128 && d.rows > 0 &&
+                      d.cols > 0 && d.cols % 8 == 0 && d.src % 16 == 0 && d.src_pitch > 0 && d.src_pitch % 16 == 0 &&
+                      (uint64_t)d.src_pitch >= 2ull * d.cols && (uint64_t)d.src_pitch < (1ull << 40) &&
+                      d.dst % 8 == 0 && d.dst_pitch % 8 == 0;
+    if (!fits) continue;
+    const cuuint64_t dims[2] = {d.cols, d.rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)d.src_pitch};
+    const cuuint32_t box[2] = {128u, 128u};
+    const cuuint32_t estr[2] = {1u, 1u};
+    const CUresult r = encode(m, d.src_code == DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                              2, reinterpret_cast<void*>(d.src), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_SUCCESS) {
+      valid[i] = 1;
+      ++ok;
+    }
+  }
+  return ok;
 }
 
 }  // namespace wb

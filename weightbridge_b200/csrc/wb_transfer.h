@@ -28,7 +28,21 @@ struct TransferArgs {
   uint32_t piece_bytes;        // TMA stage size (multiple of 16)
   uint32_t mbar_spin_limit;    // polls before an mbarrier wait gives up
   Signal sig;
+  // TMA-fed quantisation (TMA modes only; null: every block takes the register path):
+  // one 128-byte CUtensorMap per quant descriptor (64-byte aligned) and a byte per
+  // descriptor, 1 where that map is valid (encode_quant_maps)
+  const uint8_t* qmaps;
+  const uint8_t* qtma;
 };
+
+// Bytes of one 128 x 128 block of 16-bit source elements: a quant stage in shared memory.
+constexpr uint32_t kQBlockBytes = 128u * 128u * 2u;
+
+// Encode the tensor maps of the quant descriptors the TMA path can load (host): bf16 / fp16
+// sources, 128 x 128 blocks, 16-byte aligned source rows, 8-byte aligned destination rows,
+// columns a multiple of 8.  Writes maps[i] (128 bytes each) and valid[i]; returns how many
+// descriptors qualified.  Throws if the driver's encoder is unavailable.
+uint32_t encode_quant_maps(const QuantDesc* descs, uint32_t n, uint8_t* maps, uint8_t* valid);
 
 // mode 0: no TMA pipeline (bulk items must be empty); 1: 8 stages; 2: 12 stages; 3: 4 stages
 int bulk_stages(int mode);

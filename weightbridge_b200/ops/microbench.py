@@ -9,6 +9,7 @@ copy:    one contiguous bf16 buffer -> another (HBM read + write), 16-byte align
 strided: column block of a row-major matrix -> contiguous (TP column split), 2-D items;
 transpose: [heads, 128, 512] bf16 -> each matrix stored column-major (MLA's w_kc), OP_TRANSPOSE rows;
 quant:   bf16 [E, 768, 2048] expert stack -> fp8 e4m3 + 128x128 fp32 block scales;
+mixed:   half the bytes as the quant case, half as the copy case, in one program;
 split:   the same stack as split-block pieces (half of every block: rows 64-127 of each block
          row), quantised by split_quant with an amax from split_amax (pass timed on the host);
 peer-push / peer-pull / peer-quant (two GPUs, one process, peer access enabled): the kernel
@@ -79,6 +80,20 @@ def build(case: str, gbytes: float, dev, item_bytes: int):
         ops = [Op("quant", "x", (-1, a[i].data_ptr()), (-1, q[i].data_ptr()), [r, c], [c, 1], [c, 1], a.dtype,
                   q.dtype, (-1, s[i].data_ptr()), [c // 128, 1], (128, 128)) for i in range(e)]
         keep, traffic = (a, q, s), a.nbytes + q.nbytes + s.nbytes
+    elif case == "mixed":
+        # one program of both kinds, as a Qwen3-MoE sync to an fp8-expert rollout: half the source
+        # bytes are bf16 expert matrices quantised to e4m3, half a plain bf16 copy
+        r, c = 768, 2048
+        e = max(1, n // 2 // (r * c))
+        a = torch.randn(e, r, c, device=dev, dtype=torch.bfloat16)
+        q = torch.empty(e, r, c, device=dev, dtype=torch.float8_e4m3fn)
+        s = torch.empty(e, r // 128, c // 128, device=dev, dtype=torch.float32)
+        x = torch.randn(e * r * c, device=dev, dtype=torch.bfloat16)
+        y = torch.empty_like(x)
+        ops = [Op("quant", "x", (-1, a[i].data_ptr()), (-1, q[i].data_ptr()), [r, c], [c, 1], [c, 1], a.dtype,
+                  q.dtype, (-1, s[i].data_ptr()), [c // 128, 1], (128, 128)) for i in range(e)]
+        ops.append(Op("copy", "y", (-1, x.data_ptr()), (-1, y.data_ptr()), [x.numel()], [1], [1], x.dtype, x.dtype))
+        keep, traffic = (a, q, s, x, y), a.nbytes + q.nbytes + s.nbytes + 2 * x.nbytes
     elif case == "split":
         # expert-TP-like pieces: rows [64, 128) of every 128-row block row of a bf16 [E, 768, 2048]
         # stack (half of each block), one piece per 128 x 128 block, quantised with a given amax
@@ -266,7 +281,7 @@ def mc_peak(gbytes: float, iters: int, warmup: int, item_bytes: int, members: in
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--case", default="copy",
-                   choices=["copy", "strided", "transpose", "quant", "split", "peer-push", "peer-pull", "peer-quant",
+                   choices=["copy", "strided", "transpose", "quant", "mixed", "split", "peer-push", "peer-pull", "peer-quant",
                             "peer-peak", "mc-peak"])
     p.add_argument("--gbytes", type=float, default=1.0)
     p.add_argument("--mode", type=int, default=-1)
@@ -315,7 +330,8 @@ def main(argv=None):
     ms = e0.elapsed_time(e1) / a.iters
     gbs = traffic / (ms / 1e3) / 1e9
     peak = _peer_peak_gbs() if a.case.startswith("peer") else _peak_gbs()   # measured peer vs HBM copy
-    print(json.dumps({"case": a.case, "gbytes": a.gbytes, "mode": prog.config.mode, "piece": a.piece, "grid": prog.grid(),
+    print(json.dumps({"case": a.case, "gbytes": a.gbytes, "mode": prog.config.mode, "launch_mode": prog.launch_mode,
+                      "tma_quant_blocks": prog.n_tma_quant, "piece": a.piece, "grid": prog.grid(),
                       "items": len(tables.items), "qwork": len(tables.qwork), "pieces": len(tables.pieces),
                       "amax_pass_ms_host": round(amax_ms, 3) if prog.n_pieces else None, "ms": round(ms, 4),
                       "traffic_bytes": traffic, "gbs": round(gbs, 1),
