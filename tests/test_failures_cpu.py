@@ -300,6 +300,11 @@ def test_pull_direction_in_process():
             exp = ro.lay.allocate(dtype=torch.float32, fill=True, seed=step)
             assert all(torch.equal(ro.params[n], exp[n]) for n in exp), step
         assert ro.recv.pull_program is not None and len(ro.recv.pull_program.tables) > 0
+        # where the pulled bytes come from: one route per sender, summing to the program's stores
+        routes = ro.recv.routes()
+        assert len(routes) == 1 and not routes[0]["multicast"] and routes[0]["src"] == -1
+        assert sum(r["bytes"] for r in routes) == ro.recv.pull_program.bytes_written > 0
+        assert s.routes() == [] and s.delivered_bytes == 0            # the sender pushed nothing
         # other tensors (a second copy of the weights), then the first ones again: each switch
         # publishes the sender's memory anew and the receiver pulls from the right one
         params2 = lay.allocate(dtype=torch.float32, seed=7)
@@ -633,6 +638,11 @@ def test_push_alternating_tensor_sets_uses_cached_programs():
             th.join(20)
             exp = ro.lay.allocate(dtype=torch.float32, fill=True, seed=seed)
             assert all(torch.equal(ro.params[n], exp[n]) for n in exp), seed
+            # one unicast route per receiver, summing to the program's stores (kept with each
+            # cached program)
+            routes = s.routes()
+            assert len(routes) == 1 and routes[0]["dst"] == [-1] and not routes[0]["multicast"]
+            assert s.delivered_bytes == routes[0]["bytes"] == s.program.bytes_written > 0
         assert len(compiles) == 2
     finally:
         ro.close()
