@@ -266,6 +266,20 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+def _init_group(init: str, idx: int, nprocs: int, timeout_s: float = 300.0) -> None:
+    """The job's gloo group over every role process, on a TCPStore that process 0 serves at
+    ``init`` (tcp://host:port).  The store is made here rather than by a tcp:// init_method:
+    under torchrun (TORCHELASTIC_USE_AGENT_STORE=True) that method makes every rank a client
+    of a store nobody serves, when more processes than torchrun's ranks take part."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    host, port = init[len("tcp://"):].rsplit(":", 1)
+    store = dist.TCPStore(host, int(port), world_size=nprocs, is_master=(idx == 0),
+                          timeout=timedelta(seconds=timeout_s))
+    dist.init_process_group("gloo", store=store, rank=idx, world_size=nprocs,
+                            timeout=timedelta(seconds=timeout_s))
+
+
 def child_main(idx: int, port: int, nprocs: int, argv: list[str]):
     args = parse(argv)
     run_role(args, idx, nprocs, f"tcp://127.0.0.1:{port}")
@@ -332,7 +346,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
             print(f"[bench rank {idx}] {time.time() - t_start:7.1f}s {msg}", file=sys.stderr, flush=True)
 
     if init is not None:
-        dist.init_process_group("gloo", init_method=init, rank=idx, world_size=nprocs)
+        _init_group(init, idx, nprocs)
     model, roles, desc = scenario(args.config, args.gpus)
     phase("process group up")
     role = roles[idx]

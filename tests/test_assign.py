@@ -77,3 +77,33 @@ def test_replicas_and_expected_senders():
     assert expected_senders(plan, 2) == [0, 1]
     w_senders = [s for s in plan for r in plan[s] for n in plan[s][r] if n == "w"]
     assert sorted(w_senders) == [0, 1]      # the two copies of w spread over the two replicas
+
+
+def test_replica_consistent_assignment_serves_every_replica_alike():
+    """Multicast fan-out (Llama TP2 x PP2 -> 4 TP1 replicas): with ``replica_consistent`` every
+    sender writes the same entries to every replica (so one multicast store serves them all),
+    each replica still receives every entry exactly once, and TP-replicated entries (layer
+    norms) are still spread over the TP ranks.  Without it the per-replica balancing gives
+    replicas different sources for those entries."""
+    arch = get_arch("tiny-llama")
+    smetas = []
+    for pp in range(2):
+        for tp in range(2):
+            lay = MegatronLayout(arch, tp=2, pp=2, tp_rank=tp, pp_rank=pp)
+            smetas.append(_meta(lay, lay.param_shapes()))
+    rl = SGLangLayout(arch, tp=1)
+    rmetas = {4 + j: _meta(rl, {n: sh for n, (sh, _k) in rl.param_specs().items()}) for j in range(4)}
+    plan = assign_sources(smetas, rmetas, replica_consistent=True)
+    for s, rs in plan.items():
+        lists = [rs.get(r, []) for r in sorted(rmetas)]
+        assert all(x == lists[0] for x in lists), s
+    for r, meta in rmetas.items():
+        got = sorted(n for s in plan for n in plan[s].get(r, []))
+        # an entry split by TP arrives from both TP ranks of its stage, a replicated one from one
+        assert set(got) == set(meta.names())
+    norms = [n for n in rmetas[4].names() if "norm" in n]
+    owners = {n: [s for s in plan if n in plan[s].get(4, [])] for n in norms}
+    assert all(len(o) == 1 for o in owners.values())
+    assert len({o[0] for o in owners.values()}) > 2          # spread over both TP ranks of both stages
+    loose = assign_sources(smetas, rmetas)
+    assert any(len({tuple(rs.get(r, [])) for r in rmetas}) > 1 for rs in loose.values())

@@ -93,3 +93,32 @@ def test_reference_arm_prints_one_json_line():
     assert out.returncode == 0
     line = json.loads(out.stdout.strip().splitlines()[-1])
     assert line["impl"] == "reference" and ("unavailable" in line or "value" in line)
+
+
+def _join(init, idx, nprocs, q):
+    import os
+    os.environ["TORCHELASTIC_USE_AGENT_STORE"] = "True"       # what torchrun sets in every rank
+    import torch.distributed as dist
+    bench._init_group(init, idx, nprocs, timeout_s=30)
+    dist.barrier()
+    q.put(idx)
+    dist.destroy_process_group()
+
+
+def test_job_group_forms_with_more_processes_than_torchrun_ranks():
+    """The bench's job-wide group (16 processes on 8 torchrun ranks for the colocated 70B
+    layout) forms under torchrun's environment: process 0 serves the store itself."""
+    import multiprocessing as mp
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_join, args=(f"tcp://127.0.0.1:{port}", i, 3, q)) for i in range(3)]
+    for p in ps:
+        p.start()
+    got = sorted(q.get(timeout=60) for _ in ps)
+    for p in ps:
+        p.join(30)
+    assert got == [0, 1, 2] and all(p.exitcode == 0 for p in ps)

@@ -89,10 +89,11 @@ def _quant_op(x, q, s):
               x.dtype, torch.float8_e4m3fn, (-1, s.data_ptr()), [s.stride(0), 1], (128, 128))
 
 
-def _quant_case(dev, src_dtype, n, k, seed=0):
+def _quant_case(dev, src_dtype, n, k, seed=0, dst_pitch=None):
+    """A random [n, k] source and its e4m3 destination (rows ``dst_pitch`` bytes apart) + scales."""
     g = torch.Generator(device="cpu").manual_seed(seed)
     x = (torch.randn(n, k, generator=g) * 3).to(src_dtype).to(dev)
-    q = torch.zeros(n, k, dtype=torch.float8_e4m3fn, device=dev)
+    q = torch.zeros(n, dst_pitch or k, dtype=torch.float8_e4m3fn, device=dev)[:, :k]
     s = torch.zeros((n + 127) // 128, (k + 127) // 128, dtype=torch.float32, device=dev)
     return x, q, s
 
@@ -109,10 +110,13 @@ def test_gpu_quant_partial_blocks_and_fp32_source(mode):
     TMA modes bf16/fp16 matrices whose columns are a multiple of 8 arrive by tensor-map loads
     (past-the-edge rows and columns read as zero), the others take the register path."""
     dev = torch.device("cuda", 0)
-    cases = [(torch.float32, (200, 300), False), (torch.bfloat16, (130, 256), True), (torch.float16, (64, 100), False),
-             (torch.bfloat16, (257, 136), True), (torch.float16, (128, 384), True)]
-    for src_dtype, (n, k), tma in cases:
-        x, q, s = _quant_case(dev, src_dtype, n, k)
+    # (dtype, shape, TMA-eligible, destination row pitch): 16-byte destination rows take the
+    # 16-byte stores (also with a last block 8 columns wide), others 8-byte stores
+    cases = [(torch.float32, (200, 300), False, None), (torch.bfloat16, (130, 256), True, None),
+             (torch.float16, (64, 100), False, None), (torch.bfloat16, (257, 136), True, None),
+             (torch.float16, (128, 384), True, None), (torch.bfloat16, (200, 264), True, 272)]
+    for src_dtype, (n, k), tma, pitch in cases:
+        x, q, s = _quant_case(dev, src_dtype, n, k, dst_pitch=pitch)
         prog = TransferProgram(lower_ops([_quant_op(x, q, s)], ABS, ABS), dev, [], LaunchConfig(mode=mode))
         nblocks = s.numel()
         assert prog.n_tma_quant == (nblocks if tma and mode != MODE_VECTOR else 0), (src_dtype, n, k)
@@ -120,6 +124,9 @@ def test_gpu_quant_partial_blocks_and_fp32_source(mode):
         torch.cuda.synchronize()
         assert prog.read_status() == 0
         _check_quant(x, q, s)
+        if pitch:                      # the row padding past column k stays untouched
+            full = torch.as_strided(q, (n, pitch), (pitch, 1))
+            assert not full[:, k:].view(torch.uint8).any()
 
 
 @pytest.mark.parametrize("mode", [MODE_BULK8, MODE_BULK4])

@@ -34,3 +34,23 @@ def test_report_cli_json():
 def test_report_fsdp_trainer_counts_split_pieces():
     rep = report("tiny-llama-fp8", {"world": 3}, {"tp": 1, "quant": "fp8_linear"}, trainer_kind="fsdp")
     assert len(rep["senders"]) == 3 and sum(s["split_pieces"] for s in rep["senders"]) > 0
+
+
+def test_report_multicast_counts_copies_once_per_replica_group():
+    """One TP1 sender into three TP1 replicas: unicast leaves the sender three times, multicast
+    once (at the given multicast rate); every replica takes in the whole model either way."""
+    uni = report("tiny-llama", {"tp": 1}, {"tp": 1}, replicas=3, link_gbs=800.0)
+    mc = report("tiny-llama", {"tp": 1}, {"tp": 1}, replicas=3, link_gbs=800.0, multicast=True, mc_gbs=400.0)
+    model = uni["receivers"][0]["ingress_bytes"]
+    assert [r["ingress_bytes"] for r in mc["receivers"]] == [model] * 3
+    assert uni["senders"][0]["bytes_written"] == 3 * model and uni["senders"][0]["multicast_bytes"] == 0
+    assert mc["senders"][0]["multicast_bytes"] == model and mc["senders"][0]["bytes_written"] == 0
+    assert abs(uni["link_bound_ms"] - 3 * model / 800e6) < 1e-9
+    assert abs(mc["link_bound_ms"] - model / 400e6) < 1e-9          # egress at the multicast rate
+
+
+def test_report_multicast_pipeline_stages_all_multicast():
+    """TP2 x PP2 into four replicas: with the replica-consistent assignment every sender serves
+    its entries to all four by multicast (none falls back to per-replica stores)."""
+    rep = report("tiny-llama", {"tp": 2, "pp": 2}, {"tp": 1}, replicas=4, multicast=True, mc_gbs=500.0)
+    assert all(s["multicast_bytes"] > 0 and s["bytes_written"] == 0 for s in rep["senders"])

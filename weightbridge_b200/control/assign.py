@@ -60,17 +60,35 @@ def _overlap_bytes(s_shards, r_shards, itemsize: int) -> int:
     return n * itemsize
 
 
+def receiver_replicas(receiver_metas: dict[int, WeightData]) -> list[list[int]]:
+    """Receivers with identical metadata (rollout replicas of one layout), groups of two or more."""
+    by_key: dict[str, list[int]] = defaultdict(list)
+    for r in sorted(receiver_metas):
+        by_key[json.dumps(receiver_metas[r].to_jsonable(), sort_keys=True)].append(r)
+    return [g for g in by_key.values() if len(g) > 1]
+
+
 def assign_sources(sender_metas: list[WeightData], receiver_metas: dict[int, WeightData],
-                   load_balance: bool = True) -> dict[int, dict[int, list[str]]]:
+                   load_balance: bool = True, replica_consistent: bool = False) -> dict[int, dict[int, list[str]]]:
     """``plan[sender][receiver] = [entry names]`` (both as indices into the inputs).
 
     Two passes: entries only one replica group can serve are assigned first (their load is
     fixed), then replicated entries, largest first, each to the least-loaded member of its
     group (longest-processing-time greedy), so every sender ends with about the same bytes.
+
+    ``replica_consistent`` (multicast fan-out): receivers with identical metadata get each
+    replicated entry from the same sender, so every sender writes the same entries to every
+    replica of such a group and one multicast store can serve them all; the entry then costs
+    its sender one copy of the bytes, not one per replica.
     """
     groups = replica_groups(sender_metas)
     load = [0] * len(sender_metas)
     plan: dict[int, dict[int, list[str]]] = defaultdict(lambda: defaultdict(list))
+    replicas = {r: [r] for r in receiver_metas}
+    if replica_consistent:
+        for g in receiver_replicas(receiver_metas):
+            for r in g:
+                replicas[r] = g
     flexible: list[tuple[int, int, str, list[int]]] = []      # (bytes, receiver, name, group)
     for r in sorted(receiver_metas):
         rmeta = receiver_metas[r]
@@ -87,13 +105,14 @@ def assign_sources(sender_metas: list[WeightData], receiver_metas: dict[int, Wei
                     s = min(group)
                     load[s] += nbytes
                     plan[s][r].append(name)
-                else:
+                elif replicas[r][0] == r:      # a replica group's entry is placed once, for all of it
                     flexible.append((nbytes, r, name, group))
     flexible.sort(key=lambda t: (-t[0], t[1], t[2]))
     for nbytes, r, name, group in flexible:
         s = min(group, key=lambda x: (load[x], x))
         load[s] += nbytes
-        plan[s][r].append(name)
+        for rr in replicas[r]:
+            plan[s][rr].append(name)
     # keep each receiver's names in its metadata order (deterministic, cache friendly)
     order = {r: {n: i for i, n in enumerate(m.names())} for r, m in receiver_metas.items()}
     for s in plan:

@@ -360,7 +360,8 @@ class WeightSender:
         sess = self.session
         smeta_objs = [WeightData(m) for m in metas]
         rmeta_objs = {r: WeightData(m) for r, m in receivers.items()}
-        plan = assign_sources(smeta_objs, rmeta_objs, cfg.load_balance)
+        # multicast: every replica of a layout takes each entry from the same sender
+        plan = assign_sources(smeta_objs, rmeta_objs, cfg.load_balance, replica_consistent=cfg.mode == "nvls")
         sess.set_json("senders/meta", metas)
         sess.set("direction", session_direction(cfg, rmeta_objs.values()))
         sess.set("wire_chunk", str(int(cfg.wire_chunk_bytes)))      # receivers cut their wires alike
@@ -723,7 +724,7 @@ class WeightSender:
             validate_tables(tables, storage_ranges(state_dict.values()), dst_ranges)
             for f in flags:
                 _check_flag(f, dst_ranges)
-        from ..ops.executor import HostProgram, LaunchConfig, TransferProgram
+        from ..ops.executor import MODE_AUTO, MODE_VECTOR, HostProgram, LaunchConfig, TransferProgram
         if not len(tables):                # pull mode without quantised blocks: nothing to push
             self._program = None
             return
@@ -733,6 +734,14 @@ class WeightSender:
             self._program = HostProgram(tables, flags)
             return
         lc = LaunchConfig(mode=cfg.kernel_mode, piece_bytes=cfg.piece_bytes, grid=cfg.grid or None)
+        if (lc.mode == MODE_AUTO and len(tables.qwork)
+                and any(int(self._rinfo[r].get("device", -1)) != device.index for r in self.targets)):
+            # quant blocks stored into another GPU keep the register path (vector mode), the one
+            # measured end to end at 0.863 of the peer peak (Qwen3-30B-A3B EP2 -> TP2).  One sender
+            # into one peer, both quantisers run alike (0.878 / 0.881), but the sync with four
+            # senders each storing into four peers (EP4 -> TP4) reached only 0.659 with the
+            # tensor-map-fed one, a gap not yet profiled; it stays for blocks quantised locally
+            lc.mode = MODE_VECTOR
         torch.cuda.set_device(device)
         self._program = TransferProgram(tables, device, flags, lc)
         self._stream = torch.cuda.Stream(device)

@@ -478,13 +478,29 @@ __device__ void quant_block_smem(const QuantDesc& d, uint32_t block, const uint8
   const float scale = amax > 0.f ? __fdiv_rn(amax, kE4M3Max) : 1.f;
   const float inv = __frcp_rn(scale);
   uint8_t* dst = reinterpret_cast<uint8_t*>(d.dst) + r0 * d.dst_pitch + c0;
+  // 16-byte stores where the destination allows: lane pairs (c, c ^ 1) swap one 8-byte half,
+  // so the even lane stores columns [16m, 16m + 16) and the odd lane [64 + 16m, 80 + 16m)
+  // (c = 2m, 2m + 1): one warp instruction writes each of its rows as 128 contiguous bytes,
+  // whole lines on NVLink when the destination is a peer GPU
+  const bool wide = ((reinterpret_cast<uint64_t>(dst) | (uint64_t)d.dst_pitch) & 15) == 0;
+  const bool odd = cc & 1u;
   #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const uint32_t r = rg + 32u * k;
+    const uint2 lo = quant8(v[k][0], bf16, inv), hi = quant8(v[k][1], bf16, inv);
+    const uint2 give = odd ? lo : hi;
+    const uint2 got = make_uint2(__shfl_xor_sync(0xffffffffu, give.x, 1), __shfl_xor_sync(0xffffffffu, give.y, 1));
     if (r >= nr) continue;
     uint8_t* row = dst + r * d.dst_pitch;
-    if (cc * 8u < nc) st8(row + cc * 8u, quant8(v[k][0], bf16, inv));
-    if (64u + cc * 8u < nc) st8(row + 64u + cc * 8u, quant8(v[k][1], bf16, inv));
+    if (wide) {
+      const uint32_t col = odd ? 64u + 8u * (cc - 1u) : 8u * cc;          // 16-byte aligned
+      const uint4 v16 = odd ? make_uint4(got.x, got.y, hi.x, hi.y) : make_uint4(lo.x, lo.y, got.x, got.y);
+      if (col + 16u <= nc) st16(row + col, v16);
+      else if (col + 8u <= nc) st8(row + col, make_uint2(v16.x, v16.y));
+    } else {
+      if (cc * 8u < nc) st8(row + cc * 8u, lo);
+      if (64u + cc * 8u < nc) st8(row + 64u + cc * 8u, hi);
+    }
   }
   if (threadIdx.x == 0)
     *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(d.scale) + br * d.scale_pitch + bc * 4u) = scale;

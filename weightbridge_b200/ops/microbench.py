@@ -44,6 +44,8 @@ def _peak_gbs() -> float | None:
 
 PEER_PEAK_FILE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "..", "profiles",
                               "nvlink_peer_peak.json")
+MC_PEAK_FILE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "..", "profiles",
+                            "nvlink_multicast_store_peak.json")
 FALLBACK_PEER_GBS = 770.0     # an earlier peer-copy measurement on B200s, used when no file exists
 
 
@@ -53,6 +55,14 @@ def _peer_peak_gbs() -> float:
         return float(json.load(open(PEER_PEAK_FILE))["best_gbs"])
     except (OSError, KeyError, ValueError):
         return FALLBACK_PEER_GBS
+
+
+def _mc_peak_gbs() -> float | None:
+    """The measured multicast store rate out of one GPU (``--case mc-peak``), if recorded."""
+    try:
+        return float(json.load(open(MC_PEAK_FILE))["best_gbs"])
+    except (OSError, KeyError, ValueError):
+        return None
 
 
 def build(case: str, gbytes: float, dev, item_bytes: int):
@@ -245,8 +255,11 @@ def mc_peak(gbytes: float, iters: int, warmup: int, item_bytes: int, members: in
         a = torch.randn(n, device=d0, dtype=torch.bfloat16)
         ops = [Op("copy", "x", (-1, a.data_ptr()), (-1, 0), [n], [1], [1], a.dtype, a.dtype)]
         mc_tables = lower_ops(ops, lambda x: 0, lambda x: va, item_bytes=item_bytes, multicast=True)
-        uc_tables = lower_ops([Op("copy", "x", (-1, a.data_ptr()), (-1, pools[d].ptr), [n], [1], [1], a.dtype, a.dtype)
-                               for d in range(1, k)], lambda x: 0, lambda x: 0, item_bytes=item_bytes)
+        # unicast comparison: plain peer tensors (caching allocator, peer access enabled above);
+        # the members' VMM pools are mapped for their own GPU only, so GPU 0 must not store there
+        peers = [torch.empty(n, device=torch.device("cuda", d), dtype=torch.bfloat16) for d in range(1, k)]
+        uc_tables = lower_ops([Op("copy", "x", (-1, a.data_ptr()), (-1, b.data_ptr()), [n], [1], [1], a.dtype, a.dtype)
+                               for b in peers], lambda x: 0, lambda x: 0, item_bytes=item_bytes)
         with ClockSampler() as clk, torch.cuda.device(d0):
             s0 = torch.cuda.current_stream(d0)
             mc = TransferProgram(mc_tables, d0, [], LaunchConfig(mode=0))
@@ -263,7 +276,9 @@ def mc_peak(gbytes: float, iters: int, warmup: int, item_bytes: int, members: in
         out["best_gbs"] = out["multicast_egress_gbs"]
         out["clocks"] = clk.summary()
         out["device"] = torch.cuda.get_device_name(d0)
-        del mc, uc, a
+        ok += [torch.equal(b.to(d0), a) for b in peers]
+        out["verified_members"] = ok
+        del mc, uc, a, peers
         torch.cuda.synchronize()
     finally:
         if va is not None:

@@ -3,10 +3,12 @@
     python -m weightbridge_b200.plan_report --model qwen3-30b-a3b --trainer ep=4 \\
         --rollout tp=4,moe_ep=4,quant=fp8_experts
     python -m weightbridge_b200.plan_report --model llama3-8b --trainer tp=2,pp=2 --rollout tp=1 --replicas 4 --json
+    python -m weightbridge_b200.plan_report --model llama3-8b --trainer tp=1 --rollout tp=1 --replicas 7 --multicast
 
 Builds both layouts on the ``meta`` device, runs the source assignment and the planner for
 every (sender, receiver) pair, and reports per-sender and per-receiver bytes, work rows,
-quantised blocks and split-block pieces, plus the sync time the busiest link allows.  Trainer
+quantised blocks and split-block pieces, plus the sync time the busiest link allows
+(``--multicast``: the ``nvls`` mode's plan, multicast copies counted once per replica group).  Trainer
 ranks are enumerated as pipeline stage x expert-parallel rank x max(tp, etp) with
 ``tp_rank = t % tp`` and ``etp_rank = t % etp`` (``--trainer-kind fsdp``: ``world`` ranks of
 an FSDP-sharded model); rollout workers as replica x tp rank.
@@ -63,45 +65,67 @@ def _meta_binding(lay):
 
 
 def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs: float | None = None,
-           trainer_kind: str = "megatron") -> dict:
+           trainer_kind: str = "megatron", multicast: bool = False, mc_gbs: float | None = None) -> dict:
     """``link_gbs``: per-GPU link bandwidth of the estimate (default: the measured GPU -> GPU
-    peak, ``ops/microbench.py:peer_peak``)."""
+    peak, ``ops/microbench.py:peer_peak``).  ``multicast``: the ``nvls`` mode's plan, where the
+    workers with identical layouts (replicas) form groups, the source assignment is
+    replica-consistent and a sender's aligned same-dtype copies leave its GPU once per group,
+    at ``mc_gbs`` (default: the measured multicast store rate, ``--case mc-peak``)."""
+    from .control.assign import receiver_replicas
+    from .core.plan import multicast_ok
+    from .ops.microbench import _mc_peak_gbs, _peer_peak_gbs
     if link_gbs is None:
-        from .ops.microbench import _peer_peak_gbs
         link_gbs = _peer_peak_gbs()
+    if mc_gbs is None:
+        mc_gbs = (_mc_peak_gbs() or link_gbs) if multicast else link_gbs
     arch = get_arch(model)
     senders = [_meta_binding(l) for l in trainer_layouts(arch, trainer, trainer_kind)]
     receivers = [_meta_binding(l) for l in rollout_layouts(arch, rollout, replicas)]
     smetas = [m for m, _ in senders]
     rmetas = {r: m for r, (m, _) in enumerate(receivers)}
-    plan = assign_sources(smetas, rmetas)
+    plan = assign_sources(smetas, rmetas, replica_consistent=multicast)
+    groups = {g[0]: g for g in receiver_replicas(rmetas)} if multicast else {}
+    grouped = {r for g in groups.values() for r in g}
     srows, ingress = [], [0] * len(receivers)
     for s, (smeta, sphys) in enumerate(senders):
         row = {"sender": s, "targets": 0, "bytes_read": 0, "bytes_written": 0, "items": 0,
-               "quant_blocks": 0, "split_pieces": 0}
+               "quant_blocks": 0, "split_pieces": 0, "multicast_bytes": 0}
         for r, names in sorted(plan.get(s, {}).items()):
-            if not names:
-                continue
-            t = lower_ops(plan_pair(sphys, receivers[r][1], names=names), _ABS, _ABS, receiver=r)
-            row["targets"] += 1
-            row["bytes_read"] += t.bytes_read
-            row["bytes_written"] += t.bytes_written
-            row["items"] += len(t.items)
-            row["quant_blocks"] += len(t.qwork)
-            row["split_pieces"] += len(t.pieces)
-            ingress[r] += t.bytes_written
+            if not names or (r in grouped and r not in groups):
+                continue                       # a replica group is planned through its first worker
+            ops = plan_pair(sphys, receivers[r][1], names=names)
+            reps = groups.get(r, [r])
+            parts = [(lower_ops(ops, _ABS, _ABS, receiver=r), len(reps))]
+            if len(reps) > 1:                  # multicast copies once, the rest once per replica
+                mc = [o for o in ops if multicast_ok(o, _ABS, _ABS)]
+                uni = [o for o in ops if not multicast_ok(o, _ABS, _ABS)]
+                mct = lower_ops(mc, _ABS, _ABS, multicast=True)
+                row["multicast_bytes"] += mct.bytes_written
+                parts = [(mct, 0), (lower_ops(uni, _ABS, _ABS, receiver=r), len(reps))]
+            for t, copies in parts:
+                row["bytes_read"] += t.bytes_read
+                row["bytes_written"] += t.bytes_written * copies
+                row["items"] += len(t.items)
+                row["quant_blocks"] += len(t.qwork) * max(copies, 1)
+                row["split_pieces"] += len(t.pieces) * max(copies, 1)
+                for rr in reps:
+                    ingress[rr] += t.bytes_written
+            row["targets"] += len(reps)
         srows.append(row)
+    # time per GPU: unicast bytes at the peer rate, multicast bytes at the multicast rate
+    s_ms = [(r["bytes_written"] / link_gbs + r["multicast_bytes"] / mc_gbs) / 1e6 for r in srows]
     egress = max((r["bytes_written"] for r in srows), default=0)
     inmax = max(ingress, default=0)
     return {
         "model": model, "trainer_kind": trainer_kind, "trainer": trainer, "rollout": rollout, "replicas": replicas,
+        "multicast": multicast,
         "senders": srows,
         "receivers": [{"receiver": r, "ingress_bytes": b,
                        "senders": sorted(s for s, t in plan.items() if t.get(r))} for r, b in enumerate(ingress)],
         "total_written_bytes": sum(ingress),
         "busiest_sender_bytes": egress, "busiest_receiver_bytes": inmax,
-        "link_gbs": link_gbs,
-        "link_bound_ms": max(egress, inmax) / (link_gbs * 1e9) * 1e3,
+        "link_gbs": link_gbs, "multicast_gbs": mc_gbs if multicast else None,
+        "link_bound_ms": max(max(s_ms, default=0.0), inmax / (link_gbs * 1e9) * 1e3),
         "note": "link-bound estimate for senders and receivers on different GPUs; a colocated pair "
                 "moves its bytes through HBM instead",
     }
@@ -120,24 +144,32 @@ def main(argv=None) -> int:
     ap.add_argument("--replicas", type=int, default=1, help="rollout replicas (each with the rollout layout)")
     ap.add_argument("--link-gbs", type=float, default=None,
                     help="per-GPU link bandwidth for the estimate (default: the measured peer peak)")
+    ap.add_argument("--multicast", action="store_true",
+                    help="the nvls mode: replicas of one layout served by multicast stores")
+    ap.add_argument("--mc-gbs", type=float, default=None,
+                    help="multicast store rate out of one GPU (default: the measured one)")
     ap.add_argument("--json", action="store_true")
     a = ap.parse_args(argv)
-    rep = report(a.model, _kv(a.trainer), _kv(a.rollout), a.replicas, a.link_gbs, a.trainer_kind)
+    rep = report(a.model, _kv(a.trainer), _kv(a.rollout), a.replicas, a.link_gbs, a.trainer_kind,
+                 multicast=a.multicast, mc_gbs=a.mc_gbs)
     if a.json:
         print(json.dumps(rep))
         return 0
     print(f"{a.model}: trainer {a.trainer or 'tp=1'} ({len(rep['senders'])} ranks) -> rollout "
           f"{a.rollout or 'tp=1'} x{a.replicas} ({len(rep['receivers'])} workers)")
-    print(f"{'sender':>6} {'targets':>7} {'read GB':>9} {'written GB':>10} {'items':>8} {'quant blk':>9} {'split pcs':>9}")
+    print(f"{'sender':>6} {'targets':>7} {'read GB':>9} {'written GB':>10} {'multicast GB':>12} {'items':>8} "
+          f"{'quant blk':>9} {'split pcs':>9}")
     for r in rep["senders"]:
         print(f"{r['sender']:>6} {r['targets']:>7} {_gb(r['bytes_read']):>9} {_gb(r['bytes_written']):>10} "
-              f"{r['items']:>8} {r['quant_blocks']:>9} {r['split_pieces']:>9}")
+              f"{_gb(r['multicast_bytes']):>12} {r['items']:>8} {r['quant_blocks']:>9} {r['split_pieces']:>9}")
     print(f"{'worker':>6} {'ingress GB':>10}  senders")
     for r in rep["receivers"]:
         print(f"{r['receiver']:>6} {_gb(r['ingress_bytes']):>10}  {r['senders']}")
-    print(f"total written {_gb(rep['total_written_bytes'])} GB; busiest sender {_gb(rep['busiest_sender_bytes'])} GB, "
+    mc = max((r["multicast_bytes"] for r in rep["senders"]), default=0)
+    print(f"total written {_gb(rep['total_written_bytes'])} GB; busiest sender {_gb(rep['busiest_sender_bytes'])} GB"
+          + (f" unicast + {_gb(mc)} GB multicast" if rep["multicast"] else "") + ", "
           f"busiest worker {_gb(rep['busiest_receiver_bytes'])} GB -> {rep['link_bound_ms']:.2f} ms at "
-          f"{rep['link_gbs']:.0f} GB/s per link")
+          f"{rep['link_gbs']:.0f} GB/s per link" + (f", multicast at {rep['multicast_gbs']:.0f} GB/s" if rep["multicast"] else ""))
     return 0
 
 
