@@ -14,8 +14,9 @@ Configurations (strong scaling: the model, hence the bytes moved per sync, is fi
                      outnumber senders: the case NVLink multicast, --transfer nvls, is for)
   qwen3-moe-fp8      Qwen3-30B-A3B, trainer EP4 -> rollout TP4 (EP4 experts), experts quantised
                      to fp8 e4m3 with 128x128 fp32 block scales in the transfer kernel (N=8)
-  qwen3-moe-fp8-etp  the same with trainer expert TP 4 instead of EP (192-row expert slices): every
-                     expert fp8 block is split over two senders, which exchange its amax (N=8)
+  qwen3-moe-fp8-etp  the same with trainer expert TP instead of EP.  N=8: expert TP 4, 192-row
+                     slices, so every expert fp8 block is split over two senders, which exchange
+                     its amax; N=4: expert TP 2, 384-row slices of whole blocks (no split blocks)
   llama70b-colocated Llama-3-70B, trainer TP8 on GPUs 0-7 -> two rollout replicas at TP4 in
                      separate processes on GPUs 0-3 and 4-7 (N=8, 16 processes)
   deepseek-lite-fp8  DeepSeek-V2-Lite (MLA + 64 routed and 2 shared experts), trainer TP2 x EP2 ->
