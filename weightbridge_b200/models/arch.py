@@ -267,6 +267,8 @@ PRESETS: dict[str, ModelArch] = {
                                num_experts=128, moe_ffn=768, top_k=8),
     # small test models of every family
     "tiny-qwen2": ModelArch("tiny-qwen2", "qwen2", 2, 128, 4, 2, 32, 256, 512),
+    # Llama-3-70B's attention shape in miniature (8 heads, 8 KV heads): splits at TP 8 as 70B does
+    "tiny-llama-tp8": ModelArch("tiny-llama-tp8", "llama", 2, 256, 8, 8, 32, 512, 1024),
     # head dim and FFN in multiples of 128: every linear layer block-quantisable (fp8_linear)
     "tiny-llama-fp8": ModelArch("tiny-llama-fp8", "llama", 2, 256, 4, 2, 128, 512, 1024),
     "tiny-qwen3": ModelArch("tiny-qwen3", "qwen3", 2, 128, 8, 2, 32, 256, 520),
