@@ -18,7 +18,8 @@ Configurations (strong scaling: the model, hence the bytes moved per sync, is fi
                      slices, so every expert fp8 block is split over two senders, which exchange
                      its amax; N=4: expert TP 2, 384-row slices of whole blocks (no split blocks)
   llama70b-colocated Llama-3-70B, trainer TP8 on GPUs 0-7 -> two rollout replicas at TP4 in
-                     separate processes on GPUs 0-3 and 4-7 (N=8, 16 processes)
+                     separate processes, interleaved: tp rank t of replica e on GPU 2t + e
+                     (N=8, 16 processes)
   deepseek-lite-fp8  DeepSeek-V2-Lite (MLA + 64 routed and 2 shared experts), trainer TP2 x EP2 ->
                      rollout TP4 (EP4 experts, fp8 e4m3 blocks), MLA's w_kc / w_vc written with
                      kv_b_proj (N=8; N=4: TP2 -> TP2)
@@ -165,9 +166,13 @@ def scenario(config: str, n: int) -> tuple[str, list[Role], str]:
     if config == "llama70b-colocated":
         if n != 8:
             raise SystemExit("llama70b-colocated runs on 8 GPUs")
+        # tp rank t of replica e on GPU 2t + e: every worker's rows come from trainer ranks 2t and
+        # 2t + 1, one of them on its own GPU, so half the bytes stay in HBM (141 of 282 GB; with
+        # replica 0 on GPUs 0-3 and replica 1 on 4-7 only 35 GB would, doubling the NVLink bound)
         roles = [Role("trainer", i, dict(tp=8, tp_rank=i)) for i in range(8)]
-        roles += [Role("rollout", i, dict(tp=4, tp_rank=i % 4), i // 4, i % 4, i % 4 == 0) for i in range(8)]
-        return "llama3-70b", roles, "tp8 -> 2 replicas x tp4, colocated (16 processes)"
+        roles += [Role("rollout", 2 * (i % 4) + i // 4, dict(tp=4, tp_rank=i % 4), i // 4, i % 4, i % 4 == 0)
+                  for i in range(8)]
+        return "llama3-70b", roles, "tp8 -> 2 replicas x tp4, colocated, replicas interleaved (16 processes)"
     if config == "deepseek-lite-fp8":
         if n not in (4, 8):
             raise SystemExit("deepseek-lite-fp8 runs on 4 or 8 GPUs")
@@ -188,26 +193,9 @@ def _measured_peaks() -> dict:
 
 
 def _link_bytes(routes: list[dict]) -> tuple[dict, dict, dict, int]:
-    """Per-GPU NVLink bytes of one sync: unicast egress, multicast egress, ingress, and the bytes
-    that stay on one GPU.  A unicast route to its own GPU stays in HBM; a multicast store leaves
-    its sender's GPU once and the NVSwitch delivers it to every replica's GPU (its own included)."""
-    egress: dict[int, int] = {}
-    mc_egress: dict[int, int] = {}
-    ingress: dict[int, int] = {}
-    local = 0
-    for r in routes:
-        n, src = int(r["bytes"]), int(r["src"])
-        remote = list(r["dst"]) if r["multicast"] else [d for d in r["dst"] if d != src]
-        local += n * (len(r["dst"]) - len(remote))
-        if not remote:
-            continue
-        if r["multicast"]:
-            mc_egress[src] = mc_egress.get(src, 0) + n
-        else:
-            egress[src] = egress.get(src, 0) + n * len(remote)
-        for d in remote:
-            ingress[d] = ingress.get(d, 0) + n
-    return egress, mc_egress, ingress, local
+    """Per-GPU unicast egress, multicast egress, ingress and GPU-local bytes of one sync."""
+    from weightbridge_b200.utils.links import link_bytes
+    return link_bytes(routes)
 
 
 def _roofline(routes: list[dict], bytes_read: float, payload: float, ms: float) -> dict:
@@ -215,19 +203,17 @@ def _roofline(routes: list[dict], bytes_read: float, payload: float, ms: float) 
     writes) when every byte stays on its GPU; otherwise ideal time / measured time, where the
     ideal time is the busiest GPU's NVLink egress or ingress: unicast bytes at the measured
     GPU -> GPU peak, multicast stores at the measured multicast store peak."""
+    from weightbridge_b200.utils.links import busiest_link
     egress, mc_egress, ingress, _local = _link_bytes(routes)
-    if not egress and not mc_egress:
+    peak, source = _peer_peak()
+    mc_peak, mc_source = _mc_peak(peak)
+    worst = busiest_link(routes, peak, mc_peak)
+    if worst is None:
         peak = float(_measured_peaks().get("hbm_gbs", 6650.0))
         achieved = (bytes_read + payload) / (ms / 1e3) / 1e9
         return {"bound": "hbm copy (read + write)", "peak_gbs": peak, "achieved_gbs": round(achieved, 1),
                 "fraction_of_measured": round(achieved / peak, 3)}
-    peak, source = _peer_peak()
-    mc_peak, mc_source = _mc_peak(peak)
-    times = [(("egress", d), egress.get(d, 0) / peak + mc_egress.get(d, 0) / mc_peak)
-             for d in set(egress) | set(mc_egress)]
-    times += [(("ingress", d), b / peak) for d, b in ingress.items()]
-    (side, dev), t = max(times, key=lambda x: x[1])          # seconds * 1e9 (bytes / (GB/s))
-    ideal_ms = t / 1e6
+    side, dev, ideal_ms = worst
     out = {"bound": f"nvlink, busiest GPU ({side} of GPU {dev})", "ideal_ms": round(ideal_ms, 4),
            "peak_gbs": peak, "peak_source": source, "fraction_of_measured": round(ideal_ms / ms, 3),
            "egress_gb": {str(d): round(b / 1e9, 3) for d, b in sorted(egress.items())},

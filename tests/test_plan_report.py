@@ -54,3 +54,19 @@ def test_report_multicast_pipeline_stages_all_multicast():
     its entries to all four by multicast (none falls back to per-replica stores)."""
     rep = report("tiny-llama", {"tp": 2, "pp": 2}, {"tp": 1}, replicas=4, multicast=True, mc_gbs=500.0)
     assert all(s["multicast_bytes"] > 0 and s["bytes_written"] == 0 for s in rep["senders"])
+
+
+def test_report_colocated_interleaved_replicas_halve_the_link_bytes():
+    """Config 5's shape (TP8 trainer, two TP4 replicas on the same 8 GPUs): with the replicas'
+    ranks interleaved every worker finds one of its two source ranks on its own GPU, so half of
+    all bytes stay in HBM and the busiest GPU moves half as much over NVLink as with the replicas
+    in blocks (replica 0 on GPUs 0-3)."""
+    kw = dict(replicas=2, link_gbs=800.0)
+    block = report("tiny-llama-tp8", {"tp": 8}, {"tp": 4}, colocated="block", **kw)
+    inter = report("tiny-llama-tp8", {"tp": 8}, {"tp": 4}, colocated="interleaved", **kw)
+    apart = report("tiny-llama-tp8", {"tp": 8}, {"tp": 4}, **kw)
+    total = inter["total_written_bytes"]
+    assert apart["gpu_local_bytes"] == 0
+    assert block["gpu_local_bytes"] < total // 4
+    assert abs(inter["gpu_local_bytes"] - total / 2) < total * 0.05
+    assert inter["link_bound_ms"] < 0.6 * block["link_bound_ms"]

@@ -4,6 +4,7 @@
         --rollout tp=4,moe_ep=4,quant=fp8_experts
     python -m weightbridge_b200.plan_report --model llama3-8b --trainer tp=2,pp=2 --rollout tp=1 --replicas 4 --json
     python -m weightbridge_b200.plan_report --model llama3-8b --trainer tp=1 --rollout tp=1 --replicas 7 --multicast
+    python -m weightbridge_b200.plan_report --model llama3-70b --trainer tp=8 --rollout tp=4 --replicas 2 --colocated interleaved
 
 Builds both layouts on the ``meta`` device, runs the source assignment and the planner for
 every (sender, receiver) pair, and reports per-sender and per-receiver bytes, work rows,
@@ -65,12 +66,19 @@ def _meta_binding(lay):
 
 
 def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs: float | None = None,
-           trainer_kind: str = "megatron", multicast: bool = False, mc_gbs: float | None = None) -> dict:
+           trainer_kind: str = "megatron", multicast: bool = False, mc_gbs: float | None = None,
+           colocated: str | bool = False) -> dict:
     """``link_gbs``: per-GPU link bandwidth of the estimate (default: the measured GPU -> GPU
     peak, ``ops/microbench.py:peer_peak``).  ``multicast``: the ``nvls`` mode's plan, where the
     workers with identical layouts (replicas) form groups, the source assignment is
     replica-consistent and a sender's aligned same-dtype copies leave its GPU once per group,
-    at ``mc_gbs`` (default: the measured multicast store rate, ``--case mc-peak``)."""
+    at ``mc_gbs`` (default: the measured multicast store rate, ``--case mc-peak``).
+    GPUs: trainer rank s on GPU s; rollout worker w (tp rank t of replica e) on GPU ``trainers + w``,
+    or beside the trainer ranks with ``colocated``: ``"block"`` (or True) puts it on GPU
+    ``w % trainers`` (replica after replica), ``"interleaved"`` on GPU ``(t * replicas + e) %
+    trainers`` (the replicas' ranks alternate); bytes between a trainer rank and a worker on its
+    own GPU stay in HBM."""
+    from .utils.links import busiest_link, link_bytes
     from .control.assign import receiver_replicas
     from .core.plan import multicast_ok
     from .ops.microbench import _mc_peak_gbs, _peer_peak_gbs
@@ -86,6 +94,14 @@ def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs
     plan = assign_sources(smetas, rmetas, replica_consistent=multicast)
     groups = {g[0]: g for g in receiver_replicas(rmetas)} if multicast else {}
     grouped = {r for g in groups.values() for r in g}
+    ntp = int(rollout.get("tp", 1))
+    if colocated == "interleaved":
+        gpu = lambda w: ((w % ntp) * replicas + w // ntp) % len(senders)       # noqa: E731
+    elif colocated:
+        gpu = lambda w: w % len(senders)                                          # noqa: E731
+    else:
+        gpu = lambda w: len(senders) + w                                          # noqa: E731
+    routes: list[dict] = []
     srows, ingress = [], [0] * len(receivers)
     for s, (smeta, sphys) in enumerate(senders):
         row = {"sender": s, "targets": 0, "bytes_read": 0, "bytes_written": 0, "items": 0,
@@ -110,10 +126,18 @@ def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs
                 row["split_pieces"] += len(t.pieces) * max(copies, 1)
                 for rr in reps:
                     ingress[rr] += t.bytes_written
+                if copies == 0:
+                    routes.append({"src": s, "dst": [gpu(rr) for rr in reps], "bytes": t.bytes_written,
+                                   "multicast": True})
+                else:
+                    routes += [{"src": s, "dst": [gpu(rr)], "bytes": t.bytes_written, "multicast": False}
+                               for rr in reps]
             row["targets"] += len(reps)
         srows.append(row)
-    # time per GPU: unicast bytes at the peer rate, multicast bytes at the multicast rate
-    s_ms = [(r["bytes_written"] / link_gbs + r["multicast_bytes"] / mc_gbs) / 1e6 for r in srows]
+    # time per GPU: unicast bytes at the peer rate, multicast bytes at the multicast rate;
+    # bytes between a trainer rank and a worker on its own GPU stay in HBM
+    egress_b, mc_b, ingress_b, local = link_bytes(routes)
+    worst = busiest_link(routes, link_gbs, mc_gbs)
     egress = max((r["bytes_written"] for r in srows), default=0)
     inmax = max(ingress, default=0)
     return {
@@ -125,9 +149,14 @@ def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs
         "total_written_bytes": sum(ingress),
         "busiest_sender_bytes": egress, "busiest_receiver_bytes": inmax,
         "link_gbs": link_gbs, "multicast_gbs": mc_gbs if multicast else None,
-        "link_bound_ms": max(max(s_ms, default=0.0), inmax / (link_gbs * 1e9) * 1e3),
-        "note": "link-bound estimate for senders and receivers on different GPUs; a colocated pair "
-                "moves its bytes through HBM instead",
+        "colocated": colocated, "gpu_local_bytes": local,
+        "gpu_egress_bytes": {str(d): b for d, b in sorted(egress_b.items())},
+        "gpu_multicast_egress_bytes": {str(d): b for d, b in sorted(mc_b.items())},
+        "gpu_ingress_bytes": {str(d): b for d, b in sorted(ingress_b.items())},
+        "busiest_gpu": None if worst is None else {"side": worst[0], "gpu": worst[1]},
+        "link_bound_ms": 0.0 if worst is None else worst[2],
+        "note": "NVLink-bound estimate (the busiest GPU's egress or ingress); bytes between a trainer rank "
+                "and a worker on its own GPU move through HBM and are left out",
     }
 
 
@@ -148,10 +177,13 @@ def main(argv=None) -> int:
                     help="the nvls mode: replicas of one layout served by multicast stores")
     ap.add_argument("--mc-gbs", type=float, default=None,
                     help="multicast store rate out of one GPU (default: the measured one)")
+    ap.add_argument("--colocated", nargs="?", const="block", default=None, choices=["block", "interleaved"],
+                    help="rollout workers on the trainers' GPUs: block (worker w on GPU w %% trainers) or "
+                         "interleaved (tp rank t of replica e on GPU t * replicas + e); else GPUs of their own")
     ap.add_argument("--json", action="store_true")
     a = ap.parse_args(argv)
     rep = report(a.model, _kv(a.trainer), _kv(a.rollout), a.replicas, a.link_gbs, a.trainer_kind,
-                 multicast=a.multicast, mc_gbs=a.mc_gbs)
+                 multicast=a.multicast, mc_gbs=a.mc_gbs, colocated=a.colocated or False)
     if a.json:
         print(json.dumps(rep))
         return 0
@@ -166,10 +198,18 @@ def main(argv=None) -> int:
     for r in rep["receivers"]:
         print(f"{r['receiver']:>6} {_gb(r['ingress_bytes']):>10}  {r['senders']}")
     mc = max((r["multicast_bytes"] for r in rep["senders"]), default=0)
-    print(f"total written {_gb(rep['total_written_bytes'])} GB; busiest sender {_gb(rep['busiest_sender_bytes'])} GB"
-          + (f" unicast + {_gb(mc)} GB multicast" if rep["multicast"] else "") + ", "
-          f"busiest worker {_gb(rep['busiest_receiver_bytes'])} GB -> {rep['link_bound_ms']:.2f} ms at "
-          f"{rep['link_gbs']:.0f} GB/s per link" + (f", multicast at {rep['multicast_gbs']:.0f} GB/s" if rep["multicast"] else ""))
+    line = f"total written {_gb(rep['total_written_bytes'])} GB; busiest sender {_gb(rep['busiest_sender_bytes'])} GB"
+    if rep["multicast"]:
+        line += f" unicast + {_gb(mc)} GB multicast"
+    line += f", busiest worker {_gb(rep['busiest_receiver_bytes'])} GB"
+    if rep["colocated"]:
+        line += f"; {_gb(rep['gpu_local_bytes'])} GB stay within GPUs"
+    worst = rep["busiest_gpu"]
+    where = f" ({worst['side']} of GPU {worst['gpu']})" if worst else ""
+    line += f" -> {rep['link_bound_ms']:.2f} ms{where} at {rep['link_gbs']:.0f} GB/s per link"
+    if rep["multicast"]:
+        line += f", multicast at {rep['multicast_gbs']:.0f} GB/s"
+    print(line)
     return 0
 
 
