@@ -226,7 +226,7 @@ def _roofline(routes: list[dict], bytes_read: float, payload: float, ms: float) 
 
 def _mc_peak(fallback: float) -> tuple[float, str]:
     """Multicast store bandwidth out of one GPU (``multimem.st`` through the NVSwitch), measured
-    on B200s of this pool (profiles/nvlink_multicast_store_peak.json, written by
+    on B200s (profiles/nvlink_multicast_store_peak.json, written by
     ``python -m weightbridge_b200.ops.microbench --case mc-peak``)."""
     try:
         with open(os.path.join(ROOT, "profiles", "nvlink_multicast_store_peak.json")) as f:
@@ -237,7 +237,7 @@ def _mc_peak(fallback: float) -> tuple[float, str]:
 
 def _peer_peak() -> tuple[float, str]:
     """GPU -> GPU peak: the largest of copy engine, push kernel and pull kernel measured on two
-    B200s of this pool (profiles/nvlink_peer_peak.json, written by
+    B200s (profiles/nvlink_peer_peak.json, written by
     ``python -m weightbridge_b200.ops.microbench --case peer-peak``)."""
     try:
         with open(os.path.join(ROOT, "profiles", "nvlink_peer_peak.json")) as f:

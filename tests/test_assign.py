@@ -107,3 +107,24 @@ def test_replica_consistent_assignment_serves_every_replica_alike():
     assert len({o[0] for o in owners.values()}) > 2          # spread over both TP ranks of both stages
     loose = assign_sources(smetas, rmetas)
     assert any(len({tuple(rs.get(r, [])) for r in rmetas}) > 1 for rs in loose.values())
+
+
+def test_replicated_entries_come_from_the_receivers_own_gpu():
+    """Trainer DP 2 (two identical TP1 ranks on GPUs A and B) into two colocated TP1 workers on
+    A and B: each worker takes every entry from the rank on its own GPU (HBM copies), where the
+    GPU-blind assignment balances bytes across both ranks (half of them over NVLink)."""
+    arch = get_arch("tiny-llama")
+    lay = MegatronLayout(arch, tp=1)
+    smetas = [_meta(lay, lay.param_shapes()) for _ in range(2)]
+    rl = SGLangLayout(arch, tp=1)
+    rmetas = {2: _meta(rl, {n: sh for n, (sh, _k) in rl.param_specs().items()}),
+              3: _meta(rl, {n: sh for n, (sh, _k) in rl.param_specs().items()})}
+    plan = assign_sources(smetas, rmetas, sender_gpus=["A", "B"], receiver_gpus={2: "A", 3: "B"})
+    assert set(plan) == {0, 1}
+    assert set(plan[0]) == {2} and set(plan[1]) == {3}
+    assert sorted(plan[0][2]) == sorted(rmetas[2].names()) and sorted(plan[1][3]) == sorted(rmetas[3].names())
+    blind = assign_sources(smetas, rmetas)
+    assert any(len(rs) > 1 for rs in blind.values())               # some entries cross GPUs
+    # a worker on a GPU no trainer rank holds balances as before
+    far = assign_sources(smetas, rmetas, sender_gpus=["A", "B"], receiver_gpus={2: "C", 3: "D"})
+    assert _bytes(far, smetas, rmetas) == _bytes(blind, smetas, rmetas)

@@ -70,3 +70,13 @@ def test_report_colocated_interleaved_replicas_halve_the_link_bytes():
     assert block["gpu_local_bytes"] < total // 4
     assert abs(inter["gpu_local_bytes"] - total / 2) < total * 0.05
     assert inter["link_bound_ms"] < 0.6 * block["link_bound_ms"]
+
+
+def test_report_colocated_data_parallel_trainer_copies_locally():
+    """Megatron DP 2 (two identical TP1 ranks) into two TP1 workers on the same two GPUs: every
+    entry comes from the rank on the worker's own GPU, so nothing crosses NVLink."""
+    rep = report("tiny-llama", {"tp": 1, "dp": 2}, {"tp": 1}, replicas=2, colocated="block")
+    assert len(rep["senders"]) == 2 and rep["link_bound_ms"] == 0
+    assert rep["gpu_local_bytes"] == rep["total_written_bytes"] > 0
+    apart = report("tiny-llama", {"tp": 1, "dp": 2}, {"tp": 1}, replicas=2)
+    assert apart["link_bound_ms"] > 0 and apart["gpu_local_bytes"] == 0

@@ -5,7 +5,8 @@ of an EP-only layout); shards of different replica groups must not overlap.  For
 receiver entry and every replica group that overlaps it, one member of the group sends it.
 Entries a single sender holds are fixed; replicated entries are then placed largest first on
 the least-loaded member (ties: lowest rank), so every sender's NVLink egress carries about
-the same bytes and the slowest link, which sets the sync time, is as short as possible.
+the same bytes and the slowest link, which sets the sync time, is as short as possible.  When
+the GPUs are known, a member on the receiver's own GPU is preferred (an HBM copy).
 
 Parity: the reference deduplicates identical shards by keeping the lowest rank and raises
 on partial overlap (``wbridge/backend/direct_sender.py:31-71``); the overlap rule is the
@@ -69,7 +70,8 @@ def receiver_replicas(receiver_metas: dict[int, WeightData]) -> list[list[int]]:
 
 
 def assign_sources(sender_metas: list[WeightData], receiver_metas: dict[int, WeightData],
-                   load_balance: bool = True, replica_consistent: bool = False) -> dict[int, dict[int, list[str]]]:
+                   load_balance: bool = True, replica_consistent: bool = False,
+                   sender_gpus: list | None = None, receiver_gpus: dict | None = None) -> dict[int, dict[int, list[str]]]:
     """``plan[sender][receiver] = [entry names]`` (both as indices into the inputs).
 
     Two passes: entries only one replica group can serve are assigned first (their load is
@@ -80,7 +82,15 @@ def assign_sources(sender_metas: list[WeightData], receiver_metas: dict[int, Wei
     replicated entry from the same sender, so every sender writes the same entries to every
     replica of such a group and one multicast store can serve them all; the entry then costs
     its sender one copy of the bytes, not one per replica.
+
+    ``sender_gpus`` / ``receiver_gpus`` (GPU identities, None for host memory): a replicated
+    entry goes to a receiver from a member on the receiver's own GPU where there is one (an
+    HBM copy, no link bytes, not counted as load); the others balance the link load.
     """
+    def gpu(x, table):
+        return None if table is None else table[x]
+    local = lambda s_, r_: (gpu(s_, sender_gpus) is not None                          # noqa: E731
+                            and gpu(s_, sender_gpus) == gpu(r_, receiver_gpus))
     groups = replica_groups(sender_metas)
     load = [0] * len(sender_metas)
     plan: dict[int, dict[int, list[str]]] = defaultdict(lambda: defaultdict(list))
@@ -103,14 +113,18 @@ def assign_sources(sender_metas: list[WeightData], receiver_metas: dict[int, Wei
                     continue
                 if len(group) == 1 or not load_balance:
                     s = min(group)
-                    load[s] += nbytes
+                    load[s] += 0 if local(s, r) else nbytes
                     plan[s][r].append(name)
                 elif replicas[r][0] == r:      # a replica group's entry is placed once, for all of it
                     flexible.append((nbytes, r, name, group))
     flexible.sort(key=lambda t: (-t[0], t[1], t[2]))
     for nbytes, r, name, group in flexible:
-        s = min(group, key=lambda x: (load[x], x))
-        load[s] += nbytes
+        near = [x for x in group if len(replicas[r]) == 1 and local(x, r)]
+        if near:
+            s = min(near, key=lambda x: (load[x], x))
+        else:
+            s = min(group, key=lambda x: (load[x], x))
+            load[s] += nbytes
         for rr in replicas[r]:
             plan[s][rr].append(name)
     # keep each receiver's names in its metadata order (deterministic, cache friendly)

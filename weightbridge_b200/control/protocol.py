@@ -46,6 +46,20 @@ class ConnectRequest(BaseModel):
     protocol: int = 1                    # PROTOCOL_VERSION of the sender (absent: an older sender)
 
 
+def gpu_id(device) -> str | None:
+    """A process-independent name of the GPU behind ``device`` (its UUID, base64; the index
+    depends on CUDA_VISIBLE_DEVICES), or None for host memory or when it cannot be read."""
+    import torch
+    dev = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
+    if dev.type != "cuda":
+        return None
+    try:
+        from ..ops._ext import ext
+        return b64(ext().device_uuid(dev.index if dev.index is not None else torch.cuda.current_device()))
+    except Exception:
+        return None
+
+
 def b64(data: bytes) -> str:
     return base64.b64encode(data).decode("ascii")
 

@@ -42,7 +42,7 @@ from ..utils.config import WIRE_MODES, TransferConfig, normalize_mode
 from ..utils.trace import nvtx_range
 from .assign import expected_senders, restrict
 from .protocol import (CONNECT_REQUEST, METADATA_REQUEST, PROTOCOL_VERSION, RECEIVE_REQUEST, STATS_REQUEST,
-                       STOP_REQUEST, UPDATE_REQUEST, ReceiverState, b64)
+                       STOP_REQUEST, UPDATE_REQUEST, ReceiverState, b64, gpu_id)
 from .session import Janitor, PeerError, Session, SessionTimeout
 from .board import word_digest
 
@@ -94,6 +94,7 @@ class WeightReceiver:
         self._bound = False                           # tensors bound and exported for this session
         self._pull_versions, self._pull_prog, self._pull_imports = None, None, {}   # pull direction
         self._pull_devices: dict[int, int] = {}      # GPU ordinal of each sender pulled from
+        self._gpu_id: str | None | bool = False       # this worker's GPU UUID (False: not read yet)
         self._pull_stream = None
         self._pull_progs: dict = {}                   # pull programs by entry-subset digest
         self._pull_src: dict = {}
@@ -274,9 +275,11 @@ class WeightReceiver:
     def _on_controller(self, sock, data: dict) -> None:
         t = data.get("type")
         if t == METADATA_REQUEST:
+            if self._gpu_id is False:
+                self._gpu_id = gpu_id(self.device)
             self._reply(sock, data, {"rank": self.rank, "metadata": self.metadata.to_jsonable(),
                                      "state": self._state.value, "device": str(self.device),
-                                     "host": socket.gethostname(), "pid": os.getpid()})
+                                     "gpu": self._gpu_id, "host": socket.gethostname(), "pid": os.getpid()})
         elif t == CONNECT_REQUEST:
             if self._state == ReceiverState.AWAITING_SCHEDULER_UPDATE:
                 self._reply(sock, data, {"status": "error", "detail": "cannot connect while awaiting scheduler update"})

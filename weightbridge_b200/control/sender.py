@@ -48,7 +48,7 @@ from ..core.shard import WeightData, covered_numel, shard_numel
 from ..utils.config import WIRE_MODES, TransferConfig, normalize_mode
 from .assign import assign_sources, restrict
 from ..utils.trace import nvtx_range
-from .protocol import PROTOCOL_VERSION
+from .protocol import PROTOCOL_VERSION, gpu_id
 from .session import Janitor, PeerError, Session, SessionTimeout, local_address
 from .board import digest_word
 
@@ -211,6 +211,7 @@ class WeightSender:
         metas = self._all_gather(sender_metadata.to_jsonable())
         self._sender_devices = self._all_gather(torch.cuda.current_device() if torch.cuda.is_available() else -1)
         self._sender_hosts = self._all_gather(socket.gethostname())
+        self._sender_gpus = self._all_gather(gpu_id(torch.cuda.current_device()) if torch.cuda.is_available() else None)
         info = None
         if self.rank == 0:
             try:
@@ -340,12 +341,14 @@ class WeightSender:
         counts = []
         base = self.world_size
         where = []                                   # (host, device) of every worker
+        rgpus: dict[int, str | None] = {}
         for url in self.receiver_urls:
             resp = _get_with_retry(http, f"{url}/wbridge/metadata", cfg.http_timeout_s)
             workers = sorted(resp.json(), key=lambda w: w["rank"])
             for i, w in enumerate(workers):
                 receivers[base + i] = w["metadata"]
                 where.append((w.get("host"), str(w.get("device", ""))))
+                rgpus[base + i] = w.get("gpu")
             counts.append(len(workers))
             base += len(workers)
         if cfg.mode == "auto":
@@ -360,8 +363,10 @@ class WeightSender:
         sess = self.session
         smeta_objs = [WeightData(m) for m in metas]
         rmeta_objs = {r: WeightData(m) for r, m in receivers.items()}
-        # multicast: every replica of a layout takes each entry from the same sender
-        plan = assign_sources(smeta_objs, rmeta_objs, cfg.load_balance, replica_consistent=cfg.mode == "nvls")
+        # multicast: every replica of a layout takes each entry from the same sender; otherwise a
+        # replicated entry comes from a trainer rank on the worker's own GPU where there is one
+        plan = assign_sources(smeta_objs, rmeta_objs, cfg.load_balance, replica_consistent=cfg.mode == "nvls",
+                              sender_gpus=self._sender_gpus, receiver_gpus=rgpus)
         sess.set_json("senders/meta", metas)
         sess.set("direction", session_direction(cfg, rmeta_objs.values()))
         sess.set("wire_chunk", str(int(cfg.wire_chunk_bytes)))      # receivers cut their wires alike

@@ -10,7 +10,7 @@ Builds both layouts on the ``meta`` device, runs the source assignment and the p
 every (sender, receiver) pair, and reports per-sender and per-receiver bytes, work rows,
 quantised blocks and split-block pieces, plus the sync time the busiest link allows
 (``--multicast``: the ``nvls`` mode's plan, multicast copies counted once per replica group).  Trainer
-ranks are enumerated as pipeline stage x expert-parallel rank x max(tp, etp) with
+ranks are enumerated as data-parallel replica x pipeline stage x expert-parallel rank x max(tp, etp) with
 ``tp_rank = t % tp`` and ``etp_rank = t % etp`` (``--trainer-kind fsdp``: ``world`` ranks of
 an FSDP-sharded model); rollout workers as replica x tp rank.
 The reference has no equivalent (it plans inside ``connect``, ``wbridge/backend/direct_sender.py:74-168``).
@@ -46,11 +46,11 @@ def trainer_layouts(arch, spec: dict, kind: str = "megatron") -> list:
         from .parallel.fsdp import FSDPLayout
         world = int(spec.get("world", 1))
         return [FSDPLayout(arch, world=world, rank=i, dim=int(spec.get("dim", 0))) for i in range(world)]
-    tp, pp, ep, etp = (int(spec.get(k, 1)) for k in ("tp", "pp", "ep", "etp"))
-    extra = {k: v for k, v in spec.items() if k not in ("tp", "pp", "ep", "etp")}
+    tp, pp, ep, etp, dp = (int(spec.get(k, 1)) for k in ("tp", "pp", "ep", "etp", "dp"))
+    extra = {k: v for k, v in spec.items() if k not in ("tp", "pp", "ep", "etp", "dp")}
     return [MegatronLayout(arch, tp=tp, pp=pp, ep=ep, etp=etp, tp_rank=t % tp, pp_rank=p, ep_rank=e,
                            etp_rank=t % etp, **extra)
-            for p in range(pp) for e in range(ep) for t in range(max(tp, etp))]
+            for _d in range(dp) for p in range(pp) for e in range(ep) for t in range(max(tp, etp))]
 
 
 def rollout_layouts(arch, spec: dict, replicas: int) -> list[SGLangLayout]:
@@ -91,9 +91,6 @@ def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs
     receivers = [_meta_binding(l) for l in rollout_layouts(arch, rollout, replicas)]
     smetas = [m for m, _ in senders]
     rmetas = {r: m for r, (m, _) in enumerate(receivers)}
-    plan = assign_sources(smetas, rmetas, replica_consistent=multicast)
-    groups = {g[0]: g for g in receiver_replicas(rmetas)} if multicast else {}
-    grouped = {r for g in groups.values() for r in g}
     ntp = int(rollout.get("tp", 1))
     if colocated == "interleaved":
         gpu = lambda w: ((w % ntp) * replicas + w // ntp) % len(senders)       # noqa: E731
@@ -101,6 +98,12 @@ def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs
         gpu = lambda w: w % len(senders)                                          # noqa: E731
     else:
         gpu = lambda w: len(senders) + w                                          # noqa: E731
+    # the assignment the sender's connect makes: GPU-aware (a replicated entry from the worker's
+    # own GPU where a trainer rank there holds it), replica-consistent with multicast
+    plan = assign_sources(smetas, rmetas, replica_consistent=multicast, sender_gpus=list(range(len(senders))),
+                          receiver_gpus={w: gpu(w) for w in rmetas})
+    groups = {g[0]: g for g in receiver_replicas(rmetas)} if multicast else {}
+    grouped = {r for g in groups.values() for r in g}
     routes: list[dict] = []
     srows, ingress = [], [0] * len(receivers)
     for s, (smeta, sphys) in enumerate(senders):
