@@ -70,7 +70,7 @@ class SyncStats:
     bytes_written: int = 0
     receivers: list[int] = field(default_factory=list)
     status: int = 0
-    link_gbs: float = 770.0         # bandwidth the fraction below is taken against
+    link_gbs: float = 788.0         # bandwidth the fraction below is taken against (measured peer peak)
     marks: dict = field(default_factory=dict)   # time.perf_counter() at the sync's steps (start, done, armed, end)
 
     @property
