@@ -7,6 +7,7 @@ memory on every sync) and a status word.  A sync is then a single kernel launch.
 """
 from __future__ import annotations
 
+import logging
 import os
 from dataclasses import dataclass
 
@@ -15,6 +16,8 @@ import torch
 
 from ..core.plan import OP_COPY, Tables
 from ._ext import ext
+
+logger = logging.getLogger(__name__)
 
 # TMA pipeline modes of the kernel (stages x piece bytes of shared memory per CTA).  In the
 # TMA modes the same shared memory is also the ring of quant stages (32 KiB blocks loaded by
@@ -117,7 +120,12 @@ class TransferProgram:
             qd = np.ascontiguousarray(tables.qdescs)
             maps = np.zeros(len(qd) * 128, dtype=np.uint8)
             valid = np.zeros(len(qd), dtype=np.uint8)
-            if ext().encode_quant_maps(qd.ctypes.data, len(qd), maps.ctypes.data, valid.ctypes.data):
+            try:
+                n_maps = ext().encode_quant_maps(qd.ctypes.data, len(qd), maps.ctypes.data, valid.ctypes.data)
+            except RuntimeError as e:           # no tensor-map encoder in this driver: register path
+                logger.warning("quant blocks take the register path: %s", e)
+                n_maps = 0
+            if n_maps:
                 self.qmaps = torch.from_numpy(maps).to(dev)          # caching-allocator blocks: 512-byte aligned
                 self.qtma = torch.from_numpy(valid).to(dev)
                 self.n_tma_quant = int(valid[tables.qwork["desc"]].sum())
