@@ -87,10 +87,13 @@ def assign_sources(sender_metas: list[WeightData], receiver_metas: dict[int, Wei
     entry goes to a receiver from a member on the receiver's own GPU where there is one (an
     HBM copy, no link bytes, not counted as load); the others balance the link load.
     """
-    def gpu(x, table):
-        return None if table is None else table[x]
-    local = lambda s_, r_: (gpu(s_, sender_gpus) is not None                          # noqa: E731
-                            and gpu(s_, sender_gpus) == gpu(r_, receiver_gpus))
+    def local(s_: int, r_: int) -> bool:
+        """Sender ``s_`` and receiver ``r_`` share a GPU (the copy stays in its HBM)."""
+        if sender_gpus is None or receiver_gpus is None:
+            return False
+        g = sender_gpus[s_]
+        return g is not None and g == receiver_gpus.get(r_)
+
     groups = replica_groups(sender_metas)
     load = [0] * len(sender_metas)
     plan: dict[int, dict[int, list[str]]] = defaultdict(lambda: defaultdict(list))
