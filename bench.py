@@ -71,6 +71,8 @@ def parse(argv=None):
                    help="nvls: rollout pools in VMM memory, multicast stores to replica groups")
     p.add_argument("--no-pool", action="store_true",
                    help="allocate every rollout parameter separately (one IPC handle each)")
+    p.add_argument("--placement", default="interleaved", choices=["interleaved", "block"],
+                   help="llama70b-colocated: replicas' ranks alternate over the GPUs, or replica 0 on GPUs 0-3")
     p.add_argument("--no-torch-p2p", action="store_true",
                    help="skip the same-box comparison with the reference's algorithm (torch copies + NCCL P2P)")
     p.add_argument("--stall-dump-s", type=float, default=150.0,
@@ -124,7 +126,7 @@ class Role:
     host: bool = False
 
 
-def scenario(config: str, n: int) -> tuple[str, list[Role], str]:
+def scenario(config: str, n: int, placement: str = "interleaved") -> tuple[str, list[Role], str]:
     if config == "llama8b":
         if n == 1:
             return "llama3-8b", [Role("trainer", 0, dict(tp=1)),
@@ -170,9 +172,9 @@ def scenario(config: str, n: int) -> tuple[str, list[Role], str]:
         # 2t + 1, one of them on its own GPU, so half the bytes stay in HBM (141 of 282 GB; with
         # replica 0 on GPUs 0-3 and replica 1 on 4-7 only 35 GB would, doubling the NVLink bound)
         roles = [Role("trainer", i, dict(tp=8, tp_rank=i)) for i in range(8)]
-        roles += [Role("rollout", 2 * (i % 4) + i // 4, dict(tp=4, tp_rank=i % 4), i // 4, i % 4, i % 4 == 0)
-                  for i in range(8)]
-        return "llama3-70b", roles, "tp8 -> 2 replicas x tp4, colocated, replicas interleaved (16 processes)"
+        gpu = (lambda i: 2 * (i % 4) + i // 4) if placement == "interleaved" else (lambda i: i)    # noqa: E731
+        roles += [Role("rollout", gpu(i), dict(tp=4, tp_rank=i % 4), i // 4, i % 4, i % 4 == 0) for i in range(8)]
+        return "llama3-70b", roles, f"tp8 -> 2 replicas x tp4, colocated, replicas {placement} (16 processes)"
     if config == "deepseek-lite-fp8":
         if n not in (4, 8):
             raise SystemExit("deepseek-lite-fp8 runs on 4 or 8 GPUs")
@@ -280,7 +282,7 @@ def launch_main(args):
     rank = int(os.environ.get("RANK", "0"))
     if launched != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={launched}")
-    _model, roles, _desc = scenario(args.config, args.gpus)
+    _model, roles, _desc = scenario(args.config, args.gpus, args.placement)
     nprocs = len(roles)
     children = []
     argv = sys.argv[1:]
@@ -334,7 +336,7 @@ def run_role(args, idx: int, nprocs: int, init: str | None):
 
     if init is not None:
         _init_group(init, idx, nprocs)
-    model, roles, desc = scenario(args.config, args.gpus)
+    model, roles, desc = scenario(args.config, args.gpus, args.placement)
     phase("process group up")
     role = roles[idx]
     arch = get_arch(model)
@@ -697,7 +699,7 @@ def torch_p2p_main(args):
     from weightbridge_b200.parallel.sglang import SGLangLayout
     launched = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    model, roles, desc = scenario(args.config, args.gpus)
+    model, roles, desc = scenario(args.config, args.gpus, args.placement)
     if len(roles) != launched or len({r.device for r in roles}) != len(roles):
         if rank == 0:
             print(json.dumps({"impl": "torch-p2p", "unavailable":
