@@ -2,7 +2,8 @@
 
 Prints one JSON object: the native extension (and the file it was loaded from), torch / CUDA /
 NCCL versions, and per GPU its name, compute capability, SM count and multicast (NVLS)
-support, plus the peer-access matrix that ``gpu_direct`` relies on.  Reads settings only.
+support, plus the peer-access matrix that ``gpu_direct`` relies on and the measured NVLink
+figures the planner's estimates use (``profiles/``).  Reads settings only.
 """
 from __future__ import annotations
 
@@ -49,6 +50,9 @@ def report() -> dict:
         notes.append("the transfer kernels are built for sm_100a (B200) only")
     if n > 1 and "peer_access" in out and not all(all(r) for r in out["peer_access"]):
         notes.append("some GPU pairs lack peer access: gpu_direct needs it between senders and receivers")
+    # the NVLink figures the dry-run planner and the benchmark's roofline divide by
+    from .ops.microbench import _mc_peak_gbs, _peer_peak_gbs
+    out["measured_link_gbs"] = {"gpu_to_gpu": _peer_peak_gbs(), "multicast_store": _mc_peak_gbs()}
     out["notes"] = notes
     return out
 
