@@ -80,3 +80,30 @@ def test_report_colocated_data_parallel_trainer_copies_locally():
     assert rep["gpu_local_bytes"] == rep["total_written_bytes"] > 0
     apart = report("tiny-llama", {"tp": 1, "dp": 2}, {"tp": 1}, replicas=2)
     assert apart["link_bound_ms"] > 0 and apart["gpu_local_bytes"] == 0
+
+
+def test_report_placement_search_matches_or_beats_the_structured_placements():
+    """``colocated="best"``: exhaustive over 8 workers on 8 GPUs (config 5's shape) finds a
+    placement as good as the interleaved one; with data-parallel trainer ranks every worker can
+    sit beside a rank holding all it needs (nothing crosses NVLink); past 8 workers the hill
+    climb runs and does no worse than the block placement."""
+    kw = dict(replicas=2, link_gbs=800.0)
+    best = report("tiny-llama-tp8", {"tp": 8}, {"tp": 4}, colocated="best", **kw)
+    inter = report("tiny-llama-tp8", {"tp": 8}, {"tp": 4}, colocated="interleaved", **kw)
+    assert sorted(best["placement"]) == list(range(8))
+    assert best["link_bound_ms"] <= inter["link_bound_ms"] * 1.001
+    dp = report("tiny-llama", {"tp": 1, "dp": 4}, {"tp": 2}, colocated="best", **kw)
+    assert dp["link_bound_ms"] == 0 and dp["gpu_local_bytes"] == dp["total_written_bytes"]
+    many = report("tiny-llama", {"tp": 2}, {"tp": 1}, replicas=10, colocated="best", link_gbs=800.0)
+    block = report("tiny-llama", {"tp": 2}, {"tp": 1}, replicas=10, colocated="block", link_gbs=800.0)
+    assert len(many["placement"]) == 10 and max(many["placement"].count(g) for g in range(2)) <= 5
+    assert many["link_bound_ms"] <= block["link_bound_ms"] * 1.001
+
+
+def test_placement_cost_model():
+    from weightbridge_b200.utils.placement import best_placement, link_cost
+    # worker 0 needs 10 bytes from sender 1, worker 1 needs 10 from sender 0: crossing is free
+    sources = {0: {(1,): 10}, 1: {(0,): 10}}
+    assert link_cost([0, 1], sources, 2) == 10 and link_cost([1, 0], sources, 2) == 0
+    p, c = best_placement(sources, 2, tp=1, replicas=2)
+    assert p == [1, 0] and c == 0

@@ -61,6 +61,26 @@ def _overlap_bytes(s_shards, r_shards, itemsize: int) -> int:
     return n * itemsize
 
 
+def overlap_sources(sender_metas: list[WeightData], receiver_metas: dict[int, WeightData]) -> dict[int, dict]:
+    """For every receiver, the bytes of its entries by the senders that can serve them:
+    ``{receiver: {(sender, ...): bytes}}``, a tuple of identical replicas (trainer DP, or a
+    TP-replicated norm) or a single sender (its own shard).  The placement search's input."""
+    groups = replica_groups(sender_metas)
+    out: dict[int, dict] = {}
+    for r, rmeta in receiver_metas.items():
+        acc: dict[tuple, int] = defaultdict(int)
+        for name, r_shards, r_dtype in rmeta:
+            q = rmeta.quant(name)
+            if q and q.get("role") == "scale":
+                continue
+            for group in groups.get(name, []):
+                n = _overlap_bytes(sender_metas[group[0]].shards(name), r_shards, r_dtype.itemsize)
+                if n:
+                    acc[tuple(sorted(group))] += n
+        out[r] = dict(acc)
+    return out
+
+
 def receiver_replicas(receiver_metas: dict[int, WeightData]) -> list[list[int]]:
     """Receivers with identical metadata (rollout replicas of one layout), groups of two or more."""
     by_key: dict[str, list[int]] = defaultdict(list)

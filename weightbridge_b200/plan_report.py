@@ -76,8 +76,9 @@ def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs
     GPUs: trainer rank s on GPU s; rollout worker w (tp rank t of replica e) on GPU ``trainers + w``,
     or beside the trainer ranks with ``colocated``: ``"block"`` (or True) puts it on GPU
     ``w % trainers`` (replica after replica), ``"interleaved"`` on GPU ``(t * replicas + e) %
-    trainers`` (the replicas' ranks alternate); bytes between a trainer rank and a worker on its
-    own GPU stay in HBM."""
+    trainers`` (the replicas' ranks alternate), ``"best"`` where the placement search puts it
+    (``utils/placement.py``); bytes between a trainer rank and a worker on its own GPU stay in
+    HBM."""
     from .utils.links import busiest_link, link_bytes
     from .control.assign import receiver_replicas
     from .core.plan import multicast_ok
@@ -92,7 +93,13 @@ def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs
     smetas = [m for m, _ in senders]
     rmetas = {r: m for r, (m, _) in enumerate(receivers)}
     ntp = int(rollout.get("tp", 1))
-    if colocated == "interleaved":
+    placement = None
+    if colocated == "best":                 # search the worker -> GPU placement (utils/placement.py)
+        from .control.assign import overlap_sources
+        from .utils.placement import best_placement
+        placement, _cost = best_placement(overlap_sources(smetas, rmetas), len(senders), ntp, replicas)
+        gpu = placement.__getitem__
+    elif colocated == "interleaved":
         gpu = lambda w: ((w % ntp) * replicas + w // ntp) % len(senders)       # noqa: E731
     elif colocated:
         gpu = lambda w: w % len(senders)                                          # noqa: E731
@@ -152,7 +159,8 @@ def report(model: str, trainer: dict, rollout: dict, replicas: int = 1, link_gbs
         "total_written_bytes": sum(ingress),
         "busiest_sender_bytes": egress, "busiest_receiver_bytes": inmax,
         "link_gbs": link_gbs, "multicast_gbs": mc_gbs if multicast else None,
-        "colocated": colocated, "gpu_local_bytes": local,
+        "colocated": colocated, "placement": placement if placement is not None else
+        ([gpu(w) for w in range(len(receivers))] if colocated else None), "gpu_local_bytes": local,
         "gpu_egress_bytes": {str(d): b for d, b in sorted(egress_b.items())},
         "gpu_multicast_egress_bytes": {str(d): b for d, b in sorted(mc_b.items())},
         "gpu_ingress_bytes": {str(d): b for d, b in sorted(ingress_b.items())},
@@ -180,9 +188,10 @@ def main(argv=None) -> int:
                     help="the nvls mode: replicas of one layout served by multicast stores")
     ap.add_argument("--mc-gbs", type=float, default=None,
                     help="multicast store rate out of one GPU (default: the measured one)")
-    ap.add_argument("--colocated", nargs="?", const="block", default=None, choices=["block", "interleaved"],
-                    help="rollout workers on the trainers' GPUs: block (worker w on GPU w %% trainers) or "
-                         "interleaved (tp rank t of replica e on GPU t * replicas + e); else GPUs of their own")
+    ap.add_argument("--colocated", nargs="?", const="block", default=None, choices=["block", "interleaved", "best"],
+                    help="rollout workers on the trainers' GPUs: block (worker w on GPU w %% trainers), "
+                         "interleaved (tp rank t of replica e on GPU t * replicas + e) or best (searched); "
+                         "else GPUs of their own")
     ap.add_argument("--json", action="store_true")
     a = ap.parse_args(argv)
     rep = report(a.model, _kv(a.trainer), _kv(a.rollout), a.replicas, a.link_gbs, a.trainer_kind,
@@ -206,7 +215,7 @@ def main(argv=None) -> int:
         line += f" unicast + {_gb(mc)} GB multicast"
     line += f", busiest worker {_gb(rep['busiest_receiver_bytes'])} GB"
     if rep["colocated"]:
-        line += f"; {_gb(rep['gpu_local_bytes'])} GB stay within GPUs"
+        line += f"; {_gb(rep['gpu_local_bytes'])} GB stay within GPUs (worker -> GPU {rep['placement']})"
     worst = rep["busiest_gpu"]
     where = f" ({worst['side']} of GPU {worst['gpu']})" if worst else ""
     line += f" -> {rep['link_bound_ms']:.2f} ms{where} at {rep['link_gbs']:.0f} GB/s per link"
