@@ -541,6 +541,23 @@ class WeightSender:
             m.map()
         logger.info("sender %d: %d multicast group(s)", self.rank, len(self._mc))
 
+    def _leave_session(self) -> None:
+        """The session store lives in rank 0's process: rank 0 keeps it up until every other
+        sender rank has left (bounded by the sync deadline), so a rank still finishing its last
+        sync, reading its workers' keys, is not cut off by rank 0 leaving first.  The other
+        ranks say they left."""
+        sess = self.session
+        if sess is None or self.world_size <= 1:
+            return
+        try:
+            if self.rank == 0:
+                sess.wait([f"left/{r}" for r in range(1, self.world_size)], self.config.sync_timeout_s,
+                          "the other sender ranks to leave")
+            else:
+                sess.set(f"left/{self.rank}", "1")
+        except Exception as e:       # a rank that never leaves (gone) costs the wait, nothing else
+            logger.warning("sender %d: leaving the session: %s", self.rank, e)
+
     def _teardown_multicast(self) -> None:
         """Unmap, tell the group, and unbind only once every sender of the group unmapped
         (no multimem store can then reach this device's backing).  Also undoes a set-up that
@@ -634,6 +651,7 @@ class WeightSender:
         self._close_watch()
         self._close_arm_channel()
         self._teardown_multicast()
+        self._leave_session()
         for imp in self._imports.values():
             imp.close()
         self._imports.clear()
