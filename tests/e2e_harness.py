@@ -241,7 +241,8 @@ def fanout_trainer_proc(rank, world, tport, urls, q, n_syncs, model, mode, devic
             sender.send(views)
         prog = sender.program
         mc_items = int(((prog.tables.items["op"] & 0xFF) == OP_COPY_MC).sum()) if prog is not None else 0
-        q.put(("trainer", rank, {"epoch": sender.epoch, "mc_groups": len(sender._mc), "mc_items": mc_items}))
+        q.put(("trainer", rank, {"epoch": sender.epoch, "mc_groups": len(sender._mc), "mc_items": mc_items,
+                                 "targets": sorted(sender.targets)}))
     except Exception:
         import traceback
         q.put(("error", traceback.format_exc(), rank))

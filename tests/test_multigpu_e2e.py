@@ -149,3 +149,27 @@ def test_nvls_fanout_sender_on_a_replica_gpu():
         pytest.skip("no NVLink multicast on this machine")
     rep = run_fanout("tiny-llama", "nvls", [dict(tp=1)], dict(tp=1), ["cuda:0"], ["cuda:0", "cuda:1"])
     assert rep[0]["mc_groups"] == 1 and rep[0]["mc_items"] > 0
+
+
+def test_nvls_fanout_tp2_trainer_multicasts_from_both_ranks():
+    """TP2 trainer into two TP1 replicas by multicast: the layer norms both TP ranks hold go to
+    both replicas from the same rank (replica-consistent assignment), so each rank writes the
+    same entries to both replicas and joins the multicast group."""
+    _need(4)
+    from tests.e2e_harness import run_fanout
+    from weightbridge_b200.parallel.nvls import nvls_supported
+    if not nvls_supported(0):
+        pytest.skip("no NVLink multicast on this machine")
+    rep = run_fanout("tiny-llama", "nvls", [dict(tp=2, tp_rank=0), dict(tp=2, tp_rank=1)], dict(tp=1),
+                     ["cuda:0", "cuda:1"], ["cuda:2", "cuda:3"])
+    assert all(r["mc_groups"] == 1 and r["mc_items"] > 0 for r in rep.values()), rep
+
+
+def test_data_parallel_trainer_serves_the_worker_on_its_gpu():
+    """Two identical trainer ranks (DP 2) on GPUs 0 and 1, a TP1 worker beside each: every entry
+    reaches a worker from the rank on its own GPU (an HBM copy), none over NVLink."""
+    _need(2)
+    from tests.e2e_harness import run_fanout
+    rep = run_fanout("tiny-llama", "gpu_direct", [dict(tp=1), dict(tp=1)], dict(tp=1), ["cuda:0", "cuda:1"],
+                     ["cuda:0", "cuda:1"])
+    assert rep[0]["targets"] == [2] and rep[1]["targets"] == [3], rep
